@@ -1,0 +1,108 @@
+/*
+ * kadllm_b200 -- C ABI of the B200-native GRBeam library (sm_100a).
+ *
+ * Every entry point takes plain device pointers, element counts / strides
+ * (in elements, not bytes), dtype codes and a cudaStream_t passed as void*.
+ * None allocates device memory: callers (the Python host layer, through torch)
+ * own every buffer.  Calls are asynchronous on `stream`; argument errors are
+ * reported synchronously through the return code, with a message available
+ * from kadllm_last_error() on the calling thread.
+ *
+ * Reference interfaces each entry point replaces are cited per function
+ * (paths relative to the Kadllm project, Greek-Guardian/Kadllm).
+ */
+#ifndef KADLLM_B200_H_
+#define KADLLM_B200_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define KADLLM_API __attribute__((visibility("default")))
+#else
+#define KADLLM_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* dtype codes */
+enum { KADLLM_F32 = 0, KADLLM_F16 = 1, KADLLM_BF16 = 2 };
+
+/* status codes: mapped by the Python layer to ValueError / TypeError /
+ * NotImplementedError / RuntimeError, the reference's error conventions
+ * (src/kadllm/ops.py:17-67, src/kadllm/kernels/flash_attention.py:20-23). */
+enum {
+  KADLLM_OK = 0,
+  KADLLM_EINVAL = 1,      /* bad shape / argument        -> ValueError          */
+  KADLLM_EDTYPE = 2,      /* unsupported dtype           -> TypeError           */
+  KADLLM_EUNSUPPORTED = 3,/* valid but not implemented   -> NotImplementedError */
+  KADLLM_ECUDA = 4        /* CUDA launch / runtime error -> RuntimeError        */
+};
+
+/* Message of the last failed call on this thread ("" if none). */
+KADLLM_API const char* kadllm_last_error(void);
+/* Library ABI version. */
+KADLLM_API int kadllm_abi_version(void);
+
+/* ------------------------------------------------------------------------
+ * Gated delta rule replay from a shared, request-sized state.
+ * Replaces src/kadllm/kernels/gated_delta.py:145 beam_fused_recurrent_gdn
+ * (the Triton path of src/kadllm/ops.py:70 gated_delta).
+ *   q, k  [BW, T, H, K]   contiguous, dtype x_dtype (f32/f16/bf16)
+ *   v     [BW, T, HV, V]  contiguous, x_dtype
+ *   log_decay, beta [BW, T, HV] contiguous, any float dtype
+ *   state [B, HV, K, V]   contiguous, any float dtype; never written
+ *   out   [BW, T, HV, V]  contiguous, x_dtype
+ * BW = batch * beam_width; beams of request b are rows b*W .. b*W+W-1.
+ * K == V in {32, 64, 128}; 1 <= T <= 8; HV % H == 0.  scale <= 0 -> K^-0.5.
+ * ------------------------------------------------------------------------ */
+KADLLM_API int kadllm_gated_delta_replay(const void* q, const void* k, const void* v, int x_dtype,
+                              const void* log_decay, int decay_dtype, const void* beta,
+                              int beta_dtype, const void* state, int state_dtype, void* out,
+                              int64_t batch, int64_t beam_width, int64_t steps, int64_t heads,
+                              int64_t v_heads, int64_t k_dim, int64_t v_dim, float scale,
+                              void* stream);
+
+/* ------------------------------------------------------------------------
+ * Fused GDN token mixer for beam decode (BF16): causal conv1d replay + SiLU,
+ * gates, gated delta replay from the shared state and the gated RMSNorm, i.e.
+ * src/kadllm/adapters/qwen3_5.py:273-305 (_linear) from the packed input
+ * projection up to (not including) out_proj.
+ *   proj        [BW*T, ld_proj] bf16, row = beam_row*T + t; columns
+ *               [q (H*K) | k (H*K) | v (HV*V) | z (HV*V) | b (HV) | a (HV)]
+ *   conv_state  [B, conv_dim, conv_hist] bf16 contiguous (last 3 taps used)
+ *   conv_weight [conv_dim, 4] bf16 contiguous
+ *   rec_state   [B, HV, K, V] bf16 contiguous
+ *   a_log, dt_bias [HV] f32; norm_weight [V] f32 (values of the BF16 params)
+ *   out         [BW*T, HV*V] bf16
+ * ------------------------------------------------------------------------ */
+KADLLM_API int kadllm_gdn_mixer_replay(const void* proj, int64_t ld_proj, const void* conv_state,
+                            int64_t conv_hist, const void* conv_weight, const void* rec_state,
+                            const float* a_log, const float* dt_bias, const float* norm_weight,
+                            float norm_eps, void* out, int64_t batch, int64_t beam_width,
+                            int64_t steps, int64_t heads, int64_t v_heads, int64_t k_dim,
+                            int64_t v_dim, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Depthwise causal conv1d replay from a shared prefix state (+ SiLU).
+ * Replaces src/kadllm/kernels/causal_conv1d.py:59 beam_causal_conv1d_update
+ * (the Triton path of src/kadllm/ops.py:166 causal_conv1d).
+ *   x      [BW, C, T] with element strides (xs0, xs1, xs2)  (may be a view)
+ *   state  [B, C, hist] with strides (ss0, ss1, ss2); the last width-1 taps
+ *          are used; never written
+ *   weight [C, width] contiguous; bias [C] or NULL
+ *   out    [BW, C, T] contiguous.  x/state/weight/bias/out share `dtype`.
+ * width <= 8; silu != 0 applies SiLU.
+ * ------------------------------------------------------------------------ */
+KADLLM_API int kadllm_causal_conv1d_replay(const void* x, int64_t xs0, int64_t xs1, int64_t xs2,
+                                const void* state, int64_t ss0, int64_t ss1, int64_t ss2,
+                                int64_t hist, const void* weight, const void* bias, void* out,
+                                int dtype, int64_t batch, int64_t beam_width, int64_t channels,
+                                int64_t steps, int64_t width, int silu, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KADLLM_B200_H_ */

@@ -1,0 +1,90 @@
+"""ctypes binding of the C ABI in ``include/kadllm_b200.h``.
+
+The shared library is built in-tree (``python -m kadllm_b200.build``).  There
+is no fallback: importing an operator without the library, or calling one on
+non-CUDA tensors, raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().with_name("libkadllm_b200.so")
+
+P, I, L, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
+
+# entry point -> argument types (all return int status)
+SIGNATURES: dict[str, list] = {
+    "kadllm_gated_delta_replay": [P, P, P, I, P, I, P, I, P, I, P, L, L, L, L, L, L, L, F, P],
+    "kadllm_gdn_mixer_replay": [P, L, P, L, P, P, P, P, P, F, P, L, L, L, L, L, L, L, P],
+    "kadllm_causal_conv1d_replay": [P, L, L, L, P, L, L, L, L, P, P, P, I, L, L, L, L, L, I, P],
+}
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"kadllm_b200 CUDA library missing ({LIB_PATH.name}); build it with "
+                "`python -m kadllm_b200.build`"
+            )
+        handle = ctypes.CDLL(str(LIB_PATH))
+        handle.kadllm_last_error.restype = ctypes.c_char_p
+        handle.kadllm_last_error.argtypes = []
+        handle.kadllm_abi_version.restype = ctypes.c_int
+        for name, args in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.argtypes = args
+            fn.restype = ctypes.c_int
+        _lib = handle
+    return _lib
+
+
+_ERRORS = {1: ValueError, 2: TypeError, 3: NotImplementedError, 4: RuntimeError}
+
+
+def call(name: str, *args) -> None:
+    """Invoke an entry point and map a nonzero status to the reference's exception types."""
+    rc = getattr(lib(), name)(*args)
+    if rc:
+        msg = lib().kadllm_last_error().decode(errors="replace")
+        raise _ERRORS.get(rc, RuntimeError)(msg)
+
+
+DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return DTYPE_CODES[t.dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {t.dtype}; expected float32, float16 or bfloat16") from None
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def require_cuda(*tensors: torch.Tensor) -> None:
+    if not all(t.is_cuda for t in tensors):
+        raise RuntimeError("kadllm_b200 operators run only on CUDA tensors (no CPU path)")
+    if len({t.device for t in tensors}) != 1:
+        raise ValueError("all tensors must be on the same device")
+
+
+def aligned(t: torch.Tensor, nbytes: int = 16) -> torch.Tensor:
+    """Contiguous tensor whose data pointer is ``nbytes``-aligned (copies only if needed)."""
+    t = t.contiguous()
+    if t.data_ptr() % nbytes:
+        t = t.clone()
+    return t

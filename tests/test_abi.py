@@ -1,0 +1,55 @@
+"""The C-ABI library builds, loads without a GPU and exports every declared symbol."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "kadllm_b200.h"
+
+
+def declared_functions() -> list[str]:
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(kadllm_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def library():
+    from kadllm_b200 import build
+
+    path = build.build()
+    return ctypes.CDLL(str(path))
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    assert "kadllm_last_error" in names and "kadllm_gated_delta_replay" in names
+    assert len(names) >= 4
+
+
+def test_library_exports_every_declared_symbol(library):
+    missing = [n for n in declared_functions() if not hasattr(library, n)]
+    assert missing == []
+
+
+def test_signatures_cover_every_compute_entry_point():
+    from kadllm_b200 import _lib
+
+    compute = [n for n in declared_functions() if n not in ("kadllm_last_error", "kadllm_abi_version")]
+    assert sorted(compute) == sorted(_lib.SIGNATURES)
+
+
+def test_argument_errors_are_reported_without_a_gpu(library):
+    from kadllm_b200 import _lib
+
+    lib = _lib.lib()
+    # T = 9 exceeds the replay limit: rejected on the host, before any launch
+    rc = lib.kadllm_gated_delta_replay(None, None, None, 2, None, 0, None, 0, None, 2, None,
+                                       1, 1, 9, 1, 1, 32, 32, 0.0, None)
+    assert rc == 3
+    assert b"suffix steps" in lib.kadllm_last_error()
+    rc = lib.kadllm_gated_delta_replay(None, None, None, 7, None, 0, None, 0, None, 2, None,
+                                       1, 1, 1, 1, 1, 32, 32, 0.0, None)
+    assert rc == 2
