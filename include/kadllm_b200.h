@@ -101,6 +101,28 @@ KADLLM_API int kadllm_causal_conv1d_replay(const void* x, int64_t xs0, int64_t x
                                 int dtype, int64_t batch, int64_t beam_width, int64_t channels,
                                 int64_t steps, int64_t width, int silu, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Shared-prefix + causal-suffix GQA attention for beam decode (BF16).
+ * Replaces src/kadllm/kernels/flash_attention.py:11 prefix_attention_flash
+ * (the accelerated path of src/kadllm/ops.py:252 prefix_attention).
+ *   q        [BW, T, H, D]   strides (sq_bw, sq_t, sq_h), D contiguous
+ *   prefix_k [B, L, HK, D]   strides (spk_b, spk_l, spk_h); prefix_v likewise
+ *   suffix_k [BW, T, HK, D]  strides (ssk_bw, ssk_t, ssk_h); suffix_v likewise
+ *   prefix_mask [B, L] uint8 (nonzero = valid key) or NULL
+ *   gate     [BW, T, H*D] strides (sg_bw, sg_t) or NULL: out *= sigmoid(gate)
+ *   out      [BW, T, H, D]   strides (so_bw, so_t, so_h)
+ * Fully masked or empty (L = 0) prefixes contribute nothing; T <= 8;
+ * D in {32, 64, 128, 256}.  q and prefix rows must be 16-byte aligned.
+ * ------------------------------------------------------------------------ */
+KADLLM_API int kadllm_prefix_attention(
+    const void* q, int64_t sq_bw, int64_t sq_t, int64_t sq_h, const void* prefix_k, int64_t spk_b,
+    int64_t spk_l, int64_t spk_h, const void* prefix_v, int64_t spv_b, int64_t spv_l, int64_t spv_h,
+    const void* suffix_k, int64_t ssk_bw, int64_t ssk_t, int64_t ssk_h, const void* suffix_v,
+    int64_t ssv_bw, int64_t ssv_t, int64_t ssv_h, const void* prefix_mask, const void* gate,
+    int64_t sg_bw, int64_t sg_t, void* out, int64_t so_bw, int64_t so_t, int64_t so_h, int dtype,
+    int64_t batch, int64_t beam_width, int64_t steps, int64_t heads, int64_t kv_heads,
+    int64_t prefix_len, int64_t head_dim, float scale, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

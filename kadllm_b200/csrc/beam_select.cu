@@ -1,0 +1,352 @@
+// Per-request beam selection over the full vocabulary (one GRBeam step).
+//
+// Semantics: src/kadllm/grbeam.py:93-122.  For request b with Wp parent beams
+// and vocabulary V:  logp = log_softmax(float(logits[b, w, :]))  (over the full,
+// unmasked row), masked entries -> -inf (no renormalisation), score = logp +
+// parent_score[b, w]; keep the top `width` of the Wp*V candidates, sorted by
+// score; parent = idx // V, token = idx % V; the new history is the parent's
+// history followed by the token.  Each score is evaluated in the reference's
+// fp32 order ((x - max) - log(sum)) + parent.  Ties are broken by the lower flat
+// index (torch.topk leaves their order unspecified).
+//
+// The reference loops over requests on the host (32 launches of a 254 MB
+// temporary each).  Here the whole batch is four launches and no temporary of
+// logits size:
+//   1. rowstats   per row: max (HBM pass), then sum-exp and a 2048-bin histogram
+//                 of (max - x) in 1/32-nat bins (second pass, L2-resident);
+//   2. threshold  per request: shifts every row histogram by the row's score
+//                 offset into a request histogram and picks the highest score
+//                 threshold that provably keeps >= width candidates above it;
+//   3. collect    per row: re-reads the logits, appends candidates >= threshold
+//                 (score, flat index) to a per-request buffer;
+//   4. finalize   per request: bitonic sort of the buffer (score desc, index
+//                 asc), writes scores and the gathered history.
+// Buffers live in a caller-provided workspace (kadllm_beam_select_workspace).
+#include "common.cuh"
+
+namespace kb {
+namespace {
+
+constexpr int kRowBins = 2048;     // (max - x) in [0, 64) nats, last bin = farther
+constexpr int kReqBins = 4096;
+constexpr float kBinsPerNat = 32.f;
+constexpr int kCap = 16384;        // candidates kept per request
+constexpr int kRowThreads = 512;
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct SelArgs {
+  const void* logits; int dtype; int64_t ld;
+  const float* parent;         // [B*Wp] or null (zeros)
+  const uint8_t* mask;         // [B*Wp, V] or null
+  const int64_t* old_hist;     // [B*Wp, depth] or null
+  float* out_scores;           // [B*W]
+  int64_t* out_hist;           // [B*W, depth+1]
+  float2* rowstat;             // [rows] (max, log-sum-exp offset)
+  uint32_t* rowhist;           // [rows, kRowBins]
+  float* thresh;               // [B]
+  uint32_t* count;             // [B]
+  uint32_t* flags;             // [1] bit 0: candidate overflow
+  unsigned long long* cand;    // [B, kCap]
+  int B, Wp, W, depth;
+  int64_t V;
+};
+
+template <typename T>
+__device__ __forceinline__ float to_f(T v);
+template <> __device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+// Visit every element of a row: f(index, value).  Uses 16-byte loads when the
+// row is 16-byte aligned and V is a multiple of the vector width.
+template <typename T, typename F>
+__device__ __forceinline__ void for_row(const T* row, int64_t V, bool vec, F&& f) {
+  constexpr int N = 16 / sizeof(T);
+  if (vec) {
+    for (int64_t i = int64_t(threadIdx.x) * N; i < V; i += int64_t(blockDim.x) * N) {
+      const uint4 u = *reinterpret_cast<const uint4*>(row + i);
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int j = 0; j < N; ++j) f(i + j, to_f<T>(e[j]));
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < V; i += blockDim.x) f(i, to_f<T>(row[i]));
+  }
+}
+
+__device__ float block_reduce(float v, bool is_max, float* red) {
+  v = is_max ? warp_max(v) : warp_sum(v);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    float x = lane < nw ? red[lane] : (is_max ? -INFINITY : 0.f);
+    x = is_max ? warp_max(x) : warp_sum(x);
+    if (lane == 0) red[32] = x;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float order_inv(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kRowThreads) rowstats_kernel(const SelArgs a, bool vec) {
+  __shared__ uint32_t hist[kRowBins];
+  __shared__ float red[33];
+  const int64_t r = blockIdx.x;
+  const T* row = reinterpret_cast<const T*>(a.logits) + r * a.ld;
+  float m = -INFINITY;
+  for_row<T>(row, a.V, vec, [&](int64_t, float x) { m = fmaxf(m, x); });
+  m = block_reduce(m, true, red);
+  for (int i = threadIdx.x; i < kRowBins; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  const float ml = m * kLog2e;
+  const uint8_t* mrow = a.mask ? a.mask + r * a.V : nullptr;
+  float s = 0.f;
+  for_row<T>(row, a.V, vec, [&](int64_t i, float x) {
+    s += exp2f(x * kLog2e - ml);
+    if (mrow == nullptr || mrow[i]) {
+      const float d = (m - x) * kBinsPerNat;
+      const int bin = d < float(kRowBins - 1) ? int(d) : kRowBins - 1;
+      atomicAdd(&hist[bin], 1u);
+    }
+  });
+  s = block_reduce(s, false, red);
+  if (threadIdx.x == 0) a.rowstat[r] = make_float2(m, logf(s));
+  __syncthreads();
+  for (int i = threadIdx.x; i < kRowBins; i += blockDim.x) a.rowhist[r * kRowBins + i] = hist[i];
+}
+
+__global__ void __launch_bounds__(1024) threshold_kernel(const SelArgs a) {
+  __shared__ uint32_t rh[kReqBins];
+  __shared__ float red[33];
+  __shared__ uint32_t scan[1024];
+  const int b = blockIdx.x;
+  // S_ref: best candidate score of the request (score of each row's max element)
+  float sref = -INFINITY;
+  for (int w = threadIdx.x; w < a.Wp; w += blockDim.x) {
+    const float p = a.parent ? a.parent[int64_t(b) * a.Wp + w] : 0.f;
+    const float2 st = a.rowstat[int64_t(b) * a.Wp + w];
+    sref = fmaxf(sref, p - st.y);
+  }
+  sref = block_reduce(sref, true, red);
+  for (int i = threadIdx.x; i < kReqBins; i += blockDim.x) rh[i] = 0;
+  __syncthreads();
+  if (sref > -INFINITY) {
+    for (int w = 0; w < a.Wp; ++w) {
+      const int64_t r = int64_t(b) * a.Wp + w;
+      const float p = a.parent ? a.parent[r] : 0.f;
+      const float off = p - a.rowstat[r].y;
+      if (!(off > -INFINITY)) continue;
+      const float e = (sref - off) * kBinsPerNat;
+      if (e >= float(kReqBins)) continue;
+      const int base = int(e) + 1;
+      for (int j = threadIdx.x; j < kRowBins - 1; j += blockDim.x) {
+        const uint32_t c = a.rowhist[r * kRowBins + j];
+        if (c && base + j < kReqBins) atomicAdd(&rh[base + j], c);
+      }
+    }
+  }
+  __syncthreads();
+  // smallest K with cumulative count >= W: each thread owns 4 consecutive bins
+  constexpr int per = kReqBins / 1024;
+  uint32_t local = 0;
+  for (int j = 0; j < per; ++j) local += rh[threadIdx.x * per + j];
+  scan[threadIdx.x] = local;
+  __syncthreads();
+  for (int off = 1; off < 1024; off <<= 1) {
+    const uint32_t v = threadIdx.x >= off ? scan[threadIdx.x - off] : 0;
+    __syncthreads();
+    scan[threadIdx.x] += v;
+    __syncthreads();
+  }
+  __shared__ int found;
+  if (threadIdx.x == 0) found = kReqBins;
+  __syncthreads();
+  uint32_t run = scan[threadIdx.x] - local;
+  for (int j = 0; j < per; ++j) {
+    run += rh[threadIdx.x * per + j];
+    if (run >= uint32_t(a.W)) {
+      atomicMin(&found, threadIdx.x * per + j);
+      break;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // half a bin of slack absorbs fp32 rounding of the evaluated scores
+    a.thresh[b] = (found < kReqBins && sref > -INFINITY)
+                      ? sref - (float(found) + 1.5f) / kBinsPerNat
+                      : -INFINITY;
+    a.count[b] = 0;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) collect_kernel(const SelArgs a, bool vec) {
+  const int64_t r = blockIdx.x;
+  const int b = int(r / a.Wp), w = int(r % a.Wp);
+  const float p = a.parent ? a.parent[r] : 0.f;
+  const float2 st = a.rowstat[r];
+  const float tau = a.thresh[b];
+  if (!(p > -INFINITY) || (p - st.y) < tau) return;  // no candidate of this row reaches tau
+  const T* row = reinterpret_cast<const T*>(a.logits) + r * a.ld;
+  const uint8_t* mrow = a.mask ? a.mask + r * a.V : nullptr;
+  const uint32_t base_idx = uint32_t(int64_t(w) * a.V);
+  unsigned long long* out = a.cand + int64_t(b) * kCap;
+  for_row<T>(row, a.V, vec, [&](int64_t i, float x) {
+    const float score = ((x - st.x) - st.y) + p;
+    if (score >= tau && score > -INFINITY && (mrow == nullptr || mrow[i])) {
+      const uint32_t pos = atomicAdd(&a.count[b], 1u);
+      if (pos < kCap) {
+        const uint32_t idx = base_idx + uint32_t(i);
+        out[pos] = (static_cast<unsigned long long>(order_key(score)) << 32) | (0xffffffffu - idx);
+      }
+    }
+  });
+}
+
+__global__ void __launch_bounds__(1024) finalize_kernel(const SelArgs a) {
+  extern __shared__ unsigned long long keys[];
+  const int b = blockIdx.x;
+  const uint32_t total = a.count[b];
+  const int n = int(min(total, uint32_t(kCap)));
+  if (total > uint32_t(kCap) && threadIdx.x == 0) atomicOr(a.flags, 1u);
+  int N = 1;
+  while (N < max(n, a.W)) N <<= 1;
+  for (int i = threadIdx.x; i < N; i += blockDim.x) keys[i] = i < n ? a.cand[int64_t(b) * kCap + i] : 0ull;
+  __syncthreads();
+  // bitonic sort, descending
+  for (int k = 2; k <= N; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < N; i += blockDim.x) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const unsigned long long x = keys[i], y = keys[ixj];
+          const bool desc = (i & k) == 0;
+          if (desc ? (x < y) : (x > y)) {
+            keys[i] = y;
+            keys[ixj] = x;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int w = threadIdx.x; w < a.W; w += blockDim.x) {
+    float score = -INFINITY;
+    uint32_t idx = 0;
+    if (w < n) {
+      const unsigned long long k = keys[w];
+      score = order_inv(uint32_t(k >> 32));
+      idx = 0xffffffffu - uint32_t(k & 0xffffffffull);
+    }
+    const int64_t parent = int64_t(idx) / a.V, token = int64_t(idx) % a.V;
+    const int64_t o = int64_t(b) * a.W + w;
+    a.out_scores[o] = score;
+    int64_t* h = a.out_hist + o * (a.depth + 1);
+    const int64_t* src = a.old_hist ? a.old_hist + (int64_t(b) * a.Wp + parent) * a.depth : nullptr;
+    for (int d = 0; d < a.depth; ++d) h[d] = src[d];
+    h[a.depth] = token;
+  }
+}
+
+struct Workspace {
+  size_t rowstat, rowhist, thresh, count, flags, cand, total;
+  Workspace(int64_t B, int64_t Wp) {
+    auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
+    const int64_t rows = B * Wp;
+    rowstat = 0;
+    rowhist = al(rowstat + rows * sizeof(float2));
+    thresh = al(rowhist + rows * kRowBins * sizeof(uint32_t));
+    count = al(thresh + B * sizeof(float));
+    flags = al(count + B * sizeof(uint32_t));
+    cand = al(flags + sizeof(uint32_t));
+    total = al(cand + B * kCap * sizeof(unsigned long long));
+  }
+};
+
+template <typename T>
+int launch_select(SelArgs& a, bool vec, cudaStream_t s) {
+  const int64_t rows = int64_t(a.B) * a.Wp;
+  rowstats_kernel<T><<<unsigned(rows), kRowThreads, 0, s>>>(a, vec);
+  threshold_kernel<<<a.B, 1024, 0, s>>>(a);
+  collect_kernel<T><<<unsigned(rows), 256, 0, s>>>(a, vec);
+  int N = 1;
+  while (N < max(kCap, a.W)) N <<= 1;
+  const size_t smem = size_t(N) * sizeof(unsigned long long);
+  if (cudaFuncSetAttribute(finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess) {
+    set_error("beam select: cannot reserve %zu bytes of shared memory", smem);
+    return KADLLM_ECUDA;
+  }
+  finalize_kernel<<<a.B, 1024, smem, s>>>(a);
+  KB_CHECK_LAUNCH("beam select launch");
+  return KADLLM_OK;
+}
+
+}  // namespace
+}  // namespace kb
+
+extern "C" int64_t kadllm_beam_select_workspace(int64_t batch, int64_t prev_width) {
+  return int64_t(kb::Workspace(batch, prev_width).total);
+}
+
+extern "C" int kadllm_beam_select(const void* logits, int logits_dtype, int64_t ld_row, const float* parent_scores,
+                                  const void* mask, const int64_t* old_history, float* out_scores,
+                                  int64_t* out_history, void* workspace, int64_t workspace_bytes, int64_t batch,
+                                  int64_t prev_width, int64_t vocab, int64_t width, int64_t depth,
+                                  void* stream) {
+  using namespace kb;
+  KB_REQUIRE(valid_dtype(logits_dtype), KADLLM_EDTYPE, "beam select: unsupported logits dtype");
+  KB_REQUIRE(batch >= 1 && prev_width >= 1 && vocab >= 1 && width >= 1 && depth >= 0, KADLLM_EINVAL,
+             "beam select: empty dimensions");
+  KB_REQUIRE(width <= prev_width * vocab, KADLLM_EINVAL, "beam width exceeds the number of candidate slots");
+  KB_REQUIRE(width <= kCap, KADLLM_EUNSUPPORTED, "beam select: width %lld above %d", (long long)width, kCap);
+  KB_REQUIRE(prev_width * vocab < 0xffffffffll, KADLLM_EUNSUPPORTED, "beam select: more than 2^32 candidates");
+  KB_REQUIRE(batch <= 65535 && batch * prev_width <= 2147483647ll, KADLLM_EINVAL, "beam select: too many rows");
+  KB_REQUIRE(ld_row >= vocab, KADLLM_EINVAL, "beam select: row stride shorter than the vocabulary");
+  KB_REQUIRE(logits && out_scores && out_history && workspace && (depth == 0 || old_history), KADLLM_EINVAL,
+             "beam select: null pointer");
+  const Workspace ws(batch, prev_width);
+  KB_REQUIRE(workspace_bytes >= int64_t(ws.total), KADLLM_EINVAL, "beam select: workspace too small");
+  KB_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, KADLLM_EINVAL,
+             "beam select: workspace must be 256-byte aligned");
+  char* w = static_cast<char*>(workspace);
+  SelArgs a{};
+  a.logits = logits; a.dtype = logits_dtype; a.ld = ld_row;
+  a.parent = parent_scores; a.mask = static_cast<const uint8_t*>(mask); a.old_hist = old_history;
+  a.out_scores = out_scores; a.out_hist = out_history;
+  a.rowstat = reinterpret_cast<float2*>(w + ws.rowstat);
+  a.rowhist = reinterpret_cast<uint32_t*>(w + ws.rowhist);
+  a.thresh = reinterpret_cast<float*>(w + ws.thresh);
+  a.count = reinterpret_cast<uint32_t*>(w + ws.count);
+  a.flags = reinterpret_cast<uint32_t*>(w + ws.flags);
+  a.cand = reinterpret_cast<unsigned long long*>(w + ws.cand);
+  a.B = int(batch); a.Wp = int(prev_width); a.W = int(width); a.depth = int(depth); a.V = vocab;
+  const int esz = dtype_size(logits_dtype);
+  const int vw = 16 / esz;
+  const bool vec = (reinterpret_cast<uintptr_t>(logits) & 15) == 0 && vocab % vw == 0 && ld_row % vw == 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (logits_dtype == KADLLM_BF16) return launch_select<__nv_bfloat16>(a, vec, s);
+  if (logits_dtype == KADLLM_F16) return launch_select<__half>(a, vec, s);
+  return launch_select<float>(a, vec, s);
+}
+
+extern "C" int kadllm_beam_select_status(const void* workspace, int64_t batch, int64_t prev_width,
+                                         uint32_t* flags_out, void* stream) {
+  using namespace kb;
+  KB_REQUIRE(workspace && flags_out, KADLLM_EINVAL, "beam select status: null pointer");
+  const Workspace ws(batch, prev_width);
+  cudaError_t e = cudaMemcpyAsync(flags_out, static_cast<const char*>(workspace) + ws.flags, sizeof(uint32_t),
+                                  cudaMemcpyDeviceToHost, static_cast<cudaStream_t>(stream));
+  if (e == cudaSuccess) e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  KB_REQUIRE(e == cudaSuccess, KADLLM_ECUDA, "beam select status: %s", cudaGetErrorString(e));
+  return KADLLM_OK;
+}

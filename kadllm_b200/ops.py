@@ -170,3 +170,87 @@ def causal_conv1d(
         1 if activation == "silu" else 0, _lib.stream(x.device),
     )
     return out
+
+
+def merge_attention(prefix_out, prefix_lse, suffix_out, suffix_lse):
+    """Merge two independently normalised attention partitions by LSE
+    (``src/kadllm/ops.py:243-249``).  The CUDA kernel performs this merge
+    internally; the helper is kept for API compatibility."""
+    total = torch.logaddexp(prefix_lse, suffix_lse)
+    return (
+        prefix_out * (prefix_lse - total).exp()[..., None]
+        + suffix_out * (suffix_lse - total).exp()[..., None]
+    )
+
+
+def prefix_attention(
+    q,
+    prefix_k,
+    prefix_v,
+    suffix_k,
+    suffix_v,
+    *,
+    beam_width: int = 1,
+    prefix_mask: torch.Tensor | None = None,
+    scale: float | None = None,
+    backend: str = "auto",
+):
+    """Shared-prefix attention plus a causal replay suffix, with GQA support.
+
+    Layout: q [B*W,T,H,D], prefix K/V [B,L,HK,D] (strided views accepted),
+    suffix K/V [B*W,T,HK,D].  prefix_mask [B,L] is True for valid keys.
+    Mirrors ``src/kadllm/ops.py:252-308``.  Unlike the reference's FlashAttention
+    path, padded prefixes (``prefix_mask``) are supported.  BF16 only.
+    """
+    _width(beam_width)
+    tensors = (q, prefix_k, prefix_v, suffix_k, suffix_v)
+    _same_device(tensors)
+    if any(t.ndim != 4 for t in tensors):
+        raise ValueError("attention inputs must all have rank 4")
+    BW, T, H, D = q.shape
+    B, L, HK, DK = prefix_k.shape
+    if (
+        min(BW, T, H, D, B, HK) < 1
+        or BW != B * beam_width
+        or H % HK
+        or DK != D
+        or prefix_v.shape != prefix_k.shape
+        or suffix_k.shape != (BW, T, HK, D)
+        or suffix_v.shape != suffix_k.shape
+    ):
+        raise ValueError("incompatible attention shapes")
+    if len({t.dtype for t in tensors}) != 1:
+        raise ValueError("attention inputs must have the same dtype")
+    if prefix_mask is not None and (
+        prefix_mask.shape != (B, L) or prefix_mask.dtype != torch.bool or prefix_mask.device != q.device
+    ):
+        raise ValueError("prefix_mask must be bool [B,L] on the query device")
+    _backend(backend, _ACCEL + ("flash_attn",))
+    _lib.require_cuda(*tensors)
+    if q.dtype != torch.bfloat16:
+        raise ValueError("the CUDA attention kernel requires bfloat16 inputs")
+    scale = 1 / math.sqrt(D) if scale is None else float(scale)
+
+    def rows(t):
+        # inner dim contiguous, 16-byte aligned rows
+        if t.stride(-1) != 1 or any(s % 8 for s in t.stride()[:-1]) or t.data_ptr() % 16:
+            t = t.contiguous()
+        return t
+
+    q, prefix_k, prefix_v = rows(q), rows(prefix_k), rows(prefix_v)
+    suffix_k, suffix_v = (
+        t if t.stride(-1) == 1 and not any(x % 2 for x in t.stride()) and t.data_ptr() % 4 == 0
+        else t.contiguous()
+        for t in (suffix_k, suffix_v)
+    )
+    mask = None if prefix_mask is None else prefix_mask.contiguous().view(torch.uint8)
+    out = torch.empty((BW, T, H, D), dtype=q.dtype, device=q.device)
+    _lib.call(
+        "kadllm_prefix_attention",
+        q.data_ptr(), *q.stride()[:3], prefix_k.data_ptr(), *prefix_k.stride()[:3],
+        prefix_v.data_ptr(), *prefix_v.stride()[:3], suffix_k.data_ptr(), *suffix_k.stride()[:3],
+        suffix_v.data_ptr(), *suffix_v.stride()[:3], _lib.ptr(mask), None, 0, 0,
+        out.data_ptr(), *out.stride()[:3], _lib.dtype_code(q), B, beam_width, T, H, HK, L, D,
+        scale, _lib.stream(q.device),
+    )
+    return out
