@@ -123,6 +123,35 @@ KADLLM_API int kadllm_prefix_attention(
     int64_t batch, int64_t beam_width, int64_t steps, int64_t heads, int64_t kv_heads,
     int64_t prefix_len, int64_t head_dim, float scale, void* stream);
 
+/* ------------------------------------------------------------------------
+ * One GRBeam selection step for a whole batch: fp32 log-softmax of every row
+ * (full vocabulary), optional mask (-inf, no renormalisation), + parent score,
+ * top-`width` of the prev_width*vocab candidates per request, sorted by score
+ * (ties: lower flat index first), and the gathered history.
+ * Replaces the per-request loop of src/kadllm/grbeam.py:103-122.
+ *   logits        [B*Wp rows, V] with row stride ld_row, dtype logits_dtype
+ *   parent_scores [B, Wp] f32 or NULL (all zero, first step)
+ *   mask          [B*Wp, V] uint8 (nonzero = allowed) or NULL
+ *   old_history   [B, Wp, depth] int64 or NULL when depth == 0
+ *   out_scores    [B, width] f32;  out_history [B, width, depth+1] int64
+ *   workspace     >= kadllm_beam_select_workspace(B, Wp) bytes, 256-byte
+ *                 aligned, caller-owned; zero its flags word before first use
+ *                 (a zero-filled allocation does).
+ * At most 16384 candidates above the per-request threshold are kept; an
+ * overflow sets a flag read by kadllm_beam_select_status.
+ * ------------------------------------------------------------------------ */
+KADLLM_API int64_t kadllm_beam_select_workspace(int64_t batch, int64_t prev_width);
+KADLLM_API int kadllm_beam_select(const void* logits, int logits_dtype, int64_t ld_row,
+                                  const float* parent_scores, const void* mask,
+                                  const int64_t* old_history, float* out_scores,
+                                  int64_t* out_history, void* workspace, int64_t workspace_bytes,
+                                  int64_t batch, int64_t prev_width, int64_t vocab, int64_t width,
+                                  int64_t depth, void* stream);
+/* Copies the workspace's flag word to *flags_out (bit 0: candidate overflow)
+ * after synchronising `stream`. */
+KADLLM_API int kadllm_beam_select_status(const void* workspace, int64_t batch, int64_t prev_width,
+                                         uint32_t* flags_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -18,6 +18,8 @@ P, I, L, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
 
 # entry point -> argument types (all return int status)
 SIGNATURES: dict[str, list] = {
+    "kadllm_beam_select": [P, I, L, P, P, P, P, P, P, L, L, L, L, L, L, P],
+    "kadllm_beam_select_status": [P, L, L, P, P],
     "kadllm_gated_delta_replay": [P, P, P, I, P, I, P, I, P, I, P, L, L, L, L, L, L, L, F, P],
     "kadllm_gdn_mixer_replay": [P, L, P, L, P, P, P, P, P, F, P, L, L, L, L, L, L, L, P],
     "kadllm_causal_conv1d_replay": [P, L, L, L, P, L, L, L, L, P, P, P, I, L, L, L, L, L, I, P],
@@ -40,6 +42,8 @@ def lib() -> ctypes.CDLL:
         handle.kadllm_last_error.restype = ctypes.c_char_p
         handle.kadllm_last_error.argtypes = []
         handle.kadllm_abi_version.restype = ctypes.c_int
+        handle.kadllm_beam_select_workspace.restype = ctypes.c_int64
+        handle.kadllm_beam_select_workspace.argtypes = [L, L]
         for name, args in SIGNATURES.items():
             fn = getattr(handle, name)
             fn.argtypes = args

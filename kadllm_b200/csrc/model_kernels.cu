@@ -1,0 +1,281 @@
+// Row-wise kernels of the Qwen3.5 hybrid decoder (BF16), each HBM-bound.
+//
+//   embed_rmsnorm   x = embed[ids]; normed = RMSNorm(x)          (TF:1227-1290 + TF:711-728)
+//   add_rmsnorm     x = bf16(x + delta); normed = RMSNorm(x)    (residual + next norm, TF:744-783)
+//   silu_mul        act = bf16(bf16(silu(gate)) * up)            (Qwen3_5MLP, TF:695-708)
+//   qk_norm_rope    per-head RMSNorm (1+w) of q and k, partial RoPE on the first
+//                   rotary_dim dims, scatter q / k / v to their destinations
+//                   (Qwen3_5Attention q/k path, TF:661-676; rotary TF:566-595)
+// TF: transformers/models/qwen3_5/modeling_qwen3_5.py.  RMSNorm: fp32 statistics,
+// x * rsqrt(mean(x^2) + eps) * (1 + w), one rounding to bf16.  Rounding points
+// mirror the BF16 torch modules so the pipeline tracks the reference bit for bit
+// up to accumulation order.
+#include "common.cuh"
+
+namespace kb {
+namespace {
+
+// One warp per row of H elements (H % 256 == 0 -> 8 bf16 per lane per step).
+template <int H>
+__device__ __forceinline__ void load_row(const __nv_bfloat16* p, float (&v)[H / 32]) {
+#pragma unroll
+  for (int c = 0; c < H / 256; ++c) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p + c * 256 + (threadIdx.x & 31) * 8);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[c * 8 + 2 * j] = __low2float(h[j]);
+      v[c * 8 + 2 * j + 1] = __high2float(h[j]);
+    }
+  }
+}
+
+template <int H>
+__device__ __forceinline__ void store_row(__nv_bfloat16* p, const float (&v)[H / 32]) {
+#pragma unroll
+  for (int c = 0; c < H / 256; ++c) {
+    uint4 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(v[c * 8 + 2 * j], v[c * 8 + 2 * j + 1]);
+    *reinterpret_cast<uint4*>(p + c * 256 + (threadIdx.x & 31) * 8) = u;
+  }
+}
+
+template <int H>
+__device__ __forceinline__ void rms_row(const float (&x)[H / 32], const float* w, float eps, float (&out)[H / 32]) {
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < H / 32; ++i) ss += x[i] * x[i];
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(ss / float(H) + eps);
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int c = 0; c < H / 256; ++c)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int col = c * 256 + lane * 8 + j;
+      out[c * 8 + j] = (x[c * 8 + j] * inv) * (1.0f + w[col]);
+    }
+}
+
+template <int H>
+__global__ void __launch_bounds__(256) embed_rmsnorm_kernel(const int64_t* ids, int ids_per_row_stride,
+                                                            const __nv_bfloat16* table, int64_t vocab,
+                                                            const float* w, float eps, __nv_bfloat16* x,
+                                                            __nv_bfloat16* normed, int64_t rows) {
+  const int64_t r = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  int64_t id = ids[r];
+  id = id < 0 ? 0 : (id >= vocab ? vocab - 1 : id);
+  float v[H / 32], o[H / 32];
+  load_row<H>(table + id * H, v);
+  store_row<H>(x + r * H, v);
+  rms_row<H>(v, w, eps, o);
+  store_row<H>(normed + r * H, o);
+}
+
+template <int H>
+__global__ void __launch_bounds__(256) add_rmsnorm_kernel(__nv_bfloat16* x, const __nv_bfloat16* delta,
+                                                          int64_t ld_delta, const float* w, float eps,
+                                                          __nv_bfloat16* normed, int64_t rows, int64_t row_step,
+                                                          int64_t row_offset) {
+  const int64_t i = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (i >= rows) return;
+  const int64_t r = i * row_step + row_offset;  // residual row (normed is written densely at i)
+  float v[H / 32], d[H / 32], o[H / 32];
+  load_row<H>(x + r * H, v);
+  if (delta) {
+    load_row<H>(delta + r * ld_delta, d);
+#pragma unroll
+    for (int j = 0; j < H / 32; ++j) v[j] = bf16r(v[j] + d[j]);
+    store_row<H>(x + r * H, v);
+  }
+  rms_row<H>(v, w, eps, o);
+  store_row<H>(normed + i * H, o);
+}
+
+__global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* gu, int64_t ld, int64_t inter,
+                                                       __nv_bfloat16* out, int64_t rows) {
+  const int64_t chunks = inter / 8;
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= rows * chunks) return;
+  const int64_t r = i / chunks, c = (i % chunks) * 8;
+  const uint4 gv = *reinterpret_cast<const uint4*>(gu + r * ld + c);
+  const uint4 uv = *reinterpret_cast<const uint4*>(gu + r * ld + inter + c);
+  const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv);
+  const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&uv);
+  uint4 ov;
+  __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&ov);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float g0 = __low2float(g2[j]), g1 = __high2float(g2[j]);
+    const float a0 = bf16r(silu_f(g0)), a1 = bf16r(silu_f(g1));
+    o2[j] = __floats2bfloat162_rn(a0 * __low2float(u2[j]), a1 * __high2float(u2[j]));
+  }
+  *reinterpret_cast<uint4*>(out + r * inter + c) = ov;
+}
+
+// One warp per (row, head).  D elements per head, EPL = D / 32 per lane (contiguous).
+template <int D>
+__global__ void __launch_bounds__(256) qk_norm_rope_kernel(
+    const __nv_bfloat16* proj, int64_t ld_proj, int Hq, int HK, const float* qw, const float* kw, float eps,
+    const __nv_bfloat16* cos_tab, const __nv_bfloat16* sin_tab, int rot, const int64_t* pos_of_row,
+    int64_t pos_base, int64_t rows_per_seq, __nv_bfloat16* q_out, int64_t sq_row, int64_t sq_h,
+    __nv_bfloat16* k_out, int64_t sk_seq, int64_t sk_pos, int64_t sk_h, __nv_bfloat16* v_out, int64_t sv_seq,
+    int64_t sv_pos, int64_t sv_h, int64_t rows) {
+  constexpr int EPL = D / 32;
+  const int heads = Hq + 2 * HK;
+  const int64_t item = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (item >= rows * heads) return;
+  const int64_t r = item / heads;
+  const int h = int(item % heads);
+  const int lane = threadIdx.x & 31;
+  // row r = (sequence s, position-in-sequence p); prefill: s = request; decode: s = beam row
+  const int64_t s = r / rows_per_seq, p = r % rows_per_seq;
+  const int64_t pos = pos_base + (pos_of_row ? pos_of_row[r] : p);
+  const __nv_bfloat16* src;
+  if (h < Hq) src = proj + r * ld_proj + int64_t(h) * 2 * D;             // q of head h (gate follows it)
+  else if (h < Hq + HK) src = proj + r * ld_proj + int64_t(Hq) * 2 * D + int64_t(h - Hq) * D;
+  else src = proj + r * ld_proj + int64_t(Hq) * 2 * D + int64_t(HK) * D + int64_t(h - Hq - HK) * D;
+  float v[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) v[e] = __bfloat162float(src[lane * EPL + e]);
+  if (h >= Hq + HK) {  // value: plain copy into the cache / suffix layout
+    const int hk = h - Hq - HK;
+    __nv_bfloat16* dst = v_out + s * sv_seq + p * sv_pos + hk * sv_h + lane * EPL;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) dst[e] = __float2bfloat16_rn(v[e]);
+    return;
+  }
+  const float* w = h < Hq ? qw : kw;
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) ss += v[e] * v[e];
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(ss / float(D) + eps);
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) v[e] = bf16r((v[e] * inv) * (1.0f + w[lane * EPL + e]));
+  // partial rotary: dims [0, rot) rotate with the partner half rot/2 away
+  const int half = rot / 2;
+  const int partner = half / EPL;  // lane distance (half % EPL == 0 checked on the host)
+  float pv[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) pv[e] = __shfl_xor_sync(0xffffffffu, v[e], partner);
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    const int d = lane * EPL + e;
+    if (d < rot) {
+      const float c = __bfloat162float(cos_tab[pos * rot + d]);
+      const float sn = __bfloat162float(sin_tab[pos * rot + d]);
+      const float rh = d < half ? -pv[e] : pv[e];  // rotate_half
+      v[e] = bf16r(bf16r(v[e] * c) + bf16r(rh * sn));
+    }
+  }
+  __nv_bfloat16* dst;
+  if (h < Hq) dst = q_out + r * sq_row + int64_t(h) * sq_h + lane * EPL;
+  else dst = k_out + s * sk_seq + p * sk_pos + int64_t(h - Hq) * sk_h + lane * EPL;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) dst[e] = __float2bfloat16_rn(v[e]);
+}
+
+}  // namespace
+}  // namespace kb
+
+using namespace kb;
+
+extern "C" int kadllm_embed_rmsnorm(const int64_t* ids, const void* table, int64_t vocab, const float* weight,
+                                    float eps, void* x, void* normed, int64_t rows, int64_t hidden, void* stream) {
+  KB_REQUIRE(rows >= 1 && vocab >= 1, KADLLM_EINVAL, "embed: empty");
+  KB_REQUIRE(ids && table && weight && x && normed, KADLLM_EINVAL, "embed: null pointer");
+  const unsigned grid = unsigned((rows + 7) / 8);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto T = static_cast<const __nv_bfloat16*>(table);
+  auto X = static_cast<__nv_bfloat16*>(x);
+  auto N = static_cast<__nv_bfloat16*>(normed);
+  if (hidden == 1024) embed_rmsnorm_kernel<1024><<<grid, 256, 0, s>>>(ids, 1, T, vocab, weight, eps, X, N, rows);
+  else if (hidden == 2048) embed_rmsnorm_kernel<2048><<<grid, 256, 0, s>>>(ids, 1, T, vocab, weight, eps, X, N, rows);
+  else if (hidden == 256) embed_rmsnorm_kernel<256><<<grid, 256, 0, s>>>(ids, 1, T, vocab, weight, eps, X, N, rows);
+  else if (hidden == 512) embed_rmsnorm_kernel<512><<<grid, 256, 0, s>>>(ids, 1, T, vocab, weight, eps, X, N, rows);
+  else {
+    set_error("embed: hidden size %lld not in {256, 512, 1024, 2048}", (long long)hidden);
+    return KADLLM_EUNSUPPORTED;
+  }
+  KB_CHECK_LAUNCH("embed launch");
+  return KADLLM_OK;
+}
+
+extern "C" int kadllm_add_rmsnorm(void* x, const void* delta, int64_t ld_delta, const float* weight, float eps,
+                                  void* normed, int64_t rows, int64_t row_step, int64_t row_offset, int64_t hidden,
+                                  void* stream) {
+  KB_REQUIRE(x && weight && normed && rows >= 1 && row_step >= 1, KADLLM_EINVAL, "add_rmsnorm: bad arguments");
+  const unsigned grid = unsigned((rows + 7) / 8);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto X = static_cast<__nv_bfloat16*>(x);
+  auto Dl = static_cast<const __nv_bfloat16*>(delta);
+  auto N = static_cast<__nv_bfloat16*>(normed);
+#define KB_NORM_CASE(HH)                                                                                  \
+  if (hidden == HH) {                                                                                     \
+    add_rmsnorm_kernel<HH><<<grid, 256, 0, s>>>(X, Dl, ld_delta, weight, eps, N, rows, row_step, row_offset); \
+    KB_CHECK_LAUNCH("add_rmsnorm launch");                                                                \
+    return KADLLM_OK;                                                                                     \
+  }
+  KB_NORM_CASE(1024)
+  KB_NORM_CASE(2048)
+  KB_NORM_CASE(256)
+  KB_NORM_CASE(512)
+#undef KB_NORM_CASE
+  set_error("add_rmsnorm: hidden size %lld not in {256, 512, 1024, 2048}", (long long)hidden);
+  return KADLLM_EUNSUPPORTED;
+}
+
+extern "C" int kadllm_silu_mul(const void* gate_up, int64_t ld, int64_t inter, void* out, int64_t rows,
+                               void* stream) {
+  KB_REQUIRE(gate_up && out && rows >= 1 && inter % 8 == 0 && ld % 8 == 0, KADLLM_EINVAL,
+             "silu_mul: bad arguments (intermediate size and stride must be multiples of 8)");
+  const int64_t n = rows * (inter / 8);
+  silu_mul_kernel<<<unsigned((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(gate_up), ld, inter, static_cast<__nv_bfloat16*>(out), rows);
+  KB_CHECK_LAUNCH("silu_mul launch");
+  return KADLLM_OK;
+}
+
+extern "C" int kadllm_qk_norm_rope(const void* proj, int64_t ld_proj, int64_t q_heads, int64_t kv_heads,
+                                   int64_t head_dim, const float* q_weight, const float* k_weight, float eps,
+                                   const void* cos_tab, const void* sin_tab, int64_t rotary_dim,
+                                   const int64_t* pos_of_row, int64_t pos_base, int64_t rows_per_seq, void* q_out,
+                                   int64_t sq_row, int64_t sq_h, void* k_out, int64_t sk_seq, int64_t sk_pos,
+                                   int64_t sk_h, void* v_out, int64_t sv_seq, int64_t sv_pos, int64_t sv_h,
+                                   int64_t rows, void* stream) {
+  KB_REQUIRE(proj && q_weight && k_weight && cos_tab && sin_tab && q_out && k_out && v_out, KADLLM_EINVAL,
+             "qk_norm_rope: null pointer");
+  KB_REQUIRE(rows >= 1 && rows_per_seq >= 1 && q_heads >= 1 && kv_heads >= 1, KADLLM_EINVAL, "qk_norm_rope: empty");
+  const int epl = int(head_dim / 32);
+  KB_REQUIRE(rotary_dim % 2 == 0 && rotary_dim <= head_dim && epl >= 1 && (rotary_dim / 2) % epl == 0, KADLLM_EINVAL,
+             "qk_norm_rope: rotary_dim/2 must be a multiple of head_dim/32");
+  const int64_t items = rows * (q_heads + 2 * kv_heads);
+  const unsigned grid = unsigned((items + 7) / 8);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto P = static_cast<const __nv_bfloat16*>(proj);
+  auto C = static_cast<const __nv_bfloat16*>(cos_tab);
+  auto S = static_cast<const __nv_bfloat16*>(sin_tab);
+  auto Q = static_cast<__nv_bfloat16*>(q_out);
+  auto K = static_cast<__nv_bfloat16*>(k_out);
+  auto Vv = static_cast<__nv_bfloat16*>(v_out);
+#define KB_QK_CASE(DD)                                                                                          \
+  if (head_dim == DD) {                                                                                         \
+    qk_norm_rope_kernel<DD><<<grid, 256, 0, s>>>(P, ld_proj, int(q_heads), int(kv_heads), q_weight, k_weight, eps, \
+                                                 C, S, int(rotary_dim), pos_of_row, pos_base, rows_per_seq, Q,      \
+                                                 sq_row, sq_h, K, sk_seq, sk_pos, sk_h, Vv, sv_seq, sv_pos, sv_h,   \
+                                                 rows);                                                             \
+    KB_CHECK_LAUNCH("qk_norm_rope launch");                                                                     \
+    return KADLLM_OK;                                                                                           \
+  }
+  KB_QK_CASE(256)
+  KB_QK_CASE(128)
+  KB_QK_CASE(64)
+  KB_QK_CASE(32)
+#undef KB_QK_CASE
+  set_error("qk_norm_rope: head_dim %lld not in {32, 64, 128, 256}", (long long)head_dim);
+  return KADLLM_EUNSUPPORTED;
+}
