@@ -109,7 +109,7 @@ KADLLM_API int kadllm_causal_conv1d_replay(const void* x, int64_t xs0, int64_t x
  *   prefix_k [B, L, HK, D]   strides (spk_b, spk_l, spk_h); prefix_v likewise
  *   suffix_k [BW, T, HK, D]  strides (ssk_bw, ssk_t, ssk_h); suffix_v likewise
  *   prefix_mask [B, L] uint8 (nonzero = valid key) or NULL
- *   gate     [BW, T, H*D] strides (sg_bw, sg_t) or NULL: out *= sigmoid(gate)
+ *   gate     [BW, T, H, D] strides (sg_bw, sg_t, sg_h) or NULL: out = o * sigmoid(gate)
  *   out      [BW, T, H, D]   strides (so_bw, so_t, so_h)
  * Fully masked or empty (L = 0) prefixes contribute nothing; T <= 8;
  * D in {32, 64, 128, 256}.  q and prefix rows must be 16-byte aligned.
@@ -119,7 +119,7 @@ KADLLM_API int kadllm_prefix_attention(
     int64_t spk_l, int64_t spk_h, const void* prefix_v, int64_t spv_b, int64_t spv_l, int64_t spv_h,
     const void* suffix_k, int64_t ssk_bw, int64_t ssk_t, int64_t ssk_h, const void* suffix_v,
     int64_t ssv_bw, int64_t ssv_t, int64_t ssv_h, const void* prefix_mask, const void* gate,
-    int64_t sg_bw, int64_t sg_t, void* out, int64_t so_bw, int64_t so_t, int64_t so_h, int dtype,
+    int64_t sg_bw, int64_t sg_t, int64_t sg_h, void* out, int64_t so_bw, int64_t so_t, int64_t so_h, int dtype,
     int64_t batch, int64_t beam_width, int64_t steps, int64_t heads, int64_t kv_heads,
     int64_t prefix_len, int64_t head_dim, float scale, void* stream);
 
@@ -151,6 +151,78 @@ KADLLM_API int kadllm_beam_select(const void* logits, int logits_dtype, int64_t 
  * after synchronising `stream`. */
 KADLLM_API int kadllm_beam_select_status(const void* workspace, int64_t batch, int64_t prev_width,
                                          uint32_t* flags_out, void* stream);
+
+/* ========================================================================
+ * Model building blocks of the native Qwen3.5 hybrid pipeline (BF16).  Each
+ * replaces a Transformers module on the reference's prefill / decode path
+ * (transformers/models/qwen3_5/modeling_qwen3_5.py, called from
+ * src/kadllm/adapters/qwen3_5.py:235-364).
+ * ====================================================================== */
+
+/* x = embed[ids] and normed = RMSNorm(x) * (1 + weight) (Qwen3_5RMSNorm);
+ * ids [rows] int64, table [vocab, hidden], x / normed [rows, hidden]. */
+KADLLM_API int kadllm_embed_rmsnorm(const int64_t* ids, const void* table, int64_t vocab,
+                                    const float* weight, float eps, void* x, void* normed,
+                                    int64_t rows, int64_t hidden, void* stream);
+
+/* Residual add + RMSNorm (1 + w): for i < rows, r = i*row_step + row_offset:
+ * x[r] = bf16(x[r] + delta[r]) (skipped when delta is NULL), normed[i] = RMSNorm(x[r]).
+ * hidden in {128, 256, 512, 1024, 2048}. */
+KADLLM_API int kadllm_add_rmsnorm(void* x, const void* delta, int64_t ld_delta, const float* weight,
+                                  float eps, void* normed, int64_t rows, int64_t row_step,
+                                  int64_t row_offset, int64_t hidden, void* stream);
+
+/* act[r, :] = bf16(bf16(silu(gate_up[r, :inter])) * gate_up[r, inter:2*inter]) (Qwen3_5MLP). */
+KADLLM_API int kadllm_silu_mul(const void* gate_up, int64_t ld, int64_t inter, void* out,
+                               int64_t rows, void* stream);
+
+/* Attention input path: from the packed projection row [q0|gate0|q1|gate1|...|k|v]
+ * (ld_proj per row) apply q_norm / k_norm (RMSNorm 1+w over head_dim) and partial
+ * RoPE (cos/sin tables [positions, rotary_dim] bf16) at position
+ * pos_base + (pos_of_row ? pos_of_row[r] : r % rows_per_seq), and scatter:
+ * q -> q_out[r*sq_row + h*sq_h], k / v -> (k|v)_out[s*s?_seq + p*s?_pos + hk*s?_h]
+ * with s = r / rows_per_seq, p = r % rows_per_seq (prefill: the prefix cache
+ * [B, HK, L, D]; decode: the per-beam suffix). */
+KADLLM_API int kadllm_qk_norm_rope(const void* proj, int64_t ld_proj, int64_t q_heads,
+                                   int64_t kv_heads, int64_t head_dim, const float* q_weight,
+                                   const float* k_weight, float eps, const void* cos_tab,
+                                   const void* sin_tab, int64_t rotary_dim,
+                                   const int64_t* pos_of_row, int64_t pos_base,
+                                   int64_t rows_per_seq, void* q_out, int64_t sq_row, int64_t sq_h,
+                                   void* k_out, int64_t sk_seq, int64_t sk_pos, int64_t sk_h,
+                                   void* v_out, int64_t sv_seq, int64_t sv_pos, int64_t sv_h,
+                                   int64_t rows, void* stream);
+
+/* Prompt conv: out[b*L+t, c] = bf16(silu(sum_j w[c,j] x[b*L+t-3+j, c])) with zero
+ * left padding, x = proj[:, :channels]; conv_state[b, c, 0..3] = x at positions
+ * L-4 .. L-1 (zero before the prompt) -- the prefix the decode conv replays from. */
+KADLLM_API int kadllm_conv1d_prefill(const void* proj, int64_t ld_proj, const void* weight,
+                                     void* out, int64_t ld_out, void* conv_state, int64_t batch,
+                                     int64_t length, int64_t channels, void* stream);
+
+/* Prompt gated delta rule, chunked (64) on the tensor cores, gates from the
+ * projection (beta = sigmoid(b), g = -exp(a_log) softplus(a + dt_bias)) and the
+ * gated RMSNorm fused on the output; writes the final state [B, HV, K, V] bf16
+ * once per request.  qkv [B*L, ld_qkv] conv outputs (q | k | v); proj holds
+ * z at column z_col (+ hv*V), then b (HV), then a (HV).  out [B*L, ld_out]. */
+KADLLM_API int kadllm_gdn_prefill(const void* qkv, int64_t ld_qkv, const void* proj,
+                                  int64_t ld_proj, int64_t z_col, const float* a_log,
+                                  const float* dt_bias, const float* norm_weight, float norm_eps,
+                                  void* out, int64_t ld_out, void* state, int64_t batch,
+                                  int64_t length, int64_t heads, int64_t v_heads, int64_t k_dim,
+                                  int64_t v_dim, void* stream);
+
+/* Prompt causal GQA attention (flash loop on the tensor cores) with the fused
+ * output gate out = bf16(o) * bf16(sigmoid(gate)) (gate may be NULL).
+ * q [B*L rows, H, D] (sq_row, sq_h); k / v [B, HK, L, D] via (s?_b, s?_l, s?_h);
+ * gate rows / heads (sg_row, sg_h); out (so_row, so_h). */
+KADLLM_API int kadllm_causal_attention(const void* q, int64_t sq_row, int64_t sq_h, const void* k,
+                                       int64_t sk_b, int64_t sk_l, int64_t sk_h, const void* v,
+                                       int64_t sv_b, int64_t sv_l, int64_t sv_h, const void* gate,
+                                       int64_t sg_row, int64_t sg_h, void* out, int64_t so_row,
+                                       int64_t so_h, int64_t batch, int64_t length, int64_t heads,
+                                       int64_t kv_heads, int64_t head_dim, float scale,
+                                       void* stream);
 
 #ifdef __cplusplus
 }

@@ -18,13 +18,20 @@ P, I, L, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
 
 # entry point -> argument types (all return int status)
 SIGNATURES: dict[str, list] = {
+    "kadllm_embed_rmsnorm": [P, P, L, P, F, P, P, L, L, P],
+    "kadllm_add_rmsnorm": [P, P, L, P, F, P, L, L, L, L, P],
+    "kadllm_silu_mul": [P, L, L, P, L, P],
+    "kadllm_qk_norm_rope": [P, L, L, L, L, P, P, F, P, P, L, P, L, L, P, L, L, P, L, L, L, P, L, L, L, L, P],
+    "kadllm_conv1d_prefill": [P, L, P, P, L, P, L, L, L, P],
+    "kadllm_gdn_prefill": [P, L, P, L, L, P, P, P, F, P, L, P, L, L, L, L, L, L, P],
+    "kadllm_causal_attention": [P, L, L, P, L, L, L, P, L, L, L, P, L, L, P, L, L, L, L, L, L, L, F, P],
     "kadllm_beam_select": [P, I, L, P, P, P, P, P, P, L, L, L, L, L, L, P],
     "kadllm_beam_select_status": [P, L, L, P, P],
     "kadllm_gated_delta_replay": [P, P, P, I, P, I, P, I, P, I, P, L, L, L, L, L, L, L, F, P],
     "kadllm_gdn_mixer_replay": [P, L, P, L, P, P, P, P, P, F, P, L, L, L, L, L, L, L, P],
     "kadllm_causal_conv1d_replay": [P, L, L, L, P, L, L, L, L, P, P, P, I, L, L, L, L, L, I, P],
     "kadllm_prefix_attention": [P, L, L, L, P, L, L, L, P, L, L, L, P, L, L, L, P, L, L, L, P, P,
-                                L, L, P, L, L, L, I, L, L, L, L, L, L, L, F, P],
+                                L, L, L, P, L, L, L, I, L, L, L, L, L, L, L, F, P],
 }
 
 _lib = None

@@ -80,8 +80,10 @@ class HybridConfig:
             raise ValueError("attention head_dim must be 32, 64, 128 or 256")
         if self.rotary_dim % 2 or self.rotary_dim > self.head_dim:
             raise ValueError("rotary dim must be even and at most head_dim")
-        if self.hidden_size % 8 or self.intermediate_size % 8:
-            raise ValueError("hidden and intermediate sizes must be multiples of 8")
+        if self.hidden_size not in (128, 256, 512, 1024, 2048):
+            raise ValueError("hidden size must be one of 128, 256, 512, 1024, 2048")
+        if self.intermediate_size % 8:
+            raise ValueError("intermediate size must be a multiple of 8")
 
     # ---- conversions -----------------------------------------------------
     @classmethod

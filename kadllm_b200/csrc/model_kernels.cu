@@ -15,48 +15,63 @@
 namespace kb {
 namespace {
 
-// One warp per row of H elements (H % 256 == 0 -> 8 bf16 per lane per step).
+// One warp per row of H elements: lane holds H/32 values as H/(32*VEC) chunks
+// of VEC consecutive elements (VEC = 8 -> 16-byte accesses; 4 -> 8-byte).
+template <int H>
+struct RowMap {
+  static constexpr int EPL = H / 32;
+  static constexpr int VEC = EPL >= 8 ? 8 : EPL;
+  static constexpr int CHUNKS = EPL / VEC;
+  __device__ static int col(int c, int j) { return c * 32 * VEC + (threadIdx.x & 31) * VEC + j; }
+};
+
 template <int H>
 __device__ __forceinline__ void load_row(const __nv_bfloat16* p, float (&v)[H / 32]) {
+  using M = RowMap<H>;
 #pragma unroll
-  for (int c = 0; c < H / 256; ++c) {
-    const uint4 u = *reinterpret_cast<const uint4*>(p + c * 256 + (threadIdx.x & 31) * 8);
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+  for (int c = 0; c < M::CHUNKS; ++c) {
+    __nv_bfloat162 h[M::VEC / 2];
+    if constexpr (M::VEC == 8) {
+      *reinterpret_cast<uint4*>(h) = *reinterpret_cast<const uint4*>(p + M::col(c, 0));
+    } else {
+      *reinterpret_cast<uint2*>(h) = *reinterpret_cast<const uint2*>(p + M::col(c, 0));
+    }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      v[c * 8 + 2 * j] = __low2float(h[j]);
-      v[c * 8 + 2 * j + 1] = __high2float(h[j]);
+    for (int j = 0; j < M::VEC / 2; ++j) {
+      v[c * M::VEC + 2 * j] = __low2float(h[j]);
+      v[c * M::VEC + 2 * j + 1] = __high2float(h[j]);
     }
   }
 }
 
 template <int H>
 __device__ __forceinline__ void store_row(__nv_bfloat16* p, const float (&v)[H / 32]) {
+  using M = RowMap<H>;
 #pragma unroll
-  for (int c = 0; c < H / 256; ++c) {
-    uint4 u;
-    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+  for (int c = 0; c < M::CHUNKS; ++c) {
+    __nv_bfloat162 h[M::VEC / 2];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(v[c * 8 + 2 * j], v[c * 8 + 2 * j + 1]);
-    *reinterpret_cast<uint4*>(p + c * 256 + (threadIdx.x & 31) * 8) = u;
+    for (int j = 0; j < M::VEC / 2; ++j) h[j] = __floats2bfloat162_rn(v[c * M::VEC + 2 * j], v[c * M::VEC + 2 * j + 1]);
+    if constexpr (M::VEC == 8) {
+      *reinterpret_cast<uint4*>(p + M::col(c, 0)) = *reinterpret_cast<uint4*>(h);
+    } else {
+      *reinterpret_cast<uint2*>(p + M::col(c, 0)) = *reinterpret_cast<uint2*>(h);
+    }
   }
 }
 
 template <int H>
 __device__ __forceinline__ void rms_row(const float (&x)[H / 32], const float* w, float eps, float (&out)[H / 32]) {
+  using M = RowMap<H>;
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < H / 32; ++i) ss += x[i] * x[i];
   ss = warp_sum(ss);
   const float inv = 1.0f / sqrtf(ss / float(H) + eps);
-  const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int c = 0; c < H / 256; ++c)
+  for (int c = 0; c < M::CHUNKS; ++c)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int col = c * 256 + lane * 8 + j;
-      out[c * 8 + j] = (x[c * 8 + j] * inv) * (1.0f + w[col]);
-    }
+    for (int j = 0; j < M::VEC; ++j) out[c * M::VEC + j] = (x[c * M::VEC + j] * inv) * (1.0f + w[M::col(c, j)]);
 }
 
 template <int H>
@@ -197,8 +212,9 @@ extern "C" int kadllm_embed_rmsnorm(const int64_t* ids, const void* table, int64
   else if (hidden == 2048) embed_rmsnorm_kernel<2048><<<grid, 256, 0, s>>>(ids, 1, T, vocab, weight, eps, X, N, rows);
   else if (hidden == 256) embed_rmsnorm_kernel<256><<<grid, 256, 0, s>>>(ids, 1, T, vocab, weight, eps, X, N, rows);
   else if (hidden == 512) embed_rmsnorm_kernel<512><<<grid, 256, 0, s>>>(ids, 1, T, vocab, weight, eps, X, N, rows);
+  else if (hidden == 128) embed_rmsnorm_kernel<128><<<grid, 256, 0, s>>>(ids, 1, T, vocab, weight, eps, X, N, rows);
   else {
-    set_error("embed: hidden size %lld not in {256, 512, 1024, 2048}", (long long)hidden);
+    set_error("embed: hidden size %lld not in {128, 256, 512, 1024, 2048}", (long long)hidden);
     return KADLLM_EUNSUPPORTED;
   }
   KB_CHECK_LAUNCH("embed launch");
@@ -224,8 +240,9 @@ extern "C" int kadllm_add_rmsnorm(void* x, const void* delta, int64_t ld_delta, 
   KB_NORM_CASE(2048)
   KB_NORM_CASE(256)
   KB_NORM_CASE(512)
+  KB_NORM_CASE(128)
 #undef KB_NORM_CASE
-  set_error("add_rmsnorm: hidden size %lld not in {256, 512, 1024, 2048}", (long long)hidden);
+  set_error("add_rmsnorm: hidden size %lld not in {128, 256, 512, 1024, 2048}", (long long)hidden);
   return KADLLM_EUNSUPPORTED;
 }
 

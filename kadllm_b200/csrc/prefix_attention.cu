@@ -34,7 +34,7 @@ struct AttnArgs {
   const __nv_bfloat16* sk; int64_t ssk_bw, ssk_t, ssk_h;
   const __nv_bfloat16* sv; int64_t ssv_bw, ssv_t, ssv_h;
   const uint8_t* mask;  // [B, L] or null
-  const __nv_bfloat16* gate; int64_t sg_bw, sg_t;  // [BW, T, H*D] or null
+  const __nv_bfloat16* gate; int64_t sg_bw, sg_t, sg_h;  // gate rows / steps / heads, or null
   __nv_bfloat16* out; int64_t so_bw, so_t, so_h;
   int B, W, T, H, HK, G, L;
   float scale_log2;
@@ -48,7 +48,11 @@ struct AttnSmem {
   static constexpr size_t bytes = (q_elems + 4 * kv_elems) * 2 + 2 * kBN * 4 + kBM * kTMax * 4;
 };
 
-template <int D>
+// CAUSAL = false: beam decode (rows = (beam, t, g), prefix + per-beam suffix).
+// CAUSAL = true : prompt prefill (rows = (position, g) of one request, keys are
+//                 the request's own positions <= the row's position; q rows are
+//                 indexed by token row b * L + position, the suffix is absent).
+template <int D, bool CAUSAL>
 __global__ void __launch_bounds__(kThreads) prefix_attention_kernel(const AttnArgs a) {
   using S = AttnSmem<D>;
   constexpr int STR = S::kStride;
@@ -63,7 +67,7 @@ __global__ void __launch_bounds__(kThreads) prefix_attention_kernel(const AttnAr
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int b = blockIdx.y / a.HK, hk = blockIdx.y % a.HK;
   const int TG = a.T * a.G;
-  const int R = a.W * TG;
+  const int R = CAUSAL ? a.L * a.G : a.W * TG;
   const int row0 = blockIdx.x * kBM;
 
   // ---- Q tile (rows = (beam, t, g) of this request / kv head) -----------------------
@@ -72,15 +76,22 @@ __global__ void __launch_bounds__(kThreads) prefix_attention_kernel(const AttnAr
     __nv_bfloat16* dst = sQ + r * STR + c * 8;
     const int gr = row0 + r;
     if (gr < R) {
-      const int beam = gr / TG, rem = gr % TG, t = rem / a.G, g = rem % a.G;
-      const __nv_bfloat16* src = a.q + (int64_t(b) * a.W + beam) * a.sq_bw + int64_t(t) * a.sq_t +
-                                 int64_t(hk * a.G + g) * a.sq_h + c * 8;
+      const __nv_bfloat16* src;
+      if constexpr (CAUSAL) {
+        const int pos = gr / a.G, g = gr % a.G;
+        src = a.q + (int64_t(b) * a.L + pos) * a.sq_bw + int64_t(hk * a.G + g) * a.sq_h + c * 8;
+      } else {
+        const int beam = gr / TG, rem = gr % TG, t = rem / a.G, g = rem % a.G;
+        src = a.q + (int64_t(b) * a.W + beam) * a.sq_bw + int64_t(t) * a.sq_t + int64_t(hk * a.G + g) * a.sq_h + c * 8;
+      }
       cp_async16(dst, src);
     } else {
       *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
     }
   }
-  const int nkb = (a.L + kBN - 1) / kBN;
+  int nkeys = a.L;
+  if constexpr (CAUSAL) nkeys = min(a.L, (min(R - 1, row0 + kBM - 1)) / a.G + 1);
+  const int nkb = (nkeys + kBN - 1) / kBN;
   auto load_kv = [&](int kb, int buf) {
     for (int i = tid; i < kBN * CH; i += kThreads) {
       const int r = i / CH, c = i % CH;
@@ -105,6 +116,8 @@ __global__ void __launch_bounds__(kThreads) prefix_attention_kernel(const AttnAr
   cp_async_commit();
 
   const int g = lane >> 2, tq = lane & 3;
+  // causal: positions of this thread's two rows
+  const int cpos0 = (row0 + warp * 16 + g) / a.G, cpos1 = (row0 + warp * 16 + g + 8) / a.G;
   float o[D / 8][4];
 #pragma unroll
   for (int j = 0; j < D / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
@@ -148,6 +161,13 @@ __global__ void __launch_bounds__(kThreads) prefix_attention_kernel(const AttnAr
       s[j][1] = s[j][1] * a.scale_log2 + mb;
       s[j][2] = s[j][2] * a.scale_log2 + ma;
       s[j][3] = s[j][3] * a.scale_log2 + mb;
+      if constexpr (CAUSAL) {
+        const int key = kb * kBN + j * 8 + tq * 2;
+        if (key > cpos0) s[j][0] = -INFINITY;
+        if (key + 1 > cpos0) s[j][1] = -INFINITY;
+        if (key > cpos1) s[j][2] = -INFINITY;
+        if (key + 1 > cpos1) s[j][3] = -INFINITY;
+      }
       mx0 = fmaxf(mx0, fmaxf(s[j][0], s[j][1]));
       mx1 = fmaxf(mx1, fmaxf(s[j][2], s[j][3]));
     }
@@ -203,6 +223,30 @@ __global__ void __launch_bounds__(kThreads) prefix_attention_kernel(const AttnAr
   l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
 
+  if constexpr (CAUSAL) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int gr = row0 + warp * 16 + g + half * 8;
+      if (gr >= R) continue;
+      const int pos = gr / a.G, gg = gr % a.G;
+      const float inv = 1.f / (half ? l1 : l0);
+      const int64_t trow = int64_t(b) * a.L + pos;
+#pragma unroll
+      for (int j = 0; j < D / 8; ++j) {
+        const int col = j * 8 + tq * 2;
+        float v0 = o[j][half * 2] * inv, v1 = o[j][half * 2 + 1] * inv;
+        if (a.gate) {
+          const __nv_bfloat162 gv =
+              *reinterpret_cast<const __nv_bfloat162*>(a.gate + trow * a.sg_bw + int64_t(hk * a.G + gg) * a.sg_h + col);
+          v0 = bf16r(v0) * bf16r(sigmoid_f(__low2float(gv)));
+          v1 = bf16r(v1) * bf16r(sigmoid_f(__high2float(gv)));
+        }
+        *reinterpret_cast<__nv_bfloat162*>(a.out + trow * a.so_bw + int64_t(hk * a.G + gg) * a.so_h + col) =
+            __floats2bfloat162_rn(v0, v1);
+      }
+    }
+    return;
+  }
   // ---- suffix scores: row (beam, t, g) attends to its beam's keys s <= t -----------
   for (int i = 0; i < 16; ++i) {
     const int wr = warp * 16 + i;
@@ -260,7 +304,7 @@ __global__ void __launch_bounds__(kThreads) prefix_attention_kernel(const AttnAr
       v0 *= inv;
       v1 *= inv;
       if (a.gate) {
-        const __nv_bfloat16* gp = a.gate + brow * a.sg_bw + int64_t(t) * a.sg_t + int64_t(hk * a.G + gg) * D + col;
+        const __nv_bfloat16* gp = a.gate + brow * a.sg_bw + int64_t(t) * a.sg_t + int64_t(hk * a.G + gg) * a.sg_h + col;
         const __nv_bfloat162 gv = *reinterpret_cast<const __nv_bfloat162*>(gp);
         v0 = bf16r(v0) * bf16r(sigmoid_f(__low2float(gv)));
         v1 = bf16r(v1) * bf16r(sigmoid_f(__high2float(gv)));
@@ -271,15 +315,15 @@ __global__ void __launch_bounds__(kThreads) prefix_attention_kernel(const AttnAr
   }
 }
 
-template <int D>
+template <int D, bool CAUSAL = false>
 int launch_attn(const AttnArgs& a, cudaStream_t stream) {
   const size_t smem = AttnSmem<D>::bytes;
-  auto kern = prefix_attention_kernel<D>;
+  auto kern = prefix_attention_kernel<D, CAUSAL>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess) {
-    set_error("prefix attention: cannot reserve %zu bytes of shared memory", smem);
+    set_error("attention: cannot reserve %zu bytes of shared memory", smem);
     return KADLLM_ECUDA;
   }
-  const int64_t R = int64_t(a.W) * a.T * a.G;
+  const int64_t R = CAUSAL ? int64_t(a.L) * a.G : int64_t(a.W) * a.T * a.G;
   dim3 grid(unsigned((R + kBM - 1) / kBM), unsigned(a.B * a.HK));
   kern<<<grid, kThreads, smem, stream>>>(a);
   KB_CHECK_LAUNCH("prefix attention launch");
@@ -296,7 +340,7 @@ extern "C" int kadllm_prefix_attention(
     int64_t spk_l, int64_t spk_h, const void* prefix_v, int64_t spv_b, int64_t spv_l, int64_t spv_h,
     const void* suffix_k, int64_t ssk_bw, int64_t ssk_t, int64_t ssk_h, const void* suffix_v,
     int64_t ssv_bw, int64_t ssv_t, int64_t ssv_h, const void* prefix_mask, const void* gate,
-    int64_t sg_bw, int64_t sg_t, void* out, int64_t so_bw, int64_t so_t, int64_t so_h, int dtype,
+    int64_t sg_bw, int64_t sg_t, int64_t sg_h, void* out, int64_t so_bw, int64_t so_t, int64_t so_h, int dtype,
     int64_t batch, int64_t beam_width, int64_t steps, int64_t heads, int64_t kv_heads,
     int64_t prefix_len, int64_t head_dim, float scale, void* stream) {
   using namespace kb;
@@ -318,7 +362,7 @@ extern "C" int kadllm_prefix_attention(
   KB_REQUIRE((reinterpret_cast<uintptr_t>(suffix_k) & 3) == 0 && (reinterpret_cast<uintptr_t>(suffix_v) & 3) == 0 &&
                  (reinterpret_cast<uintptr_t>(out) & 3) == 0 && (reinterpret_cast<uintptr_t>(gate) & 3) == 0 &&
                  even(ssk_bw) && even(ssk_t) && even(ssk_h) && even(ssv_bw) && even(ssv_t) && even(ssv_h) &&
-                 even(so_bw) && even(so_t) && even(so_h) && even(sg_bw) && even(sg_t),
+                 even(so_bw) && even(so_t) && even(so_h) && even(sg_bw) && even(sg_t) && even(sg_h),
              KADLLM_EINVAL, "prefix attention: suffix / gate / output strides must be even and 4-byte aligned");
   AttnArgs a{};
   a.q = static_cast<const __nv_bfloat16*>(q); a.sq_bw = sq_bw; a.sq_t = sq_t; a.sq_h = sq_h;
@@ -327,7 +371,7 @@ extern "C" int kadllm_prefix_attention(
   a.sk = static_cast<const __nv_bfloat16*>(suffix_k); a.ssk_bw = ssk_bw; a.ssk_t = ssk_t; a.ssk_h = ssk_h;
   a.sv = static_cast<const __nv_bfloat16*>(suffix_v); a.ssv_bw = ssv_bw; a.ssv_t = ssv_t; a.ssv_h = ssv_h;
   a.mask = static_cast<const uint8_t*>(prefix_mask);
-  a.gate = static_cast<const __nv_bfloat16*>(gate); a.sg_bw = sg_bw; a.sg_t = sg_t;
+  a.gate = static_cast<const __nv_bfloat16*>(gate); a.sg_bw = sg_bw; a.sg_t = sg_t; a.sg_h = sg_h;
   a.out = static_cast<__nv_bfloat16*>(out); a.so_bw = so_bw; a.so_t = so_t; a.so_h = so_h;
   a.B = int(batch); a.W = int(beam_width); a.T = int(steps); a.H = int(heads); a.HK = int(kv_heads);
   a.G = int(heads / kv_heads); a.L = int(prefix_len);
@@ -340,6 +384,43 @@ extern "C" int kadllm_prefix_attention(
     case 256: return launch_attn<256>(a, s);
     default:
       set_error("prefix attention: head_dim %lld not in {32, 64, 128, 256}", (long long)head_dim);
+      return KADLLM_EUNSUPPORTED;
+  }
+}
+
+extern "C" int kadllm_causal_attention(const void* q, int64_t sq_row, int64_t sq_h, const void* k, int64_t sk_b,
+                                       int64_t sk_l, int64_t sk_h, const void* v, int64_t sv_b, int64_t sv_l,
+                                       int64_t sv_h, const void* gate, int64_t sg_row, int64_t sg_h, void* out,
+                                       int64_t so_row, int64_t so_h, int64_t batch, int64_t length, int64_t heads,
+                                       int64_t kv_heads, int64_t head_dim, float scale, void* stream) {
+  using namespace kb;
+  KB_REQUIRE(q && k && v && out, KADLLM_EINVAL, "causal attention: null pointer");
+  KB_REQUIRE(batch >= 1 && length >= 1 && heads >= 1 && kv_heads >= 1 && heads % kv_heads == 0, KADLLM_EINVAL,
+             "causal attention: bad dimensions");
+  KB_REQUIRE(batch * kv_heads <= 65535, KADLLM_EINVAL, "causal attention: too many (request, kv head) pairs");
+  KB_REQUIRE(aligned16(q) && aligned16(k) && aligned16(v) && sq_row % 8 == 0 && sq_h % 8 == 0 && sk_b % 8 == 0 &&
+                 sk_l % 8 == 0 && sk_h % 8 == 0 && sv_b % 8 == 0 && sv_l % 8 == 0 && sv_h % 8 == 0,
+             KADLLM_EINVAL, "causal attention: rows must be 16-byte aligned");
+  KB_REQUIRE((reinterpret_cast<uintptr_t>(out) & 3) == 0 && (reinterpret_cast<uintptr_t>(gate) & 3) == 0 &&
+                 so_row % 2 == 0 && so_h % 2 == 0 && sg_row % 2 == 0 && sg_h % 2 == 0,
+             KADLLM_EINVAL, "causal attention: gate / output strides must be even");
+  AttnArgs a{};
+  a.q = static_cast<const __nv_bfloat16*>(q); a.sq_bw = sq_row; a.sq_t = 0; a.sq_h = sq_h;
+  a.pk = static_cast<const __nv_bfloat16*>(k); a.spk_b = sk_b; a.spk_l = sk_l; a.spk_h = sk_h;
+  a.pv = static_cast<const __nv_bfloat16*>(v); a.spv_b = sv_b; a.spv_l = sv_l; a.spv_h = sv_h;
+  a.gate = static_cast<const __nv_bfloat16*>(gate); a.sg_bw = sg_row; a.sg_t = 0; a.sg_h = sg_h;
+  a.out = static_cast<__nv_bfloat16*>(out); a.so_bw = so_row; a.so_t = 0; a.so_h = so_h;
+  a.B = int(batch); a.W = 1; a.T = 1; a.H = int(heads); a.HK = int(kv_heads); a.G = int(heads / kv_heads);
+  a.L = int(length);
+  a.scale_log2 = scale * kLog2e;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (head_dim) {
+    case 32: return launch_attn<32, true>(a, s);
+    case 64: return launch_attn<64, true>(a, s);
+    case 128: return launch_attn<128, true>(a, s);
+    case 256: return launch_attn<256, true>(a, s);
+    default:
+      set_error("causal attention: head_dim %lld not in {32, 64, 128, 256}", (long long)head_dim);
       return KADLLM_EUNSUPPORTED;
   }
 }

@@ -1,0 +1,277 @@
+"""Native BF16 execution of the hybrid Qwen3.5 stack for GRBeam.
+
+``HybridModel`` holds the weights packed for this pipeline (one input GEMM per
+token mixer and per MLP) and runs
+
+* ``prefill(ids)``: the prompt through every layer (conv + chunked gated delta
+  rule for GDN layers, causal flash attention for full-attention layers),
+  producing the first-token logits and the immutable, request-sized prefix
+  (conv state, recurrent state, K/V) exactly where the reference keeps them
+  (``Qwen35GRBeamAdapter.prefill``, ``src/kadllm/adapters/qwen3_5.py:235-262``);
+* ``decode(history, state)``: suffix replay of every beam from the shared
+  prefix (``Qwen35GRBeamAdapter.decode``, ``src/kadllm/adapters/qwen3_5.py:333-364``)
+  through the fused GDN mixer and the shared-prefix attention kernels.
+
+Token mixers, norms, activations, attention and selection are hand-written
+sm_100a kernels (``csrc/``); the plain projections are cuBLAS BF16 GEMMs
+issued through ``torch.nn.functional.linear``.  Everything stays on the GPU;
+there is no CPU path.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from . import _lib
+from .config import LINEAR, HybridConfig
+
+BF16 = torch.bfloat16
+
+
+@dataclass
+class GDNLayer:
+    w_in: torch.Tensor      # [conv_dim + value_dim + 2*HV, H]: qkv | z | b | a
+    w_out: torch.Tensor     # [H, value_dim]
+    conv_w: torch.Tensor    # [conv_dim, 4]
+    a_log: torch.Tensor     # [HV] f32
+    dt_bias: torch.Tensor   # [HV] f32
+    norm_w: torch.Tensor    # [V] f32
+
+
+@dataclass
+class AttnLayer:
+    w_in: torch.Tensor      # [(2*Hq + 2*HK) * D, H]: (q|gate) per head | k | v
+    w_o: torch.Tensor       # [H, Hq*D]
+    q_norm: torch.Tensor    # [D] f32
+    k_norm: torch.Tensor    # [D] f32
+
+
+@dataclass
+class Layer:
+    kind: str
+    mixer: GDNLayer | AttnLayer
+    input_ln: torch.Tensor  # [H] f32
+    post_ln: torch.Tensor   # [H] f32
+    w_gu: torch.Tensor      # [2*I, H]: gate | up
+    w_down: torch.Tensor    # [H, I]
+
+
+@dataclass(frozen=True)
+class HybridPrefix:
+    """Immutable request-sized prefix (``Qwen35Prefix``, ``src/kadllm/adapters/qwen3_5.py:21-26``).
+
+    ``layers[i]`` is (conv_state [B, conv_dim, 4], recurrent_state [B, HV, K, V])
+    for GDN layers and (K, V) as [B, L, HK, D] views of [B, HK, L, D] caches
+    for attention layers -- the reference's layouts and BF16 dtypes.
+    """
+
+    length: int
+    batch: int
+    owner: object
+    layers: tuple
+
+
+class HybridModel:
+    def __init__(self, cfg: HybridConfig, weights: dict[str, torch.Tensor], device=None):
+        cfg.validate()
+        self.cfg = cfg
+        dev = torch.device(device) if device is not None else next(iter(weights.values())).device
+        if dev.type != "cuda":
+            raise RuntimeError("kadllm_b200 runs on CUDA devices only")
+        self.device = dev
+        _lib.lib()  # fail loudly now if the CUDA library is missing
+
+        def bf(name):
+            return weights[name].to(device=dev, dtype=BF16).contiguous()
+
+        def f32(name):
+            return weights[name].to(device=dev, dtype=torch.float32).contiguous()
+
+        self.embed = bf("embed_tokens.weight")
+        self.lm_head = bf("lm_head.weight") if "lm_head.weight" in weights else self.embed
+        self.final_norm = f32("norm.weight")
+        self.layers: list[Layer] = []
+        for i, kind in enumerate(cfg.layer_types):
+            p = f"layers.{i}."
+            if kind == LINEAR:
+                q = p + "linear_attn."
+                mixer = GDNLayer(
+                    w_in=torch.cat([bf(q + "in_proj_qkv.weight"), bf(q + "in_proj_z.weight"),
+                                    bf(q + "in_proj_b.weight"), bf(q + "in_proj_a.weight")]).contiguous(),
+                    w_out=bf(q + "out_proj.weight"),
+                    conv_w=bf(q + "conv1d.weight").reshape(cfg.conv_dim, -1).contiguous(),
+                    a_log=f32(q + "A_log"), dt_bias=f32(q + "dt_bias"), norm_w=f32(q + "norm.weight"))
+            else:
+                q = p + "self_attn."
+                mixer = AttnLayer(
+                    w_in=torch.cat([bf(q + "q_proj.weight"), bf(q + "k_proj.weight"),
+                                    bf(q + "v_proj.weight")]).contiguous(),
+                    w_o=bf(q + "o_proj.weight"), q_norm=f32(q + "q_norm.weight"),
+                    k_norm=f32(q + "k_norm.weight"))
+            self.layers.append(Layer(
+                kind=kind, mixer=mixer, input_ln=f32(p + "input_layernorm.weight"),
+                post_ln=f32(p + "post_attention_layernorm.weight"),
+                w_gu=torch.cat([bf(p + "mlp.gate_proj.weight"), bf(p + "mlp.up_proj.weight")]).contiguous(),
+                w_down=bf(p + "mlp.down_proj.weight")))
+        self._rope_len = 0
+        self._cos = self._sin = None
+        self.owner = object()
+
+    # ------------------------------------------------------------------ helpers
+    def _stream(self):
+        return _lib.stream(self.device)
+
+    def _rope(self, n: int):
+        """cos/sin tables [n, rotary_dim] in BF16, computed like
+        ``Qwen3_5TextRotaryEmbedding`` (fp32 inv_freq x position, cos/sin, cast)."""
+        if n > self._rope_len:
+            n = max(n, 2 * self._rope_len, 4096)
+            rd = self.cfg.rotary_dim
+            inv = 1.0 / (self.cfg.rope_theta ** (torch.arange(0, rd, 2, dtype=torch.int64, device=self.device)
+                                                 .float() / rd))
+            pos = torch.arange(n, device=self.device, dtype=torch.float32)
+            freqs = pos[:, None] * inv[None, :]
+            emb = torch.cat([freqs, freqs], -1)
+            self._cos = emb.cos().to(BF16).contiguous()
+            self._sin = emb.sin().to(BF16).contiguous()
+            self._rope_len = n
+        return self._cos, self._sin
+
+    def _embed(self, ids: torch.Tensor):
+        rows = ids.numel()
+        H = self.cfg.hidden_size
+        x = torch.empty(rows, H, dtype=BF16, device=self.device)
+        normed = torch.empty_like(x)
+        _lib.call("kadllm_embed_rmsnorm", ids.data_ptr(), self.embed.data_ptr(), self.cfg.vocab_size,
+                  self.layers[0].input_ln.data_ptr(), self.cfg.rms_norm_eps, x.data_ptr(), normed.data_ptr(),
+                  rows, H, self._stream())
+        return x, normed
+
+    def _add_norm(self, x, delta, weight, normed, rows=None, step=1, offset=0):
+        rows = x.shape[0] if rows is None else rows
+        _lib.call("kadllm_add_rmsnorm", x.data_ptr(), _lib.ptr(delta), 0 if delta is None else delta.stride(0),
+                  weight.data_ptr(), self.cfg.rms_norm_eps, normed.data_ptr(), rows, step, offset,
+                  self.cfg.hidden_size, self._stream())
+
+    def _mlp(self, layer: Layer, normed):
+        gu = F.linear(normed, layer.w_gu)
+        inter = self.cfg.intermediate_size
+        act = torch.empty(gu.shape[0], inter, dtype=BF16, device=self.device)
+        _lib.call("kadllm_silu_mul", gu.data_ptr(), gu.stride(0), inter, act.data_ptr(), gu.shape[0],
+                  self._stream())
+        return F.linear(act, layer.w_down)
+
+    def _qk_rope(self, P, rows, pos_base, rows_per_seq, q_out, k_out, k_strides, v_out, v_strides, mixer):
+        c = self.cfg
+        cos, sin = self._rope(pos_base + rows_per_seq + 1)
+        _lib.call("kadllm_qk_norm_rope", P.data_ptr(), P.stride(0), c.num_attention_heads, c.num_key_value_heads,
+                  c.head_dim, mixer.q_norm.data_ptr(), mixer.k_norm.data_ptr(), c.rms_norm_eps, cos.data_ptr(),
+                  sin.data_ptr(), c.rotary_dim, None, pos_base, rows_per_seq, q_out.data_ptr(),
+                  c.num_attention_heads * c.head_dim, c.head_dim, k_out.data_ptr(), *k_strides, v_out.data_ptr(),
+                  *v_strides, rows, self._stream())
+
+    # ------------------------------------------------------------------ prefill
+    @torch.no_grad()
+    def prefill(self, ids: torch.Tensor):
+        """ids [B, L] -> (logits [B, V] bf16, HybridPrefix)."""
+        c = self.cfg
+        B, L = ids.shape
+        ids = ids.to(device=self.device, dtype=torch.int64).contiguous()
+        R = B * L
+        x, normed = self._embed(ids.reshape(-1))
+        s = self._stream()
+        prefix = []
+        hk, D, hq = c.num_key_value_heads, c.head_dim, c.num_attention_heads
+        for i, layer in enumerate(self.layers):
+            m = layer.mixer
+            P = F.linear(normed, m.w_in)
+            if layer.kind == LINEAR:
+                qkv = torch.empty(R, c.conv_dim, dtype=BF16, device=self.device)
+                conv_state = torch.empty(B, c.conv_dim, 4, dtype=BF16, device=self.device)
+                _lib.call("kadllm_conv1d_prefill", P.data_ptr(), P.stride(0), m.conv_w.data_ptr(), qkv.data_ptr(),
+                          qkv.stride(0), conv_state.data_ptr(), B, L, c.conv_dim, s)
+                out = torch.empty(R, c.value_dim, dtype=BF16, device=self.device)
+                rec = torch.empty(B, c.linear_num_value_heads, c.linear_key_head_dim, c.linear_value_head_dim,
+                                  dtype=BF16, device=self.device)
+                _lib.call("kadllm_gdn_prefill", qkv.data_ptr(), qkv.stride(0), P.data_ptr(), P.stride(0), c.conv_dim,
+                          m.a_log.data_ptr(), m.dt_bias.data_ptr(), m.norm_w.data_ptr(), c.rms_norm_eps,
+                          out.data_ptr(), out.stride(0), rec.data_ptr(), B, L, c.linear_num_key_heads,
+                          c.linear_num_value_heads, c.linear_key_head_dim, c.linear_value_head_dim, s)
+                delta = F.linear(out, m.w_out)
+                prefix.append((conv_state, rec))
+            else:
+                q = torch.empty(R, hq, D, dtype=BF16, device=self.device)
+                kc = torch.empty(B, hk, L, D, dtype=BF16, device=self.device)
+                vc = torch.empty_like(kc)
+                cache_strides = (hk * L * D, D, L * D)  # (sequence, position, head)
+                self._qk_rope(P, R, 0, L, q, kc, cache_strides, vc, cache_strides, m)
+                out = torch.empty(R, hq * D, dtype=BF16, device=self.device)
+                gate = P[:, D:]  # gate of head h at column h*2D + D
+                _lib.call("kadllm_causal_attention", q.data_ptr(), hq * D, D, kc.data_ptr(), *kc.stride()[:3],
+                          vc.data_ptr(), *vc.stride()[:3], gate.data_ptr(), P.stride(0), 2 * D, out.data_ptr(),
+                          out.stride(0), D, B, L, hq, hk, D, D ** -0.5, s)
+                delta = F.linear(out, m.w_o)
+                prefix.append((kc.transpose(1, 2), vc.transpose(1, 2)))
+            self._add_norm(x, delta, layer.post_ln, normed)
+            delta = self._mlp(layer, normed)
+            if i + 1 < len(self.layers):
+                self._add_norm(x, delta, self.layers[i + 1].input_ln, normed)
+        last = torch.empty(B, c.hidden_size, dtype=BF16, device=self.device)
+        self._add_norm(x, delta, self.final_norm, last, rows=B, step=L, offset=L - 1)
+        logits = F.linear(last, self.lm_head)
+        return logits, HybridPrefix(L, B, self.owner, tuple(prefix))
+
+    # ------------------------------------------------------------------ decode
+    @torch.no_grad()
+    def decode_hidden(self, history: torch.Tensor, state: HybridPrefix) -> torch.Tensor:
+        """Replay history [B, W, T] -> final-norm hidden of the last position [B*W, H]."""
+        c = self.cfg
+        B, W, T = history.shape
+        BW, R = B * W, B * W * T
+        ids = history.to(device=self.device, dtype=torch.int64).reshape(-1).contiguous()
+        x, normed = self._embed(ids)
+        s = self._stream()
+        hk, D, hq = c.num_key_value_heads, c.head_dim, c.num_attention_heads
+        for i, (layer, cached) in enumerate(zip(self.layers, state.layers)):
+            m = layer.mixer
+            P = F.linear(normed, m.w_in)
+            if layer.kind == LINEAR:
+                out = torch.empty(R, c.value_dim, dtype=BF16, device=self.device)
+                conv_state, rec = cached
+                _lib.call("kadllm_gdn_mixer_replay", P.data_ptr(), P.stride(0), conv_state.data_ptr(),
+                          conv_state.shape[-1], m.conv_w.data_ptr(), rec.data_ptr(), m.a_log.data_ptr(),
+                          m.dt_bias.data_ptr(), m.norm_w.data_ptr(), c.rms_norm_eps, out.data_ptr(), B, W, T,
+                          c.linear_num_key_heads, c.linear_num_value_heads, c.linear_key_head_dim,
+                          c.linear_value_head_dim, s)
+                delta = F.linear(out, m.w_out)
+            else:
+                q = torch.empty(R, hq, D, dtype=BF16, device=self.device)
+                ks = torch.empty(R, hk, D, dtype=BF16, device=self.device)
+                vs = torch.empty_like(ks)
+                suffix_strides = (T * hk * D, hk * D, D)  # (beam row, step, head)
+                self._qk_rope(P, R, state.length, T, q, ks, suffix_strides, vs, suffix_strides, m)
+                pk, pv = cached  # [B, L, HK, D] views
+                out = torch.empty(R, hq * D, dtype=BF16, device=self.device)
+                gate = P[:, D:]
+                _lib.call("kadllm_prefix_attention", q.data_ptr(), T * hq * D, hq * D, D, pk.data_ptr(),
+                          *pk.stride()[:3], pv.data_ptr(), *pv.stride()[:3], ks.data_ptr(), *suffix_strides,
+                          vs.data_ptr(), *suffix_strides, None, gate.data_ptr(), T * P.stride(0), P.stride(0), 2 * D,
+                          out.data_ptr(), T * hq * D, hq * D, D, _lib.DTYPE_CODES[BF16], B, W, T, hq, hk,
+                          state.length, D, D ** -0.5, s)
+                delta = F.linear(out, m.w_o)
+            self._add_norm(x, delta, layer.post_ln, normed)
+            delta = self._mlp(layer, normed)
+            if i + 1 < len(self.layers):
+                self._add_norm(x, delta, self.layers[i + 1].input_ln, normed)
+        last = torch.empty(BW, c.hidden_size, dtype=BF16, device=self.device)
+        self._add_norm(x, delta, self.final_norm, last, rows=BW, step=T, offset=T - 1)
+        return last
+
+    @torch.no_grad()
+    def decode(self, history: torch.Tensor, state: HybridPrefix) -> torch.Tensor:
+        """Replay [B, W, T] suffix tokens; return [B, W, V] logits (BF16)."""
+        B, W, _ = history.shape
+        return F.linear(self.decode_hidden(history, state), self.lm_head).view(B, W, -1)

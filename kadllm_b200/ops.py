@@ -249,7 +249,7 @@ def prefix_attention(
         "kadllm_prefix_attention",
         q.data_ptr(), *q.stride()[:3], prefix_k.data_ptr(), *prefix_k.stride()[:3],
         prefix_v.data_ptr(), *prefix_v.stride()[:3], suffix_k.data_ptr(), *suffix_k.stride()[:3],
-        suffix_v.data_ptr(), *suffix_v.stride()[:3], _lib.ptr(mask), None, 0, 0,
+        suffix_v.data_ptr(), *suffix_v.stride()[:3], _lib.ptr(mask), None, 0, 0, 0,
         out.data_ptr(), *out.stride()[:3], _lib.dtype_code(q), B, beam_width, T, H, HK, L, D,
         scale, _lib.stream(q.device),
     )

@@ -1,0 +1,119 @@
+"""End-to-end GPU parity of the native hybrid pipeline (prefill, decode, search)."""
+
+import numpy as np
+import pytest
+import torch
+
+from kadllm_b200.config import TINY, HybridConfig
+from kadllm_b200.synthetic import numpy_weights, random_prompts
+from oracle import grbeam_oracle as O
+from tests.parity import assert_close_rel, beam_mismatches, bf16_tol, load
+
+pytestmark = pytest.mark.gpu
+
+
+def _hf_tiny():
+    from transformers import Qwen3_5TextConfig
+    from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5TextModel
+
+    w = numpy_weights(TINY, seed=0, init="test")
+    model = Qwen3_5TextModel._from_config(Qwen3_5TextConfig(**TINY.to_hf_kwargs()), dtype=torch.bfloat16)
+    model.load_state_dict({k: torch.from_numpy(v).to(torch.bfloat16) for k, v in w.items()})
+    model = model.eval().cuda()
+    head = torch.nn.Linear(TINY.hidden_size, TINY.vocab_size, bias=False).eval()
+    head.weight = model.embed_tokens.weight
+    return model, head
+
+
+def test_tiny_model_matches_reference_golden():
+    """BASELINE config 1 architecture, BF16, through the drop-in adapter + search."""
+    from kadllm_b200 import grbeam_search
+    from kadllm_b200.adapters import Qwen35GRBeamAdapter
+
+    g = load("model_bf16.npz")
+    model, head = _hf_tiny()
+    adapter = Qwen35GRBeamAdapter(model, head)
+    ids = torch.from_numpy(g["ids"]).cuda()
+    pre = adapter.prefill(ids)
+    assert_close_rel(pre.logits.float().cpu().numpy(), g["prefill_logits"], rel=2e-2, what="prefill logits")
+    for i, (a, b) in enumerate(pre.state.layers):
+        assert_close_rel(a.float().cpu().numpy(), g[f"layer{i}_a"], rel=2e-2, what=f"layer {i} a")
+        assert_close_rel(b.float().cpu().numpy(), g[f"layer{i}_b"], rel=2e-2, what=f"layer {i} b")
+    for step in (1, 2):
+        hist = torch.from_numpy(g[f"decode{step}_history"]).cuda()
+        got = adapter.decode(hist, pre.state).float().cpu().numpy()
+        assert_close_rel(got, g[f"decode{step}_logits"], rel=2e-2, what=f"decode step {step}")
+    res = grbeam_search(adapter, ids, [8, 8, 8])
+    tol = 2 * bf16_tol(g["decode2_logits"])
+    assert beam_mismatches(res.tokens.cpu().numpy(), res.scores.cpu().numpy(), g["tokens"], g["scores"], tol) == []
+    assert bool(res.valid.all())
+
+
+MID = HybridConfig(
+    vocab_size=2048, hidden_size=1024, intermediate_size=1024,
+    layer_types=("linear_attention", "linear_attention", "linear_attention", "full_attention"),
+    num_attention_heads=8, num_key_value_heads=2, head_dim=256,
+    linear_num_key_heads=16, linear_num_value_heads=16, linear_key_head_dim=128, linear_value_head_dim=128,
+    rope_theta=10_000_000.0,
+)
+
+
+@pytest.fixture(scope="module")
+def mid():
+    from kadllm_b200.model import HybridModel
+
+    w = {k: O.bf16(v) for k, v in numpy_weights(MID, seed=1, init="test").items()}
+    engine = HybridModel(MID, {k: torch.from_numpy(v) for k, v in w.items()}, device="cuda")
+    return engine, O.HybridOracle(MID, w, "bf16")
+
+
+def test_qwen35_head_dims_prefill_matches_oracle(mid):
+    """0.8B head dims (GDN 16x128, attention 8q/2kv x 256, rotary 64), ragged last chunk."""
+    engine, orc = mid
+    ids = random_prompts(2, 100, MID.vocab_size, seed=4)
+    logits, state = engine.prefill(torch.from_numpy(ids).cuda())
+    ref_logits, ref_layers = orc.prefill(ids)
+    assert_close_rel(logits.float().cpu().numpy(), ref_logits, rel=2e-2, what="prefill logits")
+    for i, ((a, b), (ra, rb)) in enumerate(zip(state.layers, ref_layers)):
+        assert_close_rel(a.float().cpu().numpy(), ra, rel=2e-2, what=f"layer {i} a")
+        assert_close_rel(b.float().cpu().numpy(), rb, rel=2e-2, what=f"layer {i} b")
+
+
+def test_qwen35_head_dims_decode_and_search_match_oracle(mid):
+    from kadllm_b200 import grbeam_search
+    from kadllm_b200.adapters import NativeGRBeamAdapter
+
+    engine, orc = mid
+    ids = random_prompts(2, 70, MID.vocab_size, seed=5)
+    _, ref_layers = orc.prefill(ids)
+    tids = torch.from_numpy(ids).cuda()
+    _, state = engine.prefill(tids)
+    hist = np.random.default_rng(0).integers(0, MID.vocab_size, (2, 8, 3))
+    got = engine.decode(torch.from_numpy(hist).cuda(), state).float().cpu().numpy()
+    ref = orc.decode(hist, 70, ref_layers)
+    assert_close_rel(got, ref, rel=2e-2, what="decode logits T=3")
+    res = grbeam_search(NativeGRBeamAdapter(engine), tids, [8, 8, 8])
+    tok, sc, _ = O.grbeam_search(orc, ids, [8, 8, 8])
+    tol = 4 * bf16_tol(ref)
+    assert beam_mismatches(res.tokens.cpu().numpy(), res.scores.cpu().numpy(), tok, sc, tol) == []
+
+
+def test_prefix_is_immutable_and_owner_checked(mid):
+    from kadllm_b200.adapters import NativeGRBeamAdapter
+
+    engine, _ = mid
+    adapter = NativeGRBeamAdapter(engine)
+    ids = torch.from_numpy(random_prompts(1, 40, MID.vocab_size, seed=6)).cuda()
+    pre = adapter.prefill(ids)
+    snap = [tuple(t.clone() for t in layer) for layer in pre.state.layers]
+    adapter.decode(torch.zeros(1, 4, 2, dtype=torch.long, device="cuda"), pre.state)
+    for layer, old in zip(pre.state.layers, snap):
+        for t, o in zip(layer, old):
+            assert torch.equal(t, o)
+    with pytest.raises(ValueError):
+        adapter.decode(torch.zeros(2, 4, 2, dtype=torch.long, device="cuda"), pre.state)
+    other = NativeGRBeamAdapter(type(engine).__new__(type(engine)))
+    other._owner = object()
+    other.engine = engine
+    with pytest.raises(ValueError):
+        other.decode(torch.zeros(1, 4, 2, dtype=torch.long, device="cuda"), pre.state)
