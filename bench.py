@@ -1,0 +1,343 @@
+"""GRBeam benchmark: requests/s on the Qwen3.5-0.8B-shaped hybrid (B200).
+
+Workload (BASELINE config 2 per GPU): random-init BF16 weights N(0, 0.02)
+(seed 0), 32 requests of 1024 uniform-random prompt tokens per GPU, beam width
+256, 3 output tokens (prefill + 2 decode steps + selection), full 248,320-token
+vocabulary.  One step = one ``grbeam_search`` call over one 32-request batch
+per GPU; with N GPUs every rank runs its own batch (weak scaling: requests
+shard across GPUs with replicated weights) and the results are all-gathered
+over NCCL at the end of each step.
+
+``value``   requests/s with the prompts already resident in HBM;
+``e2e``     the same through the public API from pinned host buffers, with the
+            prompt upload and the token / score download inside the timed region.
+Timing: CUDA events on the launching stream between barriers, max over ranks.
+The working set (1.5 GB of weights, GBs of activations / logits) exceeds the
+126 MB L2, so no explicit flush is needed between steps.
+
+``--impl reference`` times the reference algorithm's CPU restatement (the
+numpy oracle port of Kadllm's torch path) on the host cores for one request
+per step; rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+BATCH, PROMPT, BEAM, DEPTH = 32, 1024, 256, 3
+METRIC = "requests/s (Qwen3.5-0.8B, bs32, prefix 1024, beam 256, 3 tokens) at 1/2/4/8 B200"
+WORKLOAD = "qwen3.5-0.8b-shaped hybrid, bf16 random N(0,0.02) seed 0, B=32/GPU, prefix 1024, beam 256, depth 3"
+
+
+def algorithmic_flops(cfg, B=BATCH, L=PROMPT, W=BEAM, depth=DEPTH) -> float:
+    """Dense FLOPs of one GRBeam call: linears 2*params*tokens, attention
+    QK^T + PV, GDN state products, LM head (prefill last token + each decode row)."""
+    H, I = cfg.hidden_size, cfg.intermediate_size
+    gdn_params = cfg.gdn_in_dim * H + H * cfg.value_dim
+    attn_params = cfg.attn_in_dim * H + H * cfg.num_attention_heads * cfg.head_dim
+    n_gdn = sum(1 for k in cfg.layer_types if k == "linear_attention")
+    n_attn = cfg.num_layers - n_gdn
+    per_token = 2 * (n_gdn * gdn_params + n_attn * attn_params + cfg.num_layers * 3 * H * I)
+    decode_rows = sum(B * W * t for t in range(1, depth))  # suffix replay rows
+    flops = per_token * (B * L + decode_rows)
+    hq, d = cfg.num_attention_heads, cfg.head_dim
+    flops += n_attn * 4 * B * hq * d * L * L / 2  # causal prefill attention
+    flops += n_attn * sum(4 * B * W * t * hq * d * (L + t) for t in range(1, depth))
+    hv, dk, dv = cfg.linear_num_value_heads, cfg.linear_key_head_dim, cfg.linear_value_head_dim
+    flops += n_gdn * B * hv * L * (6 * dk * dv + 4 * 64 * (dk + dv))  # chunked scan
+    flops += n_gdn * sum(B * W * t * hv * 2 * 2 * dk * dv for t in range(1, depth))
+    flops += 2 * H * cfg.vocab_size * (B + B * W * (depth - 1))
+    return float(flops)
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.path = ROOT / "gpurun_out" / f"clocks_gpu{gpu}.csv"
+
+    def __enter__(self):
+        try:
+            self.path.parent.mkdir(exist_ok=True)
+            self.out = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu), "-lms", "200"], stdout=self.out,
+                                         stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.out.close()
+
+    def summary(self) -> dict:
+        if self.proc is None or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        mhz, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(mhz)}
+
+
+def measured_peaks() -> tuple[dict, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text()), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (oracle port of the reference's torch path)
+# ---------------------------------------------------------------------------
+def cpu_reference_sample(weights_np, cfg, seed: int, prompt=PROMPT):
+    """One request through the oracle (fp32, all host threads); returns seconds."""
+    from kadllm_b200.synthetic import random_prompts
+    from oracle import grbeam_oracle as O
+
+    orc = O.HybridOracle(cfg, weights_np, "fp32")
+    ids = random_prompts(1, prompt, cfg.vocab_size, seed=seed)
+    t0 = time.perf_counter()
+    O.grbeam_search(orc, ids, [BEAM] * DEPTH)
+    return time.perf_counter() - t0
+
+
+def numpy_weights_from(model_weights):
+    return {k: v.float().cpu().numpy() for k, v in model_weights.items()}
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    import torch
+
+    from kadllm_b200.config import QWEN35_08B
+    from kadllm_b200.synthetic import numpy_weights
+
+    cfg = QWEN35_08B
+    weights = numpy_weights(cfg, seed=0, init="spec")
+    threads = os.cpu_count() or 1
+    times = []
+    for i in range(args.warmup + args.steps):
+        dt = cpu_reference_sample(weights, cfg, seed=i)
+        if i >= args.warmup:
+            times.append(dt)
+    per_req = statistics.mean(times)
+    value = 1.0 / per_req
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "requests/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_req * 1000, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD + " (CPU sample: 1 request per step)", "global_batch": 1,
+                   "seq_len": PROMPT, "beam": BEAM, "depth": DEPTH, "parallelism": "host cores"},
+        "cpu_baseline": {"value": value, "unit": "requests/s", "cores": threads, "kind": "port",
+                         "sample": "1 request (prefix 1024, beam 256, 3 tokens) per step, numpy oracle fp32, "
+                                   f"OpenBLAS {threads} threads"},
+        "e2e": {"value": value, "unit": "requests/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "torch_threads": torch.get_num_threads(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU leg
+# ---------------------------------------------------------------------------
+def run_native(args, rank: int, world: int, local_rank: int) -> None:
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from kadllm_b200 import _lib, grbeam_search
+    from kadllm_b200.adapters import NativeGRBeamAdapter
+    from kadllm_b200.config import QWEN35_08B
+    from kadllm_b200.model import HybridModel
+    from kadllm_b200.synthetic import random_prompts, torch_weights
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    cfg = QWEN35_08B
+    weights = torch_weights(cfg, seed=0, device=dev)
+    engine = HybridModel(cfg, weights, device=dev)
+    adapter = NativeGRBeamAdapter(engine)
+    ids_host = torch.from_numpy(random_prompts(BATCH, PROMPT, cfg.vocab_size, seed=rank)).pin_memory()
+    ids_dev = ids_host.to(dev)
+    tok_host = torch.empty(BATCH, BEAM, DEPTH, dtype=torch.int64).pin_memory()
+    sc_host = torch.empty(BATCH, BEAM, dtype=torch.float32).pin_memory()
+    widths = [BEAM] * DEPTH
+
+    def gather(res):
+        if world > 1:
+            toks = torch.empty(world * BATCH, BEAM, DEPTH, dtype=torch.int64, device=dev)
+            scs = torch.empty(world * BATCH, BEAM, dtype=torch.float32, device=dev)
+            dist.all_gather_into_tensor(toks, res.tokens.contiguous())
+            dist.all_gather_into_tensor(scs, res.scores.contiguous())
+            return toks, scs
+        return res.tokens, res.scores
+
+    def step_device():
+        return gather(grbeam_search(adapter, ids_dev, widths))
+
+    def step_e2e():
+        ids = ids_host.to(dev, non_blocking=True)
+        res = grbeam_search(adapter, ids, widths)
+        tok_host.copy_(res.tokens, non_blocking=True)
+        sc_host.copy_(res.scores, non_blocking=True)
+        return gather(res)
+
+    def timed(fn, steps):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        launches0 = _lib.launch_count
+        start.record()
+        for _ in range(steps):
+            fn()
+        end.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms = torch.tensor([start.elapsed_time(end)], device=dev)
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return float(ms.item()) / steps, _lib.launch_count - launches0
+
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            step_device()
+        with ClockSampler(local_rank) as clocks:
+            ms, launches = timed(step_device, args.steps)
+        ms_e2e, _ = timed(step_e2e, args.steps)
+        res = grbeam_search(adapter, ids_dev, widths)
+        valid = bool(res.valid.all().item())
+        distinct = all(len({tuple(b) for b in req}) == BEAM for req in res.tokens.cpu().tolist())
+        prof = profile_kernels(engine, adapter, ids_dev, widths, args) if rank == 0 else None
+
+    if rank != 0:
+        return
+    flops = algorithmic_flops(cfg)
+    peaks, peak_kind = measured_peaks()
+    value = world * BATCH / (ms / 1000)
+    line = {
+        "metric": METRIC, "value": value, "unit": "requests/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random prompts, random-init weights)",
+        "config": {"workload": WORKLOAD, "model": "qwen3.5-0.8b-shaped", "global_batch": world * BATCH,
+                   "seq_len": PROMPT, "beam": BEAM, "depth": DEPTH, "parallelism": f"dp{world} (request shards)",
+                   "l2": "working set > 126 MB L2 (weights 1.5 GB, logits 4 GB per step); no flush"},
+        "e2e": {"value": world * BATCH / (ms_e2e / 1000), "unit": "requests/s",
+                "h2d_bytes_per_step": BATCH * PROMPT * 8, "d2h_bytes_per_step": BATCH * BEAM * (DEPTH * 8 + 4)},
+        "gpu_launches": launches,
+        "clocks": clocks.summary(),
+        "path_roofline": {"bound": "tensor", "algorithmic_tflop_per_step": flops / 1e12,
+                          "achieved": flops / (ms / 1000) / 1e12,
+                          "peak": peaks.get("bf16_tflops_sustained"), "unit": "TFLOP/s",
+                          "frac": flops / (ms / 1000) / 1e12 / peaks.get("bf16_tflops_sustained"),
+                          "peak_kind": f"{peak_kind} sustained bf16"},
+        "checks": {"all_valid": valid, "distinct_beams": distinct},
+    }
+    if prof:
+        line["roofline"] = prof["roofline"]
+        line["kernel_ms"] = prof["kernel_ms"]
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(weights, cfg)
+    print(json.dumps(line), flush=True)
+
+
+def profile_kernels(engine, adapter, ids_dev, widths, args):
+    """Per-entry-point device time over one extra search, CUDA events on the
+    launching stream; the dominant kernel's roofline is derived from it."""
+    import torch
+
+    from kadllm_b200 import _lib, grbeam_search
+    from kadllm_b200.roofline import KernelTimer, roofline_for
+
+    timer = KernelTimer()
+    with timer.install():
+        grbeam_search(adapter, ids_dev, widths)
+    torch.cuda.synchronize()
+    totals = timer.totals()
+    peaks, kind = measured_peaks()
+    roof = roofline_for(args.roofline_kernel or max(totals, key=lambda k: totals[k][0]), timer, engine.cfg,
+                        peaks, kind)
+    return {"roofline": roof, "kernel_ms": {k: round(v[0], 3) for k, v in sorted(totals.items())}}
+
+
+def cpu_baseline(weights, cfg) -> dict:
+    """The oracle port on the host cores for one request (fp32)."""
+    w = numpy_weights_from(weights)
+    dt = cpu_reference_sample(w, cfg, seed=123)
+    threads = os.cpu_count() or 1
+    return {"value": 1.0 / dt, "unit": "requests/s", "cores": threads, "kind": "port",
+            "sample": f"1 request (prefix {PROMPT}, beam {BEAM}, {DEPTH} tokens), numpy oracle fp32, "
+                      f"{dt:.1f} s on {threads} host threads"}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["native", "reference"], default="native")
+    ap.add_argument("--roofline-kernel", default=None)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torch.distributed.run")
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    import torch
+    import torch.distributed as dist
+
+    if world > 1:
+        import datetime
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_native(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -62,9 +62,17 @@ def lib() -> ctypes.CDLL:
 _ERRORS = {1: ValueError, 2: TypeError, 3: NotImplementedError, 4: RuntimeError}
 
 
+# kernels launched per successful call of each entry point (for launch accounting)
+LAUNCHES_PER_CALL = {"kadllm_beam_select": 4, "kadllm_beam_select_status": 0}
+launch_count = 0
+
+
 def call(name: str, *args) -> None:
     """Invoke an entry point and map a nonzero status to the reference's exception types."""
+    global launch_count
     rc = getattr(lib(), name)(*args)
+    if not rc:
+        launch_count += LAUNCHES_PER_CALL.get(name, 1)
     if rc:
         msg = lib().kadllm_last_error().decode(errors="replace")
         raise _ERRORS.get(rc, RuntimeError)(msg)

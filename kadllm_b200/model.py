@@ -81,6 +81,8 @@ class HybridModel:
         dev = torch.device(device) if device is not None else next(iter(weights.values())).device
         if dev.type != "cuda":
             raise RuntimeError("kadllm_b200 runs on CUDA devices only")
+        if dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
         self.device = dev
         _lib.lib()  # fail loudly now if the CUDA library is missing
 
@@ -210,8 +212,10 @@ class HybridModel:
                 self._qk_rope(P, R, 0, L, q, kc, cache_strides, vc, cache_strides, m)
                 out = torch.empty(R, hq * D, dtype=BF16, device=self.device)
                 gate = P[:, D:]  # gate of head h at column h*2D + D
-                _lib.call("kadllm_causal_attention", q.data_ptr(), hq * D, D, kc.data_ptr(), *kc.stride()[:3],
-                          vc.data_ptr(), *vc.stride()[:3], gate.data_ptr(), P.stride(0), 2 * D, out.data_ptr(),
+                # cache [B, HK, L, D]: strides passed as (request, position, head)
+                _lib.call("kadllm_causal_attention", q.data_ptr(), hq * D, D, kc.data_ptr(), kc.stride(0),
+                          kc.stride(2), kc.stride(1), vc.data_ptr(), vc.stride(0), vc.stride(2), vc.stride(1),
+                          gate.data_ptr(), P.stride(0), 2 * D, out.data_ptr(),
                           out.stride(0), D, B, L, hq, hk, D, D ** -0.5, s)
                 delta = F.linear(out, m.w_o)
                 prefix.append((kc.transpose(1, 2), vc.transpose(1, 2)))

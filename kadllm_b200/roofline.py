@@ -1,0 +1,112 @@
+"""Per-kernel timing and roofline accounting for the benchmark.
+
+``KernelTimer`` brackets every C-ABI call with CUDA events on the launching
+(current) stream; ``work_of`` gives the algorithmic work of one call from its
+size arguments -- FLOPs for the tensor-core kernels, compulsory HBM bytes for
+the streaming ones -- so achieved = work / event time can be compared with the
+measured B200 peaks.
+"""
+
+from __future__ import annotations
+
+import contextlib
+
+import torch
+
+from . import _lib
+
+
+def work_of(name: str, args: tuple) -> tuple[str, float] | None:
+    """(bound, algorithmic work) of one call: ("tensor", FLOPs) or ("hbm", bytes)."""
+    if name == "kadllm_gdn_prefill":
+        B, L, H, HV, DK, DV = args[12:18]
+        chunks = -(-L // 64)
+        per_chunk = 2 * 64 * (2 * 64 * DK + 3 * DK * DV + 2 * 64 * DV)
+        return "tensor", float(B * HV * chunks * per_chunk)
+    if name == "kadllm_causal_attention":
+        B, L, H, HK, D = args[17:22]
+        return "tensor", float(4 * B * H * D * L * (L + 1) / 2)
+    if name == "kadllm_prefix_attention":
+        B, W, T, H, HK, L, D = args[30:37]
+        return "tensor", float(4 * B * W * T * H * D * L + 4 * B * W * H * D * T * (T + 1) / 2)
+    if name == "kadllm_gdn_mixer_replay":
+        B, W, T, H, HV, DK, DV = args[11:18]
+        R = B * W * T
+        conv_dim = 2 * H * DK + HV * DV
+        read = R * (conv_dim + HV * DV + 2 * HV) * 2 + B * HV * DK * DV * 2 + B * conv_dim * 4 * 2
+        return "hbm", float(read + R * HV * DV * 2)
+    if name == "kadllm_beam_select":
+        B, Wp, V, W, depth = args[10:15]
+        esz = 4 if args[1] == 0 else 2
+        return "hbm", float(B * Wp * V * esz)
+    if name == "kadllm_conv1d_prefill":
+        B, L, C = args[6:9]
+        return "hbm", float(B * L * C * 2 * 2)
+    if name == "kadllm_silu_mul":
+        inter, rows = args[2], args[4]
+        return "hbm", float(rows * inter * 2 * 3)
+    if name == "kadllm_add_rmsnorm":
+        rows, H = args[6], args[9]
+        return "hbm", float(rows * H * 2 * (4 if args[1] else 2))
+    return None
+
+
+class KernelTimer:
+    def __init__(self):
+        self.records: list[tuple[str, tuple, torch.cuda.Event, torch.cuda.Event]] = []
+
+    @contextlib.contextmanager
+    def install(self):
+        original = _lib.call
+
+        def timed_call(name, *args):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            original(name, *args)
+            e.record()
+            self.records.append((name, args, s, e))
+
+        _lib.call = timed_call
+        try:
+            yield self
+        finally:
+            _lib.call = original
+
+    def totals(self) -> dict[str, tuple[float, int]]:
+        """name -> (total ms, calls); synchronise first."""
+        out: dict[str, list] = {}
+        for name, _, s, e in self.records:
+            t = out.setdefault(name, [0.0, 0])
+            t[0] += s.elapsed_time(e)
+            t[1] += 1
+        return {k: (v[0], v[1]) for k, v in out.items()}
+
+
+def roofline_for(name: str, timer: KernelTimer, cfg, peaks: dict, peak_kind: str) -> dict:
+    """Roofline of kernel `name` over the timed calls: achieved = work / duration."""
+    work, ms, calls, bound = 0.0, 0.0, 0, None
+    for n, args, s, e in timer.records:
+        if n != name:
+            continue
+        w = work_of(n, args)
+        if w is None:
+            continue
+        bound, amount = w
+        work += amount
+        ms += s.elapsed_time(e)
+        calls += 1
+    if not calls:
+        return {"kernel": name, "bound": None, "achieved": None, "peak": None, "unit": None, "frac": None,
+                "traffic": None}
+    if bound == "tensor":
+        achieved = work / (ms / 1e3) / 1e12
+        peak = peaks["bf16_tflops"]
+        unit, per_launch = "TFLOP/s", work / calls / 1e12
+    else:
+        achieved = work / (ms / 1e3) / 1e9
+        peak = peaks["hbm_gbs"]
+        unit, per_launch = "GB/s", work / calls
+    return {"kernel": name, "bound": "tensor" if bound == "tensor" else "hbm", "achieved": achieved,
+            "peak": peak, "unit": unit, "frac": achieved / peak, "traffic": None, "launches": calls,
+            "avg_launch_ms": ms / calls, "work_per_launch": per_launch,
+            "peak_kind": f"{peak_kind} ({'bf16 burst' if bound == 'tensor' else 'HBM copy'})"}

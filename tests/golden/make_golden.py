@@ -10,7 +10,8 @@ Every fixture records inputs and the reference's outputs:
 * ``model_<dtype>.npz``  tiny hybrid through
   ``Qwen35GRBeamAdapter`` (torch backends) + ``grbeam_search`` with widths
   [8, 8, 8]: prefill logits, every prefix tensor, decode logits for both decode
-  steps (all beams), final tokens / scores / valid.  Weights are regenerated
+  steps (all beams) and for fixed histories of 1-3 tokens shared by both dtypes,
+  final tokens / scores / valid.  Weights are regenerated
   from ``kadllm_b200.synthetic.numpy_weights(TINY, seed=0, init="test")``.
 * ``ops_<dtype>.npz``    seeded inputs and outputs of ``kadllm.ops.gated_delta``,
   ``causal_conv1d`` and ``prefix_attention`` (torch paths), including a masked
@@ -79,6 +80,11 @@ def main(ref_src: str) -> None:
         out["decode1_logits"] = adapter.decode(hist1, pre.state).float().numpy()
         out["decode2_history"] = hist2.numpy()
         out["decode2_logits"] = adapter.decode(hist2, pre.state).float().numpy()
+        # the same fixed histories in both dtypes, so BF16 error can be measured against fp32
+        fixed = np.random.default_rng(7).integers(0, cfg.vocab_size, (2, 8, 3))
+        for T in (1, 2, 3):
+            out[f"fixed{T}_history"] = fixed[:, :, :T]
+            out[f"fixed{T}_logits"] = adapter.decode(torch.from_numpy(fixed[:, :, :T]), pre.state).float().numpy()
         np.savez_compressed(HERE / f"model_{name}.npz", **out)
         print("model", name, res.scores[0].tolist())
 

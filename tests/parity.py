@@ -74,3 +74,17 @@ def assert_close_rel(actual, desired, rel: float = 1e-2, peak: float = 5e-2, wha
     top = float(np.max(np.abs(d))) if d.size else 0.0
     worst = float(np.max(np.abs(a - d))) if d.size else 0.0
     assert worst <= peak * max(top, 1e-30), f"{what}: max abs error {worst:.3e} > {peak} x {top:.3e}"
+
+
+def rel_l2(a, b) -> float:
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / (np.linalg.norm(b) or 1.0))
+
+
+def assert_bf16_as_accurate(ours, ref_bf16, exact, slack: float = 1.5, floor: float = 5e-3, what: str = "") -> None:
+    """End-to-end BF16 check: ours must be as close to the exact (fp32) answer as
+    the reference's own BF16 path is (within ``slack`` x, plus ``floor``)."""
+    e_ours = rel_l2(ours, exact)
+    e_ref = rel_l2(ref_bf16, exact)
+    assert e_ours <= slack * e_ref + floor, f"{what}: error vs fp32 {e_ours:.3e}, reference bf16 {e_ref:.3e}"

@@ -1,0 +1,178 @@
+"""Per-kernel GPU parity of the model building blocks against the oracle's pieces."""
+
+import numpy as np
+import pytest
+import torch
+
+from kadllm_b200 import _lib
+from oracle import grbeam_oracle as O
+from tests.parity import assert_close_rel
+
+pytestmark = pytest.mark.gpu
+bf = torch.bfloat16
+R = O.Rounding("bf16")
+
+
+def T(a, dtype=bf):
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).cuda().to(dtype)
+
+
+def N(t):
+    return t.float().cpu().numpy()
+
+
+def S():
+    return _lib.stream(torch.device("cuda"))
+
+
+@pytest.mark.parametrize("H", [128, 1024])
+def test_embed_and_add_rmsnorm(H):
+    rng = np.random.default_rng(H)
+    V, rows = 300, 37
+    table = O.bf16(rng.standard_normal((V, H)).astype(np.float32))
+    w = O.bf16(0.1 * rng.standard_normal(H).astype(np.float32))
+    ids = rng.integers(0, V, rows)
+    x = torch.empty(rows, H, dtype=bf, device="cuda")
+    nrm = torch.empty_like(x)
+    tid = torch.from_numpy(ids).cuda()
+    ttab, wt = T(table), T(w, torch.float32)
+    _lib.call("kadllm_embed_rmsnorm", tid.data_ptr(), ttab.data_ptr(), V, wt.data_ptr(), 1e-6,
+              x.data_ptr(), nrm.data_ptr(), rows, H, S())
+    np.testing.assert_array_equal(N(x), table[ids])
+    assert_close_rel(N(nrm), O.rms_norm(table[ids], w, 1e-6, R), rel=5e-3, what="embed norm")
+    delta = O.bf16(rng.standard_normal((rows, H)).astype(np.float32))
+    td = T(delta)
+    _lib.call("kadllm_add_rmsnorm", x.data_ptr(), td.data_ptr(), H, wt.data_ptr(), 1e-6, nrm.data_ptr(), rows,
+              1, 0, H, S())
+    xr = R(table[ids] + delta)
+    np.testing.assert_array_equal(N(x), xr)
+    assert_close_rel(N(nrm), O.rms_norm(xr, w, 1e-6, R), rel=5e-3, what="add norm")
+    last = torch.empty(3, H, dtype=bf, device="cuda")
+    _lib.call("kadllm_add_rmsnorm", x.data_ptr(), None, 0, wt.data_ptr(), 1e-6, last.data_ptr(), 3, 12, 11, H, S())
+    assert_close_rel(N(last), O.rms_norm(xr[11::12][:3], w, 1e-6, R), rel=5e-3, what="strided norm")
+
+
+def test_silu_mul():
+    rng = np.random.default_rng(0)
+    rows, inter = 19, 384
+    gu = O.bf16(rng.standard_normal((rows, 2 * inter)).astype(np.float32))
+    out = torch.empty(rows, inter, dtype=bf, device="cuda")
+    tgu = T(gu)
+    _lib.call("kadllm_silu_mul", tgu.data_ptr(), 2 * inter, inter, out.data_ptr(), rows, S())
+    ref = R(R(O.silu(gu[:, :inter])) * gu[:, inter:])
+    assert_close_rel(N(out), ref, rel=5e-3, what="silu_mul")
+
+
+@pytest.mark.parametrize("D,hq,hk", [(32, 4, 2), (256, 8, 2)])
+def test_qk_norm_rope_prefill_and_decode(D, hq, hk):
+    from kadllm_b200.config import TINY
+
+    cfg = TINY.with_(head_dim=D, num_attention_heads=hq, num_key_value_heads=hk, rope_theta=1e7)
+    rng = np.random.default_rng(D)
+    B, L = 2, 9
+    rows = B * L
+    ld = (2 * hq + 2 * hk) * D
+    P = O.bf16(rng.standard_normal((rows, ld)).astype(np.float32))
+    qw = O.bf16(0.1 * rng.standard_normal(D).astype(np.float32))
+    kw = O.bf16(0.1 * rng.standard_normal(D).astype(np.float32))
+    rot = cfg.rotary_dim
+    pos = torch.arange(64, device="cuda", dtype=torch.float32)
+    inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, rot, 2, device="cuda").float() / rot))
+    emb = torch.cat([pos[:, None] * inv, pos[:, None] * inv], -1)
+    cos, sin = emb.cos().to(bf).contiguous(), emb.sin().to(bf).contiguous()
+    q = torch.empty(rows, hq, D, dtype=bf, device="cuda")
+    kc = torch.zeros(B, hk, L, D, dtype=bf, device="cuda")
+    vc = torch.zeros_like(kc)
+    st = (hk * L * D, D, L * D)
+    tP, tqw, tkw = T(P), T(qw, torch.float32), T(kw, torch.float32)
+    _lib.call("kadllm_qk_norm_rope", tP.data_ptr(), ld, hq, hk, D, tqw.data_ptr(),
+              tkw.data_ptr(), 1e-6, cos.data_ptr(), sin.data_ptr(), rot, None, 5, L,
+              q.data_ptr(), hq * D, D, kc.data_ptr(), *st, vc.data_ptr(), *st, rows, S())
+    c_np, s_np = N(cos)[5:5 + L], N(sin)[5:5 + L]
+    x = P.reshape(B, L, -1)
+    qs = x[..., : 2 * hq * D].reshape(B, L, hq, 2 * D)[..., :D]
+    ks = x[..., 2 * hq * D: 2 * hq * D + hk * D].reshape(B, L, hk, D)
+    vs = x[..., 2 * hq * D + hk * D:].reshape(B, L, hk, D)
+    rq = O.apply_rotary(O.rms_norm(qs, qw, 1e-6, R), c_np, s_np, R)
+    rk = O.apply_rotary(O.rms_norm(ks, kw, 1e-6, R), c_np, s_np, R)
+    assert_close_rel(N(q).reshape(B, L, hq, D), rq, rel=5e-3, what="q")
+    assert_close_rel(N(kc).transpose(0, 2, 1, 3), rk, rel=5e-3, what="k")
+    np.testing.assert_array_equal(N(vc).transpose(0, 2, 1, 3), vs)
+
+
+def test_conv1d_prefill():
+    rng = np.random.default_rng(1)
+    B, L, C = 2, 70, 384
+    ld = C + 40
+    P = O.bf16(rng.standard_normal((B * L, ld)).astype(np.float32))
+    w = O.bf16(0.5 * rng.standard_normal((C, 4)).astype(np.float32))
+    out = torch.empty(B * L, C, dtype=bf, device="cuda")
+    state = torch.empty(B, C, 4, dtype=bf, device="cuda")
+    tP, tw = T(P), T(w)
+    _lib.call("kadllm_conv1d_prefill", tP.data_ptr(), ld, tw.data_ptr(), out.data_ptr(), C, state.data_ptr(), B,
+              L, C, S())
+    x = P[:, :C].reshape(B, L, C).transpose(0, 2, 1)  # B C L
+    xp = np.concatenate([np.zeros((B, C, 3), np.float32), x], -1)
+    acc = sum(xp[:, :, j:j + L] * w[None, :, j:j + 1] for j in range(4))
+    ref = O.silu(acc).transpose(0, 2, 1).reshape(B * L, C)
+    assert_close_rel(N(out), ref, rel=5e-3, what="conv out")
+    np.testing.assert_array_equal(N(state), x[:, :, L - 4:])
+
+
+@pytest.mark.parametrize("K,H,L", [(32, 4, 100), (128, 2, 130)])
+def test_gdn_prefill_matches_chunk_rule(K, H, L):
+    rng = np.random.default_rng(K + L)
+    B, HV = 2, H
+    kd, vd = H * K, HV * K
+    C = 2 * kd + vd
+    ld = C + vd + 2 * HV
+    qkv = O.bf16(rng.standard_normal((B * L, C)).astype(np.float32))
+    P = O.bf16(rng.standard_normal((B * L, ld)).astype(np.float32))
+    a_log = O.bf16(np.log(rng.uniform(1, 16, HV)).astype(np.float32))
+    dtb = O.bf16(rng.uniform(-1, 1, HV).astype(np.float32))
+    nw = O.bf16(1 + 0.1 * rng.standard_normal(K).astype(np.float32))
+    out = torch.empty(B * L, vd, dtype=bf, device="cuda")
+    state = torch.empty(B, HV, K, K, dtype=bf, device="cuda")
+    keep = [T(qkv), T(P), T(a_log, torch.float32), T(dtb, torch.float32), T(nw, torch.float32)]
+    _lib.call("kadllm_gdn_prefill", keep[0].data_ptr(), C, keep[1].data_ptr(), ld, C, keep[2].data_ptr(),
+              keep[3].data_ptr(), keep[4].data_ptr(), 1e-6, out.data_ptr(), vd,
+              state.data_ptr(), B, L, H, HV, K, K, S())
+    x = qkv.reshape(B, L, C)
+    q = x[..., :kd].reshape(B, L, H, K)
+    k = x[..., kd:2 * kd].reshape(B, L, H, K)
+    v = x[..., 2 * kd:].reshape(B, L, HV, K)
+    Pz = P.reshape(B, L, ld)
+    beta = R(O.sigmoid(Pz[..., C + vd:C + vd + HV]))
+    g = (-np.exp(a_log) * O.softplus(Pz[..., C + vd + HV:] + dtb)).astype(np.float32)
+    # fp32 L2 normalisation (the kernel normalises in fp32, like fla)
+    o, st = O.chunk_gated_delta_rule(q, k, v, g, beta, O.Rounding("fp32"))
+    o = R(o)
+    ref = O.rms_norm_gated(o.reshape(-1, K), Pz[..., C:C + vd].reshape(-1, K), nw, 1e-6, R).reshape(B * L, vd)
+    assert_close_rel(N(state), st, rel=1e-2, what="final state")
+    assert_close_rel(N(out), ref, rel=1e-2, what="gated output")
+
+
+@pytest.mark.parametrize("D,hq,hk,L", [(32, 4, 2, 64), (256, 8, 2, 100)])
+def test_causal_attention_prefill(D, hq, hk, L):
+    rng = np.random.default_rng(D + L)
+    B = 2
+    q = O.bf16(rng.standard_normal((B * L, hq, D)).astype(np.float32))
+    k = O.bf16(rng.standard_normal((B, hk, L, D)).astype(np.float32))
+    v = O.bf16(rng.standard_normal((B, hk, L, D)).astype(np.float32))
+    gate = O.bf16(rng.standard_normal((B * L, hq, 2 * D)).astype(np.float32))  # gate at [..., D:]
+    tq, tk, tv, tg = T(q), T(k), T(v), T(gate)
+    out = torch.empty(B * L, hq * D, dtype=bf, device="cuda")
+    gp = tg[..., D:]
+    # k / v [B, HK, L, D]: strides passed as (request, position, head)
+    _lib.call("kadllm_causal_attention", tq.data_ptr(), hq * D, D, tk.data_ptr(), tk.stride(0), tk.stride(2),
+              tk.stride(1), tv.data_ptr(), tv.stride(0), tv.stride(2), tv.stride(1), gp.data_ptr(), hq * 2 * D, 2 * D,
+              out.data_ptr(), hq * D, D, B, L, hq, hk, D, D ** -0.5, S())
+    qh = q.reshape(B, L, hq, D).transpose(0, 2, 1, 3)
+    kh = np.repeat(k, hq // hk, axis=1)
+    vh = np.repeat(v, hq // hk, axis=1)
+    s = np.matmul(qh, kh.transpose(0, 1, 3, 2)) * np.float32(D ** -0.5)
+    s = np.where(np.tril(np.ones((L, L), bool)), s, -np.inf)
+    p = np.exp(s - s.max(-1, keepdims=True))
+    o = R(np.matmul(p / p.sum(-1, keepdims=True), vh)).transpose(0, 2, 1, 3).reshape(B * L, hq * D)
+    ref = R(o * R(O.sigmoid(gate[..., D:].reshape(B * L, hq * D))))
+    assert_close_rel(N(out), ref, rel=1e-2, what="causal attention")

@@ -7,7 +7,7 @@ import torch
 from kadllm_b200.config import TINY, HybridConfig
 from kadllm_b200.synthetic import numpy_weights, random_prompts
 from oracle import grbeam_oracle as O
-from tests.parity import assert_close_rel, beam_mismatches, bf16_tol, load
+from tests.parity import assert_bf16_as_accurate, assert_close_rel, beam_mismatches, bf16_tol, load
 
 pytestmark = pytest.mark.gpu
 
@@ -31,18 +31,20 @@ def test_tiny_model_matches_reference_golden():
     from kadllm_b200.adapters import Qwen35GRBeamAdapter
 
     g = load("model_bf16.npz")
+    g32 = load("model_fp32.npz")  # same weights and prompts, fp32 reference (the exact answer)
     model, head = _hf_tiny()
     adapter = Qwen35GRBeamAdapter(model, head)
     ids = torch.from_numpy(g["ids"]).cuda()
     pre = adapter.prefill(ids)
-    assert_close_rel(pre.logits.float().cpu().numpy(), g["prefill_logits"], rel=2e-2, what="prefill logits")
+    assert_bf16_as_accurate(pre.logits.float().cpu().numpy(), g["prefill_logits"], g32["prefill_logits"],
+                            what="prefill logits")
     for i, (a, b) in enumerate(pre.state.layers):
-        assert_close_rel(a.float().cpu().numpy(), g[f"layer{i}_a"], rel=2e-2, what=f"layer {i} a")
-        assert_close_rel(b.float().cpu().numpy(), g[f"layer{i}_b"], rel=2e-2, what=f"layer {i} b")
-    for step in (1, 2):
-        hist = torch.from_numpy(g[f"decode{step}_history"]).cuda()
+        assert_bf16_as_accurate(a.float().cpu().numpy(), g[f"layer{i}_a"], g32[f"layer{i}_a"], what=f"layer {i} a")
+        assert_bf16_as_accurate(b.float().cpu().numpy(), g[f"layer{i}_b"], g32[f"layer{i}_b"], what=f"layer {i} b")
+    for T in (1, 2, 3):
+        hist = torch.from_numpy(g[f"fixed{T}_history"]).cuda()
         got = adapter.decode(hist, pre.state).float().cpu().numpy()
-        assert_close_rel(got, g[f"decode{step}_logits"], rel=2e-2, what=f"decode step {step}")
+        assert_bf16_as_accurate(got, g[f"fixed{T}_logits"], g32[f"fixed{T}_logits"], what=f"decode T={T}")
     res = grbeam_search(adapter, ids, [8, 8, 8])
     tol = 2 * bf16_tol(g["decode2_logits"])
     assert beam_mismatches(res.tokens.cpu().numpy(), res.scores.cpu().numpy(), g["tokens"], g["scores"], tol) == []
@@ -73,10 +75,12 @@ def test_qwen35_head_dims_prefill_matches_oracle(mid):
     ids = random_prompts(2, 100, MID.vocab_size, seed=4)
     logits, state = engine.prefill(torch.from_numpy(ids).cuda())
     ref_logits, ref_layers = orc.prefill(ids)
-    assert_close_rel(logits.float().cpu().numpy(), ref_logits, rel=2e-2, what="prefill logits")
-    for i, ((a, b), (ra, rb)) in enumerate(zip(state.layers, ref_layers)):
-        assert_close_rel(a.float().cpu().numpy(), ra, rel=2e-2, what=f"layer {i} a")
-        assert_close_rel(b.float().cpu().numpy(), rb, rel=2e-2, what=f"layer {i} b")
+    exact = O.HybridOracle(MID, orc.w, "fp32")
+    ex_logits, ex_layers = exact.prefill(ids)
+    assert_bf16_as_accurate(logits.float().cpu().numpy(), ref_logits, ex_logits, what="prefill logits")
+    for i, ((a, b), (ra, rb), (ea, eb)) in enumerate(zip(state.layers, ref_layers, ex_layers)):
+        assert_bf16_as_accurate(a.float().cpu().numpy(), ra, ea, what=f"layer {i} a")
+        assert_bf16_as_accurate(b.float().cpu().numpy(), rb, eb, what=f"layer {i} b")
 
 
 def test_qwen35_head_dims_decode_and_search_match_oracle(mid):
@@ -91,7 +95,9 @@ def test_qwen35_head_dims_decode_and_search_match_oracle(mid):
     hist = np.random.default_rng(0).integers(0, MID.vocab_size, (2, 8, 3))
     got = engine.decode(torch.from_numpy(hist).cuda(), state).float().cpu().numpy()
     ref = orc.decode(hist, 70, ref_layers)
-    assert_close_rel(got, ref, rel=2e-2, what="decode logits T=3")
+    exact = O.HybridOracle(MID, orc.w, "fp32")
+    _, ex_layers = exact.prefill(ids)
+    assert_bf16_as_accurate(got, ref, exact.decode(hist, 70, ex_layers), what="decode logits T=3")
     res = grbeam_search(NativeGRBeamAdapter(engine), tids, [8, 8, 8])
     tok, sc, _ = O.grbeam_search(orc, ids, [8, 8, 8])
     tol = 4 * bf16_tol(ref)
@@ -112,8 +118,7 @@ def test_prefix_is_immutable_and_owner_checked(mid):
             assert torch.equal(t, o)
     with pytest.raises(ValueError):
         adapter.decode(torch.zeros(2, 4, 2, dtype=torch.long, device="cuda"), pre.state)
-    other = NativeGRBeamAdapter(type(engine).__new__(type(engine)))
-    other._owner = object()
-    other.engine = engine
+    other = NativeGRBeamAdapter(engine)
+    other._owner = object()  # an adapter that did not create this prefix
     with pytest.raises(ValueError):
         other.decode(torch.zeros(1, 4, 2, dtype=torch.long, device="cuda"), pre.state)
