@@ -8,28 +8,33 @@
 // with q, k L2-normalised (eps 1e-6 inside the sqrt) and q scaled.
 //
 // B200 formulation (no per-beam state copy): unrolling the recurrence gives
-//     S_{t}^T x = A_t (S0^T x) + sum_{s<=t} D(s,t) d_s (k_s . x),
+//     S_t'^T k_t = A_t (S0^T k_t) + sum_{s<t} D(s,t) d_s (k_s . k_t)
+//     o_t        = A_t (S0^T q_t) + sum_{s<=t} D(s,t) d_s (k_s . q_t)
 //     A_t = prod_{r<=t} a_r,  D(s,t) = prod_{s<r<=t} a_r,  a_r = exp(g_r),
-// so the only K x V work is the GEMM  P = [q_t ; k_t]_{beams,t} x S0, which runs
-// on the tensor cores with S0 staged once in shared memory for all beams of a
-// request (a [beams*T*2, K] x [K, V] product per (request, head)).  The fp32
-// inputs are split into bf16 hi + lo parts (A = A_hi + A_lo, likewise S0 when
-// it is not bf16) so the products keep ~16 mantissa bits; the T-step
-// corrections are scalar/vector fp32 work in registers.
+// so the only K x V work is multiplying the beams' q_t / k_t rows by S0, which
+// runs on the tensor cores with S0 staged once in shared memory.
 //
-// One CTA = one (request, value head) pair and a range of beam chunks; a chunk
-// holds NB = 32 / T beams so that the GEMM has 64 rows (q and k of NB*T steps).
-
+// Thread mapping: a warp owns 8 beams.  For step t its 16-row MMA tile is
+// [q_t of the 8 beams ; k_t of the 8 beams] (rows g and g+8 of the m16n8k16
+// fragment), so after the K loop thread (g, tq) holds S0^T q_t and S0^T k_t of
+// beam g for the columns {8j + 2tq, 8j + 2tq + 1}: the recurrence, the output
+// cast and (fused mixer) the gated RMSNorm are thread-local plus two quad
+// shuffles.  q/k are split into bf16 hi + lo parts (A = A_hi + A_lo, and S0 too
+// when it is not bf16), keeping ~16 mantissa bits in the products.  Earlier
+// steps' k_s and d_s (T > 1) live in a small per-warp shared-memory slab.
+//
+// Fused mixer (kadllm_gdn_mixer_replay): q/k/v are produced on the fly by the
+// causal conv1d replay + SiLU from the packed projection row and the request's
+// conv state (src/kadllm/kernels/causal_conv1d.py:41-48), the gates from the
+// b / a columns (src/kadllm/adapters/qwen3_5.py:290-298), and the output goes
+// through Qwen3_5RMSNormGated with z (transformers modeling_qwen3_5.py:175-190).
 #include "common.cuh"
 
 namespace kb {
 namespace {
 
-constexpr int kThreads = 128;
-constexpr int kWarps = kThreads / 32;
-constexpr int kRows = 64;       // GEMM rows per chunk
-constexpr int kBeamSteps = 32;  // NB * T <= 32
 constexpr int kTMax = 8;
+constexpr int kBeamsPerWarp = 8;
 
 struct GdnArgs {
   // standalone operator inputs
@@ -54,370 +59,373 @@ struct GdnArgs {
   // common
   const void* state;
   int state_dtype;
-  int state_split;  // 1: state needs a lo part (not bf16)
+  int state_split;  // 1: S0 needs a lo part (not bf16)
   void* out;
   int out_dtype;
   int B, W, T, H, HV;
   float scale;
-  int NB;
-  int chunks_per_cta;
+  int octets_per_warp;  // beam octets each warp processes (amortises the S0 staging)
 };
 
 template <int DK, int DV>
-struct Smem {
-  static constexpr int kSStride = DV + 8;   // bf16 elements
-  static constexpr int kAStride = DK + 8;   // bf16 elements
-  static constexpr int kPStride = DV + 8;   // floats
-  static constexpr int kNch = 2 * DK + DV;  // conv channels per CTA (fused)
-  static constexpr size_t s_bytes = size_t(DK) * kSStride * 2;
-  static constexpr size_t a_bytes = size_t(kRows) * kAStride * 2;
-  static constexpr size_t p_bytes = size_t(kRows) * kPStride * 4;
-  static constexpr size_t v_bytes = size_t(kBeamSteps) * DV * 4;
-  static constexpr size_t coef_floats = 2 * kBeamSteps + 2 * kBeamSteps * kTMax;
-  static constexpr size_t conv_bytes = size_t(8) * kNch * 4;
-  static size_t total(bool split, bool fused) {
-    return s_bytes * (split ? 2 : 1) + 2 * a_bytes + p_bytes + v_bytes + coef_floats * 4 +
-           (fused ? conv_bytes : 0);
+struct Layout {
+  static constexpr int SS = DV + 8;        // bf16 row stride of the staged state
+  static constexpr int NCH = 2 * DK + DV;  // conv channels of one (q head, k head, v head)
+  __host__ __device__ static size_t state_bytes(bool split) { return size_t(DK) * SS * 2 * (split ? 2 : 1); }
+  __host__ __device__ static size_t conv_bytes(bool fused) { return fused ? size_t(NCH) * 8 * 4 : 0; }
+  // per warp: k_s (fp32) and d_s (fp32) of the steps before the last, plus the
+  // current step's bf16 outputs (read back by the gated RMSNorm)
+  __host__ __device__ static size_t warp_bytes(int T) {
+    return size_t(T > 1 ? T - 1 : 0) * kBeamsPerWarp * (DK + DV) * 4 + size_t(kBeamsPerWarp) * DV * 2;
   }
 };
 
-template <int DK, int DV, bool FUSED>
-__global__ void __launch_bounds__(kThreads) gdn_replay_kernel(const GdnArgs args) {
-  using L = Smem<DK, DV>;
-  constexpr int KPL = DK / 32;  // key elements per lane
-  constexpr int VPL = DV / 32;  // value elements per lane
-  extern __shared__ __align__(16) unsigned char smem[];
-  unsigned char* ptr = smem;
-  __nv_bfloat16* sS_hi = reinterpret_cast<__nv_bfloat16*>(ptr);
-  ptr += L::s_bytes;
-  __nv_bfloat16* sS_lo = nullptr;
-  if (args.state_split) {
-    sS_lo = reinterpret_cast<__nv_bfloat16*>(ptr);
-    ptr += L::s_bytes;
+// conv channel table, component-major [8][NCH]: c0, c1, c2 (prefix-tap partial sums
+// for t = 0, 1, 2), then w0..w3, so that for suffix step t
+//   conv_t = c_t + sum_{s = max(0, t-3)}^{t} w_{3-(t-s)} x_s      (c_t = 0 for t >= 3).
+// Evaluates two adjacent channels (c, c+1) from bf16 pairs of the projection rows.
+template <int NCH>
+__device__ __forceinline__ float2 conv_pair(const float* tab, int c, int t, const __nv_bfloat16* col0,
+                                            int64_t row_stride) {
+  float2 acc = t < 3 ? *reinterpret_cast<const float2*>(tab + t * NCH + c) : make_float2(0.f, 0.f);
+  const int s0 = t > 3 ? t - 3 : 0;
+  for (int s = s0; s <= t; ++s) {
+    const float2 w = *reinterpret_cast<const float2*>(tab + (3 + 3 - (t - s)) * NCH + c);
+    const __nv_bfloat162 x = *reinterpret_cast<const __nv_bfloat162*>(col0 + s * row_stride);
+    acc.x += w.x * __low2float(x);
+    acc.y += w.y * __high2float(x);
   }
-  __nv_bfloat16* sA_hi = reinterpret_cast<__nv_bfloat16*>(ptr);
-  ptr += L::a_bytes;
-  __nv_bfloat16* sA_lo = reinterpret_cast<__nv_bfloat16*>(ptr);
-  ptr += L::a_bytes;
-  float* sP = reinterpret_cast<float*>(ptr);
-  ptr += L::p_bytes;
-  float* sV = reinterpret_cast<float*>(ptr);
-  ptr += L::v_bytes;
-  float* sDecay = reinterpret_cast<float*>(ptr);  // [kBeamSteps]
-  float* sBeta = sDecay + kBeamSteps;             // [kBeamSteps]
-  float* sKK = sBeta + kBeamSteps;                // [kBeamSteps * kTMax]
-  float* sKQ = sKK + kBeamSteps * kTMax;          // [kBeamSteps * kTMax]
-  ptr += L::coef_floats * 4;
-  float* sConv = reinterpret_cast<float*>(ptr);  // [8][kNch]: w0..w3, tap0..tap2
+  return acc;
+}
 
-  const int tid = threadIdx.x;
-  const int lane = tid & 31;
-  const int warp = tid >> 5;
-  const int HV = args.HV, T = args.T, W = args.W;
-  const int b = blockIdx.x / HV;
-  const int hv = blockIdx.x % HV;
-  const int h = hv / (HV / args.H);
-  const int key_dim = args.H * DK;
+// TMAX: compile-time bound on T (1, 2, 4 or 8) so the per-step loops carry no dead code.
+template <int DK, int DV, bool FUSED, int TMAX>
+__global__ void __launch_bounds__(128) gdn_replay_kernel(const GdnArgs a) {
+  using Lt = Layout<DK, DV>;
+  constexpr int KK = DK / 16;  // k16 steps
+  constexpr int NT = DV / 8;   // n8 tiles
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int nwarps = blockDim.x >> 5;
+  const int T = a.T;
+  unsigned char* p = smem;
+  __nv_bfloat16* sS = reinterpret_cast<__nv_bfloat16*>(p);
+  p += Lt::state_bytes(a.state_split);
+  float* sConv = reinterpret_cast<float*>(p);  // [NCH][8]
+  p += Lt::conv_bytes(FUSED);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float* sK = reinterpret_cast<float*>(p + warp * Lt::warp_bytes(T));  // [T-1][8][DK]
+  float* sD = sK + (T > 1 ? T - 1 : 0) * kBeamsPerWarp * DK;           // [T-1][8][DV]
+  __nv_bfloat16* sO = reinterpret_cast<__nv_bfloat16*>(sD + (T > 1 ? T - 1 : 0) * kBeamsPerWarp * DV);  // [8][DV]
+
+  const int HV = a.HV;
+  const int b = blockIdx.x / HV, hv = blockIdx.x % HV;
+  const int h = hv / (HV / a.H);
+  const int key_dim = a.H * DK;
   const int conv_dim = 2 * key_dim + HV * DV;
+  const int g = lane >> 2, tq = lane & 3;
 
-  // ---- stage S0[b, hv] (K x V) as bf16 hi (+ lo) --------------------------------
+  // ---- stage S0 (bf16 hi [+ lo]) and the conv table -----------------------------------
   {
     const int64_t base = (int64_t(b) * HV + hv) * DK * DV;
-    for (int i = tid * 4; i < DK * DV; i += kThreads * 4) {
+    __nv_bfloat16* sLo = sS + DK * Lt::SS;
+    for (int i = tid * 4; i < DK * DV; i += blockDim.x * 4) {
       float f[4];
-      load4(args.state, base + i, args.state_dtype, f);
+      load4(a.state, base + i, a.state_dtype, f);
       const int kr = i / DV, vc = i % DV;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const __nv_bfloat16 hi = __float2bfloat16_rn(f[e]);
-        sS_hi[kr * L::kSStride + vc + e] = hi;
-        if (args.state_split) sS_lo[kr * L::kSStride + vc + e] = __float2bfloat16_rn(f[e] - __bfloat162float(hi));
+        sS[kr * Lt::SS + vc + e] = hi;
+        if (a.state_split) sLo[kr * Lt::SS + vc + e] = __float2bfloat16_rn(f[e] - __bfloat162float(hi));
       }
     }
-    for (int i = tid; i < kRows * L::kAStride; i += kThreads) {
-      sA_hi[i] = __float2bfloat16_rn(0.f);
-      sA_lo[i] = __float2bfloat16_rn(0.f);
-    }
     if constexpr (FUSED) {
-      for (int c = tid; c < L::kNch; c += kThreads) {
+      for (int c = tid; c < Lt::NCH; c += blockDim.x) {
         int ch;
         if (c < DK) ch = h * DK + c;
         else if (c < 2 * DK) ch = key_dim + h * DK + (c - DK);
         else ch = 2 * key_dim + hv * DV + (c - 2 * DK);
-        const __nv_bfloat16* w = args.conv_weight + int64_t(ch) * 4;
-        const __nv_bfloat16* s = args.conv_state + (int64_t(b) * conv_dim + ch) * args.conv_hist + args.conv_hist - 3;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) sConv[j * L::kNch + c] = __bfloat162float(w[j]);
-#pragma unroll
-        for (int j = 0; j < 3; ++j) sConv[(4 + j) * L::kNch + c] = __bfloat162float(s[j]);
+        const __nv_bfloat16* w = a.conv_weight + int64_t(ch) * 4;
+        const __nv_bfloat16* s = a.conv_state + (int64_t(b) * conv_dim + ch) * a.conv_hist + a.conv_hist - 3;
+        const float w0 = __bfloat162float(w[0]), w1 = __bfloat162float(w[1]);
+        const float w2 = __bfloat162float(w[2]), w3 = __bfloat162float(w[3]);
+        const float s0 = __bfloat162float(s[0]), s1 = __bfloat162float(s[1]), s2 = __bfloat162float(s[2]);
+        sConv[0 * Lt::NCH + c] = w0 * s0 + w1 * s1 + w2 * s2;
+        sConv[1 * Lt::NCH + c] = w0 * s1 + w1 * s2;
+        sConv[2 * Lt::NCH + c] = w0 * s2;
+        sConv[3 * Lt::NCH + c] = w0;  // tap applied to x_{t-3}
+        sConv[4 * Lt::NCH + c] = w1;
+        sConv[5 * Lt::NCH + c] = w2;
+        sConv[6 * Lt::NCH + c] = w3;  // tap applied to x_t
+        sConv[7 * Lt::NCH + c] = 0.f;
       }
     }
   }
   __syncthreads();
 
-  const int NB = args.NB;
-  const int chunks_total = (W + NB - 1) / NB;
-  const int c_begin = blockIdx.y * args.chunks_per_cta;
-  const int c_end = min(chunks_total, c_begin + args.chunks_per_cta);
+  for (int oct = 0; oct < a.octets_per_warp; ++oct) {
+  const int beam = ((blockIdx.y * nwarps + warp) * a.octets_per_warp + oct) * kBeamsPerWarp + g;
+  const bool valid = beam < a.W;
+  const int64_t brow = int64_t(b) * a.W + (valid ? beam : 0);
+  float At = 1.f;
+  float Dst[TMAX];
+  float kqd[TMAX], kkd[TMAX];  // k_s . q_t and k_s . k_t for the earlier steps s < t
+#pragma unroll
+  for (int s = 0; s < TMAX; ++s) Dst[s] = kqd[s] = kkd[s] = 0.f;
 
-  for (int chunk = c_begin; chunk < c_end; ++chunk) {
-    const int beam0 = chunk * NB;
-    const int nb = min(NB, W - beam0);
-
-    // ---- phase 1: q/k/v (conv + SiLU when fused), norms, gates, dot products -----
-    for (int n = warp; n < nb; n += kWarps) {
-      const int64_t r = int64_t(b) * W + beam0 + n;  // beam row in [0, BW)
-      float qn[kTMax][KPL], kn[kTMax][KPL];
-      float qwin[3][KPL], kwin[3][KPL], vwin[3][VPL];
+#pragma unroll
+  for (int t = 0; t < TMAX; ++t) {
+    if (t >= T) break;
+    const int64_t row = brow * T + t;
+    // ---- q_t, k_t, v_t of beam g at this thread's columns ---------------------------
+    float qv[KK][4], kv[KK][4];
+    float gt = 0.f, bt = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < KK; ++kk)
+#pragma unroll
+      for (int hp = 0; hp < 2; ++hp) {  // column pairs (2tq, 2tq+1) and (2tq+8, 2tq+9)
+        const int col = kk * 16 + tq * 2 + hp * 8;
+        float2 qx = make_float2(0.f, 0.f), kx = make_float2(0.f, 0.f);
+        if (valid) {
+          if constexpr (FUSED) {
+            const __nv_bfloat16* base = a.proj + (brow * T) * a.ld_proj;
+            qx = conv_pair<Lt::NCH>(sConv, col, t, base + h * DK + col, a.ld_proj);
+            kx = conv_pair<Lt::NCH>(sConv, DK + col, t, base + key_dim + h * DK + col, a.ld_proj);
+            qx = make_float2(bf16r(silu_fast(qx.x)), bf16r(silu_fast(qx.y)));
+            kx = make_float2(bf16r(silu_fast(kx.x)), bf16r(silu_fast(kx.y)));
+          } else {
+            const int64_t o = (row * a.H + h) * DK + col;
+            qx = make_float2(load_as_float(a.q, o, a.x_dtype), load_as_float(a.q, o + 1, a.x_dtype));
+            kx = make_float2(load_as_float(a.k, o, a.x_dtype), load_as_float(a.k, o + 1, a.x_dtype));
+          }
+        }
+        qv[kk][2 * hp] = qx.x;
+        qv[kk][2 * hp + 1] = qx.y;
+        kv[kk][2 * hp] = kx.x;
+        kv[kk][2 * hp + 1] = kx.y;
+      }
+    if (valid) {
       if constexpr (FUSED) {
-#pragma unroll
-        for (int j = 0; j < 3; ++j) {
-#pragma unroll
-          for (int e = 0; e < KPL; ++e) {
-            qwin[j][e] = sConv[(4 + j) * L::kNch + lane * KPL + e];
-            kwin[j][e] = sConv[(4 + j) * L::kNch + DK + lane * KPL + e];
-          }
-#pragma unroll
-          for (int e = 0; e < VPL; ++e) vwin[j][e] = sConv[(4 + j) * L::kNch + 2 * DK + lane * VPL + e];
-        }
-      }
-#pragma unroll
-      for (int t = 0; t < kTMax; ++t) {
-        if (t < T) {
-          const int64_t row = r * T + t;
-          float qv[KPL], kv[KPL], vv[VPL];
-          float gt, bt;
-          if constexpr (FUSED) {
-            const __nv_bfloat16* pr = args.proj + row * args.ld_proj;
-            // conv over [3 prefix taps, suffix] then SiLU, rounded to bf16 like the
-            // conv operator's output (src/kadllm/kernels/causal_conv1d.py:41-48)
-#pragma unroll
-            for (int e = 0; e < KPL; ++e) {
-              const int cq = lane * KPL + e;
-              const float xq = __bfloat162float(pr[h * DK + cq]);
-              const float xk = __bfloat162float(pr[key_dim + h * DK + cq]);
-              float aq = qwin[0][e] * sConv[0 * L::kNch + cq] + qwin[1][e] * sConv[1 * L::kNch + cq] +
-                         qwin[2][e] * sConv[2 * L::kNch + cq] + xq * sConv[3 * L::kNch + cq];
-              float ak = kwin[0][e] * sConv[0 * L::kNch + DK + cq] + kwin[1][e] * sConv[1 * L::kNch + DK + cq] +
-                         kwin[2][e] * sConv[2 * L::kNch + DK + cq] + xk * sConv[3 * L::kNch + DK + cq];
-              qv[e] = bf16r(silu_f(aq));
-              kv[e] = bf16r(silu_f(ak));
-              qwin[0][e] = qwin[1][e]; qwin[1][e] = qwin[2][e]; qwin[2][e] = xq;
-              kwin[0][e] = kwin[1][e]; kwin[1][e] = kwin[2][e]; kwin[2][e] = xk;
-            }
-#pragma unroll
-            for (int e = 0; e < VPL; ++e) {
-              const int cv = lane * VPL + e;
-              const float xv = __bfloat162float(pr[2 * key_dim + hv * DV + cv]);
-              float av = vwin[0][e] * sConv[0 * L::kNch + 2 * DK + cv] + vwin[1][e] * sConv[1 * L::kNch + 2 * DK + cv] +
-                         vwin[2][e] * sConv[2 * L::kNch + 2 * DK + cv] + xv * sConv[3 * L::kNch + 2 * DK + cv];
-              vv[e] = bf16r(silu_f(av));
-              vwin[0][e] = vwin[1][e]; vwin[1][e] = vwin[2][e]; vwin[2][e] = xv;
-            }
-            const int64_t gcol = conv_dim + int64_t(HV) * DV;
-            const float bl = __bfloat162float(pr[gcol + hv]);
-            const float al = __bfloat162float(pr[gcol + HV + hv]);
-            bt = bf16r(sigmoid_f(bl));
-            gt = -expf(args.a_log[hv]) * softplus_f(al + args.dt_bias[hv]);
-          } else {
-            const int64_t qo = (row * args.H + h) * DK + lane * KPL;
-            const int64_t vo = (row * HV + hv) * DV + lane * VPL;
-#pragma unroll
-            for (int e = 0; e < KPL; ++e) {
-              qv[e] = load_as_float(args.q, qo + e, args.x_dtype);
-              kv[e] = load_as_float(args.k, qo + e, args.x_dtype);
-            }
-#pragma unroll
-            for (int e = 0; e < VPL; ++e) vv[e] = load_as_float(args.v, vo + e, args.x_dtype);
-            gt = load_as_float(args.g, row * HV + hv, args.g_dtype);
-            bt = load_as_float(args.beta, row * HV + hv, args.beta_dtype);
-          }
-          float sq = 0.f, sk = 0.f;
-#pragma unroll
-          for (int e = 0; e < KPL; ++e) {
-            sq += qv[e] * qv[e];
-            sk += kv[e] * kv[e];
-          }
-          sq = warp_sum(sq);
-          sk = warp_sum(sk);
-          const float dq = sqrtf(sq + 1e-6f), dk = sqrtf(sk + 1e-6f);
-          const int qrow = n * 2 * T + t, krow = n * 2 * T + T + t;
-#pragma unroll
-          for (int e = 0; e < KPL; ++e) {
-            qn[t][e] = qv[e] / dq * args.scale;
-            kn[t][e] = kv[e] / dk;
-            const __nv_bfloat16 qh = __float2bfloat16_rn(qn[t][e]);
-            const __nv_bfloat16 kh = __float2bfloat16_rn(kn[t][e]);
-            sA_hi[qrow * L::kAStride + lane * KPL + e] = qh;
-            sA_lo[qrow * L::kAStride + lane * KPL + e] = __float2bfloat16_rn(qn[t][e] - __bfloat162float(qh));
-            sA_hi[krow * L::kAStride + lane * KPL + e] = kh;
-            sA_lo[krow * L::kAStride + lane * KPL + e] = __float2bfloat16_rn(kn[t][e] - __bfloat162float(kh));
-          }
-#pragma unroll
-          for (int e = 0; e < VPL; ++e) sV[(n * T + t) * DV + lane * VPL + e] = vv[e];
-          // dot products against earlier keys: kq[s][t] (s <= t), kk[s][t] (s < t)
-#pragma unroll
-          for (int s = 0; s < kTMax; ++s) {
-            if (s <= t) {
-              float dqs = 0.f, dks = 0.f;
-#pragma unroll
-              for (int e = 0; e < KPL; ++e) {
-                dqs += kn[s][e] * qn[t][e];
-                dks += kn[s][e] * kn[t][e];
-              }
-              dqs = warp_sum(dqs);
-              dks = warp_sum(dks);
-              if (lane == 0) {
-                sKQ[(n * T + s) * T + t] = dqs;
-                sKK[(n * T + s) * T + t] = dks;
-              }
-            }
-          }
-          if (lane == 0) {
-            sDecay[n * T + t] = expf(gt);
-            sBeta[n * T + t] = bt;
-          }
-        }
+        const __nv_bfloat16* pr = a.proj + row * a.ld_proj + conv_dim + int64_t(HV) * DV;
+        bt = bf16r(sigmoid_f(__bfloat162float(pr[hv])));
+        gt = -expf(a.a_log[hv]) * softplus_f(__bfloat162float(pr[HV + hv]) + a.dt_bias[hv]);
+      } else {
+        gt = load_as_float(a.g, row * HV + hv, a.g_dtype);
+        bt = load_as_float(a.beta, row * HV + hv, a.beta_dtype);
       }
     }
-    __syncthreads();
-
-    // ---- phase 2: P = A x S0 on the tensor cores (A = q/k rows, split hi+lo) -------
+    // ---- L2 norms (quad reduction: the 4 threads of a beam hold all K columns) -------
+    float sq = 0.f, sk = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < KK; ++kk)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        sq += qv[kk][e] * qv[kk][e];
+        sk += kv[kk][e] * kv[kk][e];
+      }
+    sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+    sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+    sk += __shfl_xor_sync(0xffffffffu, sk, 1);
+    sk += __shfl_xor_sync(0xffffffffu, sk, 2);
+    const float iq = 1.0f / sqrtf(sq + 1e-6f), ik = 1.0f / sqrtf(sk + 1e-6f);
+#pragma unroll
+    for (int kk = 0; kk < KK; ++kk)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        qv[kk][e] = qv[kk][e] * iq * a.scale;
+        kv[kk][e] = kv[kk][e] * ik;
+      }
+    // ---- dot products with this beam's earlier keys ------------------------------------
+    float kq_self;
     {
-      const int rows_used = nb * 2 * T;
-      constexpr int kNGroups = DV / 32;
-      for (int item = warp; item < 4 * kNGroups; item += kWarps) {
-        const int mt = item % 4, ng = item / 4;
-        if (mt * 16 >= rows_used) continue;
-        float acc[4][4];
+      float dqq = 0.f;
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
+      for (int kk = 0; kk < KK; ++kk)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) acc[j][e] = 0.f;
-        const int passes = args.state_split ? 3 : 2;
-        for (int pass = 0; pass < passes; ++pass) {
-          const __nv_bfloat16* sa = (pass == 1) ? sA_lo : sA_hi;
-          const __nv_bfloat16* ss = (pass == 2) ? sS_lo : sS_hi;
+        for (int e = 0; e < 4; ++e) dqq += kv[kk][e] * qv[kk][e];
+      dqq += __shfl_xor_sync(0xffffffffu, dqq, 1);
+      dqq += __shfl_xor_sync(0xffffffffu, dqq, 2);
 #pragma unroll
-          for (int kk = 0; kk < DK / 16; ++kk) {
-            uint32_t a[4];
-            ldmatrix_x4(a, sa + (mt * 16 + (lane & 15)) * L::kAStride + kk * 16 + (lane >> 4) * 8);
-            uint32_t b0[4], b1[4];
-            ldmatrix_x4_trans(b0, ss + (kk * 16 + (lane & 15)) * L::kSStride + ng * 32 + (lane >> 4) * 8);
-            ldmatrix_x4_trans(b1, ss + (kk * 16 + (lane & 15)) * L::kSStride + ng * 32 + 16 + (lane >> 4) * 8);
-            const uint32_t bf0[2] = {b0[0], b0[1]}, bf1[2] = {b0[2], b0[3]};
-            const uint32_t bf2[2] = {b1[0], b1[1]}, bf3[2] = {b1[2], b1[3]};
-            mma_bf16_16816(acc[0], a, bf0);
-            mma_bf16_16816(acc[1], a, bf1);
-            mma_bf16_16816(acc[2], a, bf2);
-            mma_bf16_16816(acc[3], a, bf3);
-          }
-        }
-        const int g = lane >> 2, tq = lane & 3;
+      for (int s = 0; s < t; ++s) {
+        {
+          const float* ks = sK + (s * kBeamsPerWarp + g) * DK;
+          float dks = 0.f, dqs = 0.f;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int col = ng * 32 + j * 8 + tq * 2;
-          *reinterpret_cast<float2*>(&sP[(mt * 16 + g) * L::kPStride + col]) = make_float2(acc[j][0], acc[j][1]);
-          *reinterpret_cast<float2*>(&sP[(mt * 16 + g + 8) * L::kPStride + col]) = make_float2(acc[j][2], acc[j][3]);
+          for (int kk = 0; kk < KK; ++kk)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float kse = ks[kk * 16 + tq * 2 + (e & 1) + (e >> 1) * 8];
+              dks += kse * kv[kk][e];
+              dqs += kse * qv[kk][e];
+            }
+          dks += __shfl_xor_sync(0xffffffffu, dks, 1);
+          dks += __shfl_xor_sync(0xffffffffu, dks, 2);
+          dqs += __shfl_xor_sync(0xffffffffu, dqs, 1);
+          dqs += __shfl_xor_sync(0xffffffffu, dqs, 2);
+          kkd[s] = dks;
+          kqd[s] = dqs;
         }
       }
+      kq_self = dqq;
     }
-    __syncthreads();
-
-    // ---- phase 3: T-step corrections, outputs (+ gated RMSNorm when fused) ---------
-    for (int n = warp; n < nb; n += kWarps) {
-      const int64_t r = int64_t(b) * W + beam0 + n;
-      float delta[kTMax][VPL];
-      float D[kTMax];
-      float At = 1.f;
+    // ---- P = [q_t ; k_t] x S0 on the tensor cores, then the factored recurrence ----
+    // The V columns are processed in two halves to bound the accumulator registers.
+    const float at = expf(gt);
+    At *= at;
 #pragma unroll
-      for (int t = 0; t < kTMax; ++t) {
-        if (t < T) {
-          const float a = sDecay[n * T + t];
-          const float bt = sBeta[n * T + t];
-          At *= a;
+    for (int s = 0; s < t; ++s) Dst[s] *= at;
+    constexpr int NH = NT / 2;
+    float ss = 0.f;  // sum of squares of the bf16 outputs (fused gated norm)
+    float* dcur = sD + (t * kBeamsPerWarp + g) * DV;
+    // A fragments of [q_t ; k_t] (rows g / g+8), split once into bf16 hi and lo parts
+    uint32_t ahi[KK][4], alo[KK][4];
 #pragma unroll
-          for (int s = 0; s < kTMax; ++s)
-            if (s < t) D[s] *= a;
-          D[t] = 1.f;
-          const float* pq = sP + (n * 2 * T + t) * L::kPStride + lane * VPL;
-          const float* pk = sP + (n * 2 * T + T + t) * L::kPStride + lane * VPL;
-          float o[VPL];
+    for (int kk = 0; kk < KK; ++kk) {
+      float hq[4], hk[4];
 #pragma unroll
-          for (int e = 0; e < VPL; ++e) {
-            float skt = At * pk[e];
+      for (int e = 0; e < 4; ++e) {
+        hq[e] = bf16r(qv[kk][e]);
+        hk[e] = bf16r(kv[kk][e]);
+      }
+      ahi[kk][0] = pack_bf16(hq[0], hq[1]);  // row g (q), k cols 2tq, 2tq+1
+      ahi[kk][1] = pack_bf16(hk[0], hk[1]);  // row g+8 (k)
+      ahi[kk][2] = pack_bf16(hq[2], hq[3]);  // row g, k cols 2tq+8, 2tq+9
+      ahi[kk][3] = pack_bf16(hk[2], hk[3]);
+      alo[kk][0] = pack_bf16(qv[kk][0] - hq[0], qv[kk][1] - hq[1]);
+      alo[kk][1] = pack_bf16(kv[kk][0] - hk[0], kv[kk][1] - hk[1]);
+      alo[kk][2] = pack_bf16(qv[kk][2] - hq[2], qv[kk][3] - hq[3]);
+      alo[kk][3] = pack_bf16(kv[kk][2] - hk[2], kv[kk][3] - hk[3]);
+    }
+    const int passes = a.state_split ? 3 : 2;
+#pragma unroll 1
+    for (int half = 0; half < 2; ++half) {
+      float acc[NH][4];
 #pragma unroll
-            for (int s = 0; s < kTMax; ++s)
-              if (s < t) skt += D[s] * sKK[(n * T + s) * T + t] * delta[s][e];
-            delta[t][e] = bt * (sV[(n * T + t) * DV + lane * VPL + e] - skt);
-            float ov = At * pq[e];
+      for (int j = 0; j < NH; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+      for (int pass = 0; pass < passes; ++pass) {
+        const __nv_bfloat16* sb = sS + (pass == 2 ? DK * Lt::SS : 0) + half * (DV / 2);
 #pragma unroll
-            for (int s = 0; s < kTMax; ++s)
-              if (s <= t) ov += D[s] * sKQ[(n * T + s) * T + t] * delta[s][e];
-            o[e] = ov;
+        for (int kk = 0; kk < KK; ++kk) {
+          const uint32_t* af = pass == 1 ? alo[kk] : ahi[kk];
+#pragma unroll
+          for (int np = 0; np < NH / 2; ++np) {
+            uint32_t bfr[4];
+            ldmatrix_x4_trans(bfr, sb + (kk * 16 + (lane & 15)) * Lt::SS + np * 16 + (lane >> 4) * 8);
+            const uint32_t b0[2] = {bfr[0], bfr[1]}, b1[2] = {bfr[2], bfr[3]};
+            mma_bf16_16816(acc[2 * np], af, b0);
+            mma_bf16_16816(acc[2 * np + 1], af, b1);
           }
-          const int64_t row = r * T + t;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < NH; ++j) {
+        const int col0 = (half * NH + j) * 8 + tq * 2;
+        float2 vp = make_float2(0.f, 0.f);
+        if (valid) {
           if constexpr (FUSED) {
-            // Qwen3_5RMSNormGated: fp32 normalise, cast, * weight (bf16), * silu(z)
-            float ss = 0.f;
-#pragma unroll
-            for (int e = 0; e < VPL; ++e) {
-              o[e] = bf16r(o[e]);
-              ss += o[e] * o[e];
-            }
-            ss = warp_sum(ss);
-            const float inv = 1.0f / sqrtf(ss / float(DV) + args.norm_eps);
-            const __nv_bfloat16* zp = args.proj + row * args.ld_proj + conv_dim + hv * DV + lane * VPL;
-            __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(args.out) + row * (int64_t(HV) * DV) + hv * DV + lane * VPL;
-#pragma unroll
-            for (int e = 0; e < VPL; ++e) {
-              const float hn = bf16r(o[e] * inv);
-              const float hw = bf16r(args.norm_weight[lane * VPL + e] * hn);
-              const float z = __bfloat162float(zp[e]);
-              op[e] = __float2bfloat16_rn(hw * silu_f(z));
-            }
+            const __nv_bfloat16* base = a.proj + (brow * T) * a.ld_proj;
+            vp = conv_pair<Lt::NCH>(sConv, 2 * DK + col0, t, base + 2 * key_dim + hv * DV + col0, a.ld_proj);
+            vp = make_float2(bf16r(silu_fast(vp.x)), bf16r(silu_fast(vp.y)));
           } else {
-            const int64_t oo = (row * HV + hv) * DV + lane * VPL;
+            const int64_t vo = (row * HV + hv) * DV + col0;
+            vp = make_float2(load_as_float(a.v, vo, a.x_dtype), load_as_float(a.v, vo + 1, a.x_dtype));
+          }
+        }
 #pragma unroll
-            for (int e = 0; e < VPL; ++e) store_from_float(args.out, oo + e, args.out_dtype, o[e]);
+        for (int e = 0; e < 2; ++e) {
+          const int col = col0 + e;
+          const float vx = e ? vp.y : vp.x;
+          float skt = At * acc[j][2 + e];
+          float o = At * acc[j][e];
+#pragma unroll
+          for (int s = 0; s < t; ++s) {
+            const float ds = sD[(s * kBeamsPerWarp + g) * DV + col];
+            skt += Dst[s] * kkd[s] * ds;
+            o += Dst[s] * kqd[s] * ds;
+          }
+          const float d = bt * (vx - skt);
+          o += d * kq_self;
+          if (t + 1 < T) dcur[col] = d;
+          if constexpr (FUSED) {
+            const __nv_bfloat16 ob = __float2bfloat16_rn(o);  // gated_delta returns v's dtype
+            const float of = __bfloat162float(ob);
+            ss += of * of;
+            sO[g * DV + col] = ob;
+          } else if (valid) {
+            store_from_float(a.out, (row * HV + hv) * DV + col, a.out_dtype, o);
           }
         }
       }
     }
-    __syncthreads();
+    if (t + 1 < T) {  // keep k_t for the later steps' dot products
+      float* kst = sK + (t * kBeamsPerWarp + g) * DK;
+#pragma unroll
+      for (int kk = 0; kk < KK; ++kk)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) kst[kk * 16 + tq * 2 + (e & 1) + (e >> 1) * 8] = kv[kk][e];
+    }
+    Dst[t] = 1.f;
+    __syncwarp();
+    // ---- gated RMSNorm (fused mixer) -------------------------------------------------
+    if constexpr (FUSED) {
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+      const float inv = 1.0f / sqrtf(ss / float(DV) + a.norm_eps);
+      if (valid) {
+        const __nv_bfloat16* zp = a.proj + row * a.ld_proj + conv_dim + hv * DV;
+        __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(a.out) + row * (int64_t(HV) * DV) + hv * DV;
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+          const int col = j * 8 + tq * 2;
+          const __nv_bfloat162 z = *reinterpret_cast<const __nv_bfloat162*>(zp + col);
+          const float o0 = __bfloat162float(sO[g * DV + col]), o1 = __bfloat162float(sO[g * DV + col + 1]);
+          const float h0 = bf16r(a.norm_weight[col] * bf16r(o0 * inv));
+          const float h1 = bf16r(a.norm_weight[col + 1] * bf16r(o1 * inv));
+          *reinterpret_cast<__nv_bfloat162*>(op + col) =
+              __floats2bfloat162_rn(h0 * silu_f(__low2float(z)), h1 * silu_f(__high2float(z)));
+        }
+      }
+    }
+    __syncwarp();
   }
+  }  // octets
 }
 
-template <int DK, int DV, bool FUSED>
+template <int DK, int DV, bool FUSED, int TMAX>
 int launch_gdn(const GdnArgs& a, cudaStream_t stream) {
-  const size_t smem = Smem<DK, DV>::total(a.state_split != 0, FUSED);
-  auto kern = gdn_replay_kernel<DK, DV, FUSED>;
+  using Lt = Layout<DK, DV>;
+  const size_t fixed = Lt::state_bytes(a.state_split != 0) + Lt::conv_bytes(FUSED);
+  const size_t per_warp = Lt::warp_bytes(a.T);
+  int warps = 4;
+  while (warps > 1 && fixed + warps * per_warp > 200 * 1024) warps >>= 1;
+  const size_t smem = fixed + warps * per_warp;
+  auto kern = gdn_replay_kernel<DK, DV, FUSED, TMAX>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess) {
     set_error("gdn replay: cannot reserve %zu bytes of shared memory", smem);
     return KADLLM_ECUDA;
   }
-  const int pairs = a.B * a.HV;
-  const int chunks_total = (a.W + a.NB - 1) / a.NB;
-  const int target = 148 * 4;
-  int splits = (target + pairs - 1) / pairs;
-  splits = splits < 1 ? 1 : (splits > chunks_total ? chunks_total : splits);
   GdnArgs args = a;
-  args.chunks_per_cta = (chunks_total + splits - 1) / splits;
-  splits = (chunks_total + args.chunks_per_cta - 1) / args.chunks_per_cta;
-  dim3 grid(pairs, splits);
-  kern<<<grid, kThreads, smem, stream>>>(args);
+  args.octets_per_warp = a.W >= 64 ? 2 : 1;
+  const int beams_per_cta = warps * kBeamsPerWarp * args.octets_per_warp;
+  dim3 grid(a.B * a.HV, (a.W + beams_per_cta - 1) / beams_per_cta);
+  kern<<<grid, warps * 32, smem, stream>>>(args);
   KB_CHECK_LAUNCH("gdn replay launch");
   return KADLLM_OK;
 }
 
+template <int DK, bool FUSED>
+int dispatch_steps(const GdnArgs& a, cudaStream_t stream) {
+  if (a.T <= 1) return launch_gdn<DK, DK, FUSED, 1>(a, stream);
+  if (a.T <= 2) return launch_gdn<DK, DK, FUSED, 2>(a, stream);
+  if (a.T <= 4) return launch_gdn<DK, DK, FUSED, 4>(a, stream);
+  return launch_gdn<DK, DK, FUSED, 8>(a, stream);
+}
+
 template <bool FUSED>
 int dispatch_gdn(int dk, int dv, const GdnArgs& a, cudaStream_t stream) {
-#define KB_GDN_CASE(K_, V_) \
-  if (dk == K_ && dv == V_) return launch_gdn<K_, V_, FUSED>(a, stream);
-  KB_GDN_CASE(128, 128)
-  KB_GDN_CASE(64, 64)
-  KB_GDN_CASE(32, 32)
-#undef KB_GDN_CASE
+  if (dk == 128 && dv == 128) return dispatch_steps<128, FUSED>(a, stream);
+  if (dk == 64 && dv == 64) return dispatch_steps<64, FUSED>(a, stream);
+  if (dk == 32 && dv == 32) return dispatch_steps<32, FUSED>(a, stream);
   set_error("gdn replay: head dims K=%d V=%d must be equal and in {32, 64, 128}", dk, dv);
   return KADLLM_EUNSUPPORTED;
 }
@@ -429,7 +437,8 @@ int check_common(int64_t B, int64_t W, int64_t T, int64_t H, int64_t HV, int64_t
              (long long)H);
   KB_REQUIRE(T <= kTMax, KADLLM_EUNSUPPORTED, "gdn replay: at most %d suffix steps (got %lld)", kTMax,
              (long long)T);
-  KB_REQUIRE(B * HV < (1ll << 31) && B * W < (1ll << 31), KADLLM_EINVAL, "gdn replay: too many rows");
+  KB_REQUIRE(B * HV < (1ll << 31) && B * W < (1ll << 31) && (W + 7) / 8 <= 65535, KADLLM_EINVAL,
+             "gdn replay: too many rows");
   return KADLLM_OK;
 }
 
@@ -455,7 +464,6 @@ extern "C" int kadllm_gated_delta_replay(const void* q, const void* k, const voi
   a.out = out; a.out_dtype = x_dtype;
   a.B = int(batch); a.W = int(beam_width); a.T = int(steps); a.H = int(heads); a.HV = int(v_heads);
   a.scale = scale > 0.f ? scale : 1.0f / sqrtf(float(k_dim));
-  a.NB = kBeamSteps / a.T;
   return dispatch_gdn<false>(int(k_dim), int(v_dim), a, static_cast<cudaStream_t>(stream));
 }
 
@@ -471,8 +479,9 @@ extern "C" int kadllm_gdn_mixer_replay(const void* proj, int64_t ld_proj, const 
              KADLLM_EINVAL, "gdn mixer: null pointer");
   const int64_t conv_dim = 2 * heads * k_dim + v_heads * v_dim;
   KB_REQUIRE(conv_hist >= 3, KADLLM_EINVAL, "gdn mixer: conv state needs >= 3 taps");
-  KB_REQUIRE(ld_proj >= conv_dim + v_heads * v_dim + 2 * v_heads, KADLLM_EINVAL,
-             "gdn mixer: projection row too short");
+  KB_REQUIRE(ld_proj >= conv_dim + v_heads * v_dim + 2 * v_heads && ld_proj % 2 == 0 &&
+                 (reinterpret_cast<uintptr_t>(proj) & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 3) == 0,
+             KADLLM_EINVAL, "gdn mixer: projection row too short or misaligned");
   GdnArgs a{};
   a.proj = static_cast<const __nv_bfloat16*>(proj); a.ld_proj = ld_proj;
   a.conv_state = static_cast<const __nv_bfloat16*>(conv_state); a.conv_hist = conv_hist;
@@ -482,6 +491,5 @@ extern "C" int kadllm_gdn_mixer_replay(const void* proj, int64_t ld_proj, const 
   a.out = out; a.out_dtype = KADLLM_BF16;
   a.B = int(batch); a.W = int(beam_width); a.T = int(steps); a.H = int(heads); a.HV = int(v_heads);
   a.scale = 1.0f / sqrtf(float(k_dim));
-  a.NB = kBeamSteps / a.T;
   return dispatch_gdn<true>(int(k_dim), int(v_dim), a, static_cast<cudaStream_t>(stream));
 }
