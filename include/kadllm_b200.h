@@ -193,24 +193,25 @@ KADLLM_API int kadllm_qk_norm_rope(const void* proj, int64_t ld_proj, int64_t q_
                                    void* v_out, int64_t sv_seq, int64_t sv_pos, int64_t sv_h,
                                    int64_t rows, void* stream);
 
-/* Prompt conv: out[b*L+t, c] = bf16(silu(sum_j w[c,j] x[b*L+t-3+j, c])) with zero
- * left padding, x = proj[:, :channels]; conv_state[b, c, 0..3] = x at positions
- * L-4 .. L-1 (zero before the prompt) -- the prefix the decode conv replays from. */
-KADLLM_API int kadllm_conv1d_prefill(const void* proj, int64_t ld_proj, const void* weight,
-                                     void* out, int64_t ld_out, void* conv_state, int64_t batch,
-                                     int64_t length, int64_t channels, void* stream);
-
-/* Prompt gated delta rule, chunked (64) on the tensor cores, gates from the
- * projection (beta = sigmoid(b), g = -exp(a_log) softplus(a + dt_bias)) and the
- * gated RMSNorm fused on the output; writes the final state [B, HV, K, V] bf16
- * once per request.  qkv [B*L, ld_qkv] conv outputs (q | k | v); proj holds
- * z at column z_col (+ hv*V), then b (HV), then a (HV).  out [B*L, ld_out]. */
-KADLLM_API int kadllm_gdn_prefill(const void* qkv, int64_t ld_qkv, const void* proj,
-                                  int64_t ld_proj, int64_t z_col, const float* a_log,
-                                  const float* dt_bias, const float* norm_weight, float norm_eps,
-                                  void* out, int64_t ld_out, void* state, int64_t batch,
-                                  int64_t length, int64_t heads, int64_t v_heads, int64_t k_dim,
-                                  int64_t v_dim, void* stream);
+/* Prompt Gated-DeltaNet layer from the packed projection (BF16), in two
+ * launches: a parallel per-(request, head, 64-token chunk) preparation (causal
+ * conv + SiLU, gates, q/k L2 norm, K K^T and Q K^T on the tensor cores, the UT
+ * transform T = (I + L)^-1) and a sequential per-(request, head) state scan
+ * (tensor-core chunk products, gated RMSNorm fused on the output).
+ * Replaces Qwen3_5GatedDeltaNet.forward on the prompt (TF:422-533 with the
+ * chunked rule TF:234-311).  proj [B*L, ld_proj] = q | k | v | z | b | a;
+ * conv_weight [conv_dim, 4]; writes conv_state [B, conv_dim, 4] (last 4
+ * pre-conv columns), out [B*L, ld_out] and state [B, HV, K, V] (bf16).
+ * workspace >= kadllm_gdn_prefill_workspace(...) bytes, 256-byte aligned. */
+KADLLM_API int64_t kadllm_gdn_prefill_workspace(int64_t batch, int64_t length, int64_t v_heads,
+                                               int64_t k_dim, int64_t v_dim);
+KADLLM_API int kadllm_gdn_prefill_split(const void* proj, int64_t ld_proj, const void* conv_weight,
+                                        void* conv_state, const float* a_log, const float* dt_bias,
+                                        const float* norm_weight, float norm_eps, void* out,
+                                        int64_t ld_out, void* state, void* workspace,
+                                        int64_t workspace_bytes, int64_t batch, int64_t length,
+                                        int64_t heads, int64_t v_heads, int64_t k_dim, int64_t v_dim,
+                                        void* stream);
 
 /* Prompt causal GQA attention (flash loop on the tensor cores) with the fused
  * output gate out = bf16(o) * bf16(sigmoid(gate)) (gate may be NULL).

@@ -22,8 +22,7 @@ SIGNATURES: dict[str, list] = {
     "kadllm_add_rmsnorm": [P, P, L, P, F, P, L, L, L, L, P],
     "kadllm_silu_mul": [P, L, L, P, L, P],
     "kadllm_qk_norm_rope": [P, L, L, L, L, P, P, F, P, P, L, P, L, L, P, L, L, P, L, L, L, P, L, L, L, L, P],
-    "kadllm_conv1d_prefill": [P, L, P, P, L, P, L, L, L, P],
-    "kadllm_gdn_prefill": [P, L, P, L, L, P, P, P, F, P, L, P, L, L, L, L, L, L, P],
+    "kadllm_gdn_prefill_split": [P, L, P, P, P, P, P, F, P, L, P, P, L, L, L, L, L, L, L, P],
     "kadllm_causal_attention": [P, L, L, P, L, L, L, P, L, L, L, P, L, L, P, L, L, L, L, L, L, L, F, P],
     "kadllm_beam_select": [P, I, L, P, P, P, P, P, P, L, L, L, L, L, L, P],
     "kadllm_beam_select_status": [P, L, L, P, P],
@@ -51,6 +50,8 @@ def lib() -> ctypes.CDLL:
         handle.kadllm_abi_version.restype = ctypes.c_int
         handle.kadllm_beam_select_workspace.restype = ctypes.c_int64
         handle.kadllm_beam_select_workspace.argtypes = [L, L]
+        handle.kadllm_gdn_prefill_workspace.restype = ctypes.c_int64
+        handle.kadllm_gdn_prefill_workspace.argtypes = [L, L, L, L, L]
         for name, args in SIGNATURES.items():
             fn = getattr(handle, name)
             fn.argtypes = args
@@ -63,7 +64,7 @@ _ERRORS = {1: ValueError, 2: TypeError, 3: NotImplementedError, 4: RuntimeError}
 
 
 # kernels launched per successful call of each entry point (for launch accounting)
-LAUNCHES_PER_CALL = {"kadllm_beam_select": 4, "kadllm_beam_select_status": 0}
+LAUNCHES_PER_CALL = {"kadllm_beam_select": 4, "kadllm_beam_select_status": 0, "kadllm_gdn_prefill_split": 2}
 launch_count = 0
 
 

@@ -39,6 +39,55 @@ __device__ __forceinline__ void warp_mma(float (&acc)[NT][4], const __nv_bfloat1
   }
 }
 
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(r) : "f"(x));
+  return r;
+}
+
+// D = A(16x8 row, tf32) * B(8x8 col, tf32) + D
+__device__ __forceinline__ void mma_tf32_1688(float d[4], const uint32_t a[4], const uint32_t b[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// acc[NT][4] += A(16 x K) * B(K x 8*NT) from row-major fp32 shared-memory blocks, TF32 tensor cores.
+template <int K, int NT>
+__device__ __forceinline__ void warp_mma_tf32(float (&acc)[NT][4], const float* A, int lda, const float* B, int ldb) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+#pragma unroll
+  for (int k0 = 0; k0 < K; k0 += 8) {
+    uint32_t a[4];
+    a[0] = to_tf32(A[g * lda + k0 + tq]);
+    a[1] = to_tf32(A[(g + 8) * lda + k0 + tq]);
+    a[2] = to_tf32(A[g * lda + k0 + tq + 4]);
+    a[3] = to_tf32(A[(g + 8) * lda + k0 + tq + 4]);
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      uint32_t b[2];
+      b[0] = to_tf32(B[(k0 + tq) * ldb + j * 8 + g]);
+      b[1] = to_tf32(B[(k0 + tq + 4) * ldb + j * 8 + g]);
+      mma_tf32_1688(acc[j], a, b);
+    }
+  }
+}
+
+// Store a 16 x 8*NT fp32 accumulator tile (scaled by `mul`) to row-major shared memory.
+template <int NT>
+__device__ __forceinline__ void store_acc(float* C, int ldc, const float (&acc)[NT][4], float mul) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+#pragma unroll
+  for (int j = 0; j < NT; ++j) {
+    C[g * ldc + j * 8 + 2 * tq] = mul * acc[j][0];
+    C[g * ldc + j * 8 + 2 * tq + 1] = mul * acc[j][1];
+    C[(g + 8) * ldc + j * 8 + 2 * tq] = mul * acc[j][2];
+    C[(g + 8) * ldc + j * 8 + 2 * tq + 1] = mul * acc[j][3];
+  }
+}
+
 template <int NT>
 __device__ __forceinline__ void zero_acc(float (&acc)[NT][4]) {
 #pragma unroll

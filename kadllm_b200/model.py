@@ -100,9 +100,13 @@ class HybridModel:
             p = f"layers.{i}."
             if kind == LINEAR:
                 q = p + "linear_attn."
+                w_in = torch.cat([bf(q + "in_proj_qkv.weight"), bf(q + "in_proj_z.weight"),
+                                  bf(q + "in_proj_b.weight"), bf(q + "in_proj_a.weight")])
+                pad = (-w_in.shape[0]) % 8  # 16-byte projection rows for vector loads
+                if pad:
+                    w_in = torch.cat([w_in, w_in.new_zeros(pad, w_in.shape[1])])
                 mixer = GDNLayer(
-                    w_in=torch.cat([bf(q + "in_proj_qkv.weight"), bf(q + "in_proj_z.weight"),
-                                    bf(q + "in_proj_b.weight"), bf(q + "in_proj_a.weight")]).contiguous(),
+                    w_in=w_in.contiguous(),
                     w_out=bf(q + "out_proj.weight"),
                     conv_w=bf(q + "conv1d.weight").reshape(cfg.conv_dim, -1).contiguous(),
                     a_log=f32(q + "A_log"), dt_bias=f32(q + "dt_bias"), norm_w=f32(q + "norm.weight"))
@@ -187,21 +191,24 @@ class HybridModel:
         s = self._stream()
         prefix = []
         hk, D, hq = c.num_key_value_heads, c.head_dim, c.num_attention_heads
+        ws = None  # GDN prefill workspace, shared by the GDN layers
         for i, layer in enumerate(self.layers):
             m = layer.mixer
             P = F.linear(normed, m.w_in)
             if layer.kind == LINEAR:
-                qkv = torch.empty(R, c.conv_dim, dtype=BF16, device=self.device)
                 conv_state = torch.empty(B, c.conv_dim, 4, dtype=BF16, device=self.device)
-                _lib.call("kadllm_conv1d_prefill", P.data_ptr(), P.stride(0), m.conv_w.data_ptr(), qkv.data_ptr(),
-                          qkv.stride(0), conv_state.data_ptr(), B, L, c.conv_dim, s)
                 out = torch.empty(R, c.value_dim, dtype=BF16, device=self.device)
                 rec = torch.empty(B, c.linear_num_value_heads, c.linear_key_head_dim, c.linear_value_head_dim,
                                   dtype=BF16, device=self.device)
-                _lib.call("kadllm_gdn_prefill", qkv.data_ptr(), qkv.stride(0), P.data_ptr(), P.stride(0), c.conv_dim,
-                          m.a_log.data_ptr(), m.dt_bias.data_ptr(), m.norm_w.data_ptr(), c.rms_norm_eps,
-                          out.data_ptr(), out.stride(0), rec.data_ptr(), B, L, c.linear_num_key_heads,
-                          c.linear_num_value_heads, c.linear_key_head_dim, c.linear_value_head_dim, s)
+                if ws is None:
+                    ws = torch.empty(_lib.lib().kadllm_gdn_prefill_workspace(
+                        B, L, c.linear_num_value_heads, c.linear_key_head_dim, c.linear_value_head_dim),
+                        dtype=torch.uint8, device=self.device)
+                _lib.call("kadllm_gdn_prefill_split", P.data_ptr(), P.stride(0), m.conv_w.data_ptr(),
+                          conv_state.data_ptr(), m.a_log.data_ptr(), m.dt_bias.data_ptr(), m.norm_w.data_ptr(),
+                          c.rms_norm_eps, out.data_ptr(), out.stride(0), rec.data_ptr(), ws.data_ptr(), ws.numel(),
+                          B, L, c.linear_num_key_heads, c.linear_num_value_heads, c.linear_key_head_dim,
+                          c.linear_value_head_dim, s)
                 delta = F.linear(out, m.w_out)
                 prefix.append((conv_state, rec))
             else:

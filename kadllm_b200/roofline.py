@@ -18,8 +18,8 @@ from . import _lib
 
 def work_of(name: str, args: tuple) -> tuple[str, float] | None:
     """(bound, algorithmic work) of one call: ("tensor", FLOPs) or ("hbm", bytes)."""
-    if name == "kadllm_gdn_prefill":
-        B, L, H, HV, DK, DV = args[12:18]
+    if name == "kadllm_gdn_prefill_split":
+        B, L, H, HV, DK, DV = args[13:19]
         chunks = -(-L // 64)
         per_chunk = 2 * 64 * (2 * 64 * DK + 3 * DK * DV + 2 * 64 * DV)
         return "tensor", float(B * HV * chunks * per_chunk)
@@ -39,9 +39,6 @@ def work_of(name: str, args: tuple) -> tuple[str, float] | None:
         B, Wp, V, W, depth = args[10:15]
         esz = 4 if args[1] == 0 else 2
         return "hbm", float(B * Wp * V * esz)
-    if name == "kadllm_conv1d_prefill":
-        B, L, C = args[6:9]
-        return "hbm", float(B * L * C * 2 * 2)
     if name == "kadllm_silu_mul":
         inter, rows = args[2], args[4]
         return "hbm", float(rows * inter * 2 * 3)

@@ -100,58 +100,6 @@ def test_qk_norm_rope_prefill_and_decode(D, hq, hk):
     np.testing.assert_array_equal(N(vc).transpose(0, 2, 1, 3), vs)
 
 
-def test_conv1d_prefill():
-    rng = np.random.default_rng(1)
-    B, L, C = 2, 70, 384
-    ld = C + 40
-    P = O.bf16(rng.standard_normal((B * L, ld)).astype(np.float32))
-    w = O.bf16(0.5 * rng.standard_normal((C, 4)).astype(np.float32))
-    out = torch.empty(B * L, C, dtype=bf, device="cuda")
-    state = torch.empty(B, C, 4, dtype=bf, device="cuda")
-    tP, tw = T(P), T(w)
-    _lib.call("kadllm_conv1d_prefill", tP.data_ptr(), ld, tw.data_ptr(), out.data_ptr(), C, state.data_ptr(), B,
-              L, C, S())
-    x = P[:, :C].reshape(B, L, C).transpose(0, 2, 1)  # B C L
-    xp = np.concatenate([np.zeros((B, C, 3), np.float32), x], -1)
-    acc = sum(xp[:, :, j:j + L] * w[None, :, j:j + 1] for j in range(4))
-    ref = O.silu(acc).transpose(0, 2, 1).reshape(B * L, C)
-    assert_close_rel(N(out), ref, rel=5e-3, what="conv out")
-    np.testing.assert_array_equal(N(state), x[:, :, L - 4:])
-
-
-@pytest.mark.parametrize("K,H,L", [(32, 4, 100), (128, 2, 130)])
-def test_gdn_prefill_matches_chunk_rule(K, H, L):
-    rng = np.random.default_rng(K + L)
-    B, HV = 2, H
-    kd, vd = H * K, HV * K
-    C = 2 * kd + vd
-    ld = C + vd + 2 * HV
-    qkv = O.bf16(rng.standard_normal((B * L, C)).astype(np.float32))
-    P = O.bf16(rng.standard_normal((B * L, ld)).astype(np.float32))
-    a_log = O.bf16(np.log(rng.uniform(1, 16, HV)).astype(np.float32))
-    dtb = O.bf16(rng.uniform(-1, 1, HV).astype(np.float32))
-    nw = O.bf16(1 + 0.1 * rng.standard_normal(K).astype(np.float32))
-    out = torch.empty(B * L, vd, dtype=bf, device="cuda")
-    state = torch.empty(B, HV, K, K, dtype=bf, device="cuda")
-    keep = [T(qkv), T(P), T(a_log, torch.float32), T(dtb, torch.float32), T(nw, torch.float32)]
-    _lib.call("kadllm_gdn_prefill", keep[0].data_ptr(), C, keep[1].data_ptr(), ld, C, keep[2].data_ptr(),
-              keep[3].data_ptr(), keep[4].data_ptr(), 1e-6, out.data_ptr(), vd,
-              state.data_ptr(), B, L, H, HV, K, K, S())
-    x = qkv.reshape(B, L, C)
-    q = x[..., :kd].reshape(B, L, H, K)
-    k = x[..., kd:2 * kd].reshape(B, L, H, K)
-    v = x[..., 2 * kd:].reshape(B, L, HV, K)
-    Pz = P.reshape(B, L, ld)
-    beta = R(O.sigmoid(Pz[..., C + vd:C + vd + HV]))
-    g = (-np.exp(a_log) * O.softplus(Pz[..., C + vd + HV:] + dtb)).astype(np.float32)
-    # fp32 L2 normalisation (the kernel normalises in fp32, like fla)
-    o, st = O.chunk_gated_delta_rule(q, k, v, g, beta, O.Rounding("fp32"))
-    o = R(o)
-    ref = O.rms_norm_gated(o.reshape(-1, K), Pz[..., C:C + vd].reshape(-1, K), nw, 1e-6, R).reshape(B * L, vd)
-    assert_close_rel(N(state), st, rel=1e-2, what="final state")
-    assert_close_rel(N(out), ref, rel=1e-2, what="gated output")
-
-
 @pytest.mark.parametrize("D,hq,hk,L", [(32, 4, 2, 64), (256, 8, 2, 100)])
 def test_causal_attention_prefill(D, hq, hk, L):
     rng = np.random.default_rng(D + L)
@@ -176,3 +124,43 @@ def test_causal_attention_prefill(D, hq, hk, L):
     o = R(np.matmul(p / p.sum(-1, keepdims=True), vh)).transpose(0, 2, 1, 3).reshape(B * L, hq * D)
     ref = R(o * R(O.sigmoid(gate[..., D:].reshape(B * L, hq * D))))
     assert_close_rel(N(out), ref, rel=1e-2, what="causal attention")
+
+
+@pytest.mark.parametrize("K,H,L", [(32, 4, 100), (128, 2, 130), (128, 2, 64), (64, 2, 3)])
+def test_gdn_prefill_split_matches_oracle(K, H, L):
+    """Conv + gates + chunked rule + gated norm from the packed projection, and
+    the conv / recurrent prefix states, against the oracle's restatement."""
+    rng = np.random.default_rng(K + L + 7)
+    B, HV = 2, H
+    kd, vd = H * K, HV * K
+    C = 2 * kd + vd
+    ld = (C + vd + 2 * HV + 7) // 8 * 8  # projection rows padded to 16 bytes
+    P = O.bf16(rng.standard_normal((B * L, ld)).astype(np.float32))
+    cw = O.bf16(0.5 * rng.standard_normal((C, 4)).astype(np.float32))
+    a_log = O.bf16(np.log(rng.uniform(1, 16, HV)).astype(np.float32))
+    dtb = O.bf16(rng.uniform(-1, 1, HV).astype(np.float32))
+    nw = O.bf16(1 + 0.1 * rng.standard_normal(K).astype(np.float32))
+    keep = [T(P), T(cw), T(a_log, torch.float32), T(dtb, torch.float32), T(nw, torch.float32)]
+    out = torch.empty(B * L, vd, dtype=bf, device="cuda")
+    state = torch.empty(B, HV, K, K, dtype=bf, device="cuda")
+    cstate = torch.empty(B, C, 4, dtype=bf, device="cuda")
+    nbytes = _lib.lib().kadllm_gdn_prefill_workspace(B, L, HV, K, K)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    _lib.call("kadllm_gdn_prefill_split", keep[0].data_ptr(), ld, keep[1].data_ptr(), cstate.data_ptr(),
+              keep[2].data_ptr(), keep[3].data_ptr(), keep[4].data_ptr(), 1e-6, out.data_ptr(), vd, state.data_ptr(),
+              ws.data_ptr(), nbytes, B, L, H, HV, K, K, S())
+    x = P[:, :C].reshape(B, L, C).transpose(0, 2, 1)  # B C L
+    xp = np.concatenate([np.zeros((B, C, 3), np.float32), x], -1)
+    conv = R(O.silu(sum(xp[:, :, j:j + L] * cw[None, :, j:j + 1] for j in range(4)))).transpose(0, 2, 1)
+    q = conv[..., :kd].reshape(B, L, H, K)
+    k = conv[..., kd:2 * kd].reshape(B, L, H, K)
+    v = conv[..., 2 * kd:].reshape(B, L, HV, K)
+    Pz = P.reshape(B, L, ld)
+    beta = R(O.sigmoid(Pz[..., C + vd:C + vd + HV]))
+    g = (-np.exp(a_log) * O.softplus(Pz[..., C + vd + HV:C + vd + 2 * HV] + dtb)).astype(np.float32)
+    o, st = O.chunk_gated_delta_rule(q, k, v, g, beta, O.Rounding("fp32"))
+    ref = O.rms_norm_gated(R(o).reshape(-1, K), Pz[..., C:C + vd].reshape(-1, K), nw, 1e-6, R).reshape(B * L, vd)
+    pad = np.concatenate([np.zeros((B, C, 4), np.float32), x], -1)[:, :, -4:]
+    np.testing.assert_array_equal(N(cstate), pad)
+    assert_close_rel(N(state), st, rel=1e-2, what="final state")
+    assert_close_rel(N(out), ref, rel=1e-2, what="gated output")
