@@ -6,9 +6,7 @@
 // by its own T suffix columns, then applies SiLU.  fp32 accumulation, one
 // rounding to the output dtype.  The state is only read.
 //
-// HBM-bound: one thread per (beam row, channel) walks the T columns keeping
-// the sliding window in registers; channels are the fastest-varying index so
-// reads of the (typically channel-contiguous) projection are coalesced.
+// HBM-bound; see the tile comment on the kernel for the access pattern.
 #include "common.cuh"
 
 namespace kb {
@@ -24,25 +22,49 @@ struct ConvArgs {
   int dtype, BW, W, C, T, width, silu;
 };
 
+// One CTA = (beam row, 32 channels, 64 time steps).  The input window (tile plus
+// width-1 steps of history, taken from the request's conv state before t = 0) is
+// staged in shared memory with the access order matching x's fastest stride, and
+// the [BW, C, T] output is written along time, so both sides are coalesced.
+constexpr int kCT = 32, kTT = 64;
+
 __global__ void __launch_bounds__(256) conv_replay_kernel(const ConvArgs a) {
-  const int c = blockIdx.y * blockDim.x + threadIdx.x;
+  __shared__ float sx[kCT][kTT + kMaxWidth];
+  __shared__ float sy[kCT][kTT + 1];
   const int r = blockIdx.x;
-  if (c >= a.C) return;
+  const int c0 = blockIdx.y * kCT;
+  const int t0 = blockIdx.z * kTT;
   const int req = r / a.W;
-  float w[kMaxWidth], win[kMaxWidth];
-  for (int j = 0; j < a.width; ++j) w[j] = load_as_float(a.weight, int64_t(c) * a.width + j, a.dtype);
-  // window[0 .. width-2] = last width-1 prefix taps
-  for (int j = 0; j < a.width - 1; ++j)
-    win[j] = load_as_float(a.state, req * a.ss0 + c * a.ss1 + int64_t(a.hist - (a.width - 1) + j) * a.ss2, a.dtype);
-  const float bias = a.bias ? load_as_float(a.bias, c, a.dtype) : 0.f;
-  for (int t = 0; t < a.T; ++t) {
-    const float xt = load_as_float(a.x, r * a.xs0 + c * a.xs1 + int64_t(t) * a.xs2, a.dtype);
-    win[a.width - 1] = xt;
-    float acc = bias;
-    for (int j = 0; j < a.width; ++j) acc += win[j] * w[j];
-    const float o = a.silu ? silu_f(acc) : acc;
-    store_from_float(a.out, (int64_t(r) * a.C + c) * a.T + t, a.dtype, o);
-    for (int j = 0; j + 1 < a.width; ++j) win[j] = win[j + 1];
+  const int halo = a.width - 1;
+  const int span = kTT + halo;
+  const bool chan_fast = a.xs1 == 1;
+  for (int i = threadIdx.x; i < kCT * span; i += blockDim.x) {
+    const int ci = chan_fast ? i % kCT : i / span;
+    const int ti = chan_fast ? i / kCT : i % span;
+    const int c = c0 + ci, t = t0 + ti - halo;
+    float v = 0.f;
+    if (c < a.C && t < a.T) {
+      if (t >= 0)
+        v = load_as_float(a.x, r * a.xs0 + c * a.xs1 + int64_t(t) * a.xs2, a.dtype);
+      else
+        v = load_as_float(a.state, req * a.ss0 + c * a.ss1 + int64_t(a.hist + t) * a.ss2, a.dtype);
+    }
+    sx[ci][ti] = v;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < kCT * kTT; i += blockDim.x) {
+    const int ci = i / kTT, tt = i % kTT;
+    const int c = c0 + ci;
+    if (c >= a.C) continue;
+    float acc = a.bias ? load_as_float(a.bias, c, a.dtype) : 0.f;
+    for (int j = 0; j < a.width; ++j) acc += sx[ci][tt + j] * load_as_float(a.weight, int64_t(c) * a.width + j, a.dtype);
+    sy[ci][tt] = a.silu ? silu_f(acc) : acc;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < kCT * kTT; i += blockDim.x) {
+    const int ci = i / kTT, tt = i % kTT;
+    const int c = c0 + ci, t = t0 + tt;
+    if (c < a.C && t < a.T) store_from_float(a.out, (int64_t(r) * a.C + c) * a.T + t, a.dtype, sy[ci][tt]);
   }
 }
 
@@ -65,10 +87,10 @@ extern "C" int kadllm_causal_conv1d_replay(const void* x, int64_t xs0, int64_t x
   KB_REQUIRE(x && state && weight && out, KADLLM_EINVAL, "conv replay: null pointer");
   ConvArgs a{x, xs0, xs1, xs2, state, ss0, ss1, ss2, int(hist), weight, bias, out, dtype,
              int(batch * beam_width), int(beam_width), int(channels), int(steps), int(width), silu};
-  const int threads = 256;
-  KB_REQUIRE((channels + threads - 1) / threads <= 65535, KADLLM_EINVAL, "conv replay: too many channels");
-  dim3 grid(unsigned(batch * beam_width), unsigned((channels + threads - 1) / threads));
-  conv_replay_kernel<<<grid, threads, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  KB_REQUIRE((channels + kCT - 1) / kCT <= 65535 && (steps + kTT - 1) / kTT <= 65535, KADLLM_EINVAL,
+             "conv replay: too many channels or steps");
+  dim3 grid(unsigned(batch * beam_width), unsigned((channels + kCT - 1) / kCT), unsigned((steps + kTT - 1) / kTT));
+  conv_replay_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(a);
   KB_CHECK_LAUNCH("conv replay launch");
   return KADLLM_OK;
 }

@@ -1,0 +1,156 @@
+"""Kernel microbenchmarks at the BASELINE shapes (seeded synthetic inputs).
+
+    python -m kadllm_b200.kernel_bench --case prefill|conv|attn|mixer|select [--reps N]
+
+Cases (BASELINE config 5 and the GRBeam step shapes):
+  prefill  chunked gated-delta prefill (conv + gates + UT transform + scan +
+           gated norm) from the packed projection: B=32, T=1024, 16 heads of 128
+  conv     causal conv1d width 4 + SiLU over T=1024, 2048 channels (B=32)
+  attn     shared-prefix decode attention: 256 beams x 8 q / 2 kv heads x d=256
+           against a 4096-token prefix plus a 3-token causal suffix
+  mixer    fused GDN decode mixer: 32 requests x 256 beams, T = 1 and 2
+  select   one selection step over 32 x 256 x 248320 bf16 logits
+Each prints one JSON line: device time per call (CUDA events, after warm-up),
+algorithmic work, achieved rate and the fraction of the measured B200 peak.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+from pathlib import Path
+
+import torch
+
+from . import _lib, ops
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def _time(fn, reps: int, warmup: int = 3) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / reps
+
+
+def case_prefill(gen, reps):
+    dev, bf = torch.device("cuda"), torch.bfloat16
+    B, L, H, HV, K = 32, 1024, 16, 16, 128
+    C = 2 * H * K + HV * K
+    ld = C + HV * K + 2 * HV
+    P = torch.randn(B * L, ld, device=dev, generator=gen).to(bf)
+    cw = (0.3 * torch.randn(C, 4, device=dev, generator=gen)).to(bf)
+    al = torch.rand(HV, device=dev, generator=gen) * 2
+    dt = torch.rand(HV, device=dev, generator=gen)
+    nw = torch.ones(K, device=dev)
+    out = torch.empty(B * L, HV * K, device=dev, dtype=bf)
+    st = torch.empty(B, HV, K, K, device=dev, dtype=bf)
+    cs = torch.empty(B, C, 4, device=dev, dtype=bf)
+    nb = _lib.lib().kadllm_gdn_prefill_workspace(B, L, HV, K, K)
+    ws = torch.empty(nb, dtype=torch.uint8, device=dev)
+    s = _lib.stream(dev)
+
+    def run():
+        _lib.call("kadllm_gdn_prefill_split", P.data_ptr(), ld, cw.data_ptr(), cs.data_ptr(), al.data_ptr(),
+                  dt.data_ptr(), nw.data_ptr(), 1e-6, out.data_ptr(), HV * K, st.data_ptr(), ws.data_ptr(), nb,
+                  B, L, H, HV, K, K, s)
+
+    ms = _time(run, reps)
+    flops = B * HV * (L // 64) * 2 * 64 * (2 * 64 * K + 3 * K * K + 2 * 64 * K)
+    return ms, "tensor", flops
+
+
+def case_conv(gen, reps):
+    dev, bf = torch.device("cuda"), torch.bfloat16
+    B, C, T = 32, 2048, 1024
+    x = torch.randn(B, T, C, device=dev, generator=gen).to(bf).transpose(1, 2)  # [B, C, T] view
+    state = torch.zeros(B, C, 3, device=dev, dtype=bf)
+    w = (0.3 * torch.randn(C, 4, device=dev, generator=gen)).to(bf)
+    ms = _time(lambda: ops.causal_conv1d(x, state, w, beam_width=1), reps)
+    return ms, "hbm", B * C * T * 2 * 2
+
+
+def case_attn(gen, reps):
+    dev, bf = torch.device("cuda"), torch.bfloat16
+    B, W, T, L, Hq, HK, D = 1, 256, 3, 4096, 8, 2, 256
+    n = lambda *s: torch.randn(*s, device=dev, generator=gen).to(bf)
+    q, sk, sv = n(B * W, T, Hq, D), n(B * W, T, HK, D), n(B * W, T, HK, D)
+    pk, pv = n(B, L, HK, D), n(B, L, HK, D)
+    ms = _time(lambda: ops.prefix_attention(q, pk, pv, sk, sv, beam_width=W), reps)
+    return ms, "tensor", 4 * B * W * T * Hq * D * L + 4 * B * W * Hq * D * T * (T + 1) / 2
+
+
+def case_mixer(gen, reps, T=1):
+    dev, bf = torch.device("cuda"), torch.bfloat16
+    B, W, H, HV, K = 32, 256, 16, 16, 128
+    C = 2 * H * K + HV * K
+    ld = C + HV * K + 2 * HV
+    proj = (0.5 * torch.randn(B * W * T, ld, device=dev, generator=gen)).to(bf)
+    cs = torch.randn(B, C, 4, device=dev, generator=gen).to(bf)
+    cw = (0.3 * torch.randn(C, 4, device=dev, generator=gen)).to(bf)
+    rec = (0.1 * torch.randn(B, HV, K, K, device=dev, generator=gen)).to(bf)
+    al = torch.rand(HV, device=dev, generator=gen) * 2
+    dt = torch.rand(HV, device=dev, generator=gen)
+    nw = torch.ones(K, device=dev)
+    out = torch.empty(B * W * T, HV * K, device=dev, dtype=bf)
+    s = _lib.stream(dev)
+
+    def run():
+        _lib.call("kadllm_gdn_mixer_replay", proj.data_ptr(), ld, cs.data_ptr(), 4, cw.data_ptr(), rec.data_ptr(),
+                  al.data_ptr(), dt.data_ptr(), nw.data_ptr(), 1e-6, out.data_ptr(), B, W, T, H, HV, K, K, s)
+
+    ms = _time(run, reps)
+    R = B * W * T
+    return ms, "hbm", R * ld * 2 + R * HV * K * 2 + B * HV * K * K * 2 + B * C * 4 * 2
+
+
+def case_select(gen, reps):
+    from .grbeam import BeamSelector
+
+    dev = torch.device("cuda")
+    B, Wp, V, W = 32, 256, 248320, 256
+    logits = (0.5 * torch.randn(B, Wp, V, device=dev, generator=gen)).to(torch.bfloat16)
+    parent = -torch.rand(B, Wp, device=dev, generator=gen) * 4
+    hist = torch.zeros(B, Wp, 1, dtype=torch.int64, device=dev)
+    sel = BeamSelector(B, Wp, dev)
+    ms = _time(lambda: sel.step(logits, parent, hist, W), reps)
+    return ms, "hbm", B * Wp * V * 2
+
+
+CASES = {"prefill": case_prefill, "conv": case_conv, "attn": case_attn, "mixer": case_mixer,
+         "mixer2": lambda g, r: case_mixer(g, r, T=2), "select": case_select}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--case", choices=sorted(CASES), required=True)
+    ap.add_argument("--reps", type=int, default=10)
+    args = ap.parse_args()
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    ms, bound, work = CASES[args.case](gen, args.reps)
+    hbm, tflops, kind = _peaks()
+    if bound == "tensor":
+        achieved, peak, unit = work / (ms / 1e3) / 1e12, tflops, "TFLOP/s"
+    else:
+        achieved, peak, unit = work / (ms / 1e3) / 1e9, hbm, "GB/s"
+    print(json.dumps({"case": args.case, "ms": ms, "bound": bound, "work": work, "achieved": achieved,
+                      "unit": unit, "peak": peak, "frac": achieved / peak, "peak_kind": kind}))
+
+
+if __name__ == "__main__":
+    main()
