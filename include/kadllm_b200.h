@@ -152,6 +152,25 @@ KADLLM_API int kadllm_beam_select(const void* logits, int logits_dtype, int64_t 
 KADLLM_API int kadllm_beam_select_status(const void* workspace, int64_t batch, int64_t prev_width,
                                          uint32_t* flags_out, void* stream);
 
+/* Allocation-free variant of kadllm_beam_select (no counterpart in the
+ * reference).  For callers that cannot allocate device memory where they
+ * select beams -- a captured CUDA-graph region with a frozen memory pool, a
+ * host that hands the library only the tensors it owns, an allocator that may
+ * not grow on the decode path.  Its scratch is one 9 MiB array in the
+ * library's device image, reserved on every GPU that loads the library until
+ * the process exits; limits: batch <= 32 and batch * prev_width <= 512 (larger
+ * sizes return KADLLM_EINVAL).  The first call on a device resolves the
+ * array's address (do it before any stream capture).  All calls share the
+ * array: calls whose work overlaps on the GPU race and must be serialised.
+ * out_flags (device, one word) receives bit 0 = candidate overflow; the other
+ * arguments and results are those of kadllm_beam_select. */
+KADLLM_API int kadllm_beam_select_noalloc(const void* logits, int logits_dtype, int64_t ld_row,
+                                          const float* parent_scores, const void* mask,
+                                          const int64_t* old_history, float* out_scores,
+                                          int64_t* out_history, uint32_t* out_flags, int64_t batch,
+                                          int64_t prev_width, int64_t vocab, int64_t width,
+                                          int64_t depth, void* stream);
+
 /* ========================================================================
  * Model building blocks of the native Qwen3.5 hybrid pipeline (BF16).  Each
  * replaces a Transformers module on the reference's prefill / decode path

@@ -26,6 +26,7 @@ SIGNATURES: dict[str, list] = {
     "kadllm_causal_attention": [P, L, L, P, L, L, L, P, L, L, L, P, L, L, P, L, L, L, L, L, L, L, F, P],
     "kadllm_beam_select": [P, I, L, P, P, P, P, P, P, L, L, L, L, L, L, P],
     "kadllm_beam_select_status": [P, L, L, P, P],
+    "kadllm_beam_select_noalloc": [P, I, L, P, P, P, P, P, P, L, L, L, L, L, P],
     "kadllm_gated_delta_replay": [P, P, P, I, P, I, P, I, P, I, P, L, L, L, L, L, L, L, F, P],
     "kadllm_gdn_mixer_replay": [P, L, P, L, P, P, P, P, P, F, P, L, L, L, L, L, L, L, P],
     "kadllm_causal_conv1d_replay": [P, L, L, L, P, L, L, L, L, P, P, P, I, L, L, L, L, L, I, P],
@@ -64,7 +65,7 @@ _ERRORS = {1: ValueError, 2: TypeError, 3: NotImplementedError, 4: RuntimeError}
 
 
 # kernels launched per successful call of each entry point (for launch accounting)
-LAUNCHES_PER_CALL = {"kadllm_beam_select": 4, "kadllm_beam_select_status": 0, "kadllm_gdn_prefill_split": 2}
+LAUNCHES_PER_CALL = {"kadllm_beam_select": 4, "kadllm_beam_select_noalloc": 4, "kadllm_beam_select_status": 0, "kadllm_gdn_prefill_split": 2}
 launch_count = 0
 
 

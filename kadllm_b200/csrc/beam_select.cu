@@ -22,6 +22,8 @@
 //   4. finalize   per request: bitonic sort of the buffer (score desc, index
 //                 asc), writes scores and the gathered history.
 // Buffers live in a caller-provided workspace (kadllm_beam_select_workspace).
+#include <mutex>
+
 #include "common.cuh"
 
 namespace kb {
@@ -298,12 +300,14 @@ extern "C" int64_t kadllm_beam_select_workspace(int64_t batch, int64_t prev_widt
   return int64_t(kb::Workspace(batch, prev_width).total);
 }
 
-extern "C" int kadllm_beam_select(const void* logits, int logits_dtype, int64_t ld_row, const float* parent_scores,
-                                  const void* mask, const int64_t* old_history, float* out_scores,
-                                  int64_t* out_history, void* workspace, int64_t workspace_bytes, int64_t batch,
-                                  int64_t prev_width, int64_t vocab, int64_t width, int64_t depth,
-                                  void* stream) {
-  using namespace kb;
+namespace kb {
+namespace {
+// Shared body of the selection entry points.  `flags` overrides the workspace's
+// flag word when non-null.
+int select_with_workspace(const void* logits, int logits_dtype, int64_t ld_row, const float* parent_scores,
+                          const void* mask, const int64_t* old_history, float* out_scores, int64_t* out_history,
+                          void* workspace, int64_t workspace_bytes, uint32_t* flags, int64_t batch,
+                          int64_t prev_width, int64_t vocab, int64_t width, int64_t depth, void* stream) {
   KB_REQUIRE(valid_dtype(logits_dtype), KADLLM_EDTYPE, "beam select: unsupported logits dtype");
   KB_REQUIRE(batch >= 1 && prev_width >= 1 && vocab >= 1 && width >= 1 && depth >= 0, KADLLM_EINVAL,
              "beam select: empty dimensions");
@@ -327,7 +331,7 @@ extern "C" int kadllm_beam_select(const void* logits, int logits_dtype, int64_t 
   a.rowhist = reinterpret_cast<uint32_t*>(w + ws.rowhist);
   a.thresh = reinterpret_cast<float*>(w + ws.thresh);
   a.count = reinterpret_cast<uint32_t*>(w + ws.count);
-  a.flags = reinterpret_cast<uint32_t*>(w + ws.flags);
+  a.flags = flags ? flags : reinterpret_cast<uint32_t*>(w + ws.flags);
   a.cand = reinterpret_cast<unsigned long long*>(w + ws.cand);
   a.B = int(batch); a.Wp = int(prev_width); a.W = int(width); a.depth = int(depth); a.V = vocab;
   const int esz = dtype_size(logits_dtype);
@@ -337,6 +341,18 @@ extern "C" int kadllm_beam_select(const void* logits, int logits_dtype, int64_t 
   if (logits_dtype == KADLLM_BF16) return launch_select<__nv_bfloat16>(a, vec, s);
   if (logits_dtype == KADLLM_F16) return launch_select<__half>(a, vec, s);
   return launch_select<float>(a, vec, s);
+}
+}  // namespace
+}  // namespace kb
+
+extern "C" int kadllm_beam_select(const void* logits, int logits_dtype, int64_t ld_row, const float* parent_scores,
+                                  const void* mask, const int64_t* old_history, float* out_scores,
+                                  int64_t* out_history, void* workspace, int64_t workspace_bytes, int64_t batch,
+                                  int64_t prev_width, int64_t vocab, int64_t width, int64_t depth,
+                                  void* stream) {
+  return kb::select_with_workspace(logits, logits_dtype, ld_row, parent_scores, mask, old_history, out_scores,
+                                   out_history, workspace, workspace_bytes, nullptr, batch, prev_width, vocab,
+                                   width, depth, stream);
 }
 
 extern "C" int kadllm_beam_select_status(const void* workspace, int64_t batch, int64_t prev_width,
@@ -349,4 +365,77 @@ extern "C" int kadllm_beam_select_status(const void* workspace, int64_t batch, i
   if (e == cudaSuccess) e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
   KB_REQUIRE(e == cudaSuccess, KADLLM_ECUDA, "beam select status: %s", cudaGetErrorString(e));
   return KADLLM_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant.  Some callers cannot allocate device memory at the
+// point where they select beams: code running inside a captured or replayed
+// CUDA-graph region whose memory pool is frozen, embedded / plugin hosts that
+// hand the library only the tensors they own, and allocators that forbid
+// growth on the decode path.  For them the selection keeps its scratch in one
+// fixed array that lives in this library's device image.
+//
+// kNoAllocScratchBytes (9 MiB) is reserved on every GPU that loads the library,
+// until the process exits.  It covers batch * prev_width <= 512 rows and
+// batch <= 32 requests (per-row histograms 4 MiB, candidate buffers 4 MiB).
+// Every call shares the array and it keeps the previous call's contents: the
+// kernels rewrite everything they read except the per-request counters, which
+// the threshold kernel clears, so no clearing is needed here -- but two calls
+// whose work overlaps on the GPU (different streams, or graph branches) race on
+// the array and must be serialised by the caller.
+// ---------------------------------------------------------------------------
+namespace kb {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(9) << 20;
+static __device__ __align__(256) unsigned char g_select_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+void* g_scratch_ptr[kMaxDevices] = {};
+std::mutex g_scratch_mutex;
+
+// The host-side symbol is only a stand-in for the array: its device address is
+// resolved once per device, with that device current.
+int scratch_for_current_device(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  KB_REQUIRE(e == cudaSuccess, KADLLM_ECUDA, "beam select (no-alloc): cudaGetDevice: %s", cudaGetErrorString(e));
+  KB_REQUIRE(dev >= 0 && dev < kMaxDevices, KADLLM_EUNSUPPORTED, "beam select (no-alloc): device %d", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_select_scratch);
+    KB_REQUIRE(e == cudaSuccess && p != nullptr, KADLLM_ECUDA,
+               "beam select (no-alloc): cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return KADLLM_OK;
+}
+
+}  // namespace
+}  // namespace kb
+
+extern "C" int kadllm_beam_select_noalloc(const void* logits, int logits_dtype, int64_t ld_row,
+                                          const float* parent_scores, const void* mask,
+                                          const int64_t* old_history, float* out_scores,
+                                          int64_t* out_history, uint32_t* out_flags, int64_t batch,
+                                          int64_t prev_width, int64_t vocab, int64_t width, int64_t depth,
+                                          void* stream) {
+  using namespace kb;
+  KB_REQUIRE(out_flags, KADLLM_EINVAL, "beam select (no-alloc): null flags pointer");
+  KB_REQUIRE(batch >= 1 && prev_width >= 1, KADLLM_EINVAL, "beam select (no-alloc): empty dimensions");
+  const Workspace ws(batch, prev_width);
+  KB_REQUIRE(ws.total <= kNoAllocScratchBytes && batch <= 32 && batch * prev_width <= 512, KADLLM_EINVAL,
+             "beam select (no-alloc): batch %lld x prev_width %lld needs %zu bytes of scratch; the static "
+             "maximum is %zu bytes (batch <= 32, batch * prev_width <= 512)",
+             (long long)batch, (long long)prev_width, ws.total, kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  if (int rc = scratch_for_current_device(&scratch)) return rc;
+  // the caller's flag word replaces the scratch flag word: clear it, the kernels OR into it
+  cudaError_t e = cudaMemsetAsync(out_flags, 0, sizeof(uint32_t), static_cast<cudaStream_t>(stream));
+  KB_REQUIRE(e == cudaSuccess, KADLLM_ECUDA, "beam select (no-alloc): %s", cudaGetErrorString(e));
+  return select_with_workspace(logits, logits_dtype, ld_row, parent_scores, mask, old_history, out_scores,
+                               out_history, scratch, int64_t(kNoAllocScratchBytes), out_flags, batch, prev_width,
+                               vocab, width, depth, stream);
 }
