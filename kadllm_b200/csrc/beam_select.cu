@@ -23,6 +23,7 @@
 //                 asc), writes scores and the gathered history.
 // Buffers live in a caller-provided workspace (kadllm_beam_select_workspace).
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -45,6 +46,7 @@ struct SelArgs {
   int64_t* out_hist;           // [B*W, depth+1]
   float2* rowstat;             // [rows] (max, log-sum-exp offset)
   uint32_t* rowhist;           // [rows, kRowBins]
+  uint32_t* rowlen;            // [rows] leading bins of rowhist that can be non-zero
   float* thresh;               // [B]
   uint32_t* count;             // [B]
   uint32_t* flags;             // [1] bit 0: candidate overflow
@@ -125,6 +127,155 @@ __global__ void __launch_bounds__(kRowThreads) rowstats_kernel(const SelArgs a, 
   if (threadIdx.x == 0) a.rowstat[r] = make_float2(m, logf(s));
   __syncthreads();
   for (int i = threadIdx.x; i < kRowBins; i += blockDim.x) a.rowhist[r * kRowBins + i] = hist[i];
+  if (threadIdx.x == 0) a.rowlen[r] = kRowBins - 1;
+}
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// BF16 logits without a mask (the decode hot path).  Persistent: one
+// 1024-thread CTA per SM loops over rows and reads each row from HBM once.
+//   pass 1 (HBM): per-thread online max and sum of exp (rescaled when the
+//     thread's max grows), packed bf16x2 max per 16-byte vector;
+//   tau: a lower bound on the row's W-th largest value.  Each warp sorts its 32
+//     per-thread maxima; the minimum over the n warps of the ceil(W/n)-th
+//     largest leaves >= W elements of the row at or above tau.  Only those can
+//     be among the request's top W (a row shares parent score and normaliser),
+//     so binning only them leaves the threshold bin unchanged, and bins past
+//     tau's stay empty (rowlen);
+//   pass 2 (L2): threads whose maximum reaches tau re-read their slice and bin
+//     d = 32 (max - x) with one FFMA (bit-identical to (max - x) * 32).  Pass 2
+//     of row r runs inside pass 1 of the CTA's next row, so HBM never idles and
+//     about one row per SM (~74 MB at V = 248320) is live in L2.
+constexpr int kStatThreads = 1024;
+
+__device__ __forceinline__ float vec_max(const uint4& u) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+  const __nv_bfloat162 t = __hmax2(__hmax2(h[0], h[1]), __hmax2(h[2], h[3]));
+  return fmaxf(__low2float(t), __high2float(t));
+}
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&x)[8]) {
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(&u);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    x[2 * j] = __uint_as_float(w[j] << 16);
+    x[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+  }
+}
+
+struct OnlineSum {
+  float m = -INFINITY, ml = 0.f, s0 = 0.f, s1 = 0.f;
+  __device__ __forceinline__ void add(const uint4& u) {
+    const float hi = vec_max(u);
+    if (hi > m) {  // rare after the first vectors; -inf and NaN vectors never enter
+      const float c = ex2_approx((m - hi) * kLog2e);
+      s0 *= c;
+      s1 *= c;
+      m = hi;
+      ml = hi * kLog2e;
+    }
+    float x[8];
+    unpack8(u, x);
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+      s0 += ex2_approx(fmaf(x[j], kLog2e, -ml));
+      s1 += ex2_approx(fmaf(x[j + 1], kLog2e, -ml));
+    }
+  }
+};
+
+__device__ __forceinline__ void bin_vec(const uint4& u, float tau, float m32, uint32_t* hist) {
+  if (vec_max(u) >= tau) {
+    float x[8];
+    unpack8(u, x);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (x[j] >= tau) atomicAdd(&hist[int(fminf(fmaf(x[j], -kBinsPerNat, m32), float(kRowBins - 1)))], 1u);
+  }
+}
+
+__global__ void __launch_bounds__(kStatThreads, 1) rowstats_bf16_kernel(const SelArgs a) {
+  __shared__ uint32_t hist[kRowBins];
+  __shared__ float red[33];
+  constexpr int nt = kStatThreads, nwarps = kStatThreads / 32;
+  const int64_t rows = int64_t(a.B) * a.Wp;
+  const int nvec = int(a.V / 8);
+  const int tid = threadIdx.x, lane = tid & 31;
+  for (int j = tid; j < kRowBins; j += nt) hist[j] = 0;
+  // the CTA's previous row, binned while the current one streams in
+  const uint4* prow = nullptr;
+  int64_t pr = -1;
+  float ptau = 0.f, pm32 = 0.f;
+  int pbin = 0;
+  bool pact = false;
+  for (int64_t r = blockIdx.x;; r += gridDim.x) {
+    const bool cur = r < rows;
+    const uint4* row = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.logits) +
+                                                      (cur ? r : 0) * a.ld);
+    OnlineSum acc;
+    if (cur) {
+      int i = tid;
+      for (; i + 3 * nt < nvec; i += 4 * nt) {  // four 16-byte HBM loads in flight
+        const uint4 u0 = row[i], u1 = row[i + nt], u2 = row[i + 2 * nt], u3 = row[i + 3 * nt];
+        if (pact) {
+          const uint4 v0 = prow[i], v1 = prow[i + nt], v2 = prow[i + 2 * nt], v3 = prow[i + 3 * nt];
+          bin_vec(v0, ptau, pm32, hist);
+          bin_vec(v1, ptau, pm32, hist);
+          bin_vec(v2, ptau, pm32, hist);
+          bin_vec(v3, ptau, pm32, hist);
+        }
+        acc.add(u0);
+        acc.add(u1);
+        acc.add(u2);
+        acc.add(u3);
+      }
+      for (; i < nvec; i += nt) {
+        acc.add(row[i]);
+        if (pact) bin_vec(prow[i], ptau, pm32, hist);
+      }
+    } else if (pact) {
+      for (int i = tid; i < nvec; i += nt) bin_vec(prow[i], ptau, pm32, hist);
+    }
+    if (pr >= 0) {  // export the previous row's bins and clear them for the next
+      __syncthreads();
+      const int len = min(pbin + 1, kRowBins - 1);
+      if (tid == 0) a.rowlen[pr] = uint32_t(len);
+      for (int j = tid; j <= pbin; j += nt) {
+        if (j < len) a.rowhist[pr * kRowBins + j] = hist[j];
+        hist[j] = 0;
+      }
+    }
+    if (!cur) break;
+    const float mt = acc.m;
+    const float m = block_reduce(mt, true, red);
+    const float sum = block_reduce((acc.s0 + acc.s1) * ex2_approx((mt - m) * kLog2e), false, red);
+    float tau = -INFINITY;
+    if (a.W <= 32 * nwarps) {
+      const int kth = (a.W + nwarps - 1) / nwarps - 1;
+      float v = mt;
+#pragma unroll
+      for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+          const float o = __shfl_xor_sync(0xffffffffu, v, j);
+          v = (((lane & j) == 0) == ((lane & k) == 0)) ? fmaxf(v, o) : fminf(v, o);
+        }
+      }
+      tau = -block_reduce(-__shfl_sync(0xffffffffu, v, kth), true, red);
+    }
+    if (tid == 0) a.rowstat[r] = make_float2(m, logf(sum));
+    prow = row;
+    pr = r;
+    ptau = tau;
+    pm32 = m * kBinsPerNat;
+    // tau's bin bounds every binned element's; -inf, NaN (all -inf row) -> last bin
+    pbin = int(fminf(fmaf(tau, -kBinsPerNat, pm32), float(kRowBins - 1)));
+    pact = mt >= tau;
+  }
 }
 
 __global__ void __launch_bounds__(1024) threshold_kernel(const SelArgs a) {
@@ -142,8 +293,9 @@ __global__ void __launch_bounds__(1024) threshold_kernel(const SelArgs a) {
   sref = block_reduce(sref, true, red);
   for (int i = threadIdx.x; i < kReqBins; i += blockDim.x) rh[i] = 0;
   __syncthreads();
-  if (sref > -INFINITY) {
-    for (int w = 0; w < a.Wp; ++w) {
+  if (sref > -INFINITY) {  // one warp per row: rows are independent, bins few
+    const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int w = threadIdx.x >> 5; w < a.Wp; w += nw) {
       const int64_t r = int64_t(b) * a.Wp + w;
       const float p = a.parent ? a.parent[r] : 0.f;
       const float off = p - a.rowstat[r].y;
@@ -151,9 +303,10 @@ __global__ void __launch_bounds__(1024) threshold_kernel(const SelArgs a) {
       const float e = (sref - off) * kBinsPerNat;
       if (e >= float(kReqBins)) continue;
       const int base = int(e) + 1;
-      for (int j = threadIdx.x; j < kRowBins - 1; j += blockDim.x) {
+      const int len = min(int(a.rowlen[r]), kReqBins - base);
+      for (int j = lane; j < len; j += 32) {
         const uint32_t c = a.rowhist[r * kRowBins + j];
-        if (c && base + j < kReqBins) atomicAdd(&rh[base + j], c);
+        if (c) atomicAdd(&rh[base + j], c);
       }
     }
   }
@@ -261,12 +414,13 @@ __global__ void __launch_bounds__(1024) finalize_kernel(const SelArgs a) {
 }
 
 struct Workspace {
-  size_t rowstat, rowhist, thresh, count, flags, cand, total;
+  size_t rowstat, rowlen, rowhist, thresh, count, flags, cand, total;
   Workspace(int64_t B, int64_t Wp) {
     auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
     const int64_t rows = B * Wp;
     rowstat = 0;
-    rowhist = al(rowstat + rows * sizeof(float2));
+    rowlen = al(rowstat + rows * sizeof(float2));
+    rowhist = al(rowlen + rows * sizeof(uint32_t));
     thresh = al(rowhist + rows * kRowBins * sizeof(uint32_t));
     count = al(thresh + B * sizeof(float));
     flags = al(count + B * sizeof(uint32_t));
@@ -278,7 +432,16 @@ struct Workspace {
 template <typename T>
 int launch_select(SelArgs& a, bool vec, cudaStream_t s) {
   const int64_t rows = int64_t(a.B) * a.Wp;
-  rowstats_kernel<T><<<unsigned(rows), kRowThreads, 0, s>>>(a, vec);
+  static int num_sms = 0;
+  if (num_sms == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      num_sms = 148;
+  }
+  if (std::is_same<T, __nv_bfloat16>::value && vec && a.mask == nullptr)
+    rowstats_bf16_kernel<<<unsigned(rows < num_sms ? rows : num_sms), kStatThreads, 0, s>>>(a);
+  else
+    rowstats_kernel<T><<<unsigned(rows), kRowThreads, 0, s>>>(a, vec);
   threshold_kernel<<<a.B, 1024, 0, s>>>(a);
   collect_kernel<T><<<unsigned(rows), 256, 0, s>>>(a, vec);
   int N = 1;
@@ -329,6 +492,7 @@ int select_with_workspace(const void* logits, int logits_dtype, int64_t ld_row, 
   a.out_scores = out_scores; a.out_hist = out_history;
   a.rowstat = reinterpret_cast<float2*>(w + ws.rowstat);
   a.rowhist = reinterpret_cast<uint32_t*>(w + ws.rowhist);
+  a.rowlen = reinterpret_cast<uint32_t*>(w + ws.rowlen);
   a.thresh = reinterpret_cast<float*>(w + ws.thresh);
   a.count = reinterpret_cast<uint32_t*>(w + ws.count);
   a.flags = flags ? flags : reinterpret_cast<uint32_t*>(w + ws.flags);

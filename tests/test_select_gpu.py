@@ -51,14 +51,21 @@ def test_search_matches_reference_golden():
     np.testing.assert_allclose(r.scores.cpu().numpy(), g["coarse_scores"], atol=1e-5)
 
 
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
-def test_select_step_matches_oracle_with_tie_rule(dtype):
+@pytest.mark.parametrize("dtype,B,Wp,V,W", [
+    (torch.float32, 3, 16, 5000, 64), (torch.bfloat16, 3, 16, 5000, 64), (torch.float16, 3, 16, 5000, 64),
+    (torch.bfloat16, 3, 16, 65536, 256), (torch.bfloat16, 3, 16, 65536, 500), (torch.bfloat16, 3, 16, 65536, 1100),
+    (torch.bfloat16, 4, 96, 32768, 256)])
+def test_select_step_matches_oracle_with_tie_rule(dtype, B, Wp, V, W):
     """One step over bf16-quantised logits (many exact ties): scores and the
-    lowest-index tie rule must match the oracle's stable top-k exactly."""
+    lowest-index tie rule must match the oracle's stable top-k exactly.  The
+    V = 65536 BF16 cases give every thread of the row-statistics kernel a
+    64-element slice, so its per-row top-W pruning bound is finite (W = 256
+    and 500, ranks 8 and 16 of each warp's thread maxima) or disabled
+    (W = 1100 > 32 x 32 warps); 4 x 96 rows exceed one row per SM, so rows are
+    binned from L2 while the next row streams in."""
     from kadllm_b200.grbeam import BeamSelector
 
     rng = np.random.default_rng(0)
-    B, Wp, V, W = 3, 16, 5000, 64
     logits = O.bf16((2 * rng.standard_normal((B, Wp, V))).astype(np.float32))
     if dtype == torch.float16:
         logits = np.float16(logits).astype(np.float32)
