@@ -212,11 +212,13 @@ KADLLM_API int kadllm_qk_norm_rope(const void* proj, int64_t ld_proj, int64_t q_
                                    void* v_out, int64_t sv_seq, int64_t sv_pos, int64_t sv_h,
                                    int64_t rows, void* stream);
 
-/* Prompt Gated-DeltaNet layer from the packed projection (BF16), in two
- * launches: a parallel per-(request, head, 64-token chunk) preparation (causal
- * conv + SiLU, gates, q/k L2 norm, K K^T and Q K^T on the tensor cores, the UT
- * transform T = (I + L)^-1) and a sequential per-(request, head) state scan
- * (tensor-core chunk products, gated RMSNorm fused on the output).
+/* Prompt Gated-DeltaNet layer from the packed projection (BF16) in the WY
+ * form of the chunked rule, two launches: a parallel per-(request, head,
+ * 64-token chunk) preparation (causal conv + SiLU, gates, q/k L2 norm, K K^T and
+ * Q K^T on the tensor cores, T = (I + L)^-1, then W = T diag(beta e^G) K and
+ * U = T diag(beta) V on the tensor cores) and a sequential per-(request, head)
+ * state scan (Vn = U - W S, O = e^G Q S + Aqk Vn, S <- e^{G_last} S + K'^T Vn on
+ * the tensor cores, gated RMSNorm fused on the output).
  * Replaces Qwen3_5GatedDeltaNet.forward on the prompt (TF:422-533 with the
  * chunked rule TF:234-311).  proj [B*L, ld_proj] = q | k | v | z | b | a;
  * conv_weight [conv_dim, 4]; writes conv_state [B, conv_dim, 4] (last 4

@@ -71,8 +71,8 @@ def case_prefill(gen, reps):
                   B, L, H, HV, K, K, s)
 
     ms = _time(run, reps)
-    flops = B * HV * (L // 64) * 2 * 64 * (2 * 64 * K + 3 * K * K + 2 * 64 * K)
-    return ms, "tensor", flops
+    # compulsory HBM bytes: projection read once, output and both states written
+    return ms, "hbm", B * L * ld * 2 + B * L * HV * K * 2 + B * HV * K * K * 2 + B * C * 4 * 2
 
 
 def case_conv(gen, reps):

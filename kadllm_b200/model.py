@@ -191,7 +191,7 @@ class HybridModel:
         s = self._stream()
         prefix = []
         hk, D, hq = c.num_key_value_heads, c.head_dim, c.num_attention_heads
-        ws = None  # GDN prefill workspace, shared by the GDN layers
+        ws = None  # GDN prefill workspace (chunk blocks), shared by the GDN layers
         for i, layer in enumerate(self.layers):
             m = layer.mixer
             P = F.linear(normed, m.w_in)

@@ -19,10 +19,15 @@ from . import _lib
 def work_of(name: str, args: tuple) -> tuple[str, float] | None:
     """(bound, algorithmic work) of one call: ("tensor", FLOPs) or ("hbm", bytes)."""
     if name == "kadllm_gdn_prefill_split":
+        # compulsory HBM bytes (the binding roof: 86 GFLOP of tensor work take a
+        # third of the time the bytes do): projection columns read once, output,
+        # both prefix states
         B, L, H, HV, DK, DV = args[13:19]
-        chunks = -(-L // 64)
-        per_chunk = 2 * 64 * (2 * 64 * DK + 3 * DK * DV + 2 * 64 * DV)
-        return "tensor", float(B * HV * chunks * per_chunk)
+        conv_dim = 2 * H * DK + HV * DV
+        rows = B * L
+        read = rows * (conv_dim + HV * DV + 2 * HV) * 2
+        write = rows * HV * DV * 2 + B * HV * DK * DV * 2 + B * conv_dim * 4 * 2
+        return "hbm", float(read + write)
     if name == "kadllm_causal_attention":
         B, L, H, HK, D = args[17:22]
         return "tensor", float(4 * B * H * D * L * (L + 1) / 2)

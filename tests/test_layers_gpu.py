@@ -126,10 +126,13 @@ def test_causal_attention_prefill(D, hq, hk, L):
     assert_close_rel(N(out), ref, rel=1e-2, what="causal attention")
 
 
-@pytest.mark.parametrize("K,H,L", [(32, 4, 100), (128, 2, 130), (128, 2, 64), (64, 2, 3)])
-def test_gdn_prefill_split_matches_oracle(K, H, L):
-    """Conv + gates + chunked rule + gated norm from the packed projection, and
-    the conv / recurrent prefix states, against the oracle's restatement."""
+@pytest.mark.parametrize("K,H,L", [(32, 4, 100), (128, 2, 130), (128, 2, 64), (64, 2, 3), (128, 2, 300),
+                                   (128, 1, 1024)])
+def test_gdn_prefill_matches_oracle(K, H, L):
+    """Conv + gates + chunked rule (WY form) + gated norm from the packed
+    projection, and the conv / recurrent prefix states, against the oracle's
+    restatement.  L = 300 and 1024 run 5 and 16 chunks, so both pipeline stages
+    of the scan are reused many times."""
     rng = np.random.default_rng(K + L + 7)
     B, HV = 2, H
     kd, vd = H * K, HV * K
@@ -147,8 +150,8 @@ def test_gdn_prefill_split_matches_oracle(K, H, L):
     nbytes = _lib.lib().kadllm_gdn_prefill_workspace(B, L, HV, K, K)
     ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
     _lib.call("kadllm_gdn_prefill_split", keep[0].data_ptr(), ld, keep[1].data_ptr(), cstate.data_ptr(),
-              keep[2].data_ptr(), keep[3].data_ptr(), keep[4].data_ptr(), 1e-6, out.data_ptr(), vd, state.data_ptr(),
-              ws.data_ptr(), nbytes, B, L, H, HV, K, K, S())
+              keep[2].data_ptr(), keep[3].data_ptr(), keep[4].data_ptr(), 1e-6, out.data_ptr(), vd,
+              state.data_ptr(), ws.data_ptr(), nbytes, B, L, H, HV, K, K, S())
     x = P[:, :C].reshape(B, L, C).transpose(0, 2, 1)  # B C L
     xp = np.concatenate([np.zeros((B, C, 3), np.float32), x], -1)
     conv = R(O.silu(sum(xp[:, :, j:j + L] * cw[None, :, j:j + 1] for j in range(4)))).transpose(0, 2, 1)
