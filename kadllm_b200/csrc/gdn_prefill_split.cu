@@ -21,15 +21,16 @@
 //         forward substitution plus two levels of TF32 block merges
 //         [[A,0],[C,D]]^-1 = [[A^-1,0],[-D^-1 C A^-1, D^-1]], then
 //         W = T diag(beta e^G) K and U = T diag(beta) V on the tensor cores.
-//       Writes one contiguous block per chunk: q | K' = e^{G_last - G} k | W | U |
+//       Writes one contiguous block per chunk: Q' = e^G q | K' = e^{G_last - G} k | W | U |
 //       Aqk = (Q K^T o exp(G_i - G_j)) lower incl. diagonal | G.
 // scan  (grid: B*HV, 8 warps) -- per chunk, with the next block prefetched by
 //       cp.async, three barriers:
-//         [W; Q] S (one pass over S)       Vn = U - W S,  O = e^G (Q S)
+//         [W; Q'] S (one pass over S)      Vn = U - W S,  O = Q' S  (Q' = e^G q)
 //         S <- e^{G_last} S + K'^T Vn      O += Aqk Vn -> gated RMSNorm -> out
 // S stays in fp32 MMA accumulators, with a BF16 copy in shared memory as the B
 // operand of the next chunk.
 #include "mma_tiles.cuh"
+#include "tcgen05.cuh"
 
 namespace kb {
 namespace {
@@ -44,6 +45,7 @@ struct SplitArgs {
   __nv_bfloat16* out; int64_t ld_out;          // [B*L, HV*DV]
   __nv_bfloat16* state;                        // [B, HV, DK, DV]
   unsigned char* blocks;                       // [B*HV, nc] chunk blocks (ChunkBlock)
+  uint32_t* status;                            // bit 0: a tensor-core wait of the scan timed out
   int B, L, nc, H, HV;
   float scale;
 };
@@ -51,7 +53,7 @@ struct SplitArgs {
 // One chunk's prep output in the workspace (dense rows).
 template <int DK, int DV>
 struct ChunkBlock {
-  static constexpr size_t q = 0;                           // [kC][DK] bf16, normalised and scaled
+  static constexpr size_t q = 0;                           // [kC][DK] bf16, e^{G_i} q_i (normalised, scaled)
   static constexpr size_t kp = q + size_t(kC) * DK * 2;    // [kC][DK] bf16, e^{G_last - G_i} k_i
   static constexpr size_t w = kp + size_t(kC) * DK * 2;    // [kC][DK] bf16, T diag(beta e^G) K
   static constexpr size_t u = w + size_t(kC) * DK * 2;     // [kC][DV] bf16, T diag(beta) V
@@ -351,7 +353,18 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const SplitArgs a) {
         __floats2bfloat162_rn(v0 * b0 * __expf(sG[j]), v1 * b1 * __expf(sG[j + 1]));
     *reinterpret_cast<__nv_bfloat162*>(sT2 + i * ST + j) = __floats2bfloat162_rn(v0 * b0, v1 * b1);
   }
-  export_tile<DK>(reinterpret_cast<__nv_bfloat16*>(blk + CB::q), sQ, SQ, kC, tid, NT);
+  {  // Q' = e^{G_i} q_i (the decay of the inter-chunk term, folded into the operand)
+    __nv_bfloat16* dq = reinterpret_cast<__nv_bfloat16*>(blk + CB::q);
+    for (int i = tid; i < kC * (DK / 8); i += NT) {
+      const int r = i / (DK / 8), cc = (i % (DK / 8)) * 8;
+      const float f = __expf(sG[r]);
+      uint4 raw = *reinterpret_cast<const uint4*>(sQ + r * SQ + cc);
+      __nv_bfloat162* hh = reinterpret_cast<__nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) hh[j] = __floats2bfloat162_rn(__low2float(hh[j]) * f, __high2float(hh[j]) * f);
+      *reinterpret_cast<uint4*>(dq + r * DK + cc) = raw;
+    }
+  }
   __syncthreads();
   // ---- warps 0-3: W = T1 K; warps 4-7: U = T2 V (tensor cores) ------------------------
   {
@@ -467,13 +480,12 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_kernel(const SplitArgs a) {
     const __nv_bfloat16* sU = reinterpret_cast<const __nv_bfloat16*>(sb + M::u);
     const __nv_bfloat16* sA = reinterpret_cast<const __nv_bfloat16*>(sb + M::aqk);
     const float* sG = reinterpret_cast<const float*>(sb + M::g);
-    // [W; Q] S for this warp's tile; Vn = U - W S -> sVn, O = e^G (Q S)
+    // [W; Q'] S for this warp's tile; Vn = U - W S -> sVn, O = Q' S (= e^G Q S)
     float pw[NT][4], o[NT][4];
     zero_acc<NT>(pw);
     zero_acc<NT>(o);
     warp_mma<DK, NT, false, true>(pw, sW, SQ, mt * 16, 0, sS, SV, 0, nh * (DV / 2));
     warp_mma<DK, NT, false, true>(o, sQ, SQ, mt * 16, 0, sS, SV, 0, nh * (DV / 2));
-    const float e0 = __expf(sG[i0]), e1 = __expf(sG[i1]);
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
       const int col = nh * (DV / 2) + j * 8 + tq * 2;
@@ -483,7 +495,6 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_kernel(const SplitArgs a) {
           __floats2bfloat162_rn(__low2float(u0) - pw[j][0], __high2float(u0) - pw[j][1]);
       *reinterpret_cast<__nv_bfloat162*>(sVn + i1 * SV + col) =
           __floats2bfloat162_rn(__low2float(u1) - pw[j][2], __high2float(u1) - pw[j][3]);
-      o[j][0] *= e0; o[j][1] *= e0; o[j][2] *= e1; o[j][3] *= e1;
     }
     __syncthreads();  // Vn complete; every read of sS for this chunk is done
     // S <- e^{G_last} S + K'^T Vn;  O += Aqk Vn
@@ -553,12 +564,288 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_kernel(const SplitArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// scan on the 5th-generation tensor cores (DK = DV = 128): S and the chunk
+// products live in tensor memory.  8 warps: warp w reads TMEM lane quadrant
+// w % 4, columns [64 (w / 4), +64).
+//   TMEM columns [0, 128): S (lane = key row);  [128, 256): P / O (lane = row)
+//   MMA1  P  = [Q'; W] S          (M 128 = 64 Q' rows + 64 W rows, K = 128)
+//   V warps (quadrants 2, 3): Vn = U - W S -> shared memory (MN-major B operand)
+//   MMA2  S (+)= K'^T Vn          (M = 128 key rows, K = 64 tokens)
+//   MMA3  P += [Aqk; 0] Vn        (rows 0..63 become O; zero rows keep M = 128)
+//   all warps: S -> BF16 copy (next MMA1's B operand), then S *= e^{G_last} of
+//   the next chunk; O warps (quadrants 0, 1) read O, and run its gated-RMSNorm
+//   epilogue during the next chunk's MMA1 -> Vn -> MMA2/3.
+// The MMA issuer is thread 64 (a V warp).  mbarriers: bar1 (MMA1) and bar2
+// (MMA2/3) complete once per chunk, so parity c & 1 names the chunk's phase.
+// ---------------------------------------------------------------------------
+struct TcScan {
+  static constexpr int D = 128;
+  static constexpr size_t a1 = 0;                          // [Q'; W] K-major, 128 rows x K 128
+  static constexpr size_t a2 = a1 + size_t(128) * D * 2;   // K' MN-major, M 128 (keys) x K 64 (tokens)
+  static constexpr size_t a3 = a2 + size_t(kC) * D * 2;    // [Aqk; 0] K-major, 128 rows x K 64
+  static constexpr size_t u = a3 + size_t(128) * kC * 2;   // U rows [kC][D], 16-byte chunks XOR-swizzled
+  static constexpr size_t stage = u + size_t(kC) * D * 2;
+  static constexpr size_t b1 = 2 * stage;                  // S (bf16) MN-major, K 128 (keys) x N 128
+  static constexpr size_t b2 = b1 + size_t(D) * D * 2;     // Vn MN-major, K 64 (tokens) x N 128
+  static constexpr size_t z = b2 + size_t(kC) * D * 2;     // z rows of the chunk whose O is pending [kC][D]
+  static constexpr size_t nw = z + size_t(kC) * D * 2;     // norm weight [D] f32
+  static constexpr size_t ss = nw + size_t(D) * 4;         // row sums of squares [kC][2]
+  static constexpr size_t bar = ss + size_t(kC) * 2 * 4;   // mbarriers bar1, bar2
+  static constexpr size_t slot = bar + 16;                 // TMEM base address
+  static constexpr size_t bytes = slot + 16;
+  static_assert(stage % 16 == 0 && b1 % 16 == 0 && b2 % 16 == 0 && z % 16 == 0 && bar % 8 == 0, "alignment");
+  static_assert(bytes <= 232448, "shared memory");
+  // core-matrix byte offset of (row, 16-byte chunk): 128-wide rows (SBO 2048, LBO 128) ...
+  __device__ static uint32_t off16(int r, int ch) { return (r >> 3) * 2048 + ch * 128 + (r & 7) * 16; }
+  // ... and 64-wide rows (SBO 1024, LBO 128)
+  __device__ static uint32_t off8(int r, int ch) { return (r >> 3) * 1024 + ch * 128 + (r & 7) * 16; }
+  // U row r, chunk ch: rows of 256 bytes, chunk index XOR (r % 8) keeps row-parallel reads conflict-free
+  __device__ static uint32_t offu(int r, int ch) { return r * 256 + ((ch ^ (r & 7)) * 16); }
+};
+
+__device__ __forceinline__ void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(n) : "memory"); }
+
+// Gated RMSNorm of one O row half (64 columns, BF16 pairs in o) times SiLU(z) to
+// the layer output; the two halves of a row exchange their sums of squares.
+// All 128 O threads call it (invalid rows skip the stores only).
+__device__ __forceinline__ void tc_o_epilogue(const SplitArgs& a, unsigned char* smem, int c, int b, int hv, int i,
+                                              int half, const uint32_t (&o)[32]) {
+  using M = TcScan;
+  const float* sNW = reinterpret_cast<const float*>(smem + M::nw);
+  float* sSS = reinterpret_cast<float*>(smem + M::ss);
+  auto lo = [](uint32_t p) { return __uint_as_float(p << 16); };
+  auto hi = [](uint32_t p) { return __uint_as_float(p & 0xffff0000u); };
+  float part = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) part += lo(o[j]) * lo(o[j]) + hi(o[j]) * hi(o[j]);
+  sSS[i * 2 + half] = part;
+  named_bar(1, 128);
+  const float inv = 1.0f / sqrtf((sSS[i * 2] + sSS[i * 2 + 1]) / 128.f + a.eps);
+  if (c * kC + i < a.L) {
+    const int64_t row = int64_t(b) * a.L + int64_t(c) * kC + i;
+    const uint4* zp = reinterpret_cast<const uint4*>(smem + M::z + i * 256 + half * 128);
+    uint4* op = reinterpret_cast<uint4*>(a.out + row * a.ld_out + hv * 128 + half * 64);
+#pragma unroll
+    for (int v = 0; v < 8; ++v) {
+      const uint4 zz = zp[v];
+      const __nv_bfloat162* z2 = reinterpret_cast<const __nv_bfloat162*>(&zz);
+      uint4 res;
+      __nv_bfloat162* r2 = reinterpret_cast<__nv_bfloat162*>(&res);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int j = half * 64 + v * 8 + 2 * e;
+        const float h0 = bf16r(sNW[j] * bf16r(lo(o[v * 4 + e]) * inv));
+        const float h1 = bf16r(sNW[j + 1] * bf16r(hi(o[v * 4 + e]) * inv));
+        r2[e] = __floats2bfloat162_rn(h0 * silu_fast(__low2float(z2[e])), h1 * silu_fast(__high2float(z2[e])));
+      }
+      op[v] = res;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) {
+  using M = TcScan;
+  using CB = ChunkBlock<128, 128>;
+  constexpr int D = 128;
+  constexpr long long kWait = 1ll << 31;  // ~1 s of SM clocks per MMA wait
+  constexpr uint32_t kId1 = tc::idesc_bf16(128, 128, 0, 1);  // K-major A, MN-major B
+  constexpr uint32_t kId2 = tc::idesc_bf16(128, 128, 1, 1);  // MN-major A and B
+  extern __shared__ __align__(16) unsigned char smem[];
+  uint64_t* bar1 = reinterpret_cast<uint64_t*>(smem + M::bar);
+  uint64_t* bar2 = bar1 + 1;
+  uint32_t* slot = reinterpret_cast<uint32_t*>(smem + M::slot);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, half = warp >> 2;
+  const int row = quad * 32 + lane;          // TMEM lane of this thread
+  const bool vwarp = quad >= 2;              // quadrants 2, 3: W rows -> Vn
+  const bool issuer = tid == 64;
+  const int bh = blockIdx.x, b = bh / a.HV, hv = bh % a.HV;
+  const int conv_dim = 2 * a.H * D + a.HV * D;
+  const unsigned char* blocks = a.blocks + int64_t(bh) * a.nc * CB::bytes;
+  const uint32_t sbase = smem_u32(smem);
+
+  auto load_block = [&](int c, int st) {
+    const unsigned char* src = blocks + int64_t(c) * CB::bytes;
+    unsigned char* dst = smem + st * M::stage;
+    for (int i = tid; i < kC * 16; i += 256) {
+      const int r = i >> 4, ch = i & 15;
+      cp_async16(dst + M::a1 + M::off16(r, ch), src + CB::q + r * 256 + ch * 16);
+      cp_async16(dst + M::a1 + M::off16(64 + r, ch), src + CB::w + r * 256 + ch * 16);
+      cp_async16(dst + M::a2 + M::off16(r, ch), src + CB::kp + r * 256 + ch * 16);
+      cp_async16(dst + M::u + M::offu(r, ch), src + CB::u + r * 256 + ch * 16);
+    }
+    for (int i = tid; i < kC * 8; i += 256) {
+      const int r = i >> 3, ch = i & 7;
+      cp_async16(dst + M::a3 + M::off8(r, ch), src + CB::aqk + r * 128 + ch * 16);
+    }
+  };
+
+  // S = 0 (bf16 copy), zero rows 64..127 of [Aqk; 0] in both stages, norm weight, barriers, TMEM
+  const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
+  for (int i = tid; i < D * D * 2 / 16; i += 256) reinterpret_cast<uint4*>(smem + M::b1)[i] = z4;
+  for (int st = 0; st < 2; ++st)
+    for (int i = tid; i < 64 * kC * 2 / 16; i += 256)
+      reinterpret_cast<uint4*>(smem + st * M::stage + M::a3 + M::off8(64, 0))[i] = z4;
+  for (int i = tid; i < D; i += 256) reinterpret_cast<float*>(smem + M::nw)[i] = a.norm_w[i];
+  if (tid == 0) {
+    tc::mbar_init(bar1, 1);
+    tc::mbar_init(bar2, 1);
+  }
+  if (warp == 0) tc::tmem_alloc(slot, 256);
+  load_block(0, 0);
+  cp_async_commit();
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *slot;
+  const uint32_t lane_off = uint32_t(quad * 32) << 16;
+  const uint32_t tS = tmem + lane_off + half * 64, tP = tmem + 128 + lane_off + half * 64;
+  bool ok = true;
+  uint32_t o[32];    // this thread's O row half (BF16 pairs), O warps
+  int pending = -1;  // chunk whose O is held in o[]
+
+  for (int c = 0; c < a.nc; ++c) {
+    const int st = c & 1;
+    const uint32_t par = uint32_t(c) & 1u;
+    const unsigned char* sb = smem + st * M::stage;
+    const uint32_t sbu = sbase + st * M::stage;
+    cp_async_wait<0>();
+    tc::fence_async_smem();
+    tc::fence_before();
+    ok = __syncthreads_and(ok);  // block c and z rows of chunk c-1 staged; chunk c-1's TMEM traffic done
+    if (!ok) break;
+    tc::fence_after();
+    if (c + 1 < a.nc) {
+      load_block(c + 1, st ^ 1);
+      cp_async_commit();
+    }
+    const float gl_next =
+        c + 1 < a.nc ? *reinterpret_cast<const float*>(blocks + int64_t(c + 1) * CB::bytes + CB::g + (kC - 1) * 4) : 0.f;
+    if (vwarp) {
+      if (issuer) {  // MMA1: P = [Q'; W] S
+#pragma unroll
+        for (int s = 0; s < 8; ++s)
+          tc::mma_bf16(tmem + 128, tc::smem_desc(sbu + M::a1 + s * 256, 128, 2048),
+                       tc::smem_desc(sbase + M::b1 + s * 4096, 2048, 128), kId1, s > 0);
+        tc::commit(bar1);
+      }
+      ok = tc::mbar_wait(bar1, par, kWait) && ok;
+      tc::fence_after();
+      const int t = row - 64;  // token of this W row
+#pragma unroll
+      for (int piece = 0; piece < 2; ++piece) {  // Vn = U - W S, columns [64 half + 32 piece, +32)
+        uint32_t r[32];
+        tc::ld32(tP + piece * 32, r);
+        tc::wait_ld();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int col = half * 64 + piece * 32 + q * 8;
+          const uint4 uu = *reinterpret_cast<const uint4*>(sb + M::u + M::offu(t, col / 8));
+          const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&uu);
+          uint4 res;
+          __nv_bfloat162* r2 = reinterpret_cast<__nv_bfloat162*>(&res);
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            r2[e] = __floats2bfloat162_rn(__low2float(u2[e]) - __uint_as_float(r[q * 8 + 2 * e]),
+                                          __high2float(u2[e]) - __uint_as_float(r[q * 8 + 2 * e + 1]));
+          *reinterpret_cast<uint4*>(smem + M::b2 + M::off16(t, col / 8)) = res;
+        }
+      }
+      tc::fence_async_smem();
+      tc::fence_before();
+      named_bar(2, 128);  // Vn staged, P's W rows read
+      tc::fence_after();
+      if (issuer) {  // MMA2: S (+)= K'^T Vn;  MMA3: P += [Aqk; 0] Vn
+#pragma unroll
+        for (int s = 0; s < 4; ++s)
+          tc::mma_bf16(tmem, tc::smem_desc(sbu + M::a2 + s * 4096, 2048, 128),
+                       tc::smem_desc(sbase + M::b2 + s * 4096, 2048, 128), kId2, c > 0 || s > 0);
+#pragma unroll
+        for (int s = 0; s < 4; ++s)
+          tc::mma_bf16(tmem + 128, tc::smem_desc(sbu + M::a3 + s * 256, 128, 1024),
+                       tc::smem_desc(sbase + M::b2 + s * 4096, 2048, 128), kId1, true);
+        tc::commit(bar2);
+      }
+    } else if (pending >= 0) {  // O warps: epilogue of chunk c-1, overlapping MMA1 -> Vn -> MMA2/3
+      tc_o_epilogue(a, smem, pending, b, hv, row, half, o);
+    }
+    ok = tc::mbar_wait(bar2, par, kWait) && ok;
+    tc::fence_after();
+    if (!vwarp) {  // z rows of chunk c for its epilogue (every O thread is past chunk c-1's z reads)
+      named_bar(1, 128);
+      for (int i = tid - (warp >= 4 ? 64 : 0); i < kC * 16; i += 128) {
+        const int r = i >> 4, ch = i & 15;
+        if (c * kC + r < a.L)
+          cp_async16(smem + M::z + r * 256 + ch * 16,
+                     a.proj + (int64_t(b) * a.L + int64_t(c) * kC + r) * a.ld_proj + conv_dim + hv * D + ch * 8);
+      }
+      cp_async_commit();
+    }
+    {  // S: bf16 copy for the next MMA1 (and the final state), then S *= e^{G_last(next chunk)}
+      const float f = __expf(gl_next);
+      const bool last = c + 1 == a.nc;
+      uint4* dst = reinterpret_cast<uint4*>(a.state + (int64_t(bh) * D + row) * D + half * 64);
+#pragma unroll
+      for (int piece = 0; piece < 2; ++piece) {
+        uint32_t r[32];
+        tc::ld32(tS + piece * 32, r);
+        tc::wait_ld();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 res;
+          __nv_bfloat162* r2 = reinterpret_cast<__nv_bfloat162*>(&res);
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            r2[e] = __floats2bfloat162_rn(__uint_as_float(r[q * 8 + 2 * e]), __uint_as_float(r[q * 8 + 2 * e + 1]));
+          *reinterpret_cast<uint4*>(smem + M::b1 + M::off16(row, half * 8 + piece * 4 + q)) = res;
+          if (last) dst[piece * 4 + q] = res;
+        }
+        if (!last) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * f);
+          tc::st32(tS + piece * 32, r);
+        }
+      }
+      tc::wait_st();
+      tc::fence_async_smem();
+    }
+    if (!vwarp) {  // O rows, read now so the next MMA1 may overwrite P
+#pragma unroll
+      for (int piece = 0; piece < 2; ++piece) {
+        uint32_t r[32];
+        tc::ld32(tP + piece * 32, r);
+        tc::wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const __nv_bfloat162 p2 = __floats2bfloat162_rn(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+          o[piece * 16 + j] = *reinterpret_cast<const uint32_t*>(&p2);
+        }
+      }
+      pending = c;
+    }
+  }
+  cp_async_wait<0>();
+  __syncthreads();  // the last chunk's z rows are staged
+  if (ok && !vwarp && pending >= 0) tc_o_epilogue(a, smem, pending, b, hv, row, half, o);
+  if (!ok && tid == 0) atomicOr(a.status, 1u);
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  if (warp == 0) tc::tmem_free(tmem, 256);
+}
+
 template <int DK, int DV>
 int launch_split(SplitArgs& a, void* ws, int64_t ws_bytes, cudaStream_t s) {
   const int64_t n = int64_t(a.B) * a.HV;
   KB_REQUIRE(ws_bytes >= int64_t(workspace_bytes<DK, DV>(a.B, a.HV, a.L)), KADLLM_EINVAL,
              "gdn prefill: workspace too small");
-  a.blocks = static_cast<unsigned char*>(ws);
+  a.status = static_cast<uint32_t*>(ws);  // bytes [0, 256): status word; chunk blocks after
+  a.blocks = static_cast<unsigned char*>(ws) + 256;
+  if (cudaMemsetAsync(a.status, 0, sizeof(uint32_t), s) != cudaSuccess) {
+    set_error("gdn prefill: cannot clear the status word");
+    return KADLLM_ECUDA;
+  }
   {
     const size_t smem = PrepSmem<DK, DV>::bytes;
     auto kern = gdn_prep_kernel<DK, DV>;
@@ -568,6 +855,18 @@ int launch_split(SplitArgs& a, void* ws, int64_t ws_bytes, cudaStream_t s) {
     }
     kern<<<dim3(a.nc, unsigned(n)), 256, smem, s>>>(a);
     KB_CHECK_LAUNCH("gdn prefill prep launch");
+  }
+  const bool tc_scan = DK == 128 && DV == 128 && a.ld_out % 8 == 0 &&
+                       (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.state) & 15) == 0;
+  if (tc_scan) {
+    const size_t smem = TcScan::bytes;
+    if (cudaFuncSetAttribute(gdn_scan_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess) {
+      set_error("gdn prefill scan: cannot reserve %zu bytes of shared memory", smem);
+      return KADLLM_ECUDA;
+    }
+    gdn_scan_tc_kernel<<<unsigned(n), 256, smem, s>>>(a);
+    KB_CHECK_LAUNCH("gdn prefill tensor-core scan launch");
+    return KADLLM_OK;
   }
   {
     const size_t smem = ScanSmem<DK, DV>::bytes;
