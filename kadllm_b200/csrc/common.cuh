@@ -128,6 +128,53 @@ __device__ __forceinline__ float softplus_f(float x) { return x > 20.0f ? x : lo
 // ---------------------------------------------------------------------------
 // Tensor-core fragments (mma.sync m16n8k16, bf16 in, fp32 accumulate)
 // ---------------------------------------------------------------------------
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: each lane an independent fp32 op, round to nearest).
+__device__ __forceinline__ uint64_t pk2(float2 v) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};\n" : "=l"(r) : "f"(v.x), "f"(v.y));
+  return r;
+}
+__device__ __forceinline__ float2 upk2(uint64_t r) {
+  float2 v;
+  asm("mov.b64 {%0, %1}, %2;\n" : "=f"(v.x), "=f"(v.y) : "l"(r));
+  return v;
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;\n" : "=l"(d) : "l"(pk2(a)), "l"(pk2(b)), "l"(pk2(c)));
+  return upk2(d);
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;\n" : "=l"(d) : "l"(pk2(a)), "l"(pk2(b)));
+  return upk2(d);
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;\n" : "=l"(d) : "l"(pk2(a)), "l"(pk2(b)));
+  return upk2(d);
+}
+__device__ __forceinline__ float fast_ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float fast_rcp(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
+// SiLU of a pair: v / (1 + 2^(-v log2 e)) with the approximate exp2 / reciprocal units.
+__device__ __forceinline__ float2 silu2(float2 v) {
+  const float2 t = mul2(v, make_float2(-1.4426950408889634f, -1.4426950408889634f));
+  const float2 d = add2(make_float2(fast_ex2(t.x), fast_ex2(t.y)), make_float2(1.f, 1.f));
+  return mul2(v, make_float2(fast_rcp(d.x), fast_rcp(d.y)));
+}
+// bf16x2 word -> (low, high) fp32 pair
+__device__ __forceinline__ float2 bf2f(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

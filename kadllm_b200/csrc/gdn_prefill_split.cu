@@ -89,8 +89,8 @@ struct PrepSmem {
   static constexpr size_t q = r_bytes;                       // q, later W
   static constexpr size_t k = q + size_t(kC) * SQ * 2;       // k, later K'
   static constexpr size_t v = k + size_t(kC) * SQ * 2;       // v, later U
-  static constexpr size_t vec = v + size_t(kC) * SV * 2;     // G | beta | raw g
-  static constexpr size_t bytes = vec + size_t(kC) * 4 * 3;
+  static constexpr size_t vec = v + size_t(kC) * SV * 2;     // G | beta | raw g | e^G | beta e^G | e^{G_last - G}
+  static constexpr size_t bytes = vec + size_t(kC) * 4 * 6;
   static_assert(t1 % 16 == 0 && a % 16 == 0 && q % 16 == 0 && k % 16 == 0 && v % 16 == 0, "alignment");
 };
 
@@ -124,6 +124,9 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const SplitArgs a) {
   float* sG = reinterpret_cast<float*>(smem + M::vec);
   float* sBeta = sG + kC;
   float* sRaw = sBeta + kC;
+  float* sEG = sRaw + kC;     // e^{G_i}
+  float* sBEG = sEG + kC;     // beta_i e^{G_i}
+  float* sEGL = sBEG + kC;    // e^{G_last - G_i}
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int c = blockIdx.x;
@@ -153,61 +156,63 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const SplitArgs a) {
   cp_async_wait<0>();
   __syncthreads();
 
-  // ---- conv + SiLU: 8 channels x 4 tokens per item, from the staged tile ---------------
+  // ---- conv + SiLU: 8 channels x 4 tokens per item, from the staged tile, in fp32 pairs -
   constexpr int NG = NCH / 8, SEG = 4;
   for (int item = tid; item < NG * (kC / SEG); item += NT) {
     const int grp = item % NG, seg = item / NG;
     const int lc = grp * 8, ch = chan(lc);
-    float w[8][4];
+    float2 w2[4][4];  // [channel pair][tap]
     {
       const uint4* wp = reinterpret_cast<const uint4*>(a.conv_w + int64_t(ch) * 4);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < 4; ++u) {  // uint4 u = taps of channels 2u, 2u + 1
         const uint4 raw = wp[u];
-        const __nv_bfloat162* hw = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          w[2 * u + j][0] = __low2float(hw[2 * j]);
-          w[2 * u + j][1] = __high2float(hw[2 * j]);
-          w[2 * u + j][2] = __low2float(hw[2 * j + 1]);
-          w[2 * u + j][3] = __high2float(hw[2 * j + 1]);
-        }
+        const float2 c0a = bf2f(raw.x), c0b = bf2f(raw.y), c1a = bf2f(raw.z), c1b = bf2f(raw.w);
+        w2[u][0] = make_float2(c0a.x, c1a.x);
+        w2[u][1] = make_float2(c0a.y, c1a.y);
+        w2[u][2] = make_float2(c0b.x, c1b.x);
+        w2[u][3] = make_float2(c0b.y, c1b.y);
       }
     }
-    auto row8 = [&](int r, float (&v)[8]) {  // staged row r = token t0 - 3 + r
+    auto row4 = [&](int r, float2 (&v)[4]) {  // staged row r = token t0 - 3 + r, 8 channels as 4 pairs
       const uint4 u = *reinterpret_cast<const uint4*>(sRawT + r * RS + lc);
-      const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        v[2 * j] = __low2float(hh[j]);
-        v[2 * j + 1] = __high2float(hh[j]);
-      }
+      v[0] = bf2f(u.x);
+      v[1] = bf2f(u.y);
+      v[2] = bf2f(u.z);
+      v[3] = bf2f(u.w);
     };
     const int r0 = seg * SEG;
-    float win[3][8];
-    row8(r0, win[0]);
-    row8(r0 + 1, win[1]);
-    row8(r0 + 2, win[2]);
+    float2 win[3][4];
+    row4(r0, win[0]);
+    row4(r0 + 1, win[1]);
+    row4(r0 + 2, win[2]);
+    __nv_bfloat16* dst = lc < DK ? sQ + lc : (lc < 2 * DK ? sK + (lc - DK) : sV + (lc - 2 * DK));
+    const int ld = lc < 2 * DK ? SQ : SV;
 #pragma unroll
     for (int r = r0; r < r0 + SEG; ++r) {
-      float x[8], o[8];
-      row8(r + 3, x);
-      const bool valid = t0 + r < a.L;
+      float2 x[4];
+      row4(r + 3, x);
+      uint4 u = make_uint4(0u, 0u, 0u, 0u);
+      if (t0 + r < a.L) {
+        uint32_t* uw = reinterpret_cast<uint32_t*>(&u);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float acc = win[0][e] * w[e][0] + win[1][e] * w[e][1] + win[2][e] * w[e][2] + x[e] * w[e][3];
-        o[e] = valid ? silu_fast(acc) : 0.f;
-        win[0][e] = win[1][e];
-        win[1][e] = win[2][e];
-        win[2][e] = x[e];
+        for (int pp = 0; pp < 4; ++pp) {
+          float2 acc = mul2(win[0][pp], w2[pp][0]);
+          acc = fma2(win[1][pp], w2[pp][1], acc);
+          acc = fma2(win[2][pp], w2[pp][2], acc);
+          acc = fma2(x[pp], w2[pp][3], acc);
+          const float2 o = silu2(acc);
+          const __nv_bfloat162 h2 = __floats2bfloat162_rn(o.x, o.y);
+          uw[pp] = *reinterpret_cast<const uint32_t*>(&h2);
+        }
       }
-      uint4 u;
-      __nv_bfloat162* hh = reinterpret_cast<__nv_bfloat162*>(&u);
+      *reinterpret_cast<uint4*>(dst + r * ld) = u;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) hh[j] = __floats2bfloat162_rn(o[2 * j], o[2 * j + 1]);
-      if (lc < DK) *reinterpret_cast<uint4*>(sQ + r * SQ + lc) = u;
-      else if (lc < 2 * DK) *reinterpret_cast<uint4*>(sK + r * SQ + (lc - DK)) = u;
-      else *reinterpret_cast<uint4*>(sV + r * SV + (lc - 2 * DK)) = u;
+      for (int pp = 0; pp < 4; ++pp) {
+        win[0][pp] = win[1][pp];
+        win[1][pp] = win[2][pp];
+        win[2][pp] = x[pp];
+      }
     }
   }
   if (c == a.nc - 1) {  // conv state: pre-conv columns of tokens L-4 .. L-1 (staged rows L-1-t0 ..)
@@ -266,6 +271,12 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const SplitArgs a) {
     sG[2 * lane + 1] = excl + v0 + v1;
   }
   __syncthreads();
+  if (tid < kC) {  // per-token decay factors (read after later barriers)
+    const float e = __expf(sG[tid]);
+    sEG[tid] = e;
+    sBEG[tid] = sBeta[tid] * e;
+    sEGL[tid] = __expf(sG[kC - 1] - sG[tid]);
+  }
   const int g8 = lane >> 2, tq = lane & 3;
   // ---- warps 0-3: K K^T -> L (fp32); warps 4-7: Q K^T -> Aqk (bf16) --------------------
   {
@@ -348,16 +359,14 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const SplitArgs a) {
     const int i = e / kC, j = e % kC;
     const float v0 = i >= j ? sL[i * SL + j] : 0.f;
     const float v1 = i >= j + 1 ? sL[i * SL + j + 1] : 0.f;
-    const float b0 = sBeta[j], b1 = sBeta[j + 1];
-    *reinterpret_cast<__nv_bfloat162*>(sT1 + i * ST + j) =
-        __floats2bfloat162_rn(v0 * b0 * __expf(sG[j]), v1 * b1 * __expf(sG[j + 1]));
-    *reinterpret_cast<__nv_bfloat162*>(sT2 + i * ST + j) = __floats2bfloat162_rn(v0 * b0, v1 * b1);
+    *reinterpret_cast<__nv_bfloat162*>(sT1 + i * ST + j) = __floats2bfloat162_rn(v0 * sBEG[j], v1 * sBEG[j + 1]);
+    *reinterpret_cast<__nv_bfloat162*>(sT2 + i * ST + j) = __floats2bfloat162_rn(v0 * sBeta[j], v1 * sBeta[j + 1]);
   }
   {  // Q' = e^{G_i} q_i (the decay of the inter-chunk term, folded into the operand)
     __nv_bfloat16* dq = reinterpret_cast<__nv_bfloat16*>(blk + CB::q);
     for (int i = tid; i < kC * (DK / 8); i += NT) {
       const int r = i / (DK / 8), cc = (i % (DK / 8)) * 8;
-      const float f = __expf(sG[r]);
+      const float f = sEG[r];
       uint4 raw = *reinterpret_cast<const uint4*>(sQ + r * SQ + cc);
       __nv_bfloat162* hh = reinterpret_cast<__nv_bfloat162*>(&raw);
 #pragma unroll
@@ -381,12 +390,15 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const SplitArgs a) {
       *reinterpret_cast<__nv_bfloat162*>(dst + r * SQ + col) = __floats2bfloat162_rn(acc[j][0], acc[j][1]);
       *reinterpret_cast<__nv_bfloat162*>(dst + (r + 8) * SQ + col) = __floats2bfloat162_rn(acc[j][2], acc[j][3]);
     }
-    const float gl = sG[kC - 1];
-    for (int e = tid; e < kC * (DK / 2); e += NT) {  // K' = e^{G_last - G_i} k_i
-      const int i = e / (DK / 2), cc = (e % (DK / 2)) * 2;
-      __nv_bfloat162* p = reinterpret_cast<__nv_bfloat162*>(sK + i * SQ + cc);
-      const float f = __expf(gl - sG[i]);
-      *p = __floats2bfloat162_rn(__low2float(*p) * f, __high2float(*p) * f);
+    for (int e = tid; e < kC * (DK / 8); e += NT) {  // K' = e^{G_last - G_i} k_i, 16 bytes at a time
+      const int i = e / (DK / 8), cc = (e % (DK / 8)) * 8;
+      uint4* p = reinterpret_cast<uint4*>(sK + i * SQ + cc);
+      const float f = sEGL[i];
+      uint4 raw = *p;
+      __nv_bfloat162* hh = reinterpret_cast<__nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) hh[j] = __floats2bfloat162_rn(__low2float(hh[j]) * f, __high2float(hh[j]) * f);
+      *p = raw;
     }
   }
   __syncthreads();
