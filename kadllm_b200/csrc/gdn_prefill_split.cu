@@ -304,20 +304,21 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const SplitArgs a) {
   }
   __syncthreads();
   // ---- T = (I + L)^-1 (warps 0-3; all threads meet every barrier) -----------------------
-  if (warp < 4) {  // diagonal 16x16 blocks by forward substitution
-    const int d0 = warp * 16;
-    for (int i = 1; i < 16; ++i) {
-      float val = 0.f;
-      const int j = lane;
-      if (j < i) {
-        val = sL[(d0 + i) * SL + d0 + j];
-        for (int m = j + 1; m < i; ++m) val += sL[(d0 + i) * SL + d0 + m] * sL[(d0 + m) * SL + d0 + j];
-        val = -val;
-      }
-      __syncwarp();
-      if (j < i) sL[(d0 + i) * SL + d0 + j] = val;
-      __syncwarp();
+  if (tid < kC) {  // diagonal 16x16 blocks: lane (block, column j) forward-substitutes column j in registers
+    const int d0 = (tid >> 4) * 16, j = tid & 15;
+    const float* Lb = sL + d0 * SL + d0;
+    float t[16];  // T[i][j] of this block; T = (I + L)^-1 is unit lower triangular
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float acc = 0.f;
+#pragma unroll
+      for (int m = 0; m < i; ++m) acc = fmaf(Lb[i * SL + m], t[m], acc);  // t[m] = 0 for m < j
+      t[i] = i < j ? 0.f : (i == j ? 1.f : -acc);
     }
+    __syncwarp();  // a block's 16 lanes share a warp: every read of L precedes the writes
+#pragma unroll
+    for (int i = 1; i < 16; ++i)
+      if (i > j) sL[(d0 + i) * SL + d0 + j] = t[i];
   }
   __syncthreads();
   if (tid < kC) sL[tid * SL + tid] = 1.f;  // sL now holds unit-lower blocks (zeros above)
