@@ -213,7 +213,8 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
     from kadllm_b200.adapters import NativeGRBeamAdapter
     from kadllm_b200.config import QWEN35_08B
     from kadllm_b200.model import HybridModel
-    from kadllm_b200.synthetic import random_prompts, torch_weights
+    from kadllm_b200.shard import gather_beams, max_over_ranks, rank_prompts
+    from kadllm_b200.synthetic import torch_weights
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -221,20 +222,14 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
     weights = torch_weights(cfg, seed=0, device=dev)
     engine = HybridModel(cfg, weights, device=dev)
     adapter = NativeGRBeamAdapter(engine)
-    ids_host = torch.from_numpy(random_prompts(BATCH, PROMPT, cfg.vocab_size, seed=rank)).pin_memory()
+    ids_host = torch.from_numpy(rank_prompts(rank, BATCH, PROMPT, cfg.vocab_size)).pin_memory()
     ids_dev = ids_host.to(dev)
     tok_host = torch.empty(BATCH, BEAM, DEPTH, dtype=torch.int64).pin_memory()
     sc_host = torch.empty(BATCH, BEAM, dtype=torch.float32).pin_memory()
     widths = [BEAM] * DEPTH
 
-    def gather(res):
-        if world > 1:
-            toks = torch.empty(world * BATCH, BEAM, DEPTH, dtype=torch.int64, device=dev)
-            scs = torch.empty(world * BATCH, BEAM, dtype=torch.float32, device=dev)
-            dist.all_gather_into_tensor(toks, res.tokens.contiguous())
-            dist.all_gather_into_tensor(scs, res.scores.contiguous())
-            return toks, scs
-        return res.tokens, res.scores
+    def gather(res):  # the path's only exchange: finished beams, in rank order
+        return gather_beams(res.tokens, res.scores)
 
     def step_device():
         return gather(grbeam_search(adapter, ids_dev, widths))
@@ -259,10 +254,8 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-        ms = torch.tensor([start.elapsed_time(end)], device=dev)
-        if world > 1:
-            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-        return float(ms.item()) / steps, _lib.launch_count - launches0
+        ms = max_over_ranks(start.elapsed_time(end), dev)
+        return ms / steps, _lib.launch_count - launches0
 
     with torch.inference_mode():
         for _ in range(args.warmup):

@@ -65,7 +65,7 @@ _ERRORS = {1: ValueError, 2: TypeError, 3: NotImplementedError, 4: RuntimeError}
 
 
 # kernels launched per successful call of each entry point (for launch accounting)
-LAUNCHES_PER_CALL = {"kadllm_beam_select": 4, "kadllm_beam_select_noalloc": 4, "kadllm_beam_select_status": 0, "kadllm_gdn_prefill_split": 2}
+LAUNCHES_PER_CALL = {"kadllm_beam_select": 4, "kadllm_beam_select_noalloc": 4, "kadllm_beam_select_status": 0, "kadllm_gdn_prefill_split": 3}
 launch_count = 0
 
 

@@ -170,6 +170,12 @@ __device__ __forceinline__ float2 silu2(float2 v) {
   const float2 d = add2(make_float2(fast_ex2(t.x), fast_ex2(t.y)), make_float2(1.f, 1.f));
   return mul2(v, make_float2(fast_rcp(d.x), fast_rcp(d.y)));
 }
+// (low, high) fp32 -> bf16x2 word, round to nearest even
+__device__ __forceinline__ uint32_t bf2_pack(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t bf2_pack_f2(float2 v) { return bf2_pack(v.x, v.y); }
 // bf16x2 word -> (low, high) fp32 pair
 __device__ __forceinline__ float2 bf2f(uint32_t w) {
   return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));

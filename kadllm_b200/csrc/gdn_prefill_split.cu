@@ -46,22 +46,32 @@ struct SplitArgs {
   __nv_bfloat16* state;                        // [B, HV, DK, DV]
   unsigned char* blocks;                       // [B*HV, nc] chunk blocks (ChunkBlock)
   uint32_t* status;                            // bit 0: a tensor-core wait of the scan timed out
+  int tc_layout;                               // chunk blocks in the tensor-core scan's shared-memory image
   int B, L, nc, H, HV;
   float scale;
 };
 
-// One chunk's prep output in the workspace (dense rows).
+// One chunk's prep output in the workspace.  Dense rows, or (tc_layout, DK = DV =
+// 128) the tensor-core scan's shared-memory image: q, w, kp as one 128-row
+// K-major core-matrix tile [Q'; W] followed by K' (the same byte order read as
+// MN-major), Aqk as a 64-wide K-major core tile, U as 256-byte rows with XOR-
+// swizzled 16-byte chunks; so the scan stages a chunk with two bulk copies.
 template <int DK, int DV>
 struct ChunkBlock {
   static constexpr size_t q = 0;                           // [kC][DK] bf16, e^{G_i} q_i (normalised, scaled)
-  static constexpr size_t kp = q + size_t(kC) * DK * 2;    // [kC][DK] bf16, e^{G_last - G_i} k_i
-  static constexpr size_t w = kp + size_t(kC) * DK * 2;    // [kC][DK] bf16, T diag(beta e^G) K
-  static constexpr size_t u = w + size_t(kC) * DK * 2;     // [kC][DV] bf16, T diag(beta) V
-  static constexpr size_t aqk = u + size_t(kC) * DV * 2;   // [kC][kC] bf16
-  static constexpr size_t g = aqk + size_t(kC) * kC * 2;   // [kC] f32, cumulative log decay
+  static constexpr size_t w = q + size_t(kC) * DK * 2;     // [kC][DK] bf16, T diag(beta e^G) K
+  static constexpr size_t kp = w + size_t(kC) * DK * 2;    // [kC][DK] bf16, e^{G_last - G_i} k_i
+  static constexpr size_t aqk = kp + size_t(kC) * DK * 2;  // [kC][kC] bf16
+  static constexpr size_t u = aqk + size_t(kC) * kC * 2;   // [kC][DV] bf16, T diag(beta) V
+  static constexpr size_t g = u + size_t(kC) * DV * 2;     // [kC] f32, cumulative log decay
   static constexpr size_t bytes = g + size_t(kC) * 4;
   static_assert(bytes % 16 == 0, "16-byte blocks");
 };
+
+// 16-byte unit o of a block region in the tensor-core image -> (row, 16-byte chunk) of the source tile.
+__device__ __forceinline__ void core16_rc(int o, int& r, int& ch) { r = ((o >> 7) << 3) | (o & 7); ch = (o >> 3) & 15; }
+__device__ __forceinline__ void core8_rc(int o, int& r, int& ch) { r = ((o >> 6) << 3) | (o & 7); ch = (o >> 3) & 7; }
+__device__ __forceinline__ void swz16_rc(int o, int& r, int& ch) { r = o >> 4; ch = (o & 15) ^ (r & 7); }
 
 template <int DK, int DV>
 size_t workspace_bytes(int64_t B, int64_t HV, int64_t L) {
@@ -94,14 +104,27 @@ struct PrepSmem {
   static_assert(t1 % 16 == 0 && a % 16 == 0 && q % 16 == 0 && k % 16 == 0 && v % 16 == 0, "alignment");
 };
 
-// Copy a [rows][cols] bf16 tile from padded shared rows to dense global rows, 16 bytes a thread.
+// Copy a [kC][COLS] bf16 tile from padded shared rows to global, 16 bytes a thread, consecutive
+// threads on consecutive destination bytes: dense rows (kind 0) or a tensor-core image (kind 1
+// core16, 2 core8, 3 swizzled rows).  scale (per row) multiplies the values when given.
 template <int COLS>
-__device__ __forceinline__ void export_tile(__nv_bfloat16* dst, const __nv_bfloat16* src, int lds, int rows, int tid,
-                                            int nthreads) {
+__device__ __forceinline__ void export_tile(unsigned char* dst, const __nv_bfloat16* src, int lds, int kind,
+                                            const float* scale, int tid, int nthreads) {
   constexpr int CH = COLS / 8;
-  for (int i = tid; i < rows * CH; i += nthreads) {
-    const int r = i / CH, c = (i % CH) * 8;
-    *reinterpret_cast<uint4*>(dst + r * COLS + c) = *reinterpret_cast<const uint4*>(src + r * lds + c);
+  for (int o = tid; o < kC * CH; o += nthreads) {
+    int r, ch;
+    if (kind == 1) core16_rc(o, r, ch);
+    else if (kind == 2) core8_rc(o, r, ch);
+    else if (kind == 3) swz16_rc(o, r, ch);
+    else { r = o / CH; ch = o % CH; }
+    uint4 raw = *reinterpret_cast<const uint4*>(src + r * lds + ch * 8);
+    if (scale) {
+      const float f = scale[r];
+      __nv_bfloat162* hh = reinterpret_cast<__nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) hh[j] = __floats2bfloat162_rn(__low2float(hh[j]) * f, __high2float(hh[j]) * f);
+    }
+    reinterpret_cast<uint4*>(dst)[o] = raw;
   }
 }
 
@@ -363,18 +386,9 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const SplitArgs a) {
     *reinterpret_cast<__nv_bfloat162*>(sT1 + i * ST + j) = __floats2bfloat162_rn(v0 * sBEG[j], v1 * sBEG[j + 1]);
     *reinterpret_cast<__nv_bfloat162*>(sT2 + i * ST + j) = __floats2bfloat162_rn(v0 * sBeta[j], v1 * sBeta[j + 1]);
   }
-  {  // Q' = e^{G_i} q_i (the decay of the inter-chunk term, folded into the operand)
-    __nv_bfloat16* dq = reinterpret_cast<__nv_bfloat16*>(blk + CB::q);
-    for (int i = tid; i < kC * (DK / 8); i += NT) {
-      const int r = i / (DK / 8), cc = (i % (DK / 8)) * 8;
-      const float f = sEG[r];
-      uint4 raw = *reinterpret_cast<const uint4*>(sQ + r * SQ + cc);
-      __nv_bfloat162* hh = reinterpret_cast<__nv_bfloat162*>(&raw);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) hh[j] = __floats2bfloat162_rn(__low2float(hh[j]) * f, __high2float(hh[j]) * f);
-      *reinterpret_cast<uint4*>(dq + r * DK + cc) = raw;
-    }
-  }
+  const bool tcl = DK == 128 && DV == 128 && a.tc_layout;
+  // Q' = e^{G_i} q_i (the decay of the inter-chunk term, folded into the operand)
+  export_tile<DK>(blk + CB::q, sQ, SQ, tcl ? 1 : 0, sEG, tid, NT);
   __syncthreads();
   // ---- warps 0-3: W = T1 K; warps 4-7: U = T2 V (tensor cores) ------------------------
   {
@@ -403,10 +417,10 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const SplitArgs a) {
     }
   }
   __syncthreads();
-  export_tile<DK>(reinterpret_cast<__nv_bfloat16*>(blk + CB::kp), sK, SQ, kC, tid, NT);
-  export_tile<DK>(reinterpret_cast<__nv_bfloat16*>(blk + CB::w), sQ, SQ, kC, tid, NT);
-  export_tile<DV>(reinterpret_cast<__nv_bfloat16*>(blk + CB::u), sV, SV, kC, tid, NT);
-  export_tile<kC>(reinterpret_cast<__nv_bfloat16*>(blk + CB::aqk), sA, ST, kC, tid, NT);
+  export_tile<DK>(blk + CB::kp, sK, SQ, tcl ? 1 : 0, nullptr, tid, NT);
+  export_tile<DK>(blk + CB::w, sQ, SQ, tcl ? 1 : 0, nullptr, tid, NT);
+  export_tile<DV>(blk + CB::u, sV, SV, tcl ? 3 : 0, nullptr, tid, NT);
+  export_tile<kC>(blk + CB::aqk, sA, ST, tcl ? 2 : 0, nullptr, tid, NT);
   if (tid < kC / 4) reinterpret_cast<float4*>(blk + CB::g)[tid] = reinterpret_cast<const float4*>(sG)[tid];
 }
 
@@ -594,67 +608,64 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_kernel(const SplitArgs a) {
 // ---------------------------------------------------------------------------
 struct TcScan {
   static constexpr int D = 128;
-  static constexpr size_t a1 = 0;                          // [Q'; W] K-major, 128 rows x K 128
-  static constexpr size_t a2 = a1 + size_t(128) * D * 2;   // K' MN-major, M 128 (keys) x K 64 (tokens)
-  static constexpr size_t a3 = a2 + size_t(kC) * D * 2;    // [Aqk; 0] K-major, 128 rows x K 64
-  static constexpr size_t u = a3 + size_t(128) * kC * 2;   // U rows [kC][D], 16-byte chunks XOR-swizzled
-  static constexpr size_t stage = u + size_t(kC) * D * 2;
+  using CB = ChunkBlock<128, 128>;
+  // one stage = the chunk block's image (copy 1: q | w | kp | aqk, copy 2: u) plus the zero
+  // rows of [Aqk; 0]
+  static constexpr size_t a1 = 0;                          // [Q'; W] K-major core tile, 128 rows x K 128
+  static constexpr size_t a2 = CB::kp;                     // K' MN-major, M 128 (keys) x K 64 (tokens)
+  static constexpr size_t a3 = CB::aqk;                    // [Aqk; 0] K-major, 128 rows x K 64
+  static constexpr size_t zero = a3 + size_t(kC) * kC * 2; // rows 64..127 of [Aqk; 0]
+  static constexpr size_t u = zero + size_t(kC) * kC * 2;  // U: 256-byte rows, XOR-swizzled chunks
+  static constexpr size_t copy1 = CB::u;                   // bytes of copy 1 (block offset 0 -> stage 0)
+  static constexpr size_t copy2 = size_t(kC) * D * 2;      // bytes of copy 2 (block u -> stage u)
+  static constexpr size_t stage = u + copy2;
   static constexpr size_t b1 = 2 * stage;                  // S (bf16) MN-major, K 128 (keys) x N 128
   static constexpr size_t b2 = b1 + size_t(D) * D * 2;     // Vn MN-major, K 64 (tokens) x N 128
-  static constexpr size_t z = b2 + size_t(kC) * D * 2;     // z rows of the chunk whose O is pending [kC][D]
-  static constexpr size_t nw = z + size_t(kC) * D * 2;     // norm weight [D] f32
-  static constexpr size_t ss = nw + size_t(D) * 4;         // row sums of squares [kC][2]
-  static constexpr size_t bar = ss + size_t(kC) * 2 * 4;   // mbarriers bar1, bar2
-  static constexpr size_t slot = bar + 16;                 // TMEM base address
-  static constexpr size_t bytes = slot + 16;
-  static_assert(stage % 16 == 0 && b1 % 16 == 0 && b2 % 16 == 0 && z % 16 == 0 && bar % 8 == 0, "alignment");
+  static constexpr size_t bar = b2 + size_t(kC) * D * 2;   // mbarriers: MMA1, MMA2/3, stage 0, stage 1
+  static constexpr size_t slot = bar + 4 * 8;              // TMEM base address
+  static constexpr size_t bytes = slot + 8;
+  static_assert(a3 + size_t(kC) * kC * 2 == CB::u && copy1 % 16 == 0 && stage % 16 == 0 && bar % 8 == 0,
+                "stage image");
   static_assert(bytes <= 232448, "shared memory");
-  // core-matrix byte offset of (row, 16-byte chunk): 128-wide rows (SBO 2048, LBO 128) ...
+  // core-matrix byte offset of (row, 16-byte chunk) in 128-wide tiles (SBO 2048, LBO 128)
   __device__ static uint32_t off16(int r, int ch) { return (r >> 3) * 2048 + ch * 128 + (r & 7) * 16; }
-  // ... and 64-wide rows (SBO 1024, LBO 128)
-  __device__ static uint32_t off8(int r, int ch) { return (r >> 3) * 1024 + ch * 128 + (r & 7) * 16; }
-  // U row r, chunk ch: rows of 256 bytes, chunk index XOR (r % 8) keeps row-parallel reads conflict-free
+  // U row r, chunk ch: rows of 256 bytes, chunk index XOR (r % 8)
   __device__ static uint32_t offu(int r, int ch) { return r * 256 + ((ch ^ (r & 7)) * 16); }
 };
 
 __device__ __forceinline__ void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(n) : "memory"); }
 
-// Gated RMSNorm of one O row half (64 columns, BF16 pairs in o) times SiLU(z) to
-// the layer output; the two halves of a row exchange their sums of squares.
-// All 128 O threads call it (invalid rows skip the stores only).
-__device__ __forceinline__ void tc_o_epilogue(const SplitArgs& a, unsigned char* smem, int c, int b, int hv, int i,
-                                              int half, const uint32_t (&o)[32]) {
-  using M = TcScan;
-  const float* sNW = reinterpret_cast<const float*>(smem + M::nw);
-  float* sSS = reinterpret_cast<float*>(smem + M::ss);
-  auto lo = [](uint32_t p) { return __uint_as_float(p << 16); };
-  auto hi = [](uint32_t p) { return __uint_as_float(p & 0xffff0000u); };
-  float part = 0.f;
+// Gated RMSNorm of the layer output in place (after the tensor-core scan stored
+// BF16 O there): one warp per (row, value head) of 128, 4 columns a lane.
+//   out = bf16( bf16(w * bf16(o * rsqrt(mean(o^2) + eps))) * silu(z) )
+// (Qwen3_5RMSNormGated, modeling_qwen3_5.py:175-190; o is the BF16 gated_delta output).
+__global__ void __launch_bounds__(256) gdn_gated_norm_kernel(const SplitArgs a) {
+  const int64_t item = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int64_t rows = int64_t(a.B) * a.L;
+  if (item >= rows * a.HV) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = item / a.HV;
+  const int hv = int(item % a.HV);
+  const int conv_dim = 2 * a.H * 128 + a.HV * 128;
+  __nv_bfloat16* op = a.out + row * a.ld_out + hv * 128 + lane * 4;
+  const __nv_bfloat16* zp = a.proj + row * a.ld_proj + conv_dim + hv * 128 + lane * 4;
+  const uint2 ov = *reinterpret_cast<const uint2*>(op);
+  const uint2 zv = *reinterpret_cast<const uint2*>(zp);
+  const float2 o0 = bf2f(ov.x), o1 = bf2f(ov.y);
+  float ss = o0.x * o0.x + o0.y * o0.y + o1.x * o1.x + o1.y * o1.y;
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(ss / 128.f + a.eps);
+  const float4 w = *reinterpret_cast<const float4*>(a.norm_w + lane * 4);
+  const float2 z0 = bf2f(zv.x), z1 = bf2f(zv.y);
+  const float x[4] = {o0.x, o0.y, o1.x, o1.y}, wz[4] = {w.x, w.y, w.z, w.w}, zz[4] = {z0.x, z0.y, z1.x, z1.y};
+  float r[4];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) part += lo(o[j]) * lo(o[j]) + hi(o[j]) * hi(o[j]);
-  sSS[i * 2 + half] = part;
-  named_bar(1, 128);
-  const float inv = 1.0f / sqrtf((sSS[i * 2] + sSS[i * 2 + 1]) / 128.f + a.eps);
-  if (c * kC + i < a.L) {
-    const int64_t row = int64_t(b) * a.L + int64_t(c) * kC + i;
-    const uint4* zp = reinterpret_cast<const uint4*>(smem + M::z + i * 256 + half * 128);
-    uint4* op = reinterpret_cast<uint4*>(a.out + row * a.ld_out + hv * 128 + half * 64);
-#pragma unroll
-    for (int v = 0; v < 8; ++v) {
-      const uint4 zz = zp[v];
-      const __nv_bfloat162* z2 = reinterpret_cast<const __nv_bfloat162*>(&zz);
-      uint4 res;
-      __nv_bfloat162* r2 = reinterpret_cast<__nv_bfloat162*>(&res);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int j = half * 64 + v * 8 + 2 * e;
-        const float h0 = bf16r(sNW[j] * bf16r(lo(o[v * 4 + e]) * inv));
-        const float h1 = bf16r(sNW[j + 1] * bf16r(hi(o[v * 4 + e]) * inv));
-        r2[e] = __floats2bfloat162_rn(h0 * silu_fast(__low2float(z2[e])), h1 * silu_fast(__high2float(z2[e])));
-      }
-      op[v] = res;
-    }
-  }
+  for (int e = 0; e < 4; ++e) r[e] = bf16r(wz[e] * bf16r(x[e] * inv)) * silu_f(zz[e]);
+  uint2 res;
+  const __nv_bfloat162 h0 = __floats2bfloat162_rn(r[0], r[1]), h1 = __floats2bfloat162_rn(r[2], r[3]);
+  res.x = *reinterpret_cast<const uint32_t*>(&h0);
+  res.y = *reinterpret_cast<const uint32_t*>(&h1);
+  *reinterpret_cast<uint2*>(op) = res;
 }
 
 __global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) {
@@ -665,8 +676,9 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) 
   constexpr uint32_t kId1 = tc::idesc_bf16(128, 128, 0, 1);  // K-major A, MN-major B
   constexpr uint32_t kId2 = tc::idesc_bf16(128, 128, 1, 1);  // MN-major A and B
   extern __shared__ __align__(16) unsigned char smem[];
-  uint64_t* bar1 = reinterpret_cast<uint64_t*>(smem + M::bar);
-  uint64_t* bar2 = bar1 + 1;
+  uint64_t* bar1 = reinterpret_cast<uint64_t*>(smem + M::bar);  // MMA1 commits
+  uint64_t* bar2 = bar1 + 1;                                       // MMA2/3 commits
+  uint64_t* ldbar = bar1 + 2;                                      // stage loads [2]
   uint32_t* slot = reinterpret_cast<uint32_t*>(smem + M::slot);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quad = warp & 3, half = warp >> 2;
@@ -674,24 +686,17 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) 
   const bool vwarp = quad >= 2;              // quadrants 2, 3: W rows -> Vn
   const bool issuer = tid == 64;
   const int bh = blockIdx.x, b = bh / a.HV, hv = bh % a.HV;
-  const int conv_dim = 2 * a.H * D + a.HV * D;
   const unsigned char* blocks = a.blocks + int64_t(bh) * a.nc * CB::bytes;
   const uint32_t sbase = smem_u32(smem);
 
-  auto load_block = [&](int c, int st) {
+  int ld_issued[2] = {0, 0};  // stage loads issued (issuer thread)
+  auto load_block = [&](int c, int st) {  // issuer: chunk block c (its shared-memory image) -> stage st
     const unsigned char* src = blocks + int64_t(c) * CB::bytes;
     unsigned char* dst = smem + st * M::stage;
-    for (int i = tid; i < kC * 16; i += 256) {
-      const int r = i >> 4, ch = i & 15;
-      cp_async16(dst + M::a1 + M::off16(r, ch), src + CB::q + r * 256 + ch * 16);
-      cp_async16(dst + M::a1 + M::off16(64 + r, ch), src + CB::w + r * 256 + ch * 16);
-      cp_async16(dst + M::a2 + M::off16(r, ch), src + CB::kp + r * 256 + ch * 16);
-      cp_async16(dst + M::u + M::offu(r, ch), src + CB::u + r * 256 + ch * 16);
-    }
-    for (int i = tid; i < kC * 8; i += 256) {
-      const int r = i >> 3, ch = i & 7;
-      cp_async16(dst + M::a3 + M::off8(r, ch), src + CB::aqk + r * 128 + ch * 16);
-    }
+    tc::mbar_expect_tx(ldbar + st, uint32_t(M::copy1 + M::copy2));
+    tc::bulk_g2s(dst, src, uint32_t(M::copy1), ldbar + st);
+    tc::bulk_g2s(dst + M::u, src + CB::u, uint32_t(M::copy2), ldbar + st);
+    ++ld_issued[st];
   };
 
   // S = 0 (bf16 copy), zero rows 64..127 of [Aqk; 0] in both stages, norm weight, barriers, TMEM
@@ -699,40 +704,33 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) 
   for (int i = tid; i < D * D * 2 / 16; i += 256) reinterpret_cast<uint4*>(smem + M::b1)[i] = z4;
   for (int st = 0; st < 2; ++st)
     for (int i = tid; i < 64 * kC * 2 / 16; i += 256)
-      reinterpret_cast<uint4*>(smem + st * M::stage + M::a3 + M::off8(64, 0))[i] = z4;
-  for (int i = tid; i < D; i += 256) reinterpret_cast<float*>(smem + M::nw)[i] = a.norm_w[i];
+      reinterpret_cast<uint4*>(smem + st * M::stage + M::zero)[i] = z4;
   if (tid == 0) {
-    tc::mbar_init(bar1, 1);
-    tc::mbar_init(bar2, 1);
+    for (int i = 0; i < 4; ++i) tc::mbar_init(bar1 + i, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   if (warp == 0) tc::tmem_alloc(slot, 256);
-  load_block(0, 0);
-  cp_async_commit();
+  tc::fence_async_smem();  // zeroed operand rows -> tensor cores
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
+  if (issuer) load_block(0, 0);
   const uint32_t tmem = *slot;
   const uint32_t lane_off = uint32_t(quad * 32) << 16;
   const uint32_t tS = tmem + lane_off + half * 64, tP = tmem + 128 + lane_off + half * 64;
   bool ok = true;
-  uint32_t o[32];    // this thread's O row half (BF16 pairs), O warps
-  int pending = -1;  // chunk whose O is held in o[]
 
   for (int c = 0; c < a.nc; ++c) {
     const int st = c & 1;
     const uint32_t par = uint32_t(c) & 1u;
     const unsigned char* sb = smem + st * M::stage;
     const uint32_t sbu = sbase + st * M::stage;
-    cp_async_wait<0>();
+    ok = tc::mbar_wait(ldbar + st, uint32_t(c >> 1) & 1u, kWait) && ok;  // block c staged
     tc::fence_async_smem();
     tc::fence_before();
-    ok = __syncthreads_and(ok);  // block c and z rows of chunk c-1 staged; chunk c-1's TMEM traffic done
+    ok = __syncthreads_and(ok);  // chunk c-1's S copy, TMEM traffic and stage reads done
     if (!ok) break;
     tc::fence_after();
-    if (c + 1 < a.nc) {
-      load_block(c + 1, st ^ 1);
-      cp_async_commit();
-    }
     const float gl_next =
         c + 1 < a.nc ? *reinterpret_cast<const float*>(blocks + int64_t(c + 1) * CB::bytes + CB::g + (kC - 1) * 4) : 0.f;
     if (vwarp) {
@@ -742,6 +740,7 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) 
           tc::mma_bf16(tmem + 128, tc::smem_desc(sbu + M::a1 + s * 256, 128, 2048),
                        tc::smem_desc(sbase + M::b1 + s * 4096, 2048, 128), kId1, s > 0);
         tc::commit(bar1);
+        if (c + 1 < a.nc) load_block(c + 1, st ^ 1);  // stage st^1 was last read by chunk c-1
       }
       ok = tc::mbar_wait(bar1, par, kWait) && ok;
       tc::fence_after();
@@ -780,20 +779,27 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) 
                        tc::smem_desc(sbase + M::b2 + s * 4096, 2048, 128), kId1, true);
         tc::commit(bar2);
       }
-    } else if (pending >= 0) {  // O warps: epilogue of chunk c-1, overlapping MMA1 -> Vn -> MMA2/3
-      tc_o_epilogue(a, smem, pending, b, hv, row, half, o);
     }
     ok = tc::mbar_wait(bar2, par, kWait) && ok;
     tc::fence_after();
-    if (!vwarp) {  // z rows of chunk c for its epilogue (every O thread is past chunk c-1's z reads)
-      named_bar(1, 128);
-      for (int i = tid - (warp >= 4 ? 64 : 0); i < kC * 16; i += 128) {
-        const int r = i >> 4, ch = i & 15;
-        if (c * kC + r < a.L)
-          cp_async16(smem + M::z + r * 256 + ch * 16,
-                     a.proj + (int64_t(b) * a.L + int64_t(c) * kC + r) * a.ld_proj + conv_dim + hv * D + ch * 8);
+    if (!vwarp) {  // O rows (lanes 0..63) -> BF16 layer output; the gated RMSNorm is a separate kernel
+      const bool valid = c * kC + row < a.L;
+      uint4* op = reinterpret_cast<uint4*>(a.out + (int64_t(b) * a.L + int64_t(c) * kC + row) * a.ld_out + hv * D + half * 64);
+#pragma unroll
+      for (int piece = 0; piece < 2; ++piece) {
+        uint32_t r[32];
+        tc::ld32(tP + piece * 32, r);
+        tc::wait_ld();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 res;
+          uint32_t* rw = reinterpret_cast<uint32_t*>(&res);
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            rw[e] = bf2_pack(__uint_as_float(r[q * 8 + 2 * e]), __uint_as_float(r[q * 8 + 2 * e + 1]));
+          if (valid) op[piece * 4 + q] = res;
+        }
       }
-      cp_async_commit();
     }
     {  // S: bf16 copy for the next MMA1 (and the final state), then S *= e^{G_last(next chunk)}
       const float f = __expf(gl_next);
@@ -823,25 +829,13 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) 
       tc::wait_st();
       tc::fence_async_smem();
     }
-    if (!vwarp) {  // O rows, read now so the next MMA1 may overwrite P
-#pragma unroll
-      for (int piece = 0; piece < 2; ++piece) {
-        uint32_t r[32];
-        tc::ld32(tP + piece * 32, r);
-        tc::wait_ld();
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const __nv_bfloat162 p2 = __floats2bfloat162_rn(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
-          o[piece * 16 + j] = *reinterpret_cast<const uint32_t*>(&p2);
-        }
-      }
-      pending = c;
-    }
   }
-  cp_async_wait<0>();
-  __syncthreads();  // the last chunk's z rows are staged
-  if (ok && !vwarp && pending >= 0) tc_o_epilogue(a, smem, pending, b, hv, row, half, o);
-  if (!ok && tid == 0) atomicOr(a.status, 1u);
+  if (!ok) {  // a wait timed out: report, and give in-flight copies a bounded time to land
+    if (tid == 0) atomicOr(a.status, 1u);
+    if (issuer)
+      for (int st = 0; st < 2; ++st)
+        if (ld_issued[st] > 0) tc::mbar_wait(ldbar + st, uint32_t(ld_issued[st] - 1) & 1u, kWait);
+  }
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
@@ -855,6 +849,10 @@ int launch_split(SplitArgs& a, void* ws, int64_t ws_bytes, cudaStream_t s) {
              "gdn prefill: workspace too small");
   a.status = static_cast<uint32_t*>(ws);  // bytes [0, 256): status word; chunk blocks after
   a.blocks = static_cast<unsigned char*>(ws) + 256;
+  const bool tc_scan = DK == 128 && DV == 128 && a.ld_out % 8 == 0 && a.ld_proj % 8 == 0 &&
+                       (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.state) & 15) == 0 &&
+                       (reinterpret_cast<uintptr_t>(a.norm_w) & 15) == 0;
+  a.tc_layout = tc_scan ? 1 : 0;
   if (cudaMemsetAsync(a.status, 0, sizeof(uint32_t), s) != cudaSuccess) {
     set_error("gdn prefill: cannot clear the status word");
     return KADLLM_ECUDA;
@@ -869,8 +867,6 @@ int launch_split(SplitArgs& a, void* ws, int64_t ws_bytes, cudaStream_t s) {
     kern<<<dim3(a.nc, unsigned(n)), 256, smem, s>>>(a);
     KB_CHECK_LAUNCH("gdn prefill prep launch");
   }
-  const bool tc_scan = DK == 128 && DV == 128 && a.ld_out % 8 == 0 &&
-                       (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.state) & 15) == 0;
   if (tc_scan) {
     const size_t smem = TcScan::bytes;
     if (cudaFuncSetAttribute(gdn_scan_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess) {
@@ -879,6 +875,9 @@ int launch_split(SplitArgs& a, void* ws, int64_t ws_bytes, cudaStream_t s) {
     }
     gdn_scan_tc_kernel<<<unsigned(n), 256, smem, s>>>(a);
     KB_CHECK_LAUNCH("gdn prefill tensor-core scan launch");
+    const int64_t items = int64_t(a.B) * a.L * a.HV;  // (row, value head) pairs, 8 per CTA
+    gdn_gated_norm_kernel<<<unsigned((items + 7) / 8), 256, 0, s>>>(a);
+    KB_CHECK_LAUNCH("gdn prefill gated norm launch");
     return KADLLM_OK;
   }
   {

@@ -110,25 +110,32 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(__nv_bfloat16* x, cons
   store_row<H>(normed + i * H, o);
 }
 
-__global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* gu, int64_t ld, int64_t inter,
+// grid (x: 512-column spans, y: rows with stride); each thread two 8-column chunks.
+// SiLU through the approximate exp2 / reciprocal units in fp32 pairs.
+__global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* gu, int64_t ld, int inter,
                                                        __nv_bfloat16* out, int64_t rows) {
-  const int64_t chunks = inter / 8;
-  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= rows * chunks) return;
-  const int64_t r = i / chunks, c = (i % chunks) * 8;
-  const uint4 gv = *reinterpret_cast<const uint4*>(gu + r * ld + c);
-  const uint4 uv = *reinterpret_cast<const uint4*>(gu + r * ld + inter + c);
-  const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv);
-  const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&uv);
-  uint4 ov;
-  __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&ov);
+  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
+    const __nv_bfloat16* g = gu + r * ld;
+    const __nv_bfloat16* u = g + inter;
+    __nv_bfloat16* o = out + r * int64_t(inter);
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float g0 = __low2float(g2[j]), g1 = __high2float(g2[j]);
-    const float a0 = bf16r(silu_f(g0)), a1 = bf16r(silu_f(g1));
-    o2[j] = __floats2bfloat162_rn(a0 * __low2float(u2[j]), a1 * __high2float(u2[j]));
+    for (int h = 0; h < 2; ++h) {
+      const int c = (blockIdx.x * 512 + h * 256 + threadIdx.x) * 8;
+      if (c >= inter) continue;
+      const uint4 gv = *reinterpret_cast<const uint4*>(g + c);
+      const uint4 uv = *reinterpret_cast<const uint4*>(u + c);
+      const uint32_t* gw = reinterpret_cast<const uint32_t*>(&gv);
+      const uint32_t* uw = reinterpret_cast<const uint32_t*>(&uv);
+      uint4 ov;
+      uint32_t* ow = reinterpret_cast<uint32_t*>(&ov);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 a = silu2(bf2f(gw[j]));
+        ow[j] = bf2_pack_f2(mul2(bf2f(bf2_pack(a.x, a.y)), bf2f(uw[j])));
+      }
+      *reinterpret_cast<uint4*>(o + c) = ov;
+    }
   }
-  *reinterpret_cast<uint4*>(out + r * inter + c) = ov;
 }
 
 // One warp per (row, head).  D elements per head, EPL = D / 32 per lane (contiguous).
@@ -250,9 +257,12 @@ extern "C" int kadllm_silu_mul(const void* gate_up, int64_t ld, int64_t inter, v
                                void* stream) {
   KB_REQUIRE(gate_up && out && rows >= 1 && inter % 8 == 0 && ld % 8 == 0, KADLLM_EINVAL,
              "silu_mul: bad arguments (intermediate size and stride must be multiples of 8)");
-  const int64_t n = rows * (inter / 8);
-  silu_mul_kernel<<<unsigned((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(gate_up), ld, inter, static_cast<__nv_bfloat16*>(out), rows);
+  KB_REQUIRE(inter < (int64_t(1) << 30) && (reinterpret_cast<uintptr_t>(gate_up) & 15) == 0 &&
+                 (reinterpret_cast<uintptr_t>(out) & 15) == 0,
+             KADLLM_EINVAL, "silu_mul: pointers must be 16-byte aligned");
+  const dim3 grid(unsigned((inter / 8 + 511) / 512), unsigned(rows < 65535 ? rows : 65535));
+  silu_mul_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(gate_up), ld, int(inter), static_cast<__nv_bfloat16*>(out), rows);
   KB_CHECK_LAUNCH("silu_mul launch");
   return KADLLM_OK;
 }
