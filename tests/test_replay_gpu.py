@@ -136,13 +136,15 @@ def test_operator_errors_match_reference_conventions():
                         torch.zeros(4, 9, 2, device="cuda"), s, beam_width=2)
 
 
+@pytest.mark.parametrize("K,H,HV", [(64, 2, 4), (128, 2, 4), (128, 4, 16)])
 @pytest.mark.parametrize("T", [1, 2, 3])
-def test_gdn_mixer_matches_oracle_composition(T):
-    """Fused conv + gates + replay + gated RMSNorm against the oracle's op chain."""
+def test_gdn_mixer_matches_oracle_composition(T, K, H, HV):
+    """Fused conv + gates + replay + gated RMSNorm against the oracle's op chain
+    (W = 33: a ragged last beam block; the 0.8B head shape is K = 128, HV = 16)."""
     from kadllm_b200 import _lib
 
-    rng = np.random.default_rng(10 + T)
-    B, W, H, HV, K = 2, 33, 2, 4, 64
+    rng = np.random.default_rng(10 + T + K + HV)
+    B, W = 2, 33
     kd, vd = H * K, HV * K
     C = 2 * kd + vd
     ld = C + vd + 2 * HV + 8
