@@ -234,6 +234,35 @@ KADLLM_API int kadllm_gdn_prefill_split(const void* proj, int64_t ld_proj, const
                                         int64_t heads, int64_t v_heads, int64_t k_dim, int64_t v_dim,
                                         void* stream);
 
+/* Tiled K / V prefix for the tensor-core attention (head_dim 256): per
+ * (sequence, kv head) blocks of 64 positions, each a 32 KB core-matrix image
+ * [8-position group][32 dim chunks][8 positions][16 bytes], zero past length.
+ * src [S][HK][L][D] via element strides (seq, pos, head). */
+KADLLM_API int64_t kadllm_kv_tile_bytes(int64_t seqs, int64_t kv_heads, int64_t length, int64_t head_dim);
+KADLLM_API int kadllm_kv_tile(const void* src, int64_t s_seq, int64_t s_pos, int64_t s_head, int64_t seqs,
+                              int64_t kv_heads, int64_t length, int64_t head_dim, void* tiles,
+                              int64_t tile_bytes, void* stream);
+
+/* Attention over a tiled prefix on tcgen05 tensor cores (head_dim 256, BF16):
+ * 128 query rows per CTA, S and O in tensor memory, bulk-copied K / V blocks.
+ * causal = 0: beam decode -- rows (beam, t, g) of q [B*W rows][T][Hq][D]
+ *   attend to the request's prefix and their beam's suffix keys s <= t
+ *   (src/kadllm/ops.py:252-341); suffix_k / suffix_v [B*W][T][HK][D].
+ * causal = 1: prompt prefill -- q rows = tokens b*L + pos, keys <= pos (SDPA in
+ *   Qwen3_5Attention, TF:620-692); suffix and steps unused.
+ * gate (optional): out = bf16(bf16(o) * bf16(sigmoid(gate))).  All strides in
+ * elements, multiples of 8; status: device word, bit 0 = a bounded wait of the
+ * kernel timed out (results invalid). */
+KADLLM_API int kadllm_attention_tiled(const void* q, int64_t sq_row, int64_t sq_t, int64_t sq_h,
+                                      const void* k_tiles, const void* v_tiles, int64_t blocks_per_head,
+                                      const void* suffix_k, int64_t ssk_row, int64_t ssk_t, int64_t ssk_h,
+                                      const void* suffix_v, int64_t ssv_row, int64_t ssv_t, int64_t ssv_h,
+                                      const void* gate, int64_t sg_row, int64_t sg_t, int64_t sg_h, void* out,
+                                      int64_t so_row, int64_t so_t, int64_t so_h, uint32_t* status,
+                                      int64_t batch, int64_t beam_width, int64_t steps, int64_t q_heads,
+                                      int64_t kv_heads, int64_t prefix_len, int64_t head_dim, float scale,
+                                      int causal, void* stream);
+
 /* Prompt causal GQA attention (flash loop on the tensor cores) with the fused
  * output gate out = bf16(o) * bf16(sigmoid(gate)) (gate may be NULL).
  * q [B*L rows, H, D] (sq_row, sq_h); k / v [B, HK, L, D] via (s?_b, s?_l, s?_h);

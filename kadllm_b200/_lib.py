@@ -23,6 +23,9 @@ SIGNATURES: dict[str, list] = {
     "kadllm_silu_mul": [P, L, L, P, L, P],
     "kadllm_qk_norm_rope": [P, L, L, L, L, P, P, F, P, P, L, P, L, L, P, L, L, P, L, L, L, P, L, L, L, L, P],
     "kadllm_gdn_prefill_split": [P, L, P, P, P, P, P, F, P, L, P, P, L, L, L, L, L, L, L, P],
+    "kadllm_kv_tile": [P, L, L, L, L, L, L, L, P, L, P],
+    "kadllm_attention_tiled": [P, L, L, L, P, P, L, P, L, L, L, P, L, L, L, P, L, L, L, P, L, L, L, P,
+                               L, L, L, L, L, L, L, F, I, P],
     "kadllm_causal_attention": [P, L, L, P, L, L, L, P, L, L, L, P, L, L, P, L, L, L, L, L, L, L, F, P],
     "kadllm_beam_select": [P, I, L, P, P, P, P, P, P, L, L, L, L, L, L, P],
     "kadllm_beam_select_status": [P, L, L, P, P],
@@ -53,6 +56,8 @@ def lib() -> ctypes.CDLL:
         handle.kadllm_beam_select_workspace.argtypes = [L, L]
         handle.kadllm_gdn_prefill_workspace.restype = ctypes.c_int64
         handle.kadllm_gdn_prefill_workspace.argtypes = [L, L, L, L, L]
+        handle.kadllm_kv_tile_bytes.restype = ctypes.c_int64
+        handle.kadllm_kv_tile_bytes.argtypes = [L, L, L, L]
         for name, args in SIGNATURES.items():
             fn = getattr(handle, name)
             fn.argtypes = args

@@ -1,0 +1,504 @@
+// Attention over a tiled K/V prefix on the 5th-generation tensor cores
+// (head_dim 256): beam decode (shared prefix + per-beam causal suffix) and
+// prompt prefill (causal).
+//
+// Semantics: src/kadllm/ops.py:252-341 (prefix_attention: softmax over the
+// request's prefix keys and the beam's own suffix keys s <= t, merged by
+// log-sum-exp) and the SDPA call of Qwen3_5Attention on the prompt
+// (transformers/models/qwen3_5/modeling_qwen3_5.py:620-692), with the output
+// gate out = bf16(bf16(o) * bf16(sigmoid(gate))) (src/kadllm/adapters/
+// qwen3_5.py:328-330).
+//
+// Tiled prefix: for each (request, kv head) the keys (and values) sit in
+// blocks of 64 positions x 256 dims, each block a 32 KB core-matrix image
+// [8-position group][32 dim chunks][8 positions][16 bytes]: read as a K-major B
+// operand (rows = keys) for S = Q K^T and as an MN-major B operand (rows =
+// dims) for O += P V, and staged with one bulk copy.  kadllm_kv_tile builds it
+// from the [B, HK, L, D] cache, zero-padding the last block.
+//
+// One CTA = 128 query rows of one (request, kv head), 4 warps = the 4 TMEM lane
+// quadrants (thread r owns query row r).  TMEM: S double buffer (2 x 64
+// columns), O (256 columns).  Per key block j: MMA_S(j+1) runs while the
+// threads turn S(j) into probabilities (online softmax in the exp2 domain; the
+// reference maximum only moves when a row maximum exceeds it by 8, so O is
+// rescaled rarely), write P (BF16, K-major core tile) to shared memory, and one
+// thread issues O += P V(j).  K and V blocks are double-buffered, refilled as
+// soon as the MMA that read them completes.  Every mbarrier wait is bounded and
+// reports through a status word.
+#include "tcgen05.cuh"
+
+namespace kb {
+namespace {
+
+constexpr int kD = 256;      // head dim
+constexpr int kRows = 128;   // query rows per CTA
+constexpr int kBlk = 64;     // keys per block
+constexpr int kTile = kBlk * kD * 2;  // bytes of one K or V block (32 KB)
+constexpr int kSufMax = 8;
+
+struct AttnTcArgs {
+  const __nv_bfloat16* q; int64_t sq_row, sq_t, sq_h;  // decode: row = beam row; causal: row = token b*L + pos
+  const unsigned char* kt; const unsigned char* vt;     // tiled prefix [B*HK][nblk][kTile]
+  int nblk;
+  const __nv_bfloat16* sk; int64_t ssk_row, ssk_t, ssk_h;  // decode suffix keys / values
+  const __nv_bfloat16* sv; int64_t ssv_row, ssv_t, ssv_h;
+  const __nv_bfloat16* gate; int64_t sg_row, sg_t, sg_h;
+  __nv_bfloat16* out; int64_t so_row, so_t, so_h;
+  uint32_t* status;
+  int B, W, T, H, HK, G, L;
+  float scale_log2;
+};
+
+struct AttnTcSmem {
+  static constexpr size_t q = 0;                                 // [128 rows][256] K-major core tile
+  static constexpr size_t k = q + size_t(kRows) * kD * 2;        // K blocks [2]
+  static constexpr size_t v = k + 2 * size_t(kTile);             // V blocks [2]
+  static constexpr size_t p = v + 2 * size_t(kTile);             // P [128 rows][64 keys] K-major core tile
+  static constexpr size_t bar = p + size_t(kRows) * kBlk * 2;    // ldK[2], ldV[2], S[2], O
+  static constexpr size_t slot = bar + 7 * 8;
+  static constexpr size_t bytes = slot + 8;
+  static_assert(bytes <= 232448, "shared memory");
+  // 16-byte unit (row r, chunk c) of a core tile whose rows have `chunks` 16-byte chunks
+  __device__ static uint32_t off(int r, int c, int chunks) { return (r >> 3) * (chunks * 128) + c * 128 + (r & 7) * 16; }
+};
+
+template <bool CAUSAL>
+__global__ void __launch_bounds__(128, 1) attn_tc_kernel(const AttnTcArgs a) {
+  using M = AttnTcSmem;
+  constexpr long long kWait = 1ll << 31;
+  constexpr uint32_t kIdS = tc::idesc_bf16(kRows, kBlk, 0, 0);  // S = Q K^T: K-major Q and K
+  constexpr uint32_t kIdO = tc::idesc_bf16(kRows, kD, 0, 1);    // O += P V: K-major P, MN-major V
+  extern __shared__ __align__(16) unsigned char smem[];
+  uint64_t* ldK = reinterpret_cast<uint64_t*>(smem + M::bar);  // [2]
+  uint64_t* ldV = ldK + 2;                                      // [2]
+  uint64_t* barS = ldK + 4;                                     // [2]
+  uint64_t* barO = ldK + 6;
+  uint32_t* slot = reinterpret_cast<uint32_t*>(smem + M::slot);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int b = blockIdx.y / a.HK, hk = blockIdx.y % a.HK;
+  const int TG = a.T * a.G;
+  const int R = CAUSAL ? a.L * a.G : a.W * TG;
+  const int row0 = blockIdx.x * kRows;
+  const int gr = row0 + tid;  // this thread's query row (= TMEM lane tid)
+  const bool rvalid = gr < R;
+  int beam = 0, t = 0, g = 0, pos = 0;
+  if (CAUSAL) {
+    pos = gr / a.G;
+    g = gr % a.G;
+  } else {
+    beam = gr / TG;
+    const int rem = gr % TG;
+    t = rem / a.G;
+    g = rem % a.G;
+  }
+  const int hq = hk * a.G + g;
+  const int64_t qoff = CAUSAL ? (int64_t(b) * a.L + pos) * a.sq_row + int64_t(hq) * a.sq_h
+                              : (int64_t(b) * a.W + beam) * a.sq_row + int64_t(t) * a.sq_t + int64_t(hq) * a.sq_h;
+  int nkeys = a.L;
+  if (CAUSAL) nkeys = min(a.L, min(R - 1, row0 + kRows - 1) / a.G + 1);
+  const int nb = (nkeys + kBlk - 1) / kBlk;
+  const unsigned char* ktile = a.kt + int64_t(b * a.HK + hk) * a.nblk * kTile;
+  const unsigned char* vtile = a.vt + int64_t(b * a.HK + hk) * a.nblk * kTile;
+  const uint32_t sbase = smem_u32(smem);
+
+  // ---- prologue: barriers, TMEM, Q tile, first K / V blocks, MMA_S(0) ----------------
+  if (tid == 0) {
+    for (int i = 0; i < 7; ++i) tc::mbar_init(ldK + i, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  if (warp == 0) tc::tmem_alloc(slot, 512);
+  for (int c = 0; c < kD / 8; ++c) {
+    unsigned char* dst = smem + M::q + M::off(tid, c, kD / 8);
+    if (rvalid) cp_async16(dst, a.q + qoff + c * 8);
+    else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+  }
+  cp_async_commit();
+  tc::fence_before();
+  __syncthreads();  // barriers initialised, TMEM address published
+  tc::fence_after();
+  const uint32_t tmem = *slot;
+  const uint32_t lane_off = uint32_t(warp * 32) << 16;
+  const uint32_t tO = tmem + 128 + lane_off;
+  int issued_k[2] = {0, 0}, issued_v[2] = {0, 0};  // loads issued per buffer (thread 0)
+  auto load_k = [&](int j) {
+    const int s = j & 1;
+    tc::mbar_expect_tx(ldK + s, uint32_t(kTile));
+    tc::bulk_g2s(smem + M::k + s * kTile, ktile + int64_t(j) * kTile, uint32_t(kTile), ldK + s);
+    ++issued_k[s];
+  };
+  auto load_v = [&](int j) {
+    const int s = j & 1;
+    tc::mbar_expect_tx(ldV + s, uint32_t(kTile));
+    tc::bulk_g2s(smem + M::v + s * kTile, vtile + int64_t(j) * kTile, uint32_t(kTile), ldV + s);
+    ++issued_v[s];
+  };
+  auto issue_s = [&](int j) {  // S[j & 1] = Q K_j^T
+    const int s = j & 1;
+#pragma unroll
+    for (int kk = 0; kk < kD / 16; ++kk)
+      tc::mma_bf16(tmem + s * kBlk, tc::smem_desc(sbase + M::q + kk * 256, 128, 4096),
+                   tc::smem_desc(sbase + M::k + s * kTile + kk * 256, 128, 4096), kIdS, kk > 0);
+    tc::commit(barS + s);
+  };
+  auto issue_o = [&](int j) {  // O (+)= P V_j
+    const int s = j & 1;
+#pragma unroll
+    for (int kk = 0; kk < kBlk / 16; ++kk)
+      tc::mma_bf16(tmem + 128, tc::smem_desc(sbase + M::p + kk * 256, 128, 1024),
+                   tc::smem_desc(sbase + M::v + s * kTile + kk * 8192, 4096, 128), kIdO, j > 0 || kk > 0);
+    tc::commit(barO);
+  };
+  if (tid == 0 && nb > 0) {
+    load_k(0);
+    load_v(0);
+    if (nb > 1) {
+      load_k(1);
+      load_v(1);
+    }
+  }
+  cp_async_wait<0>();
+  tc::fence_async_smem();
+  __syncthreads();  // Q tile staged
+  bool ok = true;
+  if (tid == 0 && nb > 0) {
+    ok = tc::mbar_wait(ldK, 0, kWait) && ok;
+    tc::fence_after();
+    issue_s(0);
+  }
+
+  // ---- key blocks ----------------------------------------------------------------------
+  const int key_lim = CAUSAL ? pos : a.L - 1;  // last key this row attends to
+  float m_ref = -INFINITY, l = 0.f;            // exp2-domain reference maximum, running sum
+  for (int j = 0; j < nb; ++j) {
+    const int sb = j & 1;
+    if (tid == 0 && j + 1 < nb) {  // MMA_S(j+1) overlaps this block's softmax
+      ok = tc::mbar_wait(ldK + ((j + 1) & 1), uint32_t((j + 1) >> 1) & 1u, kWait) && ok;
+      tc::fence_after();
+      issue_s(j + 1);
+    }
+    ok = tc::mbar_wait(barS + sb, uint32_t(j >> 1) & 1u, kWait) && ok;
+    tc::fence_after();
+    float x[kBlk];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t r[32];
+      tc::ld32(tmem + lane_off + sb * kBlk + h * 32, r);
+      tc::wait_ld();
+#pragma unroll
+      for (int c = 0; c < 32; ++c) x[h * 32 + c] = __uint_as_float(r[c]);
+    }
+    if (j * kBlk + kBlk - 1 > key_lim) {  // partial block: keys past this row's limit drop out
+#pragma unroll
+      for (int c = 0; c < kBlk; ++c)
+        if (j * kBlk + c > key_lim) x[c] = -INFINITY;
+    }
+    float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+    for (int c = 0; c < kBlk; ++c) m4[c & 3] = fmaxf(m4[c & 3], x[c]);
+    const float bmax = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * a.scale_log2;
+    float f = 1.f;
+    bool resc = false;
+    if (bmax > m_ref + 8.f) {  // move the reference (always on the first finite block)
+      f = m_ref == -INFINITY ? 0.f : fast_ex2(m_ref - bmax);
+      m_ref = bmax;
+      l *= f;
+      resc = true;
+    }
+    const float mr = m_ref == -INFINITY ? 0.f : m_ref;  // all scores are -inf while m_ref is
+    uint32_t pk[kBlk / 2];
+    float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int c = 0; c < kBlk; c += 2) {
+      const float p0 = fast_ex2(fmaf(x[c], a.scale_log2, -mr));
+      const float p1 = fast_ex2(fmaf(x[c + 1], a.scale_log2, -mr));
+      s4[(c >> 1) & 3] += p0 + p1;
+      pk[c / 2] = bf2_pack(p0, p1);
+    }
+    l += (s4[0] + s4[1]) + (s4[2] + s4[3]);
+    if (j > 0) {  // MMA_O(j-1) complete: P is free and O is stable
+      ok = tc::mbar_wait(barO, uint32_t(j - 1) & 1u, kWait) && ok;
+      tc::fence_after();
+      if (resc) {
+#pragma unroll 1
+        for (int piece = 0; piece < kD / 32; ++piece) {
+          uint32_t r[32];
+          tc::ld32(tO + piece * 32, r);
+          tc::wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) r[c] = __float_as_uint(__uint_as_float(r[c]) * f);
+          tc::st32(tO + piece * 32, r);
+        }
+        tc::wait_st();
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < kBlk / 8; ++c)
+      *reinterpret_cast<uint4*>(smem + M::p + M::off(tid, c, kBlk / 8)) =
+          make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+    tc::fence_async_smem();
+    tc::fence_before();
+    ok = __syncthreads_and(ok);  // P staged, S(j) and O rows read / rescaled
+    if (!ok) break;
+    tc::fence_after();
+    if (tid == 0) {
+      ok = tc::mbar_wait(ldV + sb, uint32_t(j >> 1) & 1u, kWait) && ok;
+      issue_o(j);
+      if (j + 2 < nb) load_k(j + 2);              // K(j) was read by MMA_S(j), complete
+      if (j >= 1 && j + 1 < nb) load_v(j + 1);    // V(j-1) was read by MMA_O(j-1), complete
+    }
+  }
+
+  // ---- epilogue: merge the beam's suffix (decode), normalise, gate, store --------------
+  if (ok && nb > 0) {
+    ok = tc::mbar_wait(barO, uint32_t(nb - 1) & 1u, kWait);  // every MMA done: K / V / P buffers free
+    tc::fence_after();
+  }
+  // stage the gate rows (V buffers, 512-byte rows, chunk c at c ^ (row % 32)) and this CTA's
+  // beams' suffix keys / values (K buffers) with one batch of cp.async
+  auto row_map = [&](int r, int& rbeam, int& rt, int& rg, int& rpos) {
+    const int grr = row0 + r;
+    if (CAUSAL) { rpos = grr / a.G; rg = grr % a.G; rbeam = 0; rt = 0; }
+    else { rbeam = grr / TG; const int rem = grr % TG; rt = rem / a.G; rg = rem % a.G; rpos = 0; }
+  };
+  const int row_hi = min(row0 + kRows, R) - 1;
+  const int beam_lo = CAUSAL ? 0 : row0 / TG;
+  const int nbeams = CAUSAL ? 0 : row_hi / TG - beam_lo + 1;
+  const bool suf_smem = !CAUSAL && int64_t(nbeams) * a.T * kD * 2 * 2 <= int64_t(2) * kTile;
+  if (a.gate) {
+    for (int i = tid; i < kRows * (kD / 8); i += kRows) {
+      const int r = i / (kD / 8), c = i % (kD / 8);
+      if (row0 + r > row_hi) continue;
+      int rb, rt, rg, rp;
+      row_map(r, rb, rt, rg, rp);
+      const int rhq = hk * a.G + rg;
+      const __nv_bfloat16* src =
+          CAUSAL ? a.gate + (int64_t(b) * a.L + rp) * a.sg_row + int64_t(rhq) * a.sg_h
+                 : a.gate + (int64_t(b) * a.W + rb) * a.sg_row + int64_t(rt) * a.sg_t + int64_t(rhq) * a.sg_h;
+      cp_async16(smem + M::v + r * 512 + ((c ^ (r & 31)) * 16), src + c * 8);
+    }
+  }
+  if (suf_smem) {
+    for (int i = tid; i < nbeams * a.T * 2 * (kD / 8); i += kRows) {
+      const int c = i % (kD / 8), rest = i / (kD / 8), kv = rest & 1, bs = rest >> 1, sidx = bs % a.T, bi = bs / a.T;
+      const int64_t br = int64_t(b) * a.W + beam_lo + bi;
+      const __nv_bfloat16* src = kv ? a.sv + br * a.ssv_row + int64_t(sidx) * a.ssv_t + int64_t(hk) * a.ssv_h
+                                    : a.sk + br * a.ssk_row + int64_t(sidx) * a.ssk_t + int64_t(hk) * a.ssk_h;
+      cp_async16(smem + M::k + ((bi * a.T + sidx) * 2 + kv) * 512 + c * 16, src + c * 8);
+    }
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();
+  const int64_t brow = int64_t(b) * a.W + beam;
+  auto suf = [&](int sidx, int kv) -> const __nv_bfloat16* {  // this row's suffix key / value s
+    if (suf_smem)
+      return reinterpret_cast<const __nv_bfloat16*>(smem + M::k + (((beam - beam_lo) * a.T + sidx) * 2 + kv) * 512);
+    return kv ? a.sv + brow * a.ssv_row + int64_t(sidx) * a.ssv_t + int64_t(hk) * a.ssv_h
+              : a.sk + brow * a.ssk_row + int64_t(sidx) * a.ssk_t + int64_t(hk) * a.ssk_h;
+  };
+  float mx = m_ref, alpha = 1.f, ssum = l;
+  float psuf[kSufMax];
+#pragma unroll
+  for (int sidx = 0; sidx < kSufMax; ++sidx) psuf[sidx] = 0.f;
+  if (!CAUSAL && rvalid) {
+    float xs[kSufMax];
+#pragma unroll
+    for (int sidx = 0; sidx < kSufMax; ++sidx) {
+      xs[sidx] = -INFINITY;
+      if (sidx < a.T && sidx <= t) {  // scores against the beam's own keys s <= t
+        const __nv_bfloat16* kp = suf(sidx, 0);
+        float acc4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
+        for (int c = 0; c < kD / 8; ++c) {
+          const uint4 qv = *reinterpret_cast<const uint4*>(smem + M::q + M::off(tid, c, kD / 8));
+          const uint4 kv = *reinterpret_cast<const uint4*>(kp + c * 8);
+          const uint32_t* qw = reinterpret_cast<const uint32_t*>(&qv);
+          const uint32_t* kw = reinterpret_cast<const uint32_t*>(&kv);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 qf = bf2f(qw[e]), kf = bf2f(kw[e]);
+            acc4[e] = fmaf(qf.x, kf.x, fmaf(qf.y, kf.y, acc4[e]));
+          }
+        }
+        xs[sidx] = ((acc4[0] + acc4[1]) + (acc4[2] + acc4[3])) * a.scale_log2;
+        mx = fmaxf(mx, xs[sidx]);
+      }
+    }
+    alpha = m_ref == -INFINITY ? 0.f : fast_ex2(m_ref - mx);  // mx is finite: key t always exists
+    ssum = l * alpha;
+#pragma unroll
+    for (int sidx = 0; sidx < kSufMax; ++sidx) {
+      psuf[sidx] = xs[sidx] == -INFINITY ? 0.f : fast_ex2(xs[sidx] - mx);
+      ssum += psuf[sidx];
+    }
+  }
+  const float inv = 1.f / ssum;
+  __nv_bfloat16* op = CAUSAL ? a.out + (int64_t(b) * a.L + pos) * a.so_row + int64_t(hq) * a.so_h
+                             : a.out + brow * a.so_row + int64_t(t) * a.so_t + int64_t(hq) * a.so_h;
+#pragma unroll 1
+  for (int piece = 0; piece < kD / 32; ++piece) {
+    uint32_t r[32];
+    tc::ld32(tO + piece * 32, r);  // whole warp (aligned), stores are per row below
+    tc::wait_ld();
+    if (!rvalid || nb == 0) continue;
+    float o[32];
+#pragma unroll
+    for (int c = 0; c < 32; ++c) o[c] = __uint_as_float(r[c]) * alpha;
+    if (!CAUSAL) {
+#pragma unroll
+      for (int sidx = 0; sidx < kSufMax; ++sidx) {
+        if (!(sidx < a.T && sidx <= t)) continue;
+        const __nv_bfloat16* vp = suf(sidx, 1) + piece * 32;
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const uint4 vv = *reinterpret_cast<const uint4*>(vp + q4 * 8);
+          const uint32_t* vw = reinterpret_cast<const uint32_t*>(&vv);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 vf = bf2f(vw[e]);
+            o[q4 * 8 + 2 * e] = fmaf(psuf[sidx], vf.x, o[q4 * 8 + 2 * e]);
+            o[q4 * 8 + 2 * e + 1] = fmaf(psuf[sidx], vf.y, o[q4 * 8 + 2 * e + 1]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int q4 = 0; q4 < 4; ++q4) {
+      uint4 res;
+      uint32_t* rw = reinterpret_cast<uint32_t*>(&res);
+      uint4 gv = make_uint4(0u, 0u, 0u, 0u);
+      const int c = piece * 4 + q4;
+      if (a.gate) gv = *reinterpret_cast<const uint4*>(smem + M::v + tid * 512 + ((c ^ (tid & 31)) * 16));
+      const uint32_t* gw = reinterpret_cast<const uint32_t*>(&gv);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float v0 = o[q4 * 8 + 2 * e] * inv, v1 = o[q4 * 8 + 2 * e + 1] * inv;
+        if (a.gate) {
+          const float2 gf = bf2f(gw[e]);
+          v0 = bf16r(v0) * bf16r(fast_rcp(1.f + fast_ex2(-1.4426950408889634f * gf.x)));
+          v1 = bf16r(v1) * bf16r(fast_rcp(1.f + fast_ex2(-1.4426950408889634f * gf.y)));
+        }
+        rw[e] = bf2_pack(v0, v1);
+      }
+      *reinterpret_cast<uint4*>(op + piece * 32 + q4 * 8) = res;
+    }
+  }
+  if (!ok && tid == 0) {  // a wait timed out: report, give in-flight copies a bounded time
+    atomicOr(a.status, 1u);
+    for (int s = 0; s < 2; ++s) {
+      if (issued_k[s] > 0) tc::mbar_wait(ldK + s, uint32_t(issued_k[s] - 1) & 1u, kWait);
+      if (issued_v[s] > 0) tc::mbar_wait(ldV + s, uint32_t(issued_v[s] - 1) & 1u, kWait);
+    }
+  }
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  if (warp == 0) tc::tmem_free(tmem, 512);
+}
+
+// [S][HK][L][D] (strides in elements: seq, pos, head) -> tiles [S*HK][nblk][kTile], zero past L.
+// Thread i writes 16-byte unit i of the destination (consecutive threads, consecutive bytes).
+__global__ void __launch_bounds__(256) kv_tile_kernel(const __nv_bfloat16* src, int64_t s_seq, int64_t s_pos,
+                                                      int64_t s_h, int HK, int L, int nblk, unsigned char* dst,
+                                                      int64_t units) {
+  const int64_t i = int64_t(blockIdx.x) * 256 + threadIdx.x;
+  if (i >= units) return;
+  constexpr int per_blk = kTile / 16;  // 2048 units: [8 key groups][32 dim chunks][8 keys]
+  const int64_t blk = i / per_blk;
+  const int u = int(i % per_blk);
+  const int kg = u >> 8, dc = (u >> 3) & 31, k8 = u & 7;
+  const int64_t sh = blk / nblk;
+  const int kb = int(blk % nblk);
+  const int64_t s = sh / HK;
+  const int h = int(sh % HK);
+  const int p = kb * kBlk + kg * 8 + k8;
+  uint4 v = make_uint4(0u, 0u, 0u, 0u);
+  if (p < L) v = *reinterpret_cast<const uint4*>(src + s * s_seq + int64_t(p) * s_pos + int64_t(h) * s_h + dc * 8);
+  reinterpret_cast<uint4*>(dst)[i] = v;
+}
+
+template <bool CAUSAL>
+int launch_attn_tc(const AttnTcArgs& a, cudaStream_t stream) {
+  auto kern = attn_tc_kernel<CAUSAL>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(AttnTcSmem::bytes)) != cudaSuccess) {
+    set_error("tiled attention: cannot reserve %zu bytes of shared memory", AttnTcSmem::bytes);
+    return KADLLM_ECUDA;
+  }
+  const int64_t R = CAUSAL ? int64_t(a.L) * a.G : int64_t(a.W) * a.T * a.G;
+  dim3 grid(unsigned((R + kRows - 1) / kRows), unsigned(a.B * a.HK));
+  kern<<<grid, kRows, AttnTcSmem::bytes, stream>>>(a);
+  KB_CHECK_LAUNCH("tiled attention launch");
+  return KADLLM_OK;
+}
+
+}  // namespace
+}  // namespace kb
+
+using namespace kb;
+
+extern "C" int64_t kadllm_kv_tile_bytes(int64_t seqs, int64_t kv_heads, int64_t length, int64_t head_dim) {
+  if (seqs < 1 || kv_heads < 1 || length < 1 || head_dim != kD) return -1;
+  return seqs * kv_heads * ((length + kBlk - 1) / kBlk) * int64_t(kTile);
+}
+
+extern "C" int kadllm_kv_tile(const void* src, int64_t s_seq, int64_t s_pos, int64_t s_head, int64_t seqs,
+                              int64_t kv_heads, int64_t length, int64_t head_dim, void* tiles, int64_t tile_bytes,
+                              void* stream) {
+  KB_REQUIRE(src && tiles, KADLLM_EINVAL, "kv_tile: null pointer");
+  KB_REQUIRE(head_dim == kD && seqs >= 1 && kv_heads >= 1 && length >= 1, KADLLM_EUNSUPPORTED,
+             "kv_tile: head_dim must be %d", kD);
+  KB_REQUIRE(s_seq % 8 == 0 && s_pos % 8 == 0 && s_head % 8 == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0 &&
+                 (reinterpret_cast<uintptr_t>(tiles) & 15) == 0,
+             KADLLM_EINVAL, "kv_tile: source rows must be 16-byte aligned");
+  const int64_t nblk = (length + kBlk - 1) / kBlk;
+  const int64_t bytes = seqs * kv_heads * nblk * kTile;
+  KB_REQUIRE(tile_bytes >= bytes, KADLLM_EINVAL, "kv_tile: tile buffer too small (%lld < %lld)", (long long)tile_bytes,
+             (long long)bytes);
+  const int64_t units = bytes / 16;
+  kv_tile_kernel<<<unsigned((units + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(src), s_seq, s_pos, s_head, int(kv_heads), int(length), int(nblk),
+      static_cast<unsigned char*>(tiles), units);
+  KB_CHECK_LAUNCH("kv_tile launch");
+  return KADLLM_OK;
+}
+
+extern "C" int kadllm_attention_tiled(const void* q, int64_t sq_row, int64_t sq_t, int64_t sq_h, const void* k_tiles,
+                                      const void* v_tiles, int64_t blocks_per_head, const void* suffix_k,
+                                      int64_t ssk_row, int64_t ssk_t, int64_t ssk_h, const void* suffix_v,
+                                      int64_t ssv_row, int64_t ssv_t, int64_t ssv_h, const void* gate, int64_t sg_row,
+                                      int64_t sg_t, int64_t sg_h, void* out, int64_t so_row, int64_t so_t,
+                                      int64_t so_h, uint32_t* status, int64_t batch, int64_t beam_width,
+                                      int64_t steps, int64_t q_heads, int64_t kv_heads, int64_t prefix_len,
+                                      int64_t head_dim, float scale, int causal, void* stream) {
+  KB_REQUIRE(q && k_tiles && v_tiles && out && status, KADLLM_EINVAL, "tiled attention: null pointer");
+  KB_REQUIRE(head_dim == kD, KADLLM_EUNSUPPORTED, "tiled attention: head_dim must be %d", kD);
+  KB_REQUIRE(batch >= 1 && q_heads >= 1 && kv_heads >= 1 && q_heads % kv_heads == 0 && prefix_len >= 1 &&
+                 blocks_per_head * kBlk >= prefix_len,
+             KADLLM_EINVAL, "tiled attention: bad dimensions");
+  if (!causal)
+    KB_REQUIRE(suffix_k && suffix_v && beam_width >= 1 && steps >= 1 && steps <= kSufMax, KADLLM_EINVAL,
+               "tiled attention: decode needs suffix keys / values and 1 <= steps <= %d", kSufMax);
+  const auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  KB_REQUIRE(al16(q) && al16(k_tiles) && al16(v_tiles) && al16(out) && (!suffix_k || al16(suffix_k)) &&
+                 (!suffix_v || al16(suffix_v)) && (!gate || al16(gate)) && sq_row % 8 == 0 && sq_t % 8 == 0 &&
+                 sq_h % 8 == 0 && so_row % 8 == 0 && so_t % 8 == 0 && so_h % 8 == 0 && ssk_row % 8 == 0 &&
+                 ssk_t % 8 == 0 && ssk_h % 8 == 0 && ssv_row % 8 == 0 && ssv_t % 8 == 0 && ssv_h % 8 == 0 &&
+                 sg_row % 8 == 0 && sg_t % 8 == 0 && sg_h % 8 == 0,
+             KADLLM_EINVAL, "tiled attention: operands and strides must be 16-byte aligned");
+  const int64_t R = causal ? prefix_len * (q_heads / kv_heads) : beam_width * steps * (q_heads / kv_heads);
+  KB_REQUIRE(R < (int64_t(1) << 30) && batch * kv_heads <= 65535, KADLLM_EINVAL, "tiled attention: too many rows");
+  AttnTcArgs a{};
+  a.q = static_cast<const __nv_bfloat16*>(q); a.sq_row = sq_row; a.sq_t = sq_t; a.sq_h = sq_h;
+  a.kt = static_cast<const unsigned char*>(k_tiles); a.vt = static_cast<const unsigned char*>(v_tiles);
+  a.nblk = int(blocks_per_head);
+  a.sk = static_cast<const __nv_bfloat16*>(suffix_k); a.ssk_row = ssk_row; a.ssk_t = ssk_t; a.ssk_h = ssk_h;
+  a.sv = static_cast<const __nv_bfloat16*>(suffix_v); a.ssv_row = ssv_row; a.ssv_t = ssv_t; a.ssv_h = ssv_h;
+  a.gate = static_cast<const __nv_bfloat16*>(gate); a.sg_row = sg_row; a.sg_t = sg_t; a.sg_h = sg_h;
+  a.out = static_cast<__nv_bfloat16*>(out); a.so_row = so_row; a.so_t = so_t; a.so_h = so_h;
+  a.status = status;
+  a.B = int(batch); a.W = int(causal ? 1 : beam_width); a.T = int(causal ? 1 : steps); a.H = int(q_heads);
+  a.HK = int(kv_heads); a.G = int(q_heads / kv_heads); a.L = int(prefix_len);
+  a.scale_log2 = (scale > 0.f ? scale : 1.0f / sqrtf(float(head_dim))) * 1.4426950408889634f;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return causal ? launch_attn_tc<true>(a, s) : launch_attn_tc<false>(a, s);
+}

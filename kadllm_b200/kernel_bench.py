@@ -7,7 +7,8 @@ Cases (BASELINE config 5 and the GRBeam step shapes):
            gated norm) from the packed projection: B=32, T=1024, 16 heads of 128
   conv     causal conv1d width 4 + SiLU over T=1024, 2048 channels (B=32)
   attn     shared-prefix decode attention: 256 beams x 8 q / 2 kv heads x d=256
-           against a 4096-token prefix plus a 3-token causal suffix
+           against a 4096-token prefix plus a 3-token causal suffix (attn_tiled:
+           the tcgen05 kernel over the tiled prefix)
   mixer    fused GDN decode mixer: 32 requests x 256 beams, T = 1 and 2
   select   one selection step over 32 x 256 x 248320 bf16 logits
 Each prints one JSON line: device time per call (CUDA events, after warm-up),
@@ -95,6 +96,33 @@ def case_attn(gen, reps):
     return ms, "tensor", 4 * B * W * T * Hq * D * L + 4 * B * W * Hq * D * T * (T + 1) / 2
 
 
+def case_attn_tiled(gen, reps):
+    dev, bf = torch.device("cuda"), torch.bfloat16
+    B, W, T, L, Hq, HK, D = 1, 256, 3, 4096, 8, 2, 256
+    n = lambda *s: torch.randn(*s, device=dev, generator=gen).to(bf)
+    q, sk, sv, gate = n(B * W, T, Hq, D), n(B * W, T, HK, D), n(B * W, T, HK, D), n(B * W, T, Hq, D)
+    kc, vc = n(B, HK, L, D), n(B, HK, L, D)
+    nbytes = _lib.lib().kadllm_kv_tile_bytes(B, HK, L, D)
+    kt = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    vt = torch.empty_like(kt)
+    s = _lib.stream(dev)
+    _lib.call("kadllm_kv_tile", kc.data_ptr(), HK * L * D, D, L * D, B, HK, L, D, kt.data_ptr(), nbytes, s)
+    _lib.call("kadllm_kv_tile", vc.data_ptr(), HK * L * D, D, L * D, B, HK, L, D, vt.data_ptr(), nbytes, s)
+    out = torch.empty(B * W, T, Hq, D, dtype=bf, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def run():
+        _lib.call("kadllm_attention_tiled", q.data_ptr(), T * Hq * D, Hq * D, D, kt.data_ptr(), vt.data_ptr(),
+                  L // 64, sk.data_ptr(), T * HK * D, HK * D, D, sv.data_ptr(), T * HK * D, HK * D, D,
+                  gate.data_ptr(), T * Hq * D, Hq * D, D, out.data_ptr(), T * Hq * D, Hq * D, D,
+                  status.data_ptr(), B, W, T, Hq, HK, L, D, D ** -0.5, 0, s)
+
+    ms = _time(run, reps)
+    if int(status.item()):
+        raise RuntimeError("tiled attention reported a timed-out wait")
+    return ms, "tensor", 4 * B * W * T * Hq * D * L + 4 * B * W * Hq * D * T * (T + 1) / 2
+
+
 def case_mixer(gen, reps, T=1):
     dev, bf = torch.device("cuda"), torch.bfloat16
     B, W, H, HV, K = 32, 256, 16, 16, 128
@@ -132,7 +160,7 @@ def case_select(gen, reps):
     return ms, "hbm", B * Wp * V * 2
 
 
-CASES = {"prefill": case_prefill, "conv": case_conv, "attn": case_attn, "mixer": case_mixer,
+CASES = {"prefill": case_prefill, "attn_tiled": case_attn_tiled, "conv": case_conv, "attn": case_attn, "mixer": case_mixer,
          "mixer2": lambda g, r: case_mixer(g, r, T=2), "select": case_select}
 
 

@@ -59,6 +59,9 @@ class Layer:
     w_down: torch.Tensor    # [H, I]
 
 
+TILED_HEAD_DIM = 256  # head dim of the tensor-core attention kernels
+
+
 @dataclass(frozen=True)
 class HybridPrefix:
     """Immutable request-sized prefix (``Qwen35Prefix``, ``src/kadllm/adapters/qwen3_5.py:21-26``).
@@ -72,6 +75,8 @@ class HybridPrefix:
     batch: int
     owner: object
     layers: tuple
+    # attention layers: (K tiles, V tiles, blocks per head) for the tensor-core kernels, else None
+    tiles: tuple = ()
 
 
 class HybridModel:
@@ -125,6 +130,27 @@ class HybridModel:
         self._rope_len = 0
         self._cos = self._sin = None
         self.owner = object()
+        # device status word of the tensor-core kernels (bit 0: a bounded wait timed out)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def check(self) -> None:
+        """Raise if a tensor-core kernel reported a timed-out wait (synchronises)."""
+        st = int(self.status.item())
+        if st:
+            raise RuntimeError(f"kadllm_b200: device status {st:#x} (a tensor-core pipeline wait timed out)")
+
+    def _tile_kv(self, kc, vc, strides):
+        """[B, HK, L, D] caches -> the tiled K / V images the tensor-core attention stages."""
+        B, hk, L, D = kc.shape
+        nbytes = _lib.lib().kadllm_kv_tile_bytes(B, hk, L, D)
+        if nbytes <= 0:
+            return None
+        kt = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        vt = torch.empty_like(kt)
+        s = self._stream()
+        _lib.call("kadllm_kv_tile", kc.data_ptr(), *strides, B, hk, L, D, kt.data_ptr(), nbytes, s)
+        _lib.call("kadllm_kv_tile", vc.data_ptr(), *strides, B, hk, L, D, vt.data_ptr(), nbytes, s)
+        return kt, vt, -(-L // 64)
 
     # ------------------------------------------------------------------ helpers
     def _stream(self):
@@ -190,6 +216,7 @@ class HybridModel:
         x, normed = self._embed(ids.reshape(-1))
         s = self._stream()
         prefix = []
+        tiles = []
         hk, D, hq = c.num_key_value_heads, c.head_dim, c.num_attention_heads
         ws = None  # GDN prefill workspace (chunk blocks), shared by the GDN layers
         for i, layer in enumerate(self.layers):
@@ -211,6 +238,7 @@ class HybridModel:
                           c.linear_value_head_dim, s)
                 delta = F.linear(out, m.w_out)
                 prefix.append((conv_state, rec))
+                tiles.append(None)
             else:
                 q = torch.empty(R, hq, D, dtype=BF16, device=self.device)
                 kc = torch.empty(B, hk, L, D, dtype=BF16, device=self.device)
@@ -219,13 +247,22 @@ class HybridModel:
                 self._qk_rope(P, R, 0, L, q, kc, cache_strides, vc, cache_strides, m)
                 out = torch.empty(R, hq * D, dtype=BF16, device=self.device)
                 gate = P[:, D:]  # gate of head h at column h*2D + D
-                # cache [B, HK, L, D]: strides passed as (request, position, head)
-                _lib.call("kadllm_causal_attention", q.data_ptr(), hq * D, D, kc.data_ptr(), kc.stride(0),
-                          kc.stride(2), kc.stride(1), vc.data_ptr(), vc.stride(0), vc.stride(2), vc.stride(1),
-                          gate.data_ptr(), P.stride(0), 2 * D, out.data_ptr(),
-                          out.stride(0), D, B, L, hq, hk, D, D ** -0.5, s)
+                tile = self._tile_kv(kc, vc, cache_strides) if D == TILED_HEAD_DIM else None
+                if tile is not None:  # tensor-core kernel over the tiled prefix
+                    kt, vt, nblk = tile
+                    _lib.call("kadllm_attention_tiled", q.data_ptr(), hq * D, 0, D, kt.data_ptr(), vt.data_ptr(),
+                              nblk, None, 0, 0, 0, None, 0, 0, 0, gate.data_ptr(), P.stride(0), 0, 2 * D,
+                              out.data_ptr(), out.stride(0), 0, D, self.status.data_ptr(), B, 1, 1, hq, hk, L, D,
+                              D ** -0.5, 1, s)
+                else:
+                    # cache [B, HK, L, D]: strides passed as (request, position, head)
+                    _lib.call("kadllm_causal_attention", q.data_ptr(), hq * D, D, kc.data_ptr(), kc.stride(0),
+                              kc.stride(2), kc.stride(1), vc.data_ptr(), vc.stride(0), vc.stride(2), vc.stride(1),
+                              gate.data_ptr(), P.stride(0), 2 * D, out.data_ptr(),
+                              out.stride(0), D, B, L, hq, hk, D, D ** -0.5, s)
                 delta = F.linear(out, m.w_o)
                 prefix.append((kc.transpose(1, 2), vc.transpose(1, 2)))
+                tiles.append(tile)
             self._add_norm(x, delta, layer.post_ln, normed)
             delta = self._mlp(layer, normed)
             if i + 1 < len(self.layers):
@@ -233,7 +270,7 @@ class HybridModel:
         last = torch.empty(B, c.hidden_size, dtype=BF16, device=self.device)
         self._add_norm(x, delta, self.final_norm, last, rows=B, step=L, offset=L - 1)
         logits = F.linear(last, self.lm_head)
-        return logits, HybridPrefix(L, B, self.owner, tuple(prefix))
+        return logits, HybridPrefix(L, B, self.owner, tuple(prefix), tuple(tiles))
 
     # ------------------------------------------------------------------ decode
     @torch.no_grad()
@@ -267,11 +304,19 @@ class HybridModel:
                 pk, pv = cached  # [B, L, HK, D] views
                 out = torch.empty(R, hq * D, dtype=BF16, device=self.device)
                 gate = P[:, D:]
-                _lib.call("kadllm_prefix_attention", q.data_ptr(), T * hq * D, hq * D, D, pk.data_ptr(),
-                          *pk.stride()[:3], pv.data_ptr(), *pv.stride()[:3], ks.data_ptr(), *suffix_strides,
-                          vs.data_ptr(), *suffix_strides, None, gate.data_ptr(), T * P.stride(0), P.stride(0), 2 * D,
-                          out.data_ptr(), T * hq * D, hq * D, D, _lib.DTYPE_CODES[BF16], B, W, T, hq, hk,
-                          state.length, D, D ** -0.5, s)
+                tile = state.tiles[i] if i < len(state.tiles) else None
+                if tile is not None:
+                    kt, vt, nblk = tile
+                    _lib.call("kadllm_attention_tiled", q.data_ptr(), T * hq * D, hq * D, D, kt.data_ptr(),
+                              vt.data_ptr(), nblk, ks.data_ptr(), *suffix_strides, vs.data_ptr(), *suffix_strides,
+                              gate.data_ptr(), T * P.stride(0), P.stride(0), 2 * D, out.data_ptr(), T * hq * D,
+                              hq * D, D, self.status.data_ptr(), B, W, T, hq, hk, state.length, D, D ** -0.5, 0, s)
+                else:
+                    _lib.call("kadllm_prefix_attention", q.data_ptr(), T * hq * D, hq * D, D, pk.data_ptr(),
+                              *pk.stride()[:3], pv.data_ptr(), *pv.stride()[:3], ks.data_ptr(), *suffix_strides,
+                              vs.data_ptr(), *suffix_strides, None, gate.data_ptr(), T * P.stride(0), P.stride(0),
+                              2 * D, out.data_ptr(), T * hq * D, hq * D, D, _lib.DTYPE_CODES[BF16], B, W, T, hq, hk,
+                              state.length, D, D ** -0.5, s)
                 delta = F.linear(out, m.w_o)
             self._add_norm(x, delta, layer.post_ln, normed)
             delta = self._mlp(layer, normed)
