@@ -29,6 +29,7 @@
 // b / a columns (src/kadllm/adapters/qwen3_5.py:290-298), and the output goes
 // through Qwen3_5RMSNormGated with z (transformers modeling_qwen3_5.py:175-190).
 #include "common.cuh"
+#include "gdn_mixer.cuh"
 
 namespace kb {
 namespace {
@@ -491,5 +492,14 @@ extern "C" int kadllm_gdn_mixer_replay(const void* proj, int64_t ld_proj, const 
   a.out = out; a.out_dtype = KADLLM_BF16;
   a.B = int(batch); a.W = int(beam_width); a.T = int(steps); a.H = int(heads); a.HV = int(v_heads);
   a.scale = 1.0f / sqrtf(float(k_dim));
+  if (k_dim == v_dim) {
+    MixerArgs m{};
+    m.proj = a.proj; m.ld_proj = ld_proj; m.conv_state = a.conv_state; m.conv_hist = conv_hist;
+    m.conv_weight = a.conv_weight; m.state = static_cast<const __nv_bfloat16*>(rec_state);
+    m.a_log = a_log; m.dt_bias = dt_bias; m.norm_weight = norm_weight; m.norm_eps = norm_eps;
+    m.out = static_cast<__nv_bfloat16*>(out);
+    m.B = a.B; m.W = a.W; m.T = a.T; m.H = a.H; m.HV = a.HV; m.D = int(k_dim); m.scale = a.scale;
+    if (gdn_mixer_staged_ok(m)) return gdn_mixer_staged(m, static_cast<cudaStream_t>(stream));
+  }
   return dispatch_gdn<true>(int(k_dim), int(v_dim), a, static_cast<cudaStream_t>(stream));
 }

@@ -1,6 +1,6 @@
 """Kernel microbenchmarks at the BASELINE shapes (seeded synthetic inputs).
 
-    python -m kadllm_b200.kernel_bench --case prefill|conv|attn|mixer|select [--reps N]
+    python -m kadllm_b200.kernel_bench --case CASE [--reps N]
 
 Cases (BASELINE config 5 and the GRBeam step shapes):
   prefill  chunked gated-delta prefill (conv + gates + UT transform + scan +
@@ -8,7 +8,9 @@ Cases (BASELINE config 5 and the GRBeam step shapes):
   conv     causal conv1d width 4 + SiLU over T=1024, 2048 channels (B=32)
   attn     shared-prefix decode attention: 256 beams x 8 q / 2 kv heads x d=256
            against a 4096-token prefix plus a 3-token causal suffix (attn_tiled:
-           the tcgen05 kernel over the tiled prefix)
+           the tcgen05 kernel over the tiled prefix; attn_step: the GRBeam
+           step's second decode, 32 requests x 256 beams, prefix 1024, T=2;
+           attn_causal: the prefill's causal attention, 32 x 1024 tokens)
   mixer    fused GDN decode mixer: 32 requests x 256 beams, T = 1 and 2
   select   one selection step over 32 x 256 x 248320 bf16 logits
 Each prints one JSON line: device time per call (CUDA events, after warm-up),
@@ -96,11 +98,13 @@ def case_attn(gen, reps):
     return ms, "tensor", 4 * B * W * T * Hq * D * L + 4 * B * W * Hq * D * T * (T + 1) / 2
 
 
-def case_attn_tiled(gen, reps):
+def case_attn_tiled(gen, reps, B=1, W=256, T=3, L=4096, causal=False):
     dev, bf = torch.device("cuda"), torch.bfloat16
-    B, W, T, L, Hq, HK, D = 1, 256, 3, 4096, 8, 2, 256
+    Hq, HK, D = 8, 2, 256
     n = lambda *s: torch.randn(*s, device=dev, generator=gen).to(bf)
-    q, sk, sv, gate = n(B * W, T, Hq, D), n(B * W, T, HK, D), n(B * W, T, HK, D), n(B * W, T, Hq, D)
+    R = B * L if causal else B * W  # causal: one query row per prefix token
+    q, gate = n(R, T, Hq, D), n(R, T, Hq, D)
+    sk, sv = n(B * W, T, HK, D), n(B * W, T, HK, D)
     kc, vc = n(B, HK, L, D), n(B, HK, L, D)
     nbytes = _lib.lib().kadllm_kv_tile_bytes(B, HK, L, D)
     kt = torch.empty(nbytes, dtype=torch.uint8, device=dev)
@@ -108,18 +112,26 @@ def case_attn_tiled(gen, reps):
     s = _lib.stream(dev)
     _lib.call("kadllm_kv_tile", kc.data_ptr(), HK * L * D, D, L * D, B, HK, L, D, kt.data_ptr(), nbytes, s)
     _lib.call("kadllm_kv_tile", vc.data_ptr(), HK * L * D, D, L * D, B, HK, L, D, vt.data_ptr(), nbytes, s)
-    out = torch.empty(B * W, T, Hq, D, dtype=bf, device=dev)
+    out = torch.empty(R, T, Hq, D, dtype=bf, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
+    nblk = -(-L // 64)
 
     def run():
-        _lib.call("kadllm_attention_tiled", q.data_ptr(), T * Hq * D, Hq * D, D, kt.data_ptr(), vt.data_ptr(),
-                  L // 64, sk.data_ptr(), T * HK * D, HK * D, D, sv.data_ptr(), T * HK * D, HK * D, D,
-                  gate.data_ptr(), T * Hq * D, Hq * D, D, out.data_ptr(), T * Hq * D, Hq * D, D,
-                  status.data_ptr(), B, W, T, Hq, HK, L, D, D ** -0.5, 0, s)
+        if causal:
+            _lib.call("kadllm_attention_tiled", q.data_ptr(), Hq * D, 0, D, kt.data_ptr(), vt.data_ptr(), nblk,
+                      None, 0, 0, 0, None, 0, 0, 0, gate.data_ptr(), Hq * D, 0, D, out.data_ptr(), Hq * D, 0, D,
+                      status.data_ptr(), B, 1, 1, Hq, HK, L, D, D ** -0.5, 1, s)
+        else:
+            _lib.call("kadllm_attention_tiled", q.data_ptr(), T * Hq * D, Hq * D, D, kt.data_ptr(), vt.data_ptr(),
+                      nblk, sk.data_ptr(), T * HK * D, HK * D, D, sv.data_ptr(), T * HK * D, HK * D, D,
+                      gate.data_ptr(), T * Hq * D, Hq * D, D, out.data_ptr(), T * Hq * D, Hq * D, D,
+                      status.data_ptr(), B, W, T, Hq, HK, L, D, D ** -0.5, 0, s)
 
     ms = _time(run, reps)
     if int(status.item()):
         raise RuntimeError("tiled attention reported a timed-out wait")
+    if causal:
+        return ms, "tensor", 4 * B * Hq * D * L * (L + 1) / 2
     return ms, "tensor", 4 * B * W * T * Hq * D * L + 4 * B * W * Hq * D * T * (T + 1) / 2
 
 
@@ -161,7 +173,9 @@ def case_select(gen, reps):
 
 
 CASES = {"prefill": case_prefill, "attn_tiled": case_attn_tiled, "conv": case_conv, "attn": case_attn, "mixer": case_mixer,
-         "mixer2": lambda g, r: case_mixer(g, r, T=2), "select": case_select}
+         "mixer2": lambda g, r: case_mixer(g, r, T=2), "select": case_select,
+         "attn_step": lambda g, r: case_attn_tiled(g, r, B=32, W=256, T=2, L=1024),
+         "attn_causal": lambda g, r: case_attn_tiled(g, r, B=32, W=1, T=1, L=1024, causal=True)}
 
 
 def main() -> None:

@@ -140,11 +140,21 @@ def test_operator_errors_match_reference_conventions():
 @pytest.mark.parametrize("T", [1, 2, 3])
 def test_gdn_mixer_matches_oracle_composition(T, K, H, HV):
     """Fused conv + gates + replay + gated RMSNorm against the oracle's op chain
-    (W = 33: a ragged last beam block; the 0.8B head shape is K = 128, HV = 16)."""
+    (W = 33: a ragged last beam octet; the 0.8B head shape is K = 128, HV = 16)."""
+    _mixer_case(T, K, H, HV, 2, 33)
+
+
+@pytest.mark.parametrize("T", [1, 2])
+def test_gdn_mixer_many_octets_per_warp(T):
+    """160 (request, head) pairs x 250 beams: each warp of the staged kernel runs
+    several beam octets through its double-buffered staging, the last one ragged."""
+    _mixer_case(T, 128, 4, 16, 10, 250)
+
+
+def _mixer_case(T, K, H, HV, B, W):
     from kadllm_b200 import _lib
 
-    rng = np.random.default_rng(10 + T + K + HV)
-    B, W = 2, 33
+    rng = np.random.default_rng(10 + T + K + HV + W)
     kd, vd = H * K, HV * K
     C = 2 * kd + vd
     ld = C + vd + 2 * HV + 8
