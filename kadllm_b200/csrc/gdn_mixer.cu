@@ -12,12 +12,18 @@
 //     d_t = beta_t (v_t - that),   o_t = A_t S0^T q_t + [t=1] a_1 (k_0.q_1) d_0 + d_t (k_t.q_t)
 // so the only D x D work is [q_t ; k_t] x S0 on the tensor cores.
 //
-// Data movement: each warp owns beam octets and stages one octet's projection
-// slices (the q, k, v, z head slices and the two gate words of all T tokens)
-// in shared memory with 16-byte cp.async copies, one octet ahead of the octet
-// it computes.  S0 is staged once per CTA with an XOR swizzle that keeps the
-// ldmatrix reads conflict-free.  The output tile goes back through the staged
-// q slice and leaves as 16-byte stores.
+// Work unit: an "octet" of 8 rows (beam, token): 8 beams for T = 1, 4 beams x
+// 2 tokens for T = 2 (row r = token r / 4, beam r % 4), one row per MMA row g.
+// A step-1 row takes k_0, d_0 and the decay of its beam's step-0 row from the
+// partner lane (lane ^ 16), so both token counts run the same code and the
+// same shared-memory footprint (two CTAs per SM).
+//
+// Data movement: each warp owns a run of octets and stages an octet's
+// projection slices (the q, k, v, z head slices and the two gate words of each
+// row) in shared memory with 16-byte cp.async copies, one octet ahead of the
+// octet it computes.  S0 is staged once per CTA with an XOR swizzle that keeps
+// the ldmatrix reads conflict-free.  The output tile goes back through the
+// staged q slice and leaves as 16-byte stores.
 //
 // Operand order: the m16n8k16 A fragment of thread (g, tq) holds k columns
 // {2tq, 2tq+1, 2tq+8, 2tq+9} of a k16 step.  The contraction order is free, so
@@ -40,8 +46,8 @@ struct MixLayout {
   static constexpr int S0B = D * D * 2;     // swizzled bf16 state
   static constexpr int TABB = 8 * NCH * 4;  // conv table [8][NCH] fp32
   static constexpr int NWB = D * 4;         // norm weight fp32
-  __host__ __device__ static constexpr int octet_bytes(int T) { return T * 8 * ROWB; }
-  static size_t smem(int T) { return size_t(S0B) + TABB + NWB + size_t(kMixWarps) * 2 * octet_bytes(T); }
+  static constexpr int OCTB = 8 * ROWB;     // one staged octet: 8 (beam, token) rows
+  static constexpr size_t SMEM = size_t(S0B) + TABB + NWB + size_t(kMixWarps) * 2 * OCTB;
 };
 
 // 16-byte chunk swizzle of state row r: distinct over the 8 rows that one
@@ -62,44 +68,43 @@ __device__ __forceinline__ float2 lo2(float4 v) { return make_float2(v.x, v.y); 
 __device__ __forceinline__ float2 hi2(float4 v) { return make_float2(v.z, v.w); }
 
 // Conv + SiLU of 8 consecutive local channels lc (a multiple of 8) at suffix
-// step t, rounded to bf16 pairs.  Conv table rows: 0..2 prefix-tap partial
-// sums c_t, 3..6 the taps w0..w3; raw input x_s is at byte `xoff` of staged row
-// (s, g) (`row0` = row (0, g), rows of one token are 8 * ROWB apart).
-template <int NCH, int ROWB>
-__device__ __forceinline__ void conv8_silu(const float* tab, int lc, int t, const unsigned char* row0, int xoff,
-                                           uint32_t out[4]) {
+// step t in {0, 1}, rounded to bf16 pairs:
+//     conv_t = c_t + w3 x_t + [t = 1] w2 x_0
+// (conv table rows 0..2: prefix-tap partial sums c_t, rows 3..6: taps w0..w3).
+// `xt` / `x0` point at the raw bf16 inputs of steps t and 0 (equal when t = 0).
+template <int NCH>
+__device__ __forceinline__ void conv8_silu(const float* tab, int lc, int t, const unsigned char* xt,
+                                           const unsigned char* x0, uint32_t out[4]) {
+  const float4 c0 = *reinterpret_cast<const float4*>(tab + t * NCH + lc);
+  const float4 c1 = *reinterpret_cast<const float4*>(tab + t * NCH + lc + 4);
+  const float4 w30 = *reinterpret_cast<const float4*>(tab + 6 * NCH + lc);
+  const float4 w31 = *reinterpret_cast<const float4*>(tab + 6 * NCH + lc + 4);
+  const uint4 x = *reinterpret_cast<const uint4*>(xt);
   float2 acc[4];
-  if (t < 3) {
-    const float4 c0 = *reinterpret_cast<const float4*>(tab + t * NCH + lc);
-    const float4 c1 = *reinterpret_cast<const float4*>(tab + t * NCH + lc + 4);
-    acc[0] = lo2(c0); acc[1] = hi2(c0); acc[2] = lo2(c1); acc[3] = hi2(c1);
-  } else {
-#pragma unroll
-    for (int p = 0; p < 4; ++p) acc[p] = make_float2(0.f, 0.f);
-  }
-#pragma unroll
-  for (int s = (t > 3 ? t - 3 : 0); s <= t; ++s) {
-    const uint4 x = *reinterpret_cast<const uint4*>(row0 + s * 8 * ROWB + xoff);
-    const float* w = tab + (6 - (t - s)) * NCH + lc;
-    const float4 w0 = *reinterpret_cast<const float4*>(w), w1 = *reinterpret_cast<const float4*>(w + 4);
-    acc[0] = fma2(lo2(w0), bf2f(x.x), acc[0]);
-    acc[1] = fma2(hi2(w0), bf2f(x.y), acc[1]);
-    acc[2] = fma2(lo2(w1), bf2f(x.z), acc[2]);
-    acc[3] = fma2(hi2(w1), bf2f(x.w), acc[3]);
+  acc[0] = fma2(lo2(w30), bf2f(x.x), lo2(c0));
+  acc[1] = fma2(hi2(w30), bf2f(x.y), hi2(c0));
+  acc[2] = fma2(lo2(w31), bf2f(x.z), lo2(c1));
+  acc[3] = fma2(hi2(w31), bf2f(x.w), hi2(c1));
+  if (t) {  // lanes of step-1 rows; the step-0 lanes of the warp skip it
+    const float4 w20 = *reinterpret_cast<const float4*>(tab + 5 * NCH + lc);
+    const float4 w21 = *reinterpret_cast<const float4*>(tab + 5 * NCH + lc + 4);
+    const uint4 y = *reinterpret_cast<const uint4*>(x0);
+    acc[0] = fma2(lo2(w20), bf2f(y.x), acc[0]);
+    acc[1] = fma2(hi2(w20), bf2f(y.y), acc[1]);
+    acc[2] = fma2(lo2(w21), bf2f(y.z), acc[2]);
+    acc[3] = fma2(hi2(w21), bf2f(y.w), acc[3]);
   }
 #pragma unroll
   for (int p = 0; p < 4; ++p) out[p] = bf2_pack_f2(silu2(acc[p]));
 }
 
 // Same for one channel pair (lc even), returned as the exact bf16 values.
-template <int NCH, int ROWB>
-__device__ __forceinline__ float2 conv2_silu(const float* tab, int lc, int t, const unsigned char* row0, int xoff) {
-  float2 acc = t < 3 ? *reinterpret_cast<const float2*>(tab + t * NCH + lc) : make_float2(0.f, 0.f);
-#pragma unroll
-  for (int s = (t > 3 ? t - 3 : 0); s <= t; ++s) {
-    const uint32_t x = *reinterpret_cast<const uint32_t*>(row0 + s * 8 * ROWB + xoff);
-    acc = fma2(*reinterpret_cast<const float2*>(tab + (6 - (t - s)) * NCH + lc), bf2f(x), acc);
-  }
+template <int NCH>
+__device__ __forceinline__ float2 conv2_silu(const float* tab, int lc, int t, const unsigned char* xt,
+                                             const unsigned char* x0) {
+  float2 acc = fma2(*reinterpret_cast<const float2*>(tab + 6 * NCH + lc), bf2f(*reinterpret_cast<const uint32_t*>(xt)),
+                    *reinterpret_cast<const float2*>(tab + t * NCH + lc));
+  if (t) acc = fma2(*reinterpret_cast<const float2*>(tab + 5 * NCH + lc), bf2f(*reinterpret_cast<const uint32_t*>(x0)), acc);
   return bf2f(bf2_pack_f2(silu2(acc)));
 }
 
@@ -122,50 +127,49 @@ __device__ __forceinline__ float chunk_dot(const uint32_t (&x)[KM][4], const uin
 template <int D, int TMAX>
 __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerArgs a, int octets_per_warp) {
   using L = MixLayout<D>;
-  constexpr int CH = L::CH, NCH = L::NCH, ROWB = L::ROWB;
-  constexpr int NT = D / 8;   // n8 tiles of the V columns
-  constexpr int NH = NT / 2;  // n8 tiles per half (bounds the accumulator registers)
-  constexpr int KM = D / 32;  // 16-byte chunks per thread per head row (= k16 step pairs)
+  constexpr int CH = L::CH, NCH = L::NCH, ROWB = L::ROWB, OCTB = L::OCTB;
+  constexpr int NT = D / 8;      // n8 tiles of the V columns
+  constexpr int NH = NT / 2;     // n8 tiles per half (bounds the accumulator registers)
+  constexpr int KM = D / 32;     // 16-byte chunks per thread per head row (= k16 step pairs)
+  constexpr int BPO = 8 / TMAX;  // beams per octet; staged row r = (token r / BPO, beam r % BPO)
   extern __shared__ __align__(16) unsigned char smem[];
   unsigned char* sS0 = smem;
   float* sTab = reinterpret_cast<float*>(smem + L::S0B);
   float* sNw = sTab + 8 * NCH;
   unsigned char* sStage = smem + L::S0B + L::TABB + L::NWB;
 
-  const int T = a.T;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, tq = lane & 3;
+  const int tg = g / BPO;  // this thread's row: suffix step tg of beam g % BPO
   const int HV = a.HV;
   const int b = blockIdx.x / HV, hv = blockIdx.x % HV;
   const int h = hv / (HV / a.H);
   const int key_dim = a.H * D;
   const int conv_dim = 2 * key_dim + HV * D;
   const int64_t ld = a.ld_proj;
-  const int octets = (a.W + 7) / 8;
+  const int octets = (a.W + BPO - 1) / BPO;
   const int oct0 = (blockIdx.y * kMixWarps + warp) * octets_per_warp;
   const int noct = max(0, min(octets_per_warp, octets - oct0));
-  const int obytes = L::octet_bytes(T);
-  unsigned char* wbuf = sStage + warp * 2 * obytes;
+  unsigned char* wbuf = sStage + warp * 2 * OCTB;
   // projection columns of the staged slices: q, k, v, z head slices; b and a gate words (aligned down)
   const int col_q = h * D, col_k = key_dim + h * D, col_v = 2 * key_dim + hv * D, col_z = conv_dim + hv * D;
   const int col_b = conv_dim + HV * D + hv, col_a = conv_dim + HV * D + HV + hv;
 
-  // Stage octet `oct` (all T tokens of its 8 beams) into `buf` (one cp.async group per call site).
+  // Stage octet `oct` into `buf` (the caller commits the cp.async group).
   auto stage = [&](int oct, unsigned char* buf) {
-    const int rows = T * 8;
-    for (int idx = lane; idx < rows * 4 * CH; idx += 32) {
+    for (int idx = lane; idx < 8 * 4 * CH; idx += 32) {
       const int r = idx / (4 * CH), piece = (idx / CH) & 3, c = idx % CH;
-      const int beam = oct * 8 + (r & 7);
+      const int beam = oct * BPO + r % BPO;
       const bool ok = beam < a.W;
-      const int64_t prow = (int64_t(b) * a.W + (ok ? beam : 0)) * T + (r >> 3);
+      const int64_t prow = (int64_t(b) * a.W + (ok ? beam : 0)) * TMAX + r / BPO;
       const int col = piece < 2 ? (piece == 0 ? col_q : col_k) : (piece == 2 ? col_v : col_z);
       cp16z(buf + r * ROWB + piece * 2 * D + c * 16, a.proj + prow * ld + col + c * 8, ok);
     }
-    if (lane < rows * 2) {
+    if (lane < 16) {
       const int r = lane >> 1, which = lane & 1;
-      const int beam = oct * 8 + (r & 7);
+      const int beam = oct * BPO + r % BPO;
       const bool ok = beam < a.W;
-      const int64_t prow = (int64_t(b) * a.W + (ok ? beam : 0)) * T + (r >> 3);
+      const int64_t prow = (int64_t(b) * a.W + (ok ? beam : 0)) * TMAX + r / BPO;
       cp4z(buf + r * ROWB + 8 * D + which * 4, a.proj + prow * ld + ((which ? col_a : col_b) & ~1), ok);
     }
   };
@@ -215,144 +219,143 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
   }
 
   for (int it = 0; it < noct; ++it) {
-    unsigned char* buf = wbuf + (it & 1) * obytes;
-    if (it + 1 < noct) stage(oct0 + it + 1, wbuf + ((it + 1) & 1) * obytes);
+    unsigned char* buf = wbuf + (it & 1) * OCTB;
+    if (it + 1 < noct) stage(oct0 + it + 1, wbuf + ((it + 1) & 1) * OCTB);
     cp_async_commit();
     cp_async_wait<1>();
     __syncwarp();
 
-    const unsigned char* row0 = buf + g * ROWB;  // staged row (t = 0, beam g)
+    unsigned char* rowg = buf + g * ROWB;                                   // this thread's row
+    const unsigned char* row0 = tg ? rowg - BPO * ROWB : rowg;              // the same beam's step 0
 
-    // ---- q_t, k_t (conv + SiLU, bf16), their norms, the gates ----------------------
-    uint32_t qw[TMAX][KM][4], kw[TMAX][KM][4];
-    float iq[TMAX], ik[TMAX], bt[TMAX], at[TMAX];
+    // ---- q, k of this row (conv + SiLU, bf16), norms, gates, dot products --------------
+    uint32_t qw[KM][4], kw[KM][4];
+    float2 sq = make_float2(0.f, 0.f), sk = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int t = 0; t < TMAX; ++t) {
-      if (t >= T) break;
-      float2 sq = make_float2(0.f, 0.f), sk = make_float2(0.f, 0.f);
+    for (int m = 0; m < KM; ++m) {
+      const int c = 4 * m + tq;
+      conv8_silu<NCH>(sTab, 8 * c, tg, rowg + c * 16, row0 + c * 16, qw[m]);
+      conv8_silu<NCH>(sTab, D + 8 * c, tg, rowg + 2 * D + c * 16, row0 + 2 * D + c * 16, kw[m]);
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const float2 qf = bf2f(qw[m][p]), kf = bf2f(kw[m][p]);
+        sq = fma2(qf, qf, sq);
+        sk = fma2(kf, kf, sk);
+      }
+    }
+    const float iq = 1.0f / sqrtf(quad_sum(sq.x + sq.y) + 1e-6f);
+    const float ik = 1.0f / sqrtf(quad_sum(sk.x + sk.y) + 1e-6f);
+    const float qs = iq * a.scale;
+    float bt, at;
+    {
+      const __nv_bfloat162 bw = *reinterpret_cast<const __nv_bfloat162*>(rowg + 8 * D);
+      const __nv_bfloat162 aw = *reinterpret_cast<const __nv_bfloat162*>(rowg + 8 * D + 4);
+      bt = bf16r(sigmoid_f(__bfloat162float((col_b & 1) ? bw.y : bw.x)));
+      at = expf(neg_a * softplus_f(__bfloat162float((col_a & 1) ? aw.y : aw.x) + dtb));
+    }
+    const float kq_self = chunk_dot<KM>(kw, qw) * ik * qs;  // k_t . q_t (normalised, q scaled)
+    float At = at, ckq = 0.f, ckk = 0.f;
+    if constexpr (TMAX == 2) {
+      // step-1 rows: k_0, its norm and decay come from the step-0 partner row (lane ^ 16)
+      uint32_t kp[KM][4];
+#pragma unroll
+      for (int m = 0; m < KM; ++m)
+#pragma unroll
+        for (int p = 0; p < 4; ++p) kp[m][p] = __shfl_xor_sync(0xffffffffu, kw[m][p], 16);
+      const float ikp = __shfl_xor_sync(0xffffffffu, ik, 16), atp = __shfl_xor_sync(0xffffffffu, at, 16);
+      const float dq = chunk_dot<KM>(kp, qw) * ikp * qs;  // k_0 . q_1
+      const float dk = chunk_dot<KM>(kp, kw) * ikp * ik;  // k_0 . k_1
+      if (tg) {
+        At = atp * at;
+        ckq = at * dq;
+        ckk = at * dk;
+      }
+    }
+
+    // ---- [q ; k] x S0 on the tensor cores, recurrence, gated RMSNorm --------------------
+    uint32_t ob[NT];
+    float ss = 0.f;
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      float acc[NH][4];
+#pragma unroll
+      for (int j = 0; j < NH; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
 #pragma unroll
       for (int m = 0; m < KM; ++m) {
-        const int c = 4 * m + tq;
-        conv8_silu<NCH, ROWB>(sTab, 8 * c, t, row0, c * 16, qw[t][m]);
-        conv8_silu<NCH, ROWB>(sTab, D + 8 * c, t, row0, 2 * D + c * 16, kw[t][m]);
 #pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          const float2 qf = bf2f(qw[t][m][p]), kf = bf2f(kw[t][m][p]);
-          sq = fma2(qf, qf, sq);
-          sk = fma2(kf, kf, sk);
+        for (int hh = 0; hh < 2; ++hh) {
+          // A rows: g = q of row g, g + 8 = k of row g; bf16 hi + lo parts
+          const float2 q0 = mul2(bf2f(qw[m][2 * hh]), make_float2(qs, qs));
+          const float2 q1 = mul2(bf2f(qw[m][2 * hh + 1]), make_float2(qs, qs));
+          const float2 k0 = mul2(bf2f(kw[m][2 * hh]), make_float2(ik, ik));
+          const float2 k1 = mul2(bf2f(kw[m][2 * hh + 1]), make_float2(ik, ik));
+          uint32_t ahi[4], alo[4];
+          ahi[0] = bf2_pack_f2(q0);
+          ahi[1] = bf2_pack_f2(k0);
+          ahi[2] = bf2_pack_f2(q1);
+          ahi[3] = bf2_pack_f2(k1);
+          const float2 neg1 = make_float2(-1.f, -1.f);
+          alo[0] = bf2_pack_f2(fma2(bf2f(ahi[0]), neg1, q0));
+          alo[1] = bf2_pack_f2(fma2(bf2f(ahi[1]), neg1, k0));
+          alo[2] = bf2_pack_f2(fma2(bf2f(ahi[2]), neg1, q1));
+          alo[3] = bf2_pack_f2(fma2(bf2f(ahi[3]), neg1, k1));
+          const unsigned char* brow = sS0 + (32 * m + rowoff[hh]) * 2 * D;
+#pragma unroll
+          for (int np = 0; np < NH / 2; ++np) {
+            const int chunk = hf * NH + 2 * np + (lane >> 4);
+            uint32_t bfr[4];
+            ldmatrix_x4_trans(bfr, brow + ((chunk ^ swz[hh]) << 4));
+            const uint32_t b0[2] = {bfr[0], bfr[1]}, b1[2] = {bfr[2], bfr[3]};
+            mma_bf16_16816(acc[2 * np], ahi, b0);
+            mma_bf16_16816(acc[2 * np + 1], ahi, b1);
+            mma_bf16_16816(acc[2 * np], alo, b0);
+            mma_bf16_16816(acc[2 * np + 1], alo, b1);
+          }
         }
       }
-      iq[t] = 1.0f / sqrtf(quad_sum(sq.x + sq.y) + 1e-6f);
-      ik[t] = 1.0f / sqrtf(quad_sum(sk.x + sk.y) + 1e-6f);
-      const unsigned char* gw = row0 + t * 8 * ROWB + 8 * D;
-      const __nv_bfloat162 bw = *reinterpret_cast<const __nv_bfloat162*>(gw);
-      const __nv_bfloat162 aw = *reinterpret_cast<const __nv_bfloat162*>(gw + 4);
-      const float bv = __bfloat162float((col_b & 1) ? bw.y : bw.x);
-      const float av = __bfloat162float((col_a & 1) ? aw.y : aw.x);
-      bt[t] = bf16r(sigmoid_f(bv));
-      at[t] = expf(neg_a * softplus_f(av + dtb));
-    }
-    // dot products of the normalised vectors (q also scaled): k_s.q_t (s <= t), k_0.k_1
-    float kq[TMAX][TMAX], kk01 = 0.f;
+      // columns (jj*8 + 2tq, +1): acc[j][0..1] = S0^T q, acc[j][2..3] = S0^T k of this row
 #pragma unroll
-    for (int t = 0; t < TMAX; ++t) {
-      if (t >= T) break;
-#pragma unroll
-      for (int s = 0; s <= t; ++s) kq[s][t] = chunk_dot<KM>(kw[s], qw[t]) * ik[s] * iq[t] * a.scale;
-      if (t == 1) kk01 = chunk_dot<KM>(kw[0], kw[1]) * ik[0] * ik[1];
-    }
-
-    // ---- per token: [q_t ; k_t] x S0 on the tensor cores, recurrence, gated norm ------
-    float dreg[TMAX > 1 ? 2 * NT : 1];  // d_0 at this thread's columns (T = 2)
-    float At = 1.f;
-#pragma unroll
-    for (int t = 0; t < TMAX; ++t) {
-      if (t >= T) break;
-      At *= at[t];
-      const float qs = iq[t] * a.scale, ks = ik[t];
-      uint32_t ob[NT];
-      float ss = 0.f;
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        float acc[NH][4];
-#pragma unroll
-        for (int j = 0; j < NH; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-#pragma unroll
-        for (int m = 0; m < KM; ++m) {
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            // A rows: g = q_t of beam g, g + 8 = k_t of beam g; hi + lo bf16 parts
-            const float2 q0 = mul2(bf2f(qw[t][m][2 * hh]), make_float2(qs, qs));
-            const float2 q1 = mul2(bf2f(qw[t][m][2 * hh + 1]), make_float2(qs, qs));
-            const float2 k0 = mul2(bf2f(kw[t][m][2 * hh]), make_float2(ks, ks));
-            const float2 k1 = mul2(bf2f(kw[t][m][2 * hh + 1]), make_float2(ks, ks));
-            uint32_t ahi[4], alo[4];
-            ahi[0] = bf2_pack_f2(q0);
-            ahi[1] = bf2_pack_f2(k0);
-            ahi[2] = bf2_pack_f2(q1);
-            ahi[3] = bf2_pack_f2(k1);
-            alo[0] = bf2_pack_f2(add2(q0, mul2(bf2f(ahi[0]), make_float2(-1.f, -1.f))));
-            alo[1] = bf2_pack_f2(add2(k0, mul2(bf2f(ahi[1]), make_float2(-1.f, -1.f))));
-            alo[2] = bf2_pack_f2(add2(q1, mul2(bf2f(ahi[2]), make_float2(-1.f, -1.f))));
-            alo[3] = bf2_pack_f2(add2(k1, mul2(bf2f(ahi[3]), make_float2(-1.f, -1.f))));
-            const unsigned char* brow = sS0 + (32 * m + rowoff[hh]) * 2 * D;
-#pragma unroll
-            for (int np = 0; np < NH / 2; ++np) {
-              const int chunk = hf * NH + 2 * np + (lane >> 4);
-              uint32_t bfr[4];
-              ldmatrix_x4_trans(bfr, brow + ((chunk ^ swz[hh]) << 4));
-              const uint32_t b0[2] = {bfr[0], bfr[1]}, b1[2] = {bfr[2], bfr[3]};
-              mma_bf16_16816(acc[2 * np], ahi, b0);
-              mma_bf16_16816(acc[2 * np + 1], ahi, b1);
-              mma_bf16_16816(acc[2 * np], alo, b0);
-              mma_bf16_16816(acc[2 * np + 1], alo, b1);
-            }
+      for (int j = 0; j < NH; ++j) {
+        const int jj = hf * NH + j, col0 = jj * 8 + 2 * tq;
+        const float2 vx = conv2_silu<NCH>(sTab, 2 * D + col0, tg, rowg + 4 * D + col0 * 2, row0 + 4 * D + col0 * 2);
+        float2 skt = mul2(make_float2(At, At), make_float2(acc[j][2], acc[j][3]));
+        float2 o = mul2(make_float2(At, At), make_float2(acc[j][0], acc[j][1]));
+        const float2 nb = make_float2(-bt, -bt);
+        float2 d = mul2(make_float2(bt, bt), vx);
+        d = fma2(nb, skt, d);  // beta (v - S^T k)
+        if constexpr (TMAX == 2) {
+          const float2 d0 = make_float2(__shfl_xor_sync(0xffffffffu, d.x, 16), __shfl_xor_sync(0xffffffffu, d.y, 16));
+          if (tg) {
+            skt = fma2(make_float2(ckk, ckk), d0, skt);
+            o = fma2(make_float2(ckq, ckq), d0, o);
+            d = fma2(nb, skt, mul2(make_float2(bt, bt), vx));
           }
         }
-        // recurrence at columns (jj*8 + 2tq, +1): acc[j][0..1] = S0^T q_t, acc[j][2..3] = S0^T k_t
-#pragma unroll
-        for (int j = 0; j < NH; ++j) {
-          const int jj = hf * NH + j, col0 = jj * 8 + 2 * tq;
-          const float2 vx = conv2_silu<NCH, ROWB>(sTab, 2 * D + col0, t, row0, 4 * D + col0 * 2);
-          float2 skt = make_float2(At * acc[j][2], At * acc[j][3]);
-          float2 o = make_float2(At * acc[j][0], At * acc[j][1]);
-          if (TMAX > 1 && t == 1) {
-            const float2 d0 = make_float2(dreg[2 * jj], dreg[2 * jj + 1]);
-            skt = fma2(make_float2(at[1] * kk01, at[1] * kk01), d0, skt);
-            o = fma2(make_float2(at[1] * kq[0][1], at[1] * kq[0][1]), d0, o);
-          }
-          const float2 d = mul2(make_float2(bt[t], bt[t]), add2(vx, mul2(skt, make_float2(-1.f, -1.f))));
-          o = fma2(d, make_float2(kq[t][t], kq[t][t]), o);
-          if (TMAX > 1 && t == 0) {
-            dreg[2 * jj] = d.x;
-            dreg[2 * jj + 1] = d.y;
-          }
-          ob[jj] = bf2_pack_f2(o);  // gated_delta returns v's dtype
-          const float2 of = bf2f(ob[jj]);
-          ss = fmaf(of.x, of.x, fmaf(of.y, of.y, ss));
-        }
-      }
-      // ---- gated RMSNorm, written over this token's staged q slice ---------------------
-      const float inv = 1.0f / sqrtf(quad_sum(ss) / float(D) + a.norm_eps);
-      unsigned char* rowt = buf + (t * 8 + g) * ROWB;
-#pragma unroll
-      for (int jj = 0; jj < NT; ++jj) {
-        const int col = jj * 8 + 2 * tq;
+        o = fma2(d, make_float2(kq_self, kq_self), o);
+        ob[jj] = bf2_pack_f2(o);  // gated_delta returns v's dtype
         const float2 of = bf2f(ob[jj]);
-        const float2 z = bf2f(*reinterpret_cast<const uint32_t*>(rowt + 6 * D + col * 2));
-        const float2 w = *reinterpret_cast<const float2*>(sNw + col);
-        const float2 sz = silu2(z);
-        const float h0 = bf16r(w.x * bf16r(of.x * inv)), h1 = bf16r(w.y * bf16r(of.y * inv));
-        *reinterpret_cast<uint32_t*>(rowt + col * 2) = bf2_pack(h0 * sz.x, h1 * sz.y);
+        ss = fmaf(of.x, of.x, fmaf(of.y, of.y, ss));
       }
+    }
+    // gated RMSNorm, written over this row's staged q slice (read only by the prep above)
+    const float inv = 1.0f / sqrtf(quad_sum(ss) / float(D) + a.norm_eps);
+#pragma unroll
+    for (int jj = 0; jj < NT; ++jj) {
+      const int col = jj * 8 + 2 * tq;
+      const float2 of = bf2f(ob[jj]);
+      const float2 z = bf2f(*reinterpret_cast<const uint32_t*>(rowg + 6 * D + col * 2));
+      const float2 w = *reinterpret_cast<const float2*>(sNw + col);
+      const float2 sz = silu2(z);
+      const float h0 = bf16r(w.x * bf16r(of.x * inv)), h1 = bf16r(w.y * bf16r(of.y * inv));
+      *reinterpret_cast<uint32_t*>(rowg + col * 2) = bf2_pack(h0 * sz.x, h1 * sz.y);
     }
     __syncwarp();
     // ---- the octet's output rows, 16 bytes per store ------------------------------------
-    for (int idx = lane; idx < T * 8 * CH; idx += 32) {
+    for (int idx = lane; idx < 8 * CH; idx += 32) {
       const int r = idx / CH, c = idx % CH;
-      const int ob_beam = (oct0 + it) * 8 + (r & 7);
-      if (ob_beam < a.W) {
-        const int64_t orow = (int64_t(b) * a.W + ob_beam) * T + (r >> 3);
+      const int beam = (oct0 + it) * BPO + r % BPO;
+      if (beam < a.W) {
+        const int64_t orow = (int64_t(b) * a.W + beam) * TMAX + r / BPO;
         *reinterpret_cast<uint4*>(a.out + orow * (int64_t(HV) * D) + hv * D + c * 8) =
             *reinterpret_cast<const uint4*>(buf + r * ROWB + c * 16);
       }
@@ -364,25 +367,26 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
 
 template <int D, int TMAX>
 int launch_mixer(const MixerArgs& a, cudaStream_t stream) {
-  const size_t smem = MixLayout<D>::smem(a.T);
+  using L = MixLayout<D>;
   auto kern = gdn_mixer_kernel<D, TMAX>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess) {
-    set_error("gdn mixer: cannot reserve %zu bytes of shared memory", smem);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L::SMEM)) != cudaSuccess) {
+    set_error("gdn mixer: cannot reserve %zu bytes of shared memory", L::SMEM);
     return KADLLM_ECUDA;
   }
   int sms = 148;
   int dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int octets = (a.W + 7) / 8;
-  const int per_sm = smem * 2 <= 220 * 1024 ? 2 : 1;
-  // split a head's octets over enough CTAs to fill about two waves, each warp taking a run of octets
+  constexpr int bpo = 8 / TMAX;
+  const int octets = (a.W + bpo - 1) / bpo;
+  // split a head's octets over enough CTAs for about two waves (two CTAs per SM), each
+  // warp taking a run of consecutive octets
   const int heads = a.B * a.HV;
-  int ny = (2 * sms * per_sm + heads - 1) / heads;
+  int ny = (4 * sms + heads - 1) / heads;
   ny = max(1, min(ny, (octets + kMixWarps - 1) / kMixWarps));
   const int opw = (octets + kMixWarps * ny - 1) / (kMixWarps * ny);
   ny = (octets + kMixWarps * opw - 1) / (kMixWarps * opw);
   const dim3 grid{unsigned(heads), unsigned(ny)};
-  kern<<<grid, kMixWarps * 32, smem, stream>>>(a, opw);
+  kern<<<grid, kMixWarps * 32, L::SMEM, stream>>>(a, opw);
   KB_CHECK_LAUNCH("gdn mixer launch");
   return KADLLM_OK;
 }
