@@ -146,11 +146,15 @@ __device__ __forceinline__ float ex2_approx(float x) {
 //     be among the request's top W (a row shares parent score and normaliser),
 //     so binning only them leaves the threshold bin unchanged, and bins past
 //     tau's stay empty (rowlen);
-//   pass 2 (L2): threads whose maximum reaches tau re-read their slice and bin
-//     d = 32 (max - x) with one FFMA (bit-identical to (max - x) * 32).  Pass 2
-//     of row r runs inside pass 1 of the CTA's next row, so HBM never idles and
-//     about one row per SM (~74 MB at V = 248320) is live in L2.
+//   pass 2: each thread's 16-byte vector maxima of the row are kept in shared
+//     memory (bf16, [slot][thread]); a thread re-reads only the vectors whose
+//     maximum reaches tau and bins d = 32 (max - x) with one FFMA (bit-identical
+//     to (max - x) * 32).  Pass 2 of row r runs inside pass 1 of the CTA's next
+//     row (two tables, alternating), so the HBM stream never waits for it and
+//     the few re-read vectors are the only extra traffic.
 constexpr int kStatThreads = 1024;
+constexpr int kStatSlots = 48;  // vectors per thread (V <= 48 * 8 * 1024) for the table
+__host__ __device__ constexpr size_t stat_smem(int slots) { return size_t(2) * slots * kStatThreads * 2; }
 
 __device__ __forceinline__ float vec_max(const uint4& u) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
@@ -169,7 +173,8 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&x)[8]) {
 
 struct OnlineSum {
   float m = -INFINITY, ml = 0.f, s0 = 0.f, s1 = 0.f;
-  __device__ __forceinline__ void add(const uint4& u) {
+  // accumulate one 16-byte vector; returns its maximum
+  __device__ __forceinline__ float add(const uint4& u) {
     const float hi = vec_max(u);
     if (hi > m) {  // rare after the first vectors; -inf and NaN vectors never enter
       const float c = ex2_approx((m - hi) * kLog2e);
@@ -185,6 +190,7 @@ struct OnlineSum {
       s0 += ex2_approx(fmaf(x[j], kLog2e, -ml));
       s1 += ex2_approx(fmaf(x[j + 1], kLog2e, -ml));
     }
+    return hi;
   }
 };
 
@@ -201,9 +207,12 @@ __device__ __forceinline__ void bin_vec(const uint4& u, float tau, float m32, ui
 __global__ void __launch_bounds__(kStatThreads, 1) rowstats_bf16_kernel(const SelArgs a) {
   __shared__ uint32_t hist[kRowBins];
   __shared__ float red[33];
+  extern __shared__ __align__(16) unsigned char dsm[];
+  __nv_bfloat16* vmax = reinterpret_cast<__nv_bfloat16*>(dsm);  // [2][slots][nt] vector maxima
   constexpr int nt = kStatThreads, nwarps = kStatThreads / 32;
   const int64_t rows = int64_t(a.B) * a.Wp;
   const int nvec = int(a.V / 8);
+  const int slots = (nvec + nt - 1) / nt;
   const int tid = threadIdx.x, lane = tid & 31;
   for (int j = tid; j < kRowBins; j += nt) hist[j] = 0;
   // the CTA's previous row, binned while the current one streams in
@@ -212,33 +221,39 @@ __global__ void __launch_bounds__(kStatThreads, 1) rowstats_bf16_kernel(const Se
   float ptau = 0.f, pm32 = 0.f;
   int pbin = 0;
   bool pact = false;
-  for (int64_t r = blockIdx.x;; r += gridDim.x) {
+  int par = 0;  // table of the current row
+  for (int64_t r = blockIdx.x;; r += gridDim.x, par ^= 1) {
     const bool cur = r < rows;
     const uint4* row = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.logits) +
                                                       (cur ? r : 0) * a.ld);
+    __nv_bfloat16* tcur = vmax + size_t(par) * slots * nt + tid;
+    const __nv_bfloat16* tprev = vmax + size_t(par ^ 1) * slots * nt + tid;
+    // previous row's vector at slot k: re-read and bin it when its maximum reaches tau
+    auto bin_prev = [&](int k) {
+      if (__bfloat162float(tprev[k * nt]) >= ptau) bin_vec(prow[tid + k * nt], ptau, pm32, hist);
+    };
     OnlineSum acc;
     if (cur) {
-      int i = tid;
-      for (; i + 3 * nt < nvec; i += 4 * nt) {  // four 16-byte HBM loads in flight
+      int i = tid, k = 0;
+      for (; i + 3 * nt < nvec; i += 4 * nt, k += 4) {  // four 16-byte HBM loads in flight
         const uint4 u0 = row[i], u1 = row[i + nt], u2 = row[i + 2 * nt], u3 = row[i + 3 * nt];
         if (pact) {
-          const uint4 v0 = prow[i], v1 = prow[i + nt], v2 = prow[i + 2 * nt], v3 = prow[i + 3 * nt];
-          bin_vec(v0, ptau, pm32, hist);
-          bin_vec(v1, ptau, pm32, hist);
-          bin_vec(v2, ptau, pm32, hist);
-          bin_vec(v3, ptau, pm32, hist);
+          bin_prev(k);
+          bin_prev(k + 1);
+          bin_prev(k + 2);
+          bin_prev(k + 3);
         }
-        acc.add(u0);
-        acc.add(u1);
-        acc.add(u2);
-        acc.add(u3);
+        tcur[k * nt] = __float2bfloat16_rn(acc.add(u0));
+        tcur[(k + 1) * nt] = __float2bfloat16_rn(acc.add(u1));
+        tcur[(k + 2) * nt] = __float2bfloat16_rn(acc.add(u2));
+        tcur[(k + 3) * nt] = __float2bfloat16_rn(acc.add(u3));
       }
-      for (; i < nvec; i += nt) {
-        acc.add(row[i]);
-        if (pact) bin_vec(prow[i], ptau, pm32, hist);
+      for (; i < nvec; i += nt, ++k) {
+        tcur[k * nt] = __float2bfloat16_rn(acc.add(row[i]));
+        if (pact) bin_prev(k);
       }
     } else if (pact) {
-      for (int i = tid; i < nvec; i += nt) bin_vec(prow[i], ptau, pm32, hist);
+      for (int k = 0; tid + k * nt < nvec; ++k) bin_prev(k);
     }
     if (pr >= 0) {  // export the previous row's bins and clear them for the next
       __syncthreads();
@@ -438,9 +453,16 @@ int launch_select(SelArgs& a, bool vec, cudaStream_t s) {
     if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
       num_sms = 148;
   }
-  if (std::is_same<T, __nv_bfloat16>::value && vec && a.mask == nullptr)
-    rowstats_bf16_kernel<<<unsigned(rows < num_sms ? rows : num_sms), kStatThreads, 0, s>>>(a);
-  else
+  const int slots = int((a.V / 8 + kStatThreads - 1) / kStatThreads);
+  if (std::is_same<T, __nv_bfloat16>::value && vec && a.mask == nullptr && slots <= kStatSlots) {
+    const size_t smem = stat_smem(slots);
+    if (cudaFuncSetAttribute(rowstats_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
+        cudaSuccess) {
+      set_error("beam select: cannot reserve %zu bytes of shared memory", smem);
+      return KADLLM_ECUDA;
+    }
+    rowstats_bf16_kernel<<<unsigned(rows < num_sms ? rows : num_sms), kStatThreads, smem, s>>>(a);
+  } else
     rowstats_kernel<T><<<unsigned(rows), kRowThreads, 0, s>>>(a, vec);
   threshold_kernel<<<a.B, 1024, 0, s>>>(a);
   collect_kernel<T><<<unsigned(rows), 256, 0, s>>>(a, vec);

@@ -300,6 +300,15 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const SplitArgs a) {
     sBEG[tid] = sBeta[tid] * e;
     sEGL[tid] = __expf(sG[kC - 1] - sG[tid]);
   }
+  // in-chunk decay matrix exp(G_i - G_j), lower triangle incl. the diagonal (zero above), once
+  // per chunk for both epilogues below; it lives in the T1 / T2 area, written only later
+  constexpr int SD = kC + 8;  // row stride: 8-byte aligned pairs, conflict-free half-warp reads
+  float* sDec = reinterpret_cast<float*>(smem + M::t1);  // [kC][SD]
+  static_assert(M::t1 + size_t(kC) * SD * 4 <= M::a, "decay matrix fits the T1 / T2 area");
+  for (int e = tid; e < kC * kC; e += NT) {
+    const int i = e / kC, j = e % kC;
+    sDec[i * SD + j] = i >= j ? __expf(sG[i] - sG[j]) : 0.f;
+  }
   const int g8 = lane >> 2, tq = lane & 3;
   // ---- warps 0-3: K K^T -> L (fp32); warps 4-7: Q K^T -> Aqk (bf16) --------------------
   {
@@ -308,17 +317,19 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const SplitArgs a) {
     float acc[8][4];
     zero_acc<8>(acc);
     warp_mma<DK, 8, false, false>(acc, is_q ? sQ : sK, SQ, mt * 16, 0, sK, SQ, 0, 0);
+    __syncthreads();  // the decay matrix is complete
 #pragma unroll
     for (int j = 0; j < 8; ++j)
 #pragma unroll
       for (int hr = 0; hr < 2; ++hr) {
         const int i = mt * 16 + g8 + hr * 8;
         const int col = j * 8 + tq * 2;
+        const float2 dec2 = *reinterpret_cast<const float2*>(sDec + i * SD + col);
         float av[2];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int cc = col + e;
-          const float dec = i >= cc ? __expf(sG[i] - sG[cc]) : 0.f;
+          const float dec = e ? dec2.y : dec2.x;
           if (is_q) av[e] = acc[j][hr * 2 + e] * dec;
           else sL[i * SL + cc] = i > cc ? sBeta[i] * acc[j][hr * 2 + e] * dec : 0.f;
         }
@@ -640,32 +651,42 @@ __device__ __forceinline__ void named_bar(int id, int n) { asm volatile("bar.syn
 //   out = bf16( bf16(w * bf16(o * rsqrt(mean(o^2) + eps))) * silu(z) )
 // (Qwen3_5RMSNormGated, modeling_qwen3_5.py:175-190; o is the BF16 gated_delta output).
 __global__ void __launch_bounds__(256) gdn_gated_norm_kernel(const SplitArgs a) {
-  const int64_t item = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  const int64_t rows = int64_t(a.B) * a.L;
-  if (item >= rows * a.HV) return;
-  const int lane = threadIdx.x & 31;
-  const int64_t row = item / a.HV;
-  const int hv = int(item % a.HV);
+  // 16 lanes per (row, value head), 8 channels (16 bytes) a lane; 32-bit item arithmetic
+  // (the launcher checks B * L * HV < 2^31)
+  const uint32_t items = uint32_t(a.B) * uint32_t(a.L) * uint32_t(a.HV);
+  const uint32_t want = blockIdx.x * 16u + (threadIdx.x >> 4);
+  const bool ok = want < items;  // past the end: recompute the last item (every lane meets the shuffles)
+  const uint32_t item = ok ? want : items - 1;
+  const int l16 = threadIdx.x & 15;
+  const uint32_t row = item / uint32_t(a.HV);
+  const int hv = int(item - row * uint32_t(a.HV));
   const int conv_dim = 2 * a.H * 128 + a.HV * 128;
-  __nv_bfloat16* op = a.out + row * a.ld_out + hv * 128 + lane * 4;
-  const __nv_bfloat16* zp = a.proj + row * a.ld_proj + conv_dim + hv * 128 + lane * 4;
-  const uint2 ov = *reinterpret_cast<const uint2*>(op);
-  const uint2 zv = *reinterpret_cast<const uint2*>(zp);
-  const float2 o0 = bf2f(ov.x), o1 = bf2f(ov.y);
-  float ss = o0.x * o0.x + o0.y * o0.y + o1.x * o1.x + o1.y * o1.y;
-  ss = warp_sum(ss);
-  const float inv = 1.0f / sqrtf(ss / 128.f + a.eps);
-  const float4 w = *reinterpret_cast<const float4*>(a.norm_w + lane * 4);
-  const float2 z0 = bf2f(zv.x), z1 = bf2f(zv.y);
-  const float x[4] = {o0.x, o0.y, o1.x, o1.y}, wz[4] = {w.x, w.y, w.z, w.w}, zz[4] = {z0.x, z0.y, z1.x, z1.y};
-  float r[4];
+  __nv_bfloat16* op = a.out + int64_t(row) * a.ld_out + hv * 128 + l16 * 8;
+  const __nv_bfloat16* zp = a.proj + int64_t(row) * a.ld_proj + conv_dim + hv * 128 + l16 * 8;
+  const uint4 ov = *reinterpret_cast<const uint4*>(op);
+  const uint4 zv = *reinterpret_cast<const uint4*>(zp);
+  const float2 o[4] = {bf2f(ov.x), bf2f(ov.y), bf2f(ov.z), bf2f(ov.w)};
+  float2 s2 = mul2(o[0], o[0]);
+  s2 = fma2(o[1], o[1], s2);
+  s2 = fma2(o[2], o[2], s2);
+  s2 = fma2(o[3], o[3], s2);
+  float ss = s2.x + s2.y;
 #pragma unroll
-  for (int e = 0; e < 4; ++e) r[e] = bf16r(wz[e] * bf16r(x[e] * inv)) * silu_f(zz[e]);
-  uint2 res;
-  const __nv_bfloat162 h0 = __floats2bfloat162_rn(r[0], r[1]), h1 = __floats2bfloat162_rn(r[2], r[3]);
-  res.x = *reinterpret_cast<const uint32_t*>(&h0);
-  res.y = *reinterpret_cast<const uint32_t*>(&h1);
-  *reinterpret_cast<uint2*>(op) = res;
+  for (int m = 8; m > 0; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+  const float inv = 1.0f / sqrtf(ss / 128.f + a.eps);
+  const float4 w0 = *reinterpret_cast<const float4*>(a.norm_w + l16 * 8);
+  const float4 w1 = *reinterpret_cast<const float4*>(a.norm_w + l16 * 8 + 4);
+  const float2 w[4] = {make_float2(w0.x, w0.y), make_float2(w0.z, w0.w), make_float2(w1.x, w1.y),
+                       make_float2(w1.z, w1.w)};
+  const uint32_t zw[4] = {zv.x, zv.y, zv.z, zv.w};
+  uint32_t res[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const float2 n = bf2f(bf2_pack_f2(mul2(o[p], make_float2(inv, inv))));  // bf16(o * inv)
+    const float2 h = bf2f(bf2_pack_f2(mul2(w[p], n)));                       // bf16(w * .)
+    res[p] = bf2_pack_f2(mul2(h, silu2(bf2f(zw[p]))));
+  }
+  if (ok) *reinterpret_cast<uint4*>(op) = make_uint4(res[0], res[1], res[2], res[3]);
 }
 
 __global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) {
@@ -851,7 +872,8 @@ int launch_split(SplitArgs& a, void* ws, int64_t ws_bytes, cudaStream_t s) {
   a.blocks = static_cast<unsigned char*>(ws) + 256;
   const bool tc_scan = DK == 128 && DV == 128 && a.ld_out % 8 == 0 && a.ld_proj % 8 == 0 &&
                        (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.state) & 15) == 0 &&
-                       (reinterpret_cast<uintptr_t>(a.norm_w) & 15) == 0;
+                       (reinterpret_cast<uintptr_t>(a.norm_w) & 15) == 0 &&
+                       (reinterpret_cast<uintptr_t>(a.proj) & 15) == 0 && int64_t(a.B) * a.L * a.HV < (1ll << 31);
   a.tc_layout = tc_scan ? 1 : 0;
   if (cudaMemsetAsync(a.status, 0, sizeof(uint32_t), s) != cudaSuccess) {
     set_error("gdn prefill: cannot clear the status word");
@@ -875,8 +897,8 @@ int launch_split(SplitArgs& a, void* ws, int64_t ws_bytes, cudaStream_t s) {
     }
     gdn_scan_tc_kernel<<<unsigned(n), 256, smem, s>>>(a);
     KB_CHECK_LAUNCH("gdn prefill tensor-core scan launch");
-    const int64_t items = int64_t(a.B) * a.L * a.HV;  // (row, value head) pairs, 8 per CTA
-    gdn_gated_norm_kernel<<<unsigned((items + 7) / 8), 256, 0, s>>>(a);
+    const int64_t items = int64_t(a.B) * a.L * a.HV;  // (row, value head) pairs, 16 per CTA
+    gdn_gated_norm_kernel<<<unsigned((items + 15) / 16), 256, 0, s>>>(a);
     KB_CHECK_LAUNCH("gdn prefill gated norm launch");
     return KADLLM_OK;
   }
