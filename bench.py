@@ -1,6 +1,6 @@
 """GRBeam benchmark: requests/s on the Qwen3.5-0.8B-shaped hybrid (B200).
 
-Workload (BASELINE config 2 per GPU): random-init BF16 weights N(0, 0.02)
+Workload (per GPU): random-init BF16 weights N(0, 0.02)
 (seed 0), 32 requests of 1024 uniform-random prompt tokens per GPU, beam width
 256, 3 output tokens (prefill + 2 decode steps + selection), full 248,320-token
 vocabulary.  One step = one ``grbeam_search`` call over one 32-request batch
@@ -299,6 +299,87 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+SID_WIDTHS = (256, 256)
+SID_LEVEL = 4096     # tokens per codebook level
+SID_GROUPS = 256     # level-1 groups (16 level-2 tokens each)
+SID_PREFIX = (512, 4096)
+
+
+def run_sid(args, rank: int, world: int, local_rank: int) -> None:
+    """Two-level conditional SID search: prefix lengths drawn
+    uniformly from 512-4096 per request, SID-only head over 2 x 4096 codebook
+    tokens, token 2 restricted to token 1's group, widths 256, 256."""
+    import numpy as np
+    import torch
+
+    from kadllm_b200 import _lib
+    from kadllm_b200.adapters import NativeGRBeamAdapter
+    from kadllm_b200.config import QWEN35_08B
+    from kadllm_b200.model import HybridModel
+    from kadllm_b200.shard import max_over_ranks
+    from kadllm_b200.sid import SidCodebook, SidHeadAdapter, sid_search
+    from kadllm_b200.synthetic import torch_weights
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    cfg = QWEN35_08B
+    engine = HybridModel(cfg, torch_weights(cfg, seed=0, device=dev), device=dev)
+    adapter = NativeGRBeamAdapter(engine)
+    cb = SidCodebook.synthetic(cfg.vocab_size, SID_LEVEL, SID_LEVEL, SID_GROUPS, seed=0)
+    head = SidHeadAdapter(adapter, cb)
+    rng = np.random.default_rng(1000 + rank)
+    lengths = rng.integers(SID_PREFIX[0], SID_PREFIX[1] + 1, args.sid_batch)
+    host = [torch.from_numpy(rng.integers(0, cfg.vocab_size, int(n))).pin_memory() for n in lengths]
+    dev_prompts = [p.to(dev) for p in host]
+    tok_host = torch.empty(args.sid_batch, SID_WIDTHS[-1], 2, dtype=torch.int64).pin_memory()
+
+    def step_device():
+        return sid_search(adapter, dev_prompts, cb, SID_WIDTHS, head=head, streams=args.sid_streams)
+
+    def step_e2e():
+        res = sid_search(adapter, [p.to(dev, non_blocking=True) for p in host], cb, SID_WIDTHS, head=head,
+                         streams=args.sid_streams)
+        tok_host.copy_(res.tokens, non_blocking=True)
+        return res
+
+    def timed(fn, steps):
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        launches0 = _lib.launch_count
+        start.record()
+        for _ in range(steps):
+            fn()
+        end.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(start.elapsed_time(end), dev) / steps, _lib.launch_count - launches0
+
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            step_device()
+        ms, launches = timed(step_device, args.steps)
+        ms_e2e, _ = timed(step_e2e, args.steps)
+        res = step_device()
+        valid = bool(res.valid.all().item())
+    if rank != 0:
+        return
+    line = {
+        "metric": "requests/s (two-level conditional SID, Qwen3.5-0.8B, prefix 512-4096, beam 256)",
+        "value": world * args.sid_batch / (ms / 1000), "unit": "requests/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random prompts and lengths, random-init weights, seeded codebooks)",
+        "config": {"workload": "sid", "model": "qwen3.5-0.8b-shaped", "batch_per_gpu": args.sid_batch,
+                   "prefix_lengths": [int(lengths.min()), int(lengths.max())], "widths": list(SID_WIDTHS),
+                   "codebook": f"2 x {SID_LEVEL} tokens, {SID_GROUPS} groups", "head": "SID-only",
+                   "streams": args.sid_streams},
+        "e2e": {"value": world * args.sid_batch / (ms_e2e / 1000), "unit": "requests/s",
+                "h2d_bytes_per_step": int(lengths.sum()) * 8, "d2h_bytes_per_step": args.sid_batch * SID_WIDTHS[-1] * 16},
+        "gpu_launches": launches,
+        "checks": {"all_valid": valid},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def profile_kernels(engine, adapter, ids_dev, widths, args):
     """Per-entry-point device time over one extra search, CUDA events on the
     launching stream; the dominant kernel's roofline is derived from it."""
@@ -335,6 +416,10 @@ def main() -> None:
     ap.add_argument("--impl", choices=["native", "reference"], default="native")
     ap.add_argument("--roofline-kernel", default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["grbeam", "sid"], default="grbeam",
+                    help="grbeam: the headline metric; sid: two-level conditional SID, prefixes 512-4096")
+    ap.add_argument("--sid-batch", type=int, default=32)
+    ap.add_argument("--sid-streams", type=int, default=1)
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -354,7 +439,7 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_native(args, rank, world, local_rank)
+        (run_sid if args.workload == "sid" else run_native)(args, rank, world, local_rank)
     finally:
         if world > 1:
             dist.destroy_process_group()

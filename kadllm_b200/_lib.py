@@ -8,6 +8,7 @@ non-CUDA tensors, raises.
 from __future__ import annotations
 
 import ctypes
+import threading
 from pathlib import Path
 
 import torch
@@ -72,6 +73,7 @@ _ERRORS = {1: ValueError, 2: TypeError, 3: NotImplementedError, 4: RuntimeError}
 # kernels launched per successful call of each entry point (for launch accounting)
 LAUNCHES_PER_CALL = {"kadllm_beam_select": 4, "kadllm_beam_select_noalloc": 4, "kadllm_beam_select_status": 0, "kadllm_gdn_prefill_split": 3}
 launch_count = 0
+_count_lock = threading.Lock()
 
 
 def call(name: str, *args) -> None:
@@ -79,7 +81,8 @@ def call(name: str, *args) -> None:
     global launch_count
     rc = getattr(lib(), name)(*args)
     if not rc:
-        launch_count += LAUNCHES_PER_CALL.get(name, 1)
+        with _count_lock:  # callers may drive several streams from several threads
+            launch_count += LAUNCHES_PER_CALL.get(name, 1)
     if rc:
         msg = lib().kadllm_last_error().decode(errors="replace")
         raise _ERRORS.get(rc, RuntimeError)(msg)

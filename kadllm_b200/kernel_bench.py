@@ -1,8 +1,8 @@
-"""Kernel microbenchmarks at the BASELINE shapes (seeded synthetic inputs).
+"""Kernel microbenchmarks at the benchmark shapes (seeded synthetic inputs).
 
     python -m kadllm_b200.kernel_bench --case CASE [--reps N]
 
-Cases (BASELINE config 5 and the GRBeam step shapes):
+Cases (the kernel microbenchmark shapes and the GRBeam step shapes):
   prefill  chunked gated-delta prefill (conv + gates + UT transform + scan +
            gated norm) from the packed projection: B=32, T=1024, 16 heads of 128
   conv     causal conv1d width 4 + SiLU over T=1024, 2048 channels (B=32)

@@ -20,6 +20,8 @@ there is no CPU path.
 
 from __future__ import annotations
 
+import threading
+
 from dataclasses import dataclass
 
 import torch
@@ -129,6 +131,8 @@ class HybridModel:
                 w_down=bf(p + "mlp.down_proj.weight")))
         self._rope_len = 0
         self._cos = self._sin = None
+        self._rope_lock = threading.Lock()
+        self._rope_retired = []  # outgrown tables stay alive: kernels on other streams may still read them
         self.owner = object()
         # device status word of the tensor-core kernels (bit 0: a bounded wait timed out)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -159,18 +163,21 @@ class HybridModel:
     def _rope(self, n: int):
         """cos/sin tables [n, rotary_dim] in BF16, computed like
         ``Qwen3_5TextRotaryEmbedding`` (fp32 inv_freq x position, cos/sin, cast)."""
-        if n > self._rope_len:
-            n = max(n, 2 * self._rope_len, 4096)
-            rd = self.cfg.rotary_dim
-            inv = 1.0 / (self.cfg.rope_theta ** (torch.arange(0, rd, 2, dtype=torch.int64, device=self.device)
-                                                 .float() / rd))
-            pos = torch.arange(n, device=self.device, dtype=torch.float32)
-            freqs = pos[:, None] * inv[None, :]
-            emb = torch.cat([freqs, freqs], -1)
-            self._cos = emb.cos().to(BF16).contiguous()
-            self._sin = emb.sin().to(BF16).contiguous()
-            self._rope_len = n
-        return self._cos, self._sin
+        with self._rope_lock:
+            if n > self._rope_len:
+                n = max(n, 2 * self._rope_len, 4096)
+                rd = self.cfg.rotary_dim
+                inv = 1.0 / (self.cfg.rope_theta ** (torch.arange(0, rd, 2, dtype=torch.int64, device=self.device)
+                                                     .float() / rd))
+                pos = torch.arange(n, device=self.device, dtype=torch.float32)
+                freqs = pos[:, None] * inv[None, :]
+                emb = torch.cat([freqs, freqs], -1)
+                cos, sin = emb.cos().to(BF16).contiguous(), emb.sin().to(BF16).contiguous()
+                torch.cuda.current_stream(self.device).synchronize()  # complete before any stream reads it
+                if self._cos is not None:
+                    self._rope_retired.append((self._cos, self._sin))
+                self._cos, self._sin, self._rope_len = cos, sin, n
+            return self._cos, self._sin
 
     def _embed(self, ids: torch.Tensor):
         rows = ids.numel()
@@ -207,8 +214,9 @@ class HybridModel:
 
     # ------------------------------------------------------------------ prefill
     @torch.no_grad()
-    def prefill(self, ids: torch.Tensor):
-        """ids [B, L] -> (logits [B, V] bf16, HybridPrefix)."""
+    def prefill(self, ids: torch.Tensor, head: torch.Tensor | None = None):
+        """ids [B, L] -> (logits [B, V] bf16, HybridPrefix).  ``head`` [V', H] replaces
+        the LM head (a SID-only head: logits over its rows only)."""
         c = self.cfg
         B, L = ids.shape
         ids = ids.to(device=self.device, dtype=torch.int64).contiguous()
@@ -269,7 +277,7 @@ class HybridModel:
                 self._add_norm(x, delta, self.layers[i + 1].input_ln, normed)
         last = torch.empty(B, c.hidden_size, dtype=BF16, device=self.device)
         self._add_norm(x, delta, self.final_norm, last, rows=B, step=L, offset=L - 1)
-        logits = F.linear(last, self.lm_head)
+        logits = F.linear(last, self.lm_head if head is None else head)
         return logits, HybridPrefix(L, B, self.owner, tuple(prefix), tuple(tiles))
 
     # ------------------------------------------------------------------ decode
@@ -327,7 +335,9 @@ class HybridModel:
         return last
 
     @torch.no_grad()
-    def decode(self, history: torch.Tensor, state: HybridPrefix) -> torch.Tensor:
-        """Replay [B, W, T] suffix tokens; return [B, W, V] logits (BF16)."""
+    def decode(self, history: torch.Tensor, state: HybridPrefix, head: torch.Tensor | None = None) -> torch.Tensor:
+        """Replay [B, W, T] suffix tokens; return [B, W, V] logits (BF16) over the LM
+        head's rows, or over ``head``'s rows when given."""
         B, W, _ = history.shape
-        return F.linear(self.decode_hidden(history, state), self.lm_head).view(B, W, -1)
+        w = self.lm_head if head is None else head
+        return F.linear(self.decode_hidden(history, state), w).view(B, W, -1)

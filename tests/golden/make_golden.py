@@ -7,7 +7,7 @@ importable (pass the reference's ``src`` directory as the first argument):
 
 Every fixture records inputs and the reference's outputs:
 
-* ``model_<dtype>.npz``  tiny hybrid through
+* ``model_<dtype>.npz``  tiny hybrid (the CPU-plumbing config) through
   ``Qwen35GRBeamAdapter`` (torch backends) + ``grbeam_search`` with widths
   [8, 8, 8]: prefill logits, every prefix tensor, decode logits for both decode
   steps (all beams) and for fixed histories of 1-3 tokens shared by both dtypes,

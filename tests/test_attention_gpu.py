@@ -54,7 +54,7 @@ def test_matches_oracle(D, L, T):
 
 @pytest.mark.parametrize("B,W,T,L", [(32, 256, 1, 1024), (32, 256, 2, 1024), (1, 256, 3, 4096)])
 def test_full_size_matches_torch_fp32(B, W, T, L):
-    """BASELINE decode shapes (8 q / 2 kv heads, d = 256) and the kernel microbench (c)."""
+    """0.8B decode shapes (8 q / 2 kv heads, d = 256) and the decode-attention microbenchmark."""
     from kadllm_b200 import ops
 
     gen = torch.Generator(device="cuda").manual_seed(L + T)

@@ -26,7 +26,7 @@ def _hf_tiny():
 
 
 def test_tiny_model_matches_reference_golden():
-    """BASELINE config 1 architecture, BF16, through the drop-in adapter + search."""
+    """The tiny CPU-plumbing architecture, BF16, through the drop-in adapter + search."""
     from kadllm_b200 import grbeam_search
     from kadllm_b200.adapters import Qwen35GRBeamAdapter
 

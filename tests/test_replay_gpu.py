@@ -64,7 +64,7 @@ def test_gated_delta_matches_oracle(T, dims):
 
 
 def test_gated_delta_full_size_matches_torch_fp32():
-    """BASELINE shape: 32 requests x 256 beams, 16 heads of 128, T = 1 and 2."""
+    """Step shape: 32 requests x 256 beams, 16 heads of 128, T = 1 and 2."""
     from kadllm_b200 import ops
 
     gen = torch.Generator(device="cuda").manual_seed(0)

@@ -84,7 +84,7 @@ def test_select_step_matches_oracle_with_tie_rule(dtype, B, Wp, V, W):
 
 
 def test_select_full_vocab_shape_and_properties():
-    """BASELINE step shape: 32 requests x 256 beams x 248320 tokens (bf16)."""
+    """Step shape: 32 requests x 256 beams x 248320 tokens (bf16)."""
     from kadllm_b200.grbeam import BeamSelector
 
     B, Wp, V, W = 32, 256, 248320, 256
