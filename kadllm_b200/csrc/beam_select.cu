@@ -171,24 +171,26 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&x)[8]) {
   }
 }
 
+// Per-thread online max and sum of exp2(x log2e - max log2e), the sum kept as a
+// pair (even / odd elements) in packed fp32x2 arithmetic.
 struct OnlineSum {
-  float m = -INFINITY, ml = 0.f, s0 = 0.f, s1 = 0.f;
+  float m = -INFINITY, ml = 0.f;
+  float2 s = make_float2(0.f, 0.f);
   // accumulate one 16-byte vector; returns its maximum
   __device__ __forceinline__ float add(const uint4& u) {
     const float hi = vec_max(u);
     if (hi > m) {  // rare after the first vectors; -inf and NaN vectors never enter
       const float c = ex2_approx((m - hi) * kLog2e);
-      s0 *= c;
-      s1 *= c;
+      s = mul2(s, make_float2(c, c));
       m = hi;
       ml = hi * kLog2e;
     }
-    float x[8];
-    unpack8(u, x);
+    const float2 l2e = make_float2(kLog2e, kLog2e), nml = make_float2(-ml, -ml);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-    for (int j = 0; j < 8; j += 2) {
-      s0 += ex2_approx(fmaf(x[j], kLog2e, -ml));
-      s1 += ex2_approx(fmaf(x[j + 1], kLog2e, -ml));
+    for (int j = 0; j < 4; ++j) {
+      const float2 t = fma2(bf2f(w[j]), l2e, nml);
+      s = add2(s, make_float2(ex2_approx(t.x), ex2_approx(t.y)));
     }
     return hi;
   }
@@ -222,10 +224,18 @@ __global__ void __launch_bounds__(kStatThreads, 1) rowstats_bf16_kernel(const Se
   int pbin = 0;
   bool pact = false;
   int par = 0;  // table of the current row
+  const __nv_bfloat16* base = reinterpret_cast<const __nv_bfloat16*>(a.logits);
+  // the first four vectors of the CTA's next row, loaded before the current row's
+  // reductions so HBM keeps streaming through them
+  uint4 f0, f1, f2, f3;
+  const bool full4 = tid + 3 * nt < nvec;
+  if (full4 && int64_t(blockIdx.x) < rows) {
+    const uint4* r0 = reinterpret_cast<const uint4*>(base + int64_t(blockIdx.x) * a.ld);
+    f0 = r0[tid]; f1 = r0[tid + nt]; f2 = r0[tid + 2 * nt]; f3 = r0[tid + 3 * nt];
+  }
   for (int64_t r = blockIdx.x;; r += gridDim.x, par ^= 1) {
     const bool cur = r < rows;
-    const uint4* row = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.logits) +
-                                                      (cur ? r : 0) * a.ld);
+    const uint4* row = reinterpret_cast<const uint4*>(base + (cur ? r : 0) * a.ld);
     __nv_bfloat16* tcur = vmax + size_t(par) * slots * nt + tid;
     const __nv_bfloat16* tprev = vmax + size_t(par ^ 1) * slots * nt + tid;
     // previous row's vector at slot k: re-read and bin it when its maximum reaches tau
@@ -236,7 +246,10 @@ __global__ void __launch_bounds__(kStatThreads, 1) rowstats_bf16_kernel(const Se
     if (cur) {
       int i = tid, k = 0;
       for (; i + 3 * nt < nvec; i += 4 * nt, k += 4) {  // four 16-byte HBM loads in flight
-        const uint4 u0 = row[i], u1 = row[i + nt], u2 = row[i + 2 * nt], u3 = row[i + 3 * nt];
+        uint4 u0 = f0, u1 = f1, u2 = f2, u3 = f3;  // first batch: prefetched
+        if (k) {
+          u0 = row[i]; u1 = row[i + nt]; u2 = row[i + 2 * nt]; u3 = row[i + 3 * nt];
+        }
         if (pact) {
           bin_prev(k);
           bin_prev(k + 1);
@@ -265,9 +278,13 @@ __global__ void __launch_bounds__(kStatThreads, 1) rowstats_bf16_kernel(const Se
       }
     }
     if (!cur) break;
+    if (full4 && r + gridDim.x < rows) {  // next row's first batch, in flight during the reductions
+      const uint4* rn = reinterpret_cast<const uint4*>(base + (r + gridDim.x) * a.ld);
+      f0 = rn[tid]; f1 = rn[tid + nt]; f2 = rn[tid + 2 * nt]; f3 = rn[tid + 3 * nt];
+    }
     const float mt = acc.m;
     const float m = block_reduce(mt, true, red);
-    const float sum = block_reduce((acc.s0 + acc.s1) * ex2_approx((mt - m) * kLog2e), false, red);
+    const float sum = block_reduce((acc.s.x + acc.s.y) * ex2_approx((mt - m) * kLog2e), false, red);
     float tau = -INFINITY;
     if (a.W <= 32 * nwarps) {
       const int kth = (a.W + nwarps - 1) / nwarps - 1;

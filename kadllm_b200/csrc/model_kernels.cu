@@ -201,6 +201,75 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
   for (int e = 0; e < EPL; ++e) dst[e] = __float2bfloat16_rn(v[e]);
 }
 
+// Head dim 256 with 16-byte rows: one warp per (row, head), 8 consecutive
+// elements (one 16-byte access) per lane, 32-bit index arithmetic.  Same
+// arithmetic and rounding points as qk_norm_rope_kernel.
+__global__ void __launch_bounds__(256) qk_norm_rope_d256_kernel(
+    const __nv_bfloat16* proj, int64_t ld_proj, int Hq, int HK, const float* qw, const float* kw, float eps,
+    const __nv_bfloat16* cos_tab, const __nv_bfloat16* sin_tab, int rot, const int64_t* pos_of_row,
+    int64_t pos_base, int rows_per_seq, __nv_bfloat16* q_out, int64_t sq_row, int64_t sq_h,
+    __nv_bfloat16* k_out, int64_t sk_seq, int64_t sk_pos, int64_t sk_h, __nv_bfloat16* v_out, int64_t sv_seq,
+    int64_t sv_pos, int64_t sv_h, uint32_t items) {
+  constexpr int D = 256;
+  const int heads = Hq + 2 * HK;
+  const uint32_t item = blockIdx.x * 8u + (threadIdx.x >> 5);
+  if (item >= items) return;  // whole warps leave together
+  const uint32_t r = item / uint32_t(heads);
+  const int h = int(item - r * uint32_t(heads));
+  const int lane = threadIdx.x & 31;
+  const uint32_t s = r / uint32_t(rows_per_seq), p = r - s * uint32_t(rows_per_seq);
+  const int64_t pos = pos_base + (pos_of_row ? pos_of_row[r] : int64_t(p));
+  const __nv_bfloat16* src = proj + int64_t(r) * ld_proj;
+  if (h < Hq) src += h * 2 * D;  // q of head h (its gate follows it)
+  else if (h < Hq + HK) src += Hq * 2 * D + (h - Hq) * D;
+  else src += Hq * 2 * D + HK * D + (h - Hq - HK) * D;
+  const uint4 raw = *reinterpret_cast<const uint4*>(src + lane * 8);
+  if (h >= Hq + HK) {  // value: plain copy into the cache / suffix layout
+    *reinterpret_cast<uint4*>(v_out + s * sv_seq + p * sv_pos + (h - Hq - HK) * sv_h + lane * 8) = raw;
+    return;
+  }
+  const uint32_t rw[4] = {raw.x, raw.y, raw.z, raw.w};
+  float v[8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = bf2f(rw[j]);
+    v[2 * j] = f.x;
+    v[2 * j + 1] = f.y;
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) ss += v[e] * v[e];
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(ss / float(D) + eps);
+  const float* w = (h < Hq ? qw : kw) + lane * 8;
+  const float4 w0 = *reinterpret_cast<const float4*>(w), w1 = *reinterpret_cast<const float4*>(w + 4);
+  const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+  for (int e = 0; e < 8; ++e) v[e] = bf16r((v[e] * inv) * (1.0f + wv[e]));
+  // partial rotary: dims [0, rot) rotate with the partner half rot/2 away (rot/2 % 8 == 0)
+  const int half = rot / 2;
+  float pv[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) pv[e] = __shfl_xor_sync(0xffffffffu, v[e], half / 8);
+  if (lane * 8 < rot) {
+    const uint4 cr = *reinterpret_cast<const uint4*>(cos_tab + pos * rot + lane * 8);
+    const uint4 sr = *reinterpret_cast<const uint4*>(sin_tab + pos * rot + lane * 8);
+    const uint32_t cw[4] = {cr.x, cr.y, cr.z, cr.w}, sw[4] = {sr.x, sr.y, sr.z, sr.w};
+    const bool lo = lane * 8 < half;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 c = bf2f(cw[j]), sn = bf2f(sw[j]);
+      const float r0 = lo ? -pv[2 * j] : pv[2 * j], r1 = lo ? -pv[2 * j + 1] : pv[2 * j + 1];  // rotate_half
+      v[2 * j] = bf16r(bf16r(v[2 * j] * c.x) + bf16r(r0 * sn.x));
+      v[2 * j + 1] = bf16r(bf16r(v[2 * j + 1] * c.y) + bf16r(r1 * sn.y));
+    }
+  }
+  __nv_bfloat16* dst = h < Hq ? q_out + int64_t(r) * sq_row + h * sq_h + lane * 8
+                              : k_out + s * sk_seq + p * sk_pos + (h - Hq) * sk_h + lane * 8;
+  *reinterpret_cast<uint4*>(dst) =
+      make_uint4(bf2_pack(v[0], v[1]), bf2_pack(v[2], v[3]), bf2_pack(v[4], v[5]), bf2_pack(v[6], v[7]));
+}
+
 }  // namespace
 }  // namespace kb
 
@@ -289,6 +358,18 @@ extern "C" int kadllm_qk_norm_rope(const void* proj, int64_t ld_proj, int64_t q_
   auto Q = static_cast<__nv_bfloat16*>(q_out);
   auto K = static_cast<__nv_bfloat16*>(k_out);
   auto Vv = static_cast<__nv_bfloat16*>(v_out);
+  const auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+  if (head_dim == 256 && items < (1ll << 31) && rows_per_seq < (1ll << 31) && al16(proj) && ld_proj % 8 == 0 &&
+      al16(q_out) && al16(k_out) && al16(v_out) && al16(q_weight) && al16(k_weight) && al16(cos_tab) &&
+      al16(sin_tab) && sq_row % 8 == 0 && sq_h % 8 == 0 && sk_seq % 8 == 0 && sk_pos % 8 == 0 && sk_h % 8 == 0 &&
+      sv_seq % 8 == 0 && sv_pos % 8 == 0 && sv_h % 8 == 0 && (rotary_dim / 2) % 8 == 0 && rotary_dim % 8 == 0) {
+    qk_norm_rope_d256_kernel<<<grid, 256, 0, s>>>(P, ld_proj, int(q_heads), int(kv_heads), q_weight, k_weight, eps, C,
+                                                  S, int(rotary_dim), pos_of_row, pos_base, int(rows_per_seq), Q,
+                                                  sq_row, sq_h, K, sk_seq, sk_pos, sk_h, Vv, sv_seq, sv_pos, sv_h,
+                                                  uint32_t(items));
+    KB_CHECK_LAUNCH("qk_norm_rope launch");
+    return KADLLM_OK;
+  }
 #define KB_QK_CASE(DD)                                                                                          \
   if (head_dim == DD) {                                                                                         \
     qk_norm_rope_kernel<DD><<<grid, 256, 0, s>>>(P, ld_proj, int(q_heads), int(kv_heads), q_weight, k_weight, eps, \
