@@ -28,6 +28,11 @@ def work_of(name: str, args: tuple) -> tuple[str, float] | None:
         read = rows * (conv_dim + HV * DV + 2 * HV) * 2
         write = rows * HV * DV * 2 + B * HV * DK * DV * 2 + B * conv_dim * 4 * 2
         return "hbm", float(read + write)
+    if name == "kadllm_attention_tiled":
+        B, W, T, H, HK, L, D = args[24:31]
+        if args[32]:  # causal prefill
+            return "tensor", float(4 * B * H * D * L * (L + 1) / 2)
+        return "tensor", float(4 * B * W * T * H * D * L + 4 * B * W * H * D * T * (T + 1) / 2)
     if name == "kadllm_causal_attention":
         B, L, H, HK, D = args[17:22]
         return "tensor", float(4 * B * H * D * L * (L + 1) / 2)
@@ -50,6 +55,24 @@ def work_of(name: str, args: tuple) -> tuple[str, float] | None:
     if name == "kadllm_add_rmsnorm":
         rows, H = args[6], args[9]
         return "hbm", float(rows * H * 2 * (4 if args[1] else 2))
+    return None
+
+
+def measured_traffic(name: str, args: tuple) -> float | None:
+    """DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one call, from
+    one ncu capture of the benchmark's shape of that call on a B200; None for
+    shapes that were not captured."""
+    if name == "kadllm_gdn_prefill_split" and tuple(args[13:19]) == (32, 1024, 16, 16, 128, 128):
+        # prep 407.1 + 557.2 MB, tcgen05 scan 605.0 + 132.7 MB, gated norm 270.5 + 92.3 MB
+        return 2064.8e6
+    if name == "kadllm_gdn_mixer_replay" and tuple(args[11:13]) == (32, 256) and tuple(args[14:18]) == (16, 16, 128, 128):
+        return {1: 186.4e6, 2: 359.3e6}.get(args[13])  # T = 1: 165.5 + 20.9 MB; T = 2: 306.2 + 53.2 MB
+    if name == "kadllm_attention_tiled" and (args[24], *args[27:31]) == (32, 8, 2, 1024, 256):
+        if args[32]:  # causal prefill: 335.7 + 110.6 MB
+            return 446.3e6
+        return 283.1e6 if tuple(args[25:27]) == (256, 2) else None  # decode T = 2: 235.0 + 48.0 MB
+    if name == "kadllm_beam_select" and tuple(args[10:13]) == (32, 256, 248320):
+        return 4822.0e6  # rowstats 4276.2 + 5.2 MB, collect 537.0 + 3.6 MB
     return None
 
 
@@ -87,6 +110,7 @@ class KernelTimer:
 def roofline_for(name: str, timer: KernelTimer, cfg, peaks: dict, peak_kind: str) -> dict:
     """Roofline of kernel `name` over the timed calls: achieved = work / duration."""
     work, ms, calls, bound = 0.0, 0.0, 0, None
+    traffic: float | None = 0.0
     for n, args, s, e in timer.records:
         if n != name:
             continue
@@ -97,6 +121,8 @@ def roofline_for(name: str, timer: KernelTimer, cfg, peaks: dict, peak_kind: str
         work += amount
         ms += s.elapsed_time(e)
         calls += 1
+        t = measured_traffic(n, args)
+        traffic = None if traffic is None or t is None else traffic + t
     if not calls:
         return {"kernel": name, "bound": None, "achieved": None, "peak": None, "unit": None, "frac": None,
                 "traffic": None}
@@ -109,6 +135,8 @@ def roofline_for(name: str, timer: KernelTimer, cfg, peaks: dict, peak_kind: str
         peak = peaks["hbm_gbs"]
         unit, per_launch = "GB/s", work / calls
     return {"kernel": name, "bound": "tensor" if bound == "tensor" else "hbm", "achieved": achieved,
-            "peak": peak, "unit": unit, "frac": achieved / peak, "traffic": None, "launches": calls,
+            "peak": peak, "unit": unit, "frac": achieved / peak,
+            "traffic": None if traffic is None else traffic / calls, "traffic_unit": "bytes per launch (ncu)",
+            "launches": calls,
             "avg_launch_ms": ms / calls, "work_per_launch": per_launch,
             "peak_kind": f"{peak_kind} ({'bf16 burst' if bound == 'tensor' else 'HBM copy'})"}
