@@ -16,13 +16,15 @@
 // dims) for O += P V, and staged with one bulk copy.  kadllm_kv_tile builds it
 // from the [B, HK, L, D] cache, zero-padding the last block.
 //
-// One CTA = 128 query rows of one (request, kv head), 4 warps = the 4 TMEM lane
-// quadrants (thread r owns query row r).  TMEM: S double buffer (2 x 64
-// columns), O (256 columns).  Per key block j: MMA_S(j+1) runs while the
-// threads turn S(j) into probabilities (online softmax in the exp2 domain; the
-// reference maximum only moves when a row maximum exceeds it by 8, so O is
-// rescaled rarely), write P (BF16, K-major core tile) to shared memory, and one
-// thread issues O += P V(j).  K and V blocks are double-buffered, refilled as
+// One CTA = 128 query rows of one (request, kv head), 8 warps.  Warps 0-3 are
+// the 4 TMEM lane quadrants: thread r owns query row r and runs its online
+// softmax.  One thread of warp 4 issues every MMA and bulk copy, so no softmax
+// warp waits for a copy; in the epilogue warps 4-7 take columns 128-255 of the
+// same rows.  TMEM: S double buffer (2 x 64 columns), O (256 columns).  Per key
+// block j: MMA_S(j+1) runs while the row threads turn S(j) into probabilities
+// (exp2 domain; the reference maximum only moves when a row maximum exceeds it
+// by 8, so O is rescaled rarely) and write P (BF16, K-major core tile) to
+// shared memory; after the block barrier the issuer starts O += P V(j).  K and V blocks are double-buffered, refilled as
 // soon as the MMA that read them completes.  Every mbarrier wait is bounded and
 // reports through a status word.
 #include "tcgen05.cuh"
@@ -35,6 +37,8 @@ constexpr int kRows = 128;   // query rows per CTA
 constexpr int kBlk = 64;     // keys per block
 constexpr int kTile = kBlk * kD * 2;  // bytes of one K or V block (32 KB)
 constexpr int kSufMax = 8;
+constexpr int kThreads = 2 * kRows;  // warps 0-3: one query row per thread (TMEM lane); warps 4-7: issue + epilogue
+constexpr int kIssuer = kRows;       // thread that issues the MMAs and the bulk copies (warp 4)
 
 struct AttnTcArgs {
   const __nv_bfloat16* q; int64_t sq_row, sq_t, sq_h;  // decode: row = beam row; causal: row = token b*L + pos
@@ -63,7 +67,7 @@ struct AttnTcSmem {
 };
 
 template <bool CAUSAL>
-__global__ void __launch_bounds__(128, 1) attn_tc_kernel(const AttnTcArgs a) {
+__global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a) {
   using M = AttnTcSmem;
   constexpr long long kWait = 1ll << 31;
   constexpr uint32_t kIdS = tc::idesc_bf16(kRows, kBlk, 0, 0);  // S = Q K^T: K-major Q and K
@@ -75,11 +79,13 @@ __global__ void __launch_bounds__(128, 1) attn_tc_kernel(const AttnTcArgs a) {
   uint64_t* barO = ldK + 6;
   uint32_t* slot = reinterpret_cast<uint32_t*>(smem + M::slot);
   const int tid = threadIdx.x, warp = tid >> 5;
+  const int row = tid & (kRows - 1), half = tid / kRows;  // query row; half 1 = warps 4-7
+  const bool soft = half == 0;                             // runs the row's online softmax
   const int b = blockIdx.y / a.HK, hk = blockIdx.y % a.HK;
   const int TG = a.T * a.G;
   const int R = CAUSAL ? a.L * a.G : a.W * TG;
   const int row0 = blockIdx.x * kRows;
-  const int gr = row0 + tid;  // this thread's query row (= TMEM lane tid)
+  const int gr = row0 + row;  // this thread's query row (= TMEM lane row)
   const bool rvalid = gr < R;
   int beam = 0, t = 0, g = 0, pos = 0;
   if (CAUSAL) {
@@ -107,8 +113,8 @@ __global__ void __launch_bounds__(128, 1) attn_tc_kernel(const AttnTcArgs a) {
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   if (warp == 0) tc::tmem_alloc(slot, 512);
-  for (int c = 0; c < kD / 8; ++c) {
-    unsigned char* dst = smem + M::q + M::off(tid, c, kD / 8);
+  for (int c = half * (kD / 16); c < (half + 1) * (kD / 16); ++c) {  // each half stages 16 of the row's chunks
+    unsigned char* dst = smem + M::q + M::off(row, c, kD / 8);
     if (rvalid) cp_async16(dst, a.q + qoff + c * 8);
     else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
   }
@@ -117,9 +123,9 @@ __global__ void __launch_bounds__(128, 1) attn_tc_kernel(const AttnTcArgs a) {
   __syncthreads();  // barriers initialised, TMEM address published
   tc::fence_after();
   const uint32_t tmem = *slot;
-  const uint32_t lane_off = uint32_t(warp * 32) << 16;
+  const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;  // TMEM lane quadrant of this warp
   const uint32_t tO = tmem + 128 + lane_off;
-  int issued_k[2] = {0, 0}, issued_v[2] = {0, 0};  // loads issued per buffer (thread 0)
+  int issued_k[2] = {0, 0}, issued_v[2] = {0, 0};  // loads issued per buffer (issuer thread)
   auto load_k = [&](int j) {
     const int s = j & 1;
     tc::mbar_expect_tx(ldK + s, uint32_t(kTile));
@@ -148,7 +154,7 @@ __global__ void __launch_bounds__(128, 1) attn_tc_kernel(const AttnTcArgs a) {
                    tc::smem_desc(sbase + M::v + s * kTile + kk * 8192, 4096, 128), kIdO, j > 0 || kk > 0);
     tc::commit(barO);
   };
-  if (tid == 0 && nb > 0) {
+  if (tid == kIssuer && nb > 0) {
     load_k(0);
     load_v(0);
     if (nb > 1) {
@@ -160,7 +166,7 @@ __global__ void __launch_bounds__(128, 1) attn_tc_kernel(const AttnTcArgs a) {
   tc::fence_async_smem();
   __syncthreads();  // Q tile staged
   bool ok = true;
-  if (tid == 0 && nb > 0) {
+  if (tid == kIssuer && nb > 0) {
     ok = tc::mbar_wait(ldK, 0, kWait) && ok;
     tc::fence_after();
     issue_s(0);
@@ -171,76 +177,78 @@ __global__ void __launch_bounds__(128, 1) attn_tc_kernel(const AttnTcArgs a) {
   float m_ref = -INFINITY, l = 0.f;            // exp2-domain reference maximum, running sum
   for (int j = 0; j < nb; ++j) {
     const int sb = j & 1;
-    if (tid == 0 && j + 1 < nb) {  // MMA_S(j+1) overlaps this block's softmax
+    if (tid == kIssuer && j + 1 < nb) {  // MMA_S(j+1) overlaps this block's softmax
       ok = tc::mbar_wait(ldK + ((j + 1) & 1), uint32_t((j + 1) >> 1) & 1u, kWait) && ok;
       tc::fence_after();
       issue_s(j + 1);
     }
-    ok = tc::mbar_wait(barS + sb, uint32_t(j >> 1) & 1u, kWait) && ok;
-    tc::fence_after();
-    float x[kBlk];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      uint32_t r[32];
-      tc::ld32(tmem + lane_off + sb * kBlk + h * 32, r);
-      tc::wait_ld();
-#pragma unroll
-      for (int c = 0; c < 32; ++c) x[h * 32 + c] = __uint_as_float(r[c]);
-    }
-    if (j * kBlk + kBlk - 1 > key_lim) {  // partial block: keys past this row's limit drop out
-#pragma unroll
-      for (int c = 0; c < kBlk; ++c)
-        if (j * kBlk + c > key_lim) x[c] = -INFINITY;
-    }
-    float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-    for (int c = 0; c < kBlk; ++c) m4[c & 3] = fmaxf(m4[c & 3], x[c]);
-    const float bmax = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * a.scale_log2;
-    float f = 1.f;
-    bool resc = false;
-    if (bmax > m_ref + 8.f) {  // move the reference (always on the first finite block)
-      f = m_ref == -INFINITY ? 0.f : fast_ex2(m_ref - bmax);
-      m_ref = bmax;
-      l *= f;
-      resc = true;
-    }
-    const float mr = m_ref == -INFINITY ? 0.f : m_ref;  // all scores are -inf while m_ref is
-    uint32_t pk[kBlk / 2];
-    float s4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int c = 0; c < kBlk; c += 2) {
-      const float p0 = fast_ex2(fmaf(x[c], a.scale_log2, -mr));
-      const float p1 = fast_ex2(fmaf(x[c + 1], a.scale_log2, -mr));
-      s4[(c >> 1) & 3] += p0 + p1;
-      pk[c / 2] = bf2_pack(p0, p1);
-    }
-    l += (s4[0] + s4[1]) + (s4[2] + s4[3]);
-    if (j > 0) {  // MMA_O(j-1) complete: P is free and O is stable
-      ok = tc::mbar_wait(barO, uint32_t(j - 1) & 1u, kWait) && ok;
+    if (soft) {  // this row's online softmax over block j, P(j) into shared memory
+      ok = tc::mbar_wait(barS + sb, uint32_t(j >> 1) & 1u, kWait) && ok;
       tc::fence_after();
-      if (resc) {
-#pragma unroll 1
-        for (int piece = 0; piece < kD / 32; ++piece) {
-          uint32_t r[32];
-          tc::ld32(tO + piece * 32, r);
-          tc::wait_ld();
+      float x[kBlk];
 #pragma unroll
-          for (int c = 0; c < 32; ++c) r[c] = __float_as_uint(__uint_as_float(r[c]) * f);
-          tc::st32(tO + piece * 32, r);
-        }
-        tc::wait_st();
+      for (int h = 0; h < 2; ++h) {
+        uint32_t r[32];
+        tc::ld32(tmem + lane_off + sb * kBlk + h * 32, r);
+        tc::wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) x[h * 32 + c] = __uint_as_float(r[c]);
       }
-    }
+      if (j * kBlk + kBlk - 1 > key_lim) {  // partial block: keys past this row's limit drop out
 #pragma unroll
-    for (int c = 0; c < kBlk / 8; ++c)
-      *reinterpret_cast<uint4*>(smem + M::p + M::off(tid, c, kBlk / 8)) =
-          make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        for (int c = 0; c < kBlk; ++c)
+          if (j * kBlk + c > key_lim) x[c] = -INFINITY;
+      }
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < kBlk; ++c) m4[c & 3] = fmaxf(m4[c & 3], x[c]);
+      const float bmax = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * a.scale_log2;
+      float f = 1.f;
+      bool resc = false;
+      if (bmax > m_ref + 8.f) {  // move the reference (always on the first finite block)
+        f = m_ref == -INFINITY ? 0.f : fast_ex2(m_ref - bmax);
+        m_ref = bmax;
+        l *= f;
+        resc = true;
+      }
+      const float mr = m_ref == -INFINITY ? 0.f : m_ref;  // all scores are -inf while m_ref is
+      uint32_t pk[kBlk / 2];
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < kBlk; c += 2) {
+        const float p0 = fast_ex2(fmaf(x[c], a.scale_log2, -mr));
+        const float p1 = fast_ex2(fmaf(x[c + 1], a.scale_log2, -mr));
+        s4[(c >> 1) & 3] += p0 + p1;
+        pk[c / 2] = bf2_pack(p0, p1);
+      }
+      l += (s4[0] + s4[1]) + (s4[2] + s4[3]);
+      if (j > 0) {  // MMA_O(j-1) complete: P is free and O is stable
+        ok = tc::mbar_wait(barO, uint32_t(j - 1) & 1u, kWait) && ok;
+        tc::fence_after();
+        if (resc) {
+#pragma unroll 1
+          for (int piece = 0; piece < kD / 32; ++piece) {
+            uint32_t r[32];
+            tc::ld32(tO + piece * 32, r);
+            tc::wait_ld();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) r[c] = __float_as_uint(__uint_as_float(r[c]) * f);
+            tc::st32(tO + piece * 32, r);
+          }
+          tc::wait_st();
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < kBlk / 8; ++c)
+        *reinterpret_cast<uint4*>(smem + M::p + M::off(row, c, kBlk / 8)) =
+            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+    }
     tc::fence_async_smem();
     tc::fence_before();
     ok = __syncthreads_and(ok);  // P staged, S(j) and O rows read / rescaled
     if (!ok) break;
     tc::fence_after();
-    if (tid == 0) {
+    if (tid == kIssuer) {
       ok = tc::mbar_wait(ldV + sb, uint32_t(j >> 1) & 1u, kWait) && ok;
       issue_o(j);
       if (j + 2 < nb) load_k(j + 2);              // K(j) was read by MMA_S(j), complete
@@ -265,7 +273,7 @@ __global__ void __launch_bounds__(128, 1) attn_tc_kernel(const AttnTcArgs a) {
   const int nbeams = CAUSAL ? 0 : row_hi / TG - beam_lo + 1;
   const bool suf_smem = !CAUSAL && int64_t(nbeams) * a.T * kD * 2 * 2 <= int64_t(2) * kTile;
   if (a.gate) {
-    for (int i = tid; i < kRows * (kD / 8); i += kRows) {
+    for (int i = tid; i < kRows * (kD / 8); i += kThreads) {
       const int r = i / (kD / 8), c = i % (kD / 8);
       if (row0 + r > row_hi) continue;
       int rb, rt, rg, rp;
@@ -278,7 +286,7 @@ __global__ void __launch_bounds__(128, 1) attn_tc_kernel(const AttnTcArgs a) {
     }
   }
   if (suf_smem) {
-    for (int i = tid; i < nbeams * a.T * 2 * (kD / 8); i += kRows) {
+    for (int i = tid; i < nbeams * a.T * 2 * (kD / 8); i += kThreads) {
       const int c = i % (kD / 8), rest = i / (kD / 8), kv = rest & 1, bs = rest >> 1, sidx = bs % a.T, bi = bs / a.T;
       const int64_t br = int64_t(b) * a.W + beam_lo + bi;
       const __nv_bfloat16* src = kv ? a.sv + br * a.ssv_row + int64_t(sidx) * a.ssv_t + int64_t(hk) * a.ssv_h
@@ -300,7 +308,7 @@ __global__ void __launch_bounds__(128, 1) attn_tc_kernel(const AttnTcArgs a) {
   float psuf[kSufMax];
 #pragma unroll
   for (int sidx = 0; sidx < kSufMax; ++sidx) psuf[sidx] = 0.f;
-  if (!CAUSAL && rvalid) {
+  if (soft && !CAUSAL && rvalid) {
     float xs[kSufMax];
 #pragma unroll
     for (int sidx = 0; sidx < kSufMax; ++sidx) {
@@ -310,7 +318,7 @@ __global__ void __launch_bounds__(128, 1) attn_tc_kernel(const AttnTcArgs a) {
         float acc4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 8
         for (int c = 0; c < kD / 8; ++c) {
-          const uint4 qv = *reinterpret_cast<const uint4*>(smem + M::q + M::off(tid, c, kD / 8));
+          const uint4 qv = *reinterpret_cast<const uint4*>(smem + M::q + M::off(row, c, kD / 8));
           const uint4 kv = *reinterpret_cast<const uint4*>(kp + c * 8);
           const uint32_t* qw = reinterpret_cast<const uint32_t*>(&qv);
           const uint32_t* kw = reinterpret_cast<const uint32_t*>(&kv);
@@ -332,11 +340,25 @@ __global__ void __launch_bounds__(128, 1) attn_tc_kernel(const AttnTcArgs a) {
       ssum += psuf[sidx];
     }
   }
-  const float inv = 1.f / ssum;
+  // the row's normaliser, prefix weight and suffix probabilities, shared with the
+  // warp-4-7 thread of the same row through the (free) P buffer
+  float* sc = reinterpret_cast<float*>(smem + M::p) + row * (2 + kSufMax);
+  static_assert(size_t(kRows) * (2 + kSufMax) * 4 <= size_t(kRows) * kBlk * 2, "row scalars fit the P buffer");
+  if (soft) {
+    sc[0] = alpha;
+    sc[1] = 1.f / ssum;
+#pragma unroll
+    for (int sidx = 0; sidx < kSufMax; ++sidx) sc[2 + sidx] = psuf[sidx];
+  }
+  __syncthreads();
+  alpha = sc[0];
+  const float inv = sc[1];
+#pragma unroll
+  for (int sidx = 0; sidx < kSufMax; ++sidx) psuf[sidx] = sc[2 + sidx];
   __nv_bfloat16* op = CAUSAL ? a.out + (int64_t(b) * a.L + pos) * a.so_row + int64_t(hq) * a.so_h
                              : a.out + brow * a.so_row + int64_t(t) * a.so_t + int64_t(hq) * a.so_h;
 #pragma unroll 1
-  for (int piece = 0; piece < kD / 32; ++piece) {
+  for (int piece = half * (kD / 64); piece < (half + 1) * (kD / 64); ++piece) {  // this half's 128 columns
     uint32_t r[32];
     tc::ld32(tO + piece * 32, r);  // whole warp (aligned), stores are per row below
     tc::wait_ld();
@@ -368,7 +390,7 @@ __global__ void __launch_bounds__(128, 1) attn_tc_kernel(const AttnTcArgs a) {
       uint32_t* rw = reinterpret_cast<uint32_t*>(&res);
       uint4 gv = make_uint4(0u, 0u, 0u, 0u);
       const int c = piece * 4 + q4;
-      if (a.gate) gv = *reinterpret_cast<const uint4*>(smem + M::v + tid * 512 + ((c ^ (tid & 31)) * 16));
+      if (a.gate) gv = *reinterpret_cast<const uint4*>(smem + M::v + row * 512 + ((c ^ (row & 31)) * 16));
       const uint32_t* gw = reinterpret_cast<const uint32_t*>(&gv);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -383,7 +405,7 @@ __global__ void __launch_bounds__(128, 1) attn_tc_kernel(const AttnTcArgs a) {
       *reinterpret_cast<uint4*>(op + piece * 32 + q4 * 8) = res;
     }
   }
-  if (!ok && tid == 0) {  // a wait timed out: report, give in-flight copies a bounded time
+  if (!ok && tid == kIssuer) {  // a wait timed out: report, give in-flight copies a bounded time
     atomicOr(a.status, 1u);
     for (int s = 0; s < 2; ++s) {
       if (issued_k[s] > 0) tc::mbar_wait(ldK + s, uint32_t(issued_k[s] - 1) & 1u, kWait);
@@ -426,7 +448,7 @@ int launch_attn_tc(const AttnTcArgs& a, cudaStream_t stream) {
   }
   const int64_t R = CAUSAL ? int64_t(a.L) * a.G : int64_t(a.W) * a.T * a.G;
   dim3 grid(unsigned((R + kRows - 1) / kRows), unsigned(a.B * a.HK));
-  kern<<<grid, kRows, AttnTcSmem::bytes, stream>>>(a);
+  kern<<<grid, kThreads, AttnTcSmem::bytes, stream>>>(a);
   KB_CHECK_LAUNCH("tiled attention launch");
   return KADLLM_OK;
 }
