@@ -16,15 +16,17 @@
 // dims) for O += P V, and staged with one bulk copy.  kadllm_kv_tile builds it
 // from the [B, HK, L, D] cache, zero-padding the last block.
 //
-// One CTA = 128 query rows of one (request, kv head), 8 warps.  Warps 0-3 are
-// the 4 TMEM lane quadrants: thread r owns query row r and runs its online
-// softmax.  One thread of warp 4 issues every MMA and bulk copy, so no softmax
-// warp waits for a copy; in the epilogue warps 4-7 take columns 128-255 of the
-// same rows.  TMEM: S double buffer (2 x 64 columns), O (256 columns).  Per key
-// block j: MMA_S(j+1) runs while the row threads turn S(j) into probabilities
-// (exp2 domain; the reference maximum only moves when a row maximum exceeds it
-// by 8, so O is rescaled rarely) and write P (BF16, K-major core tile) to
-// shared memory; after the block barrier the issuer starts O += P V(j).  K and V blocks are double-buffered, refilled as
+// One CTA = 128 query rows of one (request, kv head), 9 warps.  Query row r
+// (TMEM lane r) has two threads, r in warps 0-3 and r + 128 in warps 4-7 (the
+// same lane quadrant): they split each block's 64 key columns and the 256
+// output columns in halves, exchanging the block maximum through shared memory
+// so that both move the softmax reference identically.  Warp 8 issues every
+// MMA and bulk copy, so no softmax thread waits for a copy.  TMEM: S double
+// buffer (2 x 64 columns), O (256 columns).  Per key block j: MMA_S(j+1) runs
+// while the row threads turn S(j) into probabilities (exp2 domain; the
+// reference maximum only moves when a row maximum exceeds it by 8, so O is
+// rescaled rarely) and write P (BF16, K-major core tile) to shared memory;
+// after the block barrier the issuer starts O += P V(j).  K and V blocks are double-buffered, refilled as
 // soon as the MMA that read them completes.  Every mbarrier wait is bounded and
 // reports through a status word.
 #include "tcgen05.cuh"
@@ -37,8 +39,9 @@ constexpr int kRows = 128;   // query rows per CTA
 constexpr int kBlk = 64;     // keys per block
 constexpr int kTile = kBlk * kD * 2;  // bytes of one K or V block (32 KB)
 constexpr int kSufMax = 8;
-constexpr int kThreads = 2 * kRows;  // warps 0-3: one query row per thread (TMEM lane); warps 4-7: issue + epilogue
-constexpr int kIssuer = kRows;       // thread that issues the MMAs and the bulk copies (warp 4)
+constexpr int kRowThreads = 2 * kRows;  // two threads per query row: key columns / output columns split in halves
+constexpr int kThreads = kRowThreads + 32;  // + one warp that issues the MMAs and the bulk copies
+constexpr int kIssuer = kRowThreads;        // its issuing thread
 
 struct AttnTcArgs {
   const __nv_bfloat16* q; int64_t sq_row, sq_t, sq_h;  // decode: row = beam row; causal: row = token b*L + pos
@@ -58,7 +61,8 @@ struct AttnTcSmem {
   static constexpr size_t k = q + size_t(kRows) * kD * 2;        // K blocks [2]
   static constexpr size_t v = k + 2 * size_t(kTile);             // V blocks [2]
   static constexpr size_t p = v + 2 * size_t(kTile);             // P [128 rows][64 keys] K-major core tile
-  static constexpr size_t bar = p + size_t(kRows) * kBlk * 2;    // ldK[2], ldV[2], S[2], O
+  static constexpr size_t bm = p + size_t(kRows) * kBlk * 2;     // [2 halves][128 rows] fp32 exchange
+  static constexpr size_t bar = bm + size_t(2) * kRows * 4;       // ldK[2], ldV[2], S[2], O
   static constexpr size_t slot = bar + 7 * 8;
   static constexpr size_t bytes = slot + 8;
   static_assert(bytes <= 232448, "shared memory");
@@ -79,8 +83,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
   uint64_t* barO = ldK + 6;
   uint32_t* slot = reinterpret_cast<uint32_t*>(smem + M::slot);
   const int tid = threadIdx.x, warp = tid >> 5;
-  const int row = tid & (kRows - 1), half = tid / kRows;  // query row; half 1 = warps 4-7
-  const bool soft = half == 0;                             // runs the row's online softmax
+  const int row = tid & (kRows - 1), half = (tid / kRows) & 1;  // query row, column half
+  const bool rowthr = tid < kRowThreads;                         // warps 0-7 (warp 8 only issues)
+  float* sbm = reinterpret_cast<float*>(smem + M::bm);           // partner exchange [half][row]
   const int b = blockIdx.y / a.HK, hk = blockIdx.y % a.HK;
   const int TG = a.T * a.G;
   const int R = CAUSAL ? a.L * a.G : a.W * TG;
@@ -113,7 +118,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   if (warp == 0) tc::tmem_alloc(slot, 512);
-  for (int c = half * (kD / 16); c < (half + 1) * (kD / 16); ++c) {  // each half stages 16 of the row's chunks
+  for (int c = half * (kD / 16); rowthr && c < (half + 1) * (kD / 16); ++c) {  // each half: 16 of the row's chunks
     unsigned char* dst = smem + M::q + M::off(row, c, kD / 8);
     if (rvalid) cp_async16(dst, a.q + qoff + c * 8);
     else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
@@ -177,32 +182,47 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
   float m_ref = -INFINITY, l = 0.f;            // exp2-domain reference maximum, running sum
   for (int j = 0; j < nb; ++j) {
     const int sb = j & 1;
-    if (tid == kIssuer && j + 1 < nb) {  // MMA_S(j+1) overlaps this block's softmax
-      ok = tc::mbar_wait(ldK + ((j + 1) & 1), uint32_t((j + 1) >> 1) & 1u, kWait) && ok;
-      tc::fence_after();
-      issue_s(j + 1);
+    if (tid == kIssuer) {
+      if (j + 1 < nb) {  // MMA_S(j+1) overlaps this block's softmax
+        ok = tc::mbar_wait(ldK + ((j + 1) & 1), uint32_t((j + 1) >> 1) & 1u, kWait) && ok;
+        tc::fence_after();
+        issue_s(j + 1);
+      }
+      // refill each buffer as soon as the MMA that read it has completed
+      if (j + 2 < nb) {  // K(j) was read by MMA_S(j)
+        ok = tc::mbar_wait(barS + sb, uint32_t(j >> 1) & 1u, kWait) && ok;
+        load_k(j + 2);
+      }
+      if (j >= 1 && j + 1 < nb) {  // V(j-1) was read by MMA_O(j-1)
+        ok = tc::mbar_wait(barO, uint32_t(j - 1) & 1u, kWait) && ok;
+        load_v(j + 1);
+      }
     }
-    if (soft) {  // this row's online softmax over block j, P(j) into shared memory
+    // online softmax over block j: this thread takes key columns [32 half, 32 half + 32)
+    float x[32];
+    float pm = -INFINITY;
+    if (rowthr) {
       ok = tc::mbar_wait(barS + sb, uint32_t(j >> 1) & 1u, kWait) && ok;
       tc::fence_after();
-      float x[kBlk];
+      uint32_t r[32];
+      tc::ld32(tmem + lane_off + sb * kBlk + half * 32, r);
+      tc::wait_ld();
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t r[32];
-        tc::ld32(tmem + lane_off + sb * kBlk + h * 32, r);
-        tc::wait_ld();
+      for (int c = 0; c < 32; ++c) x[c] = __uint_as_float(r[c]);
+      const int k0 = j * kBlk + half * 32;
+      if (k0 + 31 > key_lim) {  // partial block: keys past this row's limit drop out
 #pragma unroll
-        for (int c = 0; c < 32; ++c) x[h * 32 + c] = __uint_as_float(r[c]);
-      }
-      if (j * kBlk + kBlk - 1 > key_lim) {  // partial block: keys past this row's limit drop out
-#pragma unroll
-        for (int c = 0; c < kBlk; ++c)
-          if (j * kBlk + c > key_lim) x[c] = -INFINITY;
+        for (int c = 0; c < 32; ++c)
+          if (k0 + c > key_lim) x[c] = -INFINITY;
       }
       float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int c = 0; c < kBlk; ++c) m4[c & 3] = fmaxf(m4[c & 3], x[c]);
-      const float bmax = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * a.scale_log2;
+      for (int c = 0; c < 32; ++c) m4[c & 3] = fmaxf(m4[c & 3], x[c]);
+      pm = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+      sbm[half * kRows + row] = pm;
+      asm volatile("bar.sync 1, %0;\n" ::"n"(kRowThreads) : "memory");  // the two halves' maxima
+      // both halves see the same block maximum, so they move the reference identically
+      const float bmax = fmaxf(pm, sbm[(half ^ 1) * kRows + row]) * a.scale_log2;
       float f = 1.f;
       bool resc = false;
       if (bmax > m_ref + 8.f) {  // move the reference (always on the first finite block)
@@ -212,35 +232,35 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
         resc = true;
       }
       const float mr = m_ref == -INFINITY ? 0.f : m_ref;  // all scores are -inf while m_ref is
-      uint32_t pk[kBlk / 2];
+      uint32_t pk[16];
       float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < kBlk; c += 2) {
+      for (int c = 0; c < 32; c += 2) {
         const float p0 = fast_ex2(fmaf(x[c], a.scale_log2, -mr));
         const float p1 = fast_ex2(fmaf(x[c + 1], a.scale_log2, -mr));
         s4[(c >> 1) & 3] += p0 + p1;
         pk[c / 2] = bf2_pack(p0, p1);
       }
-      l += (s4[0] + s4[1]) + (s4[2] + s4[3]);
+      l += (s4[0] + s4[1]) + (s4[2] + s4[3]);  // this half's share of the row sum
       if (j > 0) {  // MMA_O(j-1) complete: P is free and O is stable
         ok = tc::mbar_wait(barO, uint32_t(j - 1) & 1u, kWait) && ok;
         tc::fence_after();
-        if (resc) {
+        if (resc) {  // this half's 128 output columns
 #pragma unroll 1
-          for (int piece = 0; piece < kD / 32; ++piece) {
-            uint32_t r[32];
-            tc::ld32(tO + piece * 32, r);
+          for (int piece = half * (kD / 64); piece < (half + 1) * (kD / 64); ++piece) {
+            uint32_t o[32];
+            tc::ld32(tO + piece * 32, o);
             tc::wait_ld();
 #pragma unroll
-            for (int c = 0; c < 32; ++c) r[c] = __float_as_uint(__uint_as_float(r[c]) * f);
-            tc::st32(tO + piece * 32, r);
+            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * f);
+            tc::st32(tO + piece * 32, o);
           }
           tc::wait_st();
         }
       }
 #pragma unroll
-      for (int c = 0; c < kBlk / 8; ++c)
-        *reinterpret_cast<uint4*>(smem + M::p + M::off(row, c, kBlk / 8)) =
+      for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<uint4*>(smem + M::p + M::off(row, half * 4 + c, kBlk / 8)) =
             make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
     }
     tc::fence_async_smem();
@@ -251,8 +271,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
     if (tid == kIssuer) {
       ok = tc::mbar_wait(ldV + sb, uint32_t(j >> 1) & 1u, kWait) && ok;
       issue_o(j);
-      if (j + 2 < nb) load_k(j + 2);              // K(j) was read by MMA_S(j), complete
-      if (j >= 1 && j + 1 < nb) load_v(j + 1);    // V(j-1) was read by MMA_O(j-1), complete
     }
   }
 
@@ -295,8 +313,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
     }
   }
   cp_async_commit();
+  if (rowthr) sbm[half * kRows + row] = l;  // the halves' partial row sums
   cp_async_wait<0>();
   __syncthreads();
+  if (rowthr) l = sbm[row] + sbm[kRows + row];
   const int64_t brow = int64_t(b) * a.W + beam;
   auto suf = [&](int sidx, int kv) -> const __nv_bfloat16* {  // this row's suffix key / value s
     if (suf_smem)
@@ -308,7 +328,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
   float psuf[kSufMax];
 #pragma unroll
   for (int sidx = 0; sidx < kSufMax; ++sidx) psuf[sidx] = 0.f;
-  if (soft && !CAUSAL && rvalid) {
+  const bool lead = rowthr && half == 0;  // computes the row's scalars
+  if (lead && !CAUSAL && rvalid) {
     float xs[kSufMax];
 #pragma unroll
     for (int sidx = 0; sidx < kSufMax; ++sidx) {
@@ -341,10 +362,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
     }
   }
   // the row's normaliser, prefix weight and suffix probabilities, shared with the
-  // warp-4-7 thread of the same row through the (free) P buffer
+  // other half's thread of the same row through the (free) P buffer
   float* sc = reinterpret_cast<float*>(smem + M::p) + row * (2 + kSufMax);
   static_assert(size_t(kRows) * (2 + kSufMax) * 4 <= size_t(kRows) * kBlk * 2, "row scalars fit the P buffer");
-  if (soft) {
+  if (lead) {
     sc[0] = alpha;
     sc[1] = 1.f / ssum;
 #pragma unroll
@@ -358,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
   __nv_bfloat16* op = CAUSAL ? a.out + (int64_t(b) * a.L + pos) * a.so_row + int64_t(hq) * a.so_h
                              : a.out + brow * a.so_row + int64_t(t) * a.so_t + int64_t(hq) * a.so_h;
 #pragma unroll 1
-  for (int piece = half * (kD / 64); piece < (half + 1) * (kD / 64); ++piece) {  // this half's 128 columns
+  for (int piece = half * (kD / 64); rowthr && piece < (half + 1) * (kD / 64); ++piece) {  // this half's columns
     uint32_t r[32];
     tc::ld32(tO + piece * 32, r);  // whole warp (aligned), stores are per row below
     tc::wait_ld();
