@@ -208,7 +208,7 @@ __device__ __forceinline__ void bin_vec(const uint4& u, float tau, float m32, ui
 
 __global__ void __launch_bounds__(kStatThreads, 1) rowstats_bf16_kernel(const SelArgs a) {
   __shared__ uint32_t hist[kRowBins];
-  __shared__ float red[33];
+  __shared__ float red[2 * 96];
   extern __shared__ __align__(16) unsigned char dsm[];
   __nv_bfloat16* vmax = reinterpret_cast<__nv_bfloat16*>(dsm);  // [2][slots][nt] vector maxima
   constexpr int nt = kStatThreads, nwarps = kStatThreads / 32;
@@ -282,10 +282,12 @@ __global__ void __launch_bounds__(kStatThreads, 1) rowstats_bf16_kernel(const Se
       const uint4* rn = reinterpret_cast<const uint4*>(base + (r + gridDim.x) * a.ld);
       f0 = rn[tid]; f1 = rn[tid + nt]; f2 = rn[tid + 2 * nt]; f3 = rn[tid + 3 * nt];
     }
+    // one exchange per row: each warp publishes its maximum, its sum rescaled to that
+    // maximum and its ceil(W/n)-th largest thread maximum; every thread combines the 32
     const float mt = acc.m;
-    const float m = block_reduce(mt, true, red);
-    const float sum = block_reduce((acc.s.x + acc.s.y) * ex2_approx((mt - m) * kLog2e), false, red);
-    float tau = -INFINITY;
+    const float wm = warp_max(mt);
+    const float ws = warp_sum(mt == -INFINITY ? 0.f : (acc.s.x + acc.s.y) * ex2_approx((mt - wm) * kLog2e));
+    float wk = -INFINITY;
     if (a.W <= 32 * nwarps) {
       const int kth = (a.W + nwarps - 1) / nwarps - 1;
       float v = mt;
@@ -297,7 +299,26 @@ __global__ void __launch_bounds__(kStatThreads, 1) rowstats_bf16_kernel(const Se
           v = (((lane & j) == 0) == ((lane & k) == 0)) ? fmaxf(v, o) : fminf(v, o);
         }
       }
-      tau = -block_reduce(-__shfl_sync(0xffffffffu, v, kth), true, red);
+      wk = __shfl_sync(0xffffffffu, v, kth);
+    }
+    float* xr = red + (par ? 96 : 0);  // alternate rows: readers of one row never meet writers of the next
+    if (lane == 0) {
+      xr[tid >> 5] = wm;
+      xr[32 + (tid >> 5)] = ws;
+      xr[64 + (tid >> 5)] = wk;
+    }
+    __syncthreads();
+    // every warp combines the 32 entries in parallel, lane w taking warp w's (nwarps == 32)
+    static_assert(nwarps == 32, "one entry per lane");
+    const float mw = xr[lane];
+    const float m = warp_max(mw);
+    const float sum = warp_sum(mw == -INFINITY ? 0.f : xr[32 + lane] * ex2_approx((mw - m) * kLog2e));
+    float tau = -INFINITY;
+    if (a.W <= 32 * nwarps) {
+      float k = xr[64 + lane];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) k = fminf(k, __shfl_xor_sync(0xffffffffu, k, o));
+      tau = k;
     }
     if (tid == 0) a.rowstat[r] = make_float2(m, logf(sum));
     prow = row;

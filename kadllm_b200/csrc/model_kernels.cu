@@ -69,9 +69,20 @@ __device__ __forceinline__ void rms_row(const float (&x)[H / 32], const float* w
   ss = warp_sum(ss);
   const float inv = 1.0f / sqrtf(ss / float(H) + eps);
 #pragma unroll
-  for (int c = 0; c < M::CHUNKS; ++c)
+  for (int c = 0; c < M::CHUNKS; ++c) {
+    float wv[M::VEC];
+    if constexpr (M::VEC == 8) {  // weights 16-byte aligned (checked by the launcher)
+      const float4 w0 = *reinterpret_cast<const float4*>(w + M::col(c, 0));
+      const float4 w1 = *reinterpret_cast<const float4*>(w + M::col(c, 4));
+      wv[0] = w0.x; wv[1] = w0.y; wv[2] = w0.z; wv[3] = w0.w;
+      wv[4] = w1.x; wv[5] = w1.y; wv[6] = w1.z; wv[7] = w1.w;
+    } else {
 #pragma unroll
-    for (int j = 0; j < M::VEC; ++j) out[c * M::VEC + j] = (x[c * M::VEC + j] * inv) * (1.0f + w[M::col(c, j)]);
+      for (int j = 0; j < M::VEC; ++j) wv[j] = w[M::col(c, j)];
+    }
+#pragma unroll
+    for (int j = 0; j < M::VEC; ++j) out[c * M::VEC + j] = (x[c * M::VEC + j] * inv) * (1.0f + wv[j]);
+  }
 }
 
 template <int H>
@@ -91,23 +102,24 @@ __global__ void __launch_bounds__(256) embed_rmsnorm_kernel(const int64_t* ids, 
 }
 
 template <int H>
-__global__ void __launch_bounds__(256) add_rmsnorm_kernel(__nv_bfloat16* x, const __nv_bfloat16* delta,
+__global__ void __launch_bounds__(256, H <= 1024 ? 4 : 2) add_rmsnorm_kernel(__nv_bfloat16* x, const __nv_bfloat16* delta,
                                                           int64_t ld_delta, const float* w, float eps,
                                                           __nv_bfloat16* normed, int64_t rows, int64_t row_step,
                                                           int64_t row_offset) {
-  const int64_t i = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (i >= rows) return;
-  const int64_t r = i * row_step + row_offset;  // residual row (normed is written densely at i)
-  float v[H / 32], d[H / 32], o[H / 32];
-  load_row<H>(x + r * H, v);
-  if (delta) {
-    load_row<H>(delta + r * ld_delta, d);
+  // grid-stride over rows: the launcher sizes the grid to the resident CTAs (no partial last wave)
+  for (int64_t i = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5); i < rows; i += int64_t(gridDim.x) * 8) {
+    const int64_t r = i * row_step + row_offset;  // residual row (normed is written densely at i)
+    float v[H / 32], d[H / 32], o[H / 32];
+    load_row<H>(x + r * H, v);
+    if (delta) {
+      load_row<H>(delta + r * ld_delta, d);
 #pragma unroll
-    for (int j = 0; j < H / 32; ++j) v[j] = bf16r(v[j] + d[j]);
-    store_row<H>(x + r * H, v);
+      for (int j = 0; j < H / 32; ++j) v[j] = bf16r(v[j] + d[j]);
+      store_row<H>(x + r * H, v);
+    }
+    rms_row<H>(v, w, eps, o);
+    store_row<H>(normed + i * H, o);
   }
-  rms_row<H>(v, w, eps, o);
-  store_row<H>(normed + i * H, o);
 }
 
 // grid (x: 512-column spans, y: rows with stride); each thread two 8-column chunks.
@@ -279,6 +291,9 @@ extern "C" int kadllm_embed_rmsnorm(const int64_t* ids, const void* table, int64
                                     float eps, void* x, void* normed, int64_t rows, int64_t hidden, void* stream) {
   KB_REQUIRE(rows >= 1 && vocab >= 1, KADLLM_EINVAL, "embed: empty");
   KB_REQUIRE(ids && table && weight && x && normed, KADLLM_EINVAL, "embed: null pointer");
+  KB_REQUIRE(((reinterpret_cast<uintptr_t>(table) | reinterpret_cast<uintptr_t>(weight) | reinterpret_cast<uintptr_t>(x) |
+               reinterpret_cast<uintptr_t>(normed)) & 15) == 0,
+             KADLLM_EINVAL, "embed: table, weight and outputs must be 16-byte aligned");
   const unsigned grid = unsigned((rows + 7) / 8);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto T = static_cast<const __nv_bfloat16*>(table);
@@ -301,7 +316,18 @@ extern "C" int kadllm_add_rmsnorm(void* x, const void* delta, int64_t ld_delta, 
                                   void* normed, int64_t rows, int64_t row_step, int64_t row_offset, int64_t hidden,
                                   void* stream) {
   KB_REQUIRE(x && weight && normed && rows >= 1 && row_step >= 1, KADLLM_EINVAL, "add_rmsnorm: bad arguments");
-  const unsigned grid = unsigned((rows + 7) / 8);
+  const auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  KB_REQUIRE(al16(x) && al16(normed) && al16(weight) && (delta == nullptr || (al16(delta) && ld_delta % 8 == 0)),
+             KADLLM_EINVAL, "add_rmsnorm: rows and weights must be 16-byte aligned");
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      sms = 148;
+  }
+  // resident CTAs of 256 threads: 4 per SM (<= 64 registers) up to hidden 1024, else 2
+  const int64_t want = (rows + 7) / 8, resident = int64_t(sms) * (hidden <= 1024 ? 4 : 2);
+  const unsigned grid = unsigned(want < resident ? want : resident);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto X = static_cast<__nv_bfloat16*>(x);
   auto Dl = static_cast<const __nv_bfloat16*>(delta);
