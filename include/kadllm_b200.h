@@ -233,6 +233,18 @@ KADLLM_API int kadllm_gdn_prefill_split(const void* proj, int64_t ld_proj, const
                                         int64_t workspace_bytes, int64_t batch, int64_t length,
                                         int64_t heads, int64_t v_heads, int64_t k_dim, int64_t v_dim,
                                         void* stream);
+/* The same over packed requests of their own lengths: request b is rows
+ * [cu_seqlens[b], cu_seqlens[b+1]) of proj / out (device int32 [batch + 1],
+ * total_rows = cu_seqlens[batch]); max_length sizes the workspace like
+ * length above.  128-dim heads (the tensor-core scan) only. */
+KADLLM_API int kadllm_gdn_prefill_split_varlen(const void* proj, int64_t ld_proj, const void* conv_weight,
+                                               void* conv_state, const float* a_log, const float* dt_bias,
+                                               const float* norm_weight, float norm_eps, void* out,
+                                               int64_t ld_out, void* state, void* workspace,
+                                               int64_t workspace_bytes, const int32_t* cu_seqlens,
+                                               int64_t total_rows, int64_t batch, int64_t max_length,
+                                               int64_t heads, int64_t v_heads, int64_t k_dim, int64_t v_dim,
+                                               void* stream);
 
 /* Tiled K / V prefix for the tensor-core attention (head_dim 256): per
  * (sequence, kv head) blocks of 64 positions, each a 32 KB core-matrix image
@@ -242,6 +254,12 @@ KADLLM_API int64_t kadllm_kv_tile_bytes(int64_t seqs, int64_t kv_heads, int64_t 
 KADLLM_API int kadllm_kv_tile(const void* src, int64_t s_seq, int64_t s_pos, int64_t s_head, int64_t seqs,
                               int64_t kv_heads, int64_t length, int64_t head_dim, void* tiles,
                               int64_t tile_bytes, void* stream);
+/* Packed sequences: sequence s is positions [cu_seqlens[s], cu_seqlens[s+1])
+ * of src [positions][HK][D] (strides s_pos, s_head); tiles sized for
+ * max_length (kadllm_kv_tile_bytes(seqs, kv_heads, max_length, head_dim)). */
+KADLLM_API int kadllm_kv_tile_varlen(const void* src, int64_t s_pos, int64_t s_head, const int32_t* cu_seqlens,
+                                     int64_t seqs, int64_t kv_heads, int64_t max_length, int64_t head_dim,
+                                     void* tiles, int64_t tile_bytes, void* stream);
 
 /* Attention over a tiled prefix on tcgen05 tensor cores (head_dim 256, BF16):
  * 128 query rows per CTA, S and O in tensor memory, bulk-copied K / V blocks.
@@ -262,6 +280,17 @@ KADLLM_API int kadllm_attention_tiled(const void* q, int64_t sq_row, int64_t sq_
                                       int64_t batch, int64_t beam_width, int64_t steps, int64_t q_heads,
                                       int64_t kv_heads, int64_t prefix_len, int64_t head_dim, float scale,
                                       int causal, void* stream);
+/* The same with prompts of their own lengths: request b's prefix has
+ * cu_seqlens[b+1] - cu_seqlens[b] tokens (tiles from kadllm_kv_tile_varlen with
+ * max_prefix_len); causal = 1: q / gate / out rows are the packed prompt rows
+ * cu_seqlens[b] + pos.  Decode rows stay (beam, t, g) per request. */
+KADLLM_API int kadllm_attention_tiled_varlen(
+    const void* q, int64_t sq_row, int64_t sq_t, int64_t sq_h, const void* k_tiles, const void* v_tiles,
+    int64_t blocks_per_head, const void* suffix_k, int64_t ssk_row, int64_t ssk_t, int64_t ssk_h,
+    const void* suffix_v, int64_t ssv_row, int64_t ssv_t, int64_t ssv_h, const void* gate, int64_t sg_row,
+    int64_t sg_t, int64_t sg_h, void* out, int64_t so_row, int64_t so_t, int64_t so_h, uint32_t* status,
+    const int32_t* cu_seqlens, int64_t batch, int64_t beam_width, int64_t steps, int64_t q_heads, int64_t kv_heads,
+    int64_t max_prefix_len, int64_t head_dim, float scale, int causal, void* stream);
 
 /* Prompt causal GQA attention (flash loop on the tensor cores) with the fused
  * output gate out = bf16(o) * bf16(sigmoid(gate)) (gate may be NULL).

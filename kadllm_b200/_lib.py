@@ -25,8 +25,12 @@ SIGNATURES: dict[str, list] = {
     "kadllm_qk_norm_rope": [P, L, L, L, L, P, P, F, P, P, L, P, L, L, P, L, L, P, L, L, L, P, L, L, L, L, P],
     "kadllm_gdn_prefill_split": [P, L, P, P, P, P, P, F, P, L, P, P, L, L, L, L, L, L, L, P],
     "kadllm_kv_tile": [P, L, L, L, L, L, L, L, P, L, P],
+    "kadllm_kv_tile_varlen": [P, L, L, P, L, L, L, L, P, L, P],
+    "kadllm_gdn_prefill_split_varlen": [P, L, P, P, P, P, P, F, P, L, P, P, L, P, L, L, L, L, L, L, L, P],
     "kadllm_attention_tiled": [P, L, L, L, P, P, L, P, L, L, L, P, L, L, L, P, L, L, L, P, L, L, L, P,
                                L, L, L, L, L, L, L, F, I, P],
+    "kadllm_attention_tiled_varlen": [P, L, L, L, P, P, L, P, L, L, L, P, L, L, L, P, L, L, L, P, L, L, L, P,
+                                      P, L, L, L, L, L, L, L, F, I, P],
     "kadllm_causal_attention": [P, L, L, P, L, L, L, P, L, L, L, P, L, L, P, L, L, L, L, L, L, L, F, P],
     "kadllm_beam_select": [P, I, L, P, P, P, P, P, P, L, L, L, L, L, L, P],
     "kadllm_beam_select_status": [P, L, L, P, P],
@@ -71,7 +75,8 @@ _ERRORS = {1: ValueError, 2: TypeError, 3: NotImplementedError, 4: RuntimeError}
 
 
 # kernels launched per successful call of each entry point (for launch accounting)
-LAUNCHES_PER_CALL = {"kadllm_beam_select": 4, "kadllm_beam_select_noalloc": 4, "kadllm_beam_select_status": 0, "kadllm_gdn_prefill_split": 3}
+LAUNCHES_PER_CALL = {"kadllm_beam_select": 4, "kadllm_beam_select_noalloc": 4, "kadllm_beam_select_status": 0,
+                     "kadllm_gdn_prefill_split": 3, "kadllm_gdn_prefill_split_varlen": 3}
 launch_count = 0
 _count_lock = threading.Lock()
 

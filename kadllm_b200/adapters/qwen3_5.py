@@ -82,6 +82,17 @@ class Qwen35GRBeamAdapter:
         logits, state = self.engine.prefill(input_ids)
         return PrefillResult(logits, state)
 
+    @torch.no_grad()
+    def prefill_varlen(self, prompts):
+        """Prompts of their own lengths in one packed prefill (no reference counterpart: the
+        reference adapter takes unpadded ``[B, L]`` only).  ``prompts``: 1-D integer tensors."""
+        for p in prompts:
+            self._check(p)
+            if p.ndim != 1 or p.numel() < 1:
+                raise ValueError("each prompt must be a nonempty 1-D tensor")
+        logits, state = self.engine.prefill_varlen(list(prompts))
+        return PrefillResult(logits, state)
+
     def _check_state(self, history, state):
         self._check(history)
         if not isinstance(state, HybridPrefix) or state.owner is not self._owner:

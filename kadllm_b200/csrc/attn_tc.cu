@@ -52,7 +52,8 @@ struct AttnTcArgs {
   const __nv_bfloat16* gate; int64_t sg_row, sg_t, sg_h;
   __nv_bfloat16* out; int64_t so_row, so_t, so_h;
   uint32_t* status;
-  int B, W, T, H, HK, G, L;
+  const int* cu;  // varlen prompts: request b's tokens are rows [cu[b], cu[b+1]) (null: b*L .. +L)
+  int B, W, T, H, HK, G, L;  // L: the (longest) prefix length
   float scale_log2;
 };
 
@@ -88,8 +89,15 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
   float* sbm = reinterpret_cast<float*>(smem + M::bm);           // partner exchange [half][row]
   const int b = blockIdx.y / a.HK, hk = blockIdx.y % a.HK;
   const int TG = a.T * a.G;
-  const int R = CAUSAL ? a.L * a.G : a.W * TG;
+  int64_t seq0 = int64_t(b) * a.L;  // first prompt row of request b
+  int Lb = a.L;                      // its prefix length
+  if (a.cu) {
+    seq0 = a.cu[b];
+    Lb = a.cu[b + 1] - a.cu[b];
+  }
+  const int R = CAUSAL ? Lb * a.G : a.W * TG;
   const int row0 = blockIdx.x * kRows;
+  if (row0 >= R) return;  // past this request's rows (varlen): the whole CTA, before any barrier or TMEM
   const int gr = row0 + row;  // this thread's query row (= TMEM lane row)
   const bool rvalid = gr < R;
   int beam = 0, t = 0, g = 0, pos = 0;
@@ -103,10 +111,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
     g = rem % a.G;
   }
   const int hq = hk * a.G + g;
-  const int64_t qoff = CAUSAL ? (int64_t(b) * a.L + pos) * a.sq_row + int64_t(hq) * a.sq_h
+  const int64_t qoff = CAUSAL ? (seq0 + pos) * a.sq_row + int64_t(hq) * a.sq_h
                               : (int64_t(b) * a.W + beam) * a.sq_row + int64_t(t) * a.sq_t + int64_t(hq) * a.sq_h;
-  int nkeys = a.L;
-  if (CAUSAL) nkeys = min(a.L, min(R - 1, row0 + kRows - 1) / a.G + 1);
+  int nkeys = Lb;
+  if (CAUSAL) nkeys = min(Lb, min(R - 1, row0 + kRows - 1) / a.G + 1);
   const int nb = (nkeys + kBlk - 1) / kBlk;
   const unsigned char* ktile = a.kt + int64_t(b * a.HK + hk) * a.nblk * kTile;
   const unsigned char* vtile = a.vt + int64_t(b * a.HK + hk) * a.nblk * kTile;
@@ -178,7 +186,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
   }
 
   // ---- key blocks ----------------------------------------------------------------------
-  const int key_lim = CAUSAL ? pos : a.L - 1;  // last key this row attends to
+  const int key_lim = CAUSAL ? pos : Lb - 1;  // last key this row attends to
   float m_ref = -INFINITY, l = 0.f;            // exp2-domain reference maximum, running sum
   for (int j = 0; j < nb; ++j) {
     const int sb = j & 1;
@@ -298,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
       row_map(r, rb, rt, rg, rp);
       const int rhq = hk * a.G + rg;
       const __nv_bfloat16* src =
-          CAUSAL ? a.gate + (int64_t(b) * a.L + rp) * a.sg_row + int64_t(rhq) * a.sg_h
+          CAUSAL ? a.gate + (seq0 + rp) * a.sg_row + int64_t(rhq) * a.sg_h
                  : a.gate + (int64_t(b) * a.W + rb) * a.sg_row + int64_t(rt) * a.sg_t + int64_t(rhq) * a.sg_h;
       cp_async16(smem + M::v + r * 512 + ((c ^ (r & 31)) * 16), src + c * 8);
     }
@@ -376,7 +384,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
   const float inv = sc[1];
 #pragma unroll
   for (int sidx = 0; sidx < kSufMax; ++sidx) psuf[sidx] = sc[2 + sidx];
-  __nv_bfloat16* op = CAUSAL ? a.out + (int64_t(b) * a.L + pos) * a.so_row + int64_t(hq) * a.so_h
+  __nv_bfloat16* op = CAUSAL ? a.out + (seq0 + pos) * a.so_row + int64_t(hq) * a.so_h
                              : a.out + brow * a.so_row + int64_t(t) * a.so_t + int64_t(hq) * a.so_h;
 #pragma unroll 1
   for (int piece = half * (kD / 64); rowthr && piece < (half + 1) * (kD / 64); ++piece) {  // this half's columns
@@ -443,7 +451,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
 // Thread i writes 16-byte unit i of the destination (consecutive threads, consecutive bytes).
 __global__ void __launch_bounds__(256) kv_tile_kernel(const __nv_bfloat16* src, int64_t s_seq, int64_t s_pos,
                                                       int64_t s_h, int HK, int L, int nblk, unsigned char* dst,
-                                                      int64_t units) {
+                                                      int64_t units, const int* cu) {
   const int64_t i = int64_t(blockIdx.x) * 256 + threadIdx.x;
   if (i >= units) return;
   constexpr int per_blk = kTile / 16;  // 2048 units: [8 key groups][32 dim chunks][8 keys]
@@ -455,8 +463,14 @@ __global__ void __launch_bounds__(256) kv_tile_kernel(const __nv_bfloat16* src, 
   const int64_t s = sh / HK;
   const int h = int(sh % HK);
   const int p = kb * kBlk + kg * 8 + k8;
+  int64_t base = s * s_seq;  // varlen (cu): sequence s is positions [cu[s], cu[s+1]) of one packed run
+  int len = L;
+  if (cu) {
+    base = int64_t(cu[s]) * s_pos;
+    len = cu[s + 1] - cu[s];
+  }
   uint4 v = make_uint4(0u, 0u, 0u, 0u);
-  if (p < L) v = *reinterpret_cast<const uint4*>(src + s * s_seq + int64_t(p) * s_pos + int64_t(h) * s_h + dc * 8);
+  if (p < len) v = *reinterpret_cast<const uint4*>(src + base + int64_t(p) * s_pos + int64_t(h) * s_h + dc * 8);
   reinterpret_cast<uint4*>(dst)[i] = v;
 }
 
@@ -484,9 +498,10 @@ extern "C" int64_t kadllm_kv_tile_bytes(int64_t seqs, int64_t kv_heads, int64_t 
   return seqs * kv_heads * ((length + kBlk - 1) / kBlk) * int64_t(kTile);
 }
 
-extern "C" int kadllm_kv_tile(const void* src, int64_t s_seq, int64_t s_pos, int64_t s_head, int64_t seqs,
-                              int64_t kv_heads, int64_t length, int64_t head_dim, void* tiles, int64_t tile_bytes,
-                              void* stream) {
+namespace kb {
+namespace {
+int kv_tile(const void* src, int64_t s_seq, int64_t s_pos, int64_t s_head, const int* cu, int64_t seqs,
+            int64_t kv_heads, int64_t length, int64_t head_dim, void* tiles, int64_t tile_bytes, void* stream) {
   KB_REQUIRE(src && tiles, KADLLM_EINVAL, "kv_tile: null pointer");
   KB_REQUIRE(head_dim == kD && seqs >= 1 && kv_heads >= 1 && length >= 1, KADLLM_EUNSUPPORTED,
              "kv_tile: head_dim must be %d", kD);
@@ -500,19 +515,36 @@ extern "C" int kadllm_kv_tile(const void* src, int64_t s_seq, int64_t s_pos, int
   const int64_t units = bytes / 16;
   kv_tile_kernel<<<unsigned((units + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(src), s_seq, s_pos, s_head, int(kv_heads), int(length), int(nblk),
-      static_cast<unsigned char*>(tiles), units);
+      static_cast<unsigned char*>(tiles), units, cu);
   KB_CHECK_LAUNCH("kv_tile launch");
   return KADLLM_OK;
 }
+}  // namespace
+}  // namespace kb
 
-extern "C" int kadllm_attention_tiled(const void* q, int64_t sq_row, int64_t sq_t, int64_t sq_h, const void* k_tiles,
-                                      const void* v_tiles, int64_t blocks_per_head, const void* suffix_k,
-                                      int64_t ssk_row, int64_t ssk_t, int64_t ssk_h, const void* suffix_v,
-                                      int64_t ssv_row, int64_t ssv_t, int64_t ssv_h, const void* gate, int64_t sg_row,
-                                      int64_t sg_t, int64_t sg_h, void* out, int64_t so_row, int64_t so_t,
-                                      int64_t so_h, uint32_t* status, int64_t batch, int64_t beam_width,
-                                      int64_t steps, int64_t q_heads, int64_t kv_heads, int64_t prefix_len,
-                                      int64_t head_dim, float scale, int causal, void* stream) {
+extern "C" int kadllm_kv_tile(const void* src, int64_t s_seq, int64_t s_pos, int64_t s_head, int64_t seqs,
+                              int64_t kv_heads, int64_t length, int64_t head_dim, void* tiles, int64_t tile_bytes,
+                              void* stream) {
+  return kb::kv_tile(src, s_seq, s_pos, s_head, nullptr, seqs, kv_heads, length, head_dim, tiles, tile_bytes, stream);
+}
+
+extern "C" int kadllm_kv_tile_varlen(const void* src, int64_t s_pos, int64_t s_head, const int32_t* cu_seqlens,
+                                     int64_t seqs, int64_t kv_heads, int64_t max_length, int64_t head_dim, void* tiles,
+                                     int64_t tile_bytes, void* stream) {
+  KB_REQUIRE(cu_seqlens != nullptr, KADLLM_EINVAL, "kv_tile: null sequence offsets");
+  return kb::kv_tile(src, 0, s_pos, s_head, cu_seqlens, seqs, kv_heads, max_length, head_dim, tiles, tile_bytes,
+                     stream);
+}
+
+namespace kb {
+namespace {
+int attention_tiled(const void* q, int64_t sq_row, int64_t sq_t, int64_t sq_h, const void* k_tiles,
+                    const void* v_tiles, int64_t blocks_per_head, const void* suffix_k, int64_t ssk_row,
+                    int64_t ssk_t, int64_t ssk_h, const void* suffix_v, int64_t ssv_row, int64_t ssv_t, int64_t ssv_h,
+                    const void* gate, int64_t sg_row, int64_t sg_t, int64_t sg_h, void* out, int64_t so_row,
+                    int64_t so_t, int64_t so_h, uint32_t* status, const int* cu, int64_t batch, int64_t beam_width,
+                    int64_t steps, int64_t q_heads, int64_t kv_heads, int64_t prefix_len, int64_t head_dim,
+                    float scale, int causal, void* stream) {
   KB_REQUIRE(q && k_tiles && v_tiles && out && status, KADLLM_EINVAL, "tiled attention: null pointer");
   KB_REQUIRE(head_dim == kD, KADLLM_EUNSUPPORTED, "tiled attention: head_dim must be %d", kD);
   KB_REQUIRE(batch >= 1 && q_heads >= 1 && kv_heads >= 1 && q_heads % kv_heads == 0 && prefix_len >= 1 &&
@@ -539,9 +571,40 @@ extern "C" int kadllm_attention_tiled(const void* q, int64_t sq_row, int64_t sq_
   a.gate = static_cast<const __nv_bfloat16*>(gate); a.sg_row = sg_row; a.sg_t = sg_t; a.sg_h = sg_h;
   a.out = static_cast<__nv_bfloat16*>(out); a.so_row = so_row; a.so_t = so_t; a.so_h = so_h;
   a.status = status;
+  a.cu = cu;
   a.B = int(batch); a.W = int(causal ? 1 : beam_width); a.T = int(causal ? 1 : steps); a.H = int(q_heads);
   a.HK = int(kv_heads); a.G = int(q_heads / kv_heads); a.L = int(prefix_len);
   a.scale_log2 = (scale > 0.f ? scale : 1.0f / sqrtf(float(head_dim))) * 1.4426950408889634f;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return causal ? launch_attn_tc<true>(a, s) : launch_attn_tc<false>(a, s);
+}
+}  // namespace
+}  // namespace kb
+
+extern "C" int kadllm_attention_tiled(const void* q, int64_t sq_row, int64_t sq_t, int64_t sq_h, const void* k_tiles,
+                                      const void* v_tiles, int64_t blocks_per_head, const void* suffix_k,
+                                      int64_t ssk_row, int64_t ssk_t, int64_t ssk_h, const void* suffix_v,
+                                      int64_t ssv_row, int64_t ssv_t, int64_t ssv_h, const void* gate, int64_t sg_row,
+                                      int64_t sg_t, int64_t sg_h, void* out, int64_t so_row, int64_t so_t,
+                                      int64_t so_h, uint32_t* status, int64_t batch, int64_t beam_width,
+                                      int64_t steps, int64_t q_heads, int64_t kv_heads, int64_t prefix_len,
+                                      int64_t head_dim, float scale, int causal, void* stream) {
+  return kb::attention_tiled(q, sq_row, sq_t, sq_h, k_tiles, v_tiles, blocks_per_head, suffix_k, ssk_row, ssk_t,
+                             ssk_h, suffix_v, ssv_row, ssv_t, ssv_h, gate, sg_row, sg_t, sg_h, out, so_row, so_t,
+                             so_h, status, nullptr, batch, beam_width, steps, q_heads, kv_heads, prefix_len,
+                             head_dim, scale, causal, stream);
+}
+
+extern "C" int kadllm_attention_tiled_varlen(
+    const void* q, int64_t sq_row, int64_t sq_t, int64_t sq_h, const void* k_tiles, const void* v_tiles,
+    int64_t blocks_per_head, const void* suffix_k, int64_t ssk_row, int64_t ssk_t, int64_t ssk_h,
+    const void* suffix_v, int64_t ssv_row, int64_t ssv_t, int64_t ssv_h, const void* gate, int64_t sg_row,
+    int64_t sg_t, int64_t sg_h, void* out, int64_t so_row, int64_t so_t, int64_t so_h, uint32_t* status,
+    const int32_t* cu_seqlens, int64_t batch, int64_t beam_width, int64_t steps, int64_t q_heads, int64_t kv_heads,
+    int64_t max_prefix_len, int64_t head_dim, float scale, int causal, void* stream) {
+  KB_REQUIRE(cu_seqlens != nullptr, KADLLM_EINVAL, "tiled attention: null sequence offsets");
+  return kb::attention_tiled(q, sq_row, sq_t, sq_h, k_tiles, v_tiles, blocks_per_head, suffix_k, ssk_row, ssk_t,
+                             ssk_h, suffix_v, ssv_row, ssv_t, ssv_h, gate, sg_row, sg_t, sg_h, out, so_row, so_t,
+                             so_h, status, cu_seqlens, batch, beam_width, steps, q_heads, kv_heads, max_prefix_len,
+                             head_dim, scale, causal, stream);
 }

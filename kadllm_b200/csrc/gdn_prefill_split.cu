@@ -47,7 +47,9 @@ struct SplitArgs {
   unsigned char* blocks;                       // [B*HV, nc] chunk blocks (ChunkBlock)
   uint32_t* status;                            // bit 0: a tensor-core wait of the scan timed out
   int tc_layout;                               // chunk blocks in the tensor-core scan's shared-memory image
-  int B, L, nc, H, HV;
+  const int* cu;                               // varlen: request b = rows [cu[b], cu[b+1]) (null: b*L .. +L)
+  int64_t rows;                                // rows of proj / out (B*L, or cu[B])
+  int B, L, nc, H, HV;                         // L, nc: the (longest) request's length and chunk count
   float scale;
 };
 
@@ -72,6 +74,17 @@ struct ChunkBlock {
 __device__ __forceinline__ void core16_rc(int o, int& r, int& ch) { r = ((o >> 7) << 3) | (o & 7); ch = (o >> 3) & 15; }
 __device__ __forceinline__ void core8_rc(int o, int& r, int& ch) { r = ((o >> 6) << 3) | (o & 7); ch = (o >> 3) & 7; }
 __device__ __forceinline__ void swz16_rc(int o, int& r, int& ch) { r = o >> 4; ch = (o & 15) ^ (r & 7); }
+
+// Request b's first row and length (packed varlen rows, or B requests of L rows).
+__device__ __forceinline__ void seq_of(const SplitArgs& a, int b, int64_t& row0, int& len) {
+  if (a.cu) {
+    row0 = a.cu[b];
+    len = a.cu[b + 1] - a.cu[b];
+  } else {
+    row0 = int64_t(b) * a.L;
+    len = a.L;
+  }
+}
 
 template <int DK, int DV>
 size_t workspace_bytes(int64_t B, int64_t HV, int64_t L) {
@@ -159,19 +172,23 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const SplitArgs a) {
   auto chan = [&](int lc) {  // head-local channel -> projection column
     return lc < DK ? h * DK + lc : (lc < 2 * DK ? key_dim + h * DK + (lc - DK) : 2 * key_dim + hv * DV + (lc - 2 * DK));
   };
-  const __nv_bfloat16* prow0 = a.proj + int64_t(b) * a.L * a.ld_proj;
+  int64_t seq0;
+  int L;
+  seq_of(a, b, seq0, L);
+  if (t0 >= L) return;  // past this request's last chunk (varlen): the whole CTA, before any barrier
+  const __nv_bfloat16* prow0 = a.proj + seq0 * a.ld_proj;
 
   // ---- stage the raw projection tile (tokens t0-3 .. t0+63, zero outside [0, L)) -----
   for (int i = tid; i < (kC + 3) * (NCH / 8); i += NT) {
     const int r = i / (NCH / 8), lc = (i % (NCH / 8)) * 8;
     const int t = t0 - 3 + r;
     __nv_bfloat16* dst = sRawT + r * RS + lc;
-    if (t >= 0 && t < a.L) cp_async16(dst, prow0 + int64_t(t) * a.ld_proj + chan(lc));
+    if (t >= 0 && t < L) cp_async16(dst, prow0 + int64_t(t) * a.ld_proj + chan(lc));
     else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
   }
   cp_async_commit();
   float gb = 0.f, ga = 0.f;  // gate inputs of token t0 + tid
-  if (tid < kC && t0 + tid < a.L) {
+  if (tid < kC && t0 + tid < L) {
     const __nv_bfloat16* pr = prow0 + int64_t(t0 + tid) * a.ld_proj + conv_dim + int64_t(a.HV) * DV;
     gb = __bfloat162float(pr[hv]);
     ga = __bfloat162float(pr[a.HV + hv]);
@@ -216,7 +233,7 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const SplitArgs a) {
       float2 x[4];
       row4(r + 3, x);
       uint4 u = make_uint4(0u, 0u, 0u, 0u);
-      if (t0 + r < a.L) {
+      if (t0 + r < L) {
         uint32_t* uw = reinterpret_cast<uint32_t*>(&u);
 #pragma unroll
         for (int pp = 0; pp < 4; ++pp) {
@@ -238,18 +255,18 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const SplitArgs a) {
       }
     }
   }
-  if (c == a.nc - 1) {  // conv state: pre-conv columns of tokens L-4 .. L-1 (staged rows L-1-t0 ..)
+  if (t0 + kC >= L) {  // last chunk: conv state = pre-conv columns of tokens L-4 .. L-1 (staged rows L-1-t0 ..)
     for (int lc = tid; lc < NCH; lc += NT) {
       __nv_bfloat16 s4[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) s4[j] = sRawT[(a.L - 1 - t0 + j) * RS + lc];
+      for (int j = 0; j < 4; ++j) s4[j] = sRawT[(L - 1 - t0 + j) * RS + lc];
       *reinterpret_cast<uint2*>(a.conv_state + (int64_t(b) * conv_dim + chan(lc)) * 4) = *reinterpret_cast<uint2*>(s4);
     }
   }
   // ---- gates ------------------------------------------------------------------------
   if (tid < kC) {
     float g = 0.f, be = 0.f;
-    if (t0 + tid < a.L) {
+    if (t0 + tid < L) {
       be = bf16r(sigmoid_f(gb));
       g = -expf(a.a_log[hv]) * softplus_f(ga + a.dt_bias[hv]);
     }
@@ -653,7 +670,7 @@ __device__ __forceinline__ void named_bar(int id, int n) { asm volatile("bar.syn
 __global__ void __launch_bounds__(256) gdn_gated_norm_kernel(const SplitArgs a) {
   // 16 lanes per (row, value head), 8 channels (16 bytes) a lane; 32-bit item arithmetic
   // (the launcher checks B * L * HV < 2^31)
-  const uint32_t items = uint32_t(a.B) * uint32_t(a.L) * uint32_t(a.HV);
+  const uint32_t items = uint32_t(a.rows) * uint32_t(a.HV);
   const uint32_t want = blockIdx.x * 16u + (threadIdx.x >> 4);
   const bool ok = want < items;  // past the end: recompute the last item (every lane meets the shuffles)
   const uint32_t item = ok ? want : items - 1;
@@ -707,8 +724,12 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) 
   const bool vwarp = quad >= 2;              // quadrants 2, 3: W rows -> Vn
   const bool issuer = tid == 64;
   const int bh = blockIdx.x, b = bh / a.HV, hv = bh % a.HV;
-  const unsigned char* blocks = a.blocks + int64_t(bh) * a.nc * CB::bytes;
+  const unsigned char* blocks = a.blocks + int64_t(bh) * a.nc * CB::bytes;  // row of a.nc (longest) chunks
   const uint32_t sbase = smem_u32(smem);
+  int64_t seq0;
+  int L;
+  seq_of(a, b, seq0, L);
+  const int nc = (L + kC - 1) / kC;  // this request's chunks
 
   int ld_issued[2] = {0, 0};  // stage loads issued (issuer thread)
   auto load_block = [&](int c, int st) {  // issuer: chunk block c (its shared-memory image) -> stage st
@@ -741,7 +762,7 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) 
   const uint32_t tS = tmem + lane_off + half * 64, tP = tmem + 128 + lane_off + half * 64;
   bool ok = true;
 
-  for (int c = 0; c < a.nc; ++c) {
+  for (int c = 0; c < nc; ++c) {
     const int st = c & 1;
     const uint32_t par = uint32_t(c) & 1u;
     const unsigned char* sb = smem + st * M::stage;
@@ -753,7 +774,7 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) 
     if (!ok) break;
     tc::fence_after();
     const float gl_next =
-        c + 1 < a.nc ? *reinterpret_cast<const float*>(blocks + int64_t(c + 1) * CB::bytes + CB::g + (kC - 1) * 4) : 0.f;
+        c + 1 < nc ? *reinterpret_cast<const float*>(blocks + int64_t(c + 1) * CB::bytes + CB::g + (kC - 1) * 4) : 0.f;
     if (vwarp) {
       if (issuer) {  // MMA1: P = [Q'; W] S
 #pragma unroll
@@ -761,7 +782,7 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) 
           tc::mma_bf16(tmem + 128, tc::smem_desc(sbu + M::a1 + s * 256, 128, 2048),
                        tc::smem_desc(sbase + M::b1 + s * 4096, 2048, 128), kId1, s > 0);
         tc::commit(bar1);
-        if (c + 1 < a.nc) load_block(c + 1, st ^ 1);  // stage st^1 was last read by chunk c-1
+        if (c + 1 < nc) load_block(c + 1, st ^ 1);  // stage st^1 was last read by chunk c-1
       }
       ok = tc::mbar_wait(bar1, par, kWait) && ok;
       tc::fence_after();
@@ -804,8 +825,8 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) 
     ok = tc::mbar_wait(bar2, par, kWait) && ok;
     tc::fence_after();
     if (!vwarp) {  // O rows (lanes 0..63) -> BF16 layer output; the gated RMSNorm is a separate kernel
-      const bool valid = c * kC + row < a.L;
-      uint4* op = reinterpret_cast<uint4*>(a.out + (int64_t(b) * a.L + int64_t(c) * kC + row) * a.ld_out + hv * D + half * 64);
+      const bool valid = c * kC + row < L;
+      uint4* op = reinterpret_cast<uint4*>(a.out + (seq0 + int64_t(c) * kC + row) * a.ld_out + hv * D + half * 64);
 #pragma unroll
       for (int piece = 0; piece < 2; ++piece) {
         uint32_t r[32];
@@ -824,7 +845,7 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) 
     }
     {  // S: bf16 copy for the next MMA1 (and the final state), then S *= e^{G_last(next chunk)}
       const float f = __expf(gl_next);
-      const bool last = c + 1 == a.nc;
+      const bool last = c + 1 == nc;
       uint4* dst = reinterpret_cast<uint4*>(a.state + (int64_t(bh) * D + row) * D + half * 64);
 #pragma unroll
       for (int piece = 0; piece < 2; ++piece) {
@@ -873,7 +894,9 @@ int launch_split(SplitArgs& a, void* ws, int64_t ws_bytes, cudaStream_t s) {
   const bool tc_scan = DK == 128 && DV == 128 && a.ld_out % 8 == 0 && a.ld_proj % 8 == 0 &&
                        (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.state) & 15) == 0 &&
                        (reinterpret_cast<uintptr_t>(a.norm_w) & 15) == 0 &&
-                       (reinterpret_cast<uintptr_t>(a.proj) & 15) == 0 && int64_t(a.B) * a.L * a.HV < (1ll << 31);
+                       (reinterpret_cast<uintptr_t>(a.proj) & 15) == 0 && a.rows * a.HV < (1ll << 31);
+  KB_REQUIRE(tc_scan || a.cu == nullptr, KADLLM_EUNSUPPORTED,
+             "gdn prefill: packed variable-length requests need 128-dim heads and 16-byte aligned rows");
   a.tc_layout = tc_scan ? 1 : 0;
   if (cudaMemsetAsync(a.status, 0, sizeof(uint32_t), s) != cudaSuccess) {
     set_error("gdn prefill: cannot clear the status word");
@@ -897,7 +920,7 @@ int launch_split(SplitArgs& a, void* ws, int64_t ws_bytes, cudaStream_t s) {
     }
     gdn_scan_tc_kernel<<<unsigned(n), 256, smem, s>>>(a);
     KB_CHECK_LAUNCH("gdn prefill tensor-core scan launch");
-    const int64_t items = int64_t(a.B) * a.L * a.HV;  // (row, value head) pairs, 16 per CTA
+    const int64_t items = a.rows * a.HV;  // (row, value head) pairs, 16 per CTA
     gdn_gated_norm_kernel<<<unsigned((items + 15) / 16), 256, 0, s>>>(a);
     KB_CHECK_LAUNCH("gdn prefill gated norm launch");
     return KADLLM_OK;
@@ -929,15 +952,16 @@ extern "C" int64_t kadllm_gdn_prefill_workspace(int64_t batch, int64_t length, i
   return -1;
 }
 
-extern "C" int kadllm_gdn_prefill_split(const void* proj, int64_t ld_proj, const void* conv_weight, void* conv_state,
-                                        const float* a_log, const float* dt_bias, const float* norm_weight,
-                                        float norm_eps, void* out, int64_t ld_out, void* state, void* workspace,
-                                        int64_t workspace_bytes, int64_t batch, int64_t length, int64_t heads,
-                                        int64_t v_heads, int64_t k_dim, int64_t v_dim, void* stream) {
+namespace kb {
+namespace {
+int prefill_split(const void* proj, int64_t ld_proj, const void* conv_weight, void* conv_state, const float* a_log,
+                  const float* dt_bias, const float* norm_weight, float norm_eps, void* out, int64_t ld_out,
+                  void* state, void* workspace, int64_t workspace_bytes, const int* cu, int64_t rows, int64_t batch,
+                  int64_t length, int64_t heads, int64_t v_heads, int64_t k_dim, int64_t v_dim, void* stream) {
   KB_REQUIRE(proj && conv_weight && conv_state && a_log && dt_bias && norm_weight && out && state && workspace,
              KADLLM_EINVAL, "gdn prefill: null pointer");
-  KB_REQUIRE(batch >= 1 && length >= 1 && heads >= 1 && v_heads >= 1 && v_heads % heads == 0, KADLLM_EINVAL,
-             "gdn prefill: bad dimensions");
+  KB_REQUIRE(batch >= 1 && length >= 1 && rows >= 1 && heads >= 1 && v_heads >= 1 && v_heads % heads == 0,
+             KADLLM_EINVAL, "gdn prefill: bad dimensions");
   KB_REQUIRE(ld_proj % 8 == 0 && ld_out % 2 == 0 && (reinterpret_cast<uintptr_t>(proj) & 15) == 0 &&
                  (reinterpret_cast<uintptr_t>(conv_weight) & 15) == 0 && (reinterpret_cast<uintptr_t>(workspace) & 255) == 0 &&
                  (reinterpret_cast<uintptr_t>(conv_state) & 7) == 0,
@@ -951,6 +975,7 @@ extern "C" int kadllm_gdn_prefill_split(const void* proj, int64_t ld_proj, const
   a.a_log = a_log; a.dt_bias = dt_bias; a.norm_w = norm_weight; a.eps = norm_eps;
   a.out = static_cast<__nv_bfloat16*>(out); a.ld_out = ld_out;
   a.state = static_cast<__nv_bfloat16*>(state);
+  a.cu = cu; a.rows = rows;
   a.B = int(batch); a.L = int(length); a.nc = int(nc); a.H = int(heads); a.HV = int(v_heads);
   a.scale = 1.0f / sqrtf(float(k_dim));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -960,4 +985,29 @@ extern "C" int kadllm_gdn_prefill_split(const void* proj, int64_t ld_proj, const
   set_error("gdn prefill: head dims K=%lld V=%lld must be equal and in {32, 64, 128}", (long long)k_dim,
             (long long)v_dim);
   return KADLLM_EUNSUPPORTED;
+}
+}  // namespace
+}  // namespace kb
+
+extern "C" int kadllm_gdn_prefill_split(const void* proj, int64_t ld_proj, const void* conv_weight, void* conv_state,
+                                        const float* a_log, const float* dt_bias, const float* norm_weight,
+                                        float norm_eps, void* out, int64_t ld_out, void* state, void* workspace,
+                                        int64_t workspace_bytes, int64_t batch, int64_t length, int64_t heads,
+                                        int64_t v_heads, int64_t k_dim, int64_t v_dim, void* stream) {
+  return kb::prefill_split(proj, ld_proj, conv_weight, conv_state, a_log, dt_bias, norm_weight, norm_eps, out, ld_out,
+                           state, workspace, workspace_bytes, nullptr, batch * length, batch, length, heads, v_heads,
+                           k_dim, v_dim, stream);
+}
+
+extern "C" int kadllm_gdn_prefill_split_varlen(const void* proj, int64_t ld_proj, const void* conv_weight,
+                                               void* conv_state, const float* a_log, const float* dt_bias,
+                                               const float* norm_weight, float norm_eps, void* out, int64_t ld_out,
+                                               void* state, void* workspace, int64_t workspace_bytes,
+                                               const int32_t* cu_seqlens, int64_t total_rows, int64_t batch,
+                                               int64_t max_length, int64_t heads, int64_t v_heads, int64_t k_dim,
+                                               int64_t v_dim, void* stream) {
+  KB_REQUIRE(cu_seqlens != nullptr, KADLLM_EINVAL, "gdn prefill: null sequence offsets");
+  return kb::prefill_split(proj, ld_proj, conv_weight, conv_state, a_log, dt_bias, norm_weight, norm_eps, out, ld_out,
+                           state, workspace, workspace_bytes, cu_seqlens, total_rows, batch, max_length, heads,
+                           v_heads, k_dim, v_dim, stream);
 }

@@ -123,7 +123,16 @@ def grbeam_search(
     if not widths or any(not isinstance(w, int) or isinstance(w, bool) or w < 1 for w in widths):
         raise ValueError("widths must contain positive integers")
     prefill = adapter.prefill(input_ids)
-    B = input_ids.shape[0]
+    return search_from_prefill(adapter, prefill, input_ids.shape[0], widths, allowed=allowed)
+
+
+@torch.no_grad()
+def search_from_prefill(adapter: GRBeamAdapter, prefill: PrefillResult, B: int, widths: Sequence[int], *,
+                        allowed: Constraint | None = None) -> GRBeamResult:
+    """The decode / selection loop of ``grbeam_search`` after the prefill (shared by the
+    packed variable-length search)."""
+    if not widths or any(not isinstance(w, int) or isinstance(w, bool) or w < 1 for w in widths):
+        raise ValueError("widths must contain positive integers")
     if prefill.logits.ndim != 2 or prefill.logits.shape[0] != B:
         raise ValueError("prefill logits must have shape [B, vocabulary]")
     V = prefill.logits.shape[-1]
@@ -132,7 +141,7 @@ def grbeam_search(
     _lib.require_cuda(prefill.logits)
     device = prefill.logits.device
     selector = BeamSelector(B, max([1, *widths[:-1]]), device)
-    history = input_ids.new_empty(B, 1, 0).to(device)
+    history = torch.empty(B, 1, 0, dtype=torch.int64, device=device)
     scores = None
     logits = prefill.logits[:, None, :]
     fused = hasattr(adapter, "decode_select") and allowed is None

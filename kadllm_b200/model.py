@@ -73,12 +73,16 @@ class HybridPrefix:
     for attention layers -- the reference's layouts and BF16 dtypes.
     """
 
-    length: int
+    length: int  # the prefix length (the longest one for packed prompts)
     batch: int
     owner: object
     layers: tuple
     # attention layers: (K tiles, V tiles, blocks per head) for the tensor-core kernels, else None
     tiles: tuple = ()
+    # packed prompts of their own lengths (``prefill_varlen``): device int32 offsets [B + 1]
+    # and the host lengths; attention layers then hold packed [rows, HK, D] K / V
+    cu: torch.Tensor | None = None
+    lengths: tuple = ()
 
 
 class HybridModel:
@@ -203,12 +207,13 @@ class HybridModel:
                   self._stream())
         return F.linear(act, layer.w_down)
 
-    def _qk_rope(self, P, rows, pos_base, rows_per_seq, q_out, k_out, k_strides, v_out, v_strides, mixer):
+    def _qk_rope(self, P, rows, pos_base, rows_per_seq, q_out, k_out, k_strides, v_out, v_strides, mixer,
+                 pos_of_row=None, max_pos=None):
         c = self.cfg
-        cos, sin = self._rope(pos_base + rows_per_seq + 1)
+        cos, sin = self._rope((pos_base + rows_per_seq if max_pos is None else max_pos) + 1)
         _lib.call("kadllm_qk_norm_rope", P.data_ptr(), P.stride(0), c.num_attention_heads, c.num_key_value_heads,
                   c.head_dim, mixer.q_norm.data_ptr(), mixer.k_norm.data_ptr(), c.rms_norm_eps, cos.data_ptr(),
-                  sin.data_ptr(), c.rotary_dim, None, pos_base, rows_per_seq, q_out.data_ptr(),
+                  sin.data_ptr(), c.rotary_dim, _lib.ptr(pos_of_row), pos_base, rows_per_seq, q_out.data_ptr(),
                   c.num_attention_heads * c.head_dim, c.head_dim, k_out.data_ptr(), *k_strides, v_out.data_ptr(),
                   *v_strides, rows, self._stream())
 
@@ -280,6 +285,90 @@ class HybridModel:
         logits = F.linear(last, self.lm_head if head is None else head)
         return logits, HybridPrefix(L, B, self.owner, tuple(prefix), tuple(tiles))
 
+    @torch.no_grad()
+    def prefill_varlen(self, prompts, head: torch.Tensor | None = None):
+        """Prompts of their own lengths, packed into one batch: ``prompts`` is a list of
+        1-D token tensors -> (logits [B, V] bf16, HybridPrefix with ``cu`` / ``lengths``).
+
+        Every kernel sees the packed rows with per-request offsets (device int32
+        ``cu``): the GDN prefill runs each request's own chunk count, the causal
+        attention each request's own prefix, RoPE each row's own position; the
+        prefix K / V are tiled per request.  Head dim 256 attention and 128-dim
+        GDN heads only (the tensor-core paths)."""
+        c = self.cfg
+        hk, D, hq = c.num_key_value_heads, c.head_dim, c.num_attention_heads
+        if D != TILED_HEAD_DIM or (c.linear_key_head_dim, c.linear_value_head_dim) != (128, 128):
+            raise NotImplementedError("packed prompts need head_dim 256 attention and 128-dim GDN heads")
+        lens = [int(p.numel()) for p in prompts]
+        if not lens or min(lens) < 1:
+            raise ValueError("prompts must be nonempty")
+        B, Lmax = len(lens), max(lens)
+        offs = [0]
+        for n in lens:
+            offs.append(offs[-1] + n)
+        R = offs[-1]
+        ids = torch.cat([p.reshape(-1) for p in prompts]).to(device=self.device, dtype=torch.int64).contiguous()
+        cu = torch.tensor(offs, dtype=torch.int32).to(self.device)
+        pos = torch.cat([torch.arange(n, dtype=torch.int64) for n in lens]).to(self.device)  # position of each row
+        x, normed = self._embed(ids)
+        s = self._stream()
+        prefix, tiles = [], []
+        ws = None
+        for i, layer in enumerate(self.layers):
+            m = layer.mixer
+            P = F.linear(normed, m.w_in)
+            if layer.kind == LINEAR:
+                conv_state = torch.empty(B, c.conv_dim, 4, dtype=BF16, device=self.device)
+                out = torch.empty(R, c.value_dim, dtype=BF16, device=self.device)
+                rec = torch.empty(B, c.linear_num_value_heads, c.linear_key_head_dim, c.linear_value_head_dim,
+                                  dtype=BF16, device=self.device)
+                if ws is None:
+                    ws = torch.empty(_lib.lib().kadllm_gdn_prefill_workspace(
+                        B, Lmax, c.linear_num_value_heads, c.linear_key_head_dim, c.linear_value_head_dim),
+                        dtype=torch.uint8, device=self.device)
+                _lib.call("kadllm_gdn_prefill_split_varlen", P.data_ptr(), P.stride(0), m.conv_w.data_ptr(),
+                          conv_state.data_ptr(), m.a_log.data_ptr(), m.dt_bias.data_ptr(), m.norm_w.data_ptr(),
+                          c.rms_norm_eps, out.data_ptr(), out.stride(0), rec.data_ptr(), ws.data_ptr(), ws.numel(),
+                          cu.data_ptr(), R, B, Lmax, c.linear_num_key_heads, c.linear_num_value_heads,
+                          c.linear_key_head_dim, c.linear_value_head_dim, s)
+                delta = F.linear(out, m.w_out)
+                prefix.append((conv_state, rec))
+                tiles.append(None)
+            else:
+                q = torch.empty(R, hq, D, dtype=BF16, device=self.device)
+                kp = torch.empty(R, hk, D, dtype=BF16, device=self.device)  # packed rows
+                vp = torch.empty_like(kp)
+                packed = (0, hk * D, D)  # (sequence, position, head): one run of rows
+                self._qk_rope(P, R, 0, R, q, kp, packed, vp, packed, m, pos_of_row=pos, max_pos=Lmax)
+                nbytes = _lib.lib().kadllm_kv_tile_bytes(B, hk, Lmax, D)
+                kt = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+                vt = torch.empty_like(kt)
+                _lib.call("kadllm_kv_tile_varlen", kp.data_ptr(), hk * D, D, cu.data_ptr(), B, hk, Lmax, D,
+                          kt.data_ptr(), nbytes, s)
+                _lib.call("kadllm_kv_tile_varlen", vp.data_ptr(), hk * D, D, cu.data_ptr(), B, hk, Lmax, D,
+                          vt.data_ptr(), nbytes, s)
+                nblk = -(-Lmax // 64)
+                out = torch.empty(R, hq * D, dtype=BF16, device=self.device)
+                gate = P[:, D:]
+                _lib.call("kadllm_attention_tiled_varlen", q.data_ptr(), hq * D, 0, D, kt.data_ptr(), vt.data_ptr(),
+                          nblk, None, 0, 0, 0, None, 0, 0, 0, gate.data_ptr(), P.stride(0), 0, 2 * D,
+                          out.data_ptr(), out.stride(0), 0, D, self.status.data_ptr(), cu.data_ptr(), B, 1, 1, hq,
+                          hk, Lmax, D, D ** -0.5, 1, s)
+                delta = F.linear(out, m.w_o)
+                prefix.append((kp, vp))
+                tiles.append((kt, vt, nblk))
+            self._add_norm(x, delta, layer.post_ln, normed)
+            delta = self._mlp(layer, normed)
+            if i + 1 < len(self.layers):
+                self._add_norm(x, delta, self.layers[i + 1].input_ln, normed)
+        last_rows = cu[1:].long() - 1
+        xl, dl = x.index_select(0, last_rows), delta.index_select(0, last_rows)
+        last = torch.empty(B, c.hidden_size, dtype=BF16, device=self.device)
+        _lib.call("kadllm_add_rmsnorm", xl.data_ptr(), dl.data_ptr(), dl.stride(0), self.final_norm.data_ptr(),
+                  c.rms_norm_eps, last.data_ptr(), B, 1, 0, c.hidden_size, s)
+        logits = F.linear(last, self.lm_head if head is None else head)
+        return logits, HybridPrefix(Lmax, B, self.owner, tuple(prefix), tuple(tiles), cu, tuple(lens))
+
     # ------------------------------------------------------------------ decode
     @torch.no_grad()
     def decode_hidden(self, history: torch.Tensor, state: HybridPrefix) -> torch.Tensor:
@@ -291,6 +380,11 @@ class HybridModel:
         x, normed = self._embed(ids)
         s = self._stream()
         hk, D, hq = c.num_key_value_heads, c.head_dim, c.num_attention_heads
+        varlen = state.cu is not None
+        pos = None
+        if varlen:  # suffix position of row (b, w, t): the request's own prefix length + t
+            lens = torch.tensor(state.lengths, dtype=torch.int64)
+            pos = (lens.repeat_interleave(W * T) + torch.arange(T, dtype=torch.int64).repeat(B * W)).to(self.device)
         for i, (layer, cached) in enumerate(zip(self.layers, state.layers)):
             m = layer.mixer
             P = F.linear(normed, m.w_in)
@@ -308,12 +402,23 @@ class HybridModel:
                 ks = torch.empty(R, hk, D, dtype=BF16, device=self.device)
                 vs = torch.empty_like(ks)
                 suffix_strides = (T * hk * D, hk * D, D)  # (beam row, step, head)
-                self._qk_rope(P, R, state.length, T, q, ks, suffix_strides, vs, suffix_strides, m)
+                if varlen:
+                    self._qk_rope(P, R, 0, T, q, ks, suffix_strides, vs, suffix_strides, m, pos_of_row=pos,
+                                  max_pos=state.length + T)
+                else:
+                    self._qk_rope(P, R, state.length, T, q, ks, suffix_strides, vs, suffix_strides, m)
                 pk, pv = cached  # [B, L, HK, D] views
                 out = torch.empty(R, hq * D, dtype=BF16, device=self.device)
                 gate = P[:, D:]
                 tile = state.tiles[i] if i < len(state.tiles) else None
-                if tile is not None:
+                if varlen:  # every request against its own prefix length
+                    kt, vt, nblk = tile
+                    _lib.call("kadllm_attention_tiled_varlen", q.data_ptr(), T * hq * D, hq * D, D, kt.data_ptr(),
+                              vt.data_ptr(), nblk, ks.data_ptr(), *suffix_strides, vs.data_ptr(), *suffix_strides,
+                              gate.data_ptr(), T * P.stride(0), P.stride(0), 2 * D, out.data_ptr(), T * hq * D,
+                              hq * D, D, self.status.data_ptr(), state.cu.data_ptr(), B, W, T, hq, hk, state.length,
+                              D, D ** -0.5, 0, s)
+                elif tile is not None:
                     kt, vt, nblk = tile
                     _lib.call("kadllm_attention_tiled", q.data_ptr(), T * hq * D, hq * D, D, kt.data_ptr(),
                               vt.data_ptr(), nblk, ks.data_ptr(), *suffix_strides, vs.data_ptr(), *suffix_strides,

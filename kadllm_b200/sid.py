@@ -17,8 +17,10 @@ the constraint hook at ``:98-102`` and ``:110-111``):
   positions; scores are then log-probabilities over the SID tokens;
 * :func:`grbeam_search_varlen` -- requests with different prompt lengths.  The
   reference adapter takes unpadded ``[B, L]`` prompts only
-  (``src/kadllm/adapters/qwen3_5.py:106-110``), so requests are grouped by
-  length and each group is one search; results come back in request order.
+  (``src/kadllm/adapters/qwen3_5.py:106-110``); here all requests go through
+  one packed prefill (per-request offsets in every kernel) and one search, or,
+  for adapters without it, are grouped by length; results come back in
+  request order.
 * :func:`sid_search` -- the two together, returning token ids.
 """
 
@@ -29,7 +31,7 @@ from dataclasses import dataclass
 
 import torch
 
-from .grbeam import GRBeamResult, PrefillResult, grbeam_search
+from .grbeam import GRBeamResult, PrefillResult, grbeam_search, search_from_prefill
 
 
 @dataclass(frozen=True)
@@ -139,21 +141,32 @@ class SidHeadAdapter:
         return PrefillResult(logits, state)
 
     @torch.no_grad()
+    @torch.no_grad()
+    def prefill_varlen(self, prompts) -> PrefillResult:
+        for p in prompts:
+            self.base._check(p)
+            if p.ndim != 1 or p.numel() < 1:
+                raise ValueError("each prompt must be a nonempty 1-D tensor")
+        logits, state = self.base.engine.prefill_varlen(list(prompts), head=self.head)
+        return PrefillResult(logits, state)
+
+    @torch.no_grad()
     def decode(self, history: torch.Tensor, state) -> torch.Tensor:
         self.base._check_state(history, state)  # entries are codebook positions (from the selection)
         return self.base.engine.decode(self.tokens[history], state, head=self.head)
 
 
 def grbeam_search_varlen(adapter, prompts: Sequence[torch.Tensor], widths: Sequence[int], *,
-                         allowed=None, streams: int = 1) -> GRBeamResult:
+                         allowed=None, streams: int = 1, packed: bool = True) -> GRBeamResult:
     """``grbeam_search`` over requests with their own prompt lengths.
 
-    ``prompts`` are 1-D integer tensors.  Requests of equal length share one
-    search (one prefill of ``[group, L]``); the result rows follow the order
-    of ``prompts``.  With ``streams > 1`` the length groups are spread over
-    that many CUDA streams, each driven by its own host thread, so the small
-    per-group kernels (a one-request prefill scan has only one CTA per value
-    head) of different groups overlap on the device.
+    ``prompts`` are 1-D integer tensors; the result rows follow their order.
+    With ``packed`` (and an adapter that has ``prefill_varlen``: this package's
+    adapters on head dim 256 / 128-dim GDN heads) all requests share one
+    packed prefill and one search.  Otherwise requests of equal length share
+    one search (one prefill of ``[group, L]``); with ``streams > 1`` the length
+    groups are spread over that many CUDA streams, each driven by its own host
+    thread.
     """
     if len(prompts) == 0:
         raise ValueError("prompts must be nonempty")
@@ -162,6 +175,13 @@ def grbeam_search_varlen(adapter, prompts: Sequence[torch.Tensor], widths: Seque
         if p.ndim != 1 or p.numel() < 1:
             raise ValueError("each prompt must be a nonempty 1-D tensor")
         groups.setdefault(int(p.numel()), []).append(i)
+    if packed and len(groups) > 1 and hasattr(adapter, "prefill_varlen"):
+        try:
+            pre = adapter.prefill_varlen(list(prompts))
+        except NotImplementedError:
+            pre = None
+        if pre is not None:
+            return search_from_prefill(adapter, pre, len(prompts), widths, allowed=allowed)
     order = sorted(groups, reverse=True)  # longest first: the slowest groups start earliest
 
     def run(length):
@@ -215,7 +235,7 @@ def _run_on_streams(run, items, streams: int, device):
 
 def sid_search(adapter, prompts: Sequence[torch.Tensor], codebook: SidCodebook,
                widths: Sequence[int] = (256, 256), *, sid_head: bool = True, streams: int = 1,
-               head: SidHeadAdapter | None = None) -> GRBeamResult:
+               head: SidHeadAdapter | None = None, packed: bool = True) -> GRBeamResult:
     """Two-level conditional SID search; ``tokens`` holds token ids.
 
     ``sid_head=True`` scores over the codebook tokens (SID-only head; pass a
@@ -227,8 +247,9 @@ def sid_search(adapter, prompts: Sequence[torch.Tensor], codebook: SidCodebook,
         raise ValueError("two-level SID search takes two widths")
     if sid_head:
         head = head or SidHeadAdapter(adapter, codebook)
-        res = grbeam_search_varlen(head, prompts, widths, allowed=sid_constraint(codebook), streams=streams)
+        res = grbeam_search_varlen(head, prompts, widths, allowed=sid_constraint(codebook), streams=streams,
+                                   packed=packed)
         return GRBeamResult(head.tokens[res.tokens], res.scores, res.valid)
     vocab = int(adapter.engine.lm_head.shape[0])
     return grbeam_search_varlen(adapter, prompts, widths, allowed=sid_constraint(codebook, vocab=vocab),
-                                streams=streams)
+                                streams=streams, packed=packed)

@@ -122,3 +122,30 @@ def test_prefix_is_immutable_and_owner_checked(mid):
     other._owner = object()  # an adapter that did not create this prefix
     with pytest.raises(ValueError):
         other.decode(torch.zeros(1, 4, 2, dtype=torch.long, device="cuda"), pre.state)
+
+
+def test_packed_prefill_and_decode_match_per_request(mid):
+    """Prompts of lengths 70, 40, 100, 65 in one packed prefill (per-request offsets in the
+    GDN prefill, the tiled causal attention, RoPE and the K/V tiles) and one decode against
+    each request run alone through the same engine."""
+    engine, _ = mid
+    lens = (70, 40, 100, 65)
+    prompts = [torch.from_numpy(random_prompts(1, n, MID.vocab_size, seed=30 + i)[0]).cuda() for i, n in enumerate(lens)]
+    logits, state = engine.prefill_varlen(prompts)
+    assert state.lengths == lens and state.length == max(lens)
+    hist = torch.from_numpy(np.random.default_rng(1).integers(0, MID.vocab_size, (len(lens), 3, 2))).cuda()
+    dec = engine.decode(hist, state)
+    engine.check()
+    for i, p in enumerate(prompts):
+        one_logits, one_state = engine.prefill(p[None])
+        assert_close_rel(logits[i:i + 1].float().cpu().numpy(), one_logits.float().cpu().numpy(), rel=2e-2,
+                         what=f"packed prefill logits, request {i}")
+        for j, ((a, b), (oa, ob)) in enumerate(zip(state.layers, one_state.layers)):
+            if a.shape[0] == len(lens):  # GDN layer: per-request conv and recurrent state
+                assert_close_rel(a[i].float().cpu().numpy(), oa[0].float().cpu().numpy(), rel=2e-2,
+                                 what=f"conv state, layer {j}, request {i}")
+                assert_close_rel(b[i].float().cpu().numpy(), ob[0].float().cpu().numpy(), rel=2e-2,
+                                 what=f"recurrent state, layer {j}, request {i}")
+        one_dec = engine.decode(hist[i:i + 1], one_state)
+        assert_close_rel(dec[i:i + 1].float().cpu().numpy(), one_dec.float().cpu().numpy(), rel=2e-2,
+                         what=f"packed decode logits, request {i}")

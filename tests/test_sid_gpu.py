@@ -56,15 +56,15 @@ def _prompts():
     return [random_prompts(1, n, MID.vocab_size, seed=20 + i)[0] for i, n in enumerate(LENGTHS)]
 
 
-@pytest.mark.parametrize("sid_head,streams", [(True, 2), (False, 1)])
-def test_sid_search_matches_oracle(mid_sid, sid_head, streams):
-    """SID-only head over two CUDA streams (length groups in parallel host threads),
-    and the full-vocabulary head with the masked selection path on one stream."""
+@pytest.mark.parametrize("sid_head,streams,packed", [(True, 1, True), (True, 2, False), (False, 1, True)])
+def test_sid_search_matches_oracle(mid_sid, sid_head, streams, packed):
+    """SID-only head through one packed prefill of all prompts, the same through length
+    groups on two CUDA streams, and the full-vocabulary head with the masked selection."""
     adapter, orc, cb = mid_sid
     widths = (16, 16)
     prompts = _prompts()
     res = sid_search(adapter, [torch.from_numpy(p).cuda() for p in prompts], cb, widths, sid_head=sid_head,
-                     streams=streams)
+                     streams=streams, packed=packed)
     tokens = cb.tokens.numpy()
     n1 = cb.n1
     if sid_head:
