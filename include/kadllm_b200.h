@@ -304,6 +304,11 @@ KADLLM_API int kadllm_causal_attention(const void* q, int64_t sq_row, int64_t sq
                                        int64_t kv_heads, int64_t head_dim, float scale,
                                        void* stream);
 
+/* Diagnostics: one CTA runs the tensor-core kernels' bounded mbarrier wait on a
+ * barrier nothing completes, giving up after max_cycles SM clocks (1 .. 2^32)
+ * and setting bit 0 of *status, as those kernels report a timed-out wait. */
+KADLLM_API int kadllm_diag_wait_timeout(uint32_t* status, int64_t max_cycles, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -26,6 +26,7 @@ SIGNATURES: dict[str, list] = {
     "kadllm_gdn_prefill_split": [P, L, P, P, P, P, P, F, P, L, P, P, L, L, L, L, L, L, L, P],
     "kadllm_kv_tile": [P, L, L, L, L, L, L, L, P, L, P],
     "kadllm_kv_tile_varlen": [P, L, L, P, L, L, L, L, P, L, P],
+    "kadllm_diag_wait_timeout": [P, L, P],
     "kadllm_gdn_prefill_split_varlen": [P, L, P, P, P, P, P, F, P, L, P, P, L, P, L, L, L, L, L, L, L, P],
     "kadllm_attention_tiled": [P, L, L, L, P, P, L, P, L, L, L, P, L, L, L, P, L, L, L, P, L, L, L, P,
                                L, L, L, L, L, L, L, F, I, P],
