@@ -3,10 +3,13 @@
 Workload (per GPU): random-init BF16 weights N(0, 0.02)
 (seed 0), 32 requests of 1024 uniform-random prompt tokens per GPU, beam width
 256, 3 output tokens (prefill + 2 decode steps + selection), full 248,320-token
-vocabulary.  One step = one ``grbeam_search`` call over one 32-request batch
-per GPU; with N GPUs every rank runs its own batch (weak scaling: requests
-shard across GPUs with replicated weights) and the results are all-gathered
-over NCCL at the end of each step.
+vocabulary.  One step = one ``grbeam_search`` over one 32-request batch per
+GPU -- by default the whole search captured once as a CUDA graph
+(``kadllm_b200.grbeam.GraphedSearch``) and replayed each step, every kernel
+of the search running each time (``--no-graph``: eager launches); with N GPUs
+every rank runs its own batch (weak scaling: requests shard across GPUs with
+replicated weights) and the results are all-gathered over NCCL at the end of
+each step.
 
 ``value``   requests/s with the prompts already resident in HBM;
 ``e2e``     the same through the public API from pinned host buffers, with the
@@ -212,6 +215,7 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
     from kadllm_b200 import _lib, grbeam_search
     from kadllm_b200.adapters import NativeGRBeamAdapter
     from kadllm_b200.config import QWEN35_08B
+    from kadllm_b200.grbeam import GraphedSearch
     from kadllm_b200.model import HybridModel
     from kadllm_b200.shard import gather_beams, max_over_ranks, rank_prompts
     from kadllm_b200.synthetic import torch_weights
@@ -231,12 +235,30 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
     def gather(res):  # the path's only exchange: finished beams, in rank order
         return gather_beams(res.tokens, res.scores)
 
+    # the search as one CUDA graph (static prompt buffer, every kernel replayed per step);
+    # the eager path when capture is off or fails
+    graphed = None
+    launches_per_step = None
+    with torch.inference_mode():
+        n0 = _lib.launch_count
+        grbeam_search(adapter, ids_dev, widths)  # eager reference search: this library's launches per step
+        launches_per_step = _lib.launch_count - n0
+        if not args.no_graph:
+            try:
+                graphed = GraphedSearch(adapter, BATCH, PROMPT, widths, dev)
+            except Exception as exc:  # noqa: BLE001 - report and fall back to eager launches
+                print(f"bench: CUDA graph capture failed ({type(exc).__name__}: {exc}); eager launches",
+                      file=sys.stderr, flush=True)
+                graphed = None
+
     def step_device():
+        if graphed is not None:
+            return gather(graphed(ids_dev))
         return gather(grbeam_search(adapter, ids_dev, widths))
 
     def step_e2e():
         ids = ids_host.to(dev, non_blocking=True)
-        res = grbeam_search(adapter, ids, widths)
+        res = graphed(ids) if graphed is not None else grbeam_search(adapter, ids, widths)
         tok_host.copy_(res.tokens, non_blocking=True)
         sc_host.copy_(res.scores, non_blocking=True)
         return gather(res)
@@ -255,7 +277,7 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
         if world > 1:
             dist.barrier()
         ms = max_over_ranks(start.elapsed_time(end), dev)
-        return ms / steps, _lib.launch_count - launches0
+        return ms / steps, (launches_per_step * steps if graphed is not None else _lib.launch_count - launches0)
 
     with torch.inference_mode():
         for _ in range(args.warmup):
@@ -263,7 +285,9 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
         with ClockSampler(local_rank) as clocks:
             ms, launches = timed(step_device, args.steps)
         ms_e2e, _ = timed(step_e2e, args.steps)
-        res = grbeam_search(adapter, ids_dev, widths)
+        res = graphed(ids_dev) if graphed is not None else grbeam_search(adapter, ids_dev, widths)
+        if graphed is not None:
+            graphed.check()
         valid = bool(res.valid.all().item())
         distinct = all(len({tuple(b) for b in req}) == BEAM for req in res.tokens.cpu().tolist())
         prof = profile_kernels(engine, adapter, ids_dev, widths, args) if rank == 0 else None
@@ -290,6 +314,7 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
                           "frac": flops / (ms / 1000) / 1e12 / peaks.get("bf16_tflops_sustained"),
                           "peak_kind": f"{peak_kind} sustained bf16"},
         "checks": {"all_valid": valid, "distinct_beams": distinct},
+        "launch": "cuda_graph" if graphed is not None else "eager",
     }
     if prof:
         line["roofline"] = prof["roofline"]
@@ -416,6 +441,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["native", "reference"], default="native")
     ap.add_argument("--roofline-kernel", default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="eager launches instead of one CUDA graph per search")
     ap.add_argument("--workload", choices=["grbeam", "sid"], default="grbeam",
                     help="grbeam: the headline metric; sid: two-level conditional SID, prefixes 512-4096")
     ap.add_argument("--sid-batch", type=int, default=32)

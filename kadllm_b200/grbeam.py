@@ -128,9 +128,10 @@ def grbeam_search(
 
 @torch.no_grad()
 def search_from_prefill(adapter: GRBeamAdapter, prefill: PrefillResult, B: int, widths: Sequence[int], *,
-                        allowed: Constraint | None = None) -> GRBeamResult:
+                        allowed: Constraint | None = None, selector: BeamSelector | None = None) -> GRBeamResult:
     """The decode / selection loop of ``grbeam_search`` after the prefill (shared by the
-    packed variable-length search)."""
+    packed variable-length search and the graphed search).  With a caller-owned
+    ``selector`` nothing synchronises the host: the caller checks it (CUDA-graph capture)."""
     if not widths or any(not isinstance(w, int) or isinstance(w, bool) or w < 1 for w in widths):
         raise ValueError("widths must contain positive integers")
     if prefill.logits.ndim != 2 or prefill.logits.shape[0] != B:
@@ -140,7 +141,9 @@ def search_from_prefill(adapter: GRBeamAdapter, prefill: PrefillResult, B: int, 
         raise ValueError("vocabulary must be nonempty")
     _lib.require_cuda(prefill.logits)
     device = prefill.logits.device
-    selector = BeamSelector(B, max([1, *widths[:-1]]), device)
+    own = selector is None
+    if own:
+        selector = BeamSelector(B, max([1, *widths[:-1]]), device)
     history = torch.empty(B, 1, 0, dtype=torch.int64, device=device)
     scores = None
     logits = prefill.logits[:, None, :]
@@ -163,5 +166,45 @@ def search_from_prefill(adapter: GRBeamAdapter, prefill: PrefillResult, B: int, 
                 raise ValueError("constraint must return a bool mask matching logits")
         scores, history = selector.step(logits, scores, history, width, mask)
         del logits, mask
-    selector.check()
+    if own:
+        selector.check()
     return GRBeamResult(history, scores, torch.isfinite(scores))
+
+
+class GraphedSearch:
+    """A whole ``grbeam_search`` over a fixed batch shape captured once as a CUDA graph.
+
+    Every replay runs all of the search's kernels (prefill, decodes, selections)
+    from the static input buffer ``ids`` into static outputs; the launches are
+    issued by the device, not by the host.  ``__call__(ids)`` copies new prompts in
+    first; ``check()`` reads the selection's overflow flag (synchronises).  The
+    adapter must be this package's (its kernels go to the current stream).
+    """
+
+    def __init__(self, adapter, batch: int, prompt_len: int, widths: Sequence[int], device):
+        self.adapter, self.widths = adapter, list(widths)
+        self.ids = torch.zeros(batch, prompt_len, dtype=torch.int64, device=device)
+        self.selector = BeamSelector(batch, max([1, *self.widths[:-1]]), device)
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):  # allocations, tables and library workspaces before capture
+            for _ in range(2):
+                self._search()
+        torch.cuda.current_stream(device).wait_stream(side)
+        torch.cuda.synchronize(device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.result = self._search()
+
+    def _search(self) -> GRBeamResult:
+        prefill = self.adapter.prefill(self.ids)
+        return search_from_prefill(self.adapter, prefill, self.ids.shape[0], self.widths, selector=self.selector)
+
+    def __call__(self, ids: torch.Tensor | None = None) -> GRBeamResult:
+        if ids is not None:
+            self.ids.copy_(ids, non_blocking=True)
+        self.graph.replay()
+        return self.result
+
+    def check(self) -> None:
+        self.selector.check()

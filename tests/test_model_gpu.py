@@ -149,3 +149,23 @@ def test_packed_prefill_and_decode_match_per_request(mid):
         one_dec = engine.decode(hist[i:i + 1], one_state)
         assert_close_rel(dec[i:i + 1].float().cpu().numpy(), one_dec.float().cpu().numpy(), rel=2e-2,
                          what=f"packed decode logits, request {i}")
+
+
+def test_graphed_search_matches_eager(mid):
+    """A whole search captured as one CUDA graph and replayed (static prompt buffer)
+    gives the eager search's beams, for the captured prompts and for new ones."""
+    from kadllm_b200 import grbeam_search
+    from kadllm_b200.adapters import NativeGRBeamAdapter
+    from kadllm_b200.grbeam import GraphedSearch
+
+    engine, _ = mid
+    adapter = NativeGRBeamAdapter(engine)
+    widths = [8, 8, 8]
+    graphed = GraphedSearch(adapter, 2, 64, widths, torch.device("cuda"))
+    for seed in (6, 7):
+        ids = torch.from_numpy(random_prompts(2, 64, MID.vocab_size, seed=seed)).cuda()
+        got = graphed(ids)
+        graphed.check()
+        want = grbeam_search(adapter, ids, widths)
+        assert torch.equal(got.tokens, want.tokens)
+        torch.testing.assert_close(got.scores, want.scores, rtol=0, atol=0)
