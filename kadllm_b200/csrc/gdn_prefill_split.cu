@@ -649,7 +649,9 @@ struct TcScan {
   static constexpr size_t stage = u + copy2;
   static constexpr size_t b1 = 2 * stage;                  // S (bf16) MN-major, K 128 (keys) x N 128
   static constexpr size_t b2 = b1 + size_t(D) * D * 2;     // Vn MN-major, K 64 (tokens) x N 128
-  static constexpr size_t bar = b2 + size_t(kC) * D * 2;   // mbarriers: MMA1, MMA2/3, stage 0, stage 1
+  static constexpr int kGMax = 1024;                       // chunks whose last decay is preloaded
+  static constexpr size_t gl = b2 + size_t(kC) * D * 2;    // [kGMax] fp32 G_last of every chunk
+  static constexpr size_t bar = gl + size_t(kGMax) * 4;    // mbarriers: MMA1, MMA2/3, stage 0, stage 1
   static constexpr size_t slot = bar + 4 * 8;              // TMEM base address
   static constexpr size_t bytes = slot + 8;
   static_assert(a3 + size_t(kC) * kC * 2 == CB::u && copy1 % 16 == 0 && stage % 16 == 0 && bar % 8 == 0,
@@ -752,6 +754,9 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) 
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   if (warp == 0) tc::tmem_alloc(slot, 256);
+  float* sGL = reinterpret_cast<float*>(smem + M::gl);  // G_last of each chunk: off the per-chunk critical path
+  for (int i = tid; i < nc && i < M::kGMax; i += 256)
+    sGL[i] = *reinterpret_cast<const float*>(blocks + int64_t(i) * CB::bytes + CB::g + (kC - 1) * 4);
   tc::fence_async_smem();  // zeroed operand rows -> tensor cores
   tc::fence_before();
   __syncthreads();
@@ -774,7 +779,10 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) 
     if (!ok) break;
     tc::fence_after();
     const float gl_next =
-        c + 1 < nc ? *reinterpret_cast<const float*>(blocks + int64_t(c + 1) * CB::bytes + CB::g + (kC - 1) * 4) : 0.f;
+        c + 1 >= nc ? 0.f
+                    : (c + 1 < M::kGMax ? sGL[c + 1]
+                                        : *reinterpret_cast<const float*>(blocks + int64_t(c + 1) * CB::bytes + CB::g +
+                                                                          (kC - 1) * 4));
     if (vwarp) {
       if (issuer) {  // MMA1: P = [Q'; W] S
 #pragma unroll
