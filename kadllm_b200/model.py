@@ -201,7 +201,7 @@ class HybridModel:
 
     def _mlp(self, layer: Layer, normed):
         gu = F.linear(normed, layer.w_gu)
-        inter = self.cfg.intermediate_size
+        inter = layer.w_gu.shape[0] // 2  # per layer: WideTuning-merged layers are wider
         act = torch.empty(gu.shape[0], inter, dtype=BF16, device=self.device)
         _lib.call("kadllm_silu_mul", gu.data_ptr(), gu.stride(0), inter, act.data_ptr(), gu.shape[0],
                   self._stream())
