@@ -141,7 +141,6 @@ class SidHeadAdapter:
         return PrefillResult(logits, state)
 
     @torch.no_grad()
-    @torch.no_grad()
     def prefill_varlen(self, prompts) -> PrefillResult:
         for p in prompts:
             self.base._check(p)
