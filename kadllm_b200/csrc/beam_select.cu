@@ -12,8 +12,9 @@
 // The reference loops over requests on the host (32 launches of a 254 MB
 // temporary each).  Here the whole batch is four launches and no temporary of
 // logits size:
-//   1. rowstats   per row: max (HBM pass), then sum-exp and a 2048-bin histogram
-//                 of (max - x) in 1/32-nat bins (second pass, L2-resident);
+//   1. rowstats   per row: max and sum-exp, and a 2048-bin histogram of
+//                 (max - x) in 1/32-nat bins (BF16 without a mask: of the
+//                 16-byte vectors' maxima, lower bounds of the element counts);
 //   2. threshold  per request: shifts every row histogram by the row's score
 //                 offset into a request histogram and picks the highest score
 //                 threshold that provably keeps >= width candidates above it;
@@ -138,8 +139,10 @@ __device__ __forceinline__ float ex2_approx(float x) {
 
 // BF16 logits without a mask (the decode hot path).  Persistent: one
 // 1024-thread CTA per SM loops over rows and reads each row from HBM once.
-//   pass 1 (HBM): per-thread online max and sum of exp (rescaled when the
-//     thread's max grows), packed bf16x2 max per 16-byte vector;
+//   pass 1 (HBM): per-thread running max and sum of exp, packed bf16x2 max per
+//     16-byte vector.  The sum is kept relative to a reference value that moves
+//     only when a vector's maximum exceeds it by more than kRefSlack nats (the
+//     first vector, in practice), so the stream has no divergent rescale;
 //   tau: a lower bound on the row's W-th largest value.  Each warp sorts its 32
 //     per-thread maxima; the minimum over the n warps of the ceil(W/n)-th
 //     largest leaves >= W elements of the row at or above tau.  Only those can
@@ -147,19 +150,25 @@ __device__ __forceinline__ float ex2_approx(float x) {
 //     so binning only them leaves the threshold bin unchanged, and bins past
 //     tau's stay empty (rowlen);
 //   pass 2: each thread's 16-byte vector maxima of the row are kept in shared
-//     memory (bf16, [slot][thread]); a thread re-reads only the vectors whose
-//     maximum reaches tau and bins d = 32 (max - x) with one FFMA (bit-identical
-//     to (max - x) * 32).  Pass 2 of row r runs inside pass 1 of the CTA's next
-//     row (two tables, alternating), so the HBM stream never waits for it and
-//     the few re-read vectors are the only extra traffic.
+//     memory (bf16, [slot][thread]) and the maxima at or above tau are binned:
+//     d = 32 (max - vmax), one FFMA (bit-identical to (max - vmax) * 32).  A
+//     vector whose maximum reaches a score holds at least one candidate at or
+//     above it, so these counts are lower bounds of the element counts: the
+//     threshold they give still provably keeps >= width candidates (tau bounds
+//     >= W thread maxima, each in its own vector), and collect then gathers the
+//     elements exactly.  Pass 2 of row r runs inside pass 1 of the CTA's next
+//     row (two tables and two histograms, alternating), so the logits are read
+//     from HBM exactly once.
 constexpr int kStatThreads = 1024;
 constexpr int kStatSlots = 48;  // vectors per thread (V <= 48 * 8 * 1024) for the table
+constexpr float kRefSlack = 64.f;
 __host__ __device__ constexpr size_t stat_smem(int slots) { return size_t(2) * slots * kStatThreads * 2; }
 
-__device__ __forceinline__ float vec_max(const uint4& u) {
+// maximum of the 8 bf16 values (NaN ignored, like fmaxf)
+__device__ __forceinline__ __nv_bfloat16 vec_max_bf(const uint4& u) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
   const __nv_bfloat162 t = __hmax2(__hmax2(h[0], h[1]), __hmax2(h[2], h[3]));
-  return fmaxf(__low2float(t), __high2float(t));
+  return __hmax(__low2bfloat16(t), __high2bfloat16(t));
 }
 
 __device__ __forceinline__ void unpack8(const uint4& u, float (&x)[8]) {
@@ -171,157 +180,164 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&x)[8]) {
   }
 }
 
-// Per-thread online max and sum of exp2(x log2e - max log2e), the sum kept as a
-// pair (even / odd elements) in packed fp32x2 arithmetic.
+// Per-thread running max and sum of exp2(x log2e - ref log2e), the sum kept as a
+// pair (even / odd elements) in packed fp32x2 arithmetic.  ref <= m and
+// (m - ref) <= kRefSlack, so no term exceeds 2^93.
 struct OnlineSum {
-  float m = -INFINITY, ml = 0.f;
+  float m = -INFINITY, ref = -INFINITY, rl = 0.f;
   float2 s = make_float2(0.f, 0.f);
   // accumulate one 16-byte vector; returns its maximum
-  __device__ __forceinline__ float add(const uint4& u) {
-    const float hi = vec_max(u);
-    if (hi > m) {  // rare after the first vectors; -inf and NaN vectors never enter
-      const float c = ex2_approx((m - hi) * kLog2e);
+  __device__ __forceinline__ __nv_bfloat16 add(const uint4& u) {
+    const __nv_bfloat16 hb = vec_max_bf(u);
+    const float hi = __bfloat162float(hb);
+    m = fmaxf(m, hi);
+    if (hi > ref + kRefSlack) {  // the first finite vector, or a jump of more than kRefSlack nats
+      const float c = ex2_approx((ref - hi) * kLog2e);
       s = mul2(s, make_float2(c, c));
-      m = hi;
-      ml = hi * kLog2e;
+      ref = hi;
+      rl = hi * kLog2e;
     }
-    const float2 l2e = make_float2(kLog2e, kLog2e), nml = make_float2(-ml, -ml);
+    const float2 l2e = make_float2(kLog2e, kLog2e), nrl = make_float2(-rl, -rl);
     const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const float2 t = fma2(bf2f(w[j]), l2e, nml);
+      const float2 t = fma2(bf2f(w[j]), l2e, nrl);
       s = add2(s, make_float2(ex2_approx(t.x), ex2_approx(t.y)));
     }
-    return hi;
+    return hb;
+  }
+  // the sum relative to `to` (>= ref)
+  __device__ __forceinline__ float sum_at(float to) const {
+    return ref == -INFINITY ? 0.f : (s.x + s.y) * ex2_approx((ref - to) * kLog2e);
   }
 };
 
-__device__ __forceinline__ void bin_vec(const uint4& u, float tau, float m32, uint32_t* hist) {
-  if (vec_max(u) >= tau) {
-    float x[8];
-    unpack8(u, x);
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (x[j] >= tau) atomicAdd(&hist[int(fminf(fmaf(x[j], -kBinsPerNat, m32), float(kRowBins - 1)))], 1u);
-  }
-}
-
 __global__ void __launch_bounds__(kStatThreads, 1) rowstats_bf16_kernel(const SelArgs a) {
-  __shared__ uint32_t hist[kRowBins];
+  __shared__ uint32_t hists[2][kRowBins];  // alternating rows: binned during the next row, exported after it
   __shared__ float red[2 * 96];
   extern __shared__ __align__(16) unsigned char dsm[];
   __nv_bfloat16* vmax = reinterpret_cast<__nv_bfloat16*>(dsm);  // [2][slots][nt] vector maxima
   constexpr int nt = kStatThreads, nwarps = kStatThreads / 32;
-  const int64_t rows = int64_t(a.B) * a.Wp;
+  const int rows = a.B * a.Wp;  // < 2^31 (checked by the host)
   const int nvec = int(a.V / 8);
   const int slots = (nvec + nt - 1) / nt;
   const int tid = threadIdx.x, lane = tid & 31;
-  for (int j = tid; j < kRowBins; j += nt) hist[j] = 0;
+  for (int j = tid; j < 2 * kRowBins; j += nt) hists[j / kRowBins][j % kRowBins] = 0;
   // the CTA's previous row, binned while the current one streams in
-  const uint4* prow = nullptr;
-  int64_t pr = -1;
+  int pr = -1;
   float ptau = 0.f, pm32 = 0.f;
   int pbin = 0;
   bool pact = false;
-  int par = 0;  // table of the current row
+  int par = 0;  // table and histogram of the current row
   const __nv_bfloat16* base = reinterpret_cast<const __nv_bfloat16*>(a.logits);
   // the first four vectors of the CTA's next row, loaded before the current row's
   // reductions so HBM keeps streaming through them
   uint4 f0, f1, f2, f3;
   const bool full4 = tid + 3 * nt < nvec;
-  if (full4 && int64_t(blockIdx.x) < rows) {
+  if (full4 && int(blockIdx.x) < rows) {
     const uint4* r0 = reinterpret_cast<const uint4*>(base + int64_t(blockIdx.x) * a.ld);
     f0 = r0[tid]; f1 = r0[tid + nt]; f2 = r0[tid + 2 * nt]; f3 = r0[tid + 3 * nt];
   }
-  for (int64_t r = blockIdx.x;; r += gridDim.x, par ^= 1) {
+  for (int r = blockIdx.x;; r += gridDim.x, par ^= 1) {
     const bool cur = r < rows;
-    const uint4* row = reinterpret_cast<const uint4*>(base + (cur ? r : 0) * a.ld);
+    const uint4* row = reinterpret_cast<const uint4*>(base + int64_t(cur ? r : 0) * a.ld);
     __nv_bfloat16* tcur = vmax + size_t(par) * slots * nt + tid;
     const __nv_bfloat16* tprev = vmax + size_t(par ^ 1) * slots * nt + tid;
-    // previous row's vector at slot k: re-read and bin it when its maximum reaches tau
-    auto bin_prev = [&](int k) {
-      if (__bfloat162float(tprev[k * nt]) >= ptau) bin_vec(prow[tid + k * nt], ptau, pm32, hist);
+    uint32_t* phist = hists[par ^ 1];  // the previous row's bins
+    // previous row's vector at slot k (present: inside the row): bin its maximum if it reaches tau
+    auto bin_prev = [&](int k, bool present) {
+      if (present && pact) {
+        const float v = __bfloat162float(tprev[k * nt]);
+        if (v >= ptau) atomicAdd(&phist[int(fminf(fmaf(v, -kBinsPerNat, pm32), float(kRowBins - 1)))], 1u);
+      }
     };
     OnlineSum acc;
+    const int wfirst = tid - lane;  // the warp's first thread: loops below are warp-uniform
     if (cur) {
-      int i = tid, k = 0;
-      for (; i + 3 * nt < nvec; i += 4 * nt, k += 4) {  // four 16-byte HBM loads in flight
+      int k = 0;
+      for (; wfirst + (k + 3) * nt + 31 < nvec; k += 4) {  // four 16-byte HBM loads in flight
+        const int i = tid + k * nt;
         uint4 u0 = f0, u1 = f1, u2 = f2, u3 = f3;  // first batch: prefetched
         if (k) {
           u0 = row[i]; u1 = row[i + nt]; u2 = row[i + 2 * nt]; u3 = row[i + 3 * nt];
         }
-        if (pact) {
-          bin_prev(k);
-          bin_prev(k + 1);
-          bin_prev(k + 2);
-          bin_prev(k + 3);
+        if (pr >= 0) {
+          bin_prev(k, true);
+          bin_prev(k + 1, true);
+          bin_prev(k + 2, true);
+          bin_prev(k + 3, true);
         }
-        tcur[k * nt] = __float2bfloat16_rn(acc.add(u0));
-        tcur[(k + 1) * nt] = __float2bfloat16_rn(acc.add(u1));
-        tcur[(k + 2) * nt] = __float2bfloat16_rn(acc.add(u2));
-        tcur[(k + 3) * nt] = __float2bfloat16_rn(acc.add(u3));
+        tcur[k * nt] = acc.add(u0);
+        tcur[(k + 1) * nt] = acc.add(u1);
+        tcur[(k + 2) * nt] = acc.add(u2);
+        tcur[(k + 3) * nt] = acc.add(u3);
       }
-      for (; i < nvec; i += nt, ++k) {
-        tcur[k * nt] = __float2bfloat16_rn(acc.add(row[i]));
-        if (pact) bin_prev(k);
+      for (; wfirst + k * nt < nvec; ++k) {
+        const int i = tid + k * nt;
+        const bool has = i < nvec;
+        if (has) tcur[k * nt] = acc.add(row[i]);
+        if (pr >= 0) bin_prev(k, has);
       }
-    } else if (pact) {
-      for (int k = 0; tid + k * nt < nvec; ++k) bin_prev(k);
-    }
-    if (pr >= 0) {  // export the previous row's bins and clear them for the next
-      __syncthreads();
-      const int len = min(pbin + 1, kRowBins - 1);
-      if (tid == 0) a.rowlen[pr] = uint32_t(len);
-      for (int j = tid; j <= pbin; j += nt) {
-        if (j < len) a.rowhist[pr * kRowBins + j] = hist[j];
-        hist[j] = 0;
-      }
-    }
-    if (!cur) break;
-    if (full4 && r + gridDim.x < rows) {  // next row's first batch, in flight during the reductions
-      const uint4* rn = reinterpret_cast<const uint4*>(base + (r + gridDim.x) * a.ld);
-      f0 = rn[tid]; f1 = rn[tid + nt]; f2 = rn[tid + 2 * nt]; f3 = rn[tid + 3 * nt];
+    } else if (pr >= 0) {
+      for (int k = 0; wfirst + k * nt < nvec; ++k) bin_prev(k, tid + k * nt < nvec);
     }
     // one exchange per row: each warp publishes its maximum, its sum rescaled to that
     // maximum and its ceil(W/n)-th largest thread maximum; every thread combines the 32
-    const float mt = acc.m;
-    const float wm = warp_max(mt);
-    const float ws = warp_sum(mt == -INFINITY ? 0.f : (acc.s.x + acc.s.y) * ex2_approx((mt - wm) * kLog2e));
-    float wk = -INFINITY;
-    if (a.W <= 32 * nwarps) {
-      const int kth = (a.W + nwarps - 1) / nwarps - 1;
-      float v = mt;
-#pragma unroll
-      for (int k = 2; k <= 32; k <<= 1) {
-#pragma unroll
-        for (int j = k >> 1; j > 0; j >>= 1) {
-          const float o = __shfl_xor_sync(0xffffffffu, v, j);
-          v = (((lane & j) == 0) == ((lane & k) == 0)) ? fmaxf(v, o) : fminf(v, o);
-        }
+    float m = -INFINITY, sum = 0.f, tau = -INFINITY, mt = -INFINITY;
+    if (cur) {
+      if (full4 && r + int(gridDim.x) < rows) {  // next row's first batch, in flight during the reductions
+        const uint4* rn = reinterpret_cast<const uint4*>(base + int64_t(r + gridDim.x) * a.ld);
+        f0 = rn[tid]; f1 = rn[tid + nt]; f2 = rn[tid + 2 * nt]; f3 = rn[tid + 3 * nt];
       }
-      wk = __shfl_sync(0xffffffffu, v, kth);
-    }
-    float* xr = red + (par ? 96 : 0);  // alternate rows: readers of one row never meet writers of the next
-    if (lane == 0) {
-      xr[tid >> 5] = wm;
-      xr[32 + (tid >> 5)] = ws;
-      xr[64 + (tid >> 5)] = wk;
-    }
-    __syncthreads();
-    // every warp combines the 32 entries in parallel, lane w taking warp w's (nwarps == 32)
-    static_assert(nwarps == 32, "one entry per lane");
-    const float mw = xr[lane];
-    const float m = warp_max(mw);
-    const float sum = warp_sum(mw == -INFINITY ? 0.f : xr[32 + lane] * ex2_approx((mw - m) * kLog2e));
-    float tau = -INFINITY;
-    if (a.W <= 32 * nwarps) {
-      float k = xr[64 + lane];
+      mt = acc.m;
+      const float wm = warp_max(mt);
+      const float ws = warp_sum(acc.sum_at(wm));
+      float wk = -INFINITY;
+      if (a.W <= 32 * nwarps) {
+        const int kth = (a.W + nwarps - 1) / nwarps - 1;
+        float v = mt;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) k = fminf(k, __shfl_xor_sync(0xffffffffu, k, o));
-      tau = k;
+        for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+          for (int j = k >> 1; j > 0; j >>= 1) {
+            const float o = __shfl_xor_sync(0xffffffffu, v, j);
+            v = (((lane & j) == 0) == ((lane & k) == 0)) ? fmaxf(v, o) : fminf(v, o);
+          }
+        }
+        wk = __shfl_sync(0xffffffffu, v, kth);
+      }
+      float* xr = red + (par ? 96 : 0);  // alternate rows: readers of one row never meet writers of the next
+      if (lane == 0) {
+        xr[tid >> 5] = wm;
+        xr[32 + (tid >> 5)] = ws;
+        xr[64 + (tid >> 5)] = wk;
+      }
+    }
+    // every thread has streamed this row and binned the previous one
+    __syncthreads();
+    if (pr >= 0) {  // export the previous row's bins and clear them (binned into again two rows on)
+      const int len = min(pbin + 1, kRowBins - 1);
+      if (tid == 0) a.rowlen[pr] = uint32_t(len);
+      for (int j = tid; j <= pbin; j += nt) {
+        if (j < len) a.rowhist[int64_t(pr) * kRowBins + j] = phist[j];
+        phist[j] = 0;
+      }
+    }
+    if (!cur) break;
+    {  // every warp combines the 32 entries in parallel, lane w taking warp w's (nwarps == 32)
+      static_assert(nwarps == 32, "one entry per lane");
+      const float* xr = red + (par ? 96 : 0);
+      const float mw = xr[lane];
+      m = warp_max(mw);
+      sum = warp_sum(mw == -INFINITY ? 0.f : xr[32 + lane] * ex2_approx((mw - m) * kLog2e));
+      if (a.W <= 32 * nwarps) {
+        float k = xr[64 + lane];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) k = fminf(k, __shfl_xor_sync(0xffffffffu, k, o));
+        tau = k;
+      }
     }
     if (tid == 0) a.rowstat[r] = make_float2(m, logf(sum));
-    prow = row;
     pr = r;
     ptau = tau;
     pm32 = m * kBinsPerNat;
@@ -492,7 +508,7 @@ int launch_select(SelArgs& a, bool vec, cudaStream_t s) {
       num_sms = 148;
   }
   const int slots = int((a.V / 8 + kStatThreads - 1) / kStatThreads);
-  if (std::is_same<T, __nv_bfloat16>::value && vec && a.mask == nullptr && slots <= kStatSlots) {
+  if (std::is_same<T, __nv_bfloat16>::value && vec && a.mask == nullptr && slots <= kStatSlots && rows < (int64_t(1) << 30)) {
     const size_t smem = stat_smem(slots);
     if (cudaFuncSetAttribute(rowstats_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
         cudaSuccess) {
