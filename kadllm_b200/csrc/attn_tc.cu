@@ -16,12 +16,15 @@
 // dims) for O += P V, and staged with one bulk copy.  kadllm_kv_tile builds it
 // from the [B, HK, L, D] cache, zero-padding the last block.
 //
-// One CTA = 128 query rows of one (request, kv head), 9 warps.  Query row r
+// One CTA = 128 query rows of one (request, kv head), 10 warps.  Query row r
 // (TMEM lane r) has two threads, r in warps 0-3 and r + 128 in warps 4-7 (the
 // same lane quadrant): they split each block's 64 key columns and the 256
 // output columns in halves, exchanging the block maximum through shared memory
 // so that both move the softmax reference identically.  Warp 8 issues every
-// MMA and bulk copy, so no softmax thread waits for a copy.  TMEM: S double
+// MMA; warp 9 issues the bulk copies, refilling a K buffer when the S MMA that
+// read it completes and a V buffer when its O MMA completes (per-buffer
+// barriers), so neither the softmax threads nor the MMA issuer wait behind a
+// copy, and the block barrier joins only the row warps and the issuer.  TMEM: S double
 // buffer (2 x 64 columns), O (256 columns).  Per key block j: MMA_S(j+1) runs
 // while the row threads turn S(j) into probabilities (exp2 domain; the
 // reference maximum only moves when a row maximum exceeds it by 8, so O is
@@ -40,8 +43,10 @@ constexpr int kBlk = 64;     // keys per block
 constexpr int kTile = kBlk * kD * 2;  // bytes of one K or V block (32 KB)
 constexpr int kSufMax = 8;
 constexpr int kRowThreads = 2 * kRows;  // two threads per query row: key columns / output columns split in halves
-constexpr int kThreads = kRowThreads + 32;  // + one warp that issues the MMAs and the bulk copies
-constexpr int kIssuer = kRowThreads;        // its issuing thread
+constexpr int kThreads = kRowThreads + 64;  // + one warp that issues the MMAs, one that issues the bulk copies
+constexpr int kIssuer = kRowThreads;        // the MMA-issuing thread
+constexpr int kProducer = kRowThreads + 32; // the copy-issuing thread
+constexpr int kBlockSync = kRowThreads + 32;  // threads of the per-block barrier: row warps + MMA warp
 
 struct AttnTcArgs {
   const __nv_bfloat16* q; int64_t sq_row, sq_t, sq_h;  // decode: row = beam row; causal: row = token b*L + pos
@@ -63,13 +68,24 @@ struct AttnTcSmem {
   static constexpr size_t v = k + 2 * size_t(kTile);             // V blocks [2]
   static constexpr size_t p = v + 2 * size_t(kTile);             // P [128 rows][64 keys] K-major core tile
   static constexpr size_t bm = p + size_t(kRows) * kBlk * 2;     // [2 halves][128 rows] fp32 exchange
-  static constexpr size_t bar = bm + size_t(2) * kRows * 4;       // ldK[2], ldV[2], S[2], O
-  static constexpr size_t slot = bar + 7 * 8;
+  static constexpr size_t bar = bm + size_t(2) * kRows * 4;       // ldK[2], ldV[2], S[2], O, vfree[2]
+  static constexpr size_t slot = bar + 9 * 8;
   static constexpr size_t bytes = slot + 8;
   static_assert(bytes <= 232448, "shared memory");
   // 16-byte unit (row r, chunk c) of a core tile whose rows have `chunks` 16-byte chunks
   __device__ static uint32_t off(int r, int c, int chunks) { return (r >> 3) * (chunks * 128) + c * 128 + (r & 7) * 16; }
 };
+
+// AND of `v` over the row warps and the MMA warp (named barrier 2)
+__device__ __forceinline__ bool block_and(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n bar.red.and.pred p, 2, %2, q;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(r)
+      : "r"(uint32_t(v)), "n"(kBlockSync)
+      : "memory");
+  return r != 0;
+}
 
 template <bool CAUSAL>
 __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a) {
@@ -82,10 +98,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
   uint64_t* ldV = ldK + 2;                                      // [2]
   uint64_t* barS = ldK + 4;                                     // [2]
   uint64_t* barO = ldK + 6;
+  uint64_t* vfree = ldK + 7;                                    // [2]: the O MMA that read V buffer s completed
   uint32_t* slot = reinterpret_cast<uint32_t*>(smem + M::slot);
   const int tid = threadIdx.x, warp = tid >> 5;
   const int row = tid & (kRows - 1), half = (tid / kRows) & 1;  // query row, column half
-  const bool rowthr = tid < kRowThreads;                         // warps 0-7 (warp 8 only issues)
+  const bool rowthr = tid < kRowThreads;                         // warps 0-7 (warps 8, 9 only issue)
   float* sbm = reinterpret_cast<float*>(smem + M::bm);           // partner exchange [half][row]
   const int b = blockIdx.y / a.HK, hk = blockIdx.y % a.HK;
   const int TG = a.T * a.G;
@@ -122,7 +139,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
 
   // ---- prologue: barriers, TMEM, Q tile, first K / V blocks, MMA_S(0) ----------------
   if (tid == 0) {
-    for (int i = 0; i < 7; ++i) tc::mbar_init(ldK + i, 1);
+    for (int i = 0; i < 9; ++i) tc::mbar_init(ldK + i, 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   if (warp == 0) tc::tmem_alloc(slot, 512);
@@ -166,8 +183,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
       tc::mma_bf16(tmem + 128, tc::smem_desc(sbase + M::p + kk * 256, 128, 1024),
                    tc::smem_desc(sbase + M::v + s * kTile + kk * 8192, 4096, 128), kIdO, j > 0 || kk > 0);
     tc::commit(barO);
+    tc::commit(vfree + s);
   };
-  if (tid == kIssuer && nb > 0) {
+  if (tid == kProducer && nb > 0) {
     load_k(0);
     load_v(0);
     if (nb > 1) {
@@ -185,26 +203,54 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
     issue_s(0);
   }
 
+  // The epilogue's operands are staged by the row threads during the last key block with one
+  // batch of cp.async: the gate rows into the K buffers (free once the last S MMA completed;
+  // 512-byte rows, chunk c of row r at c ^ (r % 32)), this CTA's beams' suffix keys / values into
+  // the V buffer of block nb - 2 (free once its O MMA completed; that of block 1 when nb = 1).
+  const int row_hi = min(row0 + kRows, R) - 1;
+  const int beam_lo = CAUSAL ? 0 : row0 / TG;
+  const int nbeams = CAUSAL ? 0 : row_hi / TG - beam_lo + 1;
+  const bool suf_smem = !CAUSAL && int64_t(nbeams) * a.T * kD * 2 * 2 <= int64_t(kTile);
+  unsigned char* const ssuf = smem + M::v + (nb >= 2 ? (nb - 2) & 1 : 1) * kTile;
+  auto stage_gate = [&]() {  // this thread's half of its own row
+    if (!a.gate || !rvalid) return;
+    const __nv_bfloat16* src =
+        CAUSAL ? a.gate + (seq0 + pos) * a.sg_row + int64_t(hq) * a.sg_h
+               : a.gate + (int64_t(b) * a.W + beam) * a.sg_row + int64_t(t) * a.sg_t + int64_t(hq) * a.sg_h;
+#pragma unroll 4
+    for (int c = half * (kD / 16); c < (half + 1) * (kD / 16); ++c)
+      cp_async16(smem + M::k + row * 512 + ((c ^ (row & 31)) * 16), src + c * 8);
+  };
+  auto stage_suffix = [&]() {
+    if (!suf_smem) return;
+    for (int i = tid; i < nbeams * a.T * 2 * (kD / 8); i += kRowThreads) {
+      const int c = i % (kD / 8), rest = i / (kD / 8), kv = rest & 1, bs = rest >> 1, sidx = bs % a.T, bi = bs / a.T;
+      const int64_t br = int64_t(b) * a.W + beam_lo + bi;
+      const __nv_bfloat16* src = kv ? a.sv + br * a.ssv_row + int64_t(sidx) * a.ssv_t + int64_t(hk) * a.ssv_h
+                                    : a.sk + br * a.ssk_row + int64_t(sidx) * a.ssk_t + int64_t(hk) * a.ssk_h;
+      cp_async16(ssuf + ((bi * a.T + sidx) * 2 + kv) * 512 + c * 16, src + c * 8);
+    }
+  };
+
   // ---- key blocks ----------------------------------------------------------------------
   const int key_lim = CAUSAL ? pos : Lb - 1;  // last key this row attends to
   float m_ref = -INFINITY, l = 0.f;            // exp2-domain reference maximum, running sum
-  for (int j = 0; j < nb; ++j) {
+  if (tid == kProducer) {  // refill each buffer as soon as the MMA that read it has completed
+    for (int j = 0; j + 2 < nb; ++j) {
+      ok = tc::mbar_wait(barS + (j & 1), uint32_t(j >> 1) & 1u, kWait) && ok;  // K(j) read by MMA_S(j)
+      if (!ok) break;
+      load_k(j + 2);
+      ok = tc::mbar_wait(vfree + (j & 1), uint32_t(j >> 1) & 1u, kWait) && ok;  // V(j) read by MMA_O(j)
+      if (!ok) break;
+      load_v(j + 2);
+    }
+  }
+  for (int j = 0; warp < 9 && j < nb; ++j) {  // row warps and the MMA warp
     const int sb = j & 1;
-    if (tid == kIssuer) {
-      if (j + 1 < nb) {  // MMA_S(j+1) overlaps this block's softmax
-        ok = tc::mbar_wait(ldK + ((j + 1) & 1), uint32_t((j + 1) >> 1) & 1u, kWait) && ok;
-        tc::fence_after();
-        issue_s(j + 1);
-      }
-      // refill each buffer as soon as the MMA that read it has completed
-      if (j + 2 < nb) {  // K(j) was read by MMA_S(j)
-        ok = tc::mbar_wait(barS + sb, uint32_t(j >> 1) & 1u, kWait) && ok;
-        load_k(j + 2);
-      }
-      if (j >= 1 && j + 1 < nb) {  // V(j-1) was read by MMA_O(j-1)
-        ok = tc::mbar_wait(barO, uint32_t(j - 1) & 1u, kWait) && ok;
-        load_v(j + 1);
-      }
+    if (tid == kIssuer && j + 1 < nb) {  // MMA_S(j+1) overlaps this block's softmax
+      ok = tc::mbar_wait(ldK + ((j + 1) & 1), uint32_t((j + 1) >> 1) & 1u, kWait) && ok;
+      tc::fence_after();
+      issue_s(j + 1);
     }
     // online softmax over block j: this thread takes key columns [32 half, 32 half + 32)
     float x[32];
@@ -212,6 +258,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
     if (rowthr) {
       ok = tc::mbar_wait(barS + sb, uint32_t(j >> 1) & 1u, kWait) && ok;
       tc::fence_after();
+      if (j == nb - 1) {  // every S MMA has completed: the K buffers are free
+        stage_gate();
+        if (nb == 1) stage_suffix();
+        cp_async_commit();
+      }
       uint32_t r[32];
       tc::ld32(tmem + lane_off + sb * kBlk + half * 32, r);
       tc::wait_ld();
@@ -253,6 +304,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
       if (j > 0) {  // MMA_O(j-1) complete: P is free and O is stable
         ok = tc::mbar_wait(barO, uint32_t(j - 1) & 1u, kWait) && ok;
         tc::fence_after();
+        if (j == nb - 1) {  // O(nb-2) has completed: its V buffer is free
+          stage_suffix();
+          cp_async_commit();
+        }
         if (resc) {  // this half's 128 output columns
 #pragma unroll 1
           for (int piece = half * (kD / 64); piece < (half + 1) * (kD / 64); ++piece) {
@@ -273,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
     }
     tc::fence_async_smem();
     tc::fence_before();
-    ok = __syncthreads_and(ok);  // P staged, S(j) and O rows read / rescaled
+    ok = block_and(ok);  // P staged, S(j) and O rows read / rescaled
     if (!ok) break;
     tc::fence_after();
     if (tid == kIssuer) {
@@ -283,52 +338,21 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
   }
 
   // ---- epilogue: merge the beam's suffix (decode), normalise, gate, store --------------
-  if (ok && nb > 0) {
-    ok = tc::mbar_wait(barO, uint32_t(nb - 1) & 1u, kWait);  // every MMA done: K / V / P buffers free
+  // every MMA done: K / V / P buffers free.  Only the row warps and the MMA warp wait: they passed the
+  // last block barrier after O(nb-2) completed, so the parity names O(nb-1); the copy warp, which
+  // writes nothing more, follows through the barrier below.
+  if (ok && nb > 0 && warp < 9) {
+    ok = tc::mbar_wait(barO, uint32_t(nb - 1) & 1u, kWait);
     tc::fence_after();
   }
-  // stage the gate rows (V buffers, 512-byte rows, chunk c at c ^ (row % 32)) and this CTA's
-  // beams' suffix keys / values (K buffers) with one batch of cp.async
-  auto row_map = [&](int r, int& rbeam, int& rt, int& rg, int& rpos) {
-    const int grr = row0 + r;
-    if (CAUSAL) { rpos = grr / a.G; rg = grr % a.G; rbeam = 0; rt = 0; }
-    else { rbeam = grr / TG; const int rem = grr % TG; rt = rem / a.G; rg = rem % a.G; rpos = 0; }
-  };
-  const int row_hi = min(row0 + kRows, R) - 1;
-  const int beam_lo = CAUSAL ? 0 : row0 / TG;
-  const int nbeams = CAUSAL ? 0 : row_hi / TG - beam_lo + 1;
-  const bool suf_smem = !CAUSAL && int64_t(nbeams) * a.T * kD * 2 * 2 <= int64_t(2) * kTile;
-  if (a.gate) {
-    for (int i = tid; i < kRows * (kD / 8); i += kThreads) {
-      const int r = i / (kD / 8), c = i % (kD / 8);
-      if (row0 + r > row_hi) continue;
-      int rb, rt, rg, rp;
-      row_map(r, rb, rt, rg, rp);
-      const int rhq = hk * a.G + rg;
-      const __nv_bfloat16* src =
-          CAUSAL ? a.gate + (seq0 + rp) * a.sg_row + int64_t(rhq) * a.sg_h
-                 : a.gate + (int64_t(b) * a.W + rb) * a.sg_row + int64_t(rt) * a.sg_t + int64_t(rhq) * a.sg_h;
-      cp_async16(smem + M::v + r * 512 + ((c ^ (r & 31)) * 16), src + c * 8);
-    }
-  }
-  if (suf_smem) {
-    for (int i = tid; i < nbeams * a.T * 2 * (kD / 8); i += kThreads) {
-      const int c = i % (kD / 8), rest = i / (kD / 8), kv = rest & 1, bs = rest >> 1, sidx = bs % a.T, bi = bs / a.T;
-      const int64_t br = int64_t(b) * a.W + beam_lo + bi;
-      const __nv_bfloat16* src = kv ? a.sv + br * a.ssv_row + int64_t(sidx) * a.ssv_t + int64_t(hk) * a.ssv_h
-                                    : a.sk + br * a.ssk_row + int64_t(sidx) * a.ssk_t + int64_t(hk) * a.ssk_h;
-      cp_async16(smem + M::k + ((bi * a.T + sidx) * 2 + kv) * 512 + c * 16, src + c * 8);
-    }
-  }
-  cp_async_commit();
   if (rowthr) sbm[half * kRows + row] = l;  // the halves' partial row sums
-  cp_async_wait<0>();
+  cp_async_wait<0>();                       // this thread's staged gate / suffix rows
   __syncthreads();
   if (rowthr) l = sbm[row] + sbm[kRows + row];
   const int64_t brow = int64_t(b) * a.W + beam;
   auto suf = [&](int sidx, int kv) -> const __nv_bfloat16* {  // this row's suffix key / value s
     if (suf_smem)
-      return reinterpret_cast<const __nv_bfloat16*>(smem + M::k + (((beam - beam_lo) * a.T + sidx) * 2 + kv) * 512);
+      return reinterpret_cast<const __nv_bfloat16*>(ssuf + (((beam - beam_lo) * a.T + sidx) * 2 + kv) * 512);
     return kv ? a.sv + brow * a.ssv_row + int64_t(sidx) * a.ssv_t + int64_t(hk) * a.ssv_h
               : a.sk + brow * a.ssk_row + int64_t(sidx) * a.ssk_t + int64_t(hk) * a.ssk_h;
   };
@@ -419,7 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
       uint32_t* rw = reinterpret_cast<uint32_t*>(&res);
       uint4 gv = make_uint4(0u, 0u, 0u, 0u);
       const int c = piece * 4 + q4;
-      if (a.gate) gv = *reinterpret_cast<const uint4*>(smem + M::v + row * 512 + ((c ^ (row & 31)) * 16));
+      if (a.gate) gv = *reinterpret_cast<const uint4*>(smem + M::k + row * 512 + ((c ^ (row & 31)) * 16));
       const uint32_t* gw = reinterpret_cast<const uint32_t*>(&gv);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -434,8 +458,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
       *reinterpret_cast<uint4*>(op + piece * 32 + q4 * 8) = res;
     }
   }
-  if (!ok && tid == kIssuer) {  // a wait timed out: report, give in-flight copies a bounded time
-    atomicOr(a.status, 1u);
+  if (!ok && (tid == 0 || tid == kIssuer || tid == kProducer)) atomicOr(a.status, 1u);  // a wait timed out
+  if (tid == kProducer) {  // every copy has landed (normally consumed already; bounded after a timeout)
     for (int s = 0; s < 2; ++s) {
       if (issued_k[s] > 0) tc::mbar_wait(ldK + s, uint32_t(issued_k[s] - 1) & 1u, kWait);
       if (issued_v[s] > 0) tc::mbar_wait(ldV + s, uint32_t(issued_v[s] - 1) & 1u, kWait);
