@@ -18,8 +18,10 @@
 //   2. threshold  per request: shifts every row histogram by the row's score
 //                 offset into a request histogram and picks the highest score
 //                 threshold that provably keeps >= width candidates above it;
-//   3. collect    per row: re-reads the logits, appends candidates >= threshold
-//                 (score, flat index) to a per-request buffer;
+//   3. collect    per row that can reach the threshold: appends candidates >=
+//                 threshold (score, flat index) to a per-request buffer, reading
+//                 only the 512-byte chunks whose maximum (a summary rowstats
+//                 writes when the workspace has room for it) reaches it;
 //   4. finalize   per request: bitonic sort of the buffer (score desc, index
 //                 asc), writes scores and the gathered history.
 // Buffers live in a caller-provided workspace (kadllm_beam_select_workspace).
@@ -52,6 +54,7 @@ struct SelArgs {
   uint32_t* count;             // [B]
   uint32_t* flags;             // [1] bit 0: candidate overflow
   unsigned long long* cand;    // [B, kCap]
+  uint16_t* vsum;              // [rows, kSumMax] bf16 maximum of each 32-vector chunk, or null
   int B, Wp, W, depth;
   int64_t V;
 };
@@ -156,11 +159,15 @@ __device__ __forceinline__ float ex2_approx(float x) {
 //     above it, so these counts are lower bounds of the element counts: the
 //     threshold they give still provably keeps >= width candidates (tau bounds
 //     >= W thread maxima, each in its own vector), and collect then gathers the
-//     elements exactly.  Pass 2 of row r runs inside pass 1 of the CTA's next
+//     elements exactly.  With room in the workspace the same pass records, per
+//     warp and slot, the maximum of the warp's 32 vectors (one contiguous
+//     512-byte chunk), so collect reads only the chunks that can hold
+//     candidates.  Pass 2 of row r runs inside pass 1 of the CTA's next
 //     row (two tables and two histograms, alternating), so the logits are read
 //     from HBM exactly once.
 constexpr int kStatThreads = 1024;
 constexpr int kStatSlots = 48;  // vectors per thread (V <= 48 * 8 * 1024) for the table
+constexpr int kSumMax = kStatSlots * 32;  // chunks per row: (slot k, warp w) = vectors k * 1024 + 32 w + [0, 32)
 constexpr float kRefSlack = 64.f;
 __host__ __device__ constexpr size_t stat_smem(int slots) { return size_t(2) * slots * kStatThreads * 2; }
 
@@ -223,6 +230,9 @@ __global__ void __launch_bounds__(kStatThreads, 1) rowstats_bf16_kernel(const Se
   const int slots = (nvec + nt - 1) / nt;
   const int tid = threadIdx.x, lane = tid & 31;
   for (int j = tid; j < 2 * kRowBins; j += nt) hists[j / kRowBins][j % kRowBins] = 0;
+  for (int j = tid; j < 2 * slots * nt / 8; j += nt)  // table entries past the row's vectors stay -inf
+    reinterpret_cast<uint4*>(vmax)[j] = make_uint4(0xff80ff80u, 0xff80ff80u, 0xff80ff80u, 0xff80ff80u);
+  __syncthreads();  // before any thread writes its own entries
   // the CTA's previous row, binned while the current one streams in
   int pr = -1;
   float ptau = 0.f, pm32 = 0.f;
@@ -244,6 +254,7 @@ __global__ void __launch_bounds__(kStatThreads, 1) rowstats_bf16_kernel(const Se
     __nv_bfloat16* tcur = vmax + size_t(par) * slots * nt + tid;
     const __nv_bfloat16* tprev = vmax + size_t(par ^ 1) * slots * nt + tid;
     uint32_t* phist = hists[par ^ 1];  // the previous row's bins
+    uint16_t* psum = a.vsum && pr >= 0 ? a.vsum + int64_t(pr) * kSumMax : nullptr;
     // previous row's vector at slot k (present: inside the row): bin its maximum if it reaches tau
     auto bin_prev = [&](int k, bool present) {
       if (present && pact) {
@@ -280,6 +291,22 @@ __global__ void __launch_bounds__(kStatThreads, 1) rowstats_bf16_kernel(const Se
       }
     } else if (pr >= 0) {
       for (int k = 0; wfirst + k * nt < nvec; ++k) bin_prev(k, tid + k * nt < nvec);
+    }
+    if (psum) {  // the previous row's chunk maxima, from its table (intact until the barrier below):
+      // chunk (slot k, warp w) = table entries [k][32 w, 32 w + 32), one chunk per thread, the
+      // four 16-byte reads rotated so that a warp's reads spread over all banks
+      const __nv_bfloat16* tb = vmax + size_t(par ^ 1) * slots * nt;
+      for (int c = tid; c < slots * 32; c += nt) {
+        const uint4* src = reinterpret_cast<const uint4*>(tb + (c >> 5) * nt + (c & 31) * 32);
+        __nv_bfloat162 m2 = __bfloat162bfloat162(__ushort_as_bfloat16(0xff80u));
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const uint4 u = src[(jj + (c >> 1)) & 3];
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+          m2 = __hmax2(m2, __hmax2(__hmax2(h[0], h[1]), __hmax2(h[2], h[3])));
+        }
+        psum[c] = __bfloat16_as_ushort(__hmax(__low2bfloat16(m2), __high2bfloat16(m2)));  // NaN ignored
+      }
     }
     // one exchange per row: each warp publishes its maximum, its sum rescaled to that
     // maximum and its ceil(W/n)-th largest thread maximum; every thread combines the 32
@@ -425,6 +452,44 @@ __global__ void __launch_bounds__(256) collect_kernel(const SelArgs a, bool vec)
   const uint8_t* mrow = a.mask ? a.mask + r * a.V : nullptr;
   const uint32_t base_idx = uint32_t(int64_t(w) * a.V);
   unsigned long long* out = a.cand + int64_t(b) * kCap;
+  if (std::is_same<T, __nv_bfloat16>::value && a.vsum) {
+    // only the 512-byte chunks whose maximum reaches tau (the score is monotonic in x)
+    const int nvec = int(a.V / 8), nchunk = (nvec + 1023) / 1024 * 32;
+    const uint16_t* vs = a.vsum + r * kSumMax;
+    const uint4* row4 = reinterpret_cast<const uint4*>(row);
+    const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int c0 = (threadIdx.x >> 5) * 32; c0 < nchunk; c0 += nw * 32) {
+      bool hit = false;
+      const int c = c0 + lane;
+      if (c < nchunk && (c >> 5) * 1024 + (c & 31) * 32 < nvec) {  // a chunk holding vectors of the row
+        const float x = __uint_as_float(uint32_t(vs[c]) << 16);
+        hit = ((x - st.x) - st.y) + p >= tau;
+      }
+      uint32_t bal = __ballot_sync(0xffffffffu, hit);
+      while (bal) {
+        const int cc = c0 + __ffs(bal) - 1;
+        bal &= bal - 1;
+        const int vi = (cc >> 5) * 1024 + (cc & 31) * 32 + lane;
+        if (vi < nvec) {
+          const uint4 u = row4[vi];
+          const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float x = __bfloat162float(e[j]);
+            const float score = ((x - st.x) - st.y) + p;
+            if (score >= tau && score > -INFINITY) {
+              const uint32_t pos = atomicAdd(&a.count[b], 1u);
+              if (pos < kCap) {
+                const uint32_t idx = base_idx + uint32_t(vi * 8 + j);
+                out[pos] = (static_cast<unsigned long long>(order_key(score)) << 32) | (0xffffffffu - idx);
+              }
+            }
+          }
+        }
+      }
+    }
+    return;
+  }
   for_row<T>(row, a.V, vec, [&](int64_t i, float x) {
     const float score = ((x - st.x) - st.y) + p;
     if (score >= tau && score > -INFINITY && (mrow == nullptr || mrow[i])) {
@@ -483,7 +548,9 @@ __global__ void __launch_bounds__(1024) finalize_kernel(const SelArgs a) {
 }
 
 struct Workspace {
-  size_t rowstat, rowlen, rowhist, thresh, count, flags, cand, total;
+  // `base` bytes are required; the chunk-maximum summary after them (up to `total`) is optional:
+  // without it collect reads whole rows
+  size_t rowstat, rowlen, rowhist, thresh, count, flags, cand, vsum, base, total;
   Workspace(int64_t B, int64_t Wp) {
     auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
     const int64_t rows = B * Wp;
@@ -494,7 +561,8 @@ struct Workspace {
     count = al(thresh + B * sizeof(float));
     flags = al(count + B * sizeof(uint32_t));
     cand = al(flags + sizeof(uint32_t));
-    total = al(cand + B * kCap * sizeof(unsigned long long));
+    vsum = base = al(cand + B * kCap * sizeof(unsigned long long));
+    total = al(vsum + rows * kSumMax * sizeof(uint16_t));
   }
 };
 
@@ -516,8 +584,10 @@ int launch_select(SelArgs& a, bool vec, cudaStream_t s) {
       return KADLLM_ECUDA;
     }
     rowstats_bf16_kernel<<<unsigned(rows < num_sms ? rows : num_sms), kStatThreads, smem, s>>>(a);
-  } else
+  } else {
+    a.vsum = nullptr;  // only the BF16 kernel writes the chunk summary
     rowstats_kernel<T><<<unsigned(rows), kRowThreads, 0, s>>>(a, vec);
+  }
   threshold_kernel<<<a.B, 1024, 0, s>>>(a);
   collect_kernel<T><<<unsigned(rows), 256, 0, s>>>(a, vec);
   int N = 1;
@@ -558,7 +628,7 @@ int select_with_workspace(const void* logits, int logits_dtype, int64_t ld_row, 
   KB_REQUIRE(logits && out_scores && out_history && workspace && (depth == 0 || old_history), KADLLM_EINVAL,
              "beam select: null pointer");
   const Workspace ws(batch, prev_width);
-  KB_REQUIRE(workspace_bytes >= int64_t(ws.total), KADLLM_EINVAL, "beam select: workspace too small");
+  KB_REQUIRE(workspace_bytes >= int64_t(ws.base), KADLLM_EINVAL, "beam select: workspace too small");
   KB_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, KADLLM_EINVAL,
              "beam select: workspace must be 256-byte aligned");
   char* w = static_cast<char*>(workspace);
@@ -573,6 +643,7 @@ int select_with_workspace(const void* logits, int logits_dtype, int64_t ld_row, 
   a.count = reinterpret_cast<uint32_t*>(w + ws.count);
   a.flags = flags ? flags : reinterpret_cast<uint32_t*>(w + ws.flags);
   a.cand = reinterpret_cast<unsigned long long*>(w + ws.cand);
+  a.vsum = workspace_bytes >= int64_t(ws.total) ? reinterpret_cast<uint16_t*>(w + ws.vsum) : nullptr;
   a.B = int(batch); a.Wp = int(prev_width); a.W = int(width); a.depth = int(depth); a.V = vocab;
   const int esz = dtype_size(logits_dtype);
   const int vw = 16 / esz;
@@ -666,10 +737,10 @@ extern "C" int kadllm_beam_select_noalloc(const void* logits, int logits_dtype, 
   KB_REQUIRE(out_flags, KADLLM_EINVAL, "beam select (no-alloc): null flags pointer");
   KB_REQUIRE(batch >= 1 && prev_width >= 1, KADLLM_EINVAL, "beam select (no-alloc): empty dimensions");
   const Workspace ws(batch, prev_width);
-  KB_REQUIRE(ws.total <= kNoAllocScratchBytes && batch <= 32 && batch * prev_width <= 512, KADLLM_EINVAL,
+  KB_REQUIRE(ws.base <= kNoAllocScratchBytes && batch <= 32 && batch * prev_width <= 512, KADLLM_EINVAL,
              "beam select (no-alloc): batch %lld x prev_width %lld needs %zu bytes of scratch; the static "
              "maximum is %zu bytes (batch <= 32, batch * prev_width <= 512)",
-             (long long)batch, (long long)prev_width, ws.total, kNoAllocScratchBytes);
+             (long long)batch, (long long)prev_width, ws.base, kNoAllocScratchBytes);
   void* scratch = nullptr;
   if (int rc = scratch_for_current_device(&scratch)) return rc;
   // the caller's flag word replaces the scratch flag word: clear it, the kernels OR into it
