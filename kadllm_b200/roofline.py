@@ -68,11 +68,11 @@ def measured_traffic(name: str, args: tuple) -> float | None:
     if name == "kadllm_gdn_mixer_replay" and tuple(args[11:13]) == (32, 256) and tuple(args[14:18]) == (16, 16, 128, 128):
         return {1: 186.4e6, 2: 359.3e6}.get(args[13])  # T = 1: 165.5 + 20.9 MB; T = 2: 306.2 + 53.2 MB
     if name == "kadllm_attention_tiled" and (args[24], *args[27:31]) == (32, 8, 2, 1024, 256):
-        if args[32]:  # causal prefill: 335.7 + 110.6 MB
-            return 446.3e6
-        return 283.1e6 if tuple(args[25:27]) == (256, 2) else None  # decode T = 2: 235.0 + 48.0 MB
+        if args[32]:  # causal prefill: 335.6 + 109.8 MB
+            return 445.4e6
+        return 285.4e6 if tuple(args[25:27]) == (256, 2) else None  # decode T = 2: 235.0 + 50.4 MB
     if name == "kadllm_beam_select" and tuple(args[10:13]) == (32, 256, 248320):
-        return 4822.0e6  # rowstats 4276.2 + 5.2 MB, collect 537.0 + 3.6 MB
+        return 4100.4e6  # rowstats 4068.7 + 21.2 MB, collect 8.7 MB, threshold 1.3 MB, finalize 0.2 MB
     return None
 
 
