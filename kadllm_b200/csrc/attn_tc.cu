@@ -448,10 +448,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         float v0 = o[q4 * 8 + 2 * e] * inv, v1 = o[q4 * 8 + 2 * e + 1] * inv;
-        if (a.gate) {
+        if (a.gate) {  // bf16(o) * bf16(sigmoid(gate)), each pair rounded by one packed conversion
           const float2 gf = bf2f(gw[e]);
-          v0 = bf16r(v0) * bf16r(fast_rcp(1.f + fast_ex2(-1.4426950408889634f * gf.x)));
-          v1 = bf16r(v1) * bf16r(fast_rcp(1.f + fast_ex2(-1.4426950408889634f * gf.y)));
+          const float2 vr = bf2f(bf2_pack(v0, v1));
+          const float2 sr = bf2f(bf2_pack(fast_rcp(1.f + fast_ex2(-1.4426950408889634f * gf.x)),
+                                          fast_rcp(1.f + fast_ex2(-1.4426950408889634f * gf.y))));
+          v0 = vr.x * sr.x;
+          v1 = vr.y * sr.y;
         }
         rw[e] = bf2_pack(v0, v1);
       }

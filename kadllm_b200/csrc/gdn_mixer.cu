@@ -346,8 +346,9 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
       const float2 z = bf2f(*reinterpret_cast<const uint32_t*>(rowg + 6 * D + col * 2));
       const float2 w = *reinterpret_cast<const float2*>(sNw + col);
       const float2 sz = silu2(z);
-      const float h0 = bf16r(w.x * bf16r(of.x * inv)), h1 = bf16r(w.y * bf16r(of.y * inv));
-      *reinterpret_cast<uint32_t*>(rowg + col * 2) = bf2_pack(h0 * sz.x, h1 * sz.y);
+      const float2 n = bf2f(bf2_pack(of.x * inv, of.y * inv));  // bf16(o * inv), the pair in one conversion
+      const float2 h = bf2f(bf2_pack(w.x * n.x, w.y * n.y));    // bf16(w * .)
+      *reinterpret_cast<uint32_t*>(rowg + col * 2) = bf2_pack(h.x * sz.x, h.y * sz.y);
     }
     __syncwarp();
     // ---- the octet's output rows, 16 bytes per store ------------------------------------

@@ -257,7 +257,11 @@ __global__ void __launch_bounds__(256) qk_norm_rope_d256_kernel(
   const float4 w0 = *reinterpret_cast<const float4*>(w), w1 = *reinterpret_cast<const float4*>(w + 4);
   const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-  for (int e = 0; e < 8; ++e) v[e] = bf16r((v[e] * inv) * (1.0f + wv[e]));
+  for (int j = 0; j < 4; ++j) {  // bf16 rounding of each pair in one packed conversion
+    const float2 n = bf2f(bf2_pack((v[2 * j] * inv) * (1.0f + wv[2 * j]), (v[2 * j + 1] * inv) * (1.0f + wv[2 * j + 1])));
+    v[2 * j] = n.x;
+    v[2 * j + 1] = n.y;
+  }
   // partial rotary: dims [0, rot) rotate with the partner half rot/2 away (rot/2 % 8 == 0)
   const int half = rot / 2;
   float pv[8];
@@ -272,8 +276,11 @@ __global__ void __launch_bounds__(256) qk_norm_rope_d256_kernel(
     for (int j = 0; j < 4; ++j) {
       const float2 c = bf2f(cw[j]), sn = bf2f(sw[j]);
       const float r0 = lo ? -pv[2 * j] : pv[2 * j], r1 = lo ? -pv[2 * j + 1] : pv[2 * j + 1];  // rotate_half
-      v[2 * j] = bf16r(bf16r(v[2 * j] * c.x) + bf16r(r0 * sn.x));
-      v[2 * j + 1] = bf16r(bf16r(v[2 * j + 1] * c.y) + bf16r(r1 * sn.y));
+      const float2 vc = bf2f(bf2_pack(v[2 * j] * c.x, v[2 * j + 1] * c.y));  // bf16(x cos)
+      const float2 rs = bf2f(bf2_pack(r0 * sn.x, r1 * sn.y));                // bf16(rotate_half(x) sin)
+      const float2 sum = bf2f(bf2_pack(vc.x + rs.x, vc.y + rs.y));
+      v[2 * j] = sum.x;
+      v[2 * j + 1] = sum.y;
     }
   }
   __nv_bfloat16* dst = h < Hq ? q_out + int64_t(r) * sq_row + h * sq_h + lane * 8
