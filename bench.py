@@ -30,6 +30,7 @@ import json
 import os
 import statistics
 import subprocess
+import tempfile
 import sys
 import time
 from pathlib import Path
@@ -73,7 +74,7 @@ class ClockSampler:
     def __init__(self, gpu: int):
         self.gpu = gpu
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_gpu{gpu}.csv"
+        self.path = Path(tempfile.gettempdir()) / f"kadllm_b200_clocks_gpu{gpu}_{os.getpid()}.csv"
 
     def __enter__(self):
         try:
@@ -100,7 +101,9 @@ class ClockSampler:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         mhz, mx, reasons = [], None, set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in self.path.read_text().splitlines():
+        text = self.path.read_text()
+        self.path.unlink(missing_ok=True)
+        for line in text.splitlines():
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
