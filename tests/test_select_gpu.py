@@ -54,15 +54,18 @@ def test_search_matches_reference_golden():
 @pytest.mark.parametrize("dtype,B,Wp,V,W", [
     (torch.float32, 3, 16, 5000, 64), (torch.bfloat16, 3, 16, 5000, 64), (torch.float16, 3, 16, 5000, 64),
     (torch.bfloat16, 3, 16, 65536, 256), (torch.bfloat16, 3, 16, 65536, 500), (torch.bfloat16, 3, 16, 65536, 1100),
-    (torch.bfloat16, 4, 96, 32768, 256)])
+    (torch.bfloat16, 4, 96, 32768, 256), (torch.bfloat16, 3, 16, 8200, 64), (torch.bfloat16, 2, 16, 10001, 64)])
 def test_select_step_matches_oracle_with_tie_rule(dtype, B, Wp, V, W):
     """One step over bf16-quantised logits (many exact ties): scores and the
     lowest-index tie rule must match the oracle's stable top-k exactly.  The
     V = 65536 BF16 cases give every thread of the row-statistics kernel a
     64-element slice, so its per-row top-W pruning bound is finite (W = 256
     and 500, ranks 8 and 16 of each warp's thread maxima) or disabled
-    (W = 1100 > 32 x 32 warps); 4 x 96 rows exceed one row per SM, so rows are
-    binned from L2 while the next row streams in."""
+    (W = 1100 > 32 x 32 warps); 4 x 96 rows exceed one row per SM, so a row's
+    vector maxima are binned from shared memory while the next row streams in.  V = 8200 (1025 vectors) leaves
+    one vector in a second table slot, so collect's chunk summary holds a
+    partial chunk past the first slot; V = 10001 (not a multiple of 8) takes the
+    element-wise statistics path without the summary."""
     from kadllm_b200.grbeam import BeamSelector
 
     rng = np.random.default_rng(0)
