@@ -24,14 +24,15 @@
 // MMA; warp 9 issues the bulk copies, refilling a K buffer when the S MMA that
 // read it completes and a V buffer when its O MMA completes (per-buffer
 // barriers), so neither the softmax threads nor the MMA issuer wait behind a
-// copy, and the block barrier joins only the row warps and the issuer.  TMEM: S double
-// buffer (2 x 64 columns), O (256 columns).  Per key block j: MMA_S(j+1) runs
-// while the row threads turn S(j) into probabilities (exp2 domain; the
-// reference maximum only moves when a row maximum exceeds it by 8, so O is
-// rescaled rarely) and write P (BF16, K-major core tile) to shared memory;
-// after the block barrier the issuer starts O += P V(j).  K and V blocks are double-buffered, refilled as
-// soon as the MMA that read them completes.  Every mbarrier wait is bounded and
-// reports through a status word.
+// copy, and the block barrier joins only the row warps and the MMA warp.
+// TMEM: S double buffer (2 x 64 columns), O (256 columns).  Per key block j:
+// MMA_S(j+1) runs while the row threads turn S(j) into probabilities (exp2
+// domain; the reference maximum only moves when a row maximum exceeds it by 8,
+// so O is rescaled rarely) and write P (BF16, K-major core tile) to shared
+// memory; after the block barrier the issuer starts O += P V(j).  K and V blocks
+// are double-buffered.  The epilogue's gate and suffix rows are staged during
+// the last key block.  Every mbarrier wait is bounded and reports through a
+// status word.
 #include "tcgen05.cuh"
 
 namespace kb {
