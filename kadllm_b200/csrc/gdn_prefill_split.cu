@@ -179,12 +179,19 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const SplitArgs a) {
   const __nv_bfloat16* prow0 = a.proj + seq0 * a.ld_proj;
 
   // ---- stage the raw projection tile (tokens t0-3 .. t0+63, zero outside [0, L)) -----
-  for (int i = tid; i < (kC + 3) * (NCH / 8); i += NT) {
-    const int r = i / (NCH / 8), lc = (i % (NCH / 8)) * 8;
-    const int t = t0 - 3 + r;
-    __nv_bfloat16* dst = sRawT + r * RS + lc;
-    if (t >= 0 && t < L) cp_async16(dst, prow0 + int64_t(t) * a.ld_proj + chan(lc));
-    else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+  {  // each thread keeps one 16-byte column chunk and walks the rows GRP at a time
+    constexpr int CPR = NCH / 8, GRP = NT / CPR;  // chunks per staged row, rows staged at once
+    static_assert(GRP >= 1, "a block stages at least one row at a time");
+    if (tid < GRP * CPR) {
+      const int lc = (tid % CPR) * 8;
+      const __nv_bfloat16* src = prow0 + chan(lc);
+      __nv_bfloat16* dst = sRawT + lc;
+      for (int r = tid / CPR; r < kC + 3; r += GRP) {
+        const int t = t0 - 3 + r;
+        if (t >= 0 && t < L) cp_async16(dst + r * RS, src + int64_t(t) * a.ld_proj);
+        else *reinterpret_cast<uint4*>(dst + r * RS) = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
   }
   cp_async_commit();
   float gb = 0.f, ga = 0.f;  // gate inputs of token t0 + tid
