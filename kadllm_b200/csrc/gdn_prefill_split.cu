@@ -113,8 +113,9 @@ struct PrepSmem {
   static constexpr size_t k = q + size_t(kC) * SQ * 2;       // k, later K'
   static constexpr size_t v = k + size_t(kC) * SQ * 2;       // v, later U
   static constexpr size_t vec = v + size_t(kC) * SV * 2;     // G | beta | raw g | e^G | beta e^G | e^{G_last - G}
-  static constexpr size_t bytes = vec + size_t(kC) * 4 * 6;
-  static_assert(t1 % 16 == 0 && a % 16 == 0 && q % 16 == 0 && k % 16 == 0 && v % 16 == 0, "alignment");
+  static constexpr size_t cw = vec + size_t(kC) * 4 * 6;     // the head's conv taps [NCH][4] bf16
+  static constexpr size_t bytes = cw + size_t(NCH) * 4 * 2;
+  static_assert(t1 % 16 == 0 && a % 16 == 0 && q % 16 == 0 && k % 16 == 0 && v % 16 == 0 && cw % 16 == 0, "alignment");
 };
 
 // Copy a [kC][COLS] bf16 tile from padded shared rows to global, 16 bytes a thread, consecutive
@@ -163,6 +164,7 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const SplitArgs a) {
   float* sEG = sRaw + kC;     // e^{G_i}
   float* sBEG = sEG + kC;     // beta_i e^{G_i}
   float* sEGL = sBEG + kC;    // e^{G_last - G_i}
+  __nv_bfloat16* sCw = reinterpret_cast<__nv_bfloat16*>(smem + M::cw);  // [NCH][4] conv taps of the head
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int c = blockIdx.x;
@@ -192,6 +194,8 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const SplitArgs a) {
         else *reinterpret_cast<uint4*>(dst + r * RS) = make_uint4(0u, 0u, 0u, 0u);
       }
     }
+    for (int i = tid; i < NCH / 2; i += NT)  // conv taps: 16 bytes = two channels' four taps
+      cp_async16(sCw + i * 8, a.conv_w + int64_t(chan(2 * i)) * 4);
   }
   cp_async_commit();
   float gb = 0.f, ga = 0.f;  // gate inputs of token t0 + tid
@@ -207,10 +211,10 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const SplitArgs a) {
   constexpr int NG = NCH / 8, SEG = 4;
   for (int item = tid; item < NG * (kC / SEG); item += NT) {
     const int grp = item % NG, seg = item / NG;
-    const int lc = grp * 8, ch = chan(lc);
+    const int lc = grp * 8;
     float2 w2[4][4];  // [channel pair][tap]
     {
-      const uint4* wp = reinterpret_cast<const uint4*>(a.conv_w + int64_t(ch) * 4);
+      const uint4* wp = reinterpret_cast<const uint4*>(sCw + lc * 4);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {  // uint4 u = taps of channels 2u, 2u + 1
         const uint4 raw = wp[u];
