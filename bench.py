@@ -19,8 +19,8 @@ The working set (1.5 GB of weights, GBs of activations / logits) exceeds the
 126 MB L2, so no explicit flush is needed between steps.
 
 ``--impl reference`` times the reference algorithm's CPU restatement (the
-numpy oracle port of Kadllm's torch path) on the host cores for one request
-per step; rank 0 only.
+numpy oracle port of Kadllm's torch path) on all host cores, one whole request
+per step (as many steps as fit a bounded CPU budget, reported as run); rank 0 only.
 """
 
 from __future__ import annotations
@@ -129,80 +129,86 @@ def measured_peaks() -> tuple[dict, str]:
 # ---------------------------------------------------------------------------
 # CPU legs (oracle port of the reference's torch path)
 # ---------------------------------------------------------------------------
-def cpu_reference_sample(weights_np, cfg, seed: int, prompt=PROMPT) -> tuple[float, str]:
-    """Seconds for one request through the oracle (fp32, all host threads),
-    measured on a bounded sample: the request runs once through one period of
-    the layer pattern (the first ``P`` layers, e.g. 3 Gated-DeltaNet + 1
-    attention) and once with no layers (embedding, final norm, LM head and the
-    beam selection only); the layer time is scaled to the full depth:
-    t = t_0 + (num_layers / P) (t_P - t_0).  Returns (seconds, description)."""
+def host_threads() -> int:
+    """Use every host core for the CPU legs, whatever OMP_NUM_THREADS the launcher
+    set (torch.distributed.run sets 1): numpy's BLAS pool and torch's intra-op pool."""
+    n = os.cpu_count() or 1
+    try:
+        from threadpoolctl import threadpool_limits
+
+        threadpool_limits(limits=n)
+    except ImportError:  # pragma: no cover - threadpoolctl is in the image
+        pass
+    import torch
+
+    torch.set_num_threads(n)
+    return n
+
+
+def cpu_reference_request(weights_np, cfg, seed: int, prompt=PROMPT, n_layers=None) -> float:
+    """Seconds for one whole request through the oracle (fp32): prefill of a
+    ``prompt``-token prompt, two decode steps of ``BEAM`` beams and three
+    selections over the full vocabulary, through all ``n_layers`` layers (default:
+    the model's depth)."""
     import dataclasses
 
     from kadllm_b200.synthetic import random_prompts
     from oracle import grbeam_oracle as O
 
-    period = 1
-    while cfg.layer_types[period - 1] != "full_attention" and period < cfg.num_layers:
-        period += 1
+    n = cfg.num_layers if n_layers is None else n_layers
+    sub = dataclasses.replace(cfg, layer_types=tuple(cfg.layer_types[:n]))
     ids = random_prompts(1, prompt, cfg.vocab_size, seed=seed)
-
-    def timed(n_layers: int) -> float:
-        sub = dataclasses.replace(cfg, layer_types=tuple(cfg.layer_types[:n_layers]))
-        orc = O.HybridOracle(sub, weights_np, "fp32")
-        t0 = time.perf_counter()
-        O.grbeam_search(orc, ids, [BEAM] * DEPTH)
-        return time.perf_counter() - t0
-
-    t_head = timed(0)
-    t_period = timed(period)
-    total = t_head + cfg.num_layers / period * max(t_period - t_head, 0.0)
-    desc = (f"1 request (prefix {prompt}, beam {BEAM}, {DEPTH} tokens) through the numpy oracle (fp32): "
-            f"layers 0-{period - 1} ({t_period:.1f} s) and no layers ({t_head:.1f} s) timed, layer time "
-            f"scaled x{cfg.num_layers // period} to {cfg.num_layers} layers")
-    return total, desc
+    orc = O.HybridOracle(sub, weights_np, "fp32")
+    t0 = time.perf_counter()
+    O.grbeam_search(orc, ids, [BEAM] * DEPTH)
+    return time.perf_counter() - t0
 
 
-def numpy_weights_from(model_weights, max_layer: int = 4):
-    """fp32 numpy copies of the weights the CPU sample touches (layers < max_layer)."""
-    out = {}
-    for k, v in model_weights.items():
-        if k.startswith("layers.") and int(k.split(".")[1]) >= max_layer:
-            continue
-        out[k] = v.float().cpu().numpy()
-    return out
+def numpy_weights_from(model_weights):
+    """fp32 numpy copies of the benchmark weights (the oracle's input)."""
+    return {k: v.float().cpu().numpy() for k, v in model_weights.items()}
+
+
+CPU_BUDGET_S = 150.0  # the reference arm's timed samples stop once this much CPU time is spent
 
 
 def run_reference(args, rank: int, world: int) -> None:
+    """The reference arm: the oracle port on the host cores, rank 0 only.  Each step
+    is one whole request (24 layers, prefix 1024, beam 256, 3 tokens); the arm
+    runs the requested steps or as many as fit ``CPU_BUDGET_S`` (at least one),
+    and reports the steps it ran."""
     if rank != 0:
         return
-    import torch
-
     from kadllm_b200.config import QWEN35_08B
     from kadllm_b200.synthetic import numpy_weights
 
-    import dataclasses
-
     cfg = QWEN35_08B
-    # the CPU sample runs the first layer period only: generate just those weights
-    weights = numpy_weights(dataclasses.replace(cfg, layer_types=cfg.layer_types[:4]), seed=0, init="spec")
-    threads = os.cpu_count() or 1
-    times, desc = [], ""
-    for i in range(min(args.warmup, 1) + args.steps):  # one warm-up sample at most: each is ~10-30 s
-        dt, desc = cpu_reference_sample(weights, cfg, seed=i)
-        if i >= min(args.warmup, 1):
-            times.append(dt)
+    threads = host_threads()
+    weights = numpy_weights(cfg, seed=0, init="spec")
+    warm = 0
+    if args.warmup:  # one short warm-up: the embedding, final norm, LM head and selections only
+        cpu_reference_request(weights, cfg, seed=999, n_layers=0)
+        warm = 1
+    times = []
+    t_start = time.perf_counter()
+    for i in range(max(1, args.steps)):
+        times.append(cpu_reference_request(weights, cfg, seed=i))
+        if time.perf_counter() - t_start + statistics.mean(times) > CPU_BUDGET_S:
+            break
     per_req = statistics.mean(times)
     value = 1.0 / per_req
+    sample = (f"{len(times)} whole request(s) (24 layers, prefix {PROMPT}, beam {BEAM}, {DEPTH} tokens, full "
+              f"vocabulary) through the numpy oracle port (fp32), one per step, {threads} host threads; "
+              f"{per_req:.1f} s per request (min {min(times):.1f}, max {max(times):.1f})")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "requests/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_req * 1000, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD + " (CPU sample: 1 request per step)", "global_batch": 1,
+        "steps": len(times), "steps_requested": args.steps, "warmup": warm, "ms_per_step": per_req * 1000,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD + " (CPU: 1 request per step)", "global_batch": 1,
                    "seq_len": PROMPT, "beam": BEAM, "depth": DEPTH, "parallelism": "host cores"},
-        "cpu_baseline": {"value": value, "unit": "requests/s", "cores": threads, "kind": "port",
-                         "sample": desc + f"; one sample per step, {threads} host threads"},
+        "cpu_baseline": {"value": value, "unit": "requests/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "requests/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "torch_threads": torch.get_num_threads(),
+        "host_threads": threads,
     }
     print(json.dumps(line), flush=True)
 
@@ -428,12 +434,12 @@ def profile_kernels(engine, adapter, ids_dev, widths, args):
 
 
 def cpu_baseline(weights, cfg) -> dict:
-    """The oracle port on the host cores for one request (fp32)."""
-    w = numpy_weights_from(weights)
-    dt, desc = cpu_reference_sample(w, cfg, seed=123)
-    threads = os.cpu_count() or 1
+    """The oracle port on the host cores: one whole request (fp32, the benchmark's weights)."""
+    threads = host_threads()
+    dt = cpu_reference_request(numpy_weights_from(weights), cfg, seed=123)
     return {"value": 1.0 / dt, "unit": "requests/s", "cores": threads, "kind": "port",
-            "sample": desc + f" = {dt:.1f} s per request on {threads} host threads"}
+            "sample": f"1 whole request (24 layers, prefix {PROMPT}, beam {BEAM}, {DEPTH} tokens, full vocabulary) "
+                      f"through the numpy oracle port (fp32): {dt:.1f} s on {threads} host threads"}
 
 
 def main() -> None:

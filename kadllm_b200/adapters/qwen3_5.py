@@ -100,6 +100,10 @@ class Qwen35GRBeamAdapter:
         if history.ndim != 3 or min(history.shape) < 1 or history.shape[0] != state.batch:
             raise ValueError("history must be nonempty [B,W,T] matching the prefix")
 
+    def check(self) -> None:
+        """Raise if a tensor-core kernel of the engine reported a timed-out wait (synchronises)."""
+        self.engine.check()
+
     @torch.no_grad()
     def decode(self, history, state):
         self._check_state(history, state)

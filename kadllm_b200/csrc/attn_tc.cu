@@ -7,7 +7,7 @@
 // log-sum-exp) and the SDPA call of Qwen3_5Attention on the prompt
 // (transformers/models/qwen3_5/modeling_qwen3_5.py:620-692), with the output
 // gate out = bf16(bf16(o) * bf16(sigmoid(gate))) (src/kadllm/adapters/
-// qwen3_5.py:328-330).
+// qwen3_5.py:199-201).
 //
 // Tiled prefix: for each (request, kv head) the keys (and values) sit in
 // blocks of 64 positions x 256 dims, each block a 32 KB core-matrix image

@@ -1,6 +1,6 @@
 // Per-request beam selection over the full vocabulary (one GRBeam step).
 //
-// Semantics: src/kadllm/grbeam.py:93-122.  For request b with Wp parent beams
+// Semantics: src/kadllm/grbeam.py:75-104.  For request b with Wp parent beams
 // and vocabulary V:  logp = log_softmax(float(logits[b, w, :]))  (over the full,
 // unmasked row), masked entries -> -inf (no renormalisation), score = logp +
 // parent_score[b, w]; keep the top `width` of the Wp*V candidates, sorted by
@@ -548,19 +548,21 @@ __global__ void __launch_bounds__(1024) finalize_kernel(const SelArgs a) {
 }
 
 struct Workspace {
+  // The flag word sits at offset 0 whatever the widths: the steps of one search
+  // (whose previous widths differ) and the status query all find it there.
   // `base` bytes are required; the chunk-maximum summary after them (up to `total`) is optional:
   // without it collect reads whole rows
   size_t rowstat, rowlen, rowhist, thresh, count, flags, cand, vsum, base, total;
   Workspace(int64_t B, int64_t Wp) {
     auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
     const int64_t rows = B * Wp;
-    rowstat = 0;
+    flags = 0;
+    rowstat = al(flags + sizeof(uint32_t));
     rowlen = al(rowstat + rows * sizeof(float2));
     rowhist = al(rowlen + rows * sizeof(uint32_t));
     thresh = al(rowhist + rows * kRowBins * sizeof(uint32_t));
     count = al(thresh + B * sizeof(float));
-    flags = al(count + B * sizeof(uint32_t));
-    cand = al(flags + sizeof(uint32_t));
+    cand = al(count + B * sizeof(uint32_t));
     vsum = base = al(cand + B * kCap * sizeof(unsigned long long));
     total = al(vsum + rows * kSumMax * sizeof(uint16_t));
   }
@@ -649,6 +651,11 @@ int select_with_workspace(const void* logits, int logits_dtype, int64_t ld_row, 
   const int vw = 16 / esz;
   const bool vec = (reinterpret_cast<uintptr_t>(logits) & 15) == 0 && vocab % vw == 0 && ld_row % vw == 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (flags == nullptr && depth == 0) {
+    // the first step of a search (no history yet) starts the workspace's flag word afresh
+    cudaError_t e = cudaMemsetAsync(a.flags, 0, sizeof(uint32_t), s);
+    KB_REQUIRE(e == cudaSuccess, KADLLM_ECUDA, "beam select: %s", cudaGetErrorString(e));
+  }
   if (logits_dtype == KADLLM_BF16) return launch_select<__nv_bfloat16>(a, vec, s);
   if (logits_dtype == KADLLM_F16) return launch_select<__half>(a, vec, s);
   return launch_select<float>(a, vec, s);

@@ -26,7 +26,7 @@
 // Fused mixer (kadllm_gdn_mixer_replay): q/k/v are produced on the fly by the
 // causal conv1d replay + SiLU from the packed projection row and the request's
 // conv state (src/kadllm/kernels/causal_conv1d.py:41-48), the gates from the
-// b / a columns (src/kadllm/adapters/qwen3_5.py:290-298), and the output goes
+// b / a columns (src/kadllm/adapters/qwen3_5.py:161-169), and the output goes
 // through Qwen3_5RMSNormGated with z (transformers modeling_qwen3_5.py:175-190).
 #include "common.cuh"
 #include "gdn_mixer.cuh"

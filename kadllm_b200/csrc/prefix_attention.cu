@@ -15,7 +15,7 @@
 // bf16 mma.sync tensor-core tiles and a cp.async double buffer.  The T <= 8
 // suffix keys of each beam are merged in the epilogue with fp32 CUDA-core dot
 // products.  Optional fused output gate: out = bf16(bf16(o) * bf16(sigmoid(gate)))
-// (src/kadllm/adapters/qwen3_5.py:328-330).
+// (src/kadllm/adapters/qwen3_5.py:199-201).
 #include "common.cuh"
 
 namespace kb {

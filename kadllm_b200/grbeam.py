@@ -3,7 +3,7 @@
 Drop-in for Kadllm's ``src/kadllm/grbeam.py``: the same protocol
 (``PrefillResult``, ``GRBeamAdapter``, ``GRBeamResult``, ``Constraint``) and
 ``grbeam_search`` signature, validation and error messages.  The per-request
-host loop of log-softmax + top-k (``src/kadllm/grbeam.py:103-122``) is replaced
+host loop of log-softmax + top-k (``src/kadllm/grbeam.py:87-104``) is replaced
 by one batched CUDA selection (``csrc/beam_select.cu``) that also gathers the
 history; nothing of logits size is allocated.
 
@@ -114,7 +114,7 @@ def grbeam_search(
 ) -> GRBeamResult:
     """Run GRBeam with a fixed token count and an explicit width per level.
 
-    Same contract as ``src/kadllm/grbeam.py:63-123``.  Call model.eval() first.
+    Same contract as ``src/kadllm/grbeam.py:45-105``.  Call model.eval() first.
     Invalid constrained slots remain marked (score -inf, valid False; their
     tokens are unspecified) rather than invented.
     """
@@ -168,7 +168,16 @@ def search_from_prefill(adapter: GRBeamAdapter, prefill: PrefillResult, B: int, 
         del logits, mask
     if own:
         selector.check()
+        check_adapter(adapter)
     return GRBeamResult(history, scores, torch.isfinite(scores))
+
+
+def check_adapter(adapter) -> None:
+    """Raise if the adapter's device kernels reported an error (a tensor-core
+    pipeline wait that timed out).  Adapters without a ``check`` have nothing to report."""
+    check = getattr(adapter, "check", None)
+    if callable(check):
+        check()
 
 
 class GraphedSearch:
@@ -177,7 +186,8 @@ class GraphedSearch:
     Every replay runs all of the search's kernels (prefill, decodes, selections)
     from the static input buffer ``ids`` into static outputs; the launches are
     issued by the device, not by the host.  ``__call__(ids)`` copies new prompts in
-    first; ``check()`` reads the selection's overflow flag (synchronises).  The
+    first; ``check()`` reads the selection's overflow flag and the adapter's device
+    status word (synchronises).  The
     adapter must be this package's (its kernels go to the current stream).
     """
 
@@ -207,4 +217,6 @@ class GraphedSearch:
         return self.result
 
     def check(self) -> None:
+        """Raise on a selection overflow or a device error of the adapter's kernels (synchronises)."""
         self.selector.check()
+        check_adapter(self.adapter)

@@ -149,6 +149,10 @@ class SidHeadAdapter:
         logits, state = self.base.engine.prefill_varlen(list(prompts), head=self.head)
         return PrefillResult(logits, state)
 
+    def check(self) -> None:
+        """Raise if a tensor-core kernel of the engine reported a timed-out wait (synchronises)."""
+        self.base.engine.check()
+
     @torch.no_grad()
     def decode(self, history: torch.Tensor, state) -> torch.Tensor:
         self.base._check_state(history, state)  # entries are codebook positions (from the selection)

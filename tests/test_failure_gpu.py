@@ -36,3 +36,28 @@ def test_engine_check_raises_on_status():
     _lib.call("kadllm_diag_wait_timeout", engine.status.data_ptr(), 100_000, _lib.stream(engine.device))
     with pytest.raises(RuntimeError, match="timed out"):
         engine.check()
+
+
+def test_search_raises_on_engine_status():
+    """A timed-out tensor-core wait surfaces from the search itself, not only from
+    an explicit ``check()``: the drop-in ``grbeam_search`` and the graphed search both raise."""
+    from kadllm_b200 import grbeam_search
+    from kadllm_b200.adapters import NativeGRBeamAdapter
+    from kadllm_b200.config import TINY
+    from kadllm_b200.grbeam import GraphedSearch
+    from kadllm_b200.model import HybridModel
+    from kadllm_b200.synthetic import torch_weights
+
+    engine = HybridModel(TINY, torch_weights(TINY, seed=0, device="cuda"), device="cuda")
+    adapter = NativeGRBeamAdapter(engine)
+    ids = torch.randint(0, TINY.vocab_size, (2, 16), device="cuda")
+    grbeam_search(adapter, ids, [4, 4])  # clean
+    graphed = GraphedSearch(adapter, 2, 16, [4, 4], torch.device("cuda"))
+    graphed(ids)
+    graphed.check()
+    _lib.call("kadllm_diag_wait_timeout", engine.status.data_ptr(), 100_000, _lib.stream(engine.device))
+    with pytest.raises(RuntimeError, match="timed out"):
+        grbeam_search(adapter, ids, [4, 4])
+    graphed(ids)
+    with pytest.raises(RuntimeError, match="timed out"):
+        graphed.check()

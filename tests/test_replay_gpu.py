@@ -175,7 +175,7 @@ def _mixer_case(T, K, H, HV, B, W):
     _lib.call("kadllm_gdn_mixer_replay", tp.data_ptr(), ld, args[0].data_ptr(), 4, args[1].data_ptr(),
               args[2].data_ptr(), args[3].data_ptr(), args[4].data_ptr(), args[5].data_ptr(), 1e-6,
               out.data_ptr(), B, W, T, H, HV, K, K, _lib.stream(tp.device))
-    # oracle chain (src/kadllm/adapters/qwen3_5.py:273-305)
+    # oracle chain (src/kadllm/adapters/qwen3_5.py:144-177)
     r = O.Rounding("bf16")
     P = proj.reshape(BW, T, ld)
     x = np.swapaxes(P[..., :C], 1, 2)

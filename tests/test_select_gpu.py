@@ -99,7 +99,7 @@ def test_select_full_vocab_shape_and_properties():
     sel = BeamSelector(B, Wp, torch.device("cuda"))
     sc, h = sel.step(logits, parent, hist, W)
     sel.check()
-    # reference semantics (src/kadllm/grbeam.py:108-113) on the GPU in fp32
+    # reference semantics (src/kadllm/grbeam.py:90-95) on the GPU in fp32
     for b in (0, 7, 19, 31):
         logp = logits[b].float().log_softmax(-1) + parent[b, :, None]
         rs, ri = logp.reshape(-1).topk(W)
@@ -135,3 +135,29 @@ def test_oracle_search_on_gpu_selection_with_constraints():
     np.testing.assert_allclose(r.scores.cpu().numpy(), scores, atol=1e-5)
     fin = np.isfinite(scores)
     np.testing.assert_array_equal(r.tokens.cpu().numpy()[fin], history[fin])
+
+
+@pytest.mark.parametrize("max_prev", [16, 64])
+def test_overflow_reported_at_every_width_and_cleared_by_a_new_search(max_prev):
+    """More than 16384 candidates tied above the threshold set the overflow flag,
+    whether the overflowing step's previous width is below the selector's maximum
+    (the first step, Wp = 1) or equal to it; the first step of the next search
+    clears it."""
+    from kadllm_b200.grbeam import BeamSelector
+
+    B, V, W = 2, 20000, 16
+    dev = torch.device("cuda")
+    sel = BeamSelector(B, max_prev, dev)
+    empty = torch.empty(B, 1, 0, dtype=torch.long, device=dev)
+    flat = torch.zeros(B, 1, V, dtype=torch.bfloat16, device=dev)  # 20000 exact ties per request
+    sel.step(flat, None, empty, W)
+    with pytest.raises(RuntimeError, match="16384"):
+        sel.check()
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    smooth = torch.randn(B, 1, V, device=dev, generator=gen).bfloat16()
+    sc, h = sel.step(smooth, None, empty, max_prev)  # a new search: flag cleared
+    sel.check()
+    flat_wide = torch.zeros(B, max_prev, V, dtype=torch.bfloat16, device=dev)
+    sel.step(flat_wide, sc, h, W)  # Wp == max_prev, ties overflow again
+    with pytest.raises(RuntimeError, match="16384"):
+        sel.check()

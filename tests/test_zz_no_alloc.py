@@ -29,14 +29,22 @@ def test_noalloc_matches_workspace_selection_twice():
     from kadllm_b200.grbeam import BeamSelector
 
     dev = torch.device("cuda")
-    for seed, (B, Wp, V, W, depth) in enumerate([(4, 64, 3000, 48, 2), (32, 16, 5000, 16, 1)]):
+    cases = [(4, 64, 3000, 48, 2, False), (32, 16, 5000, 16, 1, False), (2, 256, 4096, 64, 1, False),
+             (4, 32, 3000, 40, 2, True)]
+    for seed, (B, Wp, V, W, depth, masked) in enumerate(cases):
         logits, parent, hist = _case(seed, B, Wp, V, depth)
-        ref_scores, ref_hist = BeamSelector(B, Wp, dev).step(logits, parent, hist, W)
+        mask = None
+        if masked:  # a constraint: every third token and all of beam 0 disallowed
+            mask = torch.ones(B, Wp, V, dtype=torch.bool, device=dev)
+            mask[..., 1::3] = False
+            mask[:, 0, :] = False
+        ref_scores, ref_hist = BeamSelector(B, Wp, dev).step(logits, parent, hist, W, mask)
         scores = torch.empty(B, W, dtype=torch.float32, device=dev)
         new_hist = torch.empty(B, W, depth + 1, dtype=torch.int64, device=dev)
         flags = torch.ones(1, dtype=torch.int32, device=dev)  # the entry point clears it
         _lib.call("kadllm_beam_select_noalloc", logits.data_ptr(), _lib.dtype_code(logits), V,
-                  parent.data_ptr(), None, hist.data_ptr(), scores.data_ptr(), new_hist.data_ptr(),
+                  parent.data_ptr(), None if mask is None else mask.view(torch.uint8).data_ptr(), hist.data_ptr(),
+                  scores.data_ptr(), new_hist.data_ptr(),
                   flags.data_ptr(), B, Wp, V, W, depth, _lib.stream(dev))
         torch.cuda.synchronize()
         np.testing.assert_allclose(scores.cpu().numpy(), ref_scores.cpu().numpy(), rtol=0, atol=1e-6)
