@@ -67,7 +67,7 @@ KADLLM_API int kadllm_gated_delta_replay(const void* q, const void* k, const voi
 /* ------------------------------------------------------------------------
  * Fused GDN token mixer for beam decode (BF16): causal conv1d replay + SiLU,
  * gates, gated delta replay from the shared state and the gated RMSNorm, i.e.
- * src/kadllm/adapters/qwen3_5.py:273-305 (_linear) from the packed input
+ * src/kadllm/adapters/qwen3_5.py:144-177 (_linear) from the packed input
  * projection up to (not including) out_proj.
  *   proj        [BW*T, ld_proj] bf16, row = beam_row*T + t; columns
  *               [q (H*K) | k (H*K) | v (HV*V) | z (HV*V) | b (HV) | a (HV)]
@@ -128,15 +128,16 @@ KADLLM_API int kadllm_prefix_attention(
  * (full vocabulary), optional mask (-inf, no renormalisation), + parent score,
  * top-`width` of the prev_width*vocab candidates per request, sorted by score
  * (ties: lower flat index first), and the gathered history.
- * Replaces the per-request loop of src/kadllm/grbeam.py:103-122.
+ * Replaces the per-request loop of src/kadllm/grbeam.py:87-104.
  *   logits        [B*Wp rows, V] with row stride ld_row, dtype logits_dtype
  *   parent_scores [B, Wp] f32 or NULL (all zero, first step)
  *   mask          [B*Wp, V] uint8 (nonzero = allowed) or NULL
  *   old_history   [B, Wp, depth] int64 or NULL when depth == 0
  *   out_scores    [B, width] f32;  out_history [B, width, depth+1] int64
  *   workspace     >= kadllm_beam_select_workspace(B, Wp) bytes, 256-byte
- *                 aligned, caller-owned; zero its flags word before first use
- *                 (a zero-filled allocation does).
+ *                 aligned, caller-owned.  Its flag word (offset 0, the same for
+ *                 every Wp) is cleared by each depth-0 call, the first step of
+ *                 a search, and OR-ed into by every later step.
  * At most 16384 candidates above the per-request threshold are kept; an
  * overflow sets a flag read by kadllm_beam_select_status.
  * ------------------------------------------------------------------------ */
@@ -148,7 +149,8 @@ KADLLM_API int kadllm_beam_select(const void* logits, int logits_dtype, int64_t 
                                   int64_t batch, int64_t prev_width, int64_t vocab, int64_t width,
                                   int64_t depth, void* stream);
 /* Copies the workspace's flag word to *flags_out (bit 0: candidate overflow)
- * after synchronising `stream`. */
+ * after synchronising `stream`.  The word is at offset 0 whatever the widths;
+ * batch and prev_width are those the workspace was sized for. */
 KADLLM_API int kadllm_beam_select_status(const void* workspace, int64_t batch, int64_t prev_width,
                                          uint32_t* flags_out, void* stream);
 
@@ -175,7 +177,7 @@ KADLLM_API int kadllm_beam_select_noalloc(const void* logits, int logits_dtype, 
  * Model building blocks of the native Qwen3.5 hybrid pipeline (BF16).  Each
  * replaces a Transformers module on the reference's prefill / decode path
  * (transformers/models/qwen3_5/modeling_qwen3_5.py, called from
- * src/kadllm/adapters/qwen3_5.py:235-364).
+ * src/kadllm/adapters/qwen3_5.py:106-235).
  * ====================================================================== */
 
 /* x = embed[ids] and normed = RMSNorm(x) * (1 + weight) (Qwen3_5RMSNorm);
@@ -303,6 +305,24 @@ KADLLM_API int kadllm_causal_attention(const void* q, int64_t sq_row, int64_t sq
                                        int64_t so_h, int64_t batch, int64_t length, int64_t heads,
                                        int64_t kv_heads, int64_t head_dim, float scale,
                                        void* stream);
+
+/* Projection GEMM on tcgen05 tensor cores (CTA pairs, tensor-map copies, FP32
+ * accumulation in tensor memory): the product C = A . B^T of
+ * torch.nn.functional.linear(A, B) for every nn.Linear of the decoder and the
+ * LM head (Qwen3_5GatedDeltaNet / Qwen3_5Attention / Qwen3_5MLP projections and
+ * lm_head, as src/kadllm/adapters/qwen3_5.py:144-202,226-235 calls them).
+ *   A [M, K] bf16, row stride lda;  B [N, K] bf16, row stride ldb;  strides
+ *   multiples of 8 elements, pointers 16-byte aligned.
+ * epilogue 0: C [M, N] = bf16(A . B^T)                                   (ldc)
+ * epilogue 1: B's rows are 128-row blocks [gate block j | up block j] (N a
+ *   multiple of 256); C [M, n_out] = bf16(bf16(silu(gate)) * up), gate and up
+ *   rounded to bf16 first -- Qwen3_5MLP's act_fn(gate_proj(x)) * up_proj(x)
+ * epilogue 2: C = bf16(resid + bf16(A . B^T)), resid [M, N] (ld_resid) may be C:
+ *   the decoder's residual update x = x + f(x)
+ * status: device word, bit 0 = a bounded wait of the kernel timed out. */
+KADLLM_API int kadllm_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc,
+                           const void* resid, int64_t ld_resid, int64_t M, int64_t N, int64_t K, int64_t n_out,
+                           int epilogue, uint32_t* status, void* stream);
 
 /* Diagnostics: one CTA runs the tensor-core kernels' bounded mbarrier wait on a
  * barrier nothing completes, giving up after max_cycles SM clocks (1 .. 2^32)

@@ -13,6 +13,7 @@ Cases (the kernel microbenchmark shapes and the GRBeam step shapes):
            attn_causal: the prefill's causal attention, 32 x 1024 tokens)
   mixer    fused GDN decode mixer: 32 requests x 256 beams, T = 1 and 2
   select   one selection step over 32 x 256 x 248320 bf16 logits
+  gemm_*   the tcgen05 projection GEMM at the step's shapes (cuBLAS timed beside it)
 Each prints one JSON line: device time per call (CUDA events, after warm-up),
 algorithmic work, achieved rate and the fraction of the measured B200 peak.
 """
@@ -172,26 +173,62 @@ def case_select(gen, reps):
     return ms, "hbm", B * Wp * V * 2
 
 
+def case_gemm(gen, reps, M, N, K, epilogue=0):
+    """kadllm_gemm at one of the step's projection shapes; the same product through
+    torch.nn.functional.linear (cuBLAS) is timed beside it (plain product only)."""
+    dev, bf = torch.device("cuda"), torch.bfloat16
+    a = torch.randn(M, K, device=dev, generator=gen).to(bf)
+    b = (0.05 * torch.randn(N, K, device=dev, generator=gen)).to(bf)
+    n_out = N // 2 if epilogue == 1 else N
+    out = torch.empty(M, n_out, device=dev, dtype=bf)
+    resid = torch.randn(M, N, device=dev, generator=gen).to(bf) if epilogue == 2 else None
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    s = _lib.stream(dev)
+
+    def run():
+        _lib.call("kadllm_gemm", a.data_ptr(), K, b.data_ptr(), K, out.data_ptr(), n_out, _lib.ptr(resid),
+                  N if resid is not None else 0, M, N, K, n_out, epilogue, status.data_ptr(), s)
+
+    ms = _time(run, reps)
+    if int(status.item()):
+        raise RuntimeError("gemm reported a timed-out wait")
+    ref_ms = _time(lambda: torch.nn.functional.linear(a, b), reps)
+    return ms, "tensor", 2.0 * M * N * K, {"shape": [M, N, K], "epilogue": epilogue, "cublas_ms": ref_ms,
+                                            "cublas_tflops": 2.0 * M * N * K / (ref_ms / 1e3) / 1e12}
+
+
 CASES = {"prefill": case_prefill, "attn_tiled": case_attn_tiled, "conv": case_conv, "attn": case_attn, "mixer": case_mixer,
          "mixer2": lambda g, r: case_mixer(g, r, T=2), "select": case_select,
          "attn_step": lambda g, r: case_attn_tiled(g, r, B=32, W=256, T=2, L=1024),
-         "attn_causal": lambda g, r: case_attn_tiled(g, r, B=32, W=1, T=1, L=1024, causal=True)}
+         "attn_causal": lambda g, r: case_attn_tiled(g, r, B=32, W=1, T=1, L=1024, causal=True),
+         # the step's projections: prefill (32 x 1024 rows) and decode (32 x 256 beams, T = 1)
+         "gemm_gdn_in": lambda g, r: case_gemm(g, r, 32768, 8224, 1024),
+         "gemm_mlp_gu": lambda g, r: case_gemm(g, r, 32768, 7168, 1024, epilogue=1),
+         "gemm_mlp_down": lambda g, r: case_gemm(g, r, 32768, 1024, 3584, epilogue=2),
+         "gemm_out": lambda g, r: case_gemm(g, r, 8192, 1024, 2048, epilogue=2),
+         "gemm_decode_in": lambda g, r: case_gemm(g, r, 8192, 8224, 1024),
+         "gemm_lm_head": lambda g, r: case_gemm(g, r, 8192, 248320, 1024)}
 
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__)
-    ap.add_argument("--case", choices=sorted(CASES), required=True)
+    ap.add_argument("--case", nargs="+", choices=sorted(CASES), required=True)
     ap.add_argument("--reps", type=int, default=10)
     args = ap.parse_args()
-    gen = torch.Generator(device="cuda").manual_seed(0)
-    ms, bound, work = CASES[args.case](gen, args.reps)
-    hbm, tflops, kind = _peaks()
-    if bound == "tensor":
-        achieved, peak, unit = work / (ms / 1e3) / 1e12, tflops, "TFLOP/s"
-    else:
-        achieved, peak, unit = work / (ms / 1e3) / 1e9, hbm, "GB/s"
-    print(json.dumps({"case": args.case, "ms": ms, "bound": bound, "work": work, "achieved": achieved,
-                      "unit": unit, "peak": peak, "frac": achieved / peak, "peak_kind": kind}))
+    for case in args.case:
+        gen = torch.Generator(device="cuda").manual_seed(0)
+        res = CASES[case](gen, args.reps)
+        ms, bound, work = res[:3]
+        hbm, tflops, kind = _peaks()
+        if bound == "tensor":
+            achieved, peak, unit = work / (ms / 1e3) / 1e12, tflops, "TFLOP/s"
+        else:
+            achieved, peak, unit = work / (ms / 1e3) / 1e9, hbm, "GB/s"
+        line = {"case": case, "ms": ms, "bound": bound, "work": work, "achieved": achieved,
+                "unit": unit, "peak": peak, "frac": achieved / peak, "peak_kind": kind}
+        if len(res) > 3:
+            line.update(res[3])
+        print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":

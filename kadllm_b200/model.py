@@ -7,14 +7,15 @@ token mixer and per MLP) and runs
   rule for GDN layers, causal flash attention for full-attention layers),
   producing the first-token logits and the immutable, request-sized prefix
   (conv state, recurrent state, K/V) exactly where the reference keeps them
-  (``Qwen35GRBeamAdapter.prefill``, ``src/kadllm/adapters/qwen3_5.py:235-262``);
+  (``Qwen35GRBeamAdapter.prefill``, ``src/kadllm/adapters/qwen3_5.py:106-133``);
 * ``decode(history, state)``: suffix replay of every beam from the shared
-  prefix (``Qwen35GRBeamAdapter.decode``, ``src/kadllm/adapters/qwen3_5.py:333-364``)
+  prefix (``Qwen35GRBeamAdapter.decode``, ``src/kadllm/adapters/qwen3_5.py:204-235``)
   through the fused GDN mixer and the shared-prefix attention kernels.
 
-Token mixers, norms, activations, attention and selection are hand-written
-sm_100a kernels (``csrc/``); the plain projections are cuBLAS BF16 GEMMs
-issued through ``torch.nn.functional.linear``.  Everything stays on the GPU;
+Token mixers, norms, attention, selection and every projection are
+hand-written sm_100a kernels (``csrc/``): the projections and the LM head run
+on the library's tcgen05 GEMM (``kadllm_gemm``), with the MLP's SiLU-mul and
+the residual updates fused into its epilogue.  Everything stays on the GPU;
 there is no CPU path.
 """
 
@@ -25,12 +26,29 @@ import threading
 from dataclasses import dataclass
 
 import torch
-import torch.nn.functional as F
 
 from . import _lib
 from .config import LINEAR, HybridConfig
 
 BF16 = torch.bfloat16
+
+# epilogues of kadllm_gemm
+GEMM_STORE, GEMM_SILU_MUL, GEMM_ADD = 0, 1, 2
+GATE_UP_BLOCK = 128  # rows per gate / up block of the interleaved MLP input weight
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """gate, up [I, H] -> [2 I', H]: 128-row blocks [gate block j | up block j], I' = I
+    rounded up to a multiple of 128 (zero rows), the layout of kadllm_gemm's SiLU-mul
+    epilogue (one 256-column tile of the product holds matching gate and up columns)."""
+    inter, hidden = gate.shape
+    padded = -(-inter // GATE_UP_BLOCK) * GATE_UP_BLOCK
+    if padded != inter:
+        gate = torch.cat([gate, gate.new_zeros(padded - inter, hidden)])
+        up = torch.cat([up, up.new_zeros(padded - inter, hidden)])
+    n = padded // GATE_UP_BLOCK
+    return torch.stack([gate.reshape(n, GATE_UP_BLOCK, hidden), up.reshape(n, GATE_UP_BLOCK, hidden)], 1) \
+        .reshape(2 * padded, hidden).contiguous()
 
 
 @dataclass
@@ -57,8 +75,9 @@ class Layer:
     mixer: GDNLayer | AttnLayer
     input_ln: torch.Tensor  # [H] f32
     post_ln: torch.Tensor   # [H] f32
-    w_gu: torch.Tensor      # [2*I, H]: gate | up
+    w_gu: torch.Tensor      # [2*I', H]: gate / up interleaved in 128-row blocks (interleave_gate_up)
     w_down: torch.Tensor    # [H, I]
+    inter: int              # I, the MLP width of this layer
 
 
 TILED_HEAD_DIM = 256  # head dim of the tensor-core attention kernels
@@ -131,8 +150,8 @@ class HybridModel:
             self.layers.append(Layer(
                 kind=kind, mixer=mixer, input_ln=f32(p + "input_layernorm.weight"),
                 post_ln=f32(p + "post_attention_layernorm.weight"),
-                w_gu=torch.cat([bf(p + "mlp.gate_proj.weight"), bf(p + "mlp.up_proj.weight")]).contiguous(),
-                w_down=bf(p + "mlp.down_proj.weight")))
+                w_gu=interleave_gate_up(bf(p + "mlp.gate_proj.weight"), bf(p + "mlp.up_proj.weight")),
+                w_down=bf(p + "mlp.down_proj.weight"), inter=int(weights[p + "mlp.gate_proj.weight"].shape[0])))
         self._rope_len = 0
         self._cos = self._sin = None
         self._rope_lock = threading.Lock()
@@ -199,13 +218,31 @@ class HybridModel:
                   weight.data_ptr(), self.cfg.rms_norm_eps, normed.data_ptr(), rows, step, offset,
                   self.cfg.hidden_size, self._stream())
 
-    def _mlp(self, layer: Layer, normed):
-        gu = F.linear(normed, layer.w_gu)
-        inter = layer.w_gu.shape[0] // 2  # per layer: WideTuning-merged layers are wider
-        act = torch.empty(gu.shape[0], inter, dtype=BF16, device=self.device)
-        _lib.call("kadllm_silu_mul", gu.data_ptr(), gu.stride(0), inter, act.data_ptr(), gu.shape[0],
-                  self._stream())
-        return F.linear(act, layer.w_down)
+    def _gemm(self, a: torch.Tensor, w: torch.Tensor, *, resid: torch.Tensor | None = None,
+              silu_inter: int | None = None) -> torch.Tensor:
+        """a [M, K] . w[N, K]^T on the tcgen05 GEMM.  ``resid``: x += a . w^T in place
+        (returns x); ``silu_inter``: w is an interleave_gate_up weight, returns the
+        [M, silu_inter] SiLU-mul activation; otherwise a new [M, N] product."""
+        M, K = a.shape
+        N = w.shape[0]
+        if silu_inter is not None:
+            epi, n_out = GEMM_SILU_MUL, silu_inter
+            out = torch.empty(M, n_out, dtype=BF16, device=self.device)
+        elif resid is not None:
+            epi, n_out, out = GEMM_ADD, N, resid
+        else:
+            epi, n_out = GEMM_STORE, N
+            out = torch.empty(M, N, dtype=BF16, device=self.device)
+        _lib.call("kadllm_gemm", a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(), out.stride(0),
+                  _lib.ptr(resid), 0 if resid is None else resid.stride(0), M, N, K, n_out, epi,
+                  self.status.data_ptr(), self._stream())
+        return out
+
+    def _mlp(self, layer: Layer, normed, x):
+        """x += down(silu(gate(normed)) * up(normed)): two GEMMs, the activation and the
+        residual update in their epilogues (per layer width: WideTuning-merged layers are wider)."""
+        act = self._gemm(normed, layer.w_gu, silu_inter=layer.inter)
+        self._gemm(act, layer.w_down, resid=x)
 
     def _qk_rope(self, P, rows, pos_base, rows_per_seq, q_out, k_out, k_strides, v_out, v_strides, mixer,
                  pos_of_row=None, max_pos=None):
@@ -219,9 +256,11 @@ class HybridModel:
 
     # ------------------------------------------------------------------ prefill
     @torch.no_grad()
-    def prefill(self, ids: torch.Tensor, head: torch.Tensor | None = None):
+    def prefill(self, ids: torch.Tensor, head: torch.Tensor | None = None, taps: list | None = None):
         """ids [B, L] -> (logits [B, V] bf16, HybridPrefix).  ``head`` [V', H] replaces
-        the LM head (a SID-only head: logits over its rows only)."""
+        the LM head (a SID-only head: logits over its rows only).  ``taps``, when given,
+        receives the hidden state of every request's last prompt position after each
+        decoder layer ([B, H] fp32 copies, for layer-by-layer parity checks)."""
         c = self.cfg
         B, L = ids.shape
         ids = ids.to(device=self.device, dtype=torch.int64).contiguous()
@@ -234,7 +273,7 @@ class HybridModel:
         ws = None  # GDN prefill workspace (chunk blocks), shared by the GDN layers
         for i, layer in enumerate(self.layers):
             m = layer.mixer
-            P = F.linear(normed, m.w_in)
+            P = self._gemm(normed, m.w_in)
             if layer.kind == LINEAR:
                 conv_state = torch.empty(B, c.conv_dim, 4, dtype=BF16, device=self.device)
                 out = torch.empty(R, c.value_dim, dtype=BF16, device=self.device)
@@ -249,7 +288,7 @@ class HybridModel:
                           c.rms_norm_eps, out.data_ptr(), out.stride(0), rec.data_ptr(), ws.data_ptr(), ws.numel(),
                           B, L, c.linear_num_key_heads, c.linear_num_value_heads, c.linear_key_head_dim,
                           c.linear_value_head_dim, s)
-                delta = F.linear(out, m.w_out)
+                self._gemm(out, m.w_out, resid=x)
                 prefix.append((conv_state, rec))
                 tiles.append(None)
             else:
@@ -273,16 +312,18 @@ class HybridModel:
                               kc.stride(2), kc.stride(1), vc.data_ptr(), vc.stride(0), vc.stride(2), vc.stride(1),
                               gate.data_ptr(), P.stride(0), 2 * D, out.data_ptr(),
                               out.stride(0), D, B, L, hq, hk, D, D ** -0.5, s)
-                delta = F.linear(out, m.w_o)
+                self._gemm(out, m.w_o, resid=x)
                 prefix.append((kc.transpose(1, 2), vc.transpose(1, 2)))
                 tiles.append(tile)
-            self._add_norm(x, delta, layer.post_ln, normed)
-            delta = self._mlp(layer, normed)
+            self._add_norm(x, None, layer.post_ln, normed)
+            self._mlp(layer, normed, x)
+            if taps is not None:
+                taps.append(x.view(B, L, -1)[:, -1].float().clone())
             if i + 1 < len(self.layers):
-                self._add_norm(x, delta, self.layers[i + 1].input_ln, normed)
+                self._add_norm(x, None, self.layers[i + 1].input_ln, normed)
         last = torch.empty(B, c.hidden_size, dtype=BF16, device=self.device)
-        self._add_norm(x, delta, self.final_norm, last, rows=B, step=L, offset=L - 1)
-        logits = F.linear(last, self.lm_head if head is None else head)
+        self._add_norm(x, None, self.final_norm, last, rows=B, step=L, offset=L - 1)
+        logits = self._gemm(last, self.lm_head if head is None else head)
         return logits, HybridPrefix(L, B, self.owner, tuple(prefix), tuple(tiles))
 
     @torch.no_grad()
@@ -316,7 +357,7 @@ class HybridModel:
         ws = None
         for i, layer in enumerate(self.layers):
             m = layer.mixer
-            P = F.linear(normed, m.w_in)
+            P = self._gemm(normed, m.w_in)
             if layer.kind == LINEAR:
                 conv_state = torch.empty(B, c.conv_dim, 4, dtype=BF16, device=self.device)
                 out = torch.empty(R, c.value_dim, dtype=BF16, device=self.device)
@@ -331,7 +372,7 @@ class HybridModel:
                           c.rms_norm_eps, out.data_ptr(), out.stride(0), rec.data_ptr(), ws.data_ptr(), ws.numel(),
                           cu.data_ptr(), R, B, Lmax, c.linear_num_key_heads, c.linear_num_value_heads,
                           c.linear_key_head_dim, c.linear_value_head_dim, s)
-                delta = F.linear(out, m.w_out)
+                self._gemm(out, m.w_out, resid=x)
                 prefix.append((conv_state, rec))
                 tiles.append(None)
             else:
@@ -354,19 +395,19 @@ class HybridModel:
                           nblk, None, 0, 0, 0, None, 0, 0, 0, gate.data_ptr(), P.stride(0), 0, 2 * D,
                           out.data_ptr(), out.stride(0), 0, D, self.status.data_ptr(), cu.data_ptr(), B, 1, 1, hq,
                           hk, Lmax, D, D ** -0.5, 1, s)
-                delta = F.linear(out, m.w_o)
+                self._gemm(out, m.w_o, resid=x)
                 prefix.append((kp, vp))
                 tiles.append((kt, vt, nblk))
-            self._add_norm(x, delta, layer.post_ln, normed)
-            delta = self._mlp(layer, normed)
+            self._add_norm(x, None, layer.post_ln, normed)
+            self._mlp(layer, normed, x)
             if i + 1 < len(self.layers):
-                self._add_norm(x, delta, self.layers[i + 1].input_ln, normed)
+                self._add_norm(x, None, self.layers[i + 1].input_ln, normed)
         last_rows = cu[1:].long() - 1
-        xl, dl = x.index_select(0, last_rows), delta.index_select(0, last_rows)
+        xl = x.index_select(0, last_rows)
         last = torch.empty(B, c.hidden_size, dtype=BF16, device=self.device)
-        _lib.call("kadllm_add_rmsnorm", xl.data_ptr(), dl.data_ptr(), dl.stride(0), self.final_norm.data_ptr(),
+        _lib.call("kadllm_add_rmsnorm", xl.data_ptr(), None, 0, self.final_norm.data_ptr(),
                   c.rms_norm_eps, last.data_ptr(), B, 1, 0, c.hidden_size, s)
-        logits = F.linear(last, self.lm_head if head is None else head)
+        logits = self._gemm(last, self.lm_head if head is None else head)
         return logits, HybridPrefix(Lmax, B, self.owner, tuple(prefix), tuple(tiles), cu, tuple(lens))
 
     # ------------------------------------------------------------------ decode
@@ -387,7 +428,7 @@ class HybridModel:
             pos = (lens.repeat_interleave(W * T) + torch.arange(T, dtype=torch.int64).repeat(B * W)).to(self.device)
         for i, (layer, cached) in enumerate(zip(self.layers, state.layers)):
             m = layer.mixer
-            P = F.linear(normed, m.w_in)
+            P = self._gemm(normed, m.w_in)
             if layer.kind == LINEAR:
                 out = torch.empty(R, c.value_dim, dtype=BF16, device=self.device)
                 conv_state, rec = cached
@@ -396,7 +437,7 @@ class HybridModel:
                           m.dt_bias.data_ptr(), m.norm_w.data_ptr(), c.rms_norm_eps, out.data_ptr(), B, W, T,
                           c.linear_num_key_heads, c.linear_num_value_heads, c.linear_key_head_dim,
                           c.linear_value_head_dim, s)
-                delta = F.linear(out, m.w_out)
+                self._gemm(out, m.w_out, resid=x)
             else:
                 q = torch.empty(R, hq, D, dtype=BF16, device=self.device)
                 ks = torch.empty(R, hk, D, dtype=BF16, device=self.device)
@@ -430,13 +471,13 @@ class HybridModel:
                               vs.data_ptr(), *suffix_strides, None, gate.data_ptr(), T * P.stride(0), P.stride(0),
                               2 * D, out.data_ptr(), T * hq * D, hq * D, D, _lib.DTYPE_CODES[BF16], B, W, T, hq, hk,
                               state.length, D, D ** -0.5, s)
-                delta = F.linear(out, m.w_o)
-            self._add_norm(x, delta, layer.post_ln, normed)
-            delta = self._mlp(layer, normed)
+                self._gemm(out, m.w_o, resid=x)
+            self._add_norm(x, None, layer.post_ln, normed)
+            self._mlp(layer, normed, x)
             if i + 1 < len(self.layers):
-                self._add_norm(x, delta, self.layers[i + 1].input_ln, normed)
+                self._add_norm(x, None, self.layers[i + 1].input_ln, normed)
         last = torch.empty(BW, c.hidden_size, dtype=BF16, device=self.device)
-        self._add_norm(x, delta, self.final_norm, last, rows=BW, step=T, offset=T - 1)
+        self._add_norm(x, None, self.final_norm, last, rows=BW, step=T, offset=T - 1)
         return last
 
     @torch.no_grad()
@@ -445,4 +486,4 @@ class HybridModel:
         head's rows, or over ``head``'s rows when given."""
         B, W, _ = history.shape
         w = self.lm_head if head is None else head
-        return F.linear(self.decode_hidden(history, state), w).view(B, W, -1)
+        return self._gemm(self.decode_hidden(history, state), w).view(B, W, -1)
