@@ -3,7 +3,8 @@
 Run in a container where the Kadllm reference sources and Transformers are
 importable (pass the reference's ``src`` directory as the first argument):
 
-    python tests/golden/make_golden.py <kadllm-src-dir>
+    python tests/golden/make_golden.py <kadllm-src-dir>              # the small fixtures
+    python tests/golden/make_golden.py <kadllm-src-dir> --headline   # the 0.8B-sized fixtures
 
 Every fixture records inputs and the reference's outputs:
 
@@ -19,6 +20,8 @@ Every fixture records inputs and the reference's outputs:
   ``torch_chunk_gated_delta_rule`` (prefill scan, with final state).
 * ``select.npz``         ``grbeam_search`` driven by a fixed-logits adapter
   (ties, a mask via ``allowed``, and an all-masked beam).
+* ``headline_<dtype>.npz`` the benchmark's 0.8B-shaped model, batch 2, prompt
+  1024, widths [256, 256, 256] (see ``headline``).
 
 The reference is not available where the GPU tests run; these files are.
 """
@@ -182,7 +185,84 @@ def main(ref_src: str) -> None:
     print("select", out["smooth_scores"].tolist())
 
 
+HEADLINE_WIDTHS = [256, 256, 256]
+HEADLINE_BATCH, HEADLINE_PROMPT = 2, 1024
+
+
+def headline(ref_src: str) -> None:
+    """The benchmark's model at its real size (Qwen3.5-0.8B-shaped: 24 layers,
+    hidden 1024, vocabulary 248,320) through the reference's torch path, in BF16
+    and fp32 with the same (BF16-valued) weights: ``headline_<dtype>.npz``.
+
+    Weights: ``kadllm_b200.synthetic.torch_weights(QWEN35_08B, seed=0,
+    device="cpu")`` (the benchmark's distributions, drawn by torch's CPU
+    generator, so the GPU test regenerates them bit-identically).  Prompts:
+    ``random_prompts(2, 1024, vocab, seed=0)``.  Recorded: the final beams
+    (tokens, scores, valid) of ``grbeam_search`` with widths [256, 256, 256]; the
+    hidden state of the last prompt position after every decoder layer (forward
+    hooks on the prefill) and after the final norm; the first-token logits; for
+    the fixed histories ``tokens[:, :, :2]`` of the BF16 search (in both files,
+    so the BF16 results can be measured against fp32 at the same histories),
+    the final-norm hidden of the last position of beams 0-7 and the logits of
+    beams 0-1 of every request.  Logits are stored as BF16 bit patterns
+    (``*_bits``, uint16) in the BF16 file and as fp32 in the fp32 file (request 0
+    / beam 0 only) to keep the files small.
+    """
+    sys.path.insert(0, ref_src)
+    from kadllm import grbeam_search
+    from kadllm.adapters import Qwen35GRBeamAdapter
+    from transformers import Qwen3_5TextConfig
+    from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5TextModel
+
+    from kadllm_b200.config import QWEN35_08B
+    from kadllm_b200.synthetic import random_prompts, torch_weights
+
+    torch.set_num_threads(__import__("os").cpu_count() or 1)
+    torch.set_grad_enabled(False)
+    cfg = QWEN35_08B
+    w = torch_weights(cfg, seed=0, device="cpu")  # BF16 values
+    ids = random_prompts(HEADLINE_BATCH, HEADLINE_PROMPT, cfg.vocab_size, seed=0)
+    tids = torch.from_numpy(ids)
+    for name, tdt in (("bf16", torch.bfloat16), ("fp32", torch.float32)):
+        model = Qwen3_5TextModel._from_config(Qwen3_5TextConfig(**cfg.to_hf_kwargs()), dtype=tdt).eval()
+        model.load_state_dict({k: v.to(tdt) for k, v in w.items()}, strict=True)
+        head = torch.nn.Linear(cfg.hidden_size, cfg.vocab_size, bias=False).eval()
+        head.weight = model.embed_tokens.weight
+        adapter = Qwen35GRBeamAdapter(model, head)
+        taps = []
+        hooks = [layer.register_forward_hook(lambda m, a, out: taps.append(out[:, -1].float().clone()))
+                 for layer in model.layers]
+        pre = adapter.prefill(tids)
+        for h in hooks:
+            h.remove()
+        final = model.norm(taps[-1].to(tdt)).float()
+        res = grbeam_search(adapter, tids, HEADLINE_WIDTHS)
+        if tdt == torch.bfloat16:  # both files decode at the BF16 search's histories
+            hist2 = res.tokens[:, :, :2].contiguous()
+        normed = []
+        hook = model.norm.register_forward_hook(lambda m, a, out: normed.append(out.float().clone()))
+        dec = adapter.decode(hist2, pre.state)
+        hook.remove()
+        dec_hidden = normed[0].reshape(HEADLINE_BATCH, -1, cfg.hidden_size)[:, :8]
+        out = dict(ids=ids, widths=np.array(HEADLINE_WIDTHS), tokens=res.tokens.numpy(),
+                   scores=res.scores.float().numpy(), valid=res.valid.numpy(),
+                   layer_hidden=torch.stack(taps).numpy(), final_hidden=final.numpy(),
+                   decode_history=hist2.numpy(), decode_hidden=dec_hidden.numpy())
+        if tdt == torch.bfloat16:
+            out["prefill_logits_bits"] = pre.logits.view(torch.int16).numpy().view(np.uint16)
+            out["decode_logits_bits"] = dec[:, :2].contiguous().view(torch.int16).numpy().view(np.uint16)
+        else:
+            out["prefill_logits0"] = pre.logits[0].numpy()
+            out["decode_logits00"] = dec[0, 0].numpy()
+        np.savez_compressed(HERE / f"headline_{name}.npz", **out)
+        print("headline", name, res.scores[:, :4].tolist(), res.scores[:, -1].tolist(), flush=True)
+        del model, adapter, pre, res, dec
+
+
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
+    if len(sys.argv) == 3 and sys.argv[2] == "--headline":
+        headline(sys.argv[1])
+    elif len(sys.argv) == 2:
+        main(sys.argv[1])
+    else:
         raise SystemExit(__doc__)
-    main(sys.argv[1])
