@@ -44,23 +44,32 @@ WORKLOAD = "qwen3.5-0.8b-shaped hybrid, bf16 random N(0,0.02) seed 0, B=32/GPU, 
 
 
 def algorithmic_flops(cfg, B=BATCH, L=PROMPT, W=BEAM, depth=DEPTH) -> float:
-    """Dense FLOPs of one GRBeam call: linears 2*params*tokens, attention
-    QK^T + PV, GDN state products, LM head (prefill last token + each decode row)."""
+    """Dense FLOPs of the work one GRBeam call needs: linears 2 * params * rows,
+    attention QK^T + PV, GDN state products, the LM head.  Needed work only: the
+    last layer's output projection and MLP run on each request's last prompt
+    position (the logits read nothing else), and each decode step replays its new
+    token only (the earlier suffix tokens' per-layer work is the parent step's)."""
     H, I = cfg.hidden_size, cfg.intermediate_size
-    gdn_params = cfg.gdn_in_dim * H + H * cfg.value_dim
-    attn_params = cfg.attn_in_dim * H + H * cfg.num_attention_heads * cfg.head_dim
-    n_gdn = sum(1 for k in cfg.layer_types if k == "linear_attention")
-    n_attn = cfg.num_layers - n_gdn
-    per_token = 2 * (n_gdn * gdn_params + n_attn * attn_params + cfg.num_layers * 3 * H * I)
-    decode_rows = sum(B * W * t for t in range(1, depth))  # suffix replay rows
-    flops = per_token * (B * L + decode_rows)
     hq, d = cfg.num_attention_heads, cfg.head_dim
-    flops += n_attn * 4 * B * hq * d * L * L / 2  # causal prefill attention
-    flops += n_attn * sum(4 * B * W * t * hq * d * (L + t) for t in range(1, depth))
     hv, dk, dv = cfg.linear_num_value_heads, cfg.linear_key_head_dim, cfg.linear_value_head_dim
-    flops += n_gdn * B * hv * L * (6 * dk * dv + 4 * 64 * (dk + dv))  # chunked scan
-    flops += n_gdn * sum(B * W * t * hv * 2 * 2 * dk * dv for t in range(1, depth))
-    flops += 2 * H * cfg.vocab_size * (B + B * W * (depth - 1))
+    n = cfg.num_layers
+    dec_rows = B * W * (depth - 1)  # one new token per beam per decode step
+    flops = 0.0
+    for i, kind in enumerate(cfg.layer_types):
+        gdn = kind == "linear_attention"
+        w_in = (cfg.gdn_in_dim if gdn else cfg.attn_in_dim) * H
+        w_post = H * (cfg.value_dim if gdn else hq * d) + 3 * H * I
+        tail_rows = B if i == n - 1 else B * L
+        flops += 2 * w_in * B * L + 2 * w_post * tail_rows  # prefill
+        flops += 2 * (w_in + w_post) * dec_rows              # decode
+        if gdn:
+            flops += B * hv * L * (6 * dk * dv + 4 * 64 * (dk + dv))  # chunked scan
+            flops += dec_rows * hv * 2 * 2 * dk * dv                  # [q; k] x S0 per new token
+        else:
+            queries = B if i == n - 1 else None
+            flops += 4 * B * hq * d * L * (L + 1) / 2 if queries is None else 4 * B * hq * d * L
+            flops += sum(4 * B * W * hq * d * (L + t) for t in range(1, depth))  # one query row per beam
+    flops += 2 * H * cfg.vocab_size * (B + dec_rows)
     return float(flops)
 
 
@@ -226,7 +235,7 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
     from kadllm_b200.config import QWEN35_08B
     from kadllm_b200.grbeam import GraphedSearch
     from kadllm_b200.model import HybridModel
-    from kadllm_b200.shard import gather_beams, max_over_ranks, rank_prompts
+    from kadllm_b200.shard import all_ranks, gather_beams, max_over_ranks, rank_prompts
     from kadllm_b200.synthetic import torch_weights
 
     torch.cuda.set_device(local_rank)
@@ -235,10 +244,17 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
     weights = torch_weights(cfg, seed=0, device=dev)
     engine = HybridModel(cfg, weights, device=dev)
     adapter = NativeGRBeamAdapter(engine)
-    ids_host = torch.from_numpy(rank_prompts(rank, BATCH, PROMPT, cfg.vocab_size)).pin_memory()
+    # per-GPU batch: 32 requests (weak scaling), or a fixed total split over the ranks (strong)
+    if args.total_requests:
+        if args.total_requests % world:
+            raise SystemExit("--total-requests must divide evenly over the ranks")
+        batch = args.total_requests // world
+    else:
+        batch = args.batch
+    ids_host = torch.from_numpy(rank_prompts(rank, batch, PROMPT, cfg.vocab_size)).pin_memory()
     ids_dev = ids_host.to(dev)
-    tok_host = torch.empty(BATCH, BEAM, DEPTH, dtype=torch.int64).pin_memory()
-    sc_host = torch.empty(BATCH, BEAM, dtype=torch.float32).pin_memory()
+    tok_host = torch.empty(batch, BEAM, DEPTH, dtype=torch.int64).pin_memory()
+    sc_host = torch.empty(batch, BEAM, dtype=torch.float32).pin_memory()
     widths = [BEAM] * DEPTH
 
     def gather(res):  # the path's only exchange: finished beams, in rank order
@@ -254,7 +270,7 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
         launches_per_step = _lib.launch_count - n0
         if not args.no_graph:
             try:
-                graphed = GraphedSearch(adapter, BATCH, PROMPT, widths, dev)
+                graphed = GraphedSearch(adapter, batch, PROMPT, widths, dev)
             except Exception as exc:  # noqa: BLE001 - report and fall back to eager launches
                 print(f"bench: CUDA graph capture failed ({type(exc).__name__}: {exc}); eager launches",
                       file=sys.stderr, flush=True)
@@ -272,7 +288,9 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
         sc_host.copy_(res.scores, non_blocking=True)
         return gather(res)
 
-    def timed(fn, steps):
+    per_rank = {}
+
+    def timed(fn, steps, key=None):
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
@@ -285,15 +303,23 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-        ms = max_over_ranks(start.elapsed_time(end), dev)
+        mine = start.elapsed_time(end)
+        if key:
+            per_rank[key] = [round(v / steps, 3) for v in all_ranks(mine, dev)]
+        ms = max_over_ranks(mine, dev)
         return ms / steps, (launches_per_step * steps if graphed is not None else _lib.launch_count - launches0)
+
+    def step_search_only():  # the same step without the result all-gather
+        return graphed(ids_dev) if graphed is not None else grbeam_search(adapter, ids_dev, widths)
 
     with torch.inference_mode():
         for _ in range(args.warmup):
             step_device()
         with ClockSampler(local_rank) as clocks:
-            ms, launches = timed(step_device, args.steps)
+            ms, launches = timed(step_device, args.steps, "step_ms")
         ms_e2e, _ = timed(step_e2e, args.steps)
+        if world > 1:  # how the step splits into search time per rank and the exchange
+            timed(step_search_only, args.steps, "search_only_ms")
         res = graphed(ids_dev) if graphed is not None else grbeam_search(adapter, ids_dev, widths)
         if graphed is not None:
             graphed.check()
@@ -303,18 +329,21 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
 
     if rank != 0:
         return
-    flops = algorithmic_flops(cfg)
+    flops = algorithmic_flops(cfg, B=batch)
     peaks, peak_kind = measured_peaks()
-    value = world * BATCH / (ms / 1000)
+    value = world * batch / (ms / 1000)
     line = {
         "metric": METRIC, "value": value, "unit": "requests/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong" if args.total_requests else "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random prompts, random-init weights)",
-        "config": {"workload": WORKLOAD, "model": "qwen3.5-0.8b-shaped", "global_batch": world * BATCH,
+        "per_rank": per_rank,
+        "config": {"workload": WORKLOAD if batch == 32 else WORKLOAD.replace("B=32/GPU", f"B={batch}/GPU"),
+                   "model": "qwen3.5-0.8b-shaped", "global_batch": world * batch,
                    "seq_len": PROMPT, "beam": BEAM, "depth": DEPTH, "parallelism": f"dp{world} (request shards)",
                    "l2": "working set > 126 MB L2 (weights 1.5 GB, logits 4 GB per step); no flush"},
-        "e2e": {"value": world * BATCH / (ms_e2e / 1000), "unit": "requests/s",
-                "h2d_bytes_per_step": BATCH * PROMPT * 8, "d2h_bytes_per_step": BATCH * BEAM * (DEPTH * 8 + 4)},
+        "e2e": {"value": world * batch / (ms_e2e / 1000), "unit": "requests/s",
+                "h2d_bytes_per_step": batch * PROMPT * 8, "d2h_bytes_per_step": batch * BEAM * (DEPTH * 8 + 4)},
         "gpu_launches": launches,
         "clocks": clocks.summary(),
         "path_roofline": {"bound": "tensor", "algorithmic_tflop_per_step": flops / 1e12,
@@ -414,6 +443,82 @@ def run_sid(args, rank: int, world: int, local_rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def hf_model(cfg, weights, device):
+    """A Transformers ``Qwen3_5ForConditionalGeneration`` holding the benchmark's weights
+    (BF16; a one-block stand-in vision tower, which GRBeam never runs) -- what the
+    reference's runner loads with ``from_pretrained``."""
+    import torch
+    from transformers import Qwen3_5Config, Qwen3_5ForConditionalGeneration
+
+    vision = dict(depth=1, hidden_size=64, intermediate_size=128, num_heads=2, out_hidden_size=cfg.hidden_size)
+    hf_cfg = Qwen3_5Config(text_config=cfg.to_hf_kwargs(), vision_config=vision,
+                           tie_word_embeddings=cfg.tie_word_embeddings)
+    with torch.device("meta"):
+        model = Qwen3_5ForConditionalGeneration(hf_cfg)
+    model = model.to_empty(device=device).to(torch.bfloat16)
+    text = model.model.language_model
+    text.load_state_dict({k: v.to(torch.bfloat16) for k, v in weights.items() if k != "lm_head.weight"},
+                         strict=False)
+    if cfg.tie_word_embeddings:
+        model.lm_head.weight = text.embed_tokens.weight
+    return model.eval()
+
+
+def run_dropin(args, rank: int, world: int, local_rank: int) -> None:
+    """The reference runner's external-backend path, unchanged: ``benchmarks/grbeam.py
+    --backend external --adapter-factory kadllm_b200.factory:make`` loads the model, calls
+    the factory and times ``search(adapter, ids, [beam] * depth).tokens.tolist()`` by wall
+    clock, eager launches, with its deterministic prompts ``10 + (i + 17 r) % 100``
+    (benchmarks/grbeam.py:219-223,254-257,299,325-346)."""
+    import torch
+
+    from kadllm_b200 import _lib
+    from kadllm_b200.config import QWEN35_08B
+    from kadllm_b200.factory import make
+    from kadllm_b200.synthetic import torch_weights
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    cfg = QWEN35_08B
+    model = hf_model(cfg, torch_weights(cfg, seed=0, device=dev), dev)
+    adapter, search = make(model)
+    ids = torch.tensor([[10 + (i + r * 17) % 100 for i in range(PROMPT)] for r in range(BATCH)], device=dev)
+    widths = [BEAM] * DEPTH
+
+    def run():
+        return search(adapter, ids, widths).tokens.tolist()
+
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            tokens = run()
+        times = []
+        n0 = _lib.launch_count
+        for _ in range(args.steps):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            tokens = run()
+            torch.cuda.synchronize()
+            times.append(time.perf_counter() - t0)
+        launches = (_lib.launch_count - n0) // max(args.steps, 1)
+    distinct = all(len({tuple(b) for b in req}) == BEAM for req in tokens)
+    if rank != 0:
+        return
+    mean = statistics.mean(times)
+    line = {
+        "metric": METRIC + " -- drop-in runner path (eager, wall clock)", "value": world * BATCH / mean,
+        "unit": "requests/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": mean * 1000, "median_ms": statistics.median(times) * 1000, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic weights; the reference runner's deterministic prompts",
+        "config": {"workload": "dropin: factory.make(Qwen3_5ForConditionalGeneration) + search(...).tokens.tolist()",
+                   "model": "qwen3.5-0.8b-shaped", "global_batch": world * BATCH, "seq_len": PROMPT,
+                   "beam": BEAM, "depth": DEPTH},
+        "library_launches_per_search": launches,
+        "checks": {"distinct_beams": distinct},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def profile_kernels(engine, adapter, ids_dev, widths, args):
     """Per-entry-point device time over one extra search, CUDA events on the
     launching stream; the dominant kernel's roofline is derived from it."""
@@ -451,9 +556,13 @@ def main() -> None:
     ap.add_argument("--roofline-kernel", default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="eager launches instead of one CUDA graph per search")
-    ap.add_argument("--workload", choices=["grbeam", "sid"], default="grbeam",
-                    help="grbeam: the headline metric; sid: two-level conditional SID, prefixes 512-4096")
+    ap.add_argument("--workload", choices=["grbeam", "sid", "dropin"], default="grbeam",
+                    help="grbeam: the headline metric; sid: two-level conditional SID, prefixes 512-4096; "
+                         "dropin: the reference runner's external-backend call, eager, wall clock")
     ap.add_argument("--sid-batch", type=int, default=32)
+    ap.add_argument("--batch", type=int, default=BATCH, help="requests per GPU (weak scaling)")
+    ap.add_argument("--total-requests", type=int, default=0,
+                    help="a fixed number of requests split over the GPUs (strong scaling, e.g. 256)")
     ap.add_argument("--sid-streams", type=int, default=1)
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
@@ -474,7 +583,7 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        (run_sid if args.workload == "sid" else run_native)(args, rank, world, local_rank)
+        {"sid": run_sid, "dropin": run_dropin}.get(args.workload, run_native)(args, rank, world, local_rank)
     finally:
         if world > 1:
             dist.destroy_process_group()

@@ -134,6 +134,8 @@ KADLLM_API int kadllm_prefix_attention(
  *   mask          [B*Wp, V] uint8 (nonzero = allowed) or NULL
  *   old_history   [B, Wp, depth] int64 or NULL when depth == 0
  *   out_scores    [B, width] f32;  out_history [B, width, depth+1] int64
+ *   out_parent    [B, width] int32 or NULL: each selected beam's previous beam
+ *                 (index in 0..Wp-1; 0 for unfilled slots)
  *   workspace     >= kadllm_beam_select_workspace(B, Wp) bytes, 256-byte
  *                 aligned, caller-owned.  Its flag word (offset 0, the same for
  *                 every Wp) is cleared by each depth-0 call, the first step of
@@ -145,9 +147,9 @@ KADLLM_API int64_t kadllm_beam_select_workspace(int64_t batch, int64_t prev_widt
 KADLLM_API int kadllm_beam_select(const void* logits, int logits_dtype, int64_t ld_row,
                                   const float* parent_scores, const void* mask,
                                   const int64_t* old_history, float* out_scores,
-                                  int64_t* out_history, void* workspace, int64_t workspace_bytes,
-                                  int64_t batch, int64_t prev_width, int64_t vocab, int64_t width,
-                                  int64_t depth, void* stream);
+                                  int64_t* out_history, int32_t* out_parent, void* workspace,
+                                  int64_t workspace_bytes, int64_t batch, int64_t prev_width,
+                                  int64_t vocab, int64_t width, int64_t depth, void* stream);
 /* Copies the workspace's flag word to *flags_out (bit 0: candidate overflow)
  * after synchronising `stream`.  The word is at offset 0 whatever the widths;
  * batch and prev_width are those the workspace was sized for. */
@@ -323,6 +325,32 @@ KADLLM_API int kadllm_causal_attention(const void* q, int64_t sq_row, int64_t sq
 KADLLM_API int kadllm_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc,
                            const void* resid, int64_t ld_resid, int64_t M, int64_t N, int64_t K, int64_t n_out,
                            int epilogue, uint32_t* status, void* stream);
+
+/* Beam reorder as index work: dst row i = src row (i / group) * src_group + index[i]
+ * (index clamped to [0, src_group)), row_bytes per row; strides in BYTES, multiples
+ * of 16.  Gathers a previous decode step's per-beam rows (projections, suffix K / V)
+ * by parent beam, as the reference's history.gather does for the tokens
+ * (src/kadllm/grbeam.py:102-104). */
+KADLLM_API int kadllm_gather_rows(const void* src, int64_t ld_src, const int32_t* index, int64_t group,
+                                  int64_t src_group, int64_t rows, int64_t row_bytes, void* dst, int64_t ld_dst,
+                                  void* stream);
+
+/* GDN decode mixer continuing a beam's suffix from the previous decode step (step
+ * reuse at T = 2; no separate counterpart in the reference, which replays both
+ * suffix tokens from the prefix, src/kadllm/adapters/qwen3_5.py:144-177): beam j
+ * of request b has the suffix [token of previous-step beam parent[b*W + j], new
+ * token]; proj_prev [B*prev_width, ld_proj] holds the previous step's projection
+ * rows (as kadllm_gdn_mixer_replay takes them at T = 1), proj [B*W, ld_proj] the
+ * new tokens' rows, out [B*W, HV*V] the new token's mixer output -- the same
+ * values kadllm_gdn_mixer_replay gives for that token at T = 2 without
+ * recomputing the first token's projection.  Head dims 64 / 128 (K == V). */
+KADLLM_API int kadllm_gdn_mixer_continue(const void* proj_prev, const int32_t* parent, int64_t prev_width,
+                                         const void* proj, int64_t ld_proj, const void* conv_state,
+                                         int64_t conv_hist, const void* conv_weight, const void* rec_state,
+                                         const float* a_log, const float* dt_bias, const float* norm_weight,
+                                         float norm_eps, void* out, int64_t batch, int64_t beam_width,
+                                         int64_t heads, int64_t v_heads, int64_t k_dim, int64_t v_dim,
+                                         void* stream);
 
 /* Diagnostics: one CTA runs the tensor-core kernels' bounded mbarrier wait on a
  * barrier nothing completes, giving up after max_cycles SM clocks (1 .. 2^32)

@@ -109,10 +109,33 @@ class Qwen35GRBeamAdapter:
         self._check_state(history, state)
         return self.engine.decode(history, state)
 
+    def end_search(self) -> None:
+        """Drop the step cache of the search that just finished (``grbeam_search`` calls it)."""
+        self._step = None
+
     @torch.no_grad()
     def decode_select(self, history, state, scores, width, selector):
-        """Decode and select in one pass (used by ``kadllm_b200.grbeam_search``)."""
+        """Decode and select in one pass (used by ``kadllm_b200.grbeam_search``).
+
+        Step reuse: a one-token decode keeps its per-layer work (projections, q / k / v)
+        and asks the selection for each new beam's parent; when the search then decodes
+        exactly the history that selection returned, the two-token replay reuses the
+        parent's first token and runs only the new one.  Results are those of a full
+        replay of both tokens (the same kernels' arithmetic on the same inputs)."""
         self._check_state(history, state)
+        T = history.shape[2]
+        step, self._step = getattr(self, "_step", None), None
+        if T == 2 and step is not None and step[0] is history and step[1] is state:
+            _, _, cache, parent, prev_width = step
+            logits = self.engine.decode(history, state, reuse=(cache, parent, prev_width))
+            return selector.step(logits, scores, history, width)
+        if T == 1 and self.engine.step_reuse:
+            cache = {}
+            logits = self.engine.decode(history, state, cache=cache)
+            new_scores, new_hist, parent = selector.step(logits, scores, history, width, parents=True)
+            del logits
+            self._step = (new_hist, state, cache, parent, history.shape[1])
+            return new_scores, new_hist
         logits = self.engine.decode(history, state)
         return selector.step(logits, scores, history, width)
 

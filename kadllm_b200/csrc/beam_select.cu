@@ -47,6 +47,7 @@ struct SelArgs {
   const int64_t* old_hist;     // [B*Wp, depth] or null
   float* out_scores;           // [B*W]
   int64_t* out_hist;           // [B*W, depth+1]
+  int32_t* out_parent;         // [B*W] previous-beam index of each selected beam, or null
   float2* rowstat;             // [rows] (max, log-sum-exp offset)
   uint32_t* rowhist;           // [rows, kRowBins]
   uint32_t* rowlen;            // [rows] leading bins of rowhist that can be non-zero
@@ -540,6 +541,7 @@ __global__ void __launch_bounds__(1024) finalize_kernel(const SelArgs a) {
     const int64_t parent = int64_t(idx) / a.V, token = int64_t(idx) % a.V;
     const int64_t o = int64_t(b) * a.W + w;
     a.out_scores[o] = score;
+    if (a.out_parent) a.out_parent[o] = int32_t(parent);
     int64_t* h = a.out_hist + o * (a.depth + 1);
     const int64_t* src = a.old_hist ? a.old_hist + (int64_t(b) * a.Wp + parent) * a.depth : nullptr;
     for (int d = 0; d < a.depth; ++d) h[d] = src[d];
@@ -617,7 +619,7 @@ namespace {
 // flag word when non-null.
 int select_with_workspace(const void* logits, int logits_dtype, int64_t ld_row, const float* parent_scores,
                           const void* mask, const int64_t* old_history, float* out_scores, int64_t* out_history,
-                          void* workspace, int64_t workspace_bytes, uint32_t* flags, int64_t batch,
+                          int32_t* out_parent, void* workspace, int64_t workspace_bytes, uint32_t* flags, int64_t batch,
                           int64_t prev_width, int64_t vocab, int64_t width, int64_t depth, void* stream) {
   KB_REQUIRE(valid_dtype(logits_dtype), KADLLM_EDTYPE, "beam select: unsupported logits dtype");
   KB_REQUIRE(batch >= 1 && prev_width >= 1 && vocab >= 1 && width >= 1 && depth >= 0, KADLLM_EINVAL,
@@ -637,7 +639,7 @@ int select_with_workspace(const void* logits, int logits_dtype, int64_t ld_row, 
   SelArgs a{};
   a.logits = logits; a.dtype = logits_dtype; a.ld = ld_row;
   a.parent = parent_scores; a.mask = static_cast<const uint8_t*>(mask); a.old_hist = old_history;
-  a.out_scores = out_scores; a.out_hist = out_history;
+  a.out_scores = out_scores; a.out_hist = out_history; a.out_parent = out_parent;
   a.rowstat = reinterpret_cast<float2*>(w + ws.rowstat);
   a.rowhist = reinterpret_cast<uint32_t*>(w + ws.rowhist);
   a.rowlen = reinterpret_cast<uint32_t*>(w + ws.rowlen);
@@ -665,12 +667,12 @@ int select_with_workspace(const void* logits, int logits_dtype, int64_t ld_row, 
 
 extern "C" int kadllm_beam_select(const void* logits, int logits_dtype, int64_t ld_row, const float* parent_scores,
                                   const void* mask, const int64_t* old_history, float* out_scores,
-                                  int64_t* out_history, void* workspace, int64_t workspace_bytes, int64_t batch,
-                                  int64_t prev_width, int64_t vocab, int64_t width, int64_t depth,
-                                  void* stream) {
+                                  int64_t* out_history, int32_t* out_parent, void* workspace,
+                                  int64_t workspace_bytes, int64_t batch, int64_t prev_width, int64_t vocab,
+                                  int64_t width, int64_t depth, void* stream) {
   return kb::select_with_workspace(logits, logits_dtype, ld_row, parent_scores, mask, old_history, out_scores,
-                                   out_history, workspace, workspace_bytes, nullptr, batch, prev_width, vocab,
-                                   width, depth, stream);
+                                   out_history, out_parent, workspace, workspace_bytes, nullptr, batch, prev_width,
+                                   vocab, width, depth, stream);
 }
 
 extern "C" int kadllm_beam_select_status(const void* workspace, int64_t batch, int64_t prev_width,
@@ -754,6 +756,6 @@ extern "C" int kadllm_beam_select_noalloc(const void* logits, int logits_dtype, 
   cudaError_t e = cudaMemsetAsync(out_flags, 0, sizeof(uint32_t), static_cast<cudaStream_t>(stream));
   KB_REQUIRE(e == cudaSuccess, KADLLM_ECUDA, "beam select (no-alloc): %s", cudaGetErrorString(e));
   return select_with_workspace(logits, logits_dtype, ld_row, parent_scores, mask, old_history, out_scores,
-                               out_history, scratch, int64_t(kNoAllocScratchBytes), out_flags, batch, prev_width,
-                               vocab, width, depth, stream);
+                               out_history, nullptr, scratch, int64_t(kNoAllocScratchBytes), out_flags, batch,
+                               prev_width, vocab, width, depth, stream);
 }

@@ -155,22 +155,34 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
   const int col_q = h * D, col_k = key_dim + h * D, col_v = 2 * key_dim + hv * D, col_z = conv_dim + hv * D;
   const int col_b = conv_dim + HV * D + hv, col_a = conv_dim + HV * D + HV + hv;
 
+  // Projection row of (token tr, beam): rows (beam, t) of proj, or in continuation mode
+  // the parent's row of the previous step (tr = 0) / the beam's row of the new token.
+  auto prow_of = [&](int tr, int beam) -> const __nv_bfloat16* {
+    if (TMAX == 2 && a.proj_prev != nullptr) {
+      if (tr == 0) {
+        const int p = min(max(a.parent[int64_t(b) * a.W + beam], 0), a.Wp - 1);
+        return a.proj_prev + (int64_t(b) * a.Wp + p) * ld;
+      }
+      return a.proj + (int64_t(b) * a.W + beam) * ld;
+    }
+    return a.proj + ((int64_t(b) * a.W + beam) * TMAX + tr) * ld;
+  };
   // Stage octet `oct` into `buf` (the caller commits the cp.async group).
   auto stage = [&](int oct, unsigned char* buf) {
     for (int idx = lane; idx < 8 * 4 * CH; idx += 32) {
       const int r = idx / (4 * CH), piece = (idx / CH) & 3, c = idx % CH;
       const int beam = oct * BPO + r % BPO;
       const bool ok = beam < a.W;
-      const int64_t prow = (int64_t(b) * a.W + (ok ? beam : 0)) * TMAX + r / BPO;
+      const __nv_bfloat16* prow = prow_of(r / BPO, ok ? beam : 0);
       const int col = piece < 2 ? (piece == 0 ? col_q : col_k) : (piece == 2 ? col_v : col_z);
-      cp16z(buf + r * ROWB + piece * 2 * D + c * 16, a.proj + prow * ld + col + c * 8, ok);
+      cp16z(buf + r * ROWB + piece * 2 * D + c * 16, prow + col + c * 8, ok);
     }
     if (lane < 16) {
       const int r = lane >> 1, which = lane & 1;
       const int beam = oct * BPO + r % BPO;
       const bool ok = beam < a.W;
-      const int64_t prow = (int64_t(b) * a.W + (ok ? beam : 0)) * TMAX + r / BPO;
-      cp4z(buf + r * ROWB + 8 * D + which * 4, a.proj + prow * ld + ((which ? col_a : col_b) & ~1), ok);
+      const __nv_bfloat16* prow = prow_of(r / BPO, ok ? beam : 0);
+      cp4z(buf + r * ROWB + 8 * D + which * 4, prow + ((which ? col_a : col_b) & ~1), ok);
     }
   };
 
@@ -352,11 +364,12 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
     }
     __syncwarp();
     // ---- the octet's output rows, 16 bytes per store ------------------------------------
+    const bool cont = TMAX == 2 && a.proj_prev != nullptr;  // continuation: the new token's rows only
     for (int idx = lane; idx < 8 * CH; idx += 32) {
       const int r = idx / CH, c = idx % CH;
       const int beam = (oct0 + it) * BPO + r % BPO;
-      if (beam < a.W) {
-        const int64_t orow = (int64_t(b) * a.W + beam) * TMAX + r / BPO;
+      if (beam < a.W && (!cont || r / BPO == 1)) {
+        const int64_t orow = cont ? int64_t(b) * a.W + beam : (int64_t(b) * a.W + beam) * TMAX + r / BPO;
         *reinterpret_cast<uint4*>(a.out + orow * (int64_t(HV) * D) + hv * D + c * 8) =
             *reinterpret_cast<const uint4*>(buf + r * ROWB + c * 16);
       }
@@ -397,7 +410,8 @@ int launch_mixer(const MixerArgs& a, cudaStream_t stream) {
 bool gdn_mixer_staged_ok(const MixerArgs& a) {
   if (!(a.D == 64 || a.D == 128) || a.T < 1 || a.T > 2 || a.conv_hist < 3) return false;
   const auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-  return al16(a.proj) && al16(a.out) && al16(a.state) && a.ld_proj % 8 == 0;
+  return al16(a.proj) && al16(a.out) && al16(a.state) && a.ld_proj % 8 == 0 &&
+         (a.proj_prev == nullptr || (a.T == 2 && al16(a.proj_prev)));
 }
 
 int gdn_mixer_staged(const MixerArgs& a, cudaStream_t stream) {

@@ -16,9 +16,14 @@ struct MixerArgs {
   const float* dt_bias;
   const float* norm_weight;
   float norm_eps;
-  __nv_bfloat16* out;  // [B*W*T, HV*D]
+  __nv_bfloat16* out;  // [B*W*T, HV*D]; continuation: [B*W, HV*D] (the new token only)
   int B, W, T, H, HV, D;
   float scale;
+  // Continuation (T = 2): token 0 of beam j is the previous step's token of beam parent[b*W + j],
+  // whose projection row is proj_prev[b*Wp + parent]; proj holds the new tokens' rows [B*W]
+  const __nv_bfloat16* proj_prev;  // [B*Wp, ld_proj] or null
+  const int32_t* parent;           // [B*W]
+  int Wp;
 };
 
 // True when the staged kernel takes this call: D in {64, 128}, T <= 2 and

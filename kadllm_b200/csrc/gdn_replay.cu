@@ -503,3 +503,36 @@ extern "C" int kadllm_gdn_mixer_replay(const void* proj, int64_t ld_proj, const 
   }
   return dispatch_gdn<true>(int(k_dim), int(v_dim), a, static_cast<cudaStream_t>(stream));
 }
+
+extern "C" int kadllm_gdn_mixer_continue(const void* proj_prev, const int32_t* parent, int64_t prev_width,
+                                        const void* proj, int64_t ld_proj, const void* conv_state,
+                                        int64_t conv_hist, const void* conv_weight, const void* rec_state,
+                                        const float* a_log, const float* dt_bias, const float* norm_weight,
+                                        float norm_eps, void* out, int64_t batch, int64_t beam_width,
+                                        int64_t heads, int64_t v_heads, int64_t k_dim, int64_t v_dim,
+                                        void* stream) {
+  using namespace kb;
+  if (int rc = check_common(batch, beam_width, 2, heads, v_heads, k_dim, v_dim)) return rc;
+  KB_REQUIRE(proj_prev && parent && proj && conv_state && conv_weight && rec_state && a_log && dt_bias &&
+                 norm_weight && out,
+             KADLLM_EINVAL, "gdn mixer (continuation): null pointer");
+  KB_REQUIRE(prev_width >= 1 && prev_width < (int64_t(1) << 30), KADLLM_EINVAL,
+             "gdn mixer (continuation): prev_width out of range");
+  const int64_t conv_dim = 2 * heads * k_dim + v_heads * v_dim;
+  KB_REQUIRE(conv_hist >= 3, KADLLM_EINVAL, "gdn mixer (continuation): conv state needs >= 3 taps");
+  KB_REQUIRE(ld_proj >= conv_dim + v_heads * v_dim + 2 * v_heads, KADLLM_EINVAL,
+             "gdn mixer (continuation): projection row too short");
+  MixerArgs m{};
+  m.proj = static_cast<const __nv_bfloat16*>(proj); m.ld_proj = ld_proj;
+  m.conv_state = static_cast<const __nv_bfloat16*>(conv_state); m.conv_hist = conv_hist;
+  m.conv_weight = static_cast<const __nv_bfloat16*>(conv_weight);
+  m.state = static_cast<const __nv_bfloat16*>(rec_state);
+  m.a_log = a_log; m.dt_bias = dt_bias; m.norm_weight = norm_weight; m.norm_eps = norm_eps;
+  m.out = static_cast<__nv_bfloat16*>(out);
+  m.B = int(batch); m.W = int(beam_width); m.T = 2; m.H = int(heads); m.HV = int(v_heads); m.D = int(k_dim);
+  m.scale = 1.0f / sqrtf(float(k_dim));
+  m.proj_prev = static_cast<const __nv_bfloat16*>(proj_prev); m.parent = parent; m.Wp = int(prev_width);
+  KB_REQUIRE(k_dim == v_dim && gdn_mixer_staged_ok(m), KADLLM_EUNSUPPORTED,
+             "gdn mixer (continuation): head dims 64 / 128 (K == V), 16-byte aligned rows only");
+  return gdn_mixer_staged(m, static_cast<cudaStream_t>(stream));
+}

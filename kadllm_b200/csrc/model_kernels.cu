@@ -294,6 +294,21 @@ __global__ void __launch_bounds__(256) qk_norm_rope_d256_kernel(
 
 using namespace kb;
 
+// dst row i = src row (i / group) * src_group + index[i] (clamped into the group), 16 bytes a thread.
+__global__ void __launch_bounds__(256) gather_rows_kernel(const unsigned char* src, int64_t ld_src,
+                                                          const int32_t* index, int group, int src_group,
+                                                          int64_t rows, int chunks, unsigned char* dst,
+                                                          int64_t ld_dst) {
+  const int64_t total = rows * chunks;
+  for (int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < total; e += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t i = e / chunks;
+    const int c = int(e - i * chunks);
+    const int p = min(max(index[i], 0), src_group - 1);
+    const int64_t r = (i / group) * src_group + p;
+    reinterpret_cast<uint4*>(dst + i * ld_dst)[c] = reinterpret_cast<const uint4*>(src + r * ld_src)[c];
+  }
+}
+
 extern "C" int kadllm_embed_rmsnorm(const int64_t* ids, const void* table, int64_t vocab, const float* weight,
                                     float eps, void* x, void* normed, int64_t rows, int64_t hidden, void* stream) {
   KB_REQUIRE(rows >= 1 && vocab >= 1, KADLLM_EINVAL, "embed: empty");
@@ -419,4 +434,24 @@ extern "C" int kadllm_qk_norm_rope(const void* proj, int64_t ld_proj, int64_t q_
 #undef KB_QK_CASE
   set_error("qk_norm_rope: head_dim %lld not in {32, 64, 128, 256}", (long long)head_dim);
   return KADLLM_EUNSUPPORTED;
+}
+
+extern "C" int kadllm_gather_rows(const void* src, int64_t ld_src, const int32_t* index, int64_t group,
+                                  int64_t src_group, int64_t rows, int64_t row_bytes, void* dst, int64_t ld_dst,
+                                  void* stream) {
+  KB_REQUIRE(src && index && dst, KADLLM_EINVAL, "gather rows: null pointer");
+  KB_REQUIRE(rows >= 1 && group >= 1 && src_group >= 1 && row_bytes >= 16 && row_bytes % 16 == 0 &&
+                 ld_src % 16 == 0 && ld_dst % 16 == 0 && ld_src >= row_bytes && ld_dst >= row_bytes &&
+                 group < (int64_t(1) << 30) && src_group < (int64_t(1) << 30) && row_bytes < (int64_t(1) << 30),
+             KADLLM_EINVAL, "gather rows: sizes and strides must be positive multiples of 16 bytes");
+  KB_REQUIRE(((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0, KADLLM_EINVAL,
+             "gather rows: pointers must be 16-byte aligned");
+  const int chunks = int(row_bytes / 16);
+  const int64_t total = rows * chunks;
+  const unsigned blocks = unsigned(total / 256 + 1 < 4096 ? total / 256 + 1 : 4096);
+  gather_rows_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const unsigned char*>(src), ld_src, index, int(group), int(src_group), rows, chunks,
+      static_cast<unsigned char*>(dst), ld_dst);
+  KB_CHECK_LAUNCH("gather rows launch");
+  return KADLLM_OK;
 }

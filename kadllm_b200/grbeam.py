@@ -64,8 +64,9 @@ class BeamSelector:
         self.workspace = torch.zeros(nbytes, dtype=torch.uint8, device=device)
 
     def step(self, logits: torch.Tensor, scores: torch.Tensor | None, history: torch.Tensor,
-             width: int, mask: torch.Tensor | None = None):
-        """logits [B, Wp, V] -> (scores [B, width] f32, history [B, width, depth+1] int64)."""
+             width: int, mask: torch.Tensor | None = None, parents: bool = False):
+        """logits [B, Wp, V] -> (scores [B, width] f32, history [B, width, depth+1] int64),
+        plus each selected beam's previous-beam index [B, width] int32 with ``parents``."""
         B, Wp, V = logits.shape
         if Wp > self.max_prev:
             raise ValueError("selection workspace too small for this width")
@@ -85,13 +86,14 @@ class BeamSelector:
         m = None if mask is None else mask.contiguous().view(torch.uint8)
         out_scores = torch.empty(B, width, dtype=torch.float32, device=logits.device)
         out_hist = torch.empty(B, width, depth + 1, dtype=torch.int64, device=logits.device)
+        out_parent = torch.empty(B, width, dtype=torch.int32, device=logits.device) if parents else None
         _lib.call(
             "kadllm_beam_select",
             logits.data_ptr(), _lib.dtype_code(logits), ld, _lib.ptr(parent), _lib.ptr(m), _lib.ptr(old),
-            out_scores.data_ptr(), out_hist.data_ptr(), self.workspace.data_ptr(),
+            out_scores.data_ptr(), out_hist.data_ptr(), _lib.ptr(out_parent), self.workspace.data_ptr(),
             self.workspace.numel(), B, Wp, V, width, depth, _lib.stream(logits.device),
         )
-        return out_scores, out_hist
+        return (out_scores, out_hist, out_parent) if parents else (out_scores, out_hist)
 
     def check(self) -> None:
         """Raise if any step overflowed its candidate buffer (synchronises)."""
@@ -166,6 +168,9 @@ def search_from_prefill(adapter: GRBeamAdapter, prefill: PrefillResult, B: int, 
                 raise ValueError("constraint must return a bool mask matching logits")
         scores, history = selector.step(logits, scores, history, width, mask)
         del logits, mask
+    end = getattr(adapter, "end_search", None)
+    if callable(end):  # release per-search caches the adapter kept between steps
+        end()
     if own:
         selector.check()
         check_adapter(adapter)

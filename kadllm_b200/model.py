@@ -160,6 +160,13 @@ class HybridModel:
         # device status word of the tensor-core kernels (bit 0: a bounded wait timed out)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
 
+    @property
+    def step_reuse(self) -> bool:
+        """Whether a two-token decode can continue from the one-token step's cache (the
+        continuing GDN mixer takes head dims 64 / 128 with K == V)."""
+        c = self.cfg
+        return c.linear_key_head_dim == c.linear_value_head_dim and c.linear_key_head_dim in (64, 128)
+
     def check(self) -> None:
         """Raise if a tensor-core kernel reported a timed-out wait (synchronises)."""
         st = int(self.status.item())
@@ -245,14 +252,23 @@ class HybridModel:
         self._gemm(act, layer.w_down, resid=x)
 
     def _qk_rope(self, P, rows, pos_base, rows_per_seq, q_out, k_out, k_strides, v_out, v_strides, mixer,
-                 pos_of_row=None, max_pos=None):
+                 pos_of_row=None, max_pos=None, q_row_stride=None):
         c = self.cfg
         cos, sin = self._rope((pos_base + rows_per_seq if max_pos is None else max_pos) + 1)
         _lib.call("kadllm_qk_norm_rope", P.data_ptr(), P.stride(0), c.num_attention_heads, c.num_key_value_heads,
                   c.head_dim, mixer.q_norm.data_ptr(), mixer.k_norm.data_ptr(), c.rms_norm_eps, cos.data_ptr(),
                   sin.data_ptr(), c.rotary_dim, _lib.ptr(pos_of_row), pos_base, rows_per_seq, q_out.data_ptr(),
-                  c.num_attention_heads * c.head_dim, c.head_dim, k_out.data_ptr(), *k_strides, v_out.data_ptr(),
-                  *v_strides, rows, self._stream())
+                  q_row_stride or c.num_attention_heads * c.head_dim, c.head_dim, k_out.data_ptr(), *k_strides,
+                  v_out.data_ptr(), *v_strides, rows, self._stream())
+
+    def _gather_rows(self, src: torch.Tensor, parent: torch.Tensor, width: int, prev_width: int,
+                     dst: torch.Tensor, dst_row_stride: int):
+        """dst row i <- src row (i // width) * prev_width + parent[i] (rows of ``src`` [B*prev_width, n],
+        contiguous; ``dst`` a view whose rows are ``dst_row_stride`` elements apart)."""
+        n = src.shape[1]
+        esz = src.element_size()
+        _lib.call("kadllm_gather_rows", src.data_ptr(), n * esz, parent.data_ptr(), width, prev_width,
+                  parent.numel(), n * esz, dst.data_ptr(), dst_row_stride * esz, self._stream())
 
     # ------------------------------------------------------------------ prefill
     @torch.no_grad()
@@ -288,7 +304,7 @@ class HybridModel:
                           c.rms_norm_eps, out.data_ptr(), out.stride(0), rec.data_ptr(), ws.data_ptr(), ws.numel(),
                           B, L, c.linear_num_key_heads, c.linear_num_value_heads, c.linear_key_head_dim,
                           c.linear_value_head_dim, s)
-                self._gemm(out, m.w_out, resid=x)
+                w_post = m.w_out
                 prefix.append((conv_state, rec))
                 tiles.append(None)
             else:
@@ -312,19 +328,41 @@ class HybridModel:
                               kc.stride(2), kc.stride(1), vc.data_ptr(), vc.stride(0), vc.stride(2), vc.stride(1),
                               gate.data_ptr(), P.stride(0), 2 * D, out.data_ptr(),
                               out.stride(0), D, B, L, hq, hk, D, D ** -0.5, s)
-                self._gemm(out, m.w_o, resid=x)
+                w_post = m.w_o
                 prefix.append((kc.transpose(1, 2), vc.transpose(1, 2)))
                 tiles.append(tile)
-            self._add_norm(x, None, layer.post_ln, normed)
-            self._mlp(layer, normed, x)
-            if taps is not None:
-                taps.append(x.view(B, L, -1)[:, -1].float().clone())
             if i + 1 < len(self.layers):
-                self._add_norm(x, None, self.layers[i + 1].input_ln, normed)
-        last = torch.empty(B, c.hidden_size, dtype=BF16, device=self.device)
-        self._add_norm(x, None, self.final_norm, last, rows=B, step=L, offset=L - 1)
+                self._post_mixer(layer, out, w_post, x, normed, self.layers[i + 1].input_ln)
+                if taps is not None:
+                    taps.append(x.view(B, L, -1)[:, -1].float().clone())
+        last_rows = torch.arange(B, device=self.device) * L + (L - 1)
+        last = self._finish_last_rows(layer, out, w_post, x, last_rows, taps)
         logits = self._gemm(last, self.lm_head if head is None else head)
         return logits, HybridPrefix(L, B, self.owner, tuple(prefix), tuple(tiles))
+
+    def _post_mixer(self, layer: Layer, out, w_post, x, normed, next_ln):
+        """x += out . w_post^T; x += MLP(RMSNorm(x)); normed = the next layer's RMSNorm(x)."""
+        self._gemm(out, w_post, resid=x)
+        self._add_norm(x, None, layer.post_ln, normed)
+        self._mlp(layer, normed, x)
+        self._add_norm(x, None, next_ln, normed)
+
+    def _finish_last_rows(self, layer: Layer, out, w_post, x, last_rows, taps=None):
+        """The last layer after its mixer, for the rows the logits read only (each
+        request's last prompt position): the mixer ran over every row for the prefix
+        state; its output projection, MLP and the final norm need only these rows.
+        Returns the final-norm hidden [len(last_rows), H]."""
+        n = last_rows.numel()
+        xl = x.index_select(0, last_rows)
+        self._gemm(out.index_select(0, last_rows), w_post, resid=xl)
+        normed = torch.empty_like(xl)
+        self._add_norm(xl, None, layer.post_ln, normed)
+        self._mlp(layer, normed, xl)
+        if taps is not None:
+            taps.append(xl.float().clone())
+        last = torch.empty(n, self.cfg.hidden_size, dtype=BF16, device=self.device)
+        self._add_norm(xl, None, self.final_norm, last)
+        return last
 
     @torch.no_grad()
     def prefill_varlen(self, prompts, head: torch.Tensor | None = None):
@@ -372,7 +410,7 @@ class HybridModel:
                           c.rms_norm_eps, out.data_ptr(), out.stride(0), rec.data_ptr(), ws.data_ptr(), ws.numel(),
                           cu.data_ptr(), R, B, Lmax, c.linear_num_key_heads, c.linear_num_value_heads,
                           c.linear_key_head_dim, c.linear_value_head_dim, s)
-                self._gemm(out, m.w_out, resid=x)
+                w_post = m.w_out
                 prefix.append((conv_state, rec))
                 tiles.append(None)
             else:
@@ -395,25 +433,30 @@ class HybridModel:
                           nblk, None, 0, 0, 0, None, 0, 0, 0, gate.data_ptr(), P.stride(0), 0, 2 * D,
                           out.data_ptr(), out.stride(0), 0, D, self.status.data_ptr(), cu.data_ptr(), B, 1, 1, hq,
                           hk, Lmax, D, D ** -0.5, 1, s)
-                self._gemm(out, m.w_o, resid=x)
+                w_post = m.w_o
                 prefix.append((kp, vp))
                 tiles.append((kt, vt, nblk))
-            self._add_norm(x, None, layer.post_ln, normed)
-            self._mlp(layer, normed, x)
             if i + 1 < len(self.layers):
-                self._add_norm(x, None, self.layers[i + 1].input_ln, normed)
-        last_rows = cu[1:].long() - 1
-        xl = x.index_select(0, last_rows)
-        last = torch.empty(B, c.hidden_size, dtype=BF16, device=self.device)
-        _lib.call("kadllm_add_rmsnorm", xl.data_ptr(), None, 0, self.final_norm.data_ptr(),
-                  c.rms_norm_eps, last.data_ptr(), B, 1, 0, c.hidden_size, s)
+                self._post_mixer(layer, out, w_post, x, normed, self.layers[i + 1].input_ln)
+        last = self._finish_last_rows(layer, out, w_post, x, cu[1:].long() - 1)
         logits = self._gemm(last, self.lm_head if head is None else head)
         return logits, HybridPrefix(Lmax, B, self.owner, tuple(prefix), tuple(tiles), cu, tuple(lens))
 
     # ------------------------------------------------------------------ decode
     @torch.no_grad()
-    def decode_hidden(self, history: torch.Tensor, state: HybridPrefix) -> torch.Tensor:
-        """Replay history [B, W, T] -> final-norm hidden of the last position [B*W, H]."""
+    def decode_hidden(self, history: torch.Tensor, state: HybridPrefix, cache: dict | None = None,
+                      reuse: tuple | None = None) -> torch.Tensor:
+        """Replay history [B, W, T] -> final-norm hidden of the last position [B*W, H].
+
+        ``cache`` (a dict; T = 1) receives what a following two-token step of these
+        beams' children reuses: per GDN layer the projection rows of the token, per
+        attention layer its q / k / v.  ``reuse = (cache, parent, prev_width)`` (T = 2):
+        the first suffix token of beam j of request b is the token of the previous
+        step's beam ``parent[b, j]`` (int32), whose per-layer work the cache holds;
+        only the new token is replayed (its projections, the continuing GDN mixer,
+        attention with the first token's q / k / v gathered by parent, MLP)."""
+        if reuse is not None:
+            return self._decode_continue(history, state, *reuse)
         c = self.cfg
         B, W, T = history.shape
         BW, R = B * W, B * W * T
@@ -437,6 +480,8 @@ class HybridModel:
                           m.dt_bias.data_ptr(), m.norm_w.data_ptr(), c.rms_norm_eps, out.data_ptr(), B, W, T,
                           c.linear_num_key_heads, c.linear_num_value_heads, c.linear_key_head_dim,
                           c.linear_value_head_dim, s)
+                if cache is not None:
+                    cache[i] = P
                 self._gemm(out, m.w_out, resid=x)
             else:
                 q = torch.empty(R, hq, D, dtype=BF16, device=self.device)
@@ -448,29 +493,10 @@ class HybridModel:
                                   max_pos=state.length + T)
                 else:
                     self._qk_rope(P, R, state.length, T, q, ks, suffix_strides, vs, suffix_strides, m)
-                pk, pv = cached  # [B, L, HK, D] views
+                if cache is not None:
+                    cache[i] = (q.view(R, hq * D), ks.view(R, hk * D), vs.view(R, hk * D))
                 out = torch.empty(R, hq * D, dtype=BF16, device=self.device)
-                gate = P[:, D:]
-                tile = state.tiles[i] if i < len(state.tiles) else None
-                if varlen:  # every request against its own prefix length
-                    kt, vt, nblk = tile
-                    _lib.call("kadllm_attention_tiled_varlen", q.data_ptr(), T * hq * D, hq * D, D, kt.data_ptr(),
-                              vt.data_ptr(), nblk, ks.data_ptr(), *suffix_strides, vs.data_ptr(), *suffix_strides,
-                              gate.data_ptr(), T * P.stride(0), P.stride(0), 2 * D, out.data_ptr(), T * hq * D,
-                              hq * D, D, self.status.data_ptr(), state.cu.data_ptr(), B, W, T, hq, hk, state.length,
-                              D, D ** -0.5, 0, s)
-                elif tile is not None:
-                    kt, vt, nblk = tile
-                    _lib.call("kadllm_attention_tiled", q.data_ptr(), T * hq * D, hq * D, D, kt.data_ptr(),
-                              vt.data_ptr(), nblk, ks.data_ptr(), *suffix_strides, vs.data_ptr(), *suffix_strides,
-                              gate.data_ptr(), T * P.stride(0), P.stride(0), 2 * D, out.data_ptr(), T * hq * D,
-                              hq * D, D, self.status.data_ptr(), B, W, T, hq, hk, state.length, D, D ** -0.5, 0, s)
-                else:
-                    _lib.call("kadllm_prefix_attention", q.data_ptr(), T * hq * D, hq * D, D, pk.data_ptr(),
-                              *pk.stride()[:3], pv.data_ptr(), *pv.stride()[:3], ks.data_ptr(), *suffix_strides,
-                              vs.data_ptr(), *suffix_strides, None, gate.data_ptr(), T * P.stride(0), P.stride(0),
-                              2 * D, out.data_ptr(), T * hq * D, hq * D, D, _lib.DTYPE_CODES[BF16], B, W, T, hq, hk,
-                              state.length, D, D ** -0.5, s)
+                self._attend(i, state, q, ks, vs, P, out, B, W, T, T * P.stride(0), P.stride(0))
                 self._gemm(out, m.w_o, resid=x)
             self._add_norm(x, None, layer.post_ln, normed)
             self._mlp(layer, normed, x)
@@ -480,10 +506,99 @@ class HybridModel:
         self._add_norm(x, None, self.final_norm, last, rows=BW, step=T, offset=T - 1)
         return last
 
+    def _attend(self, i, state, q, ks, vs, P, out, B, W, T, sg_row, sg_t):
+        """Decode attention of layer i: rows (beam, t) of q [B*W, T, Hq, D] against the
+        request's prefix and the beam's suffix keys ks / vs [B*W, T, HK, D] (row-major
+        views), the output gate from P (gate row stride sg_row per beam, sg_t per step),
+        into out [B*W, T, Hq*D]."""
+        c = self.cfg
+        hk, D, hq = c.num_key_value_heads, c.head_dim, c.num_attention_heads
+        s = self._stream()
+        suffix_strides = (T * hk * D, hk * D, D)
+        gate = P[:, D:]  # gate of head h at column h*2D + D
+        tile = state.tiles[i] if i < len(state.tiles) else None
+        pk, pv = state.layers[i]  # [B, L, HK, D] views
+        if state.cu is not None:  # every request against its own prefix length
+            kt, vt, nblk = tile
+            _lib.call("kadllm_attention_tiled_varlen", q.data_ptr(), T * hq * D, hq * D, D, kt.data_ptr(),
+                      vt.data_ptr(), nblk, ks.data_ptr(), *suffix_strides, vs.data_ptr(), *suffix_strides,
+                      gate.data_ptr(), sg_row, sg_t, 2 * D, out.data_ptr(), T * hq * D, hq * D, D,
+                      self.status.data_ptr(), state.cu.data_ptr(), B, W, T, hq, hk, state.length, D, D ** -0.5, 0, s)
+        elif tile is not None:
+            kt, vt, nblk = tile
+            _lib.call("kadllm_attention_tiled", q.data_ptr(), T * hq * D, hq * D, D, kt.data_ptr(),
+                      vt.data_ptr(), nblk, ks.data_ptr(), *suffix_strides, vs.data_ptr(), *suffix_strides,
+                      gate.data_ptr(), sg_row, sg_t, 2 * D, out.data_ptr(), T * hq * D, hq * D, D,
+                      self.status.data_ptr(), B, W, T, hq, hk, state.length, D, D ** -0.5, 0, s)
+        else:
+            _lib.call("kadllm_prefix_attention", q.data_ptr(), T * hq * D, hq * D, D, pk.data_ptr(),
+                      *pk.stride()[:3], pv.data_ptr(), *pv.stride()[:3], ks.data_ptr(), *suffix_strides,
+                      vs.data_ptr(), *suffix_strides, None, gate.data_ptr(), sg_row, sg_t, 2 * D, out.data_ptr(),
+                      T * hq * D, hq * D, D, _lib.DTYPE_CODES[BF16], B, W, T, hq, hk, state.length, D, D ** -0.5, s)
+
+    def _decode_continue(self, history, state, prev, parent, prev_width):
+        """The T = 2 step from the previous (T = 1) step's cache: rows are the new tokens only."""
+        c = self.cfg
+        B, W, T = history.shape
+        if T != 2:
+            raise ValueError("step reuse continues a one-token suffix by one token (T = 2)")
+        R = B * W
+        parent = parent.to(device=self.device, dtype=torch.int32).reshape(-1).contiguous()
+        if parent.numel() != R:
+            raise ValueError("parent must hold one previous-beam index per beam")
+        ids = history[:, :, -1].to(device=self.device, dtype=torch.int64).reshape(-1).contiguous()
+        x, normed = self._embed(ids)
+        s = self._stream()
+        hk, D, hq = c.num_key_value_heads, c.head_dim, c.num_attention_heads
+        pos = None
+        if state.cu is not None:
+            pos = (torch.tensor(state.lengths, dtype=torch.int64) + 1).repeat_interleave(W).to(self.device)
+        for i, (layer, cached) in enumerate(zip(self.layers, state.layers)):
+            m = layer.mixer
+            P = self._gemm(normed, m.w_in)
+            if layer.kind == LINEAR:
+                out = torch.empty(R, c.value_dim, dtype=BF16, device=self.device)
+                conv_state, rec = cached
+                P0 = prev[i]
+                _lib.call("kadllm_gdn_mixer_continue", P0.data_ptr(), parent.data_ptr(), prev_width, P.data_ptr(),
+                          P.stride(0), conv_state.data_ptr(), conv_state.shape[-1], m.conv_w.data_ptr(),
+                          rec.data_ptr(), m.a_log.data_ptr(), m.dt_bias.data_ptr(), m.norm_w.data_ptr(),
+                          c.rms_norm_eps, out.data_ptr(), B, W, c.linear_num_key_heads, c.linear_num_value_heads,
+                          c.linear_key_head_dim, c.linear_value_head_dim, s)
+                self._gemm(out, m.w_out, resid=x)
+            else:
+                q = torch.empty(R, 2, hq, D, dtype=BF16, device=self.device)
+                ks = torch.empty(R, 2, hk, D, dtype=BF16, device=self.device)
+                vs = torch.empty_like(ks)
+                pq, pk, pv = prev[i]  # the first token's q / k / v, rows of the previous step's beams
+                self._gather_rows(pq, parent, W, prev_width, q, 2 * hq * D)
+                self._gather_rows(pk, parent, W, prev_width, ks, 2 * hk * D)
+                self._gather_rows(pv, parent, W, prev_width, vs, 2 * hk * D)
+                kv_strides = (2 * hk * D, hk * D, D)  # (beam row, step, head) of slot 1
+                if pos is not None:
+                    self._qk_rope(P, R, 0, 1, q[:, 1], ks[:, 1], kv_strides, vs[:, 1], kv_strides, m,
+                                  pos_of_row=pos, max_pos=state.length + 2, q_row_stride=2 * hq * D)
+                else:
+                    self._qk_rope(P, R, state.length + 1, 1, q[:, 1], ks[:, 1], kv_strides, vs[:, 1], kv_strides,
+                                  m, q_row_stride=2 * hq * D)
+                out = torch.empty(R, 2, hq * D, dtype=BF16, device=self.device)
+                # the first token's query rows are recomputed alongside (their outputs unused)
+                self._attend(i, state, q, ks, vs, P, out, B, W, 2, P.stride(0), 0)
+                self._gemm(out[:, 1], m.w_o, resid=x)
+            self._add_norm(x, None, layer.post_ln, normed)
+            self._mlp(layer, normed, x)
+            if i + 1 < len(self.layers):
+                self._add_norm(x, None, self.layers[i + 1].input_ln, normed)
+        last = torch.empty(R, c.hidden_size, dtype=BF16, device=self.device)
+        self._add_norm(x, None, self.final_norm, last, rows=R)
+        return last
+
     @torch.no_grad()
-    def decode(self, history: torch.Tensor, state: HybridPrefix, head: torch.Tensor | None = None) -> torch.Tensor:
+    def decode(self, history: torch.Tensor, state: HybridPrefix, head: torch.Tensor | None = None,
+               cache: dict | None = None, reuse: tuple | None = None) -> torch.Tensor:
         """Replay [B, W, T] suffix tokens; return [B, W, V] logits (BF16) over the LM
-        head's rows, or over ``head``'s rows when given."""
+        head's rows, or over ``head``'s rows when given (``cache`` / ``reuse``: see
+        :meth:`decode_hidden`)."""
         B, W, _ = history.shape
         w = self.lm_head if head is None else head
-        return self._gemm(self.decode_hidden(history, state), w).view(B, W, -1)
+        return self._gemm(self.decode_hidden(history, state, cache=cache, reuse=reuse), w).view(B, W, -1)

@@ -49,7 +49,7 @@ def work_of(name: str, args: tuple) -> tuple[str, float] | None:
         read = R * (conv_dim + HV * DV + 2 * HV) * 2 + B * HV * DK * DV * 2 + B * conv_dim * 4 * 2
         return "hbm", float(read + R * HV * DV * 2)
     if name == "kadllm_beam_select":
-        B, Wp, V, W, depth = args[10:15]
+        B, Wp, V, W, depth = args[11:16]
         esz = 4 if args[1] == 0 else 2
         return "hbm", float(B * Wp * V * esz)
     if name == "kadllm_silu_mul":
@@ -74,7 +74,7 @@ def measured_traffic(name: str, args: tuple) -> float | None:
         if args[32]:  # causal prefill: 335.6 + 109.8 MB
             return 445.4e6
         return 285.4e6 if tuple(args[25:27]) == (256, 2) else None  # decode T = 2: 235.0 + 50.4 MB
-    if name == "kadllm_beam_select" and tuple(args[10:13]) == (32, 256, 248320):
+    if name == "kadllm_beam_select" and tuple(args[11:14]) == (32, 256, 248320):
         return 4100.4e6  # rowstats 4068.7 + 21.2 MB, collect 8.7 MB, threshold 1.3 MB, finalize 0.2 MB
     return None
 

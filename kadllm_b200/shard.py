@@ -49,3 +49,11 @@ def max_over_ranks(value: float, device: torch.device | str = "cpu") -> float:
     t = torch.tensor([float(value)], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def all_ranks(value: float, device: torch.device | str = "cpu") -> list[float]:
+    """Every rank's value, in rank order (every rank gets the list); [value] on one process."""
+    if not dist.is_available() or not dist.is_initialized() or dist.get_world_size() == 1:
+        return [float(value)]
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    return [float(x) for x in _all_gather(t).tolist()]

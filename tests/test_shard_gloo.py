@@ -25,7 +25,7 @@ def _worker(rank: int, world: int, port: int, q) -> None:
     os.environ["MASTER_PORT"] = str(port)
     import datetime
 
-    from kadllm_b200.shard import gather_beams, max_over_ranks, rank_prompts
+    from kadllm_b200.shard import all_ranks, gather_beams, max_over_ranks, rank_prompts
 
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
@@ -36,7 +36,8 @@ def _worker(rank: int, world: int, port: int, q) -> None:
         scores = torch.full((B, W), -float(rank), dtype=torch.float32) - torch.arange(W, dtype=torch.float32)
         all_t, all_s = gather_beams(tokens, scores)
         slow = max_over_ranks(10.0 + rank)
-        q.put((rank, ids, all_t.numpy(), all_s.numpy(), slow))
+        every = all_ranks(10.0 + rank)
+        q.put((rank, ids, all_t.numpy(), all_s.numpy(), slow, every))
     finally:
         dist.destroy_process_group()
 
@@ -51,8 +52,8 @@ def test_two_rank_shards_gather_and_max():
         p.start()
     got = {}
     for _ in range(world):
-        rank, ids, all_t, all_s, slow = q.get(timeout=120)
-        got[rank] = (ids, all_t, all_s, slow)
+        rank, ids, all_t, all_s, slow, every = q.get(timeout=120)
+        got[rank] = (ids, all_t, all_s, slow, every)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
@@ -61,19 +62,21 @@ def test_two_rank_shards_gather_and_max():
     B, W, D, V = 3, 4, 2, 1000
     want_t = np.concatenate([ids0[:, :W * D].reshape(B, W, D), ids1[:, :W * D].reshape(B, W, D) + V])
     for r in range(world):
-        _, all_t, all_s, slow = got[r]
+        _, all_t, all_s, slow, every = got[r]
         np.testing.assert_array_equal(all_t, want_t)  # rank order, identical on every rank
         assert all_s.shape == (world * B, W)
         np.testing.assert_array_equal(all_s[:B, 0], 0.0)
         np.testing.assert_array_equal(all_s[B:, 0], -1.0)
         assert slow == 11.0  # max over ranks
+        assert every == [10.0, 11.0]  # every rank's value, in rank order
 
 
 def test_single_process_identity():
-    from kadllm_b200.shard import gather_beams, max_over_ranks
+    from kadllm_b200.shard import all_ranks, gather_beams, max_over_ranks
 
     t = torch.arange(6).reshape(1, 3, 2)
     s = torch.zeros(1, 3)
     a, b = gather_beams(t, s)
     assert a is t and b is s
     assert max_over_ranks(2.5) == 2.5
+    assert all_ranks(2.5) == [2.5]
