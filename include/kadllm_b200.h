@@ -150,6 +150,22 @@ KADLLM_API int kadllm_beam_select(const void* logits, int logits_dtype, int64_t 
                                   int64_t* out_history, int32_t* out_parent, void* workspace,
                                   int64_t workspace_bytes, int64_t batch, int64_t prev_width,
                                   int64_t vocab, int64_t width, int64_t depth, void* stream);
+/* Fused LM head and selection (the reference's lm_head(norm(x)) then per-request
+ * log_softmax + topk, src/kadllm/adapters/qwen3_5.py:235 and
+ * src/kadllm/grbeam.py:87-104): kadllm_gemm_logits computes the BF16 logits of
+ * the B*Wp decode rows and, in its epilogue, every row's per-256-column-chunk
+ * maximum and sum of exp(x - maximum) into the selection workspace (sized by
+ * kadllm_beam_select_workspace_fused); kadllm_beam_select_fused then selects
+ * without another pass over the logits: row statistics and the threshold come
+ * from the chunk statistics, and only the chunks that can hold candidates are
+ * read.  Same outputs and tie rule as kadllm_beam_select (BF16, no mask). */
+KADLLM_API int64_t kadllm_beam_select_workspace_fused(int64_t batch, int64_t prev_width);
+KADLLM_API int kadllm_beam_select_fused(const void* logits, int64_t ld_row, const float* parent_scores,
+                                        const int64_t* old_history, float* out_scores, int64_t* out_history,
+                                        int32_t* out_parent, void* workspace, int64_t workspace_bytes,
+                                        int64_t batch, int64_t prev_width, int64_t vocab, int64_t width,
+                                        int64_t depth, void* stream);
+
 /* Copies the workspace's flag word to *flags_out (bit 0: candidate overflow)
  * after synchronising `stream`.  The word is at offset 0 whatever the widths;
  * batch and prev_width are those the workspace was sized for. */
@@ -269,7 +285,9 @@ KADLLM_API int kadllm_kv_tile_varlen(const void* src, int64_t s_pos, int64_t s_h
  * 128 query rows per CTA, S and O in tensor memory, bulk-copied K / V blocks.
  * causal = 0: beam decode -- rows (beam, t, g) of q [B*W rows][T][Hq][D]
  *   attend to the request's prefix and their beam's suffix keys s <= t
- *   (src/kadllm/ops.py:252-341); suffix_k / suffix_v [B*W][T][HK][D].
+ *   (src/kadllm/ops.py:252-341); suffix_k / suffix_v [B*W][T][HK][D]; only the
+ *   suffix steps t >= first_step have query rows (and outputs): first_step =
+ *   T - 1 attends the newest token alone while the earlier ones stay keys.
  * causal = 1: prompt prefill -- q rows = tokens b*L + pos, keys <= pos (SDPA in
  *   Qwen3_5Attention, TF:620-692); suffix and steps unused.
  * gate (optional): out = bf16(bf16(o) * bf16(sigmoid(gate))).  All strides in
@@ -281,9 +299,9 @@ KADLLM_API int kadllm_attention_tiled(const void* q, int64_t sq_row, int64_t sq_
                                       const void* suffix_v, int64_t ssv_row, int64_t ssv_t, int64_t ssv_h,
                                       const void* gate, int64_t sg_row, int64_t sg_t, int64_t sg_h, void* out,
                                       int64_t so_row, int64_t so_t, int64_t so_h, uint32_t* status,
-                                      int64_t batch, int64_t beam_width, int64_t steps, int64_t q_heads,
-                                      int64_t kv_heads, int64_t prefix_len, int64_t head_dim, float scale,
-                                      int causal, void* stream);
+                                      int64_t batch, int64_t beam_width, int64_t steps, int64_t first_step,
+                                      int64_t q_heads, int64_t kv_heads, int64_t prefix_len, int64_t head_dim,
+                                      float scale, int causal, void* stream);
 /* The same with prompts of their own lengths: request b's prefix has
  * cu_seqlens[b+1] - cu_seqlens[b] tokens (tiles from kadllm_kv_tile_varlen with
  * max_prefix_len); causal = 1: q / gate / out rows are the packed prompt rows
@@ -293,8 +311,9 @@ KADLLM_API int kadllm_attention_tiled_varlen(
     int64_t blocks_per_head, const void* suffix_k, int64_t ssk_row, int64_t ssk_t, int64_t ssk_h,
     const void* suffix_v, int64_t ssv_row, int64_t ssv_t, int64_t ssv_h, const void* gate, int64_t sg_row,
     int64_t sg_t, int64_t sg_h, void* out, int64_t so_row, int64_t so_t, int64_t so_h, uint32_t* status,
-    const int32_t* cu_seqlens, int64_t batch, int64_t beam_width, int64_t steps, int64_t q_heads, int64_t kv_heads,
-    int64_t max_prefix_len, int64_t head_dim, float scale, int causal, void* stream);
+    const int32_t* cu_seqlens, int64_t batch, int64_t beam_width, int64_t steps, int64_t first_step,
+    int64_t q_heads, int64_t kv_heads, int64_t max_prefix_len, int64_t head_dim, float scale, int causal,
+    void* stream);
 
 /* Prompt causal GQA attention (flash loop on the tensor cores) with the fused
  * output gate out = bf16(o) * bf16(sigmoid(gate)) (gate may be NULL).
@@ -325,6 +344,14 @@ KADLLM_API int kadllm_causal_attention(const void* q, int64_t sq_row, int64_t sq
 KADLLM_API int kadllm_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc,
                            const void* resid, int64_t ld_resid, int64_t M, int64_t N, int64_t K, int64_t n_out,
                            int epilogue, uint32_t* status, void* stream);
+/* The LM head of a decode step for the fused selection: logits [M = batch *
+ * prev_width, N = vocabulary] = A . B^T (BF16), plus each row's chunk statistics
+ * into `workspace` (>= kadllm_beam_select_workspace_fused(batch, prev_width)
+ * bytes, 256-byte aligned); N a multiple of 8, at most 393216. */
+KADLLM_API int kadllm_gemm_logits(const void* a, int64_t lda, const void* b, int64_t ldb, void* logits,
+                                  int64_t ld_logits, int64_t M, int64_t N, int64_t K, void* workspace,
+                                  int64_t workspace_bytes, int64_t batch, int64_t prev_width, uint32_t* status,
+                                  void* stream);
 
 /* Beam reorder as index work: dst row i = src row (i / group) * src_group + index[i]
  * (index clamped to [0, src_group)), row_bytes per row; strides in BYTES, multiples

@@ -29,9 +29,9 @@ SIGNATURES: dict[str, list] = {
     "kadllm_diag_wait_timeout": [P, L, P],
     "kadllm_gdn_prefill_split_varlen": [P, L, P, P, P, P, P, F, P, L, P, P, L, P, L, L, L, L, L, L, L, P],
     "kadllm_attention_tiled": [P, L, L, L, P, P, L, P, L, L, L, P, L, L, L, P, L, L, L, P, L, L, L, P,
-                               L, L, L, L, L, L, L, F, I, P],
+                               L, L, L, L, L, L, L, L, F, I, P],
     "kadllm_attention_tiled_varlen": [P, L, L, L, P, P, L, P, L, L, L, P, L, L, L, P, L, L, L, P, L, L, L, P,
-                                      P, L, L, L, L, L, L, L, F, I, P],
+                                      P, L, L, L, L, L, L, L, L, F, I, P],
     "kadllm_causal_attention": [P, L, L, P, L, L, L, P, L, L, L, P, L, L, P, L, L, L, L, L, L, L, F, P],
     "kadllm_beam_select": [P, I, L, P, P, P, P, P, P, P, L, L, L, L, L, L, P],
     "kadllm_beam_select_status": [P, L, L, P, P],
@@ -40,6 +40,8 @@ SIGNATURES: dict[str, list] = {
     "kadllm_gdn_mixer_replay": [P, L, P, L, P, P, P, P, P, F, P, L, L, L, L, L, L, L, P],
     "kadllm_causal_conv1d_replay": [P, L, L, L, P, L, L, L, L, P, P, P, I, L, L, L, L, L, I, P],
     "kadllm_gemm": [P, L, P, L, P, L, P, L, L, L, L, L, I, P, P],
+    "kadllm_gemm_logits": [P, L, P, L, P, L, L, L, L, P, L, L, L, P, P],
+    "kadllm_beam_select_fused": [P, L, P, P, P, P, P, P, L, L, L, L, L, L, P],
     "kadllm_gather_rows": [P, L, P, L, L, L, L, P, L, P],
     "kadllm_gdn_mixer_continue": [P, P, L, P, L, P, L, P, P, P, P, P, F, P, L, L, L, L, L, L, P],
     "kadllm_prefix_attention": [P, L, L, L, P, L, L, L, P, L, L, L, P, L, L, L, P, L, L, L, P, P,
@@ -63,6 +65,8 @@ def lib() -> ctypes.CDLL:
         handle.kadllm_abi_version.restype = ctypes.c_int
         handle.kadllm_beam_select_workspace.restype = ctypes.c_int64
         handle.kadllm_beam_select_workspace.argtypes = [L, L]
+        handle.kadllm_beam_select_workspace_fused.restype = ctypes.c_int64
+        handle.kadllm_beam_select_workspace_fused.argtypes = [L, L]
         handle.kadllm_gdn_prefill_workspace.restype = ctypes.c_int64
         handle.kadllm_gdn_prefill_workspace.argtypes = [L, L, L, L, L]
         handle.kadllm_kv_tile_bytes.restype = ctypes.c_int64
@@ -80,6 +84,7 @@ _ERRORS = {1: ValueError, 2: TypeError, 3: NotImplementedError, 4: RuntimeError}
 
 # kernels launched per successful call of each entry point (for launch accounting)
 LAUNCHES_PER_CALL = {"kadllm_beam_select": 4, "kadllm_beam_select_noalloc": 4, "kadllm_beam_select_status": 0,
+                     "kadllm_beam_select_fused": 4,
                      "kadllm_gdn_prefill_split": 3, "kadllm_gdn_prefill_split_varlen": 3}
 launch_count = 0
 _count_lock = threading.Lock()

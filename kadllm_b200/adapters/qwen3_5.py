@@ -124,20 +124,22 @@ class Qwen35GRBeamAdapter:
         replay of both tokens (the same kernels' arithmetic on the same inputs)."""
         self._check_state(history, state)
         T = history.shape[2]
+        ws = selector.workspace if self.engine.fused_select(history.shape[0], history.shape[1]) else None
+        select = selector.step_fused if ws is not None else selector.step
         step, self._step = getattr(self, "_step", None), None
         if T == 2 and step is not None and step[0] is history and step[1] is state:
             _, _, cache, parent, prev_width = step
-            logits = self.engine.decode(history, state, reuse=(cache, parent, prev_width))
-            return selector.step(logits, scores, history, width)
+            logits = self.engine.decode(history, state, reuse=(cache, parent, prev_width), select_workspace=ws)
+            return select(logits, scores, history, width)
         if T == 1 and self.engine.step_reuse:
             cache = {}
-            logits = self.engine.decode(history, state, cache=cache)
-            new_scores, new_hist, parent = selector.step(logits, scores, history, width, parents=True)
+            logits = self.engine.decode(history, state, cache=cache, select_workspace=ws)
+            new_scores, new_hist, parent = select(logits, scores, history, width, parents=True)
             del logits
             self._step = (new_hist, state, cache, parent, history.shape[1])
             return new_scores, new_hist
-        logits = self.engine.decode(history, state)
-        return selector.step(logits, scores, history, width)
+        logits = self.engine.decode(history, state, select_workspace=ws)
+        return select(logits, scores, history, width)
 
 
 class NativeGRBeamAdapter(Qwen35GRBeamAdapter):

@@ -60,6 +60,7 @@ struct AttnTcArgs {
   uint32_t* status;
   const int* cu;  // varlen prompts: request b's tokens are rows [cu[b], cu[b+1]) (null: b*L .. +L)
   int B, W, T, H, HK, G, L;  // L: the (longest) prefix length
+  int t0;                    // decode: first suffix step with query rows (rows for steps t0 .. T-1)
   float scale_log2;
 };
 
@@ -106,7 +107,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
   const bool rowthr = tid < kRowThreads;                         // warps 0-7 (warps 8, 9 only issue)
   float* sbm = reinterpret_cast<float*>(smem + M::bm);           // partner exchange [half][row]
   const int b = blockIdx.y / a.HK, hk = blockIdx.y % a.HK;
-  const int TG = a.T * a.G;
+  const int TG = (a.T - a.t0) * a.G;  // query rows per beam
   int64_t seq0 = int64_t(b) * a.L;  // first prompt row of request b
   int Lb = a.L;                      // its prefix length
   if (a.cu) {
@@ -125,7 +126,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
   } else {
     beam = gr / TG;
     const int rem = gr % TG;
-    t = rem / a.G;
+    t = a.t0 + rem / a.G;
     g = rem % a.G;
   }
   const int hq = hk * a.G + g;
@@ -509,7 +510,7 @@ int launch_attn_tc(const AttnTcArgs& a, cudaStream_t stream) {
     set_error("tiled attention: cannot reserve %zu bytes of shared memory", AttnTcSmem::bytes);
     return KADLLM_ECUDA;
   }
-  const int64_t R = CAUSAL ? int64_t(a.L) * a.G : int64_t(a.W) * a.T * a.G;
+  const int64_t R = CAUSAL ? int64_t(a.L) * a.G : int64_t(a.W) * (a.T - a.t0) * a.G;
   dim3 grid(unsigned((R + kRows - 1) / kRows), unsigned(a.B * a.HK));
   kern<<<grid, kThreads, AttnTcSmem::bytes, stream>>>(a);
   KB_CHECK_LAUNCH("tiled attention launch");
@@ -571,9 +572,11 @@ int attention_tiled(const void* q, int64_t sq_row, int64_t sq_t, int64_t sq_h, c
                     int64_t ssk_t, int64_t ssk_h, const void* suffix_v, int64_t ssv_row, int64_t ssv_t, int64_t ssv_h,
                     const void* gate, int64_t sg_row, int64_t sg_t, int64_t sg_h, void* out, int64_t so_row,
                     int64_t so_t, int64_t so_h, uint32_t* status, const int* cu, int64_t batch, int64_t beam_width,
-                    int64_t steps, int64_t q_heads, int64_t kv_heads, int64_t prefix_len, int64_t head_dim,
-                    float scale, int causal, void* stream) {
+                    int64_t steps, int64_t first_step, int64_t q_heads, int64_t kv_heads, int64_t prefix_len,
+                    int64_t head_dim, float scale, int causal, void* stream) {
   KB_REQUIRE(q && k_tiles && v_tiles && out && status, KADLLM_EINVAL, "tiled attention: null pointer");
+  KB_REQUIRE(first_step >= 0 && (causal ? first_step == 0 : first_step < steps), KADLLM_EINVAL,
+             "tiled attention: first_step must lie in [0, steps) (0 for prefill)");
   KB_REQUIRE(head_dim == kD, KADLLM_EUNSUPPORTED, "tiled attention: head_dim must be %d", kD);
   KB_REQUIRE(batch >= 1 && q_heads >= 1 && kv_heads >= 1 && q_heads % kv_heads == 0 && prefix_len >= 1 &&
                  blocks_per_head * kBlk >= prefix_len,
@@ -588,7 +591,7 @@ int attention_tiled(const void* q, int64_t sq_row, int64_t sq_t, int64_t sq_h, c
                  ssk_t % 8 == 0 && ssk_h % 8 == 0 && ssv_row % 8 == 0 && ssv_t % 8 == 0 && ssv_h % 8 == 0 &&
                  sg_row % 8 == 0 && sg_t % 8 == 0 && sg_h % 8 == 0,
              KADLLM_EINVAL, "tiled attention: operands and strides must be 16-byte aligned");
-  const int64_t R = causal ? prefix_len * (q_heads / kv_heads) : beam_width * steps * (q_heads / kv_heads);
+  const int64_t R = causal ? prefix_len * (q_heads / kv_heads) : beam_width * (steps - first_step) * (q_heads / kv_heads);
   KB_REQUIRE(R < (int64_t(1) << 30) && batch * kv_heads <= 65535, KADLLM_EINVAL, "tiled attention: too many rows");
   AttnTcArgs a{};
   a.q = static_cast<const __nv_bfloat16*>(q); a.sq_row = sq_row; a.sq_t = sq_t; a.sq_h = sq_h;
@@ -601,7 +604,7 @@ int attention_tiled(const void* q, int64_t sq_row, int64_t sq_t, int64_t sq_h, c
   a.status = status;
   a.cu = cu;
   a.B = int(batch); a.W = int(causal ? 1 : beam_width); a.T = int(causal ? 1 : steps); a.H = int(q_heads);
-  a.HK = int(kv_heads); a.G = int(q_heads / kv_heads); a.L = int(prefix_len);
+  a.HK = int(kv_heads); a.G = int(q_heads / kv_heads); a.L = int(prefix_len); a.t0 = int(first_step);
   a.scale_log2 = (scale > 0.f ? scale : 1.0f / sqrtf(float(head_dim))) * 1.4426950408889634f;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return causal ? launch_attn_tc<true>(a, s) : launch_attn_tc<false>(a, s);
@@ -615,12 +618,12 @@ extern "C" int kadllm_attention_tiled(const void* q, int64_t sq_row, int64_t sq_
                                       int64_t ssv_row, int64_t ssv_t, int64_t ssv_h, const void* gate, int64_t sg_row,
                                       int64_t sg_t, int64_t sg_h, void* out, int64_t so_row, int64_t so_t,
                                       int64_t so_h, uint32_t* status, int64_t batch, int64_t beam_width,
-                                      int64_t steps, int64_t q_heads, int64_t kv_heads, int64_t prefix_len,
-                                      int64_t head_dim, float scale, int causal, void* stream) {
+                                      int64_t steps, int64_t first_step, int64_t q_heads, int64_t kv_heads,
+                                      int64_t prefix_len, int64_t head_dim, float scale, int causal, void* stream) {
   return kb::attention_tiled(q, sq_row, sq_t, sq_h, k_tiles, v_tiles, blocks_per_head, suffix_k, ssk_row, ssk_t,
                              ssk_h, suffix_v, ssv_row, ssv_t, ssv_h, gate, sg_row, sg_t, sg_h, out, so_row, so_t,
-                             so_h, status, nullptr, batch, beam_width, steps, q_heads, kv_heads, prefix_len,
-                             head_dim, scale, causal, stream);
+                             so_h, status, nullptr, batch, beam_width, steps, first_step, q_heads, kv_heads,
+                             prefix_len, head_dim, scale, causal, stream);
 }
 
 extern "C" int kadllm_attention_tiled_varlen(
@@ -628,11 +631,12 @@ extern "C" int kadllm_attention_tiled_varlen(
     int64_t blocks_per_head, const void* suffix_k, int64_t ssk_row, int64_t ssk_t, int64_t ssk_h,
     const void* suffix_v, int64_t ssv_row, int64_t ssv_t, int64_t ssv_h, const void* gate, int64_t sg_row,
     int64_t sg_t, int64_t sg_h, void* out, int64_t so_row, int64_t so_t, int64_t so_h, uint32_t* status,
-    const int32_t* cu_seqlens, int64_t batch, int64_t beam_width, int64_t steps, int64_t q_heads, int64_t kv_heads,
-    int64_t max_prefix_len, int64_t head_dim, float scale, int causal, void* stream) {
+    const int32_t* cu_seqlens, int64_t batch, int64_t beam_width, int64_t steps, int64_t first_step,
+    int64_t q_heads, int64_t kv_heads, int64_t max_prefix_len, int64_t head_dim, float scale, int causal,
+    void* stream) {
   KB_REQUIRE(cu_seqlens != nullptr, KADLLM_EINVAL, "tiled attention: null sequence offsets");
   return kb::attention_tiled(q, sq_row, sq_t, sq_h, k_tiles, v_tiles, blocks_per_head, suffix_k, ssk_row, ssk_t,
                              ssk_h, suffix_v, ssv_row, ssv_t, ssv_h, gate, sg_row, sg_t, sg_h, out, so_row, so_t,
-                             so_h, status, cu_seqlens, batch, beam_width, steps, q_heads, kv_heads, max_prefix_len,
-                             head_dim, scale, causal, stream);
+                             so_h, status, cu_seqlens, batch, beam_width, steps, first_step, q_heads, kv_heads,
+                             max_prefix_len, head_dim, scale, causal, stream);
 }

@@ -28,15 +28,12 @@
 #include <mutex>
 #include <type_traits>
 
-#include "common.cuh"
+#include "beam_select.cuh"
 
 namespace kb {
 namespace {
 
-constexpr int kRowBins = 2048;     // (max - x) in [0, 64) nats, last bin = farther
-constexpr int kReqBins = 4096;
-constexpr float kBinsPerNat = 32.f;
-constexpr int kCap = 16384;        // candidates kept per request
+using namespace sel;
 constexpr int kRowThreads = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -56,6 +53,7 @@ struct SelArgs {
   uint32_t* flags;             // [1] bit 0: candidate overflow
   unsigned long long* cand;    // [B, kCap]
   uint16_t* vsum;              // [rows, kSumMax] bf16 maximum of each 32-vector chunk, or null
+  const float* tsum;           // [rows, kSumMax] sum of exp(x - chunk max) per chunk (fused selection), or null
   int B, Wp, W, depth;
   int64_t V;
 };
@@ -166,9 +164,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
 //     candidates.  Pass 2 of row r runs inside pass 1 of the CTA's next
 //     row (two tables and two histograms, alternating), so the logits are read
 //     from HBM exactly once.
-constexpr int kStatThreads = 1024;
-constexpr int kStatSlots = 48;  // vectors per thread (V <= 48 * 8 * 1024) for the table
-constexpr int kSumMax = kStatSlots * 32;  // chunks per row: (slot k, warp w) = vectors k * 1024 + 32 w + [0, 32)
 constexpr float kRefSlack = 64.f;
 __host__ __device__ constexpr size_t stat_smem(int slots) { return size_t(2) * slots * kStatThreads * 2; }
 
@@ -375,6 +370,70 @@ __global__ void __launch_bounds__(kStatThreads, 1) rowstats_bf16_kernel(const Se
   }
 }
 
+// Row statistics from the per-chunk statistics the LM-head GEMM wrote (fused selection):
+// one warp per row combines the chunk maxima (vsum) and sums (tsum) into the row's
+// max and log-sum-exp, and bins the chunk maxima -- each one an element of its chunk,
+// so the counts are lower bounds of the element counts, as with the 16-byte
+// vectors' maxima of rowstats_bf16_kernel -- into the row histogram, skipping the
+// chunks below a bound on the row's W-th largest chunk maximum (32 lanes x the
+// ceil(W/32)-th largest of each lane's maxima).
+constexpr int kTileStatWarps = 8;
+constexpr int kTopPerLane = 8;
+
+__global__ void __launch_bounds__(kTileStatWarps * 32) tile_rowstats_kernel(const SelArgs a, int nchunk) {
+  extern __shared__ uint32_t hsm[];  // [kTileStatWarps][kRowBins]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t rows = int64_t(a.B) * a.Wp;
+  const int64_t r = int64_t(blockIdx.x) * kTileStatWarps + warp;
+  if (r >= rows) return;  // whole warp; no block-wide barrier below
+  uint32_t* hist = hsm + warp * kRowBins;
+  const uint16_t* vs = a.vsum + r * kSumMax;
+  const float* ts = a.tsum + r * kSumMax;
+  float m = -INFINITY;
+  for (int c = lane; c < nchunk; c += 32) m = fmaxf(m, __uint_as_float(uint32_t(vs[c]) << 16));
+  m = warp_max(m);
+  const int K = (a.W + 31) / 32;  // chunk maxima per lane that 32 lanes need to hold >= W of them
+  float top[kTopPerLane];
+#pragma unroll
+  for (int i = 0; i < kTopPerLane; ++i) top[i] = -INFINITY;
+  float sum = 0.f;
+  for (int c = lane; c < nchunk; c += 32) {
+    const float x = __uint_as_float(uint32_t(vs[c]) << 16);
+    if (x > -INFINITY) sum = fmaf(ts[c], ex2_approx((x - m) * kLog2e), sum);
+    float v = x;  // insert into the lane's descending top list
+#pragma unroll
+    for (int i = 0; i < kTopPerLane; ++i) {
+      const float hi = fmaxf(top[i], v);
+      v = fminf(top[i], v);
+      top[i] = hi;
+    }
+  }
+  sum = warp_sum(sum);
+  float tau = -INFINITY;
+  if (K <= kTopPerLane) {
+    float k = top[0];
+#pragma unroll
+    for (int i = 1; i < kTopPerLane; ++i)
+      if (i == K - 1) k = top[i];
+    for (int o = 16; o > 0; o >>= 1) k = fminf(k, __shfl_xor_sync(0xffffffffu, k, o));
+    tau = k;
+  }
+  if (lane == 0) a.rowstat[r] = make_float2(m, logf(sum));
+  const float m32 = m * kBinsPerNat;
+  // tau's bin bounds every binned maximum's; -inf, NaN (an all -inf row) -> the last bin
+  const int pbin = int(fminf(fmaf(tau, -kBinsPerNat, m32), float(kRowBins - 1)));
+  const int len = min(pbin + 1, kRowBins - 1);
+  for (int j = lane; j <= pbin; j += 32) hist[j] = 0;
+  __syncwarp();
+  for (int c = lane; c < nchunk; c += 32) {
+    const float x = __uint_as_float(uint32_t(vs[c]) << 16);
+    if (x >= tau) atomicAdd(&hist[int(fminf(fmaf(x, -kBinsPerNat, m32), float(kRowBins - 1)))], 1u);
+  }
+  __syncwarp();
+  if (lane == 0) a.rowlen[r] = uint32_t(len);
+  for (int j = lane; j < len; j += 32) a.rowhist[r * kRowBins + j] = hist[j];
+}
+
 __global__ void __launch_bounds__(1024) threshold_kernel(const SelArgs a) {
   __shared__ uint32_t rh[kReqBins];
   __shared__ float red[33];
@@ -549,27 +608,6 @@ __global__ void __launch_bounds__(1024) finalize_kernel(const SelArgs a) {
   }
 }
 
-struct Workspace {
-  // The flag word sits at offset 0 whatever the widths: the steps of one search
-  // (whose previous widths differ) and the status query all find it there.
-  // `base` bytes are required; the chunk-maximum summary after them (up to `total`) is optional:
-  // without it collect reads whole rows
-  size_t rowstat, rowlen, rowhist, thresh, count, flags, cand, vsum, base, total;
-  Workspace(int64_t B, int64_t Wp) {
-    auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
-    const int64_t rows = B * Wp;
-    flags = 0;
-    rowstat = al(flags + sizeof(uint32_t));
-    rowlen = al(rowstat + rows * sizeof(float2));
-    rowhist = al(rowlen + rows * sizeof(uint32_t));
-    thresh = al(rowhist + rows * kRowBins * sizeof(uint32_t));
-    count = al(thresh + B * sizeof(float));
-    cand = al(count + B * sizeof(uint32_t));
-    vsum = base = al(cand + B * kCap * sizeof(unsigned long long));
-    total = al(vsum + rows * kSumMax * sizeof(uint16_t));
-  }
-};
-
 template <typename T>
 int launch_select(SelArgs& a, bool vec, cudaStream_t s) {
   const int64_t rows = int64_t(a.B) * a.Wp;
@@ -606,11 +644,42 @@ int launch_select(SelArgs& a, bool vec, cudaStream_t s) {
   return KADLLM_OK;
 }
 
+// The fused selection: the LM-head GEMM (kadllm_gemm_logits) already wrote every
+// row's chunk maxima and sums into the workspace; no pass over the logits.
+int launch_select_fused(SelArgs& a, cudaStream_t s) {
+  const int64_t rows = int64_t(a.B) * a.Wp;
+  const int nchunk = int((a.V + kChunk - 1) / kChunk);
+  const size_t hsmem = size_t(kTileStatWarps) * kRowBins * sizeof(uint32_t);
+  if (cudaFuncSetAttribute(tile_rowstats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(hsmem)) !=
+      cudaSuccess) {
+    set_error("beam select: cannot reserve %zu bytes of shared memory", hsmem);
+    return KADLLM_ECUDA;
+  }
+  tile_rowstats_kernel<<<unsigned((rows + kTileStatWarps - 1) / kTileStatWarps), kTileStatWarps * 32, hsmem, s>>>(
+      a, nchunk);
+  threshold_kernel<<<a.B, 1024, 0, s>>>(a);
+  collect_kernel<__nv_bfloat16><<<unsigned(rows), 256, 0, s>>>(a, true);
+  int N = 1;
+  while (N < max(kCap, a.W)) N <<= 1;
+  const size_t smem = size_t(N) * sizeof(unsigned long long);
+  if (cudaFuncSetAttribute(finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess) {
+    set_error("beam select: cannot reserve %zu bytes of shared memory", smem);
+    return KADLLM_ECUDA;
+  }
+  finalize_kernel<<<a.B, 1024, smem, s>>>(a);
+  KB_CHECK_LAUNCH("beam select launch");
+  return KADLLM_OK;
+}
+
 }  // namespace
 }  // namespace kb
 
+extern "C" int64_t kadllm_beam_select_workspace_fused(int64_t batch, int64_t prev_width) {
+  return int64_t(kb::sel::Workspace(batch, prev_width).fused);
+}
+
 extern "C" int64_t kadllm_beam_select_workspace(int64_t batch, int64_t prev_width) {
-  return int64_t(kb::Workspace(batch, prev_width).total);
+  return int64_t(kb::sel::Workspace(batch, prev_width).total);
 }
 
 namespace kb {
@@ -620,7 +689,8 @@ namespace {
 int select_with_workspace(const void* logits, int logits_dtype, int64_t ld_row, const float* parent_scores,
                           const void* mask, const int64_t* old_history, float* out_scores, int64_t* out_history,
                           int32_t* out_parent, void* workspace, int64_t workspace_bytes, uint32_t* flags, int64_t batch,
-                          int64_t prev_width, int64_t vocab, int64_t width, int64_t depth, void* stream) {
+                          int64_t prev_width, int64_t vocab, int64_t width, int64_t depth, void* stream,
+                          bool fused = false) {
   KB_REQUIRE(valid_dtype(logits_dtype), KADLLM_EDTYPE, "beam select: unsupported logits dtype");
   KB_REQUIRE(batch >= 1 && prev_width >= 1 && vocab >= 1 && width >= 1 && depth >= 0, KADLLM_EINVAL,
              "beam select: empty dimensions");
@@ -648,6 +718,13 @@ int select_with_workspace(const void* logits, int logits_dtype, int64_t ld_row, 
   a.flags = flags ? flags : reinterpret_cast<uint32_t*>(w + ws.flags);
   a.cand = reinterpret_cast<unsigned long long*>(w + ws.cand);
   a.vsum = workspace_bytes >= int64_t(ws.total) ? reinterpret_cast<uint16_t*>(w + ws.vsum) : nullptr;
+  if (fused) {
+    KB_REQUIRE(logits_dtype == KADLLM_BF16 && mask == nullptr && workspace_bytes >= int64_t(ws.fused) &&
+                   vocab <= int64_t(kSumMax) * kChunk,
+               KADLLM_EINVAL, "fused beam select: BF16 logits without a mask, a fused workspace, V <= %d",
+               kSumMax * kChunk);
+    a.tsum = reinterpret_cast<const float*>(w + ws.tsum);
+  }
   a.B = int(batch); a.Wp = int(prev_width); a.W = int(width); a.depth = int(depth); a.V = vocab;
   const int esz = dtype_size(logits_dtype);
   const int vw = 16 / esz;
@@ -657,6 +734,10 @@ int select_with_workspace(const void* logits, int logits_dtype, int64_t ld_row, 
     // the first step of a search (no history yet) starts the workspace's flag word afresh
     cudaError_t e = cudaMemsetAsync(a.flags, 0, sizeof(uint32_t), s);
     KB_REQUIRE(e == cudaSuccess, KADLLM_ECUDA, "beam select: %s", cudaGetErrorString(e));
+  }
+  if (fused) {
+    KB_REQUIRE(vec, KADLLM_EINVAL, "fused beam select: logits rows must be 16-byte aligned, V a multiple of 8");
+    return launch_select_fused(a, s);
   }
   if (logits_dtype == KADLLM_BF16) return launch_select<__nv_bfloat16>(a, vec, s);
   if (logits_dtype == KADLLM_F16) return launch_select<__half>(a, vec, s);
@@ -675,11 +756,21 @@ extern "C" int kadllm_beam_select(const void* logits, int logits_dtype, int64_t 
                                    vocab, width, depth, stream);
 }
 
+extern "C" int kadllm_beam_select_fused(const void* logits, int64_t ld_row, const float* parent_scores,
+                                        const int64_t* old_history, float* out_scores, int64_t* out_history,
+                                        int32_t* out_parent, void* workspace, int64_t workspace_bytes, int64_t batch,
+                                        int64_t prev_width, int64_t vocab, int64_t width, int64_t depth,
+                                        void* stream) {
+  return kb::select_with_workspace(logits, KADLLM_BF16, ld_row, parent_scores, nullptr, old_history, out_scores,
+                                   out_history, out_parent, workspace, workspace_bytes, nullptr, batch, prev_width,
+                                   vocab, width, depth, stream, true);
+}
+
 extern "C" int kadllm_beam_select_status(const void* workspace, int64_t batch, int64_t prev_width,
                                          uint32_t* flags_out, void* stream) {
   using namespace kb;
   KB_REQUIRE(workspace && flags_out, KADLLM_EINVAL, "beam select status: null pointer");
-  const Workspace ws(batch, prev_width);
+  const sel::Workspace ws(batch, prev_width);
   cudaError_t e = cudaMemcpyAsync(flags_out, static_cast<const char*>(workspace) + ws.flags, sizeof(uint32_t),
                                   cudaMemcpyDeviceToHost, static_cast<cudaStream_t>(stream));
   if (e == cudaSuccess) e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
@@ -745,7 +836,7 @@ extern "C" int kadllm_beam_select_noalloc(const void* logits, int logits_dtype, 
   using namespace kb;
   KB_REQUIRE(out_flags, KADLLM_EINVAL, "beam select (no-alloc): null flags pointer");
   KB_REQUIRE(batch >= 1 && prev_width >= 1, KADLLM_EINVAL, "beam select (no-alloc): empty dimensions");
-  const Workspace ws(batch, prev_width);
+  const sel::Workspace ws(batch, prev_width);
   KB_REQUIRE(ws.base <= kNoAllocScratchBytes && batch <= 32 && batch * prev_width <= 512, KADLLM_EINVAL,
              "beam select (no-alloc): batch %lld x prev_width %lld needs %zu bytes of scratch; the static "
              "maximum is %zu bytes (batch <= 32, batch * prev_width <= 512)",

@@ -36,6 +36,7 @@
 
 #include <mutex>
 
+#include "beam_select.cuh"
 #include "common.cuh"
 #include "tcgen05_pair.cuh"
 
@@ -55,7 +56,7 @@ constexpr long long kWait = 1ll << 31;
 constexpr uint32_t kBoxBytes = 32 * 128;                // epilogue staging box: 32 rows x 64 BF16
 constexpr size_t kSmemBytes = 1024 + size_t(kStages) * kStageBytes + 4 * 2 * kBoxBytes + 256;
 
-enum Epilogue { kStore = 0, kSiluMul = 1, kAddResid = 2 };
+enum Epilogue { kStore = 0, kSiluMul = 1, kAddResid = 2, kLogits = 3 };
 
 struct GemmArgs {
   __nv_bfloat16* c;
@@ -65,6 +66,8 @@ struct GemmArgs {
   int M, N, K, n_out;  // N: rows of B (columns of the product); n_out: columns of C
   int tiles_m, tiles_n;
   uint32_t* status;
+  uint16_t* vsum;  // kLogits: per (row, 256-column chunk) the BF16 maximum ...
+  float* tsum;     // ... and the sum of exp(x - that maximum), rows kSumMax apart
 };
 
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& tm, int& tn) {
@@ -221,6 +224,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     constexpr int kOutCols = EPI == kSiluMul ? kBN / 2 : kBN;  // output columns per tile
     int acc = 0, nbuf = 0;
     uint32_t acc_ph = 0, rph = 0;
+    constexpr float kLog2e = 1.4426950408889634f;
     for (int t = pair; t < total && ok; t += npairs) {
       int tm, tn;
       tile_coords(t, g.tiles_m, g.tiles_n, tm, tn);
@@ -231,6 +235,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tc::fence_after();
       const int row0 = tm * 256 + int(rank) * kBM + q * 32;
       const uint32_t tbase = tc::taddr(tmem, q * 32, acc * kBN);
+      float lm = -INFINITY, ls = 0.f;  // kLogits: this row's running chunk maximum and sum
 #pragma unroll 1
       for (int c = 0; c < kOutCols && ok; c += 64) {
         const int col = tn * kOutCols + c;
@@ -269,6 +274,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               w[16 * h + j] = bf2_pack(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
           }
         }
+        if (EPI == kLogits) {  // the BF16-rounded logits of this box into the row's chunk statistics
+          const bool full = col + 64 <= g.n_out;
+          float bm = -INFINITY;
+#pragma unroll
+          for (int k = 0; k < 32; ++k) {
+            const float2 f = bf2f(w[k]);
+            const float x0 = (full || col + 2 * k < g.n_out) ? f.x : -INFINITY;
+            const float x1 = (full || col + 2 * k + 1 < g.n_out) ? f.y : -INFINITY;
+            bm = fmaxf(bm, fmaxf(x0, x1));
+          }
+          if (bm > lm) {
+            ls = lm == -INFINITY ? 0.f : ls * fast_ex2((lm - bm) * kLog2e);
+            lm = bm;
+          }
+          if (lm > -INFINITY) {
+            const float nl = -lm * kLog2e;
+            float2 acc2 = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+              const float2 f = bf2f(w[k]);
+              const float x0 = (full || col + 2 * k < g.n_out) ? f.x : -INFINITY;
+              const float x1 = (full || col + 2 * k + 1 < g.n_out) ? f.y : -INFINITY;
+              acc2.x += fast_ex2(fmaf(x0, kLog2e, nl));
+              acc2.y += fast_ex2(fmaf(x1, kLog2e, nl));
+            }
+            ls += acc2.x + acc2.y;
+          }
+        }
         const uint32_t row_addr = smem_u32(buf) + uint32_t(lane) * 128u;
         if (EPI == kAddResid) {
           if (!tc::mbar_wait(rbar, rph, kWait)) ok = false;
@@ -297,6 +330,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           tc2::bulk_commit();
         }
         ++nbuf;
+      }
+      if (EPI == kLogits && row0 + lane < g.M && tn * kBN < g.n_out) {
+        const int64_t o = int64_t(row0 + lane) * sel::kSumMax + tn;
+        g.vsum[o] = uint16_t(__float_as_uint(lm) >> 16);  // a BF16 value (or -inf): exact
+        g.tsum[o] = ls;
       }
       tc::fence_before();
       __syncwarp();
@@ -436,4 +474,43 @@ extern "C" int kadllm_gemm(const void* a, int64_t lda, const void* b, int64_t ld
   if (epilogue == kSiluMul) return launch<kSiluMul>(ma, mb, mc, mr, g, s);
   if (epilogue == kAddResid) return launch<kAddResid>(ma, mb, mc, mr, g, s);
   return launch<kStore>(ma, mb, mc, mr, g, s);
+}
+
+extern "C" int kadllm_gemm_logits(const void* a, int64_t lda, const void* b, int64_t ldb, void* logits,
+                                  int64_t ld_logits, int64_t M, int64_t N, int64_t K, void* workspace,
+                                  int64_t workspace_bytes, int64_t batch, int64_t prev_width, uint32_t* status,
+                                  void* stream) {
+  using namespace kb;
+  KB_REQUIRE(a && b && logits && workspace && status, KADLLM_EINVAL, "gemm (logits): null pointer");
+  KB_REQUIRE(M >= 1 && N >= 1 && K >= 1 && batch >= 1 && prev_width >= 1 && M == batch * prev_width, KADLLM_EINVAL,
+             "gemm (logits): M must be batch * prev_width rows");
+  KB_REQUIRE(N <= int64_t(sel::kSumMax) * sel::kChunk && N % 8 == 0, KADLLM_EINVAL,
+             "gemm (logits): vocabulary must be a multiple of 8 and at most %d", sel::kSumMax * sel::kChunk);
+  KB_REQUIRE(M < (int64_t(1) << 30) && K < (int64_t(1) << 30), KADLLM_EINVAL, "gemm (logits): dimensions too large");
+  KB_REQUIRE(lda >= K && ldb >= K && lda % 8 == 0 && ldb % 8 == 0 && ld_logits >= N && ld_logits % 8 == 0,
+             KADLLM_EINVAL, "gemm (logits): leading dimensions must cover the rows and be multiples of 8 elements");
+  KB_REQUIRE(((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+               reinterpret_cast<uintptr_t>(logits)) & 15) == 0 && (reinterpret_cast<uintptr_t>(workspace) & 255) == 0,
+             KADLLM_EINVAL, "gemm (logits): operands 16-byte aligned, workspace 256-byte aligned");
+  const sel::Workspace ws(batch, prev_width);
+  KB_REQUIRE(workspace_bytes >= int64_t(ws.fused), KADLLM_EINVAL,
+             "gemm (logits): workspace smaller than kadllm_beam_select_workspace_fused");
+  CUtensorMap ma, mb, mc;
+  KB_REQUIRE(make_map(&ma, a, M, K, lda, kBM) && make_map(&mb, b, N, K, ldb, kBN / 2) &&
+                 make_map(&mc, logits, M, N, ld_logits, 32),
+             KADLLM_ECUDA, "gemm (logits): cannot encode the tensor maps (driver entry point cuTensorMapEncodeTiled)");
+  GemmArgs g{};
+  g.c = static_cast<__nv_bfloat16*>(logits);
+  g.ldc = ld_logits;
+  g.M = int(M);
+  g.N = int(N);
+  g.K = int(K);
+  g.n_out = int(N);
+  g.tiles_m = int((M + 255) / 256);
+  g.tiles_n = int((N + kBN - 1) / kBN);
+  g.status = status;
+  char* w = static_cast<char*>(workspace);
+  g.vsum = reinterpret_cast<uint16_t*>(w + ws.vsum);
+  g.tsum = reinterpret_cast<float*>(w + ws.tsum);
+  return launch<kLogits>(ma, mb, mc, mc, g, static_cast<cudaStream_t>(stream));
 }

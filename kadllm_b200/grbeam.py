@@ -60,8 +60,28 @@ class BeamSelector:
     def __init__(self, batch: int, max_prev_width: int, device: torch.device):
         self.batch = batch
         self.max_prev = max_prev_width
-        nbytes = int(_lib.lib().kadllm_beam_select_workspace(batch, max_prev_width))
+        # sized for the fused selection too: an LM head run through kadllm_gemm_logits writes
+        # its chunk statistics here and step_fused selects from them
+        nbytes = int(_lib.lib().kadllm_beam_select_workspace_fused(batch, max_prev_width))
         self.workspace = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+
+    def step_fused(self, logits: torch.Tensor, scores: torch.Tensor | None, history: torch.Tensor,
+                   width: int, parents: bool = False):
+        """Like :meth:`step` for BF16 logits [B, Wp, V] (contiguous) whose chunk statistics
+        the LM-head GEMM (``kadllm_gemm_logits``) wrote into this selector's workspace."""
+        B, Wp, V = logits.shape
+        if Wp > self.max_prev:
+            raise ValueError("selection workspace too small for this width")
+        depth = history.shape[2]
+        old = history.to(torch.int64).contiguous() if depth else None
+        parent = None if scores is None else scores.to(torch.float32).contiguous()
+        out_scores = torch.empty(B, width, dtype=torch.float32, device=logits.device)
+        out_hist = torch.empty(B, width, depth + 1, dtype=torch.int64, device=logits.device)
+        out_parent = torch.empty(B, width, dtype=torch.int32, device=logits.device) if parents else None
+        _lib.call("kadllm_beam_select_fused", logits.data_ptr(), V, _lib.ptr(parent), _lib.ptr(old),
+                  out_scores.data_ptr(), out_hist.data_ptr(), _lib.ptr(out_parent), self.workspace.data_ptr(),
+                  self.workspace.numel(), B, Wp, V, width, depth, _lib.stream(logits.device))
+        return (out_scores, out_hist, out_parent) if parents else (out_scores, out_hist)
 
     def step(self, logits: torch.Tensor, scores: torch.Tensor | None, history: torch.Tensor,
              width: int, mask: torch.Tensor | None = None, parents: bool = False):

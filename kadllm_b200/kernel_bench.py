@@ -121,12 +121,12 @@ def case_attn_tiled(gen, reps, B=1, W=256, T=3, L=4096, causal=False):
         if causal:
             _lib.call("kadllm_attention_tiled", q.data_ptr(), Hq * D, 0, D, kt.data_ptr(), vt.data_ptr(), nblk,
                       None, 0, 0, 0, None, 0, 0, 0, gate.data_ptr(), Hq * D, 0, D, out.data_ptr(), Hq * D, 0, D,
-                      status.data_ptr(), B, 1, 1, Hq, HK, L, D, D ** -0.5, 1, s)
+                      status.data_ptr(), B, 1, 1, 0, Hq, HK, L, D, D ** -0.5, 1, s)
         else:
             _lib.call("kadllm_attention_tiled", q.data_ptr(), T * Hq * D, Hq * D, D, kt.data_ptr(), vt.data_ptr(),
                       nblk, sk.data_ptr(), T * HK * D, HK * D, D, sv.data_ptr(), T * HK * D, HK * D, D,
                       gate.data_ptr(), T * Hq * D, Hq * D, D, out.data_ptr(), T * Hq * D, Hq * D, D,
-                      status.data_ptr(), B, W, T, Hq, HK, L, D, D ** -0.5, 0, s)
+                      status.data_ptr(), B, W, T, 0, Hq, HK, L, D, D ** -0.5, 0, s)
 
     ms = _time(run, reps)
     if int(status.item()):

@@ -167,6 +167,13 @@ class HybridModel:
         c = self.cfg
         return c.linear_key_head_dim == c.linear_value_head_dim and c.linear_key_head_dim in (64, 128)
 
+    def fused_select(self, batch: int, width: int) -> bool:
+        """Whether a decode step of batch x width rows can run the LM head with the
+        selection's chunk statistics in its epilogue (vocabulary a multiple of 8, at most
+        393216 columns)."""
+        V = self.lm_head.shape[0]
+        return V % 8 == 0 and V <= 393216 and batch * width >= 1
+
     def check(self) -> None:
         """Raise if a tensor-core kernel reported a timed-out wait (synchronises)."""
         st = int(self.status.item())
@@ -320,7 +327,7 @@ class HybridModel:
                     kt, vt, nblk = tile
                     _lib.call("kadllm_attention_tiled", q.data_ptr(), hq * D, 0, D, kt.data_ptr(), vt.data_ptr(),
                               nblk, None, 0, 0, 0, None, 0, 0, 0, gate.data_ptr(), P.stride(0), 0, 2 * D,
-                              out.data_ptr(), out.stride(0), 0, D, self.status.data_ptr(), B, 1, 1, hq, hk, L, D,
+                              out.data_ptr(), out.stride(0), 0, D, self.status.data_ptr(), B, 1, 1, 0, hq, hk, L, D,
                               D ** -0.5, 1, s)
                 else:
                     # cache [B, HK, L, D]: strides passed as (request, position, head)
@@ -431,7 +438,7 @@ class HybridModel:
                 gate = P[:, D:]
                 _lib.call("kadllm_attention_tiled_varlen", q.data_ptr(), hq * D, 0, D, kt.data_ptr(), vt.data_ptr(),
                           nblk, None, 0, 0, 0, None, 0, 0, 0, gate.data_ptr(), P.stride(0), 0, 2 * D,
-                          out.data_ptr(), out.stride(0), 0, D, self.status.data_ptr(), cu.data_ptr(), B, 1, 1, hq,
+                          out.data_ptr(), out.stride(0), 0, D, self.status.data_ptr(), cu.data_ptr(), B, 1, 1, 0, hq,
                           hk, Lmax, D, D ** -0.5, 1, s)
                 w_post = m.w_o
                 prefix.append((kp, vp))
@@ -506,11 +513,11 @@ class HybridModel:
         self._add_norm(x, None, self.final_norm, last, rows=BW, step=T, offset=T - 1)
         return last
 
-    def _attend(self, i, state, q, ks, vs, P, out, B, W, T, sg_row, sg_t):
+    def _attend(self, i, state, q, ks, vs, P, out, B, W, T, sg_row, sg_t, t0=0):
         """Decode attention of layer i: rows (beam, t) of q [B*W, T, Hq, D] against the
         request's prefix and the beam's suffix keys ks / vs [B*W, T, HK, D] (row-major
         views), the output gate from P (gate row stride sg_row per beam, sg_t per step),
-        into out [B*W, T, Hq*D]."""
+        into out [B*W, T, Hq*D]; only steps t >= t0 have queries and outputs."""
         c = self.cfg
         hk, D, hq = c.num_key_value_heads, c.head_dim, c.num_attention_heads
         s = self._stream()
@@ -523,14 +530,16 @@ class HybridModel:
             _lib.call("kadllm_attention_tiled_varlen", q.data_ptr(), T * hq * D, hq * D, D, kt.data_ptr(),
                       vt.data_ptr(), nblk, ks.data_ptr(), *suffix_strides, vs.data_ptr(), *suffix_strides,
                       gate.data_ptr(), sg_row, sg_t, 2 * D, out.data_ptr(), T * hq * D, hq * D, D,
-                      self.status.data_ptr(), state.cu.data_ptr(), B, W, T, hq, hk, state.length, D, D ** -0.5, 0, s)
+                      self.status.data_ptr(), state.cu.data_ptr(), B, W, T, t0, hq, hk, state.length, D, D ** -0.5, 0, s)
         elif tile is not None:
             kt, vt, nblk = tile
             _lib.call("kadllm_attention_tiled", q.data_ptr(), T * hq * D, hq * D, D, kt.data_ptr(),
                       vt.data_ptr(), nblk, ks.data_ptr(), *suffix_strides, vs.data_ptr(), *suffix_strides,
                       gate.data_ptr(), sg_row, sg_t, 2 * D, out.data_ptr(), T * hq * D, hq * D, D,
-                      self.status.data_ptr(), B, W, T, hq, hk, state.length, D, D ** -0.5, 0, s)
+                      self.status.data_ptr(), B, W, T, t0, hq, hk, state.length, D, D ** -0.5, 0, s)
         else:
+            if t0:
+                raise NotImplementedError("query steps after the first need the tiled (head dim 256) attention")
             _lib.call("kadllm_prefix_attention", q.data_ptr(), T * hq * D, hq * D, D, pk.data_ptr(),
                       *pk.stride()[:3], pv.data_ptr(), *pv.stride()[:3], ks.data_ptr(), *suffix_strides,
                       vs.data_ptr(), *suffix_strides, None, gate.data_ptr(), sg_row, sg_t, 2 * D, out.data_ptr(),
@@ -582,8 +591,10 @@ class HybridModel:
                     self._qk_rope(P, R, state.length + 1, 1, q[:, 1], ks[:, 1], kv_strides, vs[:, 1], kv_strides,
                                   m, q_row_stride=2 * hq * D)
                 out = torch.empty(R, 2, hq * D, dtype=BF16, device=self.device)
-                # the first token's query rows are recomputed alongside (their outputs unused)
-                self._attend(i, state, q, ks, vs, P, out, B, W, 2, P.stride(0), 0)
+                if state.tiles and state.tiles[i] is not None:  # queries of the new token only
+                    self._attend(i, state, q, ks, vs, P, out, B, W, 2, P.stride(0), 0, t0=1)
+                else:  # the first token's query rows are recomputed alongside (outputs unused)
+                    self._attend(i, state, q, ks, vs, P, out, B, W, 2, P.stride(0), 0)
                 self._gemm(out[:, 1], m.w_o, resid=x)
             self._add_norm(x, None, layer.post_ln, normed)
             self._mlp(layer, normed, x)
@@ -595,10 +606,20 @@ class HybridModel:
 
     @torch.no_grad()
     def decode(self, history: torch.Tensor, state: HybridPrefix, head: torch.Tensor | None = None,
-               cache: dict | None = None, reuse: tuple | None = None) -> torch.Tensor:
+               cache: dict | None = None, reuse: tuple | None = None,
+               select_workspace: torch.Tensor | None = None) -> torch.Tensor:
         """Replay [B, W, T] suffix tokens; return [B, W, V] logits (BF16) over the LM
         head's rows, or over ``head``'s rows when given (``cache`` / ``reuse``: see
-        :meth:`decode_hidden`)."""
+        :meth:`decode_hidden`).  With ``select_workspace`` (a selector's workspace) the
+        LM head also writes each row's chunk statistics there for the fused selection."""
         B, W, _ = history.shape
         w = self.lm_head if head is None else head
-        return self._gemm(self.decode_hidden(history, state, cache=cache, reuse=reuse), w).view(B, W, -1)
+        hidden = self.decode_hidden(history, state, cache=cache, reuse=reuse)
+        if select_workspace is None:
+            return self._gemm(hidden, w).view(B, W, -1)
+        V = w.shape[0]
+        logits = torch.empty(B * W, V, dtype=BF16, device=self.device)
+        _lib.call("kadllm_gemm_logits", hidden.data_ptr(), hidden.stride(0), w.data_ptr(), w.stride(0),
+                  logits.data_ptr(), V, B * W, V, hidden.shape[1], select_workspace.data_ptr(),
+                  select_workspace.numel(), B, W, self.status.data_ptr(), self._stream())
+        return logits.view(B, W, V)

@@ -29,10 +29,11 @@ def work_of(name: str, args: tuple) -> tuple[str, float] | None:
         write = rows * HV * DV * 2 + B * HV * DK * DV * 2 + B * conv_dim * 4 * 2
         return "hbm", float(read + write)
     if name == "kadllm_attention_tiled":
-        B, W, T, H, HK, L, D = args[24:31]
-        if args[32]:  # causal prefill
+        B, W, T, t0, H, HK, L, D = args[24:32]
+        if args[33]:  # causal prefill
             return "tensor", float(4 * B * H * D * L * (L + 1) / 2)
-        return "tensor", float(4 * B * W * T * H * D * L + 4 * B * W * H * D * T * (T + 1) / 2)
+        # query rows of steps t0 .. T-1, each against the prefix and its suffix keys s <= t
+        return "tensor", float(sum(4 * B * W * H * D * (L + t + 1) for t in range(t0, T)))
     if name == "kadllm_causal_attention":
         B, L, H, HK, D = args[17:22]
         return "tensor", float(4 * B * H * D * L * (L + 1) / 2)
@@ -47,6 +48,14 @@ def work_of(name: str, args: tuple) -> tuple[str, float] | None:
         R = B * W * T
         conv_dim = 2 * H * DK + HV * DV
         read = R * (conv_dim + HV * DV + 2 * HV) * 2 + B * HV * DK * DV * 2 + B * conv_dim * 4 * 2
+        return "hbm", float(read + R * HV * DV * 2)
+    if name == "kadllm_gdn_mixer_continue":
+        # the new rows and their parents' previous-step rows (q | k | v | z | b | a columns),
+        # the request's state and conv taps, the new rows' output
+        B, W, H, HV, DK, DV = args[14:20]
+        R = B * W
+        conv_dim = 2 * H * DK + HV * DV
+        read = 2 * R * (conv_dim + HV * DV + 2 * HV) * 2 + B * HV * DK * DV * 2 + B * conv_dim * 4 * 2
         return "hbm", float(read + R * HV * DV * 2)
     if name == "kadllm_beam_select":
         B, Wp, V, W, depth = args[11:16]
@@ -70,10 +79,10 @@ def measured_traffic(name: str, args: tuple) -> float | None:
         return 2064.8e6
     if name == "kadllm_gdn_mixer_replay" and tuple(args[11:13]) == (32, 256) and tuple(args[14:18]) == (16, 16, 128, 128):
         return {1: 186.4e6, 2: 359.3e6}.get(args[13])  # T = 1: 165.5 + 20.9 MB; T = 2: 306.2 + 53.2 MB
-    if name == "kadllm_attention_tiled" and (args[24], *args[27:31]) == (32, 8, 2, 1024, 256):
-        if args[32]:  # causal prefill: 335.6 + 109.8 MB
+    if name == "kadllm_attention_tiled" and (args[24], *args[28:32]) == (32, 8, 2, 1024, 256):
+        if args[33]:  # causal prefill: 335.6 + 109.8 MB
             return 445.4e6
-        return 285.4e6 if tuple(args[25:27]) == (256, 2) else None  # decode T = 2: 235.0 + 50.4 MB
+        return 285.4e6 if tuple(args[25:28]) == (256, 2, 0) else None  # decode T = 2: 235.0 + 50.4 MB
     if name == "kadllm_beam_select" and tuple(args[11:14]) == (32, 256, 248320):
         return 4100.4e6  # rowstats 4068.7 + 21.2 MB, collect 8.7 MB, threshold 1.3 MB, finalize 0.2 MB
     return None

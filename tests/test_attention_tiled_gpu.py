@@ -2,6 +2,7 @@
 plain PyTorch fp32 restatement of the same op (src/kadllm/ops.py:252-341 for
 decode; causal SDPA for prefill), with the fused output gate."""
 
+import numpy as np
 import pytest
 import torch
 
@@ -26,8 +27,11 @@ def _gate(o, g):  # bf16(bf16(o) * bf16(sigmoid(g)))
     return (o.to(bf).float() * torch.sigmoid(g.float()).to(bf).float()).to(bf)
 
 
-@pytest.mark.parametrize("B,W,T,L,trend", [(2, 5, 2, 100, 0.0), (1, 40, 1, 64, 0.0), (1, 7, 3, 1100, 3.0)])
-def test_decode_matches_torch(B, W, T, L, trend):
+@pytest.mark.parametrize("B,W,T,L,trend,t0", [(2, 5, 2, 100, 0.0, 0), (1, 40, 1, 64, 0.0, 0), (1, 7, 3, 1100, 3.0, 0),
+                                               (2, 5, 2, 100, 0.0, 1), (1, 7, 3, 1100, 3.0, 2)])
+def test_decode_matches_torch(B, W, T, L, trend, t0):
+    """Decode rows (beam, t) against prefix + suffix keys s <= t; with first_step t0 > 0
+    only the steps t >= t0 have query rows (earlier suffix tokens stay keys)."""
     hq, hk = 8, 2
     G = hq // hk
     gen = torch.Generator(device="cuda").manual_seed(L + W)
@@ -40,14 +44,14 @@ def test_decode_matches_torch(B, W, T, L, trend):
     vc = n(B, hk, L, D).to(bf)
     ks, vs = n(B * W, T, hk, D).to(bf), n(B * W, T, hk, D).to(bf)
     gate = n(B * W, T, hq, D).to(bf)
-    out = torch.empty(B * W, T, hq, D, dtype=bf, device="cuda")
+    out = torch.zeros(B * W, T, hq, D, dtype=bf, device="cuda")
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     kt, nblk = _tiles(kc)
     vt, _ = _tiles(vc)
     _lib.call("kadllm_attention_tiled", q.data_ptr(), T * hq * D, hq * D, D, kt.data_ptr(), vt.data_ptr(), nblk,
               ks.data_ptr(), T * hk * D, hk * D, D, vs.data_ptr(), T * hk * D, hk * D, D, gate.data_ptr(),
-              T * hq * D, hq * D, D, out.data_ptr(), T * hq * D, hq * D, D, status.data_ptr(), B, W, T, hq, hk, L, D,
-              D ** -0.5, 0, _lib.stream(q.device))
+              T * hq * D, hq * D, D, out.data_ptr(), T * hq * D, hq * D, D, status.data_ptr(), B, W, T, t0, hq, hk, L,
+              D, D ** -0.5, 0, _lib.stream(q.device))
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     # reference: per beam row, prefix keys then suffix keys s <= t
@@ -63,7 +67,9 @@ def test_decode_matches_torch(B, W, T, L, trend):
                     p = torch.softmax(keys @ q[r, t, h].float() * D ** -0.5, 0)
                     ref[r, t, h] = p @ vals
     want = _gate(ref, gate)
-    assert_close_rel(out.float().cpu().numpy(), want.float().cpu().numpy(), rel=1e-2, what="tiled decode attention")
+    assert_close_rel(out[:, t0:].float().cpu().numpy(), want[:, t0:].float().cpu().numpy(), rel=1e-2,
+                     what="tiled decode attention")
+    assert int(out[:, :t0].abs().sum()) == 0  # no rows for the steps before t0
 
 
 @pytest.mark.parametrize("B,L", [(2, 130), (1, 64)])
@@ -81,7 +87,7 @@ def test_causal_matches_torch(B, L):
     vt, _ = _tiles(vc)
     _lib.call("kadllm_attention_tiled", q.data_ptr(), hq * D, 0, D, kt.data_ptr(), vt.data_ptr(), nblk, None, 0, 0, 0,
               None, 0, 0, 0, gate.data_ptr(), hq * D, 0, D, out.data_ptr(), hq * D, 0, D, status.data_ptr(), B, 1, 1,
-              hq, hk, L, D, D ** -0.5, 1, _lib.stream(q.device))
+              0, hq, hk, L, D, D ** -0.5, 1, _lib.stream(q.device))
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     qh = q.float().view(B, L, hq, D).permute(0, 2, 1, 3)
@@ -92,3 +98,72 @@ def test_causal_matches_torch(B, L):
     ref = (torch.softmax(s, -1) @ vh).permute(0, 2, 1, 3).reshape(B * L, hq, D)
     want = _gate(ref, gate)
     assert_close_rel(out.float().cpu().numpy(), want.float().cpu().numpy(), rel=1e-2, what="tiled causal attention")
+
+
+def test_decode_at_the_benchmark_shape_sampled():
+    """The timed decode launch: 32 requests x 256 beams, T = 2, prefix 1024 (1024
+    CTAs of 128 query rows, every K/V buffer phase reused over 16 key blocks), plus the
+    continuation form (first_step 1: queries of the newest token only), checked
+    against fp32 torch on sampled (request, beam, head) rows."""
+    B, W, T, L, hq, hk = 32, 256, 2, 1024, 8, 2
+    G = hq // hk
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    n = lambda *s: torch.randn(*s, device="cuda", generator=gen)
+    q = n(B * W, T, hq, D).to(bf)
+    kc, vc = n(B, hk, L, D).to(bf), n(B, hk, L, D).to(bf)
+    ks, vs = n(B * W, T, hk, D).to(bf), n(B * W, T, hk, D).to(bf)
+    gate = n(B * W, T, hq, D).to(bf)
+    kt, nblk = _tiles(kc)
+    vt, _ = _tiles(vc)
+    rng = np.random.default_rng(0)
+    for t0 in (0, 1):
+        out = torch.zeros(B * W, T, hq, D, dtype=bf, device="cuda")
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        _lib.call("kadllm_attention_tiled", q.data_ptr(), T * hq * D, hq * D, D, kt.data_ptr(), vt.data_ptr(),
+                  nblk, ks.data_ptr(), T * hk * D, hk * D, D, vs.data_ptr(), T * hk * D, hk * D, D, gate.data_ptr(),
+                  T * hq * D, hq * D, D, out.data_ptr(), T * hq * D, hq * D, D, status.data_ptr(), B, W, T, t0, hq,
+                  hk, L, D, D ** -0.5, 0, _lib.stream(q.device))
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        got, want = [], []
+        for _ in range(48):
+            b, w, h = int(rng.integers(B)), int(rng.integers(W)), int(rng.integers(hq))
+            t = int(rng.integers(t0, T))
+            r, kv = b * W + w, h // G
+            keys = torch.cat([kc[b, kv].float(), ks[r, :t + 1, kv].float()])
+            vals = torch.cat([vc[b, kv].float(), vs[r, :t + 1, kv].float()])
+            p = torch.softmax(keys @ q[r, t, h].float() * D ** -0.5, 0)
+            want.append(_gate((p @ vals)[None], gate[r, t, h][None])[0].float())
+            got.append(out[r, t, h].float())
+        assert_close_rel(torch.stack(got).cpu().numpy(), torch.stack(want).cpu().numpy(), rel=1e-2,
+                         what=f"decode attention at the benchmark shape (first_step {t0})")
+
+
+def test_causal_at_the_benchmark_shape_sampled():
+    """The timed prefill launch: 32 requests x 1024 tokens (causal), sampled rows."""
+    B, L, hq, hk = 32, 1024, 8, 2
+    G = hq // hk
+    gen = torch.Generator(device="cuda").manual_seed(12)
+    n = lambda *s: torch.randn(*s, device="cuda", generator=gen)
+    q = n(B * L, hq, D).to(bf)
+    kc, vc = n(B, hk, L, D).to(bf), n(B, hk, L, D).to(bf)
+    gate = n(B * L, hq, D).to(bf)
+    out = torch.empty(B * L, hq, D, dtype=bf, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    kt, nblk = _tiles(kc)
+    vt, _ = _tiles(vc)
+    _lib.call("kadllm_attention_tiled", q.data_ptr(), hq * D, 0, D, kt.data_ptr(), vt.data_ptr(), nblk, None, 0, 0, 0,
+              None, 0, 0, 0, gate.data_ptr(), hq * D, 0, D, out.data_ptr(), hq * D, 0, D, status.data_ptr(), B, 1, 1,
+              0, hq, hk, L, D, D ** -0.5, 1, _lib.stream(q.device))
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    rng = np.random.default_rng(1)
+    got, want = [], []
+    for _ in range(64):
+        b, pos, h = int(rng.integers(B)), int(rng.integers(L)), int(rng.integers(hq))
+        kv = h // G
+        p = torch.softmax(kc[b, kv, :pos + 1].float() @ q[b * L + pos, h].float() * D ** -0.5, 0)
+        want.append(_gate((p @ vc[b, kv, :pos + 1].float())[None], gate[b * L + pos, h][None])[0].float())
+        got.append(out[b * L + pos, h].float())
+    assert_close_rel(torch.stack(got).cpu().numpy(), torch.stack(want).cpu().numpy(), rel=1e-2,
+                     what="causal attention at the benchmark shape")
