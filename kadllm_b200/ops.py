@@ -36,10 +36,11 @@ def _same_device(tensors):
 
 
 def _backend(name: str, accepted=_ACCEL) -> None:
-    if name == "torch":
-        raise ValueError("kadllm_b200 has no torch path; use backend='auto' or 'cuda'")
-    if name not in accepted:
-        raise ValueError(f"backend must be one of {accepted}")
+    """The reference's backend switch (``src/kadllm/ops.py:41-52``): "torch" selects its
+    eager implementation there; here every accepted name runs the same CUDA kernels (the
+    only implementation, no CPU path)."""
+    if name != "torch" and name not in accepted:
+        raise ValueError(f"backend must be one of {('torch',) + tuple(accepted)}")
 
 
 def _gdn_launch(config):
@@ -245,6 +246,9 @@ def prefix_attention(
     )
     mask = None if prefix_mask is None else prefix_mask.contiguous().view(torch.uint8)
     out = torch.empty((BW, T, H, D), dtype=q.dtype, device=q.device)
+    if D == _TILED_D and mask is None and L >= 1 and T <= 8:
+        return _prefix_attention_tiled(q, prefix_k, prefix_v, suffix_k.contiguous(), suffix_v.contiguous(), out,
+                                       B, beam_width, T, H, HK, L, D, scale)
     _lib.call(
         "kadllm_prefix_attention",
         q.data_ptr(), *q.stride()[:3], prefix_k.data_ptr(), *prefix_k.stride()[:3],
@@ -253,4 +257,32 @@ def prefix_attention(
         out.data_ptr(), *out.stride()[:3], _lib.dtype_code(q), B, beam_width, T, H, HK, L, D,
         scale, _lib.stream(q.device),
     )
+    return out
+
+
+_TILED_D = 256  # head dim of the tensor-core attention
+_status: dict = {}
+
+
+def _prefix_attention_tiled(q, prefix_k, prefix_v, suffix_k, suffix_v, out, B, W, T, H, HK, L, D, scale):
+    """Head dim 256 without a mask: the tcgen05 attention over a tiled copy of the prefix
+    (one re-layout of K / V per call), split over the key blocks when the request count
+    leaves SMs idle."""
+    lib = _lib.lib()
+    dev = q.device
+    s = _lib.stream(dev)
+    nbytes = lib.kadllm_kv_tile_bytes(B, HK, L, D)
+    kt = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    vt = torch.empty_like(kt)
+    _lib.call("kadllm_kv_tile", prefix_k.data_ptr(), *prefix_k.stride()[:3], B, HK, L, D, kt.data_ptr(), nbytes, s)
+    _lib.call("kadllm_kv_tile", prefix_v.data_ptr(), *prefix_v.stride()[:3], B, HK, L, D, vt.data_ptr(), nbytes, s)
+    status = _status.get(dev)
+    if status is None:
+        status = _status[dev] = torch.zeros(1, dtype=torch.int32, device=dev)
+    _lib.call("kadllm_attention_tiled", q.data_ptr(), *q.stride()[:3], kt.data_ptr(), vt.data_ptr(), -(-L // 64),
+              suffix_k.data_ptr(), *suffix_k.stride()[:3], suffix_v.data_ptr(), *suffix_v.stride()[:3], None, 0, 0, 0,
+              out.data_ptr(), *out.stride()[:3], status.data_ptr(), B, W, T, 0, H, HK, L, D, scale, 0, s)
+    if not torch.cuda.is_current_stream_capturing() and int(status.item()):
+        status.zero_()
+        raise RuntimeError("prefix_attention: a tensor-core pipeline wait timed out")
     return out

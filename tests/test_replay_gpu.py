@@ -116,6 +116,33 @@ def test_causal_conv1d_strided_input_and_variants():
     assert torch.equal(state, before)
 
 
+@pytest.mark.parametrize("B,W,C,T", [(2, 1, 2048, 1024), (2, 3, 136, 100), (1, 2, 64, 16)])
+def test_causal_conv1d_long_bf16_channel_contiguous(B, W, C, T):
+    """The vectorised sliding window for long BF16 suffixes in the reference's layout
+    (x = proj.transpose(1, 2), channels contiguous): the kernel microbenchmark's shape
+    (2048 channels x 1024 steps), ragged channel / step tiles, T not a multiple of 8."""
+    from kadllm_b200 import ops
+
+    rng = np.random.default_rng(C + T)
+    bf = torch.bfloat16
+    proj = O.bf16(rng.standard_normal((B * W, T, C)).astype(np.float32))
+    x = _t(proj, bf).transpose(1, 2)
+    state = _t(O.bf16(rng.standard_normal((B, C, 4)).astype(np.float32)), bf)
+    w = _t(O.bf16(0.5 * rng.standard_normal((C, 4)).astype(np.float32)), bf)
+    bias = _t(O.bf16(rng.standard_normal(C).astype(np.float32)), bf)
+    for b_, act in ((None, "silu"), (bias, None)):
+        out = ops.causal_conv1d(x, state, w, beam_width=W, bias=b_, activation=act)
+        xf, sf, wf = (t.float().cpu().numpy() for t in (x, state, w))
+        ref = O.causal_conv1d(xf, sf, wf, beam_width=W, activation=None)
+        if b_ is not None:
+            ref = ref + b_.float().cpu().numpy()[None, :, None]
+        if act == "silu":
+            ref = ref / (1 + np.exp(-ref))
+        ref = O.bf16(ref.astype(np.float32))  # one rounding of the fp32 result
+        got = out.float().cpu().numpy()
+        np.testing.assert_allclose(got, ref, rtol=2 ** -7, atol=1e-3)
+
+
 def test_operator_errors_match_reference_conventions():
     from kadllm_b200 import ops
 
