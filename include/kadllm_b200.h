@@ -315,6 +315,26 @@ KADLLM_API int kadllm_attention_tiled_varlen(
     int64_t q_heads, int64_t kv_heads, int64_t max_prefix_len, int64_t head_dim, float scale, int causal,
     void* stream);
 
+/* Decode attention split over the prefix's key blocks, for launches with fewer
+ * CTAs than SMs (a few requests, long prefixes: the kernel microbenchmark's one
+ * request x 256 beams against 4096 keys): `splits` CTAs per row tile each take a
+ * run of key blocks and write their unnormalised output and (maximum, sum) to
+ * `workspace` (>= kadllm_attention_split_workspace(...) bytes, 16-byte
+ * aligned); a combine kernel merges the runs, the beam's suffix keys and the
+ * output gate.  Arguments as kadllm_attention_tiled (decode, causal = 0). */
+KADLLM_API int64_t kadllm_attention_split_workspace(int64_t batch, int64_t beam_width, int64_t steps,
+                                                    int64_t first_step, int64_t q_heads, int64_t splits);
+KADLLM_API int kadllm_attention_tiled_split(const void* q, int64_t sq_row, int64_t sq_t, int64_t sq_h,
+                                            const void* k_tiles, const void* v_tiles, int64_t blocks_per_head,
+                                            const void* suffix_k, int64_t ssk_row, int64_t ssk_t, int64_t ssk_h,
+                                            const void* suffix_v, int64_t ssv_row, int64_t ssv_t, int64_t ssv_h,
+                                            const void* gate, int64_t sg_row, int64_t sg_t, int64_t sg_h, void* out,
+                                            int64_t so_row, int64_t so_t, int64_t so_h, uint32_t* status,
+                                            int64_t batch, int64_t beam_width, int64_t steps, int64_t first_step,
+                                            int64_t q_heads, int64_t kv_heads, int64_t prefix_len, int64_t head_dim,
+                                            float scale, int64_t splits, void* workspace, int64_t workspace_bytes,
+                                            void* stream);
+
 /* Prompt causal GQA attention (flash loop on the tensor cores) with the fused
  * output gate out = bf16(o) * bf16(sigmoid(gate)) (gate may be NULL).
  * q [B*L rows, H, D] (sq_row, sq_h); k / v [B, HK, L, D] via (s?_b, s?_l, s?_h);

@@ -32,6 +32,8 @@ SIGNATURES: dict[str, list] = {
                                L, L, L, L, L, L, L, L, F, I, P],
     "kadllm_attention_tiled_varlen": [P, L, L, L, P, P, L, P, L, L, L, P, L, L, L, P, L, L, L, P, L, L, L, P,
                                       P, L, L, L, L, L, L, L, L, F, I, P],
+    "kadllm_attention_tiled_split": [P, L, L, L, P, P, L, P, L, L, L, P, L, L, L, P, L, L, L, P, L, L, L, P,
+                                     L, L, L, L, L, L, L, L, F, L, P, L, P],
     "kadllm_causal_attention": [P, L, L, P, L, L, L, P, L, L, L, P, L, L, P, L, L, L, L, L, L, L, F, P],
     "kadllm_beam_select": [P, I, L, P, P, P, P, P, P, P, L, L, L, L, L, L, P],
     "kadllm_beam_select_status": [P, L, L, P, P],
@@ -69,6 +71,8 @@ def lib() -> ctypes.CDLL:
         handle.kadllm_beam_select_workspace_fused.argtypes = [L, L]
         handle.kadllm_gdn_prefill_workspace.restype = ctypes.c_int64
         handle.kadllm_gdn_prefill_workspace.argtypes = [L, L, L, L, L]
+        handle.kadllm_attention_split_workspace.restype = ctypes.c_int64
+        handle.kadllm_attention_split_workspace.argtypes = [L, L, L, L, L, L]
         handle.kadllm_kv_tile_bytes.restype = ctypes.c_int64
         handle.kadllm_kv_tile_bytes.argtypes = [L, L, L, L]
         for name, args in SIGNATURES.items():
@@ -84,7 +88,7 @@ _ERRORS = {1: ValueError, 2: TypeError, 3: NotImplementedError, 4: RuntimeError}
 
 # kernels launched per successful call of each entry point (for launch accounting)
 LAUNCHES_PER_CALL = {"kadllm_beam_select": 4, "kadllm_beam_select_noalloc": 4, "kadllm_beam_select_status": 0,
-                     "kadllm_beam_select_fused": 4,
+                     "kadllm_beam_select_fused": 4, "kadllm_attention_tiled_split": 2,
                      "kadllm_gdn_prefill_split": 3, "kadllm_gdn_prefill_split_varlen": 3}
 launch_count = 0
 _count_lock = threading.Lock()

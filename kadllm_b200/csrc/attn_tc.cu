@@ -61,6 +61,12 @@ struct AttnTcArgs {
   const int* cu;  // varlen prompts: request b's tokens are rows [cu[b], cu[b+1]) (null: b*L .. +L)
   int B, W, T, H, HK, G, L;  // L: the (longest) prefix length
   int t0;                    // decode: first suffix step with query rows (rows for steps t0 .. T-1)
+  // decode split over the key blocks (nsplit > 1): CTA z takes blocks [z * bps, (z + 1) * bps) and
+  // writes its unnormalised O and (reference maximum, sum) per row; a combine kernel merges the
+  // splits with the suffix keys and applies the gate
+  int nsplit, bps;
+  float* part_o;    // [nsplit][B * HK * R][kD]
+  float2* part_ml;  // [nsplit][B * HK * R]
   float scale_log2;
 };
 
@@ -134,7 +140,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
                               : (int64_t(b) * a.W + beam) * a.sq_row + int64_t(t) * a.sq_t + int64_t(hq) * a.sq_h;
   int nkeys = Lb;
   if (CAUSAL) nkeys = min(Lb, min(R - 1, row0 + kRows - 1) / a.G + 1);
-  const int nb = (nkeys + kBlk - 1) / kBlk;
+  const bool split = !CAUSAL && a.nsplit > 1;
+  const int jb = split ? int(blockIdx.z) * a.bps : 0;  // this CTA's first key block
+  const int nb = split ? max(0, min(a.bps, (nkeys + kBlk - 1) / kBlk - jb)) : (nkeys + kBlk - 1) / kBlk;
   const unsigned char* ktile = a.kt + int64_t(b * a.HK + hk) * a.nblk * kTile;
   const unsigned char* vtile = a.vt + int64_t(b * a.HK + hk) * a.nblk * kTile;
   const uint32_t sbase = smem_u32(smem);
@@ -161,13 +169,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
   auto load_k = [&](int j) {
     const int s = j & 1;
     tc::mbar_expect_tx(ldK + s, uint32_t(kTile));
-    tc::bulk_g2s(smem + M::k + s * kTile, ktile + int64_t(j) * kTile, uint32_t(kTile), ldK + s);
+    tc::bulk_g2s(smem + M::k + s * kTile, ktile + int64_t(jb + j) * kTile, uint32_t(kTile), ldK + s);
     ++issued_k[s];
   };
   auto load_v = [&](int j) {
     const int s = j & 1;
     tc::mbar_expect_tx(ldV + s, uint32_t(kTile));
-    tc::bulk_g2s(smem + M::v + s * kTile, vtile + int64_t(j) * kTile, uint32_t(kTile), ldV + s);
+    tc::bulk_g2s(smem + M::v + s * kTile, vtile + int64_t(jb + j) * kTile, uint32_t(kTile), ldV + s);
     ++issued_v[s];
   };
   auto issue_s = [&](int j) {  // S[j & 1] = Q K_j^T
@@ -261,8 +269,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
       ok = tc::mbar_wait(barS + sb, uint32_t(j >> 1) & 1u, kWait) && ok;
       tc::fence_after();
       if (j == nb - 1) {  // every S MMA has completed: the K buffers are free
-        stage_gate();
-        if (nb == 1) stage_suffix();
+        if (!split) {
+          stage_gate();
+          if (nb == 1) stage_suffix();
+        }
         cp_async_commit();
       }
       uint32_t r[32];
@@ -270,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
       tc::wait_ld();
 #pragma unroll
       for (int c = 0; c < 32; ++c) x[c] = __uint_as_float(r[c]);
-      const int k0 = j * kBlk + half * 32;
+      const int k0 = (jb + j) * kBlk + half * 32;
       if (k0 + 31 > key_lim) {  // partial block: keys past this row's limit drop out
 #pragma unroll
         for (int c = 0; c < 32; ++c)
@@ -307,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
         ok = tc::mbar_wait(barO, uint32_t(j - 1) & 1u, kWait) && ok;
         tc::fence_after();
         if (j == nb - 1) {  // O(nb-2) has completed: its V buffer is free
-          stage_suffix();
+          if (!split) stage_suffix();
           cp_async_commit();
         }
         if (resc) {  // this half's 128 output columns
@@ -351,116 +361,135 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnTcArgs a
   cp_async_wait<0>();                       // this thread's staged gate / suffix rows
   __syncthreads();
   if (rowthr) l = sbm[row] + sbm[kRows + row];
-  const int64_t brow = int64_t(b) * a.W + beam;
-  auto suf = [&](int sidx, int kv) -> const __nv_bfloat16* {  // this row's suffix key / value s
-    if (suf_smem)
-      return reinterpret_cast<const __nv_bfloat16*>(ssuf + (((beam - beam_lo) * a.T + sidx) * 2 + kv) * 512);
-    return kv ? a.sv + brow * a.ssv_row + int64_t(sidx) * a.ssv_t + int64_t(hk) * a.ssv_h
-              : a.sk + brow * a.ssk_row + int64_t(sidx) * a.ssk_t + int64_t(hk) * a.ssk_h;
-  };
-  float mx = m_ref, alpha = 1.f, ssum = l;
-  float psuf[kSufMax];
-#pragma unroll
-  for (int sidx = 0; sidx < kSufMax; ++sidx) psuf[sidx] = 0.f;
-  const bool lead = rowthr && half == 0;  // computes the row's scalars
-  if (lead && !CAUSAL && rvalid) {
-    float xs[kSufMax];
-#pragma unroll
-    for (int sidx = 0; sidx < kSufMax; ++sidx) {
-      xs[sidx] = -INFINITY;
-      if (sidx < a.T && sidx <= t) {  // scores against the beam's own keys s <= t
-        const __nv_bfloat16* kp = suf(sidx, 0);
-        float acc4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 8
-        for (int c = 0; c < kD / 8; ++c) {
-          const uint4 qv = *reinterpret_cast<const uint4*>(smem + M::q + M::off(row, c, kD / 8));
-          const uint4 kv = *reinterpret_cast<const uint4*>(kp + c * 8);
-          const uint32_t* qw = reinterpret_cast<const uint32_t*>(&qv);
-          const uint32_t* kw = reinterpret_cast<const uint32_t*>(&kv);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 qf = bf2f(qw[e]), kf = bf2f(kw[e]);
-            acc4[e] = fmaf(qf.x, kf.x, fmaf(qf.y, kf.y, acc4[e]));
-          }
-        }
-        xs[sidx] = ((acc4[0] + acc4[1]) + (acc4[2] + acc4[3])) * a.scale_log2;
-        mx = fmaxf(mx, xs[sidx]);
-      }
-    }
-    alpha = m_ref == -INFINITY ? 0.f : fast_ex2(m_ref - mx);  // mx is finite: key t always exists
-    ssum = l * alpha;
-#pragma unroll
-    for (int sidx = 0; sidx < kSufMax; ++sidx) {
-      psuf[sidx] = xs[sidx] == -INFINITY ? 0.f : fast_ex2(xs[sidx] - mx);
-      ssum += psuf[sidx];
-    }
-  }
-  // the row's normaliser, prefix weight and suffix probabilities, shared with the
-  // other half's thread of the same row through the (free) P buffer
-  float* sc = reinterpret_cast<float*>(smem + M::p) + row * (2 + kSufMax);
-  static_assert(size_t(kRows) * (2 + kSufMax) * 4 <= size_t(kRows) * kBlk * 2, "row scalars fit the P buffer");
-  if (lead) {
-    sc[0] = alpha;
-    sc[1] = 1.f / ssum;
-#pragma unroll
-    for (int sidx = 0; sidx < kSufMax; ++sidx) sc[2 + sidx] = psuf[sidx];
-  }
-  __syncthreads();
-  alpha = sc[0];
-  const float inv = sc[1];
-#pragma unroll
-  for (int sidx = 0; sidx < kSufMax; ++sidx) psuf[sidx] = sc[2 + sidx];
-  __nv_bfloat16* op = CAUSAL ? a.out + (seq0 + pos) * a.so_row + int64_t(hq) * a.so_h
-                             : a.out + brow * a.so_row + int64_t(t) * a.so_t + int64_t(hq) * a.so_h;
+  if (split) {  // unnormalised O relative to m_ref, and (m_ref, l): the combine kernel finishes the row
+    const int64_t prow = int64_t(blockIdx.z) * (int64_t(a.B) * a.HK * R) + int64_t(blockIdx.y) * R + gr;
+    if (rowthr && half == 0 && rvalid) a.part_ml[prow] = make_float2(m_ref, l);
 #pragma unroll 1
-  for (int piece = half * (kD / 64); rowthr && piece < (half + 1) * (kD / 64); ++piece) {  // this half's columns
-    uint32_t r[32];
-    tc::ld32(tO + piece * 32, r);  // whole warp (aligned), stores are per row below
-    tc::wait_ld();
-    if (!rvalid || nb == 0) continue;
-    float o[32];
+    for (int piece = half * (kD / 64); rowthr && piece < (half + 1) * (kD / 64); ++piece) {
+      uint32_t r[32];
+      tc::ld32(tO + piece * 32, r);  // whole warp (aligned)
+      tc::wait_ld();
+      if (!rvalid) continue;
+      float4* dst = reinterpret_cast<float4*>(a.part_o + prow * kD + piece * 32);
 #pragma unroll
-    for (int c = 0; c < 32; ++c) o[c] = __uint_as_float(r[c]) * alpha;
-    if (!CAUSAL) {
-#pragma unroll
+      for (int q4 = 0; q4 < 8; ++q4)
+        dst[q4] = nb > 0 ? make_float4(__uint_as_float(r[4 * q4]), __uint_as_float(r[4 * q4 + 1]),
+                                       __uint_as_float(r[4 * q4 + 2]), __uint_as_float(r[4 * q4 + 3]))
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  if (!split) {  // merge the suffix, normalise, gate, store (split rows: the combine kernel)
+    const int64_t brow = int64_t(b) * a.W + beam;
+    auto suf = [&](int sidx, int kv) -> const __nv_bfloat16* {  // this row's suffix key / value s
+      if (suf_smem)
+        return reinterpret_cast<const __nv_bfloat16*>(ssuf + (((beam - beam_lo) * a.T + sidx) * 2 + kv) * 512);
+      return kv ? a.sv + brow * a.ssv_row + int64_t(sidx) * a.ssv_t + int64_t(hk) * a.ssv_h
+                : a.sk + brow * a.ssk_row + int64_t(sidx) * a.ssk_t + int64_t(hk) * a.ssk_h;
+    };
+    float mx = m_ref, alpha = 1.f, ssum = l;
+    float psuf[kSufMax];
+  #pragma unroll
+    for (int sidx = 0; sidx < kSufMax; ++sidx) psuf[sidx] = 0.f;
+    const bool lead = rowthr && half == 0;  // computes the row's scalars
+    if (lead && !CAUSAL && rvalid) {
+      float xs[kSufMax];
+  #pragma unroll
       for (int sidx = 0; sidx < kSufMax; ++sidx) {
-        if (!(sidx < a.T && sidx <= t)) continue;
-        const __nv_bfloat16* vp = suf(sidx, 1) + piece * 32;
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          const uint4 vv = *reinterpret_cast<const uint4*>(vp + q4 * 8);
-          const uint32_t* vw = reinterpret_cast<const uint32_t*>(&vv);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 vf = bf2f(vw[e]);
-            o[q4 * 8 + 2 * e] = fmaf(psuf[sidx], vf.x, o[q4 * 8 + 2 * e]);
-            o[q4 * 8 + 2 * e + 1] = fmaf(psuf[sidx], vf.y, o[q4 * 8 + 2 * e + 1]);
+        xs[sidx] = -INFINITY;
+        if (sidx < a.T && sidx <= t) {  // scores against the beam's own keys s <= t
+          const __nv_bfloat16* kp = suf(sidx, 0);
+          float acc4[4] = {0.f, 0.f, 0.f, 0.f};
+  #pragma unroll 8
+          for (int c = 0; c < kD / 8; ++c) {
+            const uint4 qv = *reinterpret_cast<const uint4*>(smem + M::q + M::off(row, c, kD / 8));
+            const uint4 kv = *reinterpret_cast<const uint4*>(kp + c * 8);
+            const uint32_t* qw = reinterpret_cast<const uint32_t*>(&qv);
+            const uint32_t* kw = reinterpret_cast<const uint32_t*>(&kv);
+  #pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 qf = bf2f(qw[e]), kf = bf2f(kw[e]);
+              acc4[e] = fmaf(qf.x, kf.x, fmaf(qf.y, kf.y, acc4[e]));
+            }
+          }
+          xs[sidx] = ((acc4[0] + acc4[1]) + (acc4[2] + acc4[3])) * a.scale_log2;
+          mx = fmaxf(mx, xs[sidx]);
+        }
+      }
+      alpha = m_ref == -INFINITY ? 0.f : fast_ex2(m_ref - mx);  // mx is finite: key t always exists
+      ssum = l * alpha;
+  #pragma unroll
+      for (int sidx = 0; sidx < kSufMax; ++sidx) {
+        psuf[sidx] = xs[sidx] == -INFINITY ? 0.f : fast_ex2(xs[sidx] - mx);
+        ssum += psuf[sidx];
+      }
+    }
+    // the row's normaliser, prefix weight and suffix probabilities, shared with the
+    // other half's thread of the same row through the (free) P buffer
+    float* sc = reinterpret_cast<float*>(smem + M::p) + row * (2 + kSufMax);
+    static_assert(size_t(kRows) * (2 + kSufMax) * 4 <= size_t(kRows) * kBlk * 2, "row scalars fit the P buffer");
+    if (lead) {
+      sc[0] = alpha;
+      sc[1] = 1.f / ssum;
+  #pragma unroll
+      for (int sidx = 0; sidx < kSufMax; ++sidx) sc[2 + sidx] = psuf[sidx];
+    }
+    __syncthreads();
+    alpha = sc[0];
+    const float inv = sc[1];
+  #pragma unroll
+    for (int sidx = 0; sidx < kSufMax; ++sidx) psuf[sidx] = sc[2 + sidx];
+    __nv_bfloat16* op = CAUSAL ? a.out + (seq0 + pos) * a.so_row + int64_t(hq) * a.so_h
+                               : a.out + brow * a.so_row + int64_t(t) * a.so_t + int64_t(hq) * a.so_h;
+  #pragma unroll 1
+    for (int piece = half * (kD / 64); rowthr && piece < (half + 1) * (kD / 64); ++piece) {  // this half's columns
+      uint32_t r[32];
+      tc::ld32(tO + piece * 32, r);  // whole warp (aligned), stores are per row below
+      tc::wait_ld();
+      if (!rvalid || nb == 0) continue;
+      float o[32];
+  #pragma unroll
+      for (int c = 0; c < 32; ++c) o[c] = __uint_as_float(r[c]) * alpha;
+      if (!CAUSAL) {
+  #pragma unroll
+        for (int sidx = 0; sidx < kSufMax; ++sidx) {
+          if (!(sidx < a.T && sidx <= t)) continue;
+          const __nv_bfloat16* vp = suf(sidx, 1) + piece * 32;
+  #pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const uint4 vv = *reinterpret_cast<const uint4*>(vp + q4 * 8);
+            const uint32_t* vw = reinterpret_cast<const uint32_t*>(&vv);
+  #pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 vf = bf2f(vw[e]);
+              o[q4 * 8 + 2 * e] = fmaf(psuf[sidx], vf.x, o[q4 * 8 + 2 * e]);
+              o[q4 * 8 + 2 * e + 1] = fmaf(psuf[sidx], vf.y, o[q4 * 8 + 2 * e + 1]);
+            }
           }
         }
       }
-    }
-#pragma unroll
-    for (int q4 = 0; q4 < 4; ++q4) {
-      uint4 res;
-      uint32_t* rw = reinterpret_cast<uint32_t*>(&res);
-      uint4 gv = make_uint4(0u, 0u, 0u, 0u);
-      const int c = piece * 4 + q4;
-      if (a.gate) gv = *reinterpret_cast<const uint4*>(smem + M::k + row * 512 + ((c ^ (row & 31)) * 16));
-      const uint32_t* gw = reinterpret_cast<const uint32_t*>(&gv);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float v0 = o[q4 * 8 + 2 * e] * inv, v1 = o[q4 * 8 + 2 * e + 1] * inv;
-        if (a.gate) {  // bf16(o) * bf16(sigmoid(gate)), each pair rounded by one packed conversion
-          const float2 gf = bf2f(gw[e]);
-          const float2 vr = bf2f(bf2_pack(v0, v1));
-          const float2 sr = bf2f(bf2_pack(fast_rcp(1.f + fast_ex2(-1.4426950408889634f * gf.x)),
-                                          fast_rcp(1.f + fast_ex2(-1.4426950408889634f * gf.y))));
-          v0 = vr.x * sr.x;
-          v1 = vr.y * sr.y;
+  #pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint4 res;
+        uint32_t* rw = reinterpret_cast<uint32_t*>(&res);
+        uint4 gv = make_uint4(0u, 0u, 0u, 0u);
+        const int c = piece * 4 + q4;
+        if (a.gate) gv = *reinterpret_cast<const uint4*>(smem + M::k + row * 512 + ((c ^ (row & 31)) * 16));
+        const uint32_t* gw = reinterpret_cast<const uint32_t*>(&gv);
+  #pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float v0 = o[q4 * 8 + 2 * e] * inv, v1 = o[q4 * 8 + 2 * e + 1] * inv;
+          if (a.gate) {  // bf16(o) * bf16(sigmoid(gate)), each pair rounded by one packed conversion
+            const float2 gf = bf2f(gw[e]);
+            const float2 vr = bf2f(bf2_pack(v0, v1));
+            const float2 sr = bf2f(bf2_pack(fast_rcp(1.f + fast_ex2(-1.4426950408889634f * gf.x)),
+                                            fast_rcp(1.f + fast_ex2(-1.4426950408889634f * gf.y))));
+            v0 = vr.x * sr.x;
+            v1 = vr.y * sr.y;
+          }
+          rw[e] = bf2_pack(v0, v1);
         }
-        rw[e] = bf2_pack(v0, v1);
+        *reinterpret_cast<uint4*>(op + piece * 32 + q4 * 8) = res;
       }
-      *reinterpret_cast<uint4*>(op + piece * 32 + q4 * 8) = res;
     }
   }
   if (!ok && (tid == 0 || tid == kIssuer || tid == kProducer)) atomicOr(a.status, 1u);  // a wait timed out
@@ -511,10 +540,99 @@ int launch_attn_tc(const AttnTcArgs& a, cudaStream_t stream) {
     return KADLLM_ECUDA;
   }
   const int64_t R = CAUSAL ? int64_t(a.L) * a.G : int64_t(a.W) * (a.T - a.t0) * a.G;
-  dim3 grid(unsigned((R + kRows - 1) / kRows), unsigned(a.B * a.HK));
+  dim3 grid(unsigned((R + kRows - 1) / kRows), unsigned(a.B * a.HK), unsigned(CAUSAL ? 1 : max(a.nsplit, 1)));
   kern<<<grid, kThreads, AttnTcSmem::bytes, stream>>>(a);
   KB_CHECK_LAUNCH("tiled attention launch");
   return KADLLM_OK;
+}
+
+// Split decode: one warp per query row merges the splits' (O, m, l), the row's suffix keys
+// s <= t (scores q.k_s from the row's q, in the kernel's exp2 domain) and values, then
+// normalises and applies the gate like the fused epilogue.  Lane i holds dims 8i .. 8i + 7.
+__global__ void __launch_bounds__(256) attn_split_combine_kernel(const AttnTcArgs a) {
+  const int TG = (a.T - a.t0) * a.G;
+  const int64_t R = int64_t(a.W) * TG;
+  const int64_t rows = int64_t(a.B) * a.HK * R;
+  const int64_t id = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (id >= rows) return;  // whole warp
+  const int lane = threadIdx.x & 31;
+  const int bh = int(id / R), gr = int(id % R);
+  const int b = bh / a.HK, hk = bh % a.HK;
+  const int beam = gr / TG, rem = gr % TG, t = a.t0 + rem / a.G, g = rem % a.G, hq = hk * a.G + g;
+  const int64_t brow = int64_t(b) * a.W + beam;
+  float M = -INFINITY;
+  for (int sp = 0; sp < a.nsplit; ++sp) M = fmaxf(M, a.part_ml[int64_t(sp) * rows + id].x);
+  // suffix scores
+  const uint4 qv = *reinterpret_cast<const uint4*>(a.q + brow * a.sq_row + int64_t(t) * a.sq_t + int64_t(hq) * a.sq_h +
+                                                   lane * 8);
+  const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
+  float xs[kSufMax];
+#pragma unroll
+  for (int sidx = 0; sidx < kSufMax; ++sidx) {
+    xs[sidx] = -INFINITY;
+    if (sidx < a.T && sidx <= t) {
+      const uint4 kv = *reinterpret_cast<const uint4*>(a.sk + brow * a.ssk_row + int64_t(sidx) * a.ssk_t +
+                                                       int64_t(hk) * a.ssk_h + lane * 8);
+      const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
+      float acc = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 qf = bf2f(qw[e]), kf = bf2f(kw[e]);
+        acc = fmaf(qf.x, kf.x, fmaf(qf.y, kf.y, acc));
+      }
+      xs[sidx] = warp_sum(acc) * a.scale_log2;
+      M = fmaxf(M, xs[sidx]);
+    }
+  }
+  float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float L = 0.f;
+  for (int sp = 0; sp < a.nsplit; ++sp) {
+    const float2 ml = a.part_ml[int64_t(sp) * rows + id];
+    if (!(ml.x > -INFINITY)) continue;
+    const float f = fast_ex2(ml.x - M);
+    L = fmaf(ml.y, f, L);
+    const float4* src = reinterpret_cast<const float4*>(a.part_o + (int64_t(sp) * rows + id) * kD + lane * 8);
+    const float4 u0 = src[0], u1 = src[1];
+    o[0] = fmaf(u0.x, f, o[0]); o[1] = fmaf(u0.y, f, o[1]); o[2] = fmaf(u0.z, f, o[2]); o[3] = fmaf(u0.w, f, o[3]);
+    o[4] = fmaf(u1.x, f, o[4]); o[5] = fmaf(u1.y, f, o[5]); o[6] = fmaf(u1.z, f, o[6]); o[7] = fmaf(u1.w, f, o[7]);
+  }
+#pragma unroll
+  for (int sidx = 0; sidx < kSufMax; ++sidx) {
+    if (!(xs[sidx] > -INFINITY)) continue;
+    const float p = fast_ex2(xs[sidx] - M);
+    L += p;
+    const uint4 vv = *reinterpret_cast<const uint4*>(a.sv + brow * a.ssv_row + int64_t(sidx) * a.ssv_t +
+                                                     int64_t(hk) * a.ssv_h + lane * 8);
+    const uint32_t vw[4] = {vv.x, vv.y, vv.z, vv.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 vf = bf2f(vw[e]);
+      o[2 * e] = fmaf(p, vf.x, o[2 * e]);
+      o[2 * e + 1] = fmaf(p, vf.y, o[2 * e + 1]);
+    }
+  }
+  const float inv = 1.f / L;
+  uint4 gv = make_uint4(0u, 0u, 0u, 0u);
+  if (a.gate)
+    gv = *reinterpret_cast<const uint4*>(a.gate + brow * a.sg_row + int64_t(t) * a.sg_t + int64_t(hq) * a.sg_h +
+                                         lane * 8);
+  const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+  uint32_t res[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    float v0 = o[2 * e] * inv, v1 = o[2 * e + 1] * inv;
+    if (a.gate) {  // bf16(o) * bf16(sigmoid(gate)), as the fused epilogue
+      const float2 gf = bf2f(gw[e]);
+      const float2 vr = bf2f(bf2_pack(v0, v1));
+      const float2 sr = bf2f(bf2_pack(fast_rcp(1.f + fast_ex2(-1.4426950408889634f * gf.x)),
+                                      fast_rcp(1.f + fast_ex2(-1.4426950408889634f * gf.y))));
+      v0 = vr.x * sr.x;
+      v1 = vr.y * sr.y;
+    }
+    res[e] = bf2_pack(v0, v1);
+  }
+  *reinterpret_cast<uint4*>(a.out + brow * a.so_row + int64_t(t) * a.so_t + int64_t(hq) * a.so_h + lane * 8) =
+      make_uint4(res[0], res[1], res[2], res[3]);
 }
 
 }  // namespace
@@ -639,4 +757,86 @@ extern "C" int kadllm_attention_tiled_varlen(
                              ssk_h, suffix_v, ssv_row, ssv_t, ssv_h, gate, sg_row, sg_t, sg_h, out, so_row, so_t,
                              so_h, status, cu_seqlens, batch, beam_width, steps, first_step, q_heads, kv_heads,
                              max_prefix_len, head_dim, scale, causal, stream);
+}
+
+namespace kb {
+namespace {
+// Bytes of the split partials for a decode launch (0 when no split is taken).
+int64_t split_bytes(int64_t batch, int64_t beam_width, int64_t steps, int64_t first_step, int64_t q_heads,
+                    int64_t splits) {
+  if (splits <= 1) return 0;
+  const int64_t rows = batch * beam_width * (steps - first_step) * q_heads;
+  return ((splits * rows * 8 + 255) & ~int64_t(255)) + splits * rows * int64_t(kD) * 4;  // (m, l), then O
+}
+}  // namespace
+}  // namespace kb
+
+extern "C" int64_t kadllm_attention_split_workspace(int64_t batch, int64_t beam_width, int64_t steps,
+                                                    int64_t first_step, int64_t q_heads, int64_t splits) {
+  if (batch < 1 || beam_width < 1 || steps < 1 || first_step < 0 || first_step >= steps || q_heads < 1) return -1;
+  return kb::split_bytes(batch, beam_width, steps, first_step, q_heads, splits);
+}
+
+extern "C" int kadllm_attention_tiled_split(const void* q, int64_t sq_row, int64_t sq_t, int64_t sq_h,
+                                            const void* k_tiles, const void* v_tiles, int64_t blocks_per_head,
+                                            const void* suffix_k, int64_t ssk_row, int64_t ssk_t, int64_t ssk_h,
+                                            const void* suffix_v, int64_t ssv_row, int64_t ssv_t, int64_t ssv_h,
+                                            const void* gate, int64_t sg_row, int64_t sg_t, int64_t sg_h, void* out,
+                                            int64_t so_row, int64_t so_t, int64_t so_h, uint32_t* status,
+                                            int64_t batch, int64_t beam_width, int64_t steps, int64_t first_step,
+                                            int64_t q_heads, int64_t kv_heads, int64_t prefix_len, int64_t head_dim,
+                                            float scale, int64_t splits, void* workspace, int64_t workspace_bytes,
+                                            void* stream) {
+  using namespace kb;
+  const int64_t nblk_keys = (prefix_len + kBlk - 1) / kBlk;
+  if (splits > nblk_keys) splits = nblk_keys;
+  if (splits <= 1)
+    return attention_tiled(q, sq_row, sq_t, sq_h, k_tiles, v_tiles, blocks_per_head, suffix_k, ssk_row, ssk_t, ssk_h,
+                           suffix_v, ssv_row, ssv_t, ssv_h, gate, sg_row, sg_t, sg_h, out, so_row, so_t, so_h, status,
+                           nullptr, batch, beam_width, steps, first_step, q_heads, kv_heads, prefix_len, head_dim,
+                           scale, 0, stream);
+  KB_REQUIRE(splits <= 64, KADLLM_EINVAL, "tiled attention: at most 64 splits");
+  const int64_t bps = (nblk_keys + splits - 1) / splits;
+  splits = (nblk_keys + bps - 1) / bps;  // every split holds at least one key block
+  const int64_t need = split_bytes(batch, beam_width, steps, first_step, q_heads, splits);
+  KB_REQUIRE(workspace && workspace_bytes >= need && (reinterpret_cast<uintptr_t>(workspace) & 15) == 0,
+             KADLLM_EINVAL, "tiled attention: split workspace too small (%lld bytes needed)", (long long)need);
+  KB_REQUIRE(q && k_tiles && v_tiles && out && status && suffix_k && suffix_v, KADLLM_EINVAL,
+             "tiled attention: null pointer");
+  KB_REQUIRE(head_dim == kD, KADLLM_EUNSUPPORTED, "tiled attention: head_dim must be %d", kD);
+  KB_REQUIRE(batch >= 1 && q_heads >= 1 && kv_heads >= 1 && q_heads % kv_heads == 0 && prefix_len >= 1 &&
+                 blocks_per_head * kBlk >= prefix_len && beam_width >= 1 && steps >= 1 && steps <= kSufMax &&
+                 first_step >= 0 && first_step < steps,
+             KADLLM_EINVAL, "tiled attention: bad dimensions");
+  const auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  KB_REQUIRE(al16(q) && al16(k_tiles) && al16(v_tiles) && al16(out) && al16(suffix_k) && al16(suffix_v) &&
+                 (!gate || al16(gate)) && sq_row % 8 == 0 && sq_t % 8 == 0 && sq_h % 8 == 0 && so_row % 8 == 0 &&
+                 so_t % 8 == 0 && so_h % 8 == 0 && ssk_row % 8 == 0 && ssk_t % 8 == 0 && ssk_h % 8 == 0 &&
+                 ssv_row % 8 == 0 && ssv_t % 8 == 0 && ssv_h % 8 == 0 && sg_row % 8 == 0 && sg_t % 8 == 0 &&
+                 sg_h % 8 == 0,
+             KADLLM_EINVAL, "tiled attention: operands and strides must be 16-byte aligned");
+  const int64_t R = beam_width * (steps - first_step) * (q_heads / kv_heads);
+  KB_REQUIRE(R < (int64_t(1) << 30) && batch * kv_heads <= 65535, KADLLM_EINVAL, "tiled attention: too many rows");
+  AttnTcArgs a{};
+  a.q = static_cast<const __nv_bfloat16*>(q); a.sq_row = sq_row; a.sq_t = sq_t; a.sq_h = sq_h;
+  a.kt = static_cast<const unsigned char*>(k_tiles); a.vt = static_cast<const unsigned char*>(v_tiles);
+  a.nblk = int(blocks_per_head);
+  a.sk = static_cast<const __nv_bfloat16*>(suffix_k); a.ssk_row = ssk_row; a.ssk_t = ssk_t; a.ssk_h = ssk_h;
+  a.sv = static_cast<const __nv_bfloat16*>(suffix_v); a.ssv_row = ssv_row; a.ssv_t = ssv_t; a.ssv_h = ssv_h;
+  a.gate = static_cast<const __nv_bfloat16*>(gate); a.sg_row = sg_row; a.sg_t = sg_t; a.sg_h = sg_h;
+  a.out = static_cast<__nv_bfloat16*>(out); a.so_row = so_row; a.so_t = so_t; a.so_h = so_h;
+  a.status = status;
+  a.B = int(batch); a.W = int(beam_width); a.T = int(steps); a.H = int(q_heads);
+  a.HK = int(kv_heads); a.G = int(q_heads / kv_heads); a.L = int(prefix_len); a.t0 = int(first_step);
+  a.scale_log2 = (scale > 0.f ? scale : 1.0f / sqrtf(float(head_dim))) * 1.4426950408889634f;
+  a.nsplit = int(splits);
+  a.bps = int(bps);
+  const int64_t rows = batch * kv_heads * R;
+  a.part_ml = static_cast<float2*>(workspace);
+  a.part_o = reinterpret_cast<float*>(static_cast<char*>(workspace) + ((splits * rows * 8 + 255) & ~int64_t(255)));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (int rc = launch_attn_tc<false>(a, s)) return rc;
+  attn_split_combine_kernel<<<unsigned((rows + 7) / 8), 256, 0, s>>>(a);
+  KB_CHECK_LAUNCH("tiled attention split combine launch");
+  return KADLLM_OK;
 }

@@ -7,7 +7,9 @@ Cases (the kernel microbenchmark shapes and the GRBeam step shapes):
            gated norm) from the packed projection: B=32, T=1024, 16 heads of 128
   conv     causal conv1d width 4 + SiLU over T=1024, 2048 channels (B=32)
   attn     shared-prefix decode attention: 256 beams x 8 q / 2 kv heads x d=256
-           against a 4096-token prefix plus a 3-token causal suffix (attn_tiled:
+           against a 4096-token prefix plus a 3-token causal suffix, through the
+           public op (prefix re-layout included; attn_split: the kernels alone;
+           attn_tiled:
            the tcgen05 kernel over the tiled prefix; attn_step: the GRBeam
            step's second decode, 32 requests x 256 beams, prefix 1024, T=2;
            attn_causal: the prefill's causal attention, 32 x 1024 tokens)
@@ -97,6 +99,41 @@ def case_attn(gen, reps):
     pk, pv = n(B, L, HK, D), n(B, L, HK, D)
     ms = _time(lambda: ops.prefix_attention(q, pk, pv, sk, sv, beam_width=W), reps)
     return ms, "tensor", 4 * B * W * T * Hq * D * L + 4 * B * W * Hq * D * T * (T + 1) / 2
+
+
+def case_attn_split(gen, reps, B=1, W=256, T=3, L=4096):
+    """The decode attention kernels alone at the microbenchmark shape (prefix tiled once
+    outside the timed loop): the key-block split over 3 CTAs per row tile + the combine."""
+    dev, bf = torch.device("cuda"), torch.bfloat16
+    Hq, HK, D = 8, 2, 256
+    n = lambda *s: torch.randn(*s, device=dev, generator=gen).to(bf)
+    q = n(B * W, T, Hq, D)
+    sk, sv = n(B * W, T, HK, D), n(B * W, T, HK, D)
+    kc, vc = n(B, HK, L, D), n(B, HK, L, D)
+    nbytes = _lib.lib().kadllm_kv_tile_bytes(B, HK, L, D)
+    kt = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    vt = torch.empty_like(kt)
+    s = _lib.stream(dev)
+    _lib.call("kadllm_kv_tile", kc.data_ptr(), HK * L * D, D, L * D, B, HK, L, D, kt.data_ptr(), nbytes, s)
+    _lib.call("kadllm_kv_tile", vc.data_ptr(), HK * L * D, D, L * D, B, HK, L, D, vt.data_ptr(), nbytes, s)
+    out = torch.empty(B * W, T, Hq, D, dtype=bf, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    ctas = -(-(W * T * (Hq // HK)) // 128) * B * HK
+    splits = max(1, min(sms // ctas, -(-L // 64), 64))
+    ws = torch.empty(max(_lib.lib().kadllm_attention_split_workspace(B, W, T, 0, Hq, splits), 16), dtype=torch.uint8,
+                     device=dev)
+
+    def run():
+        _lib.call("kadllm_attention_tiled_split", q.data_ptr(), T * Hq * D, Hq * D, D, kt.data_ptr(), vt.data_ptr(),
+                  -(-L // 64), sk.data_ptr(), T * HK * D, HK * D, D, sv.data_ptr(), T * HK * D, HK * D, D, None, 0, 0,
+                  0, out.data_ptr(), T * Hq * D, Hq * D, D, status.data_ptr(), B, W, T, 0, Hq, HK, L, D, D ** -0.5,
+                  splits, ws.data_ptr(), ws.numel(), s)
+
+    ms = _time(run, reps)
+    if int(status.item()):
+        raise RuntimeError("tiled attention reported a timed-out wait")
+    return ms, "tensor", 4 * B * W * T * Hq * D * L + 4 * B * W * Hq * D * T * (T + 1) / 2, {"splits": splits}
 
 
 def case_attn_tiled(gen, reps, B=1, W=256, T=3, L=4096, causal=False):
@@ -197,7 +234,7 @@ def case_gemm(gen, reps, M, N, K, epilogue=0):
                                             "cublas_tflops": 2.0 * M * N * K / (ref_ms / 1e3) / 1e12}
 
 
-CASES = {"prefill": case_prefill, "attn_tiled": case_attn_tiled, "conv": case_conv, "attn": case_attn, "mixer": case_mixer,
+CASES = {"prefill": case_prefill, "attn_tiled": case_attn_tiled, "attn_split": case_attn_split, "conv": case_conv, "attn": case_attn, "mixer": case_mixer,
          "mixer2": lambda g, r: case_mixer(g, r, T=2), "select": case_select,
          "attn_step": lambda g, r: case_attn_tiled(g, r, B=32, W=256, T=2, L=1024),
          "attn_causal": lambda g, r: case_attn_tiled(g, r, B=32, W=1, T=1, L=1024, causal=True),

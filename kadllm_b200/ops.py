@@ -279,10 +279,34 @@ def _prefix_attention_tiled(q, prefix_k, prefix_v, suffix_k, suffix_v, out, B, W
     status = _status.get(dev)
     if status is None:
         status = _status[dev] = torch.zeros(1, dtype=torch.int32, device=dev)
-    _lib.call("kadllm_attention_tiled", q.data_ptr(), *q.stride()[:3], kt.data_ptr(), vt.data_ptr(), -(-L // 64),
-              suffix_k.data_ptr(), *suffix_k.stride()[:3], suffix_v.data_ptr(), *suffix_v.stride()[:3], None, 0, 0, 0,
-              out.data_ptr(), *out.stride()[:3], status.data_ptr(), B, W, T, 0, H, HK, L, D, scale, 0, s)
-    if not torch.cuda.is_current_stream_capturing() and int(status.item()):
-        status.zero_()
-        raise RuntimeError("prefix_attention: a tensor-core pipeline wait timed out")
+    # CTAs of 128 query rows per (request, kv head); split the key blocks when they leave SMs idle
+    ctas = -(-(W * T * (H // HK)) // 128) * B * HK
+    sms = _sm_count(dev)
+    splits = max(1, min(sms // ctas, -(-L // 64), 64)) if ctas < sms else 1
+    ws_bytes = lib.kadllm_attention_split_workspace(B, W, T, 0, H, splits)
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+    _lib.call("kadllm_attention_tiled_split", q.data_ptr(), *q.stride()[:3], kt.data_ptr(), vt.data_ptr(),
+              -(-L // 64), suffix_k.data_ptr(), *suffix_k.stride()[:3], suffix_v.data_ptr(), *suffix_v.stride()[:3],
+              None, 0, 0, 0, out.data_ptr(), *out.stride()[:3], status.data_ptr(), B, W, T, 0, H, HK, L, D, scale,
+              splits, ws.data_ptr(), ws.numel(), s)
     return out
+
+
+def check(device=None) -> None:
+    """Raise if a tensor-core wait of an operator timed out on ``device`` since the last
+    check (synchronises; the operators themselves never wait on the host)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    status = _status.get(dev)
+    if status is not None and int(status.item()):
+        status.zero_()
+        raise RuntimeError("kadllm_b200 operator: a tensor-core pipeline wait timed out")
+
+
+_sms: dict = {}
+
+
+def _sm_count(dev) -> int:
+    n = _sms.get(dev)
+    if n is None:
+        n = _sms[dev] = torch.cuda.get_device_properties(dev).multi_processor_count
+    return n

@@ -167,3 +167,69 @@ def test_causal_at_the_benchmark_shape_sampled():
         got.append(out[b * L + pos, h].float())
     assert_close_rel(torch.stack(got).cpu().numpy(), torch.stack(want).cpu().numpy(), rel=1e-2,
                      what="causal attention at the benchmark shape")
+
+
+@pytest.mark.parametrize("B,W,T,L,t0,splits", [(1, 40, 3, 1100, 0, 3), (2, 5, 2, 100, 1, 2), (1, 7, 1, 4096, 0, 64)])
+def test_split_decode_matches_torch(B, W, T, L, t0, splits):
+    """kadllm_attention_tiled_split: key blocks split over CTAs, partials merged with the
+    suffix keys and the gate by the combine kernel (one split per key block at most)."""
+    hq, hk = 8, 2
+    G = hq // hk
+    gen = torch.Generator(device="cuda").manual_seed(L + W + splits)
+    n = lambda *s: torch.randn(*s, device="cuda", generator=gen)
+    q = n(B * W, T, hq, D).to(bf)
+    kc, vc = n(B, hk, L, D).to(bf), n(B, hk, L, D).to(bf)
+    ks, vs = n(B * W, T, hk, D).to(bf), n(B * W, T, hk, D).to(bf)
+    gate = n(B * W, T, hq, D).to(bf)
+    out = torch.zeros(B * W, T, hq, D, dtype=bf, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    kt, nblk = _tiles(kc)
+    vt, _ = _tiles(vc)
+    nbytes = _lib.lib().kadllm_attention_split_workspace(B, W, T, t0, hq, splits)
+    ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device="cuda")
+    _lib.call("kadllm_attention_tiled_split", q.data_ptr(), T * hq * D, hq * D, D, kt.data_ptr(), vt.data_ptr(), nblk,
+              ks.data_ptr(), T * hk * D, hk * D, D, vs.data_ptr(), T * hk * D, hk * D, D, gate.data_ptr(),
+              T * hq * D, hq * D, D, out.data_ptr(), T * hq * D, hq * D, D, status.data_ptr(), B, W, T, t0, hq, hk, L,
+              D, D ** -0.5, splits, ws.data_ptr(), ws.numel(), _lib.stream(q.device))
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    ref = torch.zeros(B * W, T, hq, D, device="cuda")
+    for b in range(B):
+        for w in range(W):
+            r = b * W + w
+            for t in range(t0, T):
+                for h in range(hq):
+                    kv = h // G
+                    keys = torch.cat([kc[b, kv].float(), ks[r, :t + 1, kv].float()])
+                    vals = torch.cat([vc[b, kv].float(), vs[r, :t + 1, kv].float()])
+                    p = torch.softmax(keys @ q[r, t, h].float() * D ** -0.5, 0)
+                    ref[r, t, h] = p @ vals
+    want = _gate(ref, gate)
+    assert_close_rel(out[:, t0:].float().cpu().numpy(), want[:, t0:].float().cpu().numpy(), rel=1e-2,
+                     what="split decode attention")
+
+
+def test_public_op_long_prefix_few_requests():
+    """ops.prefix_attention at the kernel microbenchmark's shape (1 request x 256 beams x
+    3 steps, 4096 prefix keys: the split path), sampled rows against fp32 torch."""
+    from kadllm_b200 import ops
+
+    B, W, T, L, hq, hk = 1, 256, 3, 4096, 8, 2
+    G = hq // hk
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    n = lambda *s: torch.randn(*s, device="cuda", generator=gen).to(bf)
+    q, sk, sv = n(B * W, T, hq, D), n(B * W, T, hk, D), n(B * W, T, hk, D)
+    pk, pv = n(B, L, hk, D), n(B, L, hk, D)
+    out = ops.prefix_attention(q, pk, pv, sk, sv, beam_width=W)
+    rng = np.random.default_rng(2)
+    got, want = [], []
+    for _ in range(32):
+        w, t, h = int(rng.integers(W)), int(rng.integers(T)), int(rng.integers(hq))
+        kv = h // G
+        keys = torch.cat([pk[0, :, kv].float(), sk[w, :t + 1, kv].float()])
+        vals = torch.cat([pv[0, :, kv].float(), sv[w, :t + 1, kv].float()])
+        p = torch.softmax(keys @ q[w, t, h].float() * D ** -0.5, 0)
+        want.append(p @ vals)
+        got.append(out[w, t, h].float())
+    assert_close_rel(torch.stack(got).cpu().numpy(), torch.stack(want).cpu().numpy(), rel=1e-2,
+                     what="public prefix attention, long prefix")
