@@ -76,13 +76,15 @@ KADLLM_API int kadllm_gated_delta_replay(const void* q, const void* k, const voi
  *   rec_state   [B, HV, K, V] bf16 contiguous
  *   a_log, dt_bias [HV] f32; norm_weight [V] f32 (values of the BF16 params)
  *   out         [BW*T, HV*V] bf16
+ *   status      device uint32: bit 0 set when a tensor-core wait timed out
+ *               (read it after the stream synchronises; the output is then invalid)
  * ------------------------------------------------------------------------ */
 KADLLM_API int kadllm_gdn_mixer_replay(const void* proj, int64_t ld_proj, const void* conv_state,
                             int64_t conv_hist, const void* conv_weight, const void* rec_state,
                             const float* a_log, const float* dt_bias, const float* norm_weight,
                             float norm_eps, void* out, int64_t batch, int64_t beam_width,
                             int64_t steps, int64_t heads, int64_t v_heads, int64_t k_dim,
-                            int64_t v_dim, void* stream);
+                            int64_t v_dim, uint32_t* status, void* stream);
 
 /* ------------------------------------------------------------------------
  * Depthwise causal conv1d replay from a shared prefix state (+ SiLU).
@@ -397,7 +399,7 @@ KADLLM_API int kadllm_gdn_mixer_continue(const void* proj_prev, const int32_t* p
                                          const float* a_log, const float* dt_bias, const float* norm_weight,
                                          float norm_eps, void* out, int64_t batch, int64_t beam_width,
                                          int64_t heads, int64_t v_heads, int64_t k_dim, int64_t v_dim,
-                                         void* stream);
+                                         uint32_t* status, void* stream);
 
 /* Diagnostics: one CTA runs the tensor-core kernels' bounded mbarrier wait on a
  * barrier nothing completes, giving up after max_cycles SM clocks (1 .. 2^32)

@@ -10,28 +10,37 @@
 // state S0 = state[b, hv]; with a_t = exp(g_t), A_t = prod_{r<=t} a_r:
 //     S_t^T k_t (before the update) = A_t S0^T k_t + a_t (k_0.k_t) d_0   (t = 1)
 //     d_t = beta_t (v_t - that),   o_t = A_t S0^T q_t + [t=1] a_1 (k_0.q_1) d_0 + d_t (k_t.q_t)
-// so the only D x D work is [q_t ; k_t] x S0 on the tensor cores.
+// so the only D x D work is [q_t ; k_t] x S0, on the 5th-generation tensor cores.
 //
 // Work unit: an "octet" of 8 rows (beam, token): 8 beams for T = 1, 4 beams x
-// 2 tokens for T = 2 (row r = token r / 4, beam r % 4), one row per MMA row g.
-// A step-1 row takes k_0, d_0 and the decay of its beam's step-0 row from the
-// partner lane (lane ^ 16), so both token counts run the same code and the
-// same shared-memory footprint (two CTAs per SM).
+// 2 tokens for T = 2 (row r = token r / 4, beam r % 4), one row per thread
+// quad g.  A step-1 row takes k_0, d_0 and the decay of its beam's step-0 row
+// from the partner lane (lane ^ 16), so both token counts run the same code and
+// the same shared-memory footprint (two CTAs per SM).
 //
 // Data movement: each warp owns a run of octets and stages an octet's
 // projection slices (the q, k, v, z head slices and the two gate words of each
 // row) in shared memory with 16-byte cp.async copies, one octet ahead of the
-// octet it computes.  S0 is staged once per CTA with an XOR swizzle that keeps
-// the ldmatrix reads conflict-free.  The output tile goes back through the
-// staged q slice and leaves as 16-byte stores.
+// octet it computes.  S0 is staged once per CTA as an MN-major core-matrix
+// image (the B operand).  The output tile goes back through the staged q slice
+// and leaves as 16-byte stores.
 //
-// Operand order: the m16n8k16 A fragment of thread (g, tq) holds k columns
-// {2tq, 2tq+1, 2tq+8, 2tq+9} of a k16 step.  The contraction order is free, so
-// k16 steps 2m and 2m+1 take physical columns 32m + 8tq + [0, 8): a thread's A
-// data for two steps is one 16-byte chunk of its staged row, and the ldmatrix
-// row addresses of S0 apply the same permutation.  A is split into bf16 hi + lo
-// parts (two MMAs), keeping ~16 mantissa bits of the fp32 normalised q and k.
+// Contraction (tcgen05, A from tensor memory): the CTA's four warps work in
+// rounds of one octet each.  Warp w writes its octet's normalised q rows to
+// TMEM lanes 32w + g and k rows to lanes 32w + 8 + g (16x256b stores, bf16 hi
+// and lo parts in two column ranges: ~16 mantissa bits of the fp32 q and k),
+// one thread issues D/16 hi + D/16 lo MMAs of M = 128, N = D against S0 and
+// commits to an mbarrier, and each warp reads its 16 accumulator lanes back
+// with 16x256b loads, whose register layout is the m16n8 accumulator fragment
+// (thread (g, tq): columns 8j + 2tq + {0, 1} of lanes g and g + 8).  The
+// contraction order is free: a thread's pairs of channels 32m + 8tq + 2p + {0,1}
+// go to TMEM column 8i + 2tq + e (i = 2m + p / 2, e = p % 2), i.e. MMA k index
+// kappa = 32m + 16(p / 2) + 4tq + 2(p % 2) + {0,1}, and S0 row 32m + 8tq + 2p + d
+// is staged as B row kappa (a bit permutation of the row index).
+// TMEM per CTA: D accumulator columns, D/2 hi columns, D/2 lo columns.  The
+// mbarrier wait is bounded and reports through the status word.
 #include "gdn_mixer.cuh"
+#include "tcgen05.cuh"
 
 namespace kb {
 namespace {
@@ -43,16 +52,19 @@ struct MixLayout {
   static constexpr int CH = D / 8;          // 16-byte chunks in a head row
   static constexpr int NCH = 3 * D;         // conv channels: q head, k head, v head
   static constexpr int ROWB = 8 * D + 16;   // staged bytes per (token, beam): q, k, v, z, gate words
-  static constexpr int S0B = D * D * 2;     // swizzled bf16 state
+  static constexpr int S0B = D * D * 2;     // bf16 state, MN-major core-matrix image
+  static constexpr int KGRP = 16 * D;       // bytes per group of 8 B rows (D / 8 core matrices)
+  static constexpr int TCOLS = 2 * D;       // TMEM columns: accumulator, A hi, A lo
   static constexpr int TABB = 8 * NCH * 4;  // conv table [8][NCH] fp32
   static constexpr int NWB = D * 4;         // norm weight fp32
   static constexpr int OCTB = 8 * ROWB;     // one staged octet: 8 (beam, token) rows
-  static constexpr size_t SMEM = size_t(S0B) + TABB + NWB + size_t(kMixWarps) * 2 * OCTB;
+  static constexpr size_t SMEM = size_t(S0B) + TABB + NWB + size_t(kMixWarps) * 2 * OCTB + 16;  // + mbarrier, TMEM slot
 };
 
-// 16-byte chunk swizzle of state row r: distinct over the 8 rows that one
-// ldmatrix matrix reads under the permuted k order (bit 0 and bits 3-4 of r).
-__device__ __forceinline__ int s0_swz(int r) { return (r & 1) | (((r >> 3) & 3) << 1); }
+// MMA k index (B row) of state row r = 32m + 8tq + 2p + d: 32m + 16(p / 2) + 4tq + 2(p % 2) + d.
+__device__ __forceinline__ int kappa_of(int r) {
+  return (r & ~31) | (((r >> 2) & 1) << 4) | (((r >> 3) & 3) << 2) | (((r >> 1) & 1) << 1) | (r & 1);
+}
 
 // cp.async with zero fill when `valid` is false (no bytes read from gmem).
 __device__ __forceinline__ void cp16z(void* smem, const void* gmem, bool valid) {
@@ -130,13 +142,18 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
   constexpr int CH = L::CH, NCH = L::NCH, ROWB = L::ROWB, OCTB = L::OCTB;
   constexpr int NT = D / 8;      // n8 tiles of the V columns
   constexpr int NH = NT / 2;     // n8 tiles per half (bounds the accumulator registers)
-  constexpr int KM = D / 32;     // 16-byte chunks per thread per head row (= k16 step pairs)
+  constexpr int KM = D / 32;     // 16-byte chunks per thread per head row
+  constexpr int NI = D / 16;     // 8-column TMEM blocks of one A part (= MMA k16 steps)
   constexpr int BPO = 8 / TMAX;  // beams per octet; staged row r = (token r / BPO, beam r % BPO)
+  constexpr long long kWait = 1ll << 31;
+  constexpr uint32_t kIdesc = tc::idesc_bf16(128, D, 0, 1);  // A (TMEM) x MN-major S0
   extern __shared__ __align__(16) unsigned char smem[];
   unsigned char* sS0 = smem;
   float* sTab = reinterpret_cast<float*>(smem + L::S0B);
   float* sNw = sTab + 8 * NCH;
   unsigned char* sStage = smem + L::S0B + L::TABB + L::NWB;
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(sStage + kMixWarps * 2 * OCTB);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(mbar + 1);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, tq = lane & 3;
@@ -186,12 +203,17 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
     }
   };
 
-  // ---- CTA prologue: S0 (swizzled), this warp's first octet, conv table, norm weight ----
+  // ---- CTA prologue: TMEM, S0 (B operand), this warp's first octet, conv table, norm weight ----
+  if (warp == 0) tc::tmem_alloc(tslot, L::TCOLS);
+  if (tid == 0) {
+    tc::mbar_init(mbar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
   {
     const __nv_bfloat16* s0 = a.state + (int64_t(b) * HV + hv) * D * D;
     for (int idx = tid; idx < D * CH; idx += blockDim.x) {
-      const int r = idx / CH, c = idx % CH;
-      cp_async16(sS0 + r * 2 * D + ((c ^ s0_swz(r)) << 4), s0 + r * D + c * 8);
+      const int r = idx / CH, c = idx % CH, kap = kappa_of(r);
+      cp_async16(sS0 + (kap >> 3) * L::KGRP + c * 128 + (kap & 7) * 16, s0 + r * D + c * 8);
     }
     cp_async_commit();
   }
@@ -218,19 +240,20 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
   }
   for (int i = tid; i < D; i += blockDim.x) sNw[i] = a.norm_weight[i];
   const float neg_a = -expf(a.a_log[hv]), dtb = a.dt_bias[hv];
-  cp_async_wait<1>();  // S0 landed (the octet copies may still be in flight)
+  cp_async_wait<1>();       // S0 landed (the octet copies may still be in flight)
+  tc::fence_async_smem();   // ... and visible to the tensor cores
+  tc::fence_before();
   __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t t_acc = tc::taddr(tmem, 32 * warp, 0);       // this warp's 16 lanes: q rows g, k rows 8 + g
+  const uint32_t t_hi = tc::taddr(tmem, 32 * warp, D), t_lo = tc::taddr(tmem, 32 * warp, D + D / 2);
+  bool ok = true;
 
-  // ldmatrix row offsets of this lane under the permuted k order, per k16 step parity
-  int rowoff[2], swz[2];
-#pragma unroll
-  for (int hh = 0; hh < 2; ++hh) {
-    const int j = lane & 15;
-    rowoff[hh] = 8 * ((j & 7) >> 1) + 4 * hh + 2 * (j >> 3) + (j & 1);
-    swz[hh] = s0_swz(rowoff[hh]);  // s0_swz(32m + r) == s0_swz(r)
-  }
-
-  for (int it = 0; it < noct; ++it) {
+  // Rounds: every warp takes part in each round's barrier; a warp past its last octet
+  // writes no A rows and reads nothing back (its TMEM lanes hold stale values).
+  for (int it = 0; it < octets_per_warp; ++it) {
+    const bool active = it < noct;
     unsigned char* buf = wbuf + (it & 1) * OCTB;
     if (it + 1 < noct) stage(oct0 + it + 1, wbuf + ((it + 1) & 1) * OCTB);
     cp_async_commit();
@@ -284,46 +307,71 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
       }
     }
 
-    // ---- [q ; k] x S0 on the tensor cores, recurrence, gated RMSNorm --------------------
+    // ---- A = [q ; k] (bf16 hi, lo) into TMEM; one thread runs the MMAs against S0 ---------
+#pragma unroll
+    for (int part = 0; part < 2; ++part) {
+      uint32_t ar[4 * NI];
+#pragma unroll
+      for (int m = 0; m < KM; ++m)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int i = 2 * m + hh;  // TMEM column block of channel pairs 2hh, 2hh + 1 of chunk 4m + tq
+          const float2 q0 = mul2(bf2f(qw[m][2 * hh]), make_float2(qs, qs));
+          const float2 q1 = mul2(bf2f(qw[m][2 * hh + 1]), make_float2(qs, qs));
+          const float2 k0 = mul2(bf2f(kw[m][2 * hh]), make_float2(ik, ik));
+          const float2 k1 = mul2(bf2f(kw[m][2 * hh + 1]), make_float2(ik, ik));
+          const uint32_t h0 = bf2_pack_f2(q0), h1 = bf2_pack_f2(q1), h2 = bf2_pack_f2(k0), h3 = bf2_pack_f2(k1);
+          if (part == 0) {
+            ar[4 * i + 0] = h0;
+            ar[4 * i + 1] = h1;
+            ar[4 * i + 2] = h2;
+            ar[4 * i + 3] = h3;
+          } else {
+            const float2 neg1 = make_float2(-1.f, -1.f);
+            ar[4 * i + 0] = bf2_pack_f2(fma2(bf2f(h0), neg1, q0));
+            ar[4 * i + 1] = bf2_pack_f2(fma2(bf2f(h1), neg1, q1));
+            ar[4 * i + 2] = bf2_pack_f2(fma2(bf2f(h2), neg1, k0));
+            ar[4 * i + 3] = bf2_pack_f2(fma2(bf2f(h3), neg1, k1));
+          }
+        }
+      if constexpr (NI == 8) {
+        if (part == 0) tc::st16x256b_x8(t_hi, ar); else tc::st16x256b_x8(t_lo, ar);
+      } else {
+        if (part == 0) tc::st16x256b_x4(t_hi, ar); else tc::st16x256b_x4(t_lo, ar);
+      }
+    }
+    tc::wait_st();
+    tc::fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc::fence_after();
+      const uint32_t sb = smem_u32(sS0);
+#pragma unroll
+      for (int part = 0; part < 2; ++part)
+#pragma unroll
+        for (int st = 0; st < NI; ++st)
+          tc::mma_bf16_ta(tmem, tmem + D + part * (D / 2) + 8 * st, tc::smem_desc(sb + st * 2 * L::KGRP, L::KGRP, 128),
+                          kIdesc, part > 0 || st > 0);
+      tc::commit(mbar);
+    }
+    if (!active) continue;
+    ok = tc::mbar_wait(mbar, uint32_t(it) & 1u, kWait) && ok;
+    tc::fence_after();
+
+    // ---- recurrence and gated RMSNorm over the accumulator, in two column halves ---------
     uint32_t ob[NT];
     float ss = 0.f;
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
       float acc[NH][4];
+      {
+        uint32_t r[4 * NH];
+        if constexpr (NH == 8) tc::ld16x256b_x8(t_acc + hf * 64, r); else tc::ld16x256b_x4(t_acc + hf * 32, r);
+        tc::wait_ld();
 #pragma unroll
-      for (int j = 0; j < NH; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+        for (int j = 0; j < NH; ++j)
 #pragma unroll
-      for (int m = 0; m < KM; ++m) {
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          // A rows: g = q of row g, g + 8 = k of row g; bf16 hi + lo parts
-          const float2 q0 = mul2(bf2f(qw[m][2 * hh]), make_float2(qs, qs));
-          const float2 q1 = mul2(bf2f(qw[m][2 * hh + 1]), make_float2(qs, qs));
-          const float2 k0 = mul2(bf2f(kw[m][2 * hh]), make_float2(ik, ik));
-          const float2 k1 = mul2(bf2f(kw[m][2 * hh + 1]), make_float2(ik, ik));
-          uint32_t ahi[4], alo[4];
-          ahi[0] = bf2_pack_f2(q0);
-          ahi[1] = bf2_pack_f2(k0);
-          ahi[2] = bf2_pack_f2(q1);
-          ahi[3] = bf2_pack_f2(k1);
-          const float2 neg1 = make_float2(-1.f, -1.f);
-          alo[0] = bf2_pack_f2(fma2(bf2f(ahi[0]), neg1, q0));
-          alo[1] = bf2_pack_f2(fma2(bf2f(ahi[1]), neg1, k0));
-          alo[2] = bf2_pack_f2(fma2(bf2f(ahi[2]), neg1, q1));
-          alo[3] = bf2_pack_f2(fma2(bf2f(ahi[3]), neg1, k1));
-          const unsigned char* brow = sS0 + (32 * m + rowoff[hh]) * 2 * D;
-#pragma unroll
-          for (int np = 0; np < NH / 2; ++np) {
-            const int chunk = hf * NH + 2 * np + (lane >> 4);
-            uint32_t bfr[4];
-            ldmatrix_x4_trans(bfr, brow + ((chunk ^ swz[hh]) << 4));
-            const uint32_t b0[2] = {bfr[0], bfr[1]}, b1[2] = {bfr[2], bfr[3]};
-            mma_bf16_16816(acc[2 * np], ahi, b0);
-            mma_bf16_16816(acc[2 * np + 1], ahi, b1);
-            mma_bf16_16816(acc[2 * np], alo, b0);
-            mma_bf16_16816(acc[2 * np + 1], alo, b1);
-          }
-        }
+          for (int e = 0; e < 4; ++e) acc[j][e] = __uint_as_float(r[4 * j + e]);
       }
       // columns (jj*8 + 2tq, +1): acc[j][0..1] = S0^T q, acc[j][2..3] = S0^T k of this row
 #pragma unroll
@@ -377,6 +425,13 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
     __syncwarp();
   }
   cp_async_wait<0>();
+  if (!ok && lane == 0) atomicOr(a.status, 1u);  // the MMA completion wait timed out
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after();
+    tc::tmem_free(tmem, L::TCOLS);
+  }
 }
 
 template <int D, int TMAX>
@@ -410,7 +465,7 @@ int launch_mixer(const MixerArgs& a, cudaStream_t stream) {
 bool gdn_mixer_staged_ok(const MixerArgs& a) {
   if (!(a.D == 64 || a.D == 128) || a.T < 1 || a.T > 2 || a.conv_hist < 3) return false;
   const auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-  return al16(a.proj) && al16(a.out) && al16(a.state) && a.ld_proj % 8 == 0 &&
+  return a.status != nullptr && al16(a.proj) && al16(a.out) && al16(a.state) && a.ld_proj % 8 == 0 &&
          (a.proj_prev == nullptr || (a.T == 2 && al16(a.proj_prev)));
 }
 

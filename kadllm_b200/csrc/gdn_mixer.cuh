@@ -24,10 +24,11 @@ struct MixerArgs {
   const __nv_bfloat16* proj_prev;  // [B*Wp, ld_proj] or null
   const int32_t* parent;           // [B*W]
   int Wp;
+  uint32_t* status;  // device status word: bit 0 set when a tensor-core wait timed out
 };
 
-// True when the staged kernel takes this call: D in {64, 128}, T <= 2 and
-// 16-byte aligned projection rows and output.
+// True when the staged kernel takes this call: D in {64, 128}, T <= 2,
+// 16-byte aligned projection rows and output, and a status word.
 bool gdn_mixer_staged_ok(const MixerArgs& a);
 int gdn_mixer_staged(const MixerArgs& a, cudaStream_t stream);
 

@@ -473,10 +473,10 @@ extern "C" int kadllm_gdn_mixer_replay(const void* proj, int64_t ld_proj, const 
                                        const float* a_log, const float* dt_bias, const float* norm_weight,
                                        float norm_eps, void* out, int64_t batch, int64_t beam_width,
                                        int64_t steps, int64_t heads, int64_t v_heads, int64_t k_dim,
-                                       int64_t v_dim, void* stream) {
+                                       int64_t v_dim, uint32_t* status, void* stream) {
   using namespace kb;
   if (int rc = check_common(batch, beam_width, steps, heads, v_heads, k_dim, v_dim)) return rc;
-  KB_REQUIRE(proj && conv_state && conv_weight && rec_state && a_log && dt_bias && norm_weight && out,
+  KB_REQUIRE(proj && conv_state && conv_weight && rec_state && a_log && dt_bias && norm_weight && out && status,
              KADLLM_EINVAL, "gdn mixer: null pointer");
   const int64_t conv_dim = 2 * heads * k_dim + v_heads * v_dim;
   KB_REQUIRE(conv_hist >= 3, KADLLM_EINVAL, "gdn mixer: conv state needs >= 3 taps");
@@ -499,6 +499,7 @@ extern "C" int kadllm_gdn_mixer_replay(const void* proj, int64_t ld_proj, const 
     m.a_log = a_log; m.dt_bias = dt_bias; m.norm_weight = norm_weight; m.norm_eps = norm_eps;
     m.out = static_cast<__nv_bfloat16*>(out);
     m.B = a.B; m.W = a.W; m.T = a.T; m.H = a.H; m.HV = a.HV; m.D = int(k_dim); m.scale = a.scale;
+    m.status = status;
     if (gdn_mixer_staged_ok(m)) return gdn_mixer_staged(m, static_cast<cudaStream_t>(stream));
   }
   return dispatch_gdn<true>(int(k_dim), int(v_dim), a, static_cast<cudaStream_t>(stream));
@@ -510,11 +511,11 @@ extern "C" int kadllm_gdn_mixer_continue(const void* proj_prev, const int32_t* p
                                         const float* a_log, const float* dt_bias, const float* norm_weight,
                                         float norm_eps, void* out, int64_t batch, int64_t beam_width,
                                         int64_t heads, int64_t v_heads, int64_t k_dim, int64_t v_dim,
-                                        void* stream) {
+                                        uint32_t* status, void* stream) {
   using namespace kb;
   if (int rc = check_common(batch, beam_width, 2, heads, v_heads, k_dim, v_dim)) return rc;
   KB_REQUIRE(proj_prev && parent && proj && conv_state && conv_weight && rec_state && a_log && dt_bias &&
-                 norm_weight && out,
+                 norm_weight && out && status,
              KADLLM_EINVAL, "gdn mixer (continuation): null pointer");
   KB_REQUIRE(prev_width >= 1 && prev_width < (int64_t(1) << 30), KADLLM_EINVAL,
              "gdn mixer (continuation): prev_width out of range");
@@ -532,6 +533,7 @@ extern "C" int kadllm_gdn_mixer_continue(const void* proj_prev, const int32_t* p
   m.B = int(batch); m.W = int(beam_width); m.T = 2; m.H = int(heads); m.HV = int(v_heads); m.D = int(k_dim);
   m.scale = 1.0f / sqrtf(float(k_dim));
   m.proj_prev = static_cast<const __nv_bfloat16*>(proj_prev); m.parent = parent; m.Wp = int(prev_width);
+  m.status = status;
   KB_REQUIRE(k_dim == v_dim && gdn_mixer_staged_ok(m), KADLLM_EUNSUPPORTED,
              "gdn mixer (continuation): head dims 64 / 128 (K == V), 16-byte aligned rows only");
   return gdn_mixer_staged(m, static_cast<cudaStream_t>(stream));

@@ -186,11 +186,13 @@ def case_mixer(gen, reps, T=1):
     dt = torch.rand(HV, device=dev, generator=gen)
     nw = torch.ones(K, device=dev)
     out = torch.empty(B * W * T, HV * K, device=dev, dtype=bf)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
     s = _lib.stream(dev)
 
     def run():
         _lib.call("kadllm_gdn_mixer_replay", proj.data_ptr(), ld, cs.data_ptr(), 4, cw.data_ptr(), rec.data_ptr(),
-                  al.data_ptr(), dt.data_ptr(), nw.data_ptr(), 1e-6, out.data_ptr(), B, W, T, H, HV, K, K, s)
+                  al.data_ptr(), dt.data_ptr(), nw.data_ptr(), 1e-6, out.data_ptr(), B, W, T, H, HV, K, K,
+                  status.data_ptr(), s)
 
     ms = _time(run, reps)
     R = B * W * T

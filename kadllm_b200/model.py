@@ -486,7 +486,7 @@ class HybridModel:
                           conv_state.shape[-1], m.conv_w.data_ptr(), rec.data_ptr(), m.a_log.data_ptr(),
                           m.dt_bias.data_ptr(), m.norm_w.data_ptr(), c.rms_norm_eps, out.data_ptr(), B, W, T,
                           c.linear_num_key_heads, c.linear_num_value_heads, c.linear_key_head_dim,
-                          c.linear_value_head_dim, s)
+                          c.linear_value_head_dim, self.status.data_ptr(), s)
                 if cache is not None:
                     cache[i] = P
                 self._gemm(out, m.w_out, resid=x)
@@ -573,7 +573,7 @@ class HybridModel:
                           P.stride(0), conv_state.data_ptr(), conv_state.shape[-1], m.conv_w.data_ptr(),
                           rec.data_ptr(), m.a_log.data_ptr(), m.dt_bias.data_ptr(), m.norm_w.data_ptr(),
                           c.rms_norm_eps, out.data_ptr(), B, W, c.linear_num_key_heads, c.linear_num_value_heads,
-                          c.linear_key_head_dim, c.linear_value_head_dim, s)
+                          c.linear_key_head_dim, c.linear_value_head_dim, self.status.data_ptr(), s)
                 self._gemm(out, m.w_out, resid=x)
             else:
                 q = torch.empty(R, 2, hq, D, dtype=BF16, device=self.device)

@@ -196,12 +196,15 @@ def _mixer_case(T, K, H, HV, B, W):
     nw = O.bf16(1 + 0.1 * rng.standard_normal(K).astype(np.float32))
     bf = torch.bfloat16
     out = torch.empty(BW * T, vd, dtype=bf, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
     tp = _t(proj, bf)
     args = [_t(conv_state, bf), _t(conv_w, bf), _t(rec, bf), _t(a_log, torch.float32),
             _t(dt_bias, torch.float32), _t(nw, torch.float32)]
     _lib.call("kadllm_gdn_mixer_replay", tp.data_ptr(), ld, args[0].data_ptr(), 4, args[1].data_ptr(),
               args[2].data_ptr(), args[3].data_ptr(), args[4].data_ptr(), args[5].data_ptr(), 1e-6,
-              out.data_ptr(), B, W, T, H, HV, K, K, _lib.stream(tp.device))
+              out.data_ptr(), B, W, T, H, HV, K, K, status.data_ptr(), _lib.stream(tp.device))
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
     # oracle chain (src/kadllm/adapters/qwen3_5.py:144-177)
     r = O.Rounding("bf16")
     P = proj.reshape(BW, T, ld)

@@ -41,18 +41,20 @@ def test_mixer_continue_equals_two_token_replay(K, H, HV, B, W, Wp):
     dt_bias = _t(O.bf16(rng.uniform(-1, 1, HV).astype(np.float32)), torch.float32)
     nw = _t(O.bf16(1 + 0.1 * rng.standard_normal(K).astype(np.float32)), torch.float32)
     s = _lib.stream(new.device)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
     # the full replay's rows (beam, t): t = 0 the parent's previous-step row, t = 1 the new row
     gidx = (torch.arange(B, device="cuda")[:, None] * Wp + parent.long()).reshape(-1)
     both = torch.stack([prev[gidx], new], 1).reshape(B * W * 2, ld).contiguous()
     full = torch.empty(B * W * 2, vd, dtype=bf, device="cuda")
     _lib.call("kadllm_gdn_mixer_replay", both.data_ptr(), ld, conv_state.data_ptr(), 4, conv_w.data_ptr(),
               rec.data_ptr(), a_log.data_ptr(), dt_bias.data_ptr(), nw.data_ptr(), 1e-6, full.data_ptr(), B, W, 2,
-              H, HV, K, K, s)
+              H, HV, K, K, status.data_ptr(), s)
     cont = torch.empty(B * W, vd, dtype=bf, device="cuda")
     _lib.call("kadllm_gdn_mixer_continue", prev.data_ptr(), parent.data_ptr(), Wp, new.data_ptr(), ld,
               conv_state.data_ptr(), 4, conv_w.data_ptr(), rec.data_ptr(), a_log.data_ptr(), dt_bias.data_ptr(),
-              nw.data_ptr(), 1e-6, cont.data_ptr(), B, W, H, HV, K, K, s)
+              nw.data_ptr(), 1e-6, cont.data_ptr(), B, W, H, HV, K, K, status.data_ptr(), s)
     torch.cuda.synchronize()
+    assert int(status.item()) == 0
     assert torch.equal(cont, full.view(B * W, 2, vd)[:, 1])
 
 
