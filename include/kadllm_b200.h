@@ -56,13 +56,15 @@ KADLLM_API int kadllm_abi_version(void);
  *   out   [BW, T, HV, V]  contiguous, x_dtype
  * BW = batch * beam_width; beams of request b are rows b*W .. b*W+W-1.
  * K == V in {32, 64, 128}; 1 <= T <= 8; HV % H == 0.  scale <= 0 -> K^-0.5.
+ * status: device uint32, bit 0 set when a tensor-core wait timed out (read it
+ * after the stream synchronises; the output is then invalid).
  * ------------------------------------------------------------------------ */
 KADLLM_API int kadllm_gated_delta_replay(const void* q, const void* k, const void* v, int x_dtype,
                               const void* log_decay, int decay_dtype, const void* beta,
                               int beta_dtype, const void* state, int state_dtype, void* out,
                               int64_t batch, int64_t beam_width, int64_t steps, int64_t heads,
                               int64_t v_heads, int64_t k_dim, int64_t v_dim, float scale,
-                              void* stream);
+                              uint32_t* status, void* stream);
 
 /* ------------------------------------------------------------------------
  * Fused GDN token mixer for beam decode (BF16): causal conv1d replay + SiLU,

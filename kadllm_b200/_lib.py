@@ -38,7 +38,7 @@ SIGNATURES: dict[str, list] = {
     "kadllm_beam_select": [P, I, L, P, P, P, P, P, P, P, L, L, L, L, L, L, P],
     "kadllm_beam_select_status": [P, L, L, P, P],
     "kadllm_beam_select_noalloc": [P, I, L, P, P, P, P, P, P, L, L, L, L, L, P],
-    "kadllm_gated_delta_replay": [P, P, P, I, P, I, P, I, P, I, P, L, L, L, L, L, L, L, F, P],
+    "kadllm_gated_delta_replay": [P, P, P, I, P, I, P, I, P, I, P, L, L, L, L, L, L, L, F, P, P],
     "kadllm_gdn_mixer_replay": [P, L, P, L, P, P, P, P, P, F, P, L, L, L, L, L, L, L, P, P],
     "kadllm_causal_conv1d_replay": [P, L, L, L, P, L, L, L, L, P, P, P, I, L, L, L, L, L, I, P],
     "kadllm_gemm": [P, L, P, L, P, L, P, L, L, L, L, L, I, P, P],

@@ -14,14 +14,23 @@
 // so the only K x V work is multiplying the beams' q_t / k_t rows by S0, which
 // runs on the tensor cores with S0 staged once in shared memory.
 //
-// Thread mapping: a warp owns 8 beams.  For step t its 16-row MMA tile is
-// [q_t of the 8 beams ; k_t of the 8 beams] (rows g and g+8 of the m16n8k16
-// fragment), so after the K loop thread (g, tq) holds S0^T q_t and S0^T k_t of
-// beam g for the columns {8j + 2tq, 8j + 2tq + 1}: the recurrence, the output
-// cast and (fused mixer) the gated RMSNorm are thread-local plus two quad
-// shuffles.  q/k are split into bf16 hi + lo parts (A = A_hi + A_lo, and S0 too
-// when it is not bf16), keeping ~16 mantissa bits in the products.  Earlier
-// steps' k_s and d_s (T > 1) live in a small per-warp shared-memory slab.
+// Thread mapping: a warp owns 8 beams, thread quad g one beam.  For step t the
+// warp's 16 rows [q_t of the 8 beams ; k_t of the 8 beams] go to tensor memory
+// (lanes 32w + g and 32w + 8 + g, 16x256b stores) and one thread runs the
+// CTA's tcgen05 MMAs (M = 128: the warps' row blocks, N = V) against S0 staged
+// once as an MN-major shared-memory operand; the 16x256b loads of the
+// accumulator give thread (g, tq) S0^T q_t and S0^T k_t of beam g for the
+// columns {8j + 2tq, 8j + 2tq + 1}: the recurrence, the output cast and (fused
+// mixer) the gated RMSNorm are thread-local plus two quad shuffles.  The warps
+// of a CTA advance in lock step, one (octet, step) per round.  q/k are split
+// into bf16 hi + lo parts (A = A_hi + A_lo, and S0 too when it is not bf16:
+// A_hi S_hi + A_lo S_hi + A_hi S_lo), keeping ~16 mantissa bits in the
+// products.  The contraction order is a bit permutation of the key index: the
+// thread's pairs at keys 16kk + 8hp + 2tq + {0, 1} sit in TMEM column
+// 8kk + 2tq + hp, i.e. MMA k index 16kk + 4tq + 2hp + {0, 1}, and S0's rows are
+// staged in that order.  Earlier steps' k_s and d_s (T > 1) live in a small
+// per-warp shared-memory slab.  The MMA completion wait is bounded and reports
+// through the status word.
 //
 // Fused mixer (kadllm_gdn_mixer_replay): q/k/v are produced on the fly by the
 // causal conv1d replay + SiLU from the packed projection row and the request's
@@ -30,6 +39,7 @@
 // through Qwen3_5RMSNormGated with z (transformers modeling_qwen3_5.py:175-190).
 #include "common.cuh"
 #include "gdn_mixer.cuh"
+#include "tcgen05.cuh"
 
 namespace kb {
 namespace {
@@ -63,6 +73,7 @@ struct GdnArgs {
   int state_split;  // 1: S0 needs a lo part (not bf16)
   void* out;
   int out_dtype;
+  uint32_t* status;
   int B, W, T, H, HV;
   float scale;
   int octets_per_warp;  // beam octets each warp processes (amortises the S0 staging)
@@ -70,9 +81,13 @@ struct GdnArgs {
 
 template <int DK, int DV>
 struct Layout {
-  static constexpr int SS = DV + 8;        // bf16 row stride of the staged state
-  static constexpr int NCH = 2 * DK + DV;  // conv channels of one (q head, k head, v head)
-  __host__ __device__ static size_t state_bytes(bool split) { return size_t(DK) * SS * 2 * (split ? 2 : 1); }
+  static constexpr int NCH = 2 * DK + DV;   // conv channels of one (q head, k head, v head)
+  static constexpr int KGRP = 16 * DV;      // bytes per group of 8 state rows in the operand image
+  static constexpr int IMG = DK * DV * 2;   // one bf16 operand image of S0
+  static constexpr int TCOLS = DV + DK;     // TMEM columns: accumulator, A hi, A lo
+  static_assert(TCOLS == 64 || TCOLS == 128 || TCOLS == 256, "TMEM allocation is a power of two");
+  // S0 image(s), then the mbarrier and the TMEM address slot (16 bytes)
+  __host__ __device__ static size_t state_bytes(bool split) { return size_t(IMG) * (split ? 2 : 1) + 16; }
   __host__ __device__ static size_t conv_bytes(bool fused) { return fused ? size_t(NCH) * 8 * 4 : 0; }
   // per warp: k_s (fp32) and d_s (fp32) of the steps before the last, plus the
   // current step's bf16 outputs (read back by the gated RMSNorm)
@@ -100,16 +115,25 @@ __device__ __forceinline__ float2 conv_pair(const float* tab, int c, int t, cons
 }
 
 // TMAX: compile-time bound on T (1, 2, 4 or 8) so the per-step loops carry no dead code.
+// MMA k index (B row) of key r = 16kk + 8hp + 2tq + d: 16kk + 4tq + 2hp + d.
+__device__ __forceinline__ int replay_kappa(int r) {
+  return (r & ~15) | (((r >> 3) & 1) << 1) | (((r >> 1) & 3) << 2) | (r & 1);
+}
+
 template <int DK, int DV, bool FUSED, int TMAX>
 __global__ void __launch_bounds__(128) gdn_replay_kernel(const GdnArgs a) {
   using Lt = Layout<DK, DV>;
-  constexpr int KK = DK / 16;  // k16 steps
+  constexpr int KK = DK / 16;  // k16 steps (= 8-column TMEM blocks of one A part)
   constexpr int NT = DV / 8;   // n8 tiles
+  constexpr long long kWait = 1ll << 31;
+  constexpr uint32_t kIdesc = tc::idesc_bf16(128, DV, 0, 1);  // A (TMEM) x MN-major S0
   extern __shared__ __align__(16) unsigned char smem[];
   const int nwarps = blockDim.x >> 5;
   const int T = a.T;
   unsigned char* p = smem;
-  __nv_bfloat16* sS = reinterpret_cast<__nv_bfloat16*>(p);
+  unsigned char* sS = p;  // S0 hi image [, lo image]
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(p + Lt::IMG * (a.state_split ? 2 : 1));
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(mbar + 1);
   p += Lt::state_bytes(a.state_split);
   float* sConv = reinterpret_cast<float*>(p);  // [NCH][8]
   p += Lt::conv_bytes(FUSED);
@@ -125,20 +149,29 @@ __global__ void __launch_bounds__(128) gdn_replay_kernel(const GdnArgs a) {
   const int conv_dim = 2 * key_dim + HV * DV;
   const int g = lane >> 2, tq = lane & 3;
 
-  // ---- stage S0 (bf16 hi [+ lo]) and the conv table -----------------------------------
+  // ---- TMEM, S0 (bf16 hi [+ lo] MN-major operand images) and the conv table ----------
+  if (warp == 0) tc::tmem_alloc(tslot, Lt::TCOLS);
+  if (tid == 0) {
+    tc::mbar_init(mbar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
   {
     const int64_t base = (int64_t(b) * HV + hv) * DK * DV;
-    __nv_bfloat16* sLo = sS + DK * Lt::SS;
-    for (int i = tid * 4; i < DK * DV; i += blockDim.x * 4) {
-      float f[4];
+    for (int i = tid * 8; i < DK * DV; i += blockDim.x * 8) {  // 8 consecutive V columns of one key row
+      float f[8];
       load4(a.state, base + i, a.state_dtype, f);
-      const int kr = i / DV, vc = i % DV;
+      load4(a.state, base + i + 4, a.state_dtype, f + 4);
+      const int kr = i / DV, kap = replay_kappa(kr);
+      const size_t off = size_t(kap >> 3) * Lt::KGRP + ((i % DV) >> 3) * 128 + (kap & 7) * 16;
+      uint32_t hi[4], lo[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const __nv_bfloat16 hi = __float2bfloat16_rn(f[e]);
-        sS[kr * Lt::SS + vc + e] = hi;
-        if (a.state_split) sLo[kr * Lt::SS + vc + e] = __float2bfloat16_rn(f[e] - __bfloat162float(hi));
+        hi[e] = pack_bf16(f[2 * e], f[2 * e + 1]);
+        const float2 hf = bf2f(hi[e]);
+        lo[e] = pack_bf16(f[2 * e] - hf.x, f[2 * e + 1] - hf.y);
       }
+      *reinterpret_cast<uint4*>(sS + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      if (a.state_split) *reinterpret_cast<uint4*>(sS + Lt::IMG + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     }
     if constexpr (FUSED) {
       for (int c = tid; c < Lt::NCH; c += blockDim.x) {
@@ -162,7 +195,16 @@ __global__ void __launch_bounds__(128) gdn_replay_kernel(const GdnArgs a) {
       }
     }
   }
+  tc::fence_async_smem();  // the operand images, visible to the tensor cores
+  tc::fence_before();
   __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t t_acc = tc::taddr(tmem, 32 * warp, 0);  // this warp's 16 lanes: q rows g, k rows 8 + g
+  const uint32_t t_hi = tc::taddr(tmem, 32 * warp, DV), t_lo = tc::taddr(tmem, 32 * warp, DV + DK / 2);
+  const uint32_t s_img = smem_u32(sS);
+  uint32_t round = 0;
+  bool ok = true;
 
   for (int oct = 0; oct < a.octets_per_warp; ++oct) {
   const int beam = ((blockIdx.y * nwarps + warp) * a.octets_per_warp + oct) * kBeamsPerWarp + g;
@@ -278,45 +320,52 @@ __global__ void __launch_bounds__(128) gdn_replay_kernel(const GdnArgs a) {
     constexpr int NH = NT / 2;
     float ss = 0.f;  // sum of squares of the bf16 outputs (fused gated norm)
     float* dcur = sD + (t * kBeamsPerWarp + g) * DV;
-    // A fragments of [q_t ; k_t] (rows g / g+8), split once into bf16 hi and lo parts
-    uint32_t ahi[KK][4], alo[KK][4];
+    // [q_t ; k_t] (lanes g / g + 8) into TMEM as bf16 hi and lo parts; thread 0 runs the MMAs
+    {
+      uint32_t ahi[4 * KK], alo[4 * KK];
 #pragma unroll
-    for (int kk = 0; kk < KK; ++kk) {
-      float hq[4], hk[4];
+      for (int kk = 0; kk < KK; ++kk)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        hq[e] = bf16r(qv[kk][e]);
-        hk[e] = bf16r(kv[kk][e]);
-      }
-      ahi[kk][0] = pack_bf16(hq[0], hq[1]);  // row g (q), k cols 2tq, 2tq+1
-      ahi[kk][1] = pack_bf16(hk[0], hk[1]);  // row g+8 (k)
-      ahi[kk][2] = pack_bf16(hq[2], hq[3]);  // row g, k cols 2tq+8, 2tq+9
-      ahi[kk][3] = pack_bf16(hk[2], hk[3]);
-      alo[kk][0] = pack_bf16(qv[kk][0] - hq[0], qv[kk][1] - hq[1]);
-      alo[kk][1] = pack_bf16(kv[kk][0] - hk[0], kv[kk][1] - hk[1]);
-      alo[kk][2] = pack_bf16(qv[kk][2] - hq[2], qv[kk][3] - hq[3]);
-      alo[kk][3] = pack_bf16(kv[kk][2] - hk[2], kv[kk][3] - hk[3]);
+        for (int hp = 0; hp < 2; ++hp) {  // TMEM column 8kk + 2tq + hp: keys 16kk + 8hp + 2tq + {0, 1}
+          const float q0 = qv[kk][2 * hp], q1 = qv[kk][2 * hp + 1];
+          const float k0 = kv[kk][2 * hp], k1 = kv[kk][2 * hp + 1];
+          const float hq0 = bf16r(q0), hq1 = bf16r(q1), hk0 = bf16r(k0), hk1 = bf16r(k1);
+          ahi[4 * kk + hp] = pack_bf16(hq0, hq1);
+          ahi[4 * kk + 2 + hp] = pack_bf16(hk0, hk1);
+          alo[4 * kk + hp] = pack_bf16(q0 - hq0, q1 - hq1);
+          alo[4 * kk + 2 + hp] = pack_bf16(k0 - hk0, k1 - hk1);
+        }
+      tc::st16x256b<KK>(t_hi, ahi);
+      tc::st16x256b<KK>(t_lo, alo);
     }
-    const int passes = a.state_split ? 3 : 2;
+    tc::wait_st();
+    tc::fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc::fence_after();
+      const int passes = a.state_split ? 3 : 2;  // A_hi S_hi, A_lo S_hi [, A_hi S_lo]
+      for (int pass = 0; pass < passes; ++pass)
+#pragma unroll
+        for (int kk = 0; kk < KK; ++kk)
+          tc::mma_bf16_ta(tmem, tmem + DV + (pass == 1 ? DK / 2 : 0) + 8 * kk,
+                          tc::smem_desc(s_img + (pass == 2 ? Lt::IMG : 0) + kk * 2 * Lt::KGRP, Lt::KGRP, 128),
+                          kIdesc, pass > 0 || kk > 0);
+      tc::commit(mbar);
+    }
+    ok = tc::mbar_wait(mbar, round & 1u, kWait) && ok;
+    ++round;
+    tc::fence_after();
 #pragma unroll 1
     for (int half = 0; half < 2; ++half) {
       float acc[NH][4];
+      {
+        uint32_t r[4 * NH];
+        tc::ld16x256b<NH>(t_acc + half * NH * 8, r);
+        tc::wait_ld();
 #pragma unroll
-      for (int j = 0; j < NH; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-      for (int pass = 0; pass < passes; ++pass) {
-        const __nv_bfloat16* sb = sS + (pass == 2 ? DK * Lt::SS : 0) + half * (DV / 2);
+        for (int j = 0; j < NH; ++j)
 #pragma unroll
-        for (int kk = 0; kk < KK; ++kk) {
-          const uint32_t* af = pass == 1 ? alo[kk] : ahi[kk];
-#pragma unroll
-          for (int np = 0; np < NH / 2; ++np) {
-            uint32_t bfr[4];
-            ldmatrix_x4_trans(bfr, sb + (kk * 16 + (lane & 15)) * Lt::SS + np * 16 + (lane >> 4) * 8);
-            const uint32_t b0[2] = {bfr[0], bfr[1]}, b1[2] = {bfr[2], bfr[3]};
-            mma_bf16_16816(acc[2 * np], af, b0);
-            mma_bf16_16816(acc[2 * np + 1], af, b1);
-          }
-        }
+          for (int e = 0; e < 4; ++e) acc[j][e] = __uint_as_float(r[4 * j + e]);
       }
 #pragma unroll
       for (int j = 0; j < NH; ++j) {
@@ -390,6 +439,13 @@ __global__ void __launch_bounds__(128) gdn_replay_kernel(const GdnArgs a) {
     __syncwarp();
   }
   }  // octets
+  if (!ok && lane == 0) atomicOr(a.status, 1u);  // an MMA completion wait timed out
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after();
+    tc::tmem_free(tmem, Lt::TCOLS);
+  }
 }
 
 template <int DK, int DV, bool FUSED, int TMAX>
@@ -451,18 +507,18 @@ extern "C" int kadllm_gated_delta_replay(const void* q, const void* k, const voi
                                          int beta_dtype, const void* state, int state_dtype, void* out,
                                          int64_t batch, int64_t beam_width, int64_t steps, int64_t heads,
                                          int64_t v_heads, int64_t k_dim, int64_t v_dim, float scale,
-                                         void* stream) {
+                                         uint32_t* status, void* stream) {
   using namespace kb;
   if (int rc = check_common(batch, beam_width, steps, heads, v_heads, k_dim, v_dim)) return rc;
   KB_REQUIRE(valid_dtype(x_dtype) && valid_dtype(decay_dtype) && valid_dtype(beta_dtype) &&
                  valid_dtype(state_dtype),
              KADLLM_EDTYPE, "gdn replay: unsupported dtype code");
-  KB_REQUIRE(q && k && v && log_decay && beta && state && out, KADLLM_EINVAL, "gdn replay: null pointer");
+  KB_REQUIRE(q && k && v && log_decay && beta && state && out && status, KADLLM_EINVAL, "gdn replay: null pointer");
   GdnArgs a{};
   a.q = q; a.k = k; a.v = v; a.x_dtype = x_dtype;
   a.g = log_decay; a.g_dtype = decay_dtype; a.beta = beta; a.beta_dtype = beta_dtype;
   a.state = state; a.state_dtype = state_dtype; a.state_split = state_dtype != KADLLM_BF16;
-  a.out = out; a.out_dtype = x_dtype;
+  a.out = out; a.out_dtype = x_dtype; a.status = status;
   a.B = int(batch); a.W = int(beam_width); a.T = int(steps); a.H = int(heads); a.HV = int(v_heads);
   a.scale = scale > 0.f ? scale : 1.0f / sqrtf(float(k_dim));
   return dispatch_gdn<false>(int(k_dim), int(v_dim), a, static_cast<cudaStream_t>(stream));
@@ -489,7 +545,7 @@ extern "C" int kadllm_gdn_mixer_replay(const void* proj, int64_t ld_proj, const 
   a.conv_weight = static_cast<const __nv_bfloat16*>(conv_weight);
   a.a_log = a_log; a.dt_bias = dt_bias; a.norm_weight = norm_weight; a.norm_eps = norm_eps;
   a.state = rec_state; a.state_dtype = KADLLM_BF16; a.state_split = 0;
-  a.out = out; a.out_dtype = KADLLM_BF16;
+  a.out = out; a.out_dtype = KADLLM_BF16; a.status = status;
   a.B = int(batch); a.W = int(beam_width); a.T = int(steps); a.H = int(heads); a.HV = int(v_heads);
   a.scale = 1.0f / sqrtf(float(k_dim));
   if (k_dim == v_dim) {

@@ -114,6 +114,16 @@ __device__ __forceinline__ void st16(uint32_t addr, const uint32_t (&r)[16]) {
 // m16n8 accumulator fragment layout: for column block i, thread t = 4 g + q holds
 // r[4i + e] = (lane g, column 8i + 2q + e) and r[4i + 2 + e] = (lane g + 8, same column),
 // e = 0, 1 (validated on B200 with a probe of the .16x256b shape).
+__device__ __forceinline__ void ld16x256b_x2(uint32_t addr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(addr));
+}
+__device__ __forceinline__ void st16x256b_x2(uint32_t addr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.16x256b.x2.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n" ::"r"(addr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
 __device__ __forceinline__ void ld16x256b_x4(uint32_t addr, uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.16x256b.x4.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
@@ -148,6 +158,20 @@ __device__ __forceinline__ void st16x256b_x8(uint32_t addr, const uint32_t (&r)[
       "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
       "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
+}
+
+// 16x256b load / store of N = 2, 4 or 8 column blocks (4 N registers).
+template <int N>
+__device__ __forceinline__ void ld16x256b(uint32_t addr, uint32_t (&r)[4 * N]) {
+  if constexpr (N == 2) ld16x256b_x2(addr, r);
+  else if constexpr (N == 4) ld16x256b_x4(addr, r);
+  else ld16x256b_x8(addr, r);
+}
+template <int N>
+__device__ __forceinline__ void st16x256b(uint32_t addr, const uint32_t (&r)[4 * N]) {
+  if constexpr (N == 2) st16x256b_x2(addr, r);
+  else if constexpr (N == 4) st16x256b_x4(addr, r);
+  else st16x256b_x8(addr, r);
 }
 
 // mbarrier helpers (CTA scope).

@@ -199,6 +199,25 @@ def case_mixer(gen, reps, T=1):
     return ms, "hbm", R * ld * 2 + R * HV * K * 2 + B * HV * K * K * 2 + B * C * 4 * 2
 
 
+def case_replay(gen, reps, T=2):
+    """ops.gated_delta (the reference's beam replay op) at the decode shape: 32 requests x
+    256 beams, 16 heads of 128, BF16 q / k / v, fp32 gates and state."""
+    from . import ops
+
+    dev, bf = torch.device("cuda"), torch.bfloat16
+    B, W, H, HV, K = 32, 256, 16, 16, 128
+    BW = B * W
+    q = torch.randn(BW, T, H, K, device=dev, generator=gen).to(bf)
+    k = torch.randn(BW, T, H, K, device=dev, generator=gen).to(bf)
+    v = torch.randn(BW, T, HV, K, device=dev, generator=gen).to(bf)
+    g = -torch.rand(BW, T, HV, device=dev, generator=gen)
+    beta = torch.rand(BW, T, HV, device=dev, generator=gen)
+    s0 = 0.1 * torch.randn(B, HV, K, K, device=dev, generator=gen)
+    ms = _time(lambda: ops.gated_delta(q, k, v, g, beta, s0, beam_width=W), reps)
+    ops.check(dev)
+    return ms, "hbm", BW * T * (2 * H + 2 * HV) * K * 2 + BW * T * HV * 4 * 2 + B * HV * K * K * 4
+
+
 def case_select(gen, reps):
     from .grbeam import BeamSelector
 
@@ -237,7 +256,7 @@ def case_gemm(gen, reps, M, N, K, epilogue=0):
 
 
 CASES = {"prefill": case_prefill, "attn_tiled": case_attn_tiled, "attn_split": case_attn_split, "conv": case_conv, "attn": case_attn, "mixer": case_mixer,
-         "mixer2": lambda g, r: case_mixer(g, r, T=2), "select": case_select,
+         "mixer2": lambda g, r: case_mixer(g, r, T=2), "select": case_select, "replay": case_replay,
          "attn_step": lambda g, r: case_attn_tiled(g, r, B=32, W=256, T=2, L=1024),
          "attn_causal": lambda g, r: case_attn_tiled(g, r, B=32, W=1, T=1, L=1024, causal=True),
          # the step's projections: prefill (32 x 1024 rows) and decode (32 x 256 beams, T = 1)

@@ -116,7 +116,8 @@ def gated_delta(
         q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.dtype_code(q),
         log_decay.data_ptr(), _lib.dtype_code(log_decay), beta.data_ptr(), _lib.dtype_code(beta),
         shared_state.data_ptr(), _lib.dtype_code(shared_state), out.data_ptr(),
-        BW // beam_width, beam_width, T, H, HV, K, V, scale, _lib.stream(q.device),
+        BW // beam_width, beam_width, T, H, HV, K, V, scale, _status_word(q.device).data_ptr(),
+        _lib.stream(q.device),
     )
     return out
 
@@ -264,6 +265,14 @@ _TILED_D = 256  # head dim of the tensor-core attention
 _status: dict = {}
 
 
+def _status_word(dev):
+    """The device's status word of the tensor-core operators (bit 0: a wait timed out)."""
+    status = _status.get(dev)
+    if status is None:
+        status = _status[dev] = torch.zeros(1, dtype=torch.int32, device=dev)
+    return status
+
+
 def _prefix_attention_tiled(q, prefix_k, prefix_v, suffix_k, suffix_v, out, B, W, T, H, HK, L, D, scale):
     """Head dim 256 without a mask: the tcgen05 attention over a tiled copy of the prefix
     (one re-layout of K / V per call), split over the key blocks when the request count
@@ -276,9 +285,7 @@ def _prefix_attention_tiled(q, prefix_k, prefix_v, suffix_k, suffix_v, out, B, W
     vt = torch.empty_like(kt)
     _lib.call("kadllm_kv_tile", prefix_k.data_ptr(), *prefix_k.stride()[:3], B, HK, L, D, kt.data_ptr(), nbytes, s)
     _lib.call("kadllm_kv_tile", prefix_v.data_ptr(), *prefix_v.stride()[:3], B, HK, L, D, vt.data_ptr(), nbytes, s)
-    status = _status.get(dev)
-    if status is None:
-        status = _status[dev] = torch.zeros(1, dtype=torch.int32, device=dev)
+    status = _status_word(dev)
     # CTAs of 128 query rows per (request, kv head); split the key blocks when they leave SMs idle
     ctas = -(-(W * T * (H // HK)) // 128) * B * HK
     sms = _sm_count(dev)

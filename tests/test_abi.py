@@ -50,9 +50,9 @@ def test_argument_errors_are_reported_without_a_gpu(library):
     lib = _lib.lib()
     # T = 9 exceeds the replay limit: rejected on the host, before any launch
     rc = lib.kadllm_gated_delta_replay(None, None, None, 2, None, 0, None, 0, None, 2, None,
-                                       1, 1, 9, 1, 1, 32, 32, 0.0, None)
+                                       1, 1, 9, 1, 1, 32, 32, 0.0, None, None)
     assert rc == 3
     assert b"suffix steps" in lib.kadllm_last_error()
     rc = lib.kadllm_gated_delta_replay(None, None, None, 7, None, 0, None, 0, None, 2, None,
-                                       1, 1, 1, 1, 1, 32, 32, 0.0, None)
+                                       1, 1, 1, 1, 1, 32, 32, 0.0, None, None)
     assert rc == 2
