@@ -185,20 +185,24 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
     return a.proj + ((int64_t(b) * a.W + beam) * TMAX + tr) * ld;
   };
   // Stage octet `oct` into `buf` (the caller commits the cp.async group).
+  // (lane r & 7 resolves row r's projection row once; the copies take it by shuffle: every
+  // lane's idx of one iteration lies in the same row)
   auto stage = [&](int oct, unsigned char* buf) {
+    const int rl = lane & 7, beam_l = oct * BPO + rl % BPO;
+    const bool ok_l = beam_l < a.W;
+    const long long prow_l = reinterpret_cast<long long>(prow_of(rl / BPO, ok_l ? beam_l : 0));
+#pragma unroll 4
     for (int idx = lane; idx < 8 * 4 * CH; idx += 32) {
       const int r = idx / (4 * CH), piece = (idx / CH) & 3, c = idx % CH;
-      const int beam = oct * BPO + r % BPO;
-      const bool ok = beam < a.W;
-      const __nv_bfloat16* prow = prow_of(r / BPO, ok ? beam : 0);
+      const bool ok = oct * BPO + r % BPO < a.W;
+      const __nv_bfloat16* prow = reinterpret_cast<const __nv_bfloat16*>(__shfl_sync(0xffffffffu, prow_l, r));
       const int col = piece < 2 ? (piece == 0 ? col_q : col_k) : (piece == 2 ? col_v : col_z);
       cp16z(buf + r * ROWB + piece * 2 * D + c * 16, prow + col + c * 8, ok);
     }
+    const __nv_bfloat16* prow = reinterpret_cast<const __nv_bfloat16*>(__shfl_sync(0xffffffffu, prow_l, lane >> 1));
     if (lane < 16) {
       const int r = lane >> 1, which = lane & 1;
-      const int beam = oct * BPO + r % BPO;
-      const bool ok = beam < a.W;
-      const __nv_bfloat16* prow = prow_of(r / BPO, ok ? beam : 0);
+      const bool ok = oct * BPO + r % BPO < a.W;
       cp4z(buf + r * ROWB + 8 * D + which * 4, prow + ((which ? col_a : col_b) & ~1), ok);
     }
   };

@@ -27,6 +27,8 @@
 //       cp.async, three barriers:
 //         [W; Q'] S (one pass over S)      Vn = U - W S,  O = Q' S  (Q' = e^G q)
 //         S <- e^{G_last} S + K'^T Vn      O += Aqk Vn -> gated RMSNorm -> out
+//       (the tensor-core scan normalises chunk c's output rows while chunk c + 1's
+//       first MMA runs)
 // S stays in fp32 MMA accumulators, with a BF16 copy in shared memory as the B
 // operand of the next chunk.
 #include "mma_tiles.cuh"
@@ -54,15 +56,15 @@ struct SplitArgs {
 };
 
 // One chunk's prep output in the workspace.  Dense rows, or (tc_layout, DK = DV =
-// 128) the tensor-core scan's shared-memory image: q, w, kp as one 128-row
-// K-major core-matrix tile [Q'; W] followed by K' (the same byte order read as
+// 128) the tensor-core scan's shared-memory image: w, q, kp as one 128-row
+// K-major core-matrix tile [W; Q'] followed by K' (the same byte order read as
 // MN-major), Aqk as a 64-wide K-major core tile, U as 256-byte rows with XOR-
-// swizzled 16-byte chunks; so the scan stages a chunk with two bulk copies.
+// swizzled 16-byte chunks; so the scan stages a chunk with one bulk copy.
 template <int DK, int DV>
 struct ChunkBlock {
-  static constexpr size_t q = 0;                           // [kC][DK] bf16, e^{G_i} q_i (normalised, scaled)
-  static constexpr size_t w = q + size_t(kC) * DK * 2;     // [kC][DK] bf16, T diag(beta e^G) K
-  static constexpr size_t kp = w + size_t(kC) * DK * 2;    // [kC][DK] bf16, e^{G_last - G_i} k_i
+  static constexpr size_t w = 0;                           // [kC][DK] bf16, T diag(beta e^G) K
+  static constexpr size_t q = w + size_t(kC) * DK * 2;     // [kC][DK] bf16, e^{G_i} q_i (normalised, scaled)
+  static constexpr size_t kp = q + size_t(kC) * DK * 2;    // [kC][DK] bf16, e^{G_last - G_i} k_i
   static constexpr size_t aqk = kp + size_t(kC) * DK * 2;  // [kC][kC] bf16
   static constexpr size_t u = aqk + size_t(kC) * kC * 2;   // [kC][DV] bf16, T diag(beta) V
   static constexpr size_t g = u + size_t(kC) * DV * 2;     // [kC] f32, cumulative log decay
@@ -85,6 +87,9 @@ __device__ __forceinline__ void seq_of(const SplitArgs& a, int b, int64_t& row0,
     len = a.L;
   }
 }
+
+// Named barrier `id` over the first n threads of the CTA.
+__device__ __forceinline__ void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(n) : "memory"); }
 
 template <int DK, int DV>
 size_t workspace_bytes(int64_t B, int64_t HV, int64_t L) {
@@ -464,6 +469,418 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const SplitArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// prep on the 5th-generation tensor cores (DK = DV = 128, tensor-core block layout)
+// ---------------------------------------------------------------------------
+// The chunk's raw (un-normalised) bf16 conv outputs k, q, v sit in shared-memory
+// images in the core-matrix layout [token/8][feature/8][token%8][16 bytes] with a
+// 144-byte feature-chunk stride (16-byte writes spread over the banks).  Read with
+// rows = tokens they are K-major operands (SBO 2304, LBO 144); read with K = tokens,
+// N = features they are MN-major operands (SBO 144, LBO 2304).  k and q are adjacent,
+// so [K; Q] is one 128-row operand:
+//   MMA1  [K; Q] K^T (M 128, N 64, K 128): K K^T and Q K^T, scaled afterwards by the
+//         inverse L2 norms (the products of the bf16 conv outputs are exact in fp32)
+//   MMA2  [T1; T2] K and [T1; T2] V (M 128, N 128, K 64): W = T1 K (rows 0-63 of the
+//         first), U = T2 V (rows 64-127 of the second), with T1 = T diag(beta e^G / |k|),
+//         T2 = T diag(beta).
+// Epilogues run a thread per TMEM lane (row) and write the chunk block straight to
+// global memory in the tensor-core scan's image order (coalesced 16-byte stores);
+// Q' and K' are scaled copies of the q / k images, exported by warps 4-7 while
+// warps 0-3 invert (I + L).
+struct PrepTc {
+  static constexpr int D = 128, NCH = 3 * D, RS = NCH + 8, SL = kC + 1;
+  static constexpr int CST = 144;       // feature-chunk stride of an image
+  static constexpr int GST = 16 * CST;  // 8-token group stride
+  static constexpr int IMG = 8 * GST;   // one 64-token image
+  static constexpr size_t raw_bytes = size_t(kC + 3) * RS * 2;  // staged projection tile (conv input)
+  // after the conv the raw region holds L / T (fp32), the merge scratch and [T1; T2]
+  static constexpr size_t l = 0;
+  static constexpr size_t tmp = l + size_t(kC) * SL * 4;
+  static constexpr size_t t12 = (tmp + size_t(32) * 33 * 4 + 127) / 128 * 128;  // K-major, SBO 1024, LBO 128
+  static constexpr size_t k = (raw_bytes + 127) / 128 * 128;  // images k | q | v
+  static constexpr size_t q = k + IMG;
+  static constexpr size_t v = q + IMG;
+  static constexpr size_t vec = v + IMG;  // 8 x [kC] fp32
+  static constexpr size_t cw = vec + size_t(8) * kC * 4;
+  static constexpr size_t bar = cw + size_t(NCH) * 4 * 2;
+  static constexpr size_t slot = bar + 8;
+  static constexpr size_t bytes = slot + 8;
+  static_assert(t12 + size_t(2 * kC) * kC * 2 <= raw_bytes, "[T1; T2] fits the raw region");
+  static_assert(bytes <= 115 * 1024, "two CTAs per SM");
+  __device__ static uint32_t img_off(int t, int ch) { return (t >> 3) * GST + ch * CST + (t & 7) * 16; }
+};
+
+__global__ void __launch_bounds__(256, 2) gdn_prep_tc_kernel(const SplitArgs a) {
+  using M = PrepTc;
+  using CB = ChunkBlock<128, 128>;
+  constexpr int D = M::D, NCH = M::NCH, RS = M::RS, SL = M::SL, NT = 256;
+  constexpr long long kWait = 1ll << 31;
+  constexpr uint32_t kId1 = tc::idesc_bf16(128, kC, 0, 0);  // [K; Q] K^T: both K-major
+  constexpr uint32_t kId2 = tc::idesc_bf16(128, D, 0, 1);   // [T1; T2] (K-major) x K | V (MN-major)
+  extern __shared__ __align__(16) unsigned char smem[];
+  __nv_bfloat16* sRawT = reinterpret_cast<__nv_bfloat16*>(smem);  // [kC + 3][RS]
+  float* sL = reinterpret_cast<float*>(smem + M::l);
+  float* sTmp = reinterpret_cast<float*>(smem + M::tmp);
+  unsigned char* sKi = smem + M::k;
+  unsigned char* sQi = smem + M::q;
+  float* sG = reinterpret_cast<float*>(smem + M::vec);
+  float* sBeta = sG + kC;
+  float* sRaw = sBeta + kC;
+  float* sEG = sRaw + kC;   // e^{G_i}
+  float* sW1 = sEG + kC;    // beta_i e^{G_i} / |k_i|: the columns of T1
+  float* sEGL = sW1 + kC;   // e^{G_last - G_i}
+  float* sIq = sEGL + kC;   // |q_i|^2, then scale / |q_i|
+  float* sIk = sIq + kC;    // |k_i|^2, then 1 / |k_i|
+  __nv_bfloat16* sCw = reinterpret_cast<__nv_bfloat16*>(smem + M::cw);
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + M::bar);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + M::slot);
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int c = blockIdx.x;
+  const int bh = blockIdx.y, b = bh / a.HV, hv = bh % a.HV, h = hv / (a.HV / a.H);
+  const int key_dim = a.H * D, conv_dim = 2 * key_dim + a.HV * D;
+  const int t0 = c * kC;
+  auto chan = [&](int lc) {  // head-local channel -> projection column
+    return lc < D ? h * D + lc : (lc < 2 * D ? key_dim + h * D + (lc - D) : 2 * key_dim + hv * D + (lc - 2 * D));
+  };
+  int64_t seq0;
+  int L;
+  seq_of(a, b, seq0, L);
+  if (t0 >= L) return;  // past this request's last chunk (varlen): the whole CTA, before any barrier
+  const __nv_bfloat16* prow0 = a.proj + seq0 * a.ld_proj;
+  unsigned char* blk = a.blocks + (int64_t(bh) * a.nc + c) * CB::bytes;
+
+  // ---- stage the raw projection tile (tokens t0-3 .. t0+63, zero outside [0, L)) -----
+  {
+    constexpr int CPR = NCH / 8, GRP = NT / CPR;
+    if (tid < GRP * CPR) {
+      const int lc = (tid % CPR) * 8;
+      const __nv_bfloat16* src = prow0 + chan(lc);
+      __nv_bfloat16* dst = sRawT + lc;
+      for (int r = tid / CPR; r < kC + 3; r += GRP) {
+        const int t = t0 - 3 + r;
+        if (t >= 0 && t < L) cp_async16(dst + r * RS, src + int64_t(t) * a.ld_proj);
+        else *reinterpret_cast<uint4*>(dst + r * RS) = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+    for (int i = tid; i < NCH / 2; i += NT) cp_async16(sCw + i * 8, a.conv_w + int64_t(chan(2 * i)) * 4);
+  }
+  cp_async_commit();
+  float gb = 0.f, ga = 0.f;  // gate inputs of token t0 + tid
+  if (tid < kC && t0 + tid < L) {
+    const __nv_bfloat16* pr = prow0 + int64_t(t0 + tid) * a.ld_proj + conv_dim + int64_t(a.HV) * D;
+    gb = __bfloat162float(pr[hv]);
+    ga = __bfloat162float(pr[a.HV + hv]);
+  }
+  if (warp == 0) tc::tmem_alloc(tslot, 256);
+  if (tid == 0) {
+    tc::mbar_init(mbar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  cp_async_wait<0>();
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t sb = smem_u32(smem);
+
+  // ---- conv + SiLU into the k | q | v images; squared norms of q and k rows ---------
+  // 48 groups of 8 channels x 16 segments of 4 tokens = 3 items a thread; a half-warp's
+  // 16 items are the 16 groups of one of q / k / v for one segment
+  {
+    constexpr int NG = NCH / 8, SEG = 4;
+    static_assert(NG * (kC / SEG) == 3 * NT, "every thread takes the same number of items");
+    for (int item = tid; item < NG * (kC / SEG); item += NT) {
+      const int grp = item % NG, seg = item / NG;
+      const int lc = grp * 8, part = grp / (D / 8);  // 0: q, 1: k, 2: v
+      float2 w2[4][4];
+      {
+        const uint4* wp = reinterpret_cast<const uint4*>(sCw + lc * 4);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint4 raw = wp[u];
+          const float2 c0a = bf2f(raw.x), c0b = bf2f(raw.y), c1a = bf2f(raw.z), c1b = bf2f(raw.w);
+          w2[u][0] = make_float2(c0a.x, c1a.x);
+          w2[u][1] = make_float2(c0a.y, c1a.y);
+          w2[u][2] = make_float2(c0b.x, c1b.x);
+          w2[u][3] = make_float2(c0b.y, c1b.y);
+        }
+      }
+      auto row4 = [&](int r, float2 (&v)[4]) {
+        const uint4 u = *reinterpret_cast<const uint4*>(sRawT + r * RS + lc);
+        v[0] = bf2f(u.x);
+        v[1] = bf2f(u.y);
+        v[2] = bf2f(u.z);
+        v[3] = bf2f(u.w);
+      };
+      const int r0 = seg * SEG;
+      float2 win[3][4];
+      row4(r0, win[0]);
+      row4(r0 + 1, win[1]);
+      row4(r0 + 2, win[2]);
+      unsigned char* img = smem + (part == 0 ? M::q : (part == 1 ? M::k : M::v));
+      const int ch = grp % (D / 8);
+      float ssq[SEG];
+#pragma unroll
+      for (int rr = 0; rr < SEG; ++rr) {
+        const int r = r0 + rr;
+        float2 x[4];
+        row4(r + 3, x);
+        uint4 u = make_uint4(0u, 0u, 0u, 0u);
+        float2 s2 = make_float2(0.f, 0.f);
+        if (t0 + r < L) {
+          uint32_t* uw = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+          for (int pp = 0; pp < 4; ++pp) {
+            float2 acc = mul2(win[0][pp], w2[pp][0]);
+            acc = fma2(win[1][pp], w2[pp][1], acc);
+            acc = fma2(win[2][pp], w2[pp][2], acc);
+            acc = fma2(x[pp], w2[pp][3], acc);
+            uw[pp] = bf2_pack_f2(silu2(acc));
+            const float2 o = bf2f(uw[pp]);
+            s2 = fma2(o, o, s2);
+          }
+        }
+        ssq[rr] = s2.x + s2.y;
+        *reinterpret_cast<uint4*>(img + M::img_off(r, ch)) = u;
+#pragma unroll
+        for (int pp = 0; pp < 4; ++pp) {
+          win[0][pp] = win[1][pp];
+          win[1][pp] = win[2][pp];
+          win[2][pp] = x[pp];
+        }
+      }
+#pragma unroll
+      for (int rr = 0; rr < SEG; ++rr)
+#pragma unroll
+        for (int m = 1; m < 16; m <<= 1) ssq[rr] += __shfl_xor_sync(0xffffffffu, ssq[rr], m);
+      if ((lane & 15) == 0 && part < 2)
+#pragma unroll
+        for (int rr = 0; rr < SEG; ++rr) (part == 0 ? sIq : sIk)[r0 + rr] = ssq[rr];
+    }
+  }
+  if (t0 + kC >= L) {  // last chunk: conv state = pre-conv columns of tokens L-4 .. L-1
+    for (int lc = tid; lc < NCH; lc += NT) {
+      __nv_bfloat16 s4[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s4[j] = sRawT[(L - 1 - t0 + j) * RS + lc];
+      *reinterpret_cast<uint2*>(a.conv_state + (int64_t(b) * conv_dim + chan(lc)) * 4) = *reinterpret_cast<uint2*>(s4);
+    }
+  }
+  if (tid < kC) {  // gates
+    float g = 0.f, be = 0.f;
+    if (t0 + tid < L) {
+      be = bf16r(sigmoid_f(gb));
+      g = -expf(a.a_log[hv]) * softplus_f(ga + a.dt_bias[hv]);
+    }
+    sRaw[tid] = g;
+    sBeta[tid] = be;
+  }
+  tc::fence_async_smem();  // the images -> tensor cores
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+
+  // ---- MMA1 (one thread) while the others finish norms, gates and decays --------------
+  if (tid == 0) {
+#pragma unroll
+    for (int s = 0; s < D / 16; ++s) {
+      const uint64_t d = tc::smem_desc(sb + M::k + s * 2 * M::CST, M::CST, M::GST);
+      tc::mma_bf16(tmem, d, d, kId1, s > 0);
+    }
+    tc::commit(mbar);
+  }
+  if (tid < 2 * kC) {
+    const int r = tid & (kC - 1);
+    if (tid < kC) sIq[r] = a.scale / sqrtf(sIq[r] + 1e-6f);
+    else sIk[r] = 1.0f / sqrtf(sIk[r] + 1e-6f);
+  } else if (warp == 4) {  // in-chunk cumulative log decay (warp scan over 64 values)
+    const float v0 = sRaw[2 * lane], v1 = sRaw[2 * lane + 1];
+    float run = v0 + v1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, run, o);
+      if (lane >= o) run += y;
+    }
+    const float excl = run - (v0 + v1);
+    sG[2 * lane] = excl + v0;
+    sG[2 * lane + 1] = excl + v0 + v1;
+  }
+  __syncthreads();
+  if (tid < kC) {
+    const float e = __expf(sG[tid]);
+    sEG[tid] = e;
+    sW1[tid] = sBeta[tid] * e * sIk[tid];
+    sEGL[tid] = __expf(sG[kC - 1] - sG[tid]);
+  }
+  __syncthreads();
+
+  // ---- MMA1 epilogue: L = strictly-lower(beta_i K K^T o e^{G_i - G_j}) (fp32, shared),
+  //      Aqk = lower(Q K^T o e^{G_i - G_j}) (bf16, to the block), a thread per row --------
+  bool ok = tc::mbar_wait(mbar, 0, kWait);
+  tc::fence_after();
+  {
+    const int quad = warp & 3, hc = warp >> 2;  // TMEM lanes 32 quad .., columns 32 hc ..
+    const int i = (quad * 32 + lane) & (kC - 1);
+    uint32_t v[32];
+    tc::ld32(tc::taddr(tmem, quad * 32, hc * 32), v);
+    tc::wait_ld();
+    const float Gi = sG[i];
+    if (quad < 2) {  // K K^T row i
+      const float f = sBeta[i] * sIk[i];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const int j = hc * 32 + e;
+        sL[i * SL + j] = j < i ? f * sIk[j] * __uint_as_float(v[e]) * __expf(Gi - sG[j]) : 0.f;
+      }
+    } else {  // Q K^T row i -> the block's 64-wide K-major core tile
+      const float f = sIq[i];
+      uint32_t pk[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int j = hc * 32 + 2 * e;
+        const float x0 = j <= i ? f * sIk[j] * __uint_as_float(v[2 * e]) * __expf(Gi - sG[j]) : 0.f;
+        const float x1 = j + 1 <= i ? f * sIk[j + 1] * __uint_as_float(v[2 * e + 1]) * __expf(Gi - sG[j + 1]) : 0.f;
+        pk[e] = bf2_pack(x0, x1);
+      }
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4)
+        *reinterpret_cast<uint4*>(blk + CB::aqk + (i >> 3) * 1024 + (hc * 4 + q4) * 128 + (i & 7) * 16) =
+            make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+    }
+  }
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+
+  if (warp < 4) {
+    // ---- T = (I + L)^-1 (warps 0-3, named barrier 1) ---------------------------------
+    if (tid < kC) {  // diagonal 16x16 blocks: lane (block, column j) forward-substitutes column j
+      const int d0 = (tid >> 4) * 16, j = tid & 15;
+      const float* Lb = sL + d0 * SL + d0;
+      float t[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float acc = 0.f;
+#pragma unroll
+        for (int m = 0; m < i; ++m) acc = fmaf(Lb[i * SL + m], t[m], acc);
+        t[i] = i < j ? 0.f : (i == j ? 1.f : -acc);
+      }
+      __syncwarp();
+#pragma unroll
+      for (int i = 1; i < 16; ++i)
+        if (i > j) sL[(d0 + i) * SL + d0 + j] = t[i];
+    }
+    named_bar(1, 128);
+    if (tid < kC) sL[tid * SL + tid] = 1.f;
+    named_bar(1, 128);
+    {  // level 1 (16x16 blocks, TF32): T_10 = -T_11 (L_10 T_00), T_32 = -T_33 (L_32 T_22)
+      const int bp = warp >> 1, nc8 = warp & 1;
+      const int r0 = 16 + 32 * bp, c0 = 32 * bp;
+      float acc[1][4];
+      zero_acc<1>(acc);
+      warp_mma_tf32<16, 1>(acc, sL + r0 * SL + c0, SL, sL + c0 * SL + c0 + nc8 * 8, SL);
+      store_acc<1>(sTmp + bp * 16 * 33 + nc8 * 8, 33, acc, 1.f);
+      named_bar(1, 128);
+      zero_acc<1>(acc);
+      warp_mma_tf32<16, 1>(acc, sL + r0 * SL + r0, SL, sTmp + bp * 16 * 33 + nc8 * 8, 33);
+      named_bar(1, 128);
+      store_acc<1>(sL + r0 * SL + c0 + nc8 * 8, SL, acc, -1.f);
+    }
+    named_bar(1, 128);
+    {  // level 2 (32x32 blocks): T_[2:4][0:2] = -T_D (C T_A) with C = L[32:64, 0:32]
+      const int mt = warp >> 1, nh = warp & 1;
+      float acc[2][4];
+      zero_acc<2>(acc);
+      warp_mma_tf32<32, 2>(acc, sL + (32 + mt * 16) * SL, SL, sL + nh * 16, SL);
+      store_acc<2>(sTmp + mt * 16 * 33 + nh * 16, 33, acc, 1.f);
+      named_bar(1, 128);
+      zero_acc<2>(acc);
+      warp_mma_tf32<32, 2>(acc, sL + (32 + mt * 16) * SL + 32, SL, sTmp + nh * 16, 33);
+      named_bar(1, 128);
+      store_acc<2>(sL + (32 + mt * 16) * SL + nh * 16, SL, acc, -1.f);
+    }
+  } else {
+    // ---- warps 4-7: Q' = e^{G_i} scale q_i / |q_i| and K' = e^{G_last - G_i} k_i / |k_i| -------
+    const int t = tid - 128, i = t & (kC - 1);
+    const bool isk = t >= kC;
+    const unsigned char* src = isk ? sKi : sQi;
+    unsigned char* dst = blk + (isk ? CB::kp : CB::q) + (i >> 3) * 2048 + (i & 7) * 16;
+    const float f = isk ? sEGL[i] * sIk[i] : sEG[i] * sIq[i];
+#pragma unroll 4
+    for (int ch = 0; ch < D / 8; ++ch) {
+      uint4 raw = *reinterpret_cast<const uint4*>(src + M::img_off(i, ch));
+      uint32_t* w = reinterpret_cast<uint32_t*>(&raw);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) w[e] = bf2_pack_f2(mul2(bf2f(w[e]), make_float2(f, f)));
+      *reinterpret_cast<uint4*>(dst + ch * 128) = raw;
+    }
+  }
+  __syncthreads();
+
+  // ---- [T1; T2] as a K-major core tile (rows i, K = tokens j) ---------------------------
+  for (int u = tid; u < 2 * kC * (kC / 8); u += NT) {
+    const int i = (u & 7) | ((u >> 6) << 3), jc = (u >> 3) & 7;
+    const int ti = i & (kC - 1);
+    const float* fac = i >= kC ? sBeta : sW1;
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int j = jc * 8 + 2 * e;
+      const float v0 = ti >= j ? sL[ti * SL + j] : 0.f;
+      const float v1 = ti >= j + 1 ? sL[ti * SL + j + 1] : 0.f;
+      w[e] = bf2_pack(v0 * fac[j], v1 * fac[j + 1]);
+    }
+    *reinterpret_cast<uint4*>(smem + M::t12 + (i >> 3) * 1024 + jc * 128 + (i & 7) * 16) =
+        make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  tc::fence_async_smem();
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  if (tid == 0) {  // MMA2: [T1; T2] K -> columns 0..127, [T1; T2] V -> columns 128..255
+#pragma unroll
+    for (int s = 0; s < kC / 16; ++s) {
+      const uint64_t ad = tc::smem_desc(sb + M::t12 + s * 256, 128, 1024);
+      tc::mma_bf16(tmem, ad, tc::smem_desc(sb + M::k + s * 2 * M::GST, M::GST, M::CST), kId2, s > 0);
+      tc::mma_bf16(tmem + 128, ad, tc::smem_desc(sb + M::v + s * 2 * M::GST, M::GST, M::CST), kId2, s > 0);
+    }
+    tc::commit(mbar);
+  }
+  if (tid < kC / 4) reinterpret_cast<float4*>(blk + CB::g)[tid] = reinterpret_cast<const float4*>(sG)[tid];
+  ok = tc::mbar_wait(mbar, 1, kWait) && ok;
+  tc::fence_after();
+  {  // W = rows 0..63 of [T1; T2] K (quadrants 0, 1); U = rows 64..127 of [T1; T2] V (2, 3)
+    const int quad = warp & 3, hc = warp >> 2;
+    const int i = (quad * 32 + lane) & (kC - 1);
+    const bool isu = quad >= 2;
+#pragma unroll
+    for (int piece = 0; piece < 2; ++piece) {
+      uint32_t v[32];
+      tc::ld32(tc::taddr(tmem, quad * 32, (isu ? 128 : 0) + hc * 64 + piece * 32), v);
+      tc::wait_ld();
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        const int ch = hc * 8 + piece * 4 + q4;
+        uint4 res;
+        uint32_t* rw = reinterpret_cast<uint32_t*>(&res);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          rw[e] = bf2_pack(__uint_as_float(v[q4 * 8 + 2 * e]), __uint_as_float(v[q4 * 8 + 2 * e + 1]));
+        if (isu) *reinterpret_cast<uint4*>(blk + CB::u + i * 256 + ((ch ^ (i & 7)) * 16)) = res;
+        else *reinterpret_cast<uint4*>(blk + CB::w + (i >> 3) * 2048 + ch * 128 + (i & 7) * 16) = res;
+      }
+    }
+  }
+  if (!ok && lane == 0) atomicOr(a.status, 1u);  // an MMA completion wait timed out
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after();
+    tc::tmem_free(tmem, 256);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // scan
 // ---------------------------------------------------------------------------
 template <int DK, int DV>
@@ -632,97 +1049,89 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_kernel(const SplitArgs a) {
 
 // ---------------------------------------------------------------------------
 // scan on the 5th-generation tensor cores (DK = DV = 128): S and the chunk
-// products live in tensor memory.  8 warps: warp w reads TMEM lane quadrant
+// products live in tensor memory.  Warps 0-7: warp w reads TMEM lane quadrant
 // w % 4, columns [64 (w / 4), +64).
 //   TMEM columns [0, 128): S (lane = key row);  [128, 256): P / O (lane = row)
-//   MMA1  P  = [Q'; W] S          (M 128 = 64 Q' rows + 64 W rows, K = 128)
-//   V warps (quadrants 2, 3): Vn = U - W S -> shared memory (MN-major B operand)
+//   MMA1  P  = [W; Q'] S          (M 128 = 64 W rows + 64 Q' rows, K = 128)
+//   V warps (quadrants 0, 1): Vn = U - W S -> shared memory (MN-major B operand)
 //   MMA2  S (+)= K'^T Vn          (M = 128 key rows, K = 64 tokens)
-//   MMA3  P += [Aqk; 0] Vn        (rows 0..63 become O; zero rows keep M = 128)
-//   all warps: S -> BF16 copy (next MMA1's B operand), then S *= e^{G_last} of
-//   the next chunk; O warps (quadrants 0, 1) read O, and run its gated-RMSNorm
-//   epilogue during the next chunk's MMA1 -> Vn -> MMA2/3.
-// The MMA issuer is thread 64 (a V warp).  mbarriers: bar1 (MMA1) and bar2
+//   MMA3  P += [any; Aqk] Vn      (rows 64..127 become O; rows 0..63 land in the
+//                                  consumed W lanes, so no zero rows are staged)
+//   warps 0-7: S -> BF16 copy (next MMA1's B operand), then S *= e^{G_last} of
+//   the next chunk; O warps (quadrants 2, 3) stash BF16 O and its row sums of
+//   squares in shared memory, and warps 8-11 run the gated RMSNorm on the stash
+//   during the next chunk's MMA1 -> Vn -> MMA2/3.
+// The MMA issuer is thread 0 (a V warp).  mbarriers: bar1 (MMA1) and bar2
 // (MMA2/3) complete once per chunk, so parity c & 1 names the chunk's phase.
 // ---------------------------------------------------------------------------
 struct TcScan {
   static constexpr int D = 128;
   using CB = ChunkBlock<128, 128>;
-  // one stage = the chunk block's image (copy 1: q | w | kp | aqk, copy 2: u) plus the zero
-  // rows of [Aqk; 0]
-  static constexpr size_t a1 = 0;                          // [Q'; W] K-major core tile, 128 rows x K 128
+  // one stage = the chunk block's image up to G (one bulk copy): w | q | kp | aqk | u
+  static constexpr size_t a1 = CB::w;                      // [W; Q'] K-major core tile, 128 rows x K 128
   static constexpr size_t a2 = CB::kp;                     // K' MN-major, M 128 (keys) x K 64 (tokens)
-  static constexpr size_t a3 = CB::aqk;                    // [Aqk; 0] K-major, 128 rows x K 64
-  static constexpr size_t zero = a3 + size_t(kC) * kC * 2; // rows 64..127 of [Aqk; 0]
-  static constexpr size_t u = zero + size_t(kC) * kC * 2;  // U: 256-byte rows, XOR-swizzled chunks
-  static constexpr size_t copy1 = CB::u;                   // bytes of copy 1 (block offset 0 -> stage 0)
-  static constexpr size_t copy2 = size_t(kC) * D * 2;      // bytes of copy 2 (block u -> stage u)
-  static constexpr size_t stage = u + copy2;
+  // [any; Aqk] K-major, 128 rows x K 64: rows 0..63 are K' bytes, whose products land in
+  // the TMEM lanes of the W rows, already consumed when that MMA runs
+  static constexpr size_t a3 = CB::aqk - size_t(kC) * kC * 2;
+  static constexpr size_t u = CB::u;                       // U: 256-byte rows, XOR-swizzled chunks
+  static constexpr size_t stage = CB::g;                   // bytes of a stage (= of its copy)
   static constexpr size_t b1 = 2 * stage;                  // S (bf16) MN-major, K 128 (keys) x N 128
   static constexpr size_t b2 = b1 + size_t(D) * D * 2;     // Vn MN-major, K 64 (tokens) x N 128
+  static constexpr size_t ost = b2 + size_t(kC) * D * 2;   // O stash [64][128] bf16, 16-byte chunks XOR (row % 8)
   static constexpr int kGMax = 1024;                       // chunks whose last decay is preloaded
-  static constexpr size_t gl = b2 + size_t(kC) * D * 2;    // [kGMax] fp32 G_last of every chunk
+  static constexpr size_t gl = ost + size_t(kC) * D * 2;   // [kGMax] fp32 G_last of every chunk
   static constexpr size_t bar = gl + size_t(kGMax) * 4;    // mbarriers: MMA1, MMA2/3, stage 0, stage 1
   static constexpr size_t slot = bar + 4 * 8;              // TMEM base address
-  static constexpr size_t bytes = slot + 8;
-  static_assert(a3 + size_t(kC) * kC * 2 == CB::u && copy1 % 16 == 0 && stage % 16 == 0 && bar % 8 == 0,
+  static constexpr size_t nw = slot + 16;                  // [128] fp32 norm weight
+  static constexpr size_t nss = nw + size_t(D) * 4;        // [64][2] fp32 O row-half sums of squares
+  static constexpr size_t bytes = nss + size_t(kC) * 2 * 4;
+  static_assert(a1 == 0 && CB::q == size_t(kC) * D * 2 && stage % 16 == 0 && bar % 8 == 0 && nw % 16 == 0,
                 "stage image");
   static_assert(bytes <= 232448, "shared memory");
   // core-matrix byte offset of (row, 16-byte chunk) in 128-wide tiles (SBO 2048, LBO 128)
   __device__ static uint32_t off16(int r, int ch) { return (r >> 3) * 2048 + ch * 128 + (r & 7) * 16; }
-  // U row r, chunk ch: rows of 256 bytes, chunk index XOR (r % 8)
+  // U row r, chunk ch: rows of 256 bytes, chunk index XOR (r % 8); the O stash likewise
   __device__ static uint32_t offu(int r, int ch) { return r * 256 + ((ch ^ (r & 7)) * 16); }
 };
 
-__device__ __forceinline__ void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(n) : "memory"); }
-
-// Gated RMSNorm of the layer output in place (after the tensor-core scan stored
-// BF16 O there): one warp per (row, value head) of 128, 4 columns a lane.
+// Gated RMSNorm of one O row half (64 columns, BF16 in `ob`) of the tensor-core scan:
 //   out = bf16( bf16(w * bf16(o * rsqrt(mean(o^2) + eps))) * silu(z) )
-// (Qwen3_5RMSNormGated, modeling_qwen3_5.py:175-190; o is the BF16 gated_delta output).
-__global__ void __launch_bounds__(256) gdn_gated_norm_kernel(const SplitArgs a) {
-  // 16 lanes per (row, value head), 8 channels (16 bytes) a lane; 32-bit item arithmetic
-  // (the launcher checks B * L * HV < 2^31)
-  const uint32_t items = uint32_t(a.rows) * uint32_t(a.HV);
-  const uint32_t want = blockIdx.x * 16u + (threadIdx.x >> 4);
-  const bool ok = want < items;  // past the end: recompute the last item (every lane meets the shuffles)
-  const uint32_t item = ok ? want : items - 1;
-  const int l16 = threadIdx.x & 15;
-  const uint32_t row = item / uint32_t(a.HV);
-  const int hv = int(item - row * uint32_t(a.HV));
-  const int conv_dim = 2 * a.H * 128 + a.HV * 128;
-  __nv_bfloat16* op = a.out + int64_t(row) * a.ld_out + hv * 128 + l16 * 8;
-  const __nv_bfloat16* zp = a.proj + int64_t(row) * a.ld_proj + conv_dim + hv * 128 + l16 * 8;
-  const uint4 ov = *reinterpret_cast<const uint4*>(op);
-  const uint4 zv = *reinterpret_cast<const uint4*>(zp);
-  const float2 o[4] = {bf2f(ov.x), bf2f(ov.y), bf2f(ov.z), bf2f(ov.w)};
-  float2 s2 = mul2(o[0], o[0]);
-  s2 = fma2(o[1], o[1], s2);
-  s2 = fma2(o[2], o[2], s2);
-  s2 = fma2(o[3], o[3], s2);
-  float ss = s2.x + s2.y;
+// (Qwen3_5RMSNormGated, modeling_qwen3_5.py:175-190; o is the BF16 gated_delta output),
+// with ss the sum of squares over the whole row.
+__device__ __forceinline__ void gated_norm_half(const uint32_t (&ob)[32], const uint4 (&zq)[8], const float* nw,
+                                                float ss, float eps, uint4* dst) {
+  const float inv = 1.0f / sqrtf(ss / 128.f + eps);
 #pragma unroll
-  for (int m = 8; m > 0; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
-  const float inv = 1.0f / sqrtf(ss / 128.f + a.eps);
-  const float4 w0 = *reinterpret_cast<const float4*>(a.norm_w + l16 * 8);
-  const float4 w1 = *reinterpret_cast<const float4*>(a.norm_w + l16 * 8 + 4);
-  const float2 w[4] = {make_float2(w0.x, w0.y), make_float2(w0.z, w0.w), make_float2(w1.x, w1.y),
-                       make_float2(w1.z, w1.w)};
-  const uint32_t zw[4] = {zv.x, zv.y, zv.z, zv.w};
-  uint32_t res[4];
+  for (int q = 0; q < 8; ++q) {
+    const float4 w0 = *reinterpret_cast<const float4*>(nw + q * 8);
+    const float4 w1 = *reinterpret_cast<const float4*>(nw + q * 8 + 4);
+    const float2 w[4] = {make_float2(w0.x, w0.y), make_float2(w0.z, w0.w), make_float2(w1.x, w1.y),
+                         make_float2(w1.z, w1.w)};
+    const uint32_t zw[4] = {zq[q].x, zq[q].y, zq[q].z, zq[q].w};
+    uint32_t res[4];
 #pragma unroll
-  for (int p = 0; p < 4; ++p) {
-    const float2 n = bf2f(bf2_pack_f2(mul2(o[p], make_float2(inv, inv))));  // bf16(o * inv)
-    const float2 h = bf2f(bf2_pack_f2(mul2(w[p], n)));                       // bf16(w * .)
-    res[p] = bf2_pack_f2(mul2(h, silu2(bf2f(zw[p]))));
+    for (int p = 0; p < 4; ++p) {
+      const float2 n = bf2f(bf2_pack_f2(mul2(bf2f(ob[q * 4 + p]), make_float2(inv, inv))));  // bf16(o * inv)
+      const float2 h = bf2f(bf2_pack_f2(mul2(w[p], n)));                                       // bf16(w * .)
+      res[p] = bf2_pack_f2(mul2(h, silu2(bf2f(zw[p]))));
+    }
+    dst[q] = make_uint4(res[0], res[1], res[2], res[3]);
   }
-  if (ok) *reinterpret_cast<uint4*>(op) = make_uint4(res[0], res[1], res[2], res[3]);
 }
 
-__global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) {
+__device__ __forceinline__ void named_arrive(int id, int n) {
+  asm volatile("bar.arrive %0, %1;\n" ::"r"(id), "r"(n) : "memory");
+}
+
+// Sequential chunk scan, S in TMEM (12 warps).  Warps 0-7: quadrants 0, 1 (lanes 0-63) hold
+// the W rows of P = [W; Q'] S and compute Vn = U - W S; quadrants 2, 3 (lanes 64-127) hold
+// O = Q' S + Aqk Vn, staged as BF16 with its row sums of squares in shared memory; all eight
+// carry S.  Warps 8-11 apply the gated RMSNorm to the stashed O of chunk c - 1 while chunk c
+// runs (named barrier 3 hands the stash back before chunk c's O overwrites it).
+__global__ void __launch_bounds__(384, 1) gdn_scan_tc_kernel(const SplitArgs a) {
   using M = TcScan;
   using CB = ChunkBlock<128, 128>;
-  constexpr int D = 128;
+  constexpr int D = 128, NTH = 384;
   constexpr long long kWait = 1ll << 31;  // ~1 s of SM clocks per MMA wait
   constexpr uint32_t kId1 = tc::idesc_bf16(128, 128, 0, 1);  // K-major A, MN-major B
   constexpr uint32_t kId2 = tc::idesc_bf16(128, 128, 1, 1);  // MN-major A and B
@@ -731,11 +1140,15 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) 
   uint64_t* bar2 = bar1 + 1;                                       // MMA2/3 commits
   uint64_t* ldbar = bar1 + 2;                                      // stage loads [2]
   uint32_t* slot = reinterpret_cast<uint32_t*>(smem + M::slot);
+  float* sNw = reinterpret_cast<float*>(smem + M::nw);
+  float* sNss = reinterpret_cast<float*>(smem + M::nss);
+  float* sGL = reinterpret_cast<float*>(smem + M::gl);  // G_last of each chunk: off the per-chunk critical path
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int quad = warp & 3, half = warp >> 2;
-  const int row = quad * 32 + lane;          // TMEM lane of this thread
-  const bool vwarp = quad >= 2;              // quadrants 2, 3: W rows -> Vn
-  const bool issuer = tid == 64;
+  const bool nwarp = warp >= 8;  // gated RMSNorm warps
+  const int quad = warp & 3, half = (warp >> 2) & 1;
+  const int row = quad * 32 + lane;  // TMEM lane of this thread (warps 0-7)
+  const bool vwarp = !nwarp && quad < 2;
+  const bool issuer = tid == 0;
   const int bh = blockIdx.x, b = bh / a.HV, hv = bh % a.HV;
   const unsigned char* blocks = a.blocks + int64_t(bh) * a.nc * CB::bytes;  // row of a.nc (longest) chunks
   const uint32_t sbase = smem_u32(smem);
@@ -746,29 +1159,22 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) 
 
   int ld_issued[2] = {0, 0};  // stage loads issued (issuer thread)
   auto load_block = [&](int c, int st) {  // issuer: chunk block c (its shared-memory image) -> stage st
-    const unsigned char* src = blocks + int64_t(c) * CB::bytes;
-    unsigned char* dst = smem + st * M::stage;
-    tc::mbar_expect_tx(ldbar + st, uint32_t(M::copy1 + M::copy2));
-    tc::bulk_g2s(dst, src, uint32_t(M::copy1), ldbar + st);
-    tc::bulk_g2s(dst + M::u, src + CB::u, uint32_t(M::copy2), ldbar + st);
+    tc::mbar_expect_tx(ldbar + st, uint32_t(M::stage));
+    tc::bulk_g2s(smem + st * M::stage, blocks + int64_t(c) * CB::bytes, uint32_t(M::stage), ldbar + st);
     ++ld_issued[st];
   };
 
-  // S = 0 (bf16 copy), zero rows 64..127 of [Aqk; 0] in both stages, norm weight, barriers, TMEM
-  const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
-  for (int i = tid; i < D * D * 2 / 16; i += 256) reinterpret_cast<uint4*>(smem + M::b1)[i] = z4;
-  for (int st = 0; st < 2; ++st)
-    for (int i = tid; i < 64 * kC * 2 / 16; i += 256)
-      reinterpret_cast<uint4*>(smem + st * M::stage + M::zero)[i] = z4;
+  // S = 0 (bf16 copy), norm weight, G_last, barriers, TMEM
+  for (int i = tid; i < D * D * 2 / 16; i += NTH) reinterpret_cast<uint4*>(smem + M::b1)[i] = make_uint4(0u, 0u, 0u, 0u);
   if (tid == 0) {
     for (int i = 0; i < 4; ++i) tc::mbar_init(bar1 + i, 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   if (warp == 0) tc::tmem_alloc(slot, 256);
-  float* sGL = reinterpret_cast<float*>(smem + M::gl);  // G_last of each chunk: off the per-chunk critical path
-  for (int i = tid; i < nc && i < M::kGMax; i += 256)
+  if (tid < D) sNw[tid] = a.norm_w[tid];
+  for (int i = tid; i < nc && i < M::kGMax; i += NTH)
     sGL[i] = *reinterpret_cast<const float*>(blocks + int64_t(i) * CB::bytes + CB::g + (kC - 1) * 4);
-  tc::fence_async_smem();  // zeroed operand rows -> tensor cores
+  tc::fence_async_smem();  // zeroed S copy -> tensor cores
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
@@ -777,6 +1183,31 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) 
   const uint32_t lane_off = uint32_t(quad * 32) << 16;
   const uint32_t tS = tmem + lane_off + half * 64, tP = tmem + 128 + lane_off + half * 64;
   bool ok = true;
+
+  // norm warps: thread (token nr of the chunk, column half nh)
+  const int conv_dim = 2 * a.H * D + a.HV * D;
+  const int nr = (tid - 256) & (kC - 1), nh = ((tid - 256) >> 6) & 1;
+  auto norm_chunk = [&](int c, bool hand_back) {  // gated RMSNorm of chunk c's stashed O rows
+    uint32_t ob[32];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const uint4 v = *reinterpret_cast<const uint4*>(smem + M::ost + M::offu(nr, nh * 8 + q));
+      ob[4 * q] = v.x;
+      ob[4 * q + 1] = v.y;
+      ob[4 * q + 2] = v.z;
+      ob[4 * q + 3] = v.w;
+    }
+    const float ss = sNss[nr * 2] + sNss[nr * 2 + 1];
+    if (hand_back) named_arrive(3, 256);  // the stash may take chunk c + 1's O
+    const int64_t t = int64_t(c) * kC + nr;
+    if (t >= L) return;
+    const uint4* zp = reinterpret_cast<const uint4*>(a.proj + (seq0 + t) * a.ld_proj + conv_dim + hv * D + nh * 64);
+    uint4 zq[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) zq[q] = __ldg(zp + q);
+    gated_norm_half(ob, zq, sNw + nh * 64, ss, a.eps,
+                    reinterpret_cast<uint4*>(a.out + (seq0 + t) * a.ld_out + hv * D + nh * 64));
+  };
 
   for (int c = 0; c < nc; ++c) {
     const int st = c & 1;
@@ -789,13 +1220,17 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) 
     ok = __syncthreads_and(ok);  // chunk c-1's S copy, TMEM traffic and stage reads done
     if (!ok) break;
     tc::fence_after();
+    if (nwarp) {
+      if (c > 0) norm_chunk(c - 1, true);
+      continue;
+    }
     const float gl_next =
         c + 1 >= nc ? 0.f
                     : (c + 1 < M::kGMax ? sGL[c + 1]
                                         : *reinterpret_cast<const float*>(blocks + int64_t(c + 1) * CB::bytes + CB::g +
                                                                           (kC - 1) * 4));
     if (vwarp) {
-      if (issuer) {  // MMA1: P = [Q'; W] S
+      if (issuer) {  // MMA1: P = [W; Q'] S
 #pragma unroll
         for (int s = 0; s < 8; ++s)
           tc::mma_bf16(tmem + 128, tc::smem_desc(sbu + M::a1 + s * 256, 128, 2048),
@@ -805,7 +1240,7 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) 
       }
       ok = tc::mbar_wait(bar1, par, kWait) && ok;
       tc::fence_after();
-      const int t = row - 64;  // token of this W row
+      const int t = row;  // token of this W row
 #pragma unroll
       for (int piece = 0; piece < 2; ++piece) {  // Vn = U - W S, columns [64 half + 32 piece, +32)
         uint32_t r[32];
@@ -829,7 +1264,7 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) 
       tc::fence_before();
       named_bar(2, 128);  // Vn staged, P's W rows read
       tc::fence_after();
-      if (issuer) {  // MMA2: S (+)= K'^T Vn;  MMA3: P += [Aqk; 0] Vn
+      if (issuer) {  // MMA2: S (+)= K'^T Vn;  MMA3: P += [any; Aqk] Vn (lanes 64-127: O)
 #pragma unroll
         for (int s = 0; s < 4; ++s)
           tc::mma_bf16(tmem, tc::smem_desc(sbu + M::a2 + s * 4096, 2048, 128),
@@ -843,9 +1278,10 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) 
     }
     ok = tc::mbar_wait(bar2, par, kWait) && ok;
     tc::fence_after();
-    if (!vwarp) {  // O rows (lanes 0..63) -> BF16 layer output; the gated RMSNorm is a separate kernel
-      const bool valid = c * kC + row < L;
-      uint4* op = reinterpret_cast<uint4*>(a.out + (seq0 + int64_t(c) * kC + row) * a.ld_out + hv * D + half * 64);
+    if (!vwarp) {  // O rows (lanes 64..127) -> BF16 stash + row-half sums of squares
+      if (c > 0) named_bar(3, 256);  // the norm warps hold chunk c-1's stash
+      const int t = row - kC;
+      float2 s2 = make_float2(0.f, 0.f);
 #pragma unroll
       for (int piece = 0; piece < 2; ++piece) {
         uint32_t r[32];
@@ -853,14 +1289,18 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) 
         tc::wait_ld();
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          uint4 res;
-          uint32_t* rw = reinterpret_cast<uint32_t*>(&res);
+          uint32_t w[4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e)
-            rw[e] = bf2_pack(__uint_as_float(r[q * 8 + 2 * e]), __uint_as_float(r[q * 8 + 2 * e + 1]));
-          if (valid) op[piece * 4 + q] = res;
+          for (int e = 0; e < 4; ++e) {
+            w[e] = bf2_pack(__uint_as_float(r[q * 8 + 2 * e]), __uint_as_float(r[q * 8 + 2 * e + 1]));
+            const float2 f = bf2f(w[e]);
+            s2 = fma2(f, f, s2);
+          }
+          *reinterpret_cast<uint4*>(smem + M::ost + M::offu(t, half * 8 + piece * 4 + q)) =
+              make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
+      sNss[t * 2 + half] = s2.x + s2.y;
     }
     {  // S: bf16 copy for the next MMA1 (and the final state), then S *= e^{G_last(next chunk)}
       const float f = __expf(gl_next);
@@ -891,6 +1331,8 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_tc_kernel(const SplitArgs a) 
       tc::fence_async_smem();
     }
   }
+  ok = __syncthreads_and(ok);  // the last chunk's stash and sums are published
+  if (ok && nwarp && nc > 0) norm_chunk(nc - 1, false);
   if (!ok) {  // a wait timed out: report, and give in-flight copies a bounded time to land
     if (tid == 0) atomicOr(a.status, 1u);
     if (issuer)
@@ -921,7 +1363,15 @@ int launch_split(SplitArgs& a, void* ws, int64_t ws_bytes, cudaStream_t s) {
     set_error("gdn prefill: cannot clear the status word");
     return KADLLM_ECUDA;
   }
-  {
+  if (tc_scan) {
+    const size_t smem = PrepTc::bytes;
+    if (cudaFuncSetAttribute(gdn_prep_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess) {
+      set_error("gdn prefill prep: cannot reserve %zu bytes of shared memory", smem);
+      return KADLLM_ECUDA;
+    }
+    gdn_prep_tc_kernel<<<dim3(a.nc, unsigned(n)), 256, smem, s>>>(a);
+    KB_CHECK_LAUNCH("gdn prefill tensor-core prep launch");
+  } else {
     const size_t smem = PrepSmem<DK, DV>::bytes;
     auto kern = gdn_prep_kernel<DK, DV>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess) {
@@ -937,11 +1387,8 @@ int launch_split(SplitArgs& a, void* ws, int64_t ws_bytes, cudaStream_t s) {
       set_error("gdn prefill scan: cannot reserve %zu bytes of shared memory", smem);
       return KADLLM_ECUDA;
     }
-    gdn_scan_tc_kernel<<<unsigned(n), 256, smem, s>>>(a);
+    gdn_scan_tc_kernel<<<unsigned(n), 384, smem, s>>>(a);
     KB_CHECK_LAUNCH("gdn prefill tensor-core scan launch");
-    const int64_t items = a.rows * a.HV;  // (row, value head) pairs, 16 per CTA
-    gdn_gated_norm_kernel<<<unsigned((items + 15) / 16), 256, 0, s>>>(a);
-    KB_CHECK_LAUNCH("gdn prefill gated norm launch");
     return KADLLM_OK;
   }
   {

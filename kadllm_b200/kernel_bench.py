@@ -54,9 +54,9 @@ def _time(fn, reps: int, warmup: int = 3) -> float:
     return s.elapsed_time(e) / reps
 
 
-def case_prefill(gen, reps):
+def case_prefill(gen, reps, B=32):
     dev, bf = torch.device("cuda"), torch.bfloat16
-    B, L, H, HV, K = 32, 1024, 16, 16, 128
+    L, H, HV, K = 1024, 16, 16, 128
     C = 2 * H * K + HV * K
     ld = C + HV * K + 2 * HV
     P = torch.randn(B * L, ld, device=dev, generator=gen).to(bf)
@@ -199,6 +199,36 @@ def case_mixer(gen, reps, T=1):
     return ms, "hbm", R * ld * 2 + R * HV * K * 2 + B * HV * K * K * 2 + B * C * 4 * 2
 
 
+def case_mixer_cont(gen, reps):
+    """kadllm_gdn_mixer_continue at the second decode step of the benchmark: 32 requests x 256
+    beams continuing from 256 parents (random parent indices)."""
+    dev, bf = torch.device("cuda"), torch.bfloat16
+    B, W, Wp, H, HV, K = 32, 256, 256, 16, 16, 128
+    C = 2 * H * K + HV * K
+    ld = C + HV * K + 2 * HV
+    prev = (0.5 * torch.randn(B * Wp, ld, device=dev, generator=gen)).to(bf)
+    proj = (0.5 * torch.randn(B * W, ld, device=dev, generator=gen)).to(bf)
+    parent = torch.randint(0, Wp, (B, W), device=dev, generator=gen, dtype=torch.int32)
+    cs = torch.randn(B, C, 4, device=dev, generator=gen).to(bf)
+    cw = (0.3 * torch.randn(C, 4, device=dev, generator=gen)).to(bf)
+    rec = (0.1 * torch.randn(B, HV, K, K, device=dev, generator=gen)).to(bf)
+    al = torch.rand(HV, device=dev, generator=gen) * 2
+    dt = torch.rand(HV, device=dev, generator=gen)
+    nw = torch.ones(K, device=dev)
+    out = torch.empty(B * W, HV * K, device=dev, dtype=bf)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    s = _lib.stream(dev)
+
+    def run():
+        _lib.call("kadllm_gdn_mixer_continue", prev.data_ptr(), parent.data_ptr(), Wp, proj.data_ptr(), ld,
+                  cs.data_ptr(), 4, cw.data_ptr(), rec.data_ptr(), al.data_ptr(), dt.data_ptr(), nw.data_ptr(),
+                  1e-6, out.data_ptr(), B, W, H, HV, K, K, status.data_ptr(), s)
+
+    ms = _time(run, reps)
+    R = B * W
+    return ms, "hbm", 2 * R * ld * 2 + R * HV * K * 2 + B * HV * K * K * 2 + B * C * 4 * 2
+
+
 def case_replay(gen, reps, T=2):
     """ops.gated_delta (the reference's beam replay op) at the decode shape: 32 requests x
     256 beams, 16 heads of 128, BF16 q / k / v, fp32 gates and state."""
@@ -255,8 +285,9 @@ def case_gemm(gen, reps, M, N, K, epilogue=0):
                                             "cublas_tflops": 2.0 * M * N * K / (ref_ms / 1e3) / 1e12}
 
 
-CASES = {"prefill": case_prefill, "attn_tiled": case_attn_tiled, "attn_split": case_attn_split, "conv": case_conv, "attn": case_attn, "mixer": case_mixer,
+CASES = {"prefill": case_prefill, "prefill8": lambda g, r: case_prefill(g, r, B=8), "attn_tiled": case_attn_tiled, "attn_split": case_attn_split, "conv": case_conv, "attn": case_attn, "mixer": case_mixer,
          "mixer2": lambda g, r: case_mixer(g, r, T=2), "select": case_select, "replay": case_replay,
+         "mixer_cont": case_mixer_cont,
          "attn_step": lambda g, r: case_attn_tiled(g, r, B=32, W=256, T=2, L=1024),
          "attn_causal": lambda g, r: case_attn_tiled(g, r, B=32, W=1, T=1, L=1024, causal=True),
          # the step's projections: prefill (32 x 1024 rows) and decode (32 x 256 beams, T = 1)
