@@ -499,8 +499,8 @@ struct PrepTc {
   static constexpr size_t k = (raw_bytes + 127) / 128 * 128;  // images k | q | v
   static constexpr size_t q = k + IMG;
   static constexpr size_t v = q + IMG;
-  static constexpr size_t vec = v + IMG;  // 8 x [kC] fp32
-  static constexpr size_t cw = vec + size_t(8) * kC * 4;
+  static constexpr size_t vec = v + IMG;  // 11 x [kC] fp32
+  static constexpr size_t cw = vec + size_t(11) * kC * 4;
   static constexpr size_t bar = cw + size_t(NCH) * 4 * 2;
   static constexpr size_t slot = bar + 8;
   static constexpr size_t bytes = slot + 8;
@@ -530,6 +530,8 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_tc_kernel(const SplitArgs a) 
   float* sEGL = sW1 + kC;   // e^{G_last - G_i}
   float* sIq = sEGL + kC;   // |q_i|^2, then scale / |q_i|
   float* sIk = sIq + kC;    // |k_i|^2, then 1 / |k_i|
+  float* sG2 = sIk + kC;    // G_i log2 e
+  float* sIk2 = sG2 + kC;   // [kC] (1 / |k_j|, G_j log2 e) pairs
   __nv_bfloat16* sCw = reinterpret_cast<__nv_bfloat16*>(smem + M::cw);
   uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + M::bar);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + M::slot);
@@ -711,6 +713,8 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_tc_kernel(const SplitArgs a) 
     sEG[tid] = e;
     sW1[tid] = sBeta[tid] * e * sIk[tid];
     sEGL[tid] = __expf(sG[kC - 1] - sG[tid]);
+    sG2[tid] = sG[tid] * 1.4426950408889634f;
+    reinterpret_cast<float2*>(sIk2)[tid] = make_float2(sIk[tid], sG2[tid]);
   }
   __syncthreads();
 
@@ -721,16 +725,27 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_tc_kernel(const SplitArgs a) 
   {
     const int quad = warp & 3, hc = warp >> 2;  // TMEM lanes 32 quad .., columns 32 hc ..
     const int i = (quad * 32 + lane) & (kC - 1);
+    // rows 0..31 against columns 32..63 lie above the diagonal: zeros, no TMEM read
+    const bool upper = (quad & 1) == 0 && hc == 1;
     uint32_t v[32];
-    tc::ld32(tc::taddr(tmem, quad * 32, hc * 32), v);
-    tc::wait_ld();
-    const float Gi = sG[i];
+    if (!upper) {
+      tc::ld32(tc::taddr(tmem, quad * 32, hc * 32), v);
+      tc::wait_ld();
+    }
+    const float Gi = sG2[i];
+    const float2* cf = reinterpret_cast<const float2*>(sIk2) + hc * 32;  // (1 / |k_j|, G_j log2 e)
     if (quad < 2) {  // K K^T row i
       const float f = sBeta[i] * sIk[i];
+      if (upper) {
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const int j = hc * 32 + e;
-        sL[i * SL + j] = j < i ? f * sIk[j] * __uint_as_float(v[e]) * __expf(Gi - sG[j]) : 0.f;
+        for (int e = 0; e < 32; ++e) sL[i * SL + hc * 32 + e] = 0.f;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int j = hc * 32 + e;
+          const float2 c = cf[e];
+          sL[i * SL + j] = j < i ? f * c.x * __uint_as_float(v[e]) * fast_ex2(Gi - c.y) : 0.f;
+        }
       }
     } else {  // Q K^T row i -> the block's 64-wide K-major core tile
       const float f = sIq[i];
@@ -738,8 +753,10 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_tc_kernel(const SplitArgs a) 
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
         const int j = hc * 32 + 2 * e;
-        const float x0 = j <= i ? f * sIk[j] * __uint_as_float(v[2 * e]) * __expf(Gi - sG[j]) : 0.f;
-        const float x1 = j + 1 <= i ? f * sIk[j + 1] * __uint_as_float(v[2 * e + 1]) * __expf(Gi - sG[j + 1]) : 0.f;
+        const float2 c0 = cf[2 * e], c1 = cf[2 * e + 1];
+        const float x0 = !upper && j <= i ? f * c0.x * __uint_as_float(v[2 * e]) * fast_ex2(Gi - c0.y) : 0.f;
+        const float x1 =
+            !upper && j + 1 <= i ? f * c1.x * __uint_as_float(v[2 * e + 1]) * fast_ex2(Gi - c1.y) : 0.f;
         pk[e] = bf2_pack(x0, x1);
       }
 #pragma unroll

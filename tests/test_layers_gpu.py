@@ -167,3 +167,44 @@ def test_gdn_prefill_matches_oracle(K, H, L):
     np.testing.assert_array_equal(N(cstate), pad)
     assert_close_rel(N(state), st, rel=1e-2, what="final state")
     assert_close_rel(N(out), ref, rel=1e-2, what="gated output")
+
+
+def test_gdn_prefill_benchmark_shape_sampled_heads():
+    """The benchmark's prefill launch (32 requests x 1024 tokens, 16 heads of 128: 8192
+    prep CTAs, 512 scan CTAs over several waves) against the oracle on sampled
+    (request, head) pairs: output, final state and conv state."""
+    B, L, H, HV, K = 32, 1024, 16, 16, 128
+    kd, vd = H * K, HV * K
+    C = 2 * kd + vd
+    ld = C + vd + 2 * HV
+    g = torch.Generator(device="cuda").manual_seed(11)
+    P = torch.randn(B * L, ld, device="cuda", generator=g).to(bf)
+    cw = (0.5 * torch.randn(C, 4, device="cuda", generator=g)).to(bf)
+    a_log = torch.log(1 + 15 * torch.rand(HV, device="cuda", generator=g)).to(bf).float()
+    dtb = (2 * torch.rand(HV, device="cuda", generator=g) - 1).to(bf).float()
+    nw = (1 + 0.1 * torch.randn(K, device="cuda", generator=g)).to(bf).float()
+    out = torch.empty(B * L, vd, dtype=bf, device="cuda")
+    state = torch.empty(B, HV, K, K, dtype=bf, device="cuda")
+    cstate = torch.empty(B, C, 4, dtype=bf, device="cuda")
+    nbytes = _lib.lib().kadllm_gdn_prefill_workspace(B, L, HV, K, K)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    _lib.call("kadllm_gdn_prefill_split", P.data_ptr(), ld, cw.data_ptr(), cstate.data_ptr(), a_log.data_ptr(),
+              dtb.data_ptr(), nw.data_ptr(), 1e-6, out.data_ptr(), vd, state.data_ptr(), ws.data_ptr(), nbytes,
+              B, L, H, HV, K, K, S())
+    torch.cuda.synchronize()
+    cwn, aln, dtn, nwn = N(cw), N(a_log), N(dtb), N(nw)
+    for b, h in [(0, 0), (13, 7), (31, 15)]:
+        cols = np.r_[h * K:(h + 1) * K, kd + h * K:kd + (h + 1) * K, 2 * kd + h * K:2 * kd + (h + 1) * K]
+        Pb = N(P[b * L:(b + 1) * L])
+        x = Pb[:, cols].T[None]  # 1 x 3K x L
+        xp = np.concatenate([np.zeros((1, 3 * K, 3), np.float32), x], -1)
+        conv = R(O.silu(sum(xp[:, :, j:j + L] * cwn[cols][None, :, j:j + 1] for j in range(4)))).transpose(0, 2, 1)
+        q, k, v = (conv[..., i * K:(i + 1) * K].reshape(1, L, 1, K) for i in range(3))
+        beta = R(O.sigmoid(Pb[:, C + vd + h]))[None, :, None]
+        gg = (-np.exp(aln[h]) * O.softplus(Pb[:, C + vd + HV + h] + dtn[h])).astype(np.float32)[None, :, None]
+        o, st = O.chunk_gated_delta_rule(q, k, v, gg, beta, O.Rounding("fp32"))
+        ref = O.rms_norm_gated(R(o).reshape(-1, K), Pb[:, C + h * K:C + (h + 1) * K], nwn, 1e-6, R)
+        got = N(out[b * L:(b + 1) * L, h * K:(h + 1) * K])
+        assert_close_rel(got, ref, rel=1e-2, what=f"gated output (request {b}, head {h})")
+        assert_close_rel(N(state[b, h]), st[0, 0], rel=1e-2, what=f"final state (request {b}, head {h})")
+        np.testing.assert_array_equal(N(cstate[b, cols]), x[0, :, -4:])
