@@ -549,31 +549,66 @@ int launch_attn_tc(const AttnTcArgs& a, cudaStream_t stream) {
 // Split decode: one warp per query row merges the splits' (O, m, l), the row's suffix keys
 // s <= t (scores q.k_s from the row's q, in the kernel's exp2 domain) and values, then
 // normalises and applies the gate like the fused epilogue.  Lane i holds dims 8i .. 8i + 7.
-__global__ void __launch_bounds__(256) attn_split_combine_kernel(const AttnTcArgs a) {
+__global__ void __launch_bounds__(128) attn_split_combine_kernel(const AttnTcArgs a) {
   const int TG = (a.T - a.t0) * a.G;
   const int64_t R = int64_t(a.W) * TG;
   const int64_t rows = int64_t(a.B) * a.HK * R;
-  const int64_t id = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int64_t id = int64_t(blockIdx.x) * 4 + (threadIdx.x >> 5);
   if (id >= rows) return;  // whole warp
   const int lane = threadIdx.x & 31;
   const int bh = int(id / R), gr = int(id % R);
   const int b = bh / a.HK, hk = bh % a.HK;
   const int beam = gr / TG, rem = gr % TG, t = a.t0 + rem / a.G, g = rem % a.G, hq = hk * a.G + g;
   const int64_t brow = int64_t(b) * a.W + beam;
-  float M = -INFINITY;
-  for (int sp = 0; sp < a.nsplit; ++sp) M = fmaxf(M, a.part_ml[int64_t(sp) * rows + id].x);
-  // suffix scores
+  // every load up front (the first kPre splits' partials, q, the suffix keys and values,
+  // the gate), then the merge in the order of the fused epilogue
+  constexpr int kPre = 4;
+  float2 mlp[kPre];
+  float4 up[kPre][2];
+#pragma unroll
+  for (int sp = 0; sp < kPre; ++sp) {
+    mlp[sp] = make_float2(-INFINITY, 0.f);
+    up[sp][0] = up[sp][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (sp < a.nsplit) {
+      mlp[sp] = a.part_ml[int64_t(sp) * rows + id];
+      const float4* src = reinterpret_cast<const float4*>(a.part_o + (int64_t(sp) * rows + id) * kD + lane * 8);
+      up[sp][0] = src[0];
+      up[sp][1] = src[1];
+    }
+  }
   const uint4 qv = *reinterpret_cast<const uint4*>(a.q + brow * a.sq_row + int64_t(t) * a.sq_t + int64_t(hq) * a.sq_h +
                                                    lane * 8);
+  constexpr int kSufPre = 4;  // suffix keys / values loaded up front; later ones in the loops below
+  uint4 kv[kSufPre], vv[kSufPre];
+#pragma unroll
+  for (int sidx = 0; sidx < kSufPre; ++sidx) {
+    kv[sidx] = vv[sidx] = make_uint4(0u, 0u, 0u, 0u);
+    if (sidx < a.T && sidx <= t) {
+      kv[sidx] = *reinterpret_cast<const uint4*>(a.sk + brow * a.ssk_row + int64_t(sidx) * a.ssk_t +
+                                                 int64_t(hk) * a.ssk_h + lane * 8);
+      vv[sidx] = *reinterpret_cast<const uint4*>(a.sv + brow * a.ssv_row + int64_t(sidx) * a.ssv_t +
+                                                 int64_t(hk) * a.ssv_h + lane * 8);
+    }
+  }
+  uint4 gv = make_uint4(0u, 0u, 0u, 0u);
+  if (a.gate)
+    gv = *reinterpret_cast<const uint4*>(a.gate + brow * a.sg_row + int64_t(t) * a.sg_t + int64_t(hq) * a.sg_h +
+                                         lane * 8);
+  float M = -INFINITY;
+#pragma unroll
+  for (int sp = 0; sp < kPre; ++sp) M = fmaxf(M, mlp[sp].x);
+  for (int sp = kPre; sp < a.nsplit; ++sp) M = fmaxf(M, a.part_ml[int64_t(sp) * rows + id].x);
+  // suffix scores
   const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
   float xs[kSufMax];
 #pragma unroll
   for (int sidx = 0; sidx < kSufMax; ++sidx) {
     xs[sidx] = -INFINITY;
     if (sidx < a.T && sidx <= t) {
-      const uint4 kv = *reinterpret_cast<const uint4*>(a.sk + brow * a.ssk_row + int64_t(sidx) * a.ssk_t +
-                                                       int64_t(hk) * a.ssk_h + lane * 8);
-      const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
+      const uint4 k4 = sidx < kSufPre ? kv[sidx < kSufPre ? sidx : 0]
+                                      : *reinterpret_cast<const uint4*>(a.sk + brow * a.ssk_row + int64_t(sidx) * a.ssk_t +
+                                                                        int64_t(hk) * a.ssk_h + lane * 8);
+      const uint32_t kw[4] = {k4.x, k4.y, k4.z, k4.w};
       float acc = 0.f;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -586,24 +621,28 @@ __global__ void __launch_bounds__(256) attn_split_combine_kernel(const AttnTcArg
   }
   float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   float L = 0.f;
-  for (int sp = 0; sp < a.nsplit; ++sp) {
-    const float2 ml = a.part_ml[int64_t(sp) * rows + id];
-    if (!(ml.x > -INFINITY)) continue;
+  auto add_split = [&](float2 ml, float4 u0, float4 u1) {
+    if (!(ml.x > -INFINITY)) return;
     const float f = fast_ex2(ml.x - M);
     L = fmaf(ml.y, f, L);
-    const float4* src = reinterpret_cast<const float4*>(a.part_o + (int64_t(sp) * rows + id) * kD + lane * 8);
-    const float4 u0 = src[0], u1 = src[1];
     o[0] = fmaf(u0.x, f, o[0]); o[1] = fmaf(u0.y, f, o[1]); o[2] = fmaf(u0.z, f, o[2]); o[3] = fmaf(u0.w, f, o[3]);
     o[4] = fmaf(u1.x, f, o[4]); o[5] = fmaf(u1.y, f, o[5]); o[6] = fmaf(u1.z, f, o[6]); o[7] = fmaf(u1.w, f, o[7]);
+  };
+#pragma unroll
+  for (int sp = 0; sp < kPre; ++sp) add_split(mlp[sp], up[sp][0], up[sp][1]);
+  for (int sp = kPre; sp < a.nsplit; ++sp) {
+    const float4* src = reinterpret_cast<const float4*>(a.part_o + (int64_t(sp) * rows + id) * kD + lane * 8);
+    add_split(a.part_ml[int64_t(sp) * rows + id], src[0], src[1]);
   }
 #pragma unroll
   for (int sidx = 0; sidx < kSufMax; ++sidx) {
     if (!(xs[sidx] > -INFINITY)) continue;
     const float p = fast_ex2(xs[sidx] - M);
     L += p;
-    const uint4 vv = *reinterpret_cast<const uint4*>(a.sv + brow * a.ssv_row + int64_t(sidx) * a.ssv_t +
-                                                     int64_t(hk) * a.ssv_h + lane * 8);
-    const uint32_t vw[4] = {vv.x, vv.y, vv.z, vv.w};
+    const uint4 v4 = sidx < kSufPre ? vv[sidx < kSufPre ? sidx : 0]
+                                    : *reinterpret_cast<const uint4*>(a.sv + brow * a.ssv_row + int64_t(sidx) * a.ssv_t +
+                                                                      int64_t(hk) * a.ssv_h + lane * 8);
+    const uint32_t vw[4] = {v4.x, v4.y, v4.z, v4.w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const float2 vf = bf2f(vw[e]);
@@ -612,10 +651,6 @@ __global__ void __launch_bounds__(256) attn_split_combine_kernel(const AttnTcArg
     }
   }
   const float inv = 1.f / L;
-  uint4 gv = make_uint4(0u, 0u, 0u, 0u);
-  if (a.gate)
-    gv = *reinterpret_cast<const uint4*>(a.gate + brow * a.sg_row + int64_t(t) * a.sg_t + int64_t(hq) * a.sg_h +
-                                         lane * 8);
   const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
   uint32_t res[4];
 #pragma unroll
@@ -836,7 +871,7 @@ extern "C" int kadllm_attention_tiled_split(const void* q, int64_t sq_row, int64
   a.part_o = reinterpret_cast<float*>(static_cast<char*>(workspace) + ((splits * rows * 8 + 255) & ~int64_t(255)));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (int rc = launch_attn_tc<false>(a, s)) return rc;
-  attn_split_combine_kernel<<<unsigned((rows + 7) / 8), 256, 0, s>>>(a);
+  attn_split_combine_kernel<<<unsigned((rows + 3) / 4), 128, 0, s>>>(a);
   KB_CHECK_LAUNCH("tiled attention split combine launch");
   return KADLLM_OK;
 }

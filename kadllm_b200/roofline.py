@@ -75,10 +75,14 @@ def measured_traffic(name: str, args: tuple) -> float | None:
     one ncu capture of the benchmark's shape of that call on a B200; None for
     shapes that were not captured."""
     if name == "kadllm_gdn_prefill_split" and tuple(args[13:19]) == (32, 1024, 16, 16, 128, 128):
-        # prep 407.1 + 557.2 MB, tcgen05 scan 605.0 + 132.7 MB, gated norm 270.5 + 92.3 MB
-        return 2064.8e6
+        # captured at B = 8 (a quarter of the requests; traffic grows with them): tcgen05 prep
+        # 101.8 + 97.3 MB, tcgen05 scan with the gated norm 185.5 + 16.4 MB; x 4
+        return 1604.0e6
     if name == "kadllm_gdn_mixer_replay" and tuple(args[11:13]) == (32, 256) and tuple(args[14:18]) == (16, 16, 128, 128):
-        return {1: 186.4e6, 2: 359.3e6}.get(args[13])  # T = 1: 165.5 + 20.9 MB; T = 2: 306.2 + 53.2 MB
+        return {1: 181.0e6, 2: 353.6e6}.get(args[13])  # T = 1: 164.6 + 16.4 MB; T = 2: 306.0 + 47.6 MB
+    if (name == "kadllm_gdn_mixer_continue" and args[2] == 256 and tuple(args[14:16]) == (32, 256)
+            and tuple(args[16:20]) == (16, 16, 128, 128)):
+        return 295.8e6  # 273.6 + 22.2 MB (random parents: children of one parent share its rows in L2)
     if name == "kadllm_attention_tiled" and (args[24], *args[28:32]) == (32, 8, 2, 1024, 256):
         if args[33]:  # causal prefill: 335.6 + 109.8 MB
             return 445.4e6
