@@ -591,7 +591,10 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_tc_kernel(const SplitArgs a) 
   {
     constexpr int NG = NCH / 8, SEG = 4;
     static_assert(NG * (kC / SEG) == 3 * NT, "every thread takes the same number of items");
-    for (int item = tid; item < NG * (kC / SEG); item += NT) {
+    float ssq_all[3][SEG];  // per item: the squared norms' partial sums, reduced after the loop
+#pragma unroll
+    for (int it = 0; it < 3; ++it) {
+      const int item = tid + it * NT;
       const int grp = item % NG, seg = item / NG;
       const int lc = grp * 8, part = grp / (D / 8);  // 0: q, 1: k, 2: v
       float2 w2[4][4];
@@ -621,7 +624,6 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_tc_kernel(const SplitArgs a) 
       row4(r0 + 2, win[2]);
       unsigned char* img = smem + (part == 0 ? M::q : (part == 1 ? M::k : M::v));
       const int ch = grp % (D / 8);
-      float ssq[SEG];
 #pragma unroll
       for (int rr = 0; rr < SEG; ++rr) {
         const int r = r0 + rr;
@@ -642,7 +644,7 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_tc_kernel(const SplitArgs a) 
             s2 = fma2(o, o, s2);
           }
         }
-        ssq[rr] = s2.x + s2.y;
+        ssq_all[it][rr] = s2.x + s2.y;
         *reinterpret_cast<uint4*>(img + M::img_off(r, ch)) = u;
 #pragma unroll
         for (int pp = 0; pp < 4; ++pp) {
@@ -651,14 +653,23 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_tc_kernel(const SplitArgs a) 
           win[2][pp] = x[pp];
         }
       }
+    }
+    // half-warp sums (a half-warp's 16 items of one item slot are the 16 groups of one of
+    // q / k / v for one segment): 12 independent shuffle chains
+#pragma unroll
+    for (int it = 0; it < 3; ++it)
 #pragma unroll
       for (int rr = 0; rr < SEG; ++rr)
 #pragma unroll
-        for (int m = 1; m < 16; m <<= 1) ssq[rr] += __shfl_xor_sync(0xffffffffu, ssq[rr], m);
-      if ((lane & 15) == 0 && part < 2)
+        for (int m = 1; m < 16; m <<= 1) ssq_all[it][rr] += __shfl_xor_sync(0xffffffffu, ssq_all[it][rr], m);
+    if ((lane & 15) == 0)
 #pragma unroll
-        for (int rr = 0; rr < SEG; ++rr) (part == 0 ? sIq : sIk)[r0 + rr] = ssq[rr];
-    }
+      for (int it = 0; it < 3; ++it) {
+        const int item = tid + it * NT, grp = item % NG, part = grp / (D / 8), r0 = (item / NG) * SEG;
+        if (part < 2)
+#pragma unroll
+          for (int rr = 0; rr < SEG; ++rr) (part == 0 ? sIq : sIk)[r0 + rr] = ssq_all[it][rr];
+      }
   }
   if (t0 + kC >= L) {  // last chunk: conv state = pre-conv columns of tokens L-4 .. L-1
     for (int lc = tid; lc < NCH; lc += NT) {
