@@ -248,6 +248,32 @@ def case_replay(gen, reps, T=2):
     return ms, "hbm", BW * T * (2 * H + 2 * HV) * K * 2 + BW * T * HV * 4 * 2 + B * HV * K * K * 4
 
 
+def case_qk_rope(gen, reps):
+    """kadllm_qk_norm_rope at the prefill shape: 32 x 1024 rows of the attention projection
+    (8 q heads with their gates, 2 k, 2 v heads of 256), rotary dims 64."""
+    dev, bf = torch.device("cuda"), torch.bfloat16
+    rows, L, Hq, HK, D, rot = 32 * 1024, 1024, 8, 2, 256, 64
+    ld = Hq * 2 * D + 2 * HK * D
+    P = torch.randn(rows, ld, device=dev, generator=gen).to(bf)
+    qw = 0.1 * torch.randn(D, device=dev, generator=gen)
+    kw = 0.1 * torch.randn(D, device=dev, generator=gen)
+    t = torch.arange(L + 1, device=dev, dtype=torch.float32)[:, None] * (1e-4 ** (torch.arange(rot // 2, device=dev) / (rot // 2)))[None]
+    cos = torch.cat([t.cos(), t.cos()], 1).to(bf).contiguous()
+    sin = torch.cat([t.sin(), t.sin()], 1).to(bf).contiguous()
+    q = torch.empty(rows, Hq * D, device=dev, dtype=bf)
+    k = torch.empty(rows // L, L, HK, D, device=dev, dtype=bf)
+    v = torch.empty_like(k)
+    s = _lib.stream(dev)
+
+    def run():
+        _lib.call("kadllm_qk_norm_rope", P.data_ptr(), ld, Hq, HK, D, qw.data_ptr(), kw.data_ptr(), 1e-6,
+                  cos.data_ptr(), sin.data_ptr(), rot, None, 0, L, q.data_ptr(), Hq * D, D, k.data_ptr(),
+                  L * HK * D, HK * D, D, v.data_ptr(), L * HK * D, HK * D, D, rows, s)
+
+    ms = _time(run, reps)
+    return ms, "hbm", rows * (Hq + 2 * HK) * D * 2 * 2
+
+
 def case_select(gen, reps):
     from .grbeam import BeamSelector
 
@@ -287,7 +313,7 @@ def case_gemm(gen, reps, M, N, K, epilogue=0):
 
 CASES = {"prefill": case_prefill, "prefill8": lambda g, r: case_prefill(g, r, B=8), "attn_tiled": case_attn_tiled, "attn_split": case_attn_split, "conv": case_conv, "attn": case_attn, "mixer": case_mixer,
          "mixer2": lambda g, r: case_mixer(g, r, T=2), "select": case_select, "replay": case_replay,
-         "mixer_cont": case_mixer_cont,
+         "mixer_cont": case_mixer_cont, "qk_rope": case_qk_rope,
          "attn_step": lambda g, r: case_attn_tiled(g, r, B=32, W=256, T=2, L=1024),
          "attn_causal": lambda g, r: case_attn_tiled(g, r, B=32, W=1, T=1, L=1024, causal=True),
          # the step's projections: prefill (32 x 1024 rows) and decode (32 x 256 beams, T = 1)
