@@ -89,7 +89,7 @@ _ERRORS = {1: ValueError, 2: TypeError, 3: NotImplementedError, 4: RuntimeError}
 # kernels launched per successful call of each entry point (for launch accounting)
 LAUNCHES_PER_CALL = {"kadllm_beam_select": 4, "kadllm_beam_select_noalloc": 4, "kadllm_beam_select_status": 0,
                      "kadllm_beam_select_fused": 4, "kadllm_attention_tiled_split": 2,
-                     "kadllm_gdn_prefill_split": 3, "kadllm_gdn_prefill_split_varlen": 3}
+                     "kadllm_gdn_prefill_split": 2, "kadllm_gdn_prefill_split_varlen": 2}
 launch_count = 0
 _count_lock = threading.Lock()
 
