@@ -8,8 +8,9 @@ GPU -- by default the whole search captured once as a CUDA graph
 (``kadllm_b200.grbeam.GraphedSearch``) and replayed each step, every kernel
 of the search running each time (``--no-graph``: eager launches); with N GPUs
 every rank runs its own batch (weak scaling: requests shard across GPUs with
-replicated weights) and the results are all-gathered over NCCL at the end of
-each step.
+replicated weights) with no collective inside the timed steps; the results are
+all-gathered over NCCL once afterwards (``per_rank.with_gather_ms`` reports what
+a per-step gather would cost).
 
 ``value``   requests/s with the prompts already resident in HBM;
 ``e2e``     the same through the public API from pinned host buffers, with the
@@ -257,7 +258,7 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
     sc_host = torch.empty(batch, BEAM, dtype=torch.float32).pin_memory()
     widths = [BEAM] * DEPTH
 
-    def gather(res):  # the path's only exchange: finished beams, in rank order
+    def gather(res):  # the finished beams of every rank, in rank order (after the timed searches)
         return gather_beams(res.tokens, res.scores)
 
     # the search as one CUDA graph (static prompt buffer, every kernel replayed per step);
@@ -276,17 +277,17 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
                       file=sys.stderr, flush=True)
                 graphed = None
 
+    # a step is one search of this rank's requests; the requests are independent, so no
+    # collective runs between the barriers (each rank keeps its own beams)
     def step_device():
-        if graphed is not None:
-            return gather(graphed(ids_dev))
-        return gather(grbeam_search(adapter, ids_dev, widths))
+        return graphed(ids_dev) if graphed is not None else grbeam_search(adapter, ids_dev, widths)
 
     def step_e2e():
         ids = ids_host.to(dev, non_blocking=True)
         res = graphed(ids) if graphed is not None else grbeam_search(adapter, ids, widths)
         tok_host.copy_(res.tokens, non_blocking=True)
         sc_host.copy_(res.scores, non_blocking=True)
-        return gather(res)
+        return res
 
     per_rank = {}
 
@@ -309,8 +310,8 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
         ms = max_over_ranks(mine, dev)
         return ms / steps, (launches_per_step * steps if graphed is not None else _lib.launch_count - launches0)
 
-    def step_search_only():  # the same step without the result all-gather
-        return graphed(ids_dev) if graphed is not None else grbeam_search(adapter, ids_dev, widths)
+    def step_gather():  # the search plus the all-gather of every rank's beams (reported per rank)
+        return gather(step_device())
 
     with torch.inference_mode():
         for _ in range(args.warmup):
@@ -318,9 +319,10 @@ def run_native(args, rank: int, world: int, local_rank: int) -> None:
         with ClockSampler(local_rank) as clocks:
             ms, launches = timed(step_device, args.steps, "step_ms")
         ms_e2e, _ = timed(step_e2e, args.steps)
-        if world > 1:  # how the step splits into search time per rank and the exchange
-            timed(step_search_only, args.steps, "search_only_ms")
+        if world > 1:  # what a per-search gather of every rank's beams would add
+            timed(step_gather, args.steps, "with_gather_ms")
         res = graphed(ids_dev) if graphed is not None else grbeam_search(adapter, ids_dev, widths)
+        gather(res)  # the combined result (every rank takes part)
         if graphed is not None:
             graphed.check()
         valid = bool(res.valid.all().item())

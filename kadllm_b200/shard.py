@@ -1,10 +1,10 @@
 """Request sharding across ranks (one process per GPU) and the result exchange.
 
 GRBeam requests are independent, so N ranks each run their own batch of
-requests with a replicated model (weak scaling); the only exchange is one
-all-gather of the finished beams (tokens and scores) per search, and the
-timing reduction (max over ranks).  NCCL over NVLink on the GPU box; the
-same functions run on ``gloo`` for the CPU tests.
+requests with a replicated model (weak scaling) and no collective between
+them; the finished beams (tokens and scores) can be all-gathered into one
+result afterwards, and the timing takes the max over ranks.  NCCL over NVLink
+on the GPU box; the same functions run on ``gloo`` for the CPU tests.
 """
 
 from __future__ import annotations
