@@ -48,6 +48,13 @@ __device__ __forceinline__ float load_as_float(const void* p, int64_t i, int dty
   return reinterpret_cast<const float*>(p)[i];
 }
 
+// Elements i, i + 1 (i even, the row 4- / 8-byte aligned) as a float pair, in one load.
+__device__ __forceinline__ float2 load2_as_float(const void* p, int64_t i, int dtype) {
+  if (dtype == KADLLM_BF16) return __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(p)[i >> 1]);
+  if (dtype == KADLLM_F16) return __half22float2(reinterpret_cast<const __half2*>(p)[i >> 1]);
+  return reinterpret_cast<const float2*>(p)[i >> 1];
+}
+
 __device__ __forceinline__ void store_from_float(void* p, int64_t i, int dtype, float v) {
   if (dtype == KADLLM_BF16)
     reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);

@@ -238,8 +238,8 @@ __global__ void __launch_bounds__(128) gdn_replay_kernel(const GdnArgs a) {
             kx = make_float2(bf16r(silu_fast(kx.x)), bf16r(silu_fast(kx.y)));
           } else {
             const int64_t o = (row * a.H + h) * DK + col;
-            qx = make_float2(load_as_float(a.q, o, a.x_dtype), load_as_float(a.q, o + 1, a.x_dtype));
-            kx = make_float2(load_as_float(a.k, o, a.x_dtype), load_as_float(a.k, o + 1, a.x_dtype));
+            qx = load2_as_float(a.q, o, a.x_dtype);
+            kx = load2_as_float(a.k, o, a.x_dtype);
           }
         }
         qv[kk][2 * hp] = qx.x;
@@ -378,7 +378,7 @@ __global__ void __launch_bounds__(128) gdn_replay_kernel(const GdnArgs a) {
             vp = make_float2(bf16r(silu_fast(vp.x)), bf16r(silu_fast(vp.y)));
           } else {
             const int64_t vo = (row * HV + hv) * DV + col0;
-            vp = make_float2(load_as_float(a.v, vo, a.x_dtype), load_as_float(a.v, vo + 1, a.x_dtype));
+            vp = load2_as_float(a.v, vo, a.x_dtype);
           }
         }
 #pragma unroll
@@ -514,6 +514,10 @@ extern "C" int kadllm_gated_delta_replay(const void* q, const void* k, const voi
                  valid_dtype(state_dtype),
              KADLLM_EDTYPE, "gdn replay: unsupported dtype code");
   KB_REQUIRE(q && k && v && log_decay && beta && state && out && status, KADLLM_EINVAL, "gdn replay: null pointer");
+  const uintptr_t pair = uintptr_t(2 * dtype_size(x_dtype)) - 1;  // q / k / v are read as element pairs
+  KB_REQUIRE(((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) &
+              pair) == 0,
+             KADLLM_EINVAL, "gdn replay: q / k / v must be aligned to two elements");
   GdnArgs a{};
   a.q = q; a.k = k; a.v = v; a.x_dtype = x_dtype;
   a.g = log_decay; a.g_dtype = decay_dtype; a.beta = beta; a.beta_dtype = beta_dtype;
