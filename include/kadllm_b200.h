@@ -78,6 +78,10 @@ KADLLM_API int kadllm_gated_delta_replay(const void* q, const void* k, const voi
  *   rec_state   [B, HV, K, V] bf16 contiguous
  *   a_log, dt_bias [HV] f32; norm_weight [V] f32 (values of the BF16 params)
  *   out         [BW*T, HV*V] bf16
+ *   records     null, or (steps == 1, K == V in {64, 128}) kadllm_gdn_mixer_record_bytes
+ *               bytes, 16-byte aligned: per (beam row, value head) the row's raw k
+ *               (bf16), its delta (fp32) and (1/|k|, decay), from which
+ *               kadllm_gdn_mixer_continue runs the next step on the new tokens only
  *   status      device uint32: bit 0 set when a tensor-core wait timed out
  *               (read it after the stream synchronises; the output is then invalid)
  * ------------------------------------------------------------------------ */
@@ -86,7 +90,9 @@ KADLLM_API int kadllm_gdn_mixer_replay(const void* proj, int64_t ld_proj, const 
                             const float* a_log, const float* dt_bias, const float* norm_weight,
                             float norm_eps, void* out, int64_t batch, int64_t beam_width,
                             int64_t steps, int64_t heads, int64_t v_heads, int64_t k_dim,
-                            int64_t v_dim, uint32_t* status, void* stream);
+                            int64_t v_dim, void* records, uint32_t* status, void* stream);
+KADLLM_API int64_t kadllm_gdn_mixer_record_bytes(int64_t batch, int64_t beam_width, int64_t v_heads,
+                                                 int64_t v_dim);
 
 /* ------------------------------------------------------------------------
  * Depthwise causal conv1d replay from a shared prefix state (+ SiLU).
@@ -394,14 +400,17 @@ KADLLM_API int kadllm_gather_rows(const void* src, int64_t ld_src, const int32_t
  * rows (as kadllm_gdn_mixer_replay takes them at T = 1), proj [B*W, ld_proj] the
  * new tokens' rows, out [B*W, HV*V] the new token's mixer output -- the same
  * values kadllm_gdn_mixer_replay gives for that token at T = 2 without
- * recomputing the first token's projection.  Head dims 64 / 128 (K == V). */
+ * recomputing the first token's projection.  Head dims 64 / 128 (K == V).
+ * records: null (the first token is replayed from proj_prev), or the previous
+ * step's records (kadllm_gdn_mixer_replay, indexed like proj_prev): the first
+ * token's k, delta and decay come from them and only the new token is computed. */
 KADLLM_API int kadllm_gdn_mixer_continue(const void* proj_prev, const int32_t* parent, int64_t prev_width,
                                          const void* proj, int64_t ld_proj, const void* conv_state,
                                          int64_t conv_hist, const void* conv_weight, const void* rec_state,
                                          const float* a_log, const float* dt_bias, const float* norm_weight,
                                          float norm_eps, void* out, int64_t batch, int64_t beam_width,
                                          int64_t heads, int64_t v_heads, int64_t k_dim, int64_t v_dim,
-                                         uint32_t* status, void* stream);
+                                         const void* records, uint32_t* status, void* stream);
 
 /* Diagnostics: one CTA runs the tensor-core kernels' bounded mbarrier wait on a
  * barrier nothing completes, giving up after max_cycles SM clocks (1 .. 2^32)

@@ -39,13 +39,13 @@ SIGNATURES: dict[str, list] = {
     "kadllm_beam_select_status": [P, L, L, P, P],
     "kadllm_beam_select_noalloc": [P, I, L, P, P, P, P, P, P, L, L, L, L, L, P],
     "kadllm_gated_delta_replay": [P, P, P, I, P, I, P, I, P, I, P, L, L, L, L, L, L, L, F, P, P],
-    "kadllm_gdn_mixer_replay": [P, L, P, L, P, P, P, P, P, F, P, L, L, L, L, L, L, L, P, P],
+    "kadllm_gdn_mixer_replay": [P, L, P, L, P, P, P, P, P, F, P, L, L, L, L, L, L, L, P, P, P],
     "kadllm_causal_conv1d_replay": [P, L, L, L, P, L, L, L, L, P, P, P, I, L, L, L, L, L, I, P],
     "kadllm_gemm": [P, L, P, L, P, L, P, L, L, L, L, L, I, P, P],
     "kadllm_gemm_logits": [P, L, P, L, P, L, L, L, L, P, L, L, L, P, P],
     "kadllm_beam_select_fused": [P, L, P, P, P, P, P, P, L, L, L, L, L, L, P],
     "kadllm_gather_rows": [P, L, P, L, L, L, L, P, L, P],
-    "kadllm_gdn_mixer_continue": [P, P, L, P, L, P, L, P, P, P, P, P, F, P, L, L, L, L, L, L, P, P],
+    "kadllm_gdn_mixer_continue": [P, P, L, P, L, P, L, P, P, P, P, P, F, P, L, L, L, L, L, L, P, P, P],
     "kadllm_prefix_attention": [P, L, L, L, P, L, L, L, P, L, L, L, P, L, L, L, P, L, L, L, P, P,
                                 L, L, L, P, L, L, L, I, L, L, L, L, L, L, L, F, P],
 }
@@ -75,6 +75,8 @@ def lib() -> ctypes.CDLL:
         handle.kadllm_attention_split_workspace.argtypes = [L, L, L, L, L, L]
         handle.kadllm_kv_tile_bytes.restype = ctypes.c_int64
         handle.kadllm_kv_tile_bytes.argtypes = [L, L, L, L]
+        handle.kadllm_gdn_mixer_record_bytes.restype = ctypes.c_int64
+        handle.kadllm_gdn_mixer_record_bytes.argtypes = [L, L, L, L]
         for name, args in SIGNATURES.items():
             fn = getattr(handle, name)
             fn.argtypes = args

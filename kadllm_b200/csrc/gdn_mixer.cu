@@ -59,6 +59,12 @@ struct MixLayout {
   static constexpr int NWB = D * 4;         // norm weight fp32
   static constexpr int OCTB = 8 * ROWB;     // one staged octet: 8 (beam, token) rows
   static constexpr size_t SMEM = size_t(S0B) + TABB + NWB + size_t(kMixWarps) * 2 * OCTB + 16;  // + mbarrier, TMEM slot
+  // continuation from a saved first step: a row also stages the parent token's raw q | k | v
+  // slices and its saved raw k (one buffer per warp: two CTAs per SM)
+  static constexpr int ROWB_C = ROWB + 8 * D;
+  static constexpr int OCTB_C = 8 * ROWB_C;
+  static constexpr size_t SMEM_C = size_t(S0B) + TABB + NWB + size_t(kMixWarps) * OCTB_C + 16;
+  static constexpr int REC = 6 * D + 16;    // saved record per (beam, head): raw k bf16 | delta fp32 | (1/|k|, decay)
 };
 
 // MMA k index (B row) of state row r = 32m + 8tq + 2p + d: 32m + 16(p / 2) + 4tq + 2(p % 2) + d.
@@ -136,10 +142,14 @@ __device__ __forceinline__ float chunk_dot(const uint32_t (&x)[KM][4], const uin
   return quad_sum(acc.x + acc.y);
 }
 
-template <int D, int TMAX>
+// CONT (TMAX = 1): the second decode step from the first step's saved records -- octets
+// of 8 beams, each row the beam's new token, with the parent token's k, delta and decay
+// from its record and its raw q | k | v for the conv window.
+template <int D, int TMAX, bool CONT>
 __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerArgs a, int octets_per_warp) {
   using L = MixLayout<D>;
-  constexpr int CH = L::CH, NCH = L::NCH, ROWB = L::ROWB, OCTB = L::OCTB;
+  static_assert(!CONT || TMAX == 1, "the saved-state continuation stages one row per beam");
+  constexpr int CH = L::CH, NCH = L::NCH, ROWB = CONT ? L::ROWB_C : L::ROWB, OCTB = CONT ? L::OCTB_C : L::OCTB;
   constexpr int NT = D / 8;      // n8 tiles of the V columns
   constexpr int NH = NT / 2;     // n8 tiles per half (bounds the accumulator registers)
   constexpr int KM = D / 32;     // 16-byte chunks per thread per head row
@@ -152,7 +162,7 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
   float* sTab = reinterpret_cast<float*>(smem + L::S0B);
   float* sNw = sTab + 8 * NCH;
   unsigned char* sStage = smem + L::S0B + L::TABB + L::NWB;
-  uint64_t* mbar = reinterpret_cast<uint64_t*>(sStage + kMixWarps * 2 * OCTB);
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(sStage + kMixWarps * (CONT ? 1 : 2) * OCTB);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(mbar + 1);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -167,14 +177,16 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
   const int octets = (a.W + BPO - 1) / BPO;
   const int oct0 = (blockIdx.y * kMixWarps + warp) * octets_per_warp;
   const int noct = max(0, min(octets_per_warp, octets - oct0));
-  unsigned char* wbuf = sStage + warp * 2 * OCTB;
+  unsigned char* wbuf = sStage + warp * (CONT ? 1 : 2) * OCTB;
   // projection columns of the staged slices: q, k, v, z head slices; b and a gate words (aligned down)
   const int col_q = h * D, col_k = key_dim + h * D, col_v = 2 * key_dim + hv * D, col_z = conv_dim + hv * D;
   const int col_b = conv_dim + HV * D + hv, col_a = conv_dim + HV * D + HV + hv;
 
   // Projection row of (token tr, beam): rows (beam, t) of proj, or in continuation mode
   // the parent's row of the previous step (tr = 0) / the beam's row of the new token.
+  auto parent_of = [&](int beam) { return min(max(a.parent[int64_t(b) * a.W + beam], 0), a.Wp - 1); };
   auto prow_of = [&](int tr, int beam) -> const __nv_bfloat16* {
+    if (CONT) return a.proj + (int64_t(b) * a.W + beam) * ld;
     if (TMAX == 2 && a.proj_prev != nullptr) {
       if (tr == 0) {
         const int p = min(max(a.parent[int64_t(b) * a.W + beam], 0), a.Wp - 1);
@@ -205,6 +217,23 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
       const bool ok = oct * BPO + r % BPO < a.W;
       cp4z(buf + r * ROWB + 8 * D + which * 4, prow + ((which ? col_a : col_b) & ~1), ok);
     }
+    if constexpr (CONT) {  // the parent token's raw q | k | v slices and its saved raw k
+      const int pa = parent_of(ok_l ? beam_l : 0);
+      const long long pp_l = reinterpret_cast<long long>(a.proj_prev + (int64_t(b) * a.Wp + pa) * ld);
+      const long long pr_l = reinterpret_cast<long long>(a.saved + ((int64_t(b) * a.Wp + pa) * HV + hv) * L::REC);
+#pragma unroll 4
+      for (int idx = lane; idx < 8 * 4 * CH; idx += 32) {
+        const int r = idx / (4 * CH), piece = (idx / CH) & 3, c = idx % CH;
+        const bool ok = oct * BPO + r % BPO < a.W;
+        unsigned char* dst = buf + r * ROWB + 8 * D + 16 + piece * 2 * D + c * 16;
+        // both shuffles on every lane: one iteration's lanes span two pieces
+        const __nv_bfloat16* pp = reinterpret_cast<const __nv_bfloat16*>(__shfl_sync(0xffffffffu, pp_l, r));
+        const unsigned char* pr = reinterpret_cast<const unsigned char*>(__shfl_sync(0xffffffffu, pr_l, r));
+        const void* src = piece < 3 ? static_cast<const void*>(pp + (piece == 0 ? col_q : (piece == 1 ? col_k : col_v)) + c * 8)
+                                    : static_cast<const void*>(pr + c * 16);
+        cp16z(dst, src, ok);
+      }
+    }
   };
 
   // ---- CTA prologue: TMEM, S0 (B operand), this warp's first octet, conv table, norm weight ----
@@ -221,7 +250,7 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
     }
     cp_async_commit();
   }
-  if (noct > 0) stage(oct0, wbuf);
+  if (!CONT && noct > 0) stage(oct0, wbuf);
   cp_async_commit();
   for (int c = tid; c < NCH; c += blockDim.x) {
     int ch;
@@ -258,14 +287,34 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
   // writes no A rows and reads nothing back (its TMEM lanes hold stale values).
   for (int it = 0; it < octets_per_warp; ++it) {
     const bool active = it < noct;
-    unsigned char* buf = wbuf + (it & 1) * OCTB;
-    if (it + 1 < noct) stage(oct0 + it + 1, wbuf + ((it + 1) & 1) * OCTB);
-    cp_async_commit();
-    cp_async_wait<1>();
+    unsigned char* buf = CONT ? wbuf : wbuf + (it & 1) * OCTB;
+    // CONT: the parent's delta, 1/|k| and decay straight from its record into registers
+    float2 d0s[CONT ? NT : 1];
+    float2 pka = make_float2(1.f, 1.f);
+    const int my_beam = (oct0 + it) * BPO + g % BPO;
+    if constexpr (CONT) {
+      __syncwarp();  // the previous round's reads of the single buffer are done
+      if (active) stage(oct0 + it, buf);
+      cp_async_commit();
+      const unsigned char* rec =
+          a.saved + ((int64_t(b) * a.Wp + parent_of(active && my_beam < a.W ? my_beam : 0)) * HV + hv) * L::REC;
+#pragma unroll
+      for (int jj = 0; jj < NT; ++jj)
+        d0s[jj] = *reinterpret_cast<const float2*>(rec + 2 * D + (jj * 8 + 2 * tq) * 4);
+      pka = *reinterpret_cast<const float2*>(rec + 6 * D);
+      cp_async_wait<0>();
+    } else {
+      if (it + 1 < noct) stage(oct0 + it + 1, wbuf + ((it + 1) & 1) * OCTB);
+      cp_async_commit();
+      cp_async_wait<1>();
+    }
     __syncwarp();
 
-    unsigned char* rowg = buf + g * ROWB;                                   // this thread's row
-    const unsigned char* row0 = tg ? rowg - BPO * ROWB : rowg;              // the same beam's step 0
+    unsigned char* rowg = buf + g * ROWB;  // this thread's row
+    // the conv window's previous token: the same beam's step 0 (T = 2), or the parent's staged row
+    const unsigned char* row0 = CONT ? rowg + 8 * D + 16 : (tg ? rowg - BPO * ROWB : rowg);
+    constexpr int tsec = CONT ? 1 : 0;  // CONT rows are suffix step 1
+    const int tt = CONT ? tsec : tg;
 
     // ---- q, k of this row (conv + SiLU, bf16), norms, gates, dot products --------------
     uint32_t qw[KM][4], kw[KM][4];
@@ -273,8 +322,8 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
 #pragma unroll
     for (int m = 0; m < KM; ++m) {
       const int c = 4 * m + tq;
-      conv8_silu<NCH>(sTab, 8 * c, tg, rowg + c * 16, row0 + c * 16, qw[m]);
-      conv8_silu<NCH>(sTab, D + 8 * c, tg, rowg + 2 * D + c * 16, row0 + 2 * D + c * 16, kw[m]);
+      conv8_silu<NCH>(sTab, 8 * c, tt, rowg + c * 16, row0 + c * 16, qw[m]);
+      conv8_silu<NCH>(sTab, D + 8 * c, tt, rowg + 2 * D + c * 16, row0 + 2 * D + c * 16, kw[m]);
 #pragma unroll
       for (int p = 0; p < 4; ++p) {
         const float2 qf = bf2f(qw[m][p]), kf = bf2f(kw[m][p]);
@@ -308,6 +357,34 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
         At = atp * at;
         ckq = at * dq;
         ckk = at * dk;
+      }
+    }
+    if constexpr (CONT) {  // the parent token's k (raw), 1/|k| and decay from its saved record
+      uint32_t kp[KM][4];
+#pragma unroll
+      for (int m = 0; m < KM; ++m) {
+        const uint4 u = *reinterpret_cast<const uint4*>(row0 + 6 * D + (4 * m + tq) * 16);
+        kp[m][0] = u.x;
+        kp[m][1] = u.y;
+        kp[m][2] = u.z;
+        kp[m][3] = u.w;
+      }
+      const float ikp = pka.x, atp = pka.y;
+      const float dq = chunk_dot<KM>(kp, qw) * ikp * qs;  // k_0 . q_1
+      const float dk = chunk_dot<KM>(kp, kw) * ikp * ik;  // k_0 . k_1
+      At = atp * at;
+      ckq = at * dq;
+      ckk = at * dk;
+    }
+    // first decode step with a record buffer: this row's raw k and (1/|k|, decay) for the next step
+    unsigned char* srec = nullptr;
+    if constexpr (TMAX == 1 && !CONT) {
+      if (a.save != nullptr && active && my_beam < a.W) {
+        srec = a.save + ((int64_t(b) * a.W + my_beam) * HV + hv) * L::REC;
+#pragma unroll
+        for (int m = 0; m < KM; ++m)
+          *reinterpret_cast<uint4*>(srec + (4 * m + tq) * 16) = make_uint4(kw[m][0], kw[m][1], kw[m][2], kw[m][3]);
+        if (tq == 0) *reinterpret_cast<float2*>(srec + 6 * D) = make_float2(ik, at);
       }
     }
 
@@ -381,7 +458,7 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
 #pragma unroll
       for (int j = 0; j < NH; ++j) {
         const int jj = hf * NH + j, col0 = jj * 8 + 2 * tq;
-        const float2 vx = conv2_silu<NCH>(sTab, 2 * D + col0, tg, rowg + 4 * D + col0 * 2, row0 + 4 * D + col0 * 2);
+        const float2 vx = conv2_silu<NCH>(sTab, 2 * D + col0, tt, rowg + 4 * D + col0 * 2, row0 + 4 * D + col0 * 2);
         float2 skt = mul2(make_float2(At, At), make_float2(acc[j][2], acc[j][3]));
         float2 o = mul2(make_float2(At, At), make_float2(acc[j][0], acc[j][1]));
         const float2 nb = make_float2(-bt, -bt);
@@ -395,6 +472,13 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
             d = fma2(nb, skt, mul2(make_float2(bt, bt), vx));
           }
         }
+        if constexpr (CONT) {
+          const float2 d0 = d0s[jj];
+          skt = fma2(make_float2(ckk, ckk), d0, skt);
+          o = fma2(make_float2(ckq, ckq), d0, o);
+          d = fma2(nb, skt, mul2(make_float2(bt, bt), vx));
+        }
+        if (srec != nullptr) *reinterpret_cast<float2*>(srec + 2 * D + col0 * 4) = d;
         o = fma2(d, make_float2(kq_self, kq_self), o);
         ob[jj] = bf2_pack_f2(o);  // gated_delta returns v's dtype
         const float2 of = bf2f(ob[jj]);
@@ -438,12 +522,13 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
   }
 }
 
-template <int D, int TMAX>
+template <int D, int TMAX, bool CONT = false>
 int launch_mixer(const MixerArgs& a, cudaStream_t stream) {
   using L = MixLayout<D>;
-  auto kern = gdn_mixer_kernel<D, TMAX>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L::SMEM)) != cudaSuccess) {
-    set_error("gdn mixer: cannot reserve %zu bytes of shared memory", L::SMEM);
+  auto kern = gdn_mixer_kernel<D, TMAX, CONT>;
+  constexpr size_t smem = CONT ? L::SMEM_C : L::SMEM;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess) {
+    set_error("gdn mixer: cannot reserve %zu bytes of shared memory", smem);
     return KADLLM_ECUDA;
   }
   int sms = 148;
@@ -459,7 +544,7 @@ int launch_mixer(const MixerArgs& a, cudaStream_t stream) {
   const int opw = (octets + kMixWarps * ny - 1) / (kMixWarps * ny);
   ny = (octets + kMixWarps * opw - 1) / (kMixWarps * opw);
   const dim3 grid{unsigned(heads), unsigned(ny)};
-  kern<<<grid, kMixWarps * 32, L::SMEM, stream>>>(a, opw);
+  kern<<<grid, kMixWarps * 32, smem, stream>>>(a, opw);
   KB_CHECK_LAUNCH("gdn mixer launch");
   return KADLLM_OK;
 }
@@ -470,12 +555,19 @@ bool gdn_mixer_staged_ok(const MixerArgs& a) {
   if (!(a.D == 64 || a.D == 128) || a.T < 1 || a.T > 2 || a.conv_hist < 3) return false;
   const auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   return a.status != nullptr && al16(a.proj) && al16(a.out) && al16(a.state) && a.ld_proj % 8 == 0 &&
-         (a.proj_prev == nullptr || (a.T == 2 && al16(a.proj_prev)));
+         (a.proj_prev == nullptr || (a.T == 2 && al16(a.proj_prev))) && (a.save == nullptr || (a.T == 1 && al16(a.save))) &&
+         (a.saved == nullptr || (a.T == 2 && a.proj_prev != nullptr && al16(a.saved)));
 }
 
 int gdn_mixer_staged(const MixerArgs& a, cudaStream_t stream) {
+  if (a.saved != nullptr)  // the second step from the first step's records: one row per beam
+    return a.D == 128 ? launch_mixer<128, 1, true>(a, stream) : launch_mixer<64, 1, true>(a, stream);
   if (a.D == 128) return a.T == 1 ? launch_mixer<128, 1>(a, stream) : launch_mixer<128, 2>(a, stream);
   return a.T == 1 ? launch_mixer<64, 1>(a, stream) : launch_mixer<64, 2>(a, stream);
+}
+
+int64_t gdn_mixer_record_bytes(int64_t rows, int64_t v_heads, int64_t dim) {
+  return rows * v_heads * (6 * dim + 16);
 }
 
 }  // namespace kb

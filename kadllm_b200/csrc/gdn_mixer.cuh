@@ -25,11 +25,18 @@ struct MixerArgs {
   const int32_t* parent;           // [B*W]
   int Wp;
   uint32_t* status;  // device status word: bit 0 set when a tensor-core wait timed out
+  // First decode step (T = 1): per (beam row, value head) record [raw k bf16 | delta fp32 |
+  // (1/|k|, decay)] for the next step, or null.  Continuation (T = 2 with proj_prev): the
+  // previous step's records (indexed like proj_prev), or null to replay both tokens.
+  unsigned char* save;
+  const unsigned char* saved;
 };
 
 // True when the staged kernel takes this call: D in {64, 128}, T <= 2,
 // 16-byte aligned projection rows and output, and a status word.
 bool gdn_mixer_staged_ok(const MixerArgs& a);
 int gdn_mixer_staged(const MixerArgs& a, cudaStream_t stream);
+// Bytes of the first-step records of `rows` beam rows (kadllm_gdn_mixer_record_bytes).
+int64_t gdn_mixer_record_bytes(int64_t rows, int64_t v_heads, int64_t dim);
 
 }  // namespace kb

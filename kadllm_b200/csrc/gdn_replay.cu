@@ -533,7 +533,7 @@ extern "C" int kadllm_gdn_mixer_replay(const void* proj, int64_t ld_proj, const 
                                        const float* a_log, const float* dt_bias, const float* norm_weight,
                                        float norm_eps, void* out, int64_t batch, int64_t beam_width,
                                        int64_t steps, int64_t heads, int64_t v_heads, int64_t k_dim,
-                                       int64_t v_dim, uint32_t* status, void* stream) {
+                                       int64_t v_dim, void* records, uint32_t* status, void* stream) {
   using namespace kb;
   if (int rc = check_common(batch, beam_width, steps, heads, v_heads, k_dim, v_dim)) return rc;
   KB_REQUIRE(proj && conv_state && conv_weight && rec_state && a_log && dt_bias && norm_weight && out && status,
@@ -560,8 +560,11 @@ extern "C" int kadllm_gdn_mixer_replay(const void* proj, int64_t ld_proj, const 
     m.out = static_cast<__nv_bfloat16*>(out);
     m.B = a.B; m.W = a.W; m.T = a.T; m.H = a.H; m.HV = a.HV; m.D = int(k_dim); m.scale = a.scale;
     m.status = status;
+    m.save = static_cast<unsigned char*>(records);
     if (gdn_mixer_staged_ok(m)) return gdn_mixer_staged(m, static_cast<cudaStream_t>(stream));
   }
+  KB_REQUIRE(records == nullptr, KADLLM_EUNSUPPORTED,
+             "gdn mixer: first-step records need T = 1, head dims 64 / 128 (K == V) and 16-byte aligned rows");
   return dispatch_gdn<true>(int(k_dim), int(v_dim), a, static_cast<cudaStream_t>(stream));
 }
 
@@ -571,7 +574,7 @@ extern "C" int kadllm_gdn_mixer_continue(const void* proj_prev, const int32_t* p
                                         const float* a_log, const float* dt_bias, const float* norm_weight,
                                         float norm_eps, void* out, int64_t batch, int64_t beam_width,
                                         int64_t heads, int64_t v_heads, int64_t k_dim, int64_t v_dim,
-                                        uint32_t* status, void* stream) {
+                                        const void* records, uint32_t* status, void* stream) {
   using namespace kb;
   if (int rc = check_common(batch, beam_width, 2, heads, v_heads, k_dim, v_dim)) return rc;
   KB_REQUIRE(proj_prev && parent && proj && conv_state && conv_weight && rec_state && a_log && dt_bias &&
@@ -594,7 +597,13 @@ extern "C" int kadllm_gdn_mixer_continue(const void* proj_prev, const int32_t* p
   m.scale = 1.0f / sqrtf(float(k_dim));
   m.proj_prev = static_cast<const __nv_bfloat16*>(proj_prev); m.parent = parent; m.Wp = int(prev_width);
   m.status = status;
+  m.saved = static_cast<const unsigned char*>(records);
   KB_REQUIRE(k_dim == v_dim && gdn_mixer_staged_ok(m), KADLLM_EUNSUPPORTED,
              "gdn mixer (continuation): head dims 64 / 128 (K == V), 16-byte aligned rows only");
   return gdn_mixer_staged(m, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int64_t kadllm_gdn_mixer_record_bytes(int64_t batch, int64_t beam_width, int64_t v_heads, int64_t v_dim) {
+  if (batch < 1 || beam_width < 1 || v_heads < 1 || v_dim < 1) return 0;
+  return kb::gdn_mixer_record_bytes(batch * beam_width, v_heads, v_dim);
 }

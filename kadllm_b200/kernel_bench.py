@@ -191,7 +191,7 @@ def case_mixer(gen, reps, T=1):
 
     def run():
         _lib.call("kadllm_gdn_mixer_replay", proj.data_ptr(), ld, cs.data_ptr(), 4, cw.data_ptr(), rec.data_ptr(),
-                  al.data_ptr(), dt.data_ptr(), nw.data_ptr(), 1e-6, out.data_ptr(), B, W, T, H, HV, K, K,
+                  al.data_ptr(), dt.data_ptr(), nw.data_ptr(), 1e-6, out.data_ptr(), B, W, T, H, HV, K, K, None,
                   status.data_ptr(), s)
 
     ms = _time(run, reps)
@@ -199,9 +199,10 @@ def case_mixer(gen, reps, T=1):
     return ms, "hbm", R * ld * 2 + R * HV * K * 2 + B * HV * K * K * 2 + B * C * 4 * 2
 
 
-def case_mixer_cont(gen, reps):
+def case_mixer_cont(gen, reps, saved=False):
     """kadllm_gdn_mixer_continue at the second decode step of the benchmark: 32 requests x 256
-    beams continuing from 256 parents (random parent indices)."""
+    beams continuing from 256 parents (random parent indices); ``saved``: from the first
+    step's records (the new tokens only), else replaying the parents' tokens too."""
     dev, bf = torch.device("cuda"), torch.bfloat16
     B, W, Wp, H, HV, K = 32, 256, 256, 16, 16, 128
     C = 2 * H * K + HV * K
@@ -218,14 +219,24 @@ def case_mixer_cont(gen, reps):
     out = torch.empty(B * W, HV * K, device=dev, dtype=bf)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     s = _lib.stream(dev)
+    records = None
+    if saved:  # the first step over the parents, writing their records
+        records = torch.empty(_lib.lib().kadllm_gdn_mixer_record_bytes(B, Wp, HV, K), dtype=torch.uint8, device=dev)
+        out1 = torch.empty(B * Wp, HV * K, device=dev, dtype=bf)
+        _lib.call("kadllm_gdn_mixer_replay", prev.data_ptr(), ld, cs.data_ptr(), 4, cw.data_ptr(), rec.data_ptr(),
+                  al.data_ptr(), dt.data_ptr(), nw.data_ptr(), 1e-6, out1.data_ptr(), B, Wp, 1, H, HV, K, K,
+                  records.data_ptr(), status.data_ptr(), s)
 
     def run():
         _lib.call("kadllm_gdn_mixer_continue", prev.data_ptr(), parent.data_ptr(), Wp, proj.data_ptr(), ld,
                   cs.data_ptr(), 4, cw.data_ptr(), rec.data_ptr(), al.data_ptr(), dt.data_ptr(), nw.data_ptr(),
-                  1e-6, out.data_ptr(), B, W, H, HV, K, K, status.data_ptr(), s)
+                  1e-6, out.data_ptr(), B, W, H, HV, K, K, _lib.ptr(records), status.data_ptr(), s)
 
     ms = _time(run, reps)
     R = B * W
+    if saved:  # the new rows, the parents' q | k | v columns and records, the output, state and taps
+        nbytes = R * ld * 2 + R * (3 * H * K * 2 + HV * (6 * K + 16)) + R * HV * K * 2 + B * HV * K * K * 2 + B * C * 8
+        return ms, "hbm", nbytes
     return ms, "hbm", 2 * R * ld * 2 + R * HV * K * 2 + B * HV * K * K * 2 + B * C * 4 * 2
 
 
@@ -313,7 +324,8 @@ def case_gemm(gen, reps, M, N, K, epilogue=0):
 
 CASES = {"prefill": case_prefill, "prefill8": lambda g, r: case_prefill(g, r, B=8), "attn_tiled": case_attn_tiled, "attn_split": case_attn_split, "conv": case_conv, "attn": case_attn, "mixer": case_mixer,
          "mixer2": lambda g, r: case_mixer(g, r, T=2), "select": case_select, "replay": case_replay,
-         "mixer_cont": case_mixer_cont, "qk_rope": case_qk_rope,
+         "mixer_cont": case_mixer_cont, "mixer_cont_saved": lambda g, r: case_mixer_cont(g, r, saved=True),
+         "qk_rope": case_qk_rope,
          "attn_step": lambda g, r: case_attn_tiled(g, r, B=32, W=256, T=2, L=1024),
          "attn_causal": lambda g, r: case_attn_tiled(g, r, B=32, W=1, T=1, L=1024, causal=True),
          # the step's projections: prefill (32 x 1024 rows) and decode (32 x 256 beams, T = 1)

@@ -252,6 +252,11 @@ class HybridModel:
                   self.status.data_ptr(), self._stream())
         return out
 
+    def _mixer_records_ok(self) -> bool:
+        """The staged decode mixer keeps first-step records (head dims 64 / 128, K == V)."""
+        c = self.cfg
+        return c.linear_key_head_dim == c.linear_value_head_dim and c.linear_key_head_dim in (64, 128)
+
     def _mlp(self, layer: Layer, normed, x):
         """x += down(silu(gate(normed)) * up(normed)): two GEMMs, the activation and the
         residual update in their epilogues (per layer width: WideTuning-merged layers are wider)."""
@@ -482,13 +487,18 @@ class HybridModel:
             if layer.kind == LINEAR:
                 out = torch.empty(R, c.value_dim, dtype=BF16, device=self.device)
                 conv_state, rec = cached
+                # the first decode step keeps each beam's k, delta and decay for the next step
+                records = None
+                if cache is not None and T == 1 and self._mixer_records_ok():
+                    records = torch.empty(_lib.lib().kadllm_gdn_mixer_record_bytes(
+                        B, W, c.linear_num_value_heads, c.linear_value_head_dim), dtype=torch.uint8, device=self.device)
                 _lib.call("kadllm_gdn_mixer_replay", P.data_ptr(), P.stride(0), conv_state.data_ptr(),
                           conv_state.shape[-1], m.conv_w.data_ptr(), rec.data_ptr(), m.a_log.data_ptr(),
                           m.dt_bias.data_ptr(), m.norm_w.data_ptr(), c.rms_norm_eps, out.data_ptr(), B, W, T,
                           c.linear_num_key_heads, c.linear_num_value_heads, c.linear_key_head_dim,
-                          c.linear_value_head_dim, self.status.data_ptr(), s)
+                          c.linear_value_head_dim, _lib.ptr(records), self.status.data_ptr(), s)
                 if cache is not None:
-                    cache[i] = P
+                    cache[i] = (P, records)
                 self._gemm(out, m.w_out, resid=x)
             else:
                 q = torch.empty(R, hq, D, dtype=BF16, device=self.device)
@@ -568,12 +578,13 @@ class HybridModel:
             if layer.kind == LINEAR:
                 out = torch.empty(R, c.value_dim, dtype=BF16, device=self.device)
                 conv_state, rec = cached
-                P0 = prev[i]
+                P0, records = prev[i]  # the previous step's projection rows and records (or None)
                 _lib.call("kadllm_gdn_mixer_continue", P0.data_ptr(), parent.data_ptr(), prev_width, P.data_ptr(),
                           P.stride(0), conv_state.data_ptr(), conv_state.shape[-1], m.conv_w.data_ptr(),
                           rec.data_ptr(), m.a_log.data_ptr(), m.dt_bias.data_ptr(), m.norm_w.data_ptr(),
                           c.rms_norm_eps, out.data_ptr(), B, W, c.linear_num_key_heads, c.linear_num_value_heads,
-                          c.linear_key_head_dim, c.linear_value_head_dim, self.status.data_ptr(), s)
+                          c.linear_key_head_dim, c.linear_value_head_dim, _lib.ptr(records), self.status.data_ptr(),
+                          s)
                 self._gemm(out, m.w_out, resid=x)
             else:
                 q = torch.empty(R, 2, hq, D, dtype=BF16, device=self.device)

@@ -40,7 +40,8 @@ def test_signatures_cover_every_compute_entry_point():
     compute = [n for n in declared_functions()
                if n not in ("kadllm_last_error", "kadllm_abi_version", "kadllm_beam_select_workspace",
                             "kadllm_gdn_prefill_workspace", "kadllm_kv_tile_bytes",
-                            "kadllm_beam_select_workspace_fused", "kadllm_attention_split_workspace")]
+                            "kadllm_beam_select_workspace_fused", "kadllm_attention_split_workspace",
+                            "kadllm_gdn_mixer_record_bytes")]
     assert sorted(compute) == sorted(_lib.SIGNATURES)
 
 

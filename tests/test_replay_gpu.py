@@ -202,7 +202,7 @@ def _mixer_case(T, K, H, HV, B, W):
             _t(dt_bias, torch.float32), _t(nw, torch.float32)]
     _lib.call("kadllm_gdn_mixer_replay", tp.data_ptr(), ld, args[0].data_ptr(), 4, args[1].data_ptr(),
               args[2].data_ptr(), args[3].data_ptr(), args[4].data_ptr(), args[5].data_ptr(), 1e-6,
-              out.data_ptr(), B, W, T, H, HV, K, K, status.data_ptr(), _lib.stream(tp.device))
+              out.data_ptr(), B, W, T, H, HV, K, K, None, status.data_ptr(), _lib.stream(tp.device))
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     # oracle chain (src/kadllm/adapters/qwen3_5.py:144-177)

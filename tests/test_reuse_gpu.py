@@ -48,14 +48,30 @@ def test_mixer_continue_equals_two_token_replay(K, H, HV, B, W, Wp):
     full = torch.empty(B * W * 2, vd, dtype=bf, device="cuda")
     _lib.call("kadllm_gdn_mixer_replay", both.data_ptr(), ld, conv_state.data_ptr(), 4, conv_w.data_ptr(),
               rec.data_ptr(), a_log.data_ptr(), dt_bias.data_ptr(), nw.data_ptr(), 1e-6, full.data_ptr(), B, W, 2,
-              H, HV, K, K, status.data_ptr(), s)
+              H, HV, K, K, None, status.data_ptr(), s)
     cont = torch.empty(B * W, vd, dtype=bf, device="cuda")
     _lib.call("kadllm_gdn_mixer_continue", prev.data_ptr(), parent.data_ptr(), Wp, new.data_ptr(), ld,
               conv_state.data_ptr(), 4, conv_w.data_ptr(), rec.data_ptr(), a_log.data_ptr(), dt_bias.data_ptr(),
-              nw.data_ptr(), 1e-6, cont.data_ptr(), B, W, H, HV, K, K, status.data_ptr(), s)
+              nw.data_ptr(), 1e-6, cont.data_ptr(), B, W, H, HV, K, K, None, status.data_ptr(), s)
+    # the first step over the parents with records, then the new tokens only from them
+    records = torch.empty(_lib.lib().kadllm_gdn_mixer_record_bytes(B, Wp, HV, K), dtype=torch.uint8, device="cuda")
+    first = torch.empty(B * Wp, vd, dtype=bf, device="cuda")
+    plain = torch.empty(B * Wp, vd, dtype=bf, device="cuda")
+    _lib.call("kadllm_gdn_mixer_replay", prev.data_ptr(), ld, conv_state.data_ptr(), 4, conv_w.data_ptr(),
+              rec.data_ptr(), a_log.data_ptr(), dt_bias.data_ptr(), nw.data_ptr(), 1e-6, first.data_ptr(), B, Wp, 1,
+              H, HV, K, K, records.data_ptr(), status.data_ptr(), s)
+    _lib.call("kadllm_gdn_mixer_replay", prev.data_ptr(), ld, conv_state.data_ptr(), 4, conv_w.data_ptr(),
+              rec.data_ptr(), a_log.data_ptr(), dt_bias.data_ptr(), nw.data_ptr(), 1e-6, plain.data_ptr(), B, Wp, 1,
+              H, HV, K, K, None, status.data_ptr(), s)
+    cont_saved = torch.empty(B * W, vd, dtype=bf, device="cuda")
+    _lib.call("kadllm_gdn_mixer_continue", prev.data_ptr(), parent.data_ptr(), Wp, new.data_ptr(), ld,
+              conv_state.data_ptr(), 4, conv_w.data_ptr(), rec.data_ptr(), a_log.data_ptr(), dt_bias.data_ptr(),
+              nw.data_ptr(), 1e-6, cont_saved.data_ptr(), B, W, H, HV, K, K, records.data_ptr(), status.data_ptr(), s)
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     assert torch.equal(cont, full.view(B * W, 2, vd)[:, 1])
+    assert torch.equal(first, plain)  # writing the records leaves the first step's output alone
+    assert torch.equal(cont_saved, cont)
 
 
 def test_gather_rows_by_parent():
