@@ -79,9 +79,9 @@ KADLLM_API int kadllm_gated_delta_replay(const void* q, const void* k, const voi
  *   a_log, dt_bias [HV] f32; norm_weight [V] f32 (values of the BF16 params)
  *   out         [BW*T, HV*V] bf16
  *   records     null, or (steps == 1, K == V in {64, 128}) kadllm_gdn_mixer_record_bytes
- *               bytes, 16-byte aligned: per (beam row, value head) the row's raw k
- *               (bf16), its delta (fp32) and (1/|k|, decay), from which
- *               kadllm_gdn_mixer_continue runs the next step on the new tokens only
+ *               bytes, 16-byte aligned: per (beam row, value head) the row's delta
+ *               beta (v - S^T k) (V fp32 values), from which kadllm_gdn_mixer_continue
+ *               runs the next step on the new tokens only
  *   status      device uint32: bit 0 set when a tensor-core wait timed out
  *               (read it after the stream synchronises; the output is then invalid)
  * ------------------------------------------------------------------------ */
@@ -403,7 +403,8 @@ KADLLM_API int kadllm_gather_rows(const void* src, int64_t ld_src, const int32_t
  * recomputing the first token's projection.  Head dims 64 / 128 (K == V).
  * records: null (the first token is replayed from proj_prev), or the previous
  * step's records (kadllm_gdn_mixer_replay, indexed like proj_prev): the first
- * token's k, delta and decay come from them and only the new token is computed. */
+ * token's delta comes from them (its k and decay are recomputed from proj_prev)
+ * and only the new token runs against the state. */
 KADLLM_API int kadllm_gdn_mixer_continue(const void* proj_prev, const int32_t* parent, int64_t prev_width,
                                          const void* proj, int64_t ld_proj, const void* conv_state,
                                          int64_t conv_hist, const void* conv_weight, const void* rec_state,

@@ -60,11 +60,11 @@ struct MixLayout {
   static constexpr int OCTB = 8 * ROWB;     // one staged octet: 8 (beam, token) rows
   static constexpr size_t SMEM = size_t(S0B) + TABB + NWB + size_t(kMixWarps) * 2 * OCTB + 16;  // + mbarrier, TMEM slot
   // continuation from a saved first step: a row also stages the parent token's raw q | k | v
-  // slices and its saved raw k (one buffer per warp: two CTAs per SM)
-  static constexpr int ROWB_C = ROWB + 8 * D;
+  // slices and its gate word a (one buffer per warp: two CTAs per SM)
+  static constexpr int ROWB_C = ROWB + 6 * D + 16;
   static constexpr int OCTB_C = 8 * ROWB_C;
   static constexpr size_t SMEM_C = size_t(S0B) + TABB + NWB + size_t(kMixWarps) * OCTB_C + 16;
-  static constexpr int REC = 6 * D + 16;    // saved record per (beam, head): raw k bf16 | delta fp32 | (1/|k|, decay)
+  static constexpr int REC = 4 * D;         // saved record per (beam, head): the token's delta, fp32
 };
 
 // MMA k index (B row) of state row r = 32m + 8tq + 2p + d: 32m + 16(p / 2) + 4tq + 2(p % 2) + d.
@@ -143,8 +143,9 @@ __device__ __forceinline__ float chunk_dot(const uint32_t (&x)[KM][4], const uin
 }
 
 // CONT (TMAX = 1): the second decode step from the first step's saved records -- octets
-// of 8 beams, each row the beam's new token, with the parent token's k, delta and decay
-// from its record and its raw q | k | v for the conv window.
+// of 8 beams, each row the beam's new token.  The parent token's delta comes from its
+// record; its raw q | k | v (the conv window) and gate word a are staged, and its k,
+// 1/|k| and decay are recomputed from them exactly as its own first step did.
 template <int D, int TMAX, bool CONT>
 __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerArgs a, int octets_per_warp) {
   using L = MixLayout<D>;
@@ -217,22 +218,19 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
       const bool ok = oct * BPO + r % BPO < a.W;
       cp4z(buf + r * ROWB + 8 * D + which * 4, prow + ((which ? col_a : col_b) & ~1), ok);
     }
-    if constexpr (CONT) {  // the parent token's raw q | k | v slices and its saved raw k
-      const int pa = parent_of(ok_l ? beam_l : 0);
-      const long long pp_l = reinterpret_cast<long long>(a.proj_prev + (int64_t(b) * a.Wp + pa) * ld);
-      const long long pr_l = reinterpret_cast<long long>(a.saved + ((int64_t(b) * a.Wp + pa) * HV + hv) * L::REC);
+    if constexpr (CONT) {  // the parent token's raw q | k | v slices and its gate word a
+      const long long pp_l =
+          reinterpret_cast<long long>(a.proj_prev + (int64_t(b) * a.Wp + parent_of(ok_l ? beam_l : 0)) * ld);
 #pragma unroll 4
-      for (int idx = lane; idx < 8 * 4 * CH; idx += 32) {
-        const int r = idx / (4 * CH), piece = (idx / CH) & 3, c = idx % CH;
+      for (int idx = lane; idx < 8 * 3 * CH; idx += 32) {
+        const int r = idx / (3 * CH), piece = (idx / CH) % 3, c = idx % CH;
         const bool ok = oct * BPO + r % BPO < a.W;
-        unsigned char* dst = buf + r * ROWB + 8 * D + 16 + piece * 2 * D + c * 16;
-        // both shuffles on every lane: one iteration's lanes span two pieces
         const __nv_bfloat16* pp = reinterpret_cast<const __nv_bfloat16*>(__shfl_sync(0xffffffffu, pp_l, r));
-        const unsigned char* pr = reinterpret_cast<const unsigned char*>(__shfl_sync(0xffffffffu, pr_l, r));
-        const void* src = piece < 3 ? static_cast<const void*>(pp + (piece == 0 ? col_q : (piece == 1 ? col_k : col_v)) + c * 8)
-                                    : static_cast<const void*>(pr + c * 16);
-        cp16z(dst, src, ok);
+        cp16z(buf + r * ROWB + 8 * D + 16 + piece * 2 * D + c * 16,
+              pp + (piece == 0 ? col_q : (piece == 1 ? col_k : col_v)) + c * 8, ok);
       }
+      const __nv_bfloat16* pp = reinterpret_cast<const __nv_bfloat16*>(__shfl_sync(0xffffffffu, pp_l, lane & 7));
+      if (lane < 8) cp4z(buf + lane * ROWB + 14 * D + 16, pp + (col_a & ~1), oct * BPO + lane < a.W);
     }
   };
 
@@ -288,9 +286,8 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
   for (int it = 0; it < octets_per_warp; ++it) {
     const bool active = it < noct;
     unsigned char* buf = CONT ? wbuf : wbuf + (it & 1) * OCTB;
-    // CONT: the parent's delta, 1/|k| and decay straight from its record into registers
+    // CONT: the parent's delta straight from its record into registers
     float2 d0s[CONT ? NT : 1];
-    float2 pka = make_float2(1.f, 1.f);
     const int my_beam = (oct0 + it) * BPO + g % BPO;
     if constexpr (CONT) {
       __syncwarp();  // the previous round's reads of the single buffer are done
@@ -299,9 +296,7 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
       const unsigned char* rec =
           a.saved + ((int64_t(b) * a.Wp + parent_of(active && my_beam < a.W ? my_beam : 0)) * HV + hv) * L::REC;
 #pragma unroll
-      for (int jj = 0; jj < NT; ++jj)
-        d0s[jj] = *reinterpret_cast<const float2*>(rec + 2 * D + (jj * 8 + 2 * tq) * 4);
-      pka = *reinterpret_cast<const float2*>(rec + 6 * D);
+      for (int jj = 0; jj < NT; ++jj) d0s[jj] = *reinterpret_cast<const float2*>(rec + (jj * 8 + 2 * tq) * 4);
       cp_async_wait<0>();
     } else {
       if (it + 1 < noct) stage(oct0 + it + 1, wbuf + ((it + 1) & 1) * OCTB);
@@ -359,33 +354,34 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
         ckk = at * dk;
       }
     }
-    if constexpr (CONT) {  // the parent token's k (raw), 1/|k| and decay from its saved record
+    if constexpr (CONT) {
+      // the parent token's k, 1/|k| and decay, recomputed from its staged raw row exactly as
+      // its own first step computed them (conv at suffix step 0, the same summation order)
       uint32_t kp[KM][4];
+      float2 skp = make_float2(0.f, 0.f);
 #pragma unroll
       for (int m = 0; m < KM; ++m) {
-        const uint4 u = *reinterpret_cast<const uint4*>(row0 + 6 * D + (4 * m + tq) * 16);
-        kp[m][0] = u.x;
-        kp[m][1] = u.y;
-        kp[m][2] = u.z;
-        kp[m][3] = u.w;
+        const int c = 4 * m + tq;
+        conv8_silu<NCH>(sTab, D + 8 * c, 0, row0 + 2 * D + c * 16, row0 + 2 * D + c * 16, kp[m]);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const float2 kf = bf2f(kp[m][p]);
+          skp = fma2(kf, kf, skp);
+        }
       }
-      const float ikp = pka.x, atp = pka.y;
+      const float ikp = 1.0f / sqrtf(quad_sum(skp.x + skp.y) + 1e-6f);
+      const __nv_bfloat162 apw = *reinterpret_cast<const __nv_bfloat162*>(row0 + 6 * D);
+      const float atp = expf(neg_a * softplus_f(__bfloat162float((col_a & 1) ? apw.y : apw.x) + dtb));
       const float dq = chunk_dot<KM>(kp, qw) * ikp * qs;  // k_0 . q_1
       const float dk = chunk_dot<KM>(kp, kw) * ikp * ik;  // k_0 . k_1
       At = atp * at;
       ckq = at * dq;
       ckk = at * dk;
     }
-    // first decode step with a record buffer: this row's raw k and (1/|k|, decay) for the next step
+    // first decode step with a record buffer: this row's delta for the next step
     unsigned char* srec = nullptr;
     if constexpr (TMAX == 1 && !CONT) {
-      if (a.save != nullptr && active && my_beam < a.W) {
-        srec = a.save + ((int64_t(b) * a.W + my_beam) * HV + hv) * L::REC;
-#pragma unroll
-        for (int m = 0; m < KM; ++m)
-          *reinterpret_cast<uint4*>(srec + (4 * m + tq) * 16) = make_uint4(kw[m][0], kw[m][1], kw[m][2], kw[m][3]);
-        if (tq == 0) *reinterpret_cast<float2*>(srec + 6 * D) = make_float2(ik, at);
-      }
+      if (a.save != nullptr && active && my_beam < a.W) srec = a.save + ((int64_t(b) * a.W + my_beam) * HV + hv) * L::REC;
     }
 
     // ---- A = [q ; k] (bf16 hi, lo) into TMEM; one thread runs the MMAs against S0 ---------
@@ -478,7 +474,7 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
           o = fma2(make_float2(ckq, ckq), d0, o);
           d = fma2(nb, skt, mul2(make_float2(bt, bt), vx));
         }
-        if (srec != nullptr) *reinterpret_cast<float2*>(srec + 2 * D + col0 * 4) = d;
+        if (srec != nullptr) *reinterpret_cast<float2*>(srec + col0 * 4) = d;
         o = fma2(d, make_float2(kq_self, kq_self), o);
         ob[jj] = bf2_pack_f2(o);  // gated_delta returns v's dtype
         const float2 of = bf2f(ob[jj]);
@@ -567,7 +563,7 @@ int gdn_mixer_staged(const MixerArgs& a, cudaStream_t stream) {
 }
 
 int64_t gdn_mixer_record_bytes(int64_t rows, int64_t v_heads, int64_t dim) {
-  return rows * v_heads * (6 * dim + 16);
+  return rows * v_heads * 4 * dim;
 }
 
 }  // namespace kb

@@ -25,8 +25,8 @@ struct MixerArgs {
   const int32_t* parent;           // [B*W]
   int Wp;
   uint32_t* status;  // device status word: bit 0 set when a tensor-core wait timed out
-  // First decode step (T = 1): per (beam row, value head) record [raw k bf16 | delta fp32 |
-  // (1/|k|, decay)] for the next step, or null.  Continuation (T = 2 with proj_prev): the
+  // First decode step (T = 1): per (beam row, value head) record of the row's delta (fp32)
+  // for the next step, or null.  Continuation (T = 2 with proj_prev): the
   // previous step's records (indexed like proj_prev), or null to replay both tokens.
   unsigned char* save;
   const unsigned char* saved;

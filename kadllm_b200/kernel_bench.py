@@ -234,8 +234,8 @@ def case_mixer_cont(gen, reps, saved=False):
 
     ms = _time(run, reps)
     R = B * W
-    if saved:  # the new rows, the parents' q | k | v columns and records, the output, state and taps
-        nbytes = R * ld * 2 + R * (3 * H * K * 2 + HV * (6 * K + 16)) + R * HV * K * 2 + B * HV * K * K * 2 + B * C * 8
+    if saved:  # the new rows, the parents' q | k | v columns, gate a and records, the output, state and taps
+        nbytes = R * ld * 2 + R * (C * 2 + HV * 2 + HV * 4 * K) + R * HV * K * 2 + B * HV * K * K * 2 + B * C * 8
         return ms, "hbm", nbytes
     return ms, "hbm", 2 * R * ld * 2 + R * HV * K * 2 + B * HV * K * K * 2 + B * C * 4 * 2
 

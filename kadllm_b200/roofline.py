@@ -48,14 +48,18 @@ def work_of(name: str, args: tuple) -> tuple[str, float] | None:
         R = B * W * T
         conv_dim = 2 * H * DK + HV * DV
         read = R * (conv_dim + HV * DV + 2 * HV) * 2 + B * HV * DK * DV * 2 + B * conv_dim * 4 * 2
-        return "hbm", float(read + R * HV * DV * 2)
+        records = R * HV * DV * 4 if args[18] is not None else 0  # the first step's deltas, fp32
+        return "hbm", float(read + R * HV * DV * 2 + records)
     if name == "kadllm_gdn_mixer_continue":
-        # the new rows and their parents' previous-step rows (q | k | v | z | b | a columns),
-        # the request's state and conv taps, the new rows' output
+        # the new rows (q | k | v | z | b | a columns), the request's state and conv taps, the
+        # new rows' output, and either the parents' previous-step rows or, from records, the
+        # parents' q | k | v | a columns and deltas
         B, W, H, HV, DK, DV = args[14:20]
         R = B * W
         conv_dim = 2 * H * DK + HV * DV
-        read = 2 * R * (conv_dim + HV * DV + 2 * HV) * 2 + B * HV * DK * DV * 2 + B * conv_dim * 4 * 2
+        new = R * (conv_dim + HV * DV + 2 * HV) * 2
+        parents = R * (conv_dim + 2 * HV) * 2 + R * HV * DV * 4 if args[20] is not None else new
+        read = new + parents + B * HV * DK * DV * 2 + B * conv_dim * 4 * 2
         return "hbm", float(read + R * HV * DV * 2)
     if name == "kadllm_beam_select":
         B, Wp, V, W, depth = args[11:16]
@@ -84,6 +88,8 @@ def measured_traffic(name: str, args: tuple) -> float | None:
         return {1: 181.0e6, 2: 353.6e6}.get(args[13])  # T = 1: 164.6 + 16.4 MB; T = 2: 306.0 + 47.6 MB
     if (name == "kadllm_gdn_mixer_continue" and args[2] == 256 and tuple(args[14:16]) == (32, 256)
             and tuple(args[16:20]) == (16, 16, 128, 128)):
+        if args[20] is not None:  # from the first step's records: not captured
+            return None
         return 295.8e6  # 273.6 + 22.2 MB (random parents: children of one parent share its rows in L2)
     if name == "kadllm_attention_tiled" and (args[24], *args[28:32]) == (32, 8, 2, 1024, 256):
         if args[33]:  # causal prefill: 335.6 + 109.8 MB
