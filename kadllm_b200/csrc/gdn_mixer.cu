@@ -187,7 +187,6 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
   // the parent's row of the previous step (tr = 0) / the beam's row of the new token.
   auto parent_of = [&](int beam) { return min(max(a.parent[int64_t(b) * a.W + beam], 0), a.Wp - 1); };
   auto prow_of = [&](int tr, int beam) -> const __nv_bfloat16* {
-    if (CONT) return a.proj + (int64_t(b) * a.W + beam) * ld;
     if (TMAX == 2 && a.proj_prev != nullptr) {
       if (tr == 0) {
         const int p = min(max(a.parent[int64_t(b) * a.W + beam], 0), a.Wp - 1);
@@ -218,19 +217,44 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
       const bool ok = oct * BPO + r % BPO < a.W;
       cp4z(buf + r * ROWB + 8 * D + which * 4, prow + ((which ? col_a : col_b) & ~1), ok);
     }
-    if constexpr (CONT) {  // the parent token's raw q | k | v slices and its gate word a
-      const long long pp_l =
-          reinterpret_cast<long long>(a.proj_prev + (int64_t(b) * a.Wp + parent_of(ok_l ? beam_l : 0)) * ld);
+  };
+  // CONT stages an octet in two parts into its single buffer: part qk (the new rows' q | k
+  // slices and gate words, the parents' q | k slices and gate word a), read by the conv and
+  // the dot products, and part vz (the new rows' v | z slices, the parents' v slices), read
+  // by the recurrence and the norm.  The next octet's part qk loads once this octet's conv
+  // is done and its part vz once this octet's output has left, each behind the other half
+  // of the round.  The output goes out through the v slice (free after the recurrence).
+  auto stage_cont = [&](int oct, unsigned char* buf, bool qk) {
+    const int rl = lane & 7, beam_l = oct * BPO + rl;
+    const bool ok_l = beam_l < a.W;
+    const long long prow_l = reinterpret_cast<long long>(a.proj + (int64_t(b) * a.W + (ok_l ? beam_l : 0)) * ld);
+    const long long pp_l =
+        reinterpret_cast<long long>(a.proj_prev + (int64_t(b) * a.Wp + parent_of(ok_l ? beam_l : 0)) * ld);
 #pragma unroll 4
-      for (int idx = lane; idx < 8 * 3 * CH; idx += 32) {
-        const int r = idx / (3 * CH), piece = (idx / CH) % 3, c = idx % CH;
-        const bool ok = oct * BPO + r % BPO < a.W;
-        const __nv_bfloat16* pp = reinterpret_cast<const __nv_bfloat16*>(__shfl_sync(0xffffffffu, pp_l, r));
-        cp16z(buf + r * ROWB + 8 * D + 16 + piece * 2 * D + c * 16,
-              pp + (piece == 0 ? col_q : (piece == 1 ? col_k : col_v)) + c * 8, ok);
-      }
+    for (int idx = lane; idx < 8 * 2 * CH; idx += 32) {  // two slices of each new row
+      const int r = idx / (2 * CH), piece = (qk ? 0 : 2) + ((idx / CH) & 1), c = idx % CH;
+      const __nv_bfloat16* prow = reinterpret_cast<const __nv_bfloat16*>(__shfl_sync(0xffffffffu, prow_l, r));
+      const int col = piece < 2 ? (piece == 0 ? col_q : col_k) : (piece == 2 ? col_v : col_z);
+      cp16z(buf + r * ROWB + piece * 2 * D + c * 16, prow + col + c * 8, oct * BPO + r < a.W);
+    }
+    const int per = qk ? 2 * CH : CH;  // the parents' q | k slices, or their v slices
+#pragma unroll 4
+    for (int idx = lane; idx < 8 * per; idx += 32) {
+      const int r = idx / per, piece = qk ? (idx / CH) & 1 : 2, c = idx % CH;
+      const __nv_bfloat16* pp = reinterpret_cast<const __nv_bfloat16*>(__shfl_sync(0xffffffffu, pp_l, r));
+      cp16z(buf + r * ROWB + 8 * D + 16 + piece * 2 * D + c * 16,
+            pp + (piece == 0 ? col_q : (piece == 1 ? col_k : col_v)) + c * 8, oct * BPO + r < a.W);
+    }
+    if (qk) {  // lanes 0-15: the new rows' gate words b, a; lanes 16-23: the parents' a
+      const __nv_bfloat16* prow =
+          reinterpret_cast<const __nv_bfloat16*>(__shfl_sync(0xffffffffu, prow_l, (lane >> 1) & 7));
       const __nv_bfloat16* pp = reinterpret_cast<const __nv_bfloat16*>(__shfl_sync(0xffffffffu, pp_l, lane & 7));
-      if (lane < 8) cp4z(buf + lane * ROWB + 14 * D + 16, pp + (col_a & ~1), oct * BPO + lane < a.W);
+      if (lane < 16) {
+        const int r = lane >> 1, which = lane & 1;
+        cp4z(buf + r * ROWB + 8 * D + which * 4, prow + ((which ? col_a : col_b) & ~1), oct * BPO + r < a.W);
+      } else if (lane < 24) {
+        cp4z(buf + (lane - 16) * ROWB + 14 * D + 16, pp + (col_a & ~1), oct * BPO + (lane - 16) < a.W);
+      }
     }
   };
 
@@ -248,8 +272,15 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
     }
     cp_async_commit();
   }
-  if (!CONT && noct > 0) stage(oct0, wbuf);
-  cp_async_commit();
+  if constexpr (CONT) {  // both parts of this warp's first octet
+    if (noct > 0) stage_cont(oct0, wbuf, true);
+    cp_async_commit();
+    if (noct > 0) stage_cont(oct0, wbuf, false);
+    cp_async_commit();
+  } else {
+    if (noct > 0) stage(oct0, wbuf);
+    cp_async_commit();
+  }
   for (int c = tid; c < NCH; c += blockDim.x) {
     int ch;
     if (c < D) ch = h * D + c;
@@ -271,7 +302,7 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
   }
   for (int i = tid; i < D; i += blockDim.x) sNw[i] = a.norm_weight[i];
   const float neg_a = -expf(a.a_log[hv]), dtb = a.dt_bias[hv];
-  cp_async_wait<1>();       // S0 landed (the octet copies may still be in flight)
+  cp_async_wait<CONT ? 2 : 1>();  // S0 landed (the octet copies may still be in flight)
   tc::fence_async_smem();   // ... and visible to the tensor cores
   tc::fence_before();
   __syncthreads();
@@ -290,14 +321,11 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
     float2 d0s[CONT ? NT : 1];
     const int my_beam = (oct0 + it) * BPO + g % BPO;
     if constexpr (CONT) {
-      __syncwarp();  // the previous round's reads of the single buffer are done
-      if (active) stage(oct0 + it, buf);
-      cp_async_commit();
       const unsigned char* rec =
           a.saved + ((int64_t(b) * a.Wp + parent_of(active && my_beam < a.W ? my_beam : 0)) * HV + hv) * L::REC;
 #pragma unroll
       for (int jj = 0; jj < NT; ++jj) d0s[jj] = *reinterpret_cast<const float2*>(rec + (jj * 8 + 2 * tq) * 4);
-      cp_async_wait<0>();
+      cp_async_wait<1>();  // this octet's part qk (its part vz may still be in flight)
     } else {
       if (it + 1 < noct) stage(oct0 + it + 1, wbuf + ((it + 1) & 1) * OCTB);
       cp_async_commit();
@@ -378,6 +406,11 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
       ckq = at * dq;
       ckk = at * dk;
     }
+    if constexpr (CONT) {  // part qk read: the next octet's part qk
+      __syncwarp();
+      if (it + 1 < noct) stage_cont(oct0 + it + 1, buf, true);
+      cp_async_commit();
+    }
     // first decode step with a record buffer: this row's delta for the next step
     unsigned char* srec = nullptr;
     if constexpr (TMAX == 1 && !CONT) {
@@ -434,6 +467,10 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
     if (!active) continue;
     ok = tc::mbar_wait(mbar, uint32_t(it) & 1u, kWait) && ok;
     tc::fence_after();
+    if constexpr (CONT) {
+      cp_async_wait<1>();  // this octet's part vz (the next octet's part qk may still be in flight)
+      __syncwarp();
+    }
 
     // ---- recurrence and gated RMSNorm over the accumulator, in two column halves ---------
     uint32_t ob[NT];
@@ -481,7 +518,9 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
         ss = fmaf(of.x, of.x, fmaf(of.y, of.y, ss));
       }
     }
-    // gated RMSNorm, written over this row's staged q slice (read only by the prep above)
+    // gated RMSNorm, written over this row's staged q slice (read only by the prep above), or
+    // in CONT over its v slice (the q slice may already hold the next octet's)
+    constexpr int kOut = CONT ? 4 * D : 0;
     const float inv = 1.0f / sqrtf(quad_sum(ss) / float(D) + a.norm_eps);
 #pragma unroll
     for (int jj = 0; jj < NT; ++jj) {
@@ -492,7 +531,7 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
       const float2 sz = silu2(z);
       const float2 n = bf2f(bf2_pack(of.x * inv, of.y * inv));  // bf16(o * inv), the pair in one conversion
       const float2 h = bf2f(bf2_pack(w.x * n.x, w.y * n.y));    // bf16(w * .)
-      *reinterpret_cast<uint32_t*>(rowg + col * 2) = bf2_pack(h.x * sz.x, h.y * sz.y);
+      *reinterpret_cast<uint32_t*>(rowg + kOut + col * 2) = bf2_pack(h.x * sz.x, h.y * sz.y);
     }
     __syncwarp();
     // ---- the octet's output rows, 16 bytes per store ------------------------------------
@@ -503,10 +542,14 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
       if (beam < a.W && (!cont || r / BPO == 1)) {
         const int64_t orow = cont ? int64_t(b) * a.W + beam : (int64_t(b) * a.W + beam) * TMAX + r / BPO;
         *reinterpret_cast<uint4*>(a.out + orow * (int64_t(HV) * D) + hv * D + c * 8) =
-            *reinterpret_cast<const uint4*>(buf + r * ROWB + c * 16);
+            *reinterpret_cast<const uint4*>(buf + r * ROWB + kOut + c * 16);
       }
     }
     __syncwarp();
+    if constexpr (CONT) {  // part vz read: the next octet's part vz
+      if (it + 1 < noct) stage_cont(oct0 + it + 1, buf, false);
+      cp_async_commit();
+    }
   }
   cp_async_wait<0>();
   if (!ok && lane == 0) atomicOr(a.status, 1u);  // the MMA completion wait timed out
