@@ -281,27 +281,45 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
     if (noct > 0) stage(oct0, wbuf);
     cp_async_commit();
   }
-  for (int c = tid; c < NCH; c += blockDim.x) {
-    int ch;
-    if (c < D) ch = h * D + c;
-    else if (c < 2 * D) ch = key_dim + h * D + (c - D);
-    else ch = 2 * key_dim + hv * D + (c - 2 * D);
-    const __nv_bfloat16* w = a.conv_weight + int64_t(ch) * 4;
-    const __nv_bfloat16* s = a.conv_state + (int64_t(b) * conv_dim + ch) * a.conv_hist + a.conv_hist - 3;
-    const float w0 = __bfloat162float(w[0]), w1 = __bfloat162float(w[1]);
-    const float w2 = __bfloat162float(w[2]), w3 = __bfloat162float(w[3]);
-    const float s0 = __bfloat162float(s[0]), s1 = __bfloat162float(s[1]), s2 = __bfloat162float(s[2]);
-    sTab[0 * NCH + c] = w0 * s0 + w1 * s1 + w2 * s2;
-    sTab[1 * NCH + c] = w0 * s1 + w1 * s2;
-    sTab[2 * NCH + c] = w0 * s2;
-    sTab[3 * NCH + c] = w0;  // tap applied to x_{t-3}
-    sTab[4 * NCH + c] = w1;
-    sTab[5 * NCH + c] = w2;
-    sTab[6 * NCH + c] = w3;  // tap applied to x_t
-    sTab[7 * NCH + c] = 0.f;
+  // conv table: every thread's taps and prefix-state values are loaded before any is used
+  constexpr int kTabIt = (NCH + kMixWarps * 32 - 1) / (kMixWarps * 32);
+  float tw[kTabIt][4], ts[kTabIt][3];
+#pragma unroll
+  for (int i = 0; i < kTabIt; ++i) {
+    const int c = tid + i * kMixWarps * 32;
+    if (c < NCH) {
+      int ch;
+      if (c < D) ch = h * D + c;
+      else if (c < 2 * D) ch = key_dim + h * D + (c - D);
+      else ch = 2 * key_dim + hv * D + (c - 2 * D);
+      const __nv_bfloat16* w = a.conv_weight + int64_t(ch) * 4;
+      const __nv_bfloat16* s = a.conv_state + (int64_t(b) * conv_dim + ch) * a.conv_hist + a.conv_hist - 3;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) tw[i][e] = __bfloat162float(w[e]);
+#pragma unroll
+      for (int e = 0; e < 3; ++e) ts[i][e] = __bfloat162float(s[e]);
+    }
   }
-  for (int i = tid; i < D; i += blockDim.x) sNw[i] = a.norm_weight[i];
+  const float nwv = tid < D ? a.norm_weight[tid] : 0.f;
   const float neg_a = -expf(a.a_log[hv]), dtb = a.dt_bias[hv];
+#pragma unroll
+  for (int i = 0; i < kTabIt; ++i) {
+    const int c = tid + i * kMixWarps * 32;
+    if (c < NCH) {
+      const float w0 = tw[i][0], w1 = tw[i][1], w2 = tw[i][2], w3 = tw[i][3];
+      const float s0 = ts[i][0], s1 = ts[i][1], s2 = ts[i][2];
+      sTab[0 * NCH + c] = w0 * s0 + w1 * s1 + w2 * s2;
+      sTab[1 * NCH + c] = w0 * s1 + w1 * s2;
+      sTab[2 * NCH + c] = w0 * s2;
+      sTab[3 * NCH + c] = w0;  // tap applied to x_{t-3}
+      sTab[4 * NCH + c] = w1;
+      sTab[5 * NCH + c] = w2;
+      sTab[6 * NCH + c] = w3;  // tap applied to x_t
+      sTab[7 * NCH + c] = 0.f;
+    }
+  }
+  static_assert(D <= kMixWarps * 32, "one norm weight per thread");
+  if (tid < D) sNw[tid] = nwv;
   cp_async_wait<CONT ? 2 : 1>();  // S0 landed (the octet copies may still be in flight)
   tc::fence_async_smem();   // ... and visible to the tensor cores
   tc::fence_before();
