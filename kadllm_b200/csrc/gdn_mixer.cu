@@ -45,7 +45,10 @@
 namespace kb {
 namespace {
 
-constexpr int kMixWarps = 4;
+// warps per CTA: 8 for the first decode step (each warp fills 16 of its lane quadrant's 32
+// TMEM lanes, so two warps share a quadrant and one M = 128 MMA serves both), 4 otherwise
+template <int TMAX, bool CONT>
+constexpr int mix_warps() { return TMAX == 1 && !CONT ? 8 : 4; }
 
 template <int D>
 struct MixLayout {
@@ -58,12 +61,15 @@ struct MixLayout {
   static constexpr int TABB = 8 * NCH * 4;  // conv table [8][NCH] fp32
   static constexpr int NWB = D * 4;         // norm weight fp32
   static constexpr int OCTB = 8 * ROWB;     // one staged octet: 8 (beam, token) rows
-  static constexpr size_t SMEM = size_t(S0B) + TABB + NWB + size_t(kMixWarps) * 2 * OCTB + 16;  // + mbarrier, TMEM slot
   // continuation from a saved first step: a row also stages the parent token's raw q | k | v
-  // slices and its gate word a (one buffer per warp: two CTAs per SM)
+  // slices and its gate word a
   static constexpr int ROWB_C = ROWB + 6 * D + 16;
   static constexpr int OCTB_C = 8 * ROWB_C;
-  static constexpr size_t SMEM_C = size_t(S0B) + TABB + NWB + size_t(kMixWarps) * OCTB_C + 16;
+  // shared memory of a CTA of `warps` warps, one staging buffer each (+ mbarrier, TMEM slot):
+  // two CTAs per SM in every mode
+  static constexpr size_t smem(bool cont, int warps) {
+    return size_t(S0B) + TABB + NWB + size_t(warps) * (cont ? OCTB_C : OCTB) + 16;
+  }
   static constexpr int REC = 4 * D;         // saved record per (beam, head): the token's delta, fp32
 };
 
@@ -146,8 +152,8 @@ __device__ __forceinline__ float chunk_dot(const uint32_t (&x)[KM][4], const uin
 // of 8 beams, each row the beam's new token.  The parent token's delta comes from its
 // record; its raw q | k | v (the conv window) and gate word a are staged, and its k,
 // 1/|k| and decay are recomputed from them exactly as its own first step did.
-template <int D, int TMAX, bool CONT>
-__global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerArgs a, int octets_per_warp) {
+template <int D, int TMAX, bool CONT, int NW = mix_warps<TMAX, CONT>()>
+__global__ void __launch_bounds__(NW * 32, NW == 8 ? 2 : 1) gdn_mixer_kernel(const MixerArgs a, int octets_per_warp) {
   using L = MixLayout<D>;
   static_assert(!CONT || TMAX == 1, "the saved-state continuation stages one row per beam");
   constexpr int CH = L::CH, NCH = L::NCH, ROWB = CONT ? L::ROWB_C : L::ROWB, OCTB = CONT ? L::OCTB_C : L::OCTB;
@@ -163,7 +169,7 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
   float* sTab = reinterpret_cast<float*>(smem + L::S0B);
   float* sNw = sTab + 8 * NCH;
   unsigned char* sStage = smem + L::S0B + L::TABB + L::NWB;
-  uint64_t* mbar = reinterpret_cast<uint64_t*>(sStage + kMixWarps * (CONT ? 1 : 2) * OCTB);
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(sStage + NW * OCTB);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(mbar + 1);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -176,9 +182,9 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
   const int conv_dim = 2 * key_dim + HV * D;
   const int64_t ld = a.ld_proj;
   const int octets = (a.W + BPO - 1) / BPO;
-  const int oct0 = (blockIdx.y * kMixWarps + warp) * octets_per_warp;
+  const int oct0 = (blockIdx.y * NW + warp) * octets_per_warp;
   const int noct = max(0, min(octets_per_warp, octets - oct0));
-  unsigned char* wbuf = sStage + warp * (CONT ? 1 : 2) * OCTB;
+  unsigned char* wbuf = sStage + warp * OCTB;
   // projection columns of the staged slices: q, k, v, z head slices; b and a gate words (aligned down)
   const int col_q = h * D, col_k = key_dim + h * D, col_v = 2 * key_dim + hv * D, col_z = conv_dim + hv * D;
   const int col_b = conv_dim + HV * D + hv, col_a = conv_dim + HV * D + HV + hv;
@@ -196,64 +202,49 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
     }
     return a.proj + ((int64_t(b) * a.W + beam) * TMAX + tr) * ld;
   };
-  // Stage octet `oct` into `buf` (the caller commits the cp.async group).
-  // (lane r & 7 resolves row r's projection row once; the copies take it by shuffle: every
-  // lane's idx of one iteration lies in the same row)
-  auto stage = [&](int oct, unsigned char* buf) {
+  // A warp stages an octet in two parts into its single buffer (the caller commits each as
+  // a cp.async group): part qk (the rows' q | k slices and gate words; CONT: also the
+  // parents' q | k slices and gate word a), read by the conv and the dot products, and part
+  // vz (the rows' v | z slices; CONT: the parents' v slices), read by the recurrence and the
+  // norm.  The next octet's part qk loads once this octet's conv is done and its part vz once
+  // this octet's output has left, each behind the other half of the round; the output goes
+  // out through the v slices (free after the recurrence).  Lane r & 7 resolves row r's
+  // projection row once; the copies take it by shuffle (every lane's idx of one iteration
+  // lies in the same row).
+  auto stage_part = [&](int oct, unsigned char* buf, bool qk) {
     const int rl = lane & 7, beam_l = oct * BPO + rl % BPO;
     const bool ok_l = beam_l < a.W;
     const long long prow_l = reinterpret_cast<long long>(prow_of(rl / BPO, ok_l ? beam_l : 0));
 #pragma unroll 4
-    for (int idx = lane; idx < 8 * 4 * CH; idx += 32) {
-      const int r = idx / (4 * CH), piece = (idx / CH) & 3, c = idx % CH;
-      const bool ok = oct * BPO + r % BPO < a.W;
-      const __nv_bfloat16* prow = reinterpret_cast<const __nv_bfloat16*>(__shfl_sync(0xffffffffu, prow_l, r));
-      const int col = piece < 2 ? (piece == 0 ? col_q : col_k) : (piece == 2 ? col_v : col_z);
-      cp16z(buf + r * ROWB + piece * 2 * D + c * 16, prow + col + c * 8, ok);
-    }
-    const __nv_bfloat16* prow = reinterpret_cast<const __nv_bfloat16*>(__shfl_sync(0xffffffffu, prow_l, lane >> 1));
-    if (lane < 16) {
-      const int r = lane >> 1, which = lane & 1;
-      const bool ok = oct * BPO + r % BPO < a.W;
-      cp4z(buf + r * ROWB + 8 * D + which * 4, prow + ((which ? col_a : col_b) & ~1), ok);
-    }
-  };
-  // CONT stages an octet in two parts into its single buffer: part qk (the new rows' q | k
-  // slices and gate words, the parents' q | k slices and gate word a), read by the conv and
-  // the dot products, and part vz (the new rows' v | z slices, the parents' v slices), read
-  // by the recurrence and the norm.  The next octet's part qk loads once this octet's conv
-  // is done and its part vz once this octet's output has left, each behind the other half
-  // of the round.  The output goes out through the v slice (free after the recurrence).
-  auto stage_cont = [&](int oct, unsigned char* buf, bool qk) {
-    const int rl = lane & 7, beam_l = oct * BPO + rl;
-    const bool ok_l = beam_l < a.W;
-    const long long prow_l = reinterpret_cast<long long>(a.proj + (int64_t(b) * a.W + (ok_l ? beam_l : 0)) * ld);
-    const long long pp_l =
-        reinterpret_cast<long long>(a.proj_prev + (int64_t(b) * a.Wp + parent_of(ok_l ? beam_l : 0)) * ld);
-#pragma unroll 4
-    for (int idx = lane; idx < 8 * 2 * CH; idx += 32) {  // two slices of each new row
+    for (int idx = lane; idx < 8 * 2 * CH; idx += 32) {  // two slices of each row
       const int r = idx / (2 * CH), piece = (qk ? 0 : 2) + ((idx / CH) & 1), c = idx % CH;
       const __nv_bfloat16* prow = reinterpret_cast<const __nv_bfloat16*>(__shfl_sync(0xffffffffu, prow_l, r));
       const int col = piece < 2 ? (piece == 0 ? col_q : col_k) : (piece == 2 ? col_v : col_z);
-      cp16z(buf + r * ROWB + piece * 2 * D + c * 16, prow + col + c * 8, oct * BPO + r < a.W);
+      cp16z(buf + r * ROWB + piece * 2 * D + c * 16, prow + col + c * 8, oct * BPO + r % BPO < a.W);
     }
-    const int per = qk ? 2 * CH : CH;  // the parents' q | k slices, or their v slices
-#pragma unroll 4
-    for (int idx = lane; idx < 8 * per; idx += 32) {
-      const int r = idx / per, piece = qk ? (idx / CH) & 1 : 2, c = idx % CH;
-      const __nv_bfloat16* pp = reinterpret_cast<const __nv_bfloat16*>(__shfl_sync(0xffffffffu, pp_l, r));
-      cp16z(buf + r * ROWB + 8 * D + 16 + piece * 2 * D + c * 16,
-            pp + (piece == 0 ? col_q : (piece == 1 ? col_k : col_v)) + c * 8, oct * BPO + r < a.W);
-    }
-    if (qk) {  // lanes 0-15: the new rows' gate words b, a; lanes 16-23: the parents' a
+    if (qk) {  // lanes 0-15: the rows' gate words b, a
       const __nv_bfloat16* prow =
           reinterpret_cast<const __nv_bfloat16*>(__shfl_sync(0xffffffffu, prow_l, (lane >> 1) & 7));
-      const __nv_bfloat16* pp = reinterpret_cast<const __nv_bfloat16*>(__shfl_sync(0xffffffffu, pp_l, lane & 7));
       if (lane < 16) {
         const int r = lane >> 1, which = lane & 1;
-        cp4z(buf + r * ROWB + 8 * D + which * 4, prow + ((which ? col_a : col_b) & ~1), oct * BPO + r < a.W);
-      } else if (lane < 24) {
-        cp4z(buf + (lane - 16) * ROWB + 14 * D + 16, pp + (col_a & ~1), oct * BPO + (lane - 16) < a.W);
+        cp4z(buf + r * ROWB + 8 * D + which * 4, prow + ((which ? col_a : col_b) & ~1), oct * BPO + r % BPO < a.W);
+      }
+    }
+    if constexpr (CONT) {
+      const long long pp_l =
+          reinterpret_cast<long long>(a.proj_prev + (int64_t(b) * a.Wp + parent_of(ok_l ? beam_l : 0)) * ld);
+      const int per = qk ? 2 * CH : CH;  // the parents' q | k slices, or their v slices
+#pragma unroll 4
+      for (int idx = lane; idx < 8 * per; idx += 32) {
+        const int r = idx / per, piece = qk ? (idx / CH) & 1 : 2, c = idx % CH;
+        const __nv_bfloat16* pp = reinterpret_cast<const __nv_bfloat16*>(__shfl_sync(0xffffffffu, pp_l, r));
+        cp16z(buf + r * ROWB + 8 * D + 16 + piece * 2 * D + c * 16,
+              pp + (piece == 0 ? col_q : (piece == 1 ? col_k : col_v)) + c * 8, oct * BPO + r < a.W);
+      }
+      if (qk) {  // lanes 16-23: the parents' gate word a
+        const __nv_bfloat16* pp = reinterpret_cast<const __nv_bfloat16*>(__shfl_sync(0xffffffffu, pp_l, lane & 7));
+        if (lane >= 16 && lane < 24)
+          cp4z(buf + (lane - 16) * ROWB + 14 * D + 16, pp + (col_a & ~1), oct * BPO + (lane - 16) < a.W);
       }
     }
   };
@@ -272,21 +263,16 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
     }
     cp_async_commit();
   }
-  if constexpr (CONT) {  // both parts of this warp's first octet
-    if (noct > 0) stage_cont(oct0, wbuf, true);
-    cp_async_commit();
-    if (noct > 0) stage_cont(oct0, wbuf, false);
-    cp_async_commit();
-  } else {
-    if (noct > 0) stage(oct0, wbuf);
-    cp_async_commit();
-  }
+  if (noct > 0) stage_part(oct0, wbuf, true);  // both parts of this warp's first octet
+  cp_async_commit();
+  if (noct > 0) stage_part(oct0, wbuf, false);
+  cp_async_commit();
   // conv table: every thread's taps and prefix-state values are loaded before any is used
-  constexpr int kTabIt = (NCH + kMixWarps * 32 - 1) / (kMixWarps * 32);
+  constexpr int kTabIt = (NCH + NW * 32 - 1) / (NW * 32);
   float tw[kTabIt][4], ts[kTabIt][3];
 #pragma unroll
   for (int i = 0; i < kTabIt; ++i) {
-    const int c = tid + i * kMixWarps * 32;
+    const int c = tid + i * NW * 32;
     if (c < NCH) {
       int ch;
       if (c < D) ch = h * D + c;
@@ -304,7 +290,7 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
   const float neg_a = -expf(a.a_log[hv]), dtb = a.dt_bias[hv];
 #pragma unroll
   for (int i = 0; i < kTabIt; ++i) {
-    const int c = tid + i * kMixWarps * 32;
+    const int c = tid + i * NW * 32;
     if (c < NCH) {
       const float w0 = tw[i][0], w1 = tw[i][1], w2 = tw[i][2], w3 = tw[i][3];
       const float s0 = ts[i][0], s1 = ts[i][1], s2 = ts[i][2];
@@ -318,23 +304,25 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
       sTab[7 * NCH + c] = 0.f;
     }
   }
-  static_assert(D <= kMixWarps * 32, "one norm weight per thread");
+  static_assert(D <= NW * 32, "one norm weight per thread");
   if (tid < D) sNw[tid] = nwv;
-  cp_async_wait<CONT ? 2 : 1>();  // S0 landed (the octet copies may still be in flight)
+  cp_async_wait<2>();       // S0 landed (the octet copies may still be in flight)
   tc::fence_async_smem();   // ... and visible to the tensor cores
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
   const uint32_t tmem = *tslot;
-  const uint32_t t_acc = tc::taddr(tmem, 32 * warp, 0);       // this warp's 16 lanes: q rows g, k rows 8 + g
-  const uint32_t t_hi = tc::taddr(tmem, 32 * warp, D), t_lo = tc::taddr(tmem, 32 * warp, D + D / 2);
+  // this warp's 16 lanes (the first or second half of its lane quadrant): q rows g, k rows 8 + g
+  const int lane0 = 32 * (warp & 3) + 16 * (warp >> 2);
+  const uint32_t t_acc = tc::taddr(tmem, lane0, 0);
+  const uint32_t t_hi = tc::taddr(tmem, lane0, D), t_lo = tc::taddr(tmem, lane0, D + D / 2);
   bool ok = true;
 
   // Rounds: every warp takes part in each round's barrier; a warp past its last octet
   // writes no A rows and reads nothing back (its TMEM lanes hold stale values).
   for (int it = 0; it < octets_per_warp; ++it) {
     const bool active = it < noct;
-    unsigned char* buf = CONT ? wbuf : wbuf + (it & 1) * OCTB;
+    unsigned char* buf = wbuf;
     // CONT: the parent's delta straight from its record into registers
     float2 d0s[CONT ? NT : 1];
     const int my_beam = (oct0 + it) * BPO + g % BPO;
@@ -343,12 +331,8 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
           a.saved + ((int64_t(b) * a.Wp + parent_of(active && my_beam < a.W ? my_beam : 0)) * HV + hv) * L::REC;
 #pragma unroll
       for (int jj = 0; jj < NT; ++jj) d0s[jj] = *reinterpret_cast<const float2*>(rec + (jj * 8 + 2 * tq) * 4);
-      cp_async_wait<1>();  // this octet's part qk (its part vz may still be in flight)
-    } else {
-      if (it + 1 < noct) stage(oct0 + it + 1, wbuf + ((it + 1) & 1) * OCTB);
-      cp_async_commit();
-      cp_async_wait<1>();
     }
+    cp_async_wait<1>();  // this octet's part qk (its part vz may still be in flight)
     __syncwarp();
 
     unsigned char* rowg = buf + g * ROWB;  // this thread's row
@@ -424,11 +408,9 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
       ckq = at * dq;
       ckk = at * dk;
     }
-    if constexpr (CONT) {  // part qk read: the next octet's part qk
-      __syncwarp();
-      if (it + 1 < noct) stage_cont(oct0 + it + 1, buf, true);
-      cp_async_commit();
-    }
+    __syncwarp();  // part qk read: the next octet's part qk
+    if (it + 1 < noct) stage_part(oct0 + it + 1, buf, true);
+    cp_async_commit();
     // first decode step with a record buffer: this row's delta for the next step
     unsigned char* srec = nullptr;
     if constexpr (TMAX == 1 && !CONT) {
@@ -485,10 +467,8 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
     if (!active) continue;
     ok = tc::mbar_wait(mbar, uint32_t(it) & 1u, kWait) && ok;
     tc::fence_after();
-    if constexpr (CONT) {
-      cp_async_wait<1>();  // this octet's part vz (the next octet's part qk may still be in flight)
-      __syncwarp();
-    }
+    cp_async_wait<1>();  // this octet's part vz (the next octet's part qk may still be in flight)
+    __syncwarp();
 
     // ---- recurrence and gated RMSNorm over the accumulator, in two column halves ---------
     uint32_t ob[NT];
@@ -536,9 +516,10 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
         ss = fmaf(of.x, of.x, fmaf(of.y, of.y, ss));
       }
     }
-    // gated RMSNorm, written over this row's staged q slice (read only by the prep above), or
-    // in CONT over its v slice (the q slice may already hold the next octet's)
-    constexpr int kOut = CONT ? 4 * D : 0;
+    // gated RMSNorm, written over this row's staged v slice once every row of the octet has
+    // read its v slices (a step-1 row reads its step-0 row's too)
+    constexpr int kOut = 4 * D;
+    __syncwarp();
     const float inv = 1.0f / sqrtf(quad_sum(ss) / float(D) + a.norm_eps);
 #pragma unroll
     for (int jj = 0; jj < NT; ++jj) {
@@ -564,10 +545,8 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
       }
     }
     __syncwarp();
-    if constexpr (CONT) {  // part vz read: the next octet's part vz
-      if (it + 1 < noct) stage_cont(oct0 + it + 1, buf, false);
-      cp_async_commit();
-    }
+    if (it + 1 < noct) stage_part(oct0 + it + 1, buf, false);  // part vz read: the next octet's part vz
+    cp_async_commit();
   }
   cp_async_wait<0>();
   if (!ok && lane == 0) atomicOr(a.status, 1u);  // the MMA completion wait timed out
@@ -582,8 +561,10 @@ __global__ void __launch_bounds__(kMixWarps * 32) gdn_mixer_kernel(const MixerAr
 template <int D, int TMAX, bool CONT = false>
 int launch_mixer(const MixerArgs& a, cudaStream_t stream) {
   using L = MixLayout<D>;
-  auto kern = gdn_mixer_kernel<D, TMAX, CONT>;
-  constexpr size_t smem = CONT ? L::SMEM_C : L::SMEM;
+  constexpr int NW = mix_warps<TMAX, CONT>();
+  auto kern = gdn_mixer_kernel<D, TMAX, CONT, NW>;
+  constexpr size_t smem = L::smem(CONT, NW);
+  static_assert(2 * (smem + 1024) <= 233472, "two CTAs per SM");
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess) {
     set_error("gdn mixer: cannot reserve %zu bytes of shared memory", smem);
     return KADLLM_ECUDA;
@@ -597,11 +578,11 @@ int launch_mixer(const MixerArgs& a, cudaStream_t stream) {
   // warp taking a run of consecutive octets
   const int heads = a.B * a.HV;
   int ny = (4 * sms + heads - 1) / heads;
-  ny = max(1, min(ny, (octets + kMixWarps - 1) / kMixWarps));
-  const int opw = (octets + kMixWarps * ny - 1) / (kMixWarps * ny);
-  ny = (octets + kMixWarps * opw - 1) / (kMixWarps * opw);
+  ny = max(1, min(ny, (octets + NW - 1) / NW));
+  const int opw = (octets + NW * ny - 1) / (NW * ny);
+  ny = (octets + NW * opw - 1) / (NW * opw);
   const dim3 grid{unsigned(heads), unsigned(ny)};
-  kern<<<grid, kMixWarps * 32, smem, stream>>>(a, opw);
+  kern<<<grid, NW * 32, smem, stream>>>(a, opw);
   KB_CHECK_LAUNCH("gdn mixer launch");
   return KADLLM_OK;
 }
