@@ -57,3 +57,17 @@ def test_argument_errors_are_reported_without_a_gpu(library):
     rc = lib.kadllm_gated_delta_replay(None, None, None, 7, None, 0, None, 0, None, 2, None,
                                        1, 1, 1, 1, 1, 32, 32, 0.0, None, None)
     assert rc == 2
+
+
+def test_mixer_record_bytes_without_a_gpu(library):
+    from kadllm_b200 import _lib
+
+    lib = _lib.lib()
+    # one fp32 delta per (beam row, value head, value column)
+    assert lib.kadllm_gdn_mixer_record_bytes(32, 256, 16, 128) == 32 * 256 * 16 * 128 * 4
+    assert lib.kadllm_gdn_mixer_record_bytes(3, 8, 4, 64) == 3 * 8 * 4 * 64 * 4
+    assert lib.kadllm_gdn_mixer_record_bytes(0, 8, 4, 64) == 0
+    # null operands are refused on the host, before any launch (the record pointer is never read there)
+    rc = lib.kadllm_gdn_mixer_replay(None, 0, None, 4, None, None, None, None, None, 1e-6, None, 1, 1, 2, 1, 1, 128,
+                                     128, 1, None, None)
+    assert rc != 0
