@@ -174,7 +174,7 @@ def test_gdn_mixer_matches_oracle_composition(T, K, H, HV):
 @pytest.mark.parametrize("T", [1, 2])
 def test_gdn_mixer_many_octets_per_warp(T):
     """160 (request, head) pairs x 250 beams: each warp of the staged kernel runs
-    several beam octets through its double-buffered staging, the last one ragged."""
+    several beam octets through its two-part staging buffer, the last one ragged."""
     _mixer_case(T, 128, 4, 16, 10, 250)
 
 
