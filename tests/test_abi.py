@@ -71,3 +71,16 @@ def test_mixer_record_bytes_without_a_gpu(library):
     rc = lib.kadllm_gdn_mixer_replay(None, 0, None, 4, None, None, None, None, None, 1e-6, None, 1, 1, 2, 1, 1, 128,
                                      128, 1, None, None)
     assert rc != 0
+
+
+def test_mixer_records_need_one_suffix_step(library):
+    """First-step records are refused on the host (EUNSUPPORTED) for a two-token replay.
+    The pointers are aligned placeholders: the host checks reject the call before any is used."""
+    from kadllm_b200 import _lib
+
+    lib = _lib.lib()
+    fake = 1 << 20  # 16-byte aligned, never dereferenced on the host
+    rc = lib.kadllm_gdn_mixer_replay(fake, 520, fake, 4, fake, fake, fake, fake, fake, 1e-6, fake, 1, 8, 2, 1, 1, 128,
+                                     128, fake, fake, None)
+    assert rc == 3
+    assert b"records" in lib.kadllm_last_error()
