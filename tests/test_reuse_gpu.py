@@ -122,9 +122,12 @@ def test_engine_decode_continuation_matches_full_replay(mid_engine):
                      what="continued vs full two-token decode")
 
 
-def test_search_with_step_reuse_matches_full_replay(mid_engine):
+@pytest.mark.parametrize("widths", [[16, 16, 16], [8, 8, 8, 8], [16, 16], [16]])
+def test_search_with_step_reuse_matches_full_replay(mid_engine, widths):
     """The drop-in search (step reuse through decode_select) against the same search
-    through the protocol's decode only (full replay of both suffix tokens)."""
+    through the protocol's decode only (full replay of every suffix token), at depths
+    1-4: no decode step, one step, the reused second step, and a third (three-token)
+    replay after it."""
     from kadllm_b200 import grbeam_search
     from kadllm_b200.adapters import NativeGRBeamAdapter
     from kadllm_b200.grbeam import PrefillResult
@@ -141,7 +144,8 @@ def test_search_with_step_reuse_matches_full_replay(mid_engine):
             return engine.decode(history, state)
 
     ids = torch.from_numpy(random_prompts(2, 70, cfg.vocab_size, seed=8)).cuda()
-    a = grbeam_search(NativeGRBeamAdapter(engine), ids, [16, 16, 16])
-    b = grbeam_search(ProtocolOnly(), ids, [16, 16, 16])
+    a = grbeam_search(NativeGRBeamAdapter(engine), ids, widths)
+    b = grbeam_search(ProtocolOnly(), ids, widths)
+    assert a.tokens.shape == (2, widths[-1], len(widths))
     assert beam_mismatches(a.tokens.cpu().numpy(), a.scores.cpu().numpy(), b.tokens.cpu().numpy(),
                            b.scores.cpu().numpy(), 1e-3) == []
