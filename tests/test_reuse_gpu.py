@@ -122,12 +122,13 @@ def test_engine_decode_continuation_matches_full_replay(mid_engine):
                      what="continued vs full two-token decode")
 
 
-@pytest.mark.parametrize("widths", [[16, 16, 16], [8, 8, 8, 8], [16, 16], [16]])
+@pytest.mark.parametrize("widths", [[16, 16, 16], [8, 8, 8, 8], [16, 16], [16], [16, 40, 8], [4, 64, 33]])
 def test_search_with_step_reuse_matches_full_replay(mid_engine, widths):
     """The drop-in search (step reuse through decode_select) against the same search
     through the protocol's decode only (full replay of every suffix token), at depths
     1-4: no decode step, one step, the reused second step, and a third (three-token)
-    replay after it."""
+    replay after it; and with widths that change between levels (the second step's
+    beams read their parents' rows and records across widths)."""
     from kadllm_b200 import grbeam_search
     from kadllm_b200.adapters import NativeGRBeamAdapter
     from kadllm_b200.grbeam import PrefillResult
