@@ -83,13 +83,13 @@ def measured_traffic(name: str, args: tuple) -> float | None:
         # 101.8 + 97.3 MB, tcgen05 scan with the gated norm 185.5 + 16.4 MB; x 4
         return 1604.0e6
     if name == "kadllm_gdn_mixer_replay" and tuple(args[11:13]) == (32, 256) and tuple(args[14:18]) == (16, 16, 128, 128):
-        if args[18] is not None:  # the first step writing its records: not captured
-            return None
+        if args[18] is not None:  # the first step writing its records: 168.0 + 66.1 MB
+            return 234.1e6 if args[13] == 1 else None
         return {1: 181.0e6, 2: 353.6e6}.get(args[13])  # T = 1: 164.6 + 16.4 MB; T = 2: 306.0 + 47.6 MB
     if (name == "kadllm_gdn_mixer_continue" and args[2] == 256 and tuple(args[14:16]) == (32, 256)
             and tuple(args[16:20]) == (16, 16, 128, 128)):
-        if args[20] is not None:  # from the first step's records: not captured
-            return None
+        if args[20] is not None:  # from the first step's records: 300.7 + 26.6 MB
+            return 327.3e6
         return 295.8e6  # 273.6 + 22.2 MB (random parents: children of one parent share its rows in L2)
     if name == "kadllm_attention_tiled" and (args[24], *args[28:32]) == (32, 8, 2, 1024, 256):
         if args[33]:  # causal prefill: 335.6 + 109.8 MB
