@@ -363,7 +363,9 @@ KADLLM_API int kadllm_causal_attention(const void* q, int64_t sq_row, int64_t sq
  * LM head (Qwen3_5GatedDeltaNet / Qwen3_5Attention / Qwen3_5MLP projections and
  * lm_head, as src/kadllm/adapters/qwen3_5.py:144-202,226-235 calls them).
  *   A [M, K] bf16, row stride lda;  B [N, K] bf16, row stride ldb;  strides
- *   multiples of 8 elements, pointers 16-byte aligned.
+ *   multiples of 8 elements, pointers 16-byte aligned.  The output row width
+ *   (N, or n_out for epilogue 1) is a multiple of 8: C is written in 16-byte
+ *   granules, and nothing past the row end inside a padded row is touched.
  * epilogue 0: C [M, N] = bf16(A . B^T)                                   (ldc)
  * epilogue 1: B's rows are 128-row blocks [gate block j | up block j] (N a
  *   multiple of 256); C [M, n_out] = bf16(bf16(silu(gate)) * up), gate and up

@@ -447,6 +447,10 @@ extern "C" int kadllm_gemm(const void* a, int64_t lda, const void* b, int64_t ld
     n_out = N;
   }
   KB_REQUIRE(ldc >= n_out, KADLLM_EINVAL, "gemm: ldc shorter than the output row");
+  // the tensor-map store writes whole 16-byte granules: a row ending inside one would
+  // overwrite the caller's padding past n_out
+  KB_REQUIRE(n_out % 8 == 0, KADLLM_EINVAL, "gemm: the output row width %lld is not a multiple of 8",
+             static_cast<long long>(n_out));
   if (epilogue == kAddResid) {
     KB_REQUIRE(resid && ld_resid >= N && ld_resid % 8 == 0 && (reinterpret_cast<uintptr_t>(resid) & 15) == 0,
                KADLLM_EINVAL, "gemm (residual): residual pointer / stride invalid");

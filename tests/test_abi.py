@@ -84,3 +84,15 @@ def test_mixer_records_need_one_suffix_step(library):
                                      128, fake, fake, None)
     assert rc == 3
     assert b"records" in lib.kadllm_last_error()
+
+
+def test_gemm_output_row_width_multiple_of_8(library):
+    """The GEMM's tensor-map store writes 16-byte granules, so an output row width that is
+    not a multiple of 8 (padding past it in a wider row) is refused on the host (EINVAL)."""
+    from kadllm_b200 import _lib
+
+    lib = _lib.lib()
+    fake = 1 << 20  # 16-byte aligned, never dereferenced on the host
+    rc = lib.kadllm_gemm(fake, 64, fake, 64, fake, 64, None, 0, 64, 62, 64, 62, 0, fake, None)
+    assert rc == 1
+    assert b"multiple of 8" in lib.kadllm_last_error()

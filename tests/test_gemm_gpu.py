@@ -92,6 +92,24 @@ def test_gemm_residual_epilogue_in_place(M, N, K):
     assert bool((err <= bound).all()), f"max error {float(err.max())}, worst excess {float((err - bound).max())}"
 
 
+@pytest.mark.parametrize("M,N,K,ld", [(20000, 1000, 128, 1008), (77, 136, 64, 200)])
+def test_gemm_residual_epilogue_ragged_row(M, N, K, ld):
+    """Rows that end inside a 64-column residual / output box (padded row stride) and
+    several tiles per CTA pair: the padding past N is neither read into the sum nor
+    written."""
+    a, b = _operands(M, N, K, seed=N + K)
+    store = torch.randn(M, ld, device="cuda").bfloat16()
+    x = store[:, :N]
+    x0, pad0 = x.clone(), store[:, N:].clone()
+    _gemm(a, b, resid=x)
+    prod = a.float() @ b.float().T
+    ref = x0.float() + prod.bfloat16().float()
+    bound = RTOL * (prod.abs() + ref.abs()) + _atol(prod)
+    err = (x.float() - ref).abs()
+    assert bool((err <= bound).all()), f"max error {float(err.max())}, worst excess {float((err - bound).max())}"
+    assert torch.equal(store[:, N:], pad0)
+
+
 def test_gemm_rejects_bad_arguments():
     a, b = _operands(64, 64, 64, seed=0)
     out = torch.empty(64, 64, dtype=torch.bfloat16, device="cuda")
