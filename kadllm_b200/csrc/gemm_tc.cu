@@ -17,7 +17,9 @@
 //    tile crosses L2 -> SM once per pair.
 //  * One CTA per SM (192 threads): warp 0 issues the copies, warp 1 of rank 0 issues
 //    the MMAs (M = 256, N = 256, K = 16) and commits each stage back to both CTAs'
-//    "empty" barriers, warps 2-5 drain the accumulator.  Six 32 KB stages.
+//    "empty" barriers, warps 2-5 drain the accumulator.  Six 32 KB stages.  The
+//    residual update runs 320 threads: warps 2-9 drain, two per TMEM lane quadrant,
+//    with five stages in the shared memory left.
 //  * The accumulator is double-buffered in tensor memory (2 x 256 columns), so the
 //    epilogue of tile i overlaps the main loop of tile i + 1.  Tiles are spread over
 //    the pairs round-robin, grouped 8 M-tiles at a time for L2 reuse of B.
@@ -46,17 +48,27 @@ namespace {
 constexpr int kBM = 128;                                // rows of A per CTA (256 per pair)
 constexpr int kBN = 256;                                // columns of the pair's tile
 constexpr int kBK = 64;                                 // one 128-byte swizzle row of BF16
-constexpr int kStages = 6;
 constexpr uint32_t kABytes = kBM * kBK * 2;             // 16 KB
 constexpr uint32_t kBBytes = (kBN / 2) * kBK * 2;       // 16 KB (this CTA's half of B)
 constexpr uint32_t kStageBytes = kABytes + kBBytes;     // 32 KB
-constexpr int kThreads = 192;
 constexpr int kGroupM = 8;
 constexpr long long kWait = 1ll << 31;
 constexpr uint32_t kBoxBytes = 32 * 128;                // epilogue staging box: 32 rows x 64 BF16
-constexpr size_t kSmemBytes = 1024 + size_t(kStages) * kStageBytes + 4 * 2 * kBoxBytes + 256;
 
 enum Epilogue { kStore = 0, kSiluMul = 1, kAddResid = 2, kLogits = 3 };
+
+// Per epilogue: drain warps (the residual update: two per TMEM lane quadrant, each
+// taking half of the tile's columns, so that the last tile's drain, with its residual
+// copies, overlaps nothing for half as long), operand stages in the shared memory
+// they leave, threads per CTA.
+template <int EPI>
+struct Cfg {
+  static constexpr int kEpiWarps = EPI == kAddResid ? 8 : 4;
+  static constexpr int kStages = EPI == kAddResid ? 5 : 6;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  static constexpr size_t kSmemBytes =
+      1024 + size_t(kStages) * kStageBytes + size_t(kEpiWarps) * 2 * kBoxBytes + 32 * 8 + 128;
+};
 
 struct GemmArgs {
   __nv_bfloat16* c;
@@ -86,19 +98,20 @@ __device__ __forceinline__ void spin_cycles(long long n) {
 }
 
 template <int EPI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg<EPI>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_r,
                    const GemmArgs g) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(kStages) * kStageBytes + 4 * 2 * kBoxBytes);
+  constexpr int kStages = Cfg<EPI>::kStages, kEpiWarps = Cfg<EPI>::kEpiWarps;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(kStages) * kStageBytes + kEpiWarps * 2 * kBoxBytes);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;   // [2] accumulator ready (both CTAs)
   uint64_t* tempty = tfull + 2;        // [2] accumulator drained (rank 0's: 8 warps arrive)
   uint64_t* drain = tempty + 2;        // error path: the MMA issuer's last commit
-  uint64_t* rbars = drain + 1;         // [4] epilogue warps' residual-box copies
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbars + 4);
+  uint64_t* rbars = drain + 1;         // [kEpiWarps] epilogue warps' residual-box copies
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbars + kEpiWarps);
 
   const uint32_t rank = tc2::cta_rank();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -113,10 +126,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       tc::mbar_init(tfull + a, 1);
-      tc::mbar_init(tempty + a, 8);
+      tc::mbar_init(tempty + a, 2 * kEpiWarps);
     }
     tc::mbar_init(drain, 1);
-    for (int w = 0; w < 4; ++w) tc::mbar_init(rbars + w, 1);
+    for (int w = 0; w < kEpiWarps; ++w) tc::mbar_init(rbars + w, 1);
     tc2::fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -215,13 +228,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tc::mbar_wait(drain, 0, kWait);
       }
     }
-  } else {  // warps 2-5: epilogue; warp w reads TMEM lanes 32 (w % 4) .. + 31
-    const int q = warp & 3;
+  } else {  // warps 2..: epilogue; warp w reads TMEM lanes 32 (w % 4) .. + 31
+    const int q = warp & 3, part = (warp - 2) / 4;
     // two 32-row x 64-column staging boxes per warp (128-byte swizzle: chunk j of row r at
     // r * 128 + ((j ^ (r % 8)) * 16)), written from registers and stored by the tensor map
     uint8_t* stage = smem + size_t(kStages) * kStageBytes + size_t(warp - 2) * 2 * kBoxBytes;
     uint64_t* rbar = rbars + (warp - 2);
     constexpr int kOutCols = EPI == kSiluMul ? kBN / 2 : kBN;  // output columns per tile
+    constexpr int kPartCols = kOutCols / (kEpiWarps / 4);      // this warp's share of them
     int acc = 0, nbuf = 0;
     uint32_t acc_ph = 0, rph = 0;
     constexpr float kLog2e = 1.4426950408889634f;
@@ -237,7 +251,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const uint32_t tbase = tc::taddr(tmem, q * 32, acc * kBN);
       float lm = -INFINITY, ls = 0.f;  // kLogits: this row's running chunk maximum and sum
 #pragma unroll 1
-      for (int c = 0; c < kOutCols && ok; c += 64) {
+      for (int c = part * kPartCols; c < (part + 1) * kPartCols && ok; c += 64) {
         const int col = tn * kOutCols + c;
         if (row0 >= g.M || col >= g.n_out) continue;  // warp-uniform: nothing of this box is stored
         uint8_t* buf = stage + (nbuf & 1) * kBoxBytes;
@@ -394,12 +408,12 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, 
   KB_REQUIRE(cudaGetDevice(&dev) == cudaSuccess && dev < 64, KADLLM_ECUDA, "gemm: no current device");
   if (max_pairs[dev] == 0) {
     KB_REQUIRE(cudaFuncSetAttribute(gemm_tc_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    int(kSmemBytes)) == cudaSuccess,
-               KADLLM_ECUDA, "gemm: cannot reserve %zu bytes of shared memory", kSmemBytes);
+                                    int(Cfg<EPI>::kSmemBytes)) == cudaSuccess,
+               KADLLM_ECUDA, "gemm: cannot reserve %zu bytes of shared memory", Cfg<EPI>::kSmemBytes);
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(2);
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.blockDim = dim3(Cfg<EPI>::kThreads);
+    cfg.dynamicSmemBytes = Cfg<EPI>::kSmemBytes;
     cudaLaunchAttribute attr{};
     attr.id = cudaLaunchAttributeClusterDimension;
     attr.val.clusterDim.x = 2;
@@ -418,7 +432,7 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, 
   }
   const int total = g.tiles_m * g.tiles_n;
   const int pairs = total < max_pairs[dev] ? total : max_pairs[dev];
-  gemm_tc_kernel<EPI><<<dim3(2 * pairs), dim3(kThreads), kSmemBytes, s>>>(ma, mb, mc, mr, g);
+  gemm_tc_kernel<EPI><<<dim3(2 * pairs), dim3(Cfg<EPI>::kThreads), Cfg<EPI>::kSmemBytes, s>>>(ma, mb, mc, mr, g);
   KB_CHECK_LAUNCH("gemm launch");
   return KADLLM_OK;
 }
