@@ -305,6 +305,22 @@ def case_qk_rope(gen, reps):
     return ms, "hbm", rows * (Hq + 2 * HK) * D * 2 * 2
 
 
+def case_rmsnorm(gen, reps, rows=32 * 1024):
+    """kadllm_add_rmsnorm as the step calls it after each fused residual update: read the
+    hidden rows (1024 BF16), write their RMSNorm (1 + w); graph-timed (short launches)."""
+    dev, bf, H = torch.device("cuda"), torch.bfloat16, 1024
+    x = torch.randn(rows, H, device=dev, generator=gen).to(bf)
+    w = 0.1 * torch.randn(H, device=dev, generator=gen)
+    normed = torch.empty_like(x)
+
+    def run():
+        _lib.call("kadllm_add_rmsnorm", x.data_ptr(), None, 0, w.data_ptr(), 1e-6, normed.data_ptr(), rows, 1, 0, H,
+                  _lib.stream(dev))
+
+    ms = _time_graph(run, reps)
+    return ms, "hbm", rows * H * 2 * 2
+
+
 def case_select(gen, reps):
     from .grbeam import BeamSelector
 
@@ -347,6 +363,7 @@ CASES = {"prefill": case_prefill, "prefill8": lambda g, r: case_prefill(g, r, B=
          "mixer2": lambda g, r: case_mixer(g, r, T=2), "select": case_select, "replay": case_replay,
          "mixer_cont": case_mixer_cont, "mixer_cont_saved": lambda g, r: case_mixer_cont(g, r, saved=True),
          "qk_rope": case_qk_rope,
+         "rmsnorm": case_rmsnorm, "rmsnorm_decode": lambda g, r: case_rmsnorm(g, r, rows=8192),
          "attn_step": lambda g, r: case_attn_tiled(g, r, B=32, W=256, T=2, L=1024),
          "attn_causal": lambda g, r: case_attn_tiled(g, r, B=32, W=1, T=1, L=1024, causal=True),
          # the step's projections: prefill (32 x 1024 rows) and decode (32 x 256 beams, T = 1)
