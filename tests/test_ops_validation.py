@@ -7,8 +7,11 @@ device, so every rejected call is checked here with CPU (or meta) tensors: empty
 dimensions, widths that do not divide the rows, mismatched shapes, dtypes and
 devices, unknown launch tuples and activations.  Arguments that pass the checks
 reach the CUDA requirement and raise ``RuntimeError`` (the library has no CPU
-path).  No GPU is needed.
+path).  The adapter's constructor switches are checked the same way on a tiny
+CPU model.  No GPU is needed.
 """
+
+import copy
 
 import pytest
 import torch
@@ -158,3 +161,44 @@ def test_prefix_attention_empty_prefix_is_a_valid_argument(L):
     attend to the suffix only; on CPU tensors the CUDA requirement is what raises."""
     with pytest.raises(RuntimeError, match="CUDA"):
         ops.prefix_attention(*_attn(L=L), beam_width=2, prefix_mask=torch.ones(2, L, dtype=torch.bool))
+
+
+@pytest.fixture(scope="module")
+def tiny_text_model():
+    """A random-init BF16 Qwen3_5TextModel with the library's tiny hybrid dims, on CPU."""
+    from transformers import Qwen3_5TextConfig
+    from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5TextModel
+
+    from kadllm_b200.config import TINY
+
+    torch.manual_seed(0)
+    model = Qwen3_5TextModel(Qwen3_5TextConfig(**TINY.to_hf_kwargs())).to(torch.bfloat16).eval()
+    head = torch.nn.Linear(TINY.hidden_size, TINY.vocab_size, bias=False).to(torch.bfloat16).eval()
+    return model, head
+
+
+@pytest.mark.parametrize("kwargs", [
+    dict(gdn_backend="cuda"), dict(conv_backend="flash_attn"), dict(attention_backend="triton"),
+    dict(attention_backend="auto"), dict(gdn_triton_config=(32, 4, 2)),  # a launch tuple needs gdn_backend="triton"
+    dict(gdn_backend="triton", gdn_triton_config=(33, 4, 2)),
+])
+def test_adapter_rejects_backend_switches_like_the_reference(tiny_text_model, kwargs):
+    """``Qwen35GRBeamAdapter``'s switches (``src/kadllm/adapters/qwen3_5.py:61-92``)."""
+    from kadllm_b200.adapters import Qwen35GRBeamAdapter
+
+    with pytest.raises(ValueError):
+        Qwen35GRBeamAdapter(*tiny_text_model, **kwargs)
+
+
+def test_adapter_rejects_other_modules_and_dtypes(tiny_text_model):
+    from kadllm_b200.adapters import Qwen35GRBeamAdapter
+
+    model, head = tiny_text_model
+    with pytest.raises(TypeError, match="Qwen3_5TextModel"):
+        Qwen35GRBeamAdapter(head, head)
+    with pytest.raises(TypeError, match="BF16"):
+        Qwen35GRBeamAdapter(model, copy.deepcopy(head).half())
+    # valid switches on a CPU model: the engine's CUDA requirement is what raises
+    with pytest.raises(RuntimeError, match="CUDA"):
+        Qwen35GRBeamAdapter(model, head, gdn_backend="triton", conv_backend="auto", attention_backend="flash_attn",
+                            gdn_triton_config=(32, 4, 2, 8))
