@@ -202,3 +202,54 @@ def test_adapter_rejects_other_modules_and_dtypes(tiny_text_model):
     with pytest.raises(RuntimeError, match="CUDA"):
         Qwen35GRBeamAdapter(model, head, gdn_backend="triton", conv_backend="auto", attention_backend="flash_attn",
                             gdn_triton_config=(32, 4, 2, 8))
+
+
+class _FakeAdapter:
+    """Returns fixed prefill logits; decode is never reached on the host."""
+
+    def __init__(self, logits):
+        self.logits, self.prefills = logits, 0
+
+    def prefill(self, input_ids):
+        from kadllm_b200.grbeam import PrefillResult
+
+        self.prefills += 1
+        return PrefillResult(self.logits, None)
+
+    def decode(self, history, state):  # pragma: no cover - validation stops earlier
+        raise AssertionError("decode reached")
+
+
+@pytest.mark.parametrize("ids,widths", [
+    (torch.zeros(3, dtype=torch.long), [2]),        # not [B, L]
+    (torch.zeros(0, 4, dtype=torch.long), [2]),     # no requests
+    (torch.zeros(2, 0, dtype=torch.long), [2]),     # empty prompts
+    (torch.zeros(2, 4, dtype=torch.long), []),      # no levels
+    (torch.zeros(2, 4, dtype=torch.long), [2, 0]),
+    (torch.zeros(2, 4, dtype=torch.long), [True]),
+    (torch.zeros(2, 4, dtype=torch.long), [2.0]),
+])
+def test_grbeam_search_rejects_inputs_before_the_prefill(ids, widths):
+    """``grbeam_search``'s checks (``src/kadllm/grbeam.py:60-65``) run before the adapter."""
+    from kadllm_b200 import grbeam_search
+
+    adapter = _FakeAdapter(torch.zeros(2, 8))
+    with pytest.raises(ValueError):
+        grbeam_search(adapter, ids, widths)
+    assert adapter.prefills == 0
+
+
+@pytest.mark.parametrize("logits", [torch.zeros(3, 8), torch.zeros(2, 1, 8), torch.zeros(2, 0)])
+def test_grbeam_search_rejects_prefill_logits_of_another_shape(logits):
+    """``src/kadllm/grbeam.py:67-72``: [B, V] logits with V >= 1."""
+    from kadllm_b200 import grbeam_search
+
+    with pytest.raises(ValueError):
+        grbeam_search(_FakeAdapter(logits), torch.zeros(2, 4, dtype=torch.long), [2])
+
+
+def test_grbeam_search_needs_cuda_logits():
+    from kadllm_b200 import grbeam_search
+
+    with pytest.raises(RuntimeError, match="CUDA"):
+        grbeam_search(_FakeAdapter(torch.zeros(2, 8)), torch.zeros(2, 4, dtype=torch.long), [2, 2])
