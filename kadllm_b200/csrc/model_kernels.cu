@@ -218,6 +218,73 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
 // arithmetic and rounding points as qk_norm_rope_kernel.  Eight CTAs per SM (32
 // registers): each warp has one row in flight, so the resident warps bound the
 // bytes in flight (8 CTAs: 125 us vs 134 us at 5 for the 32 x 1024-row prompt).
+// Head dim 256 with 64 rotary dims (the Qwen3.5 attention): lane l holds dims 64 j + 2 l
+// and 64 j + 2 l + 1 (j = 0..3), so every lane owns two of the rotary dims (j = 0) and
+// their rotate_half partners sit 16 lanes away; the grid is (head, block of 8 rows), so
+// no item is divided by the head count.  Same roundings as qk_norm_rope_d256_kernel.
+__global__ void __launch_bounds__(256, 8) qk_norm_rope_d256_r64_kernel(
+    const __nv_bfloat16* proj, int64_t ld_proj, int Hq, int HK, const float* qw, const float* kw, float eps,
+    const __nv_bfloat16* cos_tab, const __nv_bfloat16* sin_tab, const int64_t* pos_of_row, int64_t pos_base,
+    int rows_per_seq, __nv_bfloat16* q_out, int64_t sq_row, int64_t sq_h, __nv_bfloat16* k_out, int64_t sk_seq,
+    int64_t sk_pos, int64_t sk_h, __nv_bfloat16* v_out, int64_t sv_seq, int64_t sv_pos, int64_t sv_h,
+    uint32_t rows) {
+  constexpr int D = 256, kRot = 64;
+  const int h = int(blockIdx.x);
+  const uint32_t r = blockIdx.y * 8u + (threadIdx.x >> 5);
+  if (r >= rows) return;  // whole warps leave together
+  const int lane = threadIdx.x & 31;
+  const uint32_t s = r / uint32_t(rows_per_seq), p = r - s * uint32_t(rows_per_seq);
+  const __nv_bfloat16* src = proj + int64_t(r) * ld_proj;
+  if (h < Hq) src += h * 2 * D;  // q of head h (its gate follows it)
+  else if (h < Hq + HK) src += Hq * 2 * D + (h - Hq) * D;
+  else src += Hq * 2 * D + HK * D + (h - Hq - HK) * D;
+  if (h >= Hq + HK) {  // value: plain copy into the cache / suffix layout
+    const uint4 raw = *reinterpret_cast<const uint4*>(src + lane * 8);
+    *reinterpret_cast<uint4*>(v_out + s * sv_seq + p * sv_pos + (h - Hq - HK) * sv_h + lane * 8) = raw;
+    return;
+  }
+  const int64_t pos = pos_base + (pos_of_row ? pos_of_row[r] : int64_t(p));
+  uint32_t rw[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) rw[j] = *reinterpret_cast<const uint32_t*>(src + 64 * j + 2 * lane);
+  const uint32_t cw = *reinterpret_cast<const uint32_t*>(cos_tab + pos * kRot + 2 * lane);
+  const uint32_t sw = *reinterpret_cast<const uint32_t*>(sin_tab + pos * kRot + 2 * lane);
+  float v[8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = bf2f(rw[j]);
+    v[2 * j] = f.x;
+    v[2 * j + 1] = f.y;
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) ss += v[e] * v[e];
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(ss / float(D) + eps);
+  const float* w = (h < Hq ? qw : kw) + 2 * lane;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {  // bf16 rounding of each pair in one packed conversion
+    const float2 wj = *reinterpret_cast<const float2*>(w + 64 * j);
+    const float2 n = bf2f(bf2_pack((v[2 * j] * inv) * (1.0f + wj.x), (v[2 * j + 1] * inv) * (1.0f + wj.y)));
+    v[2 * j] = n.x;
+    v[2 * j + 1] = n.y;
+  }
+  {  // rotary dims 2 l, 2 l + 1: partner half 32 dims (16 lanes) away
+    const float p0 = __shfl_xor_sync(0xffffffffu, v[0], 16), p1 = __shfl_xor_sync(0xffffffffu, v[1], 16);
+    const bool lo = lane < 16;
+    const float2 c = bf2f(cw), sn = bf2f(sw);
+    const float r0 = lo ? -p0 : p0, r1 = lo ? -p1 : p1;          // rotate_half
+    const float2 vc = bf2f(bf2_pack(v[0] * c.x, v[1] * c.y));    // bf16(x cos)
+    const float2 rs = bf2f(bf2_pack(r0 * sn.x, r1 * sn.y));      // bf16(rotate_half(x) sin)
+    const float2 sum = bf2f(bf2_pack(vc.x + rs.x, vc.y + rs.y));
+    v[0] = sum.x;
+    v[1] = sum.y;
+  }
+  __nv_bfloat16* dst = h < Hq ? q_out + int64_t(r) * sq_row + h * sq_h : k_out + s * sk_seq + p * sk_pos + (h - Hq) * sk_h;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) *reinterpret_cast<uint32_t*>(dst + 64 * j + 2 * lane) = bf2_pack(v[2 * j], v[2 * j + 1]);
+}
+
 __global__ void __launch_bounds__(256, 8) qk_norm_rope_d256_kernel(
     const __nv_bfloat16* proj, int64_t ld_proj, int Hq, int HK, const float* qw, const float* kw, float eps,
     const __nv_bfloat16* cos_tab, const __nv_bfloat16* sin_tab, int rot, const int64_t* pos_of_row,
@@ -409,6 +476,18 @@ extern "C" int kadllm_qk_norm_rope(const void* proj, int64_t ld_proj, int64_t q_
   auto K = static_cast<__nv_bfloat16*>(k_out);
   auto Vv = static_cast<__nv_bfloat16*>(v_out);
   const auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+  if (head_dim == 256 && rotary_dim == 64 && rows <= 8ll * 65535 && rows_per_seq < (1ll << 31) && al16(proj) &&
+      ld_proj % 8 == 0 && al16(q_out) && al16(k_out) && al16(v_out) && al16(q_weight) && al16(k_weight) &&
+      al16(cos_tab) && al16(sin_tab) && sq_row % 8 == 0 && sq_h % 8 == 0 && sk_seq % 8 == 0 && sk_pos % 8 == 0 &&
+      sk_h % 8 == 0 && sv_seq % 8 == 0 && sv_pos % 8 == 0 && sv_h % 8 == 0) {
+    const dim3 g2(unsigned(q_heads + 2 * kv_heads), unsigned((rows + 7) / 8));
+    qk_norm_rope_d256_r64_kernel<<<g2, 256, 0, s>>>(P, ld_proj, int(q_heads), int(kv_heads), q_weight, k_weight, eps,
+                                                     C, S, pos_of_row, pos_base, int(rows_per_seq), Q, sq_row, sq_h,
+                                                     K, sk_seq, sk_pos, sk_h, Vv, sv_seq, sv_pos, sv_h,
+                                                     uint32_t(rows));
+    KB_CHECK_LAUNCH("qk_norm_rope launch");
+    return KADLLM_OK;
+  }
   if (head_dim == 256 && items < (1ll << 31) && rows_per_seq < (1ll << 31) && al16(proj) && ld_proj % 8 == 0 &&
       al16(q_out) && al16(k_out) && al16(v_out) && al16(q_weight) && al16(k_weight) && al16(cos_tab) &&
       al16(sin_tab) && sq_row % 8 == 0 && sq_h % 8 == 0 && sk_seq % 8 == 0 && sk_pos % 8 == 0 && sk_h % 8 == 0 &&

@@ -63,20 +63,25 @@ def test_silu_mul():
     assert_close_rel(N(out), ref, rel=5e-3, what="silu_mul")
 
 
-@pytest.mark.parametrize("D,hq,hk", [(32, 4, 2), (256, 8, 2)])
-def test_qk_norm_rope_prefill_and_decode(D, hq, hk):
+@pytest.mark.parametrize("D,hq,hk,factor,B,L", [
+    (32, 4, 2, 0.25, 2, 9),
+    (256, 8, 2, 0.25, 2, 9),     # 64 rotary dims: the two-dims-per-lane kernel
+    (256, 8, 2, 0.25, 3, 700),   # ... over many 8-row blocks, rows ending inside one
+    (256, 8, 2, 0.125, 2, 9),    # 32 rotary dims: the eight-dims-per-lane kernel
+])
+def test_qk_norm_rope_prefill_and_decode(D, hq, hk, factor, B, L):
     from kadllm_b200.config import TINY
 
-    cfg = TINY.with_(head_dim=D, num_attention_heads=hq, num_key_value_heads=hk, rope_theta=1e7)
-    rng = np.random.default_rng(D)
-    B, L = 2, 9
+    cfg = TINY.with_(head_dim=D, num_attention_heads=hq, num_key_value_heads=hk, rope_theta=1e7,
+                     partial_rotary_factor=factor)
+    rng = np.random.default_rng(D + L)
     rows = B * L
     ld = (2 * hq + 2 * hk) * D
     P = O.bf16(rng.standard_normal((rows, ld)).astype(np.float32))
     qw = O.bf16(0.1 * rng.standard_normal(D).astype(np.float32))
     kw = O.bf16(0.1 * rng.standard_normal(D).astype(np.float32))
     rot = cfg.rotary_dim
-    pos = torch.arange(64, device="cuda", dtype=torch.float32)
+    pos = torch.arange(L + 5, device="cuda", dtype=torch.float32)
     inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, rot, 2, device="cuda").float() / rot))
     emb = torch.cat([pos[:, None] * inv, pos[:, None] * inv], -1)
     cos, sin = emb.cos().to(bf).contiguous(), emb.sin().to(bf).contiguous()
