@@ -184,9 +184,9 @@ KADLLM_API int kadllm_beam_select_status(const void* workspace, int64_t batch, i
 
 /* Allocation-free variant of kadllm_beam_select (no counterpart in the
  * reference).  For callers that cannot allocate device memory where they
- * select beams -- a captured CUDA-graph region with a frozen memory pool, a
- * host that hands the library only the tensors it owns, an allocator that may
- * not grow on the decode path.  Its scratch is one 9 MiB array in the
+ * select beams -- a host that hands the library only the tensors it owns, a
+ * serving runtime whose memory budget is fixed when the model loads, an
+ * allocator that may not grow on the decode path.  Its scratch is one 9 MiB array in the
  * library's device image, reserved on every GPU that loads the library until
  * the process exits; limits: batch <= 32 and batch * prev_width <= 512 (larger
  * sizes return KADLLM_EINVAL).  The first call on a device resolves the

@@ -780,11 +780,11 @@ extern "C" int kadllm_beam_select_status(const void* workspace, int64_t batch, i
 
 // ---------------------------------------------------------------------------
 // Allocation-free variant.  Some callers cannot allocate device memory at the
-// point where they select beams: code running inside a captured or replayed
-// CUDA-graph region whose memory pool is frozen, embedded / plugin hosts that
-// hand the library only the tensors they own, and allocators that forbid
-// growth on the decode path.  For them the selection keeps its scratch in one
-// fixed array that lives in this library's device image.
+// point where they select beams: embedded / plugin hosts that hand the library
+// only the tensors they own, serving runtimes whose memory budget is fixed
+// when the model loads, and allocators that forbid growth on the decode path.
+// For them the selection keeps its scratch in one fixed array that lives in
+// this library's device image.
 //
 // kNoAllocScratchBytes (9 MiB) is reserved on every GPU that loads the library,
 // until the process exits.  It covers batch * prev_width <= 512 rows and
@@ -792,8 +792,8 @@ extern "C" int kadllm_beam_select_status(const void* workspace, int64_t batch, i
 // Every call shares the array and it keeps the previous call's contents: the
 // kernels rewrite everything they read except the per-request counters, which
 // the threshold kernel clears, so no clearing is needed here -- but two calls
-// whose work overlaps on the GPU (different streams, or graph branches) race on
-// the array and must be serialised by the caller.
+// whose work overlaps on the GPU (for instance on two streams) race on the
+// array and must be serialised by the caller.
 // ---------------------------------------------------------------------------
 namespace kb {
 namespace {

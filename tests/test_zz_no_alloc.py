@@ -1,7 +1,8 @@
 """The allocation-free beam selection gives the same results as the workspace one.
 
-Some callers cannot allocate device memory where they select beams (a graph
-region with a frozen memory pool, a host that only lends its own tensors).
+Some callers cannot allocate device memory where they select beams (a host
+that only lends the library its own tensors, a runtime whose memory budget is
+fixed when the model loads).
 ``kadllm_beam_select_noalloc`` serves them from a fixed scratch array in the
 library's device image.  This file is collected last so a failure here does not
 hide the rest of the suite; it must pass alone and after the other tests.
