@@ -220,9 +220,13 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
 // bytes in flight (8 CTAs: 125 us vs 134 us at 5 for the 32 x 1024-row prompt).
 // Head dim 256 with 64 rotary dims (the Qwen3.5 attention): lane l holds dims 64 j + 2 l
 // and 64 j + 2 l + 1 (j = 0..3), so every lane owns two of the rotary dims (j = 0) and
-// their rotate_half partners sit 16 lanes away; the grid is (head, block of 8 rows), so
-// no item is divided by the head count.  Same roundings as qk_norm_rope_d256_kernel.
-__global__ void __launch_bounds__(256, 8) qk_norm_rope_d256_r64_kernel(
+// their rotate_half partners sit 16 lanes away.  The grid is (head, block of 32 rows):
+// each warp takes 4 consecutive rows of one head, so the head's offset, its norm
+// weights (1 + w) and the row's sequence / position are set up once and stepped, and
+// the next row's loads are in flight while a row is normalised.  Same roundings as
+// qk_norm_rope_d256_kernel.
+constexpr int kQkRowsPerWarp = 4;
+__global__ void __launch_bounds__(256, 5) qk_norm_rope_d256_r64_kernel(
     const __nv_bfloat16* proj, int64_t ld_proj, int Hq, int HK, const float* qw, const float* kw, float eps,
     const __nv_bfloat16* cos_tab, const __nv_bfloat16* sin_tab, const int64_t* pos_of_row, int64_t pos_base,
     int rows_per_seq, __nv_bfloat16* q_out, int64_t sq_row, int64_t sq_h, __nv_bfloat16* k_out, int64_t sk_seq,
@@ -230,59 +234,103 @@ __global__ void __launch_bounds__(256, 8) qk_norm_rope_d256_r64_kernel(
     uint32_t rows) {
   constexpr int D = 256, kRot = 64;
   const int h = int(blockIdx.x);
-  const uint32_t r = blockIdx.y * 8u + (threadIdx.x >> 5);
-  if (r >= rows) return;  // whole warps leave together
+  const uint32_t r0 = (blockIdx.y * 8u + (threadIdx.x >> 5)) * uint32_t(kQkRowsPerWarp);
+  if (r0 >= rows) return;  // whole warps leave together
+  const int n = int(min(uint32_t(kQkRowsPerWarp), rows - r0));
   const int lane = threadIdx.x & 31;
-  const uint32_t s = r / uint32_t(rows_per_seq), p = r - s * uint32_t(rows_per_seq);
-  const __nv_bfloat16* src = proj + int64_t(r) * ld_proj;
-  if (h < Hq) src += h * 2 * D;  // q of head h (its gate follows it)
-  else if (h < Hq + HK) src += Hq * 2 * D + (h - Hq) * D;
-  else src += Hq * 2 * D + HK * D + (h - Hq - HK) * D;
+  uint32_t s = r0 / uint32_t(rows_per_seq), p = r0 - s * uint32_t(rows_per_seq);  // stepped per row below
+  int hoff;  // the head's columns in the projection row
+  if (h < Hq) hoff = h * 2 * D;  // q of head h (its gate follows it)
+  else if (h < Hq + HK) hoff = Hq * 2 * D + (h - Hq) * D;
+  else hoff = Hq * 2 * D + HK * D + (h - Hq - HK) * D;
+  const __nv_bfloat16* src = proj + int64_t(r0) * ld_proj + hoff;
   if (h >= Hq + HK) {  // value: plain copy into the cache / suffix layout
-    const uint4 raw = *reinterpret_cast<const uint4*>(src + lane * 8);
-    *reinterpret_cast<uint4*>(v_out + s * sv_seq + p * sv_pos + (h - Hq - HK) * sv_h + lane * 8) = raw;
+    __nv_bfloat16* dst = v_out + (h - Hq - HK) * sv_h + lane * 8;
+    for (int i = 0; i < n; ++i) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(src + int64_t(i) * ld_proj + lane * 8);
+      *reinterpret_cast<uint4*>(dst + s * sv_seq + p * sv_pos) = raw;
+      if (++p == uint32_t(rows_per_seq)) {
+        p = 0;
+        ++s;
+      }
+    }
     return;
   }
-  const int64_t pos = pos_base + (pos_of_row ? pos_of_row[r] : int64_t(p));
-  uint32_t rw[4];
+  float w1[8];  // 1 + w of this lane's dims
+  {
+    const float* w = (h < Hq ? qw : kw) + 2 * lane;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) rw[j] = *reinterpret_cast<const uint32_t*>(src + 64 * j + 2 * lane);
-  const uint32_t cw = *reinterpret_cast<const uint32_t*>(cos_tab + pos * kRot + 2 * lane);
-  const uint32_t sw = *reinterpret_cast<const uint32_t*>(sin_tab + pos * kRot + 2 * lane);
-  float v[8];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float2 f = bf2f(rw[j]);
-    v[2 * j] = f.x;
-    v[2 * j + 1] = f.y;
+    for (int j = 0; j < 4; ++j) {
+      const float2 wj = *reinterpret_cast<const float2*>(w + 64 * j);
+      w1[2 * j] = 1.0f + wj.x;
+      w1[2 * j + 1] = 1.0f + wj.y;
+    }
   }
-  float ss = 0.f;
+  auto row_pos = [&](int i, uint32_t pp) -> int64_t {
+    return pos_base + (pos_of_row ? pos_of_row[r0 + i] : int64_t(pp));
+  };
+  uint32_t rw[4], cw, sw;
+  {  // row 0's loads
 #pragma unroll
-  for (int e = 0; e < 8; ++e) ss += v[e] * v[e];
-  ss = warp_sum(ss);
-  const float inv = 1.0f / sqrtf(ss / float(D) + eps);
-  const float* w = (h < Hq ? qw : kw) + 2 * lane;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {  // bf16 rounding of each pair in one packed conversion
-    const float2 wj = *reinterpret_cast<const float2*>(w + 64 * j);
-    const float2 n = bf2f(bf2_pack((v[2 * j] * inv) * (1.0f + wj.x), (v[2 * j + 1] * inv) * (1.0f + wj.y)));
-    v[2 * j] = n.x;
-    v[2 * j + 1] = n.y;
+    for (int j = 0; j < 4; ++j) rw[j] = *reinterpret_cast<const uint32_t*>(src + 64 * j + 2 * lane);
+    const int64_t pos = row_pos(0, p);
+    cw = *reinterpret_cast<const uint32_t*>(cos_tab + pos * kRot + 2 * lane);
+    sw = *reinterpret_cast<const uint32_t*>(sin_tab + pos * kRot + 2 * lane);
   }
-  {  // rotary dims 2 l, 2 l + 1: partner half 32 dims (16 lanes) away
-    const float p0 = __shfl_xor_sync(0xffffffffu, v[0], 16), p1 = __shfl_xor_sync(0xffffffffu, v[1], 16);
-    const bool lo = lane < 16;
-    const float2 c = bf2f(cw), sn = bf2f(sw);
-    const float r0 = lo ? -p0 : p0, r1 = lo ? -p1 : p1;          // rotate_half
-    const float2 vc = bf2f(bf2_pack(v[0] * c.x, v[1] * c.y));    // bf16(x cos)
-    const float2 rs = bf2f(bf2_pack(r0 * sn.x, r1 * sn.y));      // bf16(rotate_half(x) sin)
-    const float2 sum = bf2f(bf2_pack(vc.x + rs.x, vc.y + rs.y));
-    v[0] = sum.x;
-    v[1] = sum.y;
-  }
-  __nv_bfloat16* dst = h < Hq ? q_out + int64_t(r) * sq_row + h * sq_h : k_out + s * sk_seq + p * sk_pos + (h - Hq) * sk_h;
+  for (int i = 0; i < n; ++i) {
+    const uint32_t ps = s, pp = p;  // this row's sequence / position
+    if (++p == uint32_t(rows_per_seq)) {
+      p = 0;
+      ++s;
+    }
+    uint32_t nrw[4] = {0u, 0u, 0u, 0u}, ncw = 0u, nsw = 0u;
+    if (i + 1 < n) {  // the next row's loads, in flight while this row is computed
+      const __nv_bfloat16* nsrc = src + int64_t(i + 1) * ld_proj;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) *reinterpret_cast<uint32_t*>(dst + 64 * j + 2 * lane) = bf2_pack(v[2 * j], v[2 * j + 1]);
+      for (int j = 0; j < 4; ++j) nrw[j] = *reinterpret_cast<const uint32_t*>(nsrc + 64 * j + 2 * lane);
+      const int64_t npos = row_pos(i + 1, p);
+      ncw = *reinterpret_cast<const uint32_t*>(cos_tab + npos * kRot + 2 * lane);
+      nsw = *reinterpret_cast<const uint32_t*>(sin_tab + npos * kRot + 2 * lane);
+    }
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = bf2f(rw[j]);
+      v[2 * j] = f.x;
+      v[2 * j + 1] = f.y;
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss += v[e] * v[e];
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / float(D) + eps);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {  // bf16 rounding of each pair in one packed conversion
+      const float2 nv = bf2f(bf2_pack((v[2 * j] * inv) * w1[2 * j], (v[2 * j + 1] * inv) * w1[2 * j + 1]));
+      v[2 * j] = nv.x;
+      v[2 * j + 1] = nv.y;
+    }
+    {  // rotary dims 2 l, 2 l + 1: partner half 32 dims (16 lanes) away
+      const float p0 = __shfl_xor_sync(0xffffffffu, v[0], 16), p1 = __shfl_xor_sync(0xffffffffu, v[1], 16);
+      const bool lo = lane < 16;
+      const float2 c = bf2f(cw), sn = bf2f(sw);
+      const float q0 = lo ? -p0 : p0, q1 = lo ? -p1 : p1;          // rotate_half
+      const float2 vc = bf2f(bf2_pack(v[0] * c.x, v[1] * c.y));    // bf16(x cos)
+      const float2 rs = bf2f(bf2_pack(q0 * sn.x, q1 * sn.y));      // bf16(rotate_half(x) sin)
+      const float2 sum = bf2f(bf2_pack(vc.x + rs.x, vc.y + rs.y));
+      v[0] = sum.x;
+      v[1] = sum.y;
+    }
+    __nv_bfloat16* dst = h < Hq ? q_out + int64_t(r0 + i) * sq_row + h * sq_h
+                                : k_out + ps * sk_seq + pp * sk_pos + (h - Hq) * sk_h;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      *reinterpret_cast<uint32_t*>(dst + 64 * j + 2 * lane) = bf2_pack(v[2 * j], v[2 * j + 1]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) rw[j] = nrw[j];
+    cw = ncw;
+    sw = nsw;
+  }
 }
 
 __global__ void __launch_bounds__(256, 8) qk_norm_rope_d256_kernel(
@@ -476,11 +524,11 @@ extern "C" int kadllm_qk_norm_rope(const void* proj, int64_t ld_proj, int64_t q_
   auto K = static_cast<__nv_bfloat16*>(k_out);
   auto Vv = static_cast<__nv_bfloat16*>(v_out);
   const auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
-  if (head_dim == 256 && rotary_dim == 64 && rows <= 8ll * 65535 && rows_per_seq < (1ll << 31) && al16(proj) &&
+  if (head_dim == 256 && rotary_dim == 64 && rows <= 32ll * 65535 && rows_per_seq < (1ll << 31) && al16(proj) &&
       ld_proj % 8 == 0 && al16(q_out) && al16(k_out) && al16(v_out) && al16(q_weight) && al16(k_weight) &&
       al16(cos_tab) && al16(sin_tab) && sq_row % 8 == 0 && sq_h % 8 == 0 && sk_seq % 8 == 0 && sk_pos % 8 == 0 &&
       sk_h % 8 == 0 && sv_seq % 8 == 0 && sv_pos % 8 == 0 && sv_h % 8 == 0) {
-    const dim3 g2(unsigned(q_heads + 2 * kv_heads), unsigned((rows + 7) / 8));
+    const dim3 g2(unsigned(q_heads + 2 * kv_heads), unsigned((rows + 8 * kQkRowsPerWarp - 1) / (8 * kQkRowsPerWarp)));
     qk_norm_rope_d256_r64_kernel<<<g2, 256, 0, s>>>(P, ld_proj, int(q_heads), int(kv_heads), q_weight, k_weight, eps,
                                                      C, S, pos_of_row, pos_base, int(rows_per_seq), Q, sq_row, sq_h,
                                                      K, sk_seq, sk_pos, sk_h, Vv, sv_seq, sv_pos, sv_h,

@@ -66,7 +66,7 @@ def test_silu_mul():
 @pytest.mark.parametrize("D,hq,hk,factor,B,L", [
     (32, 4, 2, 0.25, 2, 9),
     (256, 8, 2, 0.25, 2, 9),     # 64 rotary dims: the two-dims-per-lane kernel
-    (256, 8, 2, 0.25, 3, 700),   # ... over many 8-row blocks, rows ending inside one
+    (256, 8, 2, 0.25, 3, 701),   # ... over many row blocks; sequences end inside a warp's rows
     (256, 8, 2, 0.125, 2, 9),    # 32 rotary dims: the eight-dims-per-lane kernel
 ])
 def test_qk_norm_rope_prefill_and_decode(D, hq, hk, factor, B, L):
